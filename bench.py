@@ -1,0 +1,309 @@
+#!/usr/bin/env python
+"""Headline benchmark: SSD->HBM KV restore GB/s (whole job, all ranks).
+
+One step restores one 32,768-token Llama-3.1-8B KV prefix (32 layers x 8 KV
+heads x 128 dims, bf16, block 16: 2,048 blocks x 64 KiB x 32 layers = 4.29 GB)
+from the segment-file store into seeded random blocks of a 16,384-block paged
+pool in HBM, through the public API (TuttiKVStore.get_paged -> StorageRuntime
+submit -> fused sm_100a NVMe io kernel -> emulated NVMe controllers serving the
+segment files from the host's page cache). Each rank restores its own prefix
+(weak scaling). Device time is measured with CUDA events on the launching
+stream, max over ranks. Inputs (4.29 GB per step) are far larger than L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--drives D]
+    python bench.py --impl reference     # the reference's own build
+    python bench.py --impl posix         # CPU-initiated pread + cudaMemcpy baseline
+
+For N > 1 launch with torch.distributed.run (one rank per GPU).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "kv_restore_GBps"
+BASELINE_GBPS = None  # BASELINE.md publishes no B200 number for this config
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="tutti", choices=["tutti", "reference", "posix"])
+    p.add_argument("--drives", type=int, default=4, help="emulated NVMe drives (striped mounts) per rank")
+    p.add_argument("--prefix-tokens", type=int, default=32768)
+    p.add_argument("--pool-blocks", type=int, default=16384)
+    p.add_argument("--root", default=os.environ.get("TUTTI_BENCH_ROOT", "/tmp/tutti_bench"))
+    p.add_argument("--controller-threads", type=int, default=0, help="0: auto")
+    p.add_argument("--direct-io", action="store_true", help="O_DIRECT backing reads (drive-bound)")
+    p.add_argument("--no-verify", action="store_true")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        if shutil.which("nvidia-smi") is None:
+            return self
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits"],
+                                         capture_output=True, text=True, timeout=5).stdout
+                    for line in out.strip().splitlines():
+                        f = [x.strip() for x in line.split(",")]
+                        if int(f[0]) in self.gpus:
+                            self.rows.append(f)
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(world, value: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(world, value: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def reference_arm(args):
+    """The reference's stock path cannot run on this pool; say why in one line."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    reason = None
+    if not os.path.isdir(os.path.join(ref, "tutti")):
+        reason = "reference package not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import tutti_runtime._core  # noqa: F401  (the reference's native runtime)
+        except ImportError:
+            reason = ("reference SSD->HBM restore needs its native tutti_runtime._core (CMake build needing "
+                      "gRPC/protobuf/yaml-cpp, absent offline) plus the snvme kernel module, tutti_daemon and "
+                      "bindable NVMe drives (none on the GPU box); pip install yields only the pure-Python package")
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": reason or "unknown"}))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import numpy as np
+    import torch
+
+    from tutti_b200.models.kv_geometry import LLAMA3_8B
+    from tutti_b200.storage.tutti_store import TuttiKVStore
+    from tutti_b200.index.chunk_index import chunk_keys_for_tokens
+
+    world, rank, local = dist_setup()
+    g = LLAMA3_8B
+    dev = torch.device("cuda", local)
+    nblk = args.prefix_tokens // g.block_size
+    nchunks = args.prefix_tokens // g.chunk_tokens
+    root = os.path.join(args.root, f"r{rank}")
+    shutil.rmtree(root, ignore_errors=True)
+    mounts = [os.path.join(root, f"nvme{d}") for d in range(args.drives)]
+    ncpu = os.cpu_count() or 8
+    threads = args.controller_threads or max(2, min(8, ncpu // max(1, world) // max(1, args.drives)))
+    opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": 128,
+            "max_ctas_per_op": 128, "slots_per_lease": 4, "slot_bytes": 1 << 20, "queue_depth": 256,
+            "mdts_bytes": 1 << 20}
+    backend = "nvme-gpu" if args.impl == "tutti" else "posix"
+    if backend == "posix":
+        opts = {"threads": max(4, ncpu // max(1, world)), "direct_io": bool(args.direct_io)}
+    # capacity: the prefix plus one spare file group
+    spf = max(16, (nchunks + args.drives - 1) // args.drives)
+    store = TuttiKVStore(root, g, capacity_chunks=spf * args.drives, mounts=mounts, device=local,
+                         backend=backend, runtime_options=opts, segment_file_slots=spf,
+                         namespace=b"bench")
+    store.open()
+    pool = torch.empty(g.pool_shape(args.pool_blocks), dtype=g.dtype, device=dev)
+    store.register_pool(pool)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    # Source prefix in the pool at seeded random blocks, persisted once (untimed setup).
+    rng = np.random.default_rng(rank)
+    src_blocks = rng.permutation(args.pool_blocks)[:nblk].reshape(nchunks, g.blocks_per_chunk)
+    src_idx = torch.from_numpy(src_blocks.reshape(-1)).to(dev)
+    ref = torch.randn((g.num_layers, g.planes, nblk, g.block_size, g.heads_per_rank, g.head_dim), dtype=g.dtype,
+                      device=dev, generator=gen)
+    pool[:, :, src_idx] = ref
+    tokens = torch.randint(0, 128_000, (args.prefix_tokens,), generator=torch.Generator().manual_seed(7 + rank))
+    keys = chunk_keys_for_tokens(tokens.tolist(), g.chunk_tokens)
+    t0 = time.perf_counter()
+    store.put_paged(keys, src_blocks).wait()
+    store_s = time.perf_counter() - t0
+    store.warm_targets()
+    bytes_per_step = nblk * g.num_layers * g.block_layer_bytes
+
+    perms = [rng.permutation(args.pool_blocks)[:nblk].reshape(nchunks, g.blocks_per_chunk)
+             for _ in range(args.warmup + args.steps)]
+    pinned_tables = [torch.from_numpy(p.reshape(-1).copy()).pin_memory() for p in perms]
+    dev_table = torch.empty(nblk, dtype=torch.int64, device=dev)
+    checksum = torch.zeros(1, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    launches = [0]
+
+    def step(i, e2e: bool):
+        if e2e:
+            dev_table.copy_(pinned_tables[i], non_blocking=True)  # H2D: this step's block table
+        comp = store.get_paged(keys, perms[i], stream=stream)
+        launches[0] += len(comp._ios)
+        comp.wait()
+        if e2e:
+            # D2H: the step's result (a checksum of the restored first block)
+            checksum.copy_(pool[0, 0, dev_table[0]].float().sum().reshape(1), non_blocking=True)
+            stream.synchronize()
+
+    for i in range(args.warmup):
+        step(i, False)
+    barrier(world)
+    sampler = ClockSampler([local]).start() if rank == 0 else None
+    # device-timed: K restores back to back
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    ev0.record(stream)
+    launches[0] = 0
+    for i in range(args.warmup, args.warmup + args.steps):
+        step(i, False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dev_ms = ev0.elapsed_time(ev1) / args.steps
+    n_launch = launches[0]
+    barrier(world)
+    # end to end: + H2D block table from pinned memory + D2H result readback every step
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    for i in range(args.warmup, args.warmup + args.steps):
+        step(i, True)
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev2.elapsed_time(ev3) / args.steps
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+
+    ok = True
+    if not args.no_verify:
+        last = torch.from_numpy(perms[-1].reshape(-1)).to(dev)
+        ok = bool(torch.equal(pool[:, :, last], ref))
+    ok_all = max_over_ranks(world, 0.0 if ok else 1.0) == 0.0
+    ms = max_over_ranks(world, dev_ms)
+    e2e = max_over_ranks(world, e2e_ms)
+    total_bytes = sum_over_ranks(world, float(bytes_per_step))
+    timing = store.runtime.io_timing() if store.runtime else {}
+    stats = store.runtime.controller_stats() if store.runtime else []
+    store.close()
+    if rank == 0:
+        value = total_bytes / (ms / 1e3) / 1e9
+        out = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None if BASELINE_GBPS is None else round(value / BASELINE_GBPS, 3),
+            "dtype": "bf16", "data": "synthetic (randn KV of the named shape; emulated NVMe over page-cached segment files)",
+            "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world,
+                       "seq_len": args.prefix_tokens, "parallelism": f"dp{world} (one prefix per rank)",
+                       "pool_blocks": args.pool_blocks, "drives_per_rank": args.drives,
+                       "backing": "O_DIRECT" if args.direct_io else "page cache",
+                       "controller_threads": threads, "impl": args.impl,
+                       "l2": "inputs (4.29 GB/step) larger than L2"},
+            "e2e": {"value": round(total_bytes / (e2e / 1e3) / 1e9, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": nblk * 8, "d2h_bytes_per_step": 4},
+            "gpu_launches": n_launch,
+            "verified": ok_all,
+            "store_setup_s": round(store_s, 2),
+            "clocks": clocks,
+        }
+        print(json.dumps(out))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    shutil.rmtree(root, ignore_errors=True)
+    return 0 if ok_all else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

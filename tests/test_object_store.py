@@ -1,0 +1,138 @@
+import os
+import struct
+
+import pytest
+
+from tutti_b200._native import core
+
+
+def cfg(root, **kw):
+    c = {"uri": str(root), "segment_bytes": 8192, "segment_count": 3, "segment_file_slots": 4,
+         "segment_header_bytes": 131072, "capacity_slots": 16, "fingerprint": "fp-1",
+         "mounts": [str(root / "d0"), str(root / "d1")]}
+    c.update(kw)
+    return c
+
+
+def test_digests_match_published_check_values():
+    c = core()
+    assert c.crc32c(b"123456789") == 0xE3069283  # CRC-32C check value
+    assert c.crc32c(b"") == 0
+
+
+def test_slot_placement_matches_segment_file_format(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    slot_bytes = 131072 + 3 * 8192
+    assert s.slot_bytes == slot_bytes
+    # slot % N picks the device; (slot / N) / slots_per_file the file
+    assert s.slot_path(0).endswith("d0/r0/segments/0.seg")
+    assert s.slot_path(1).endswith("d1/r0/segments/0.seg")
+    assert s.slot_path(9).endswith("d1/r0/segments/1.seg")
+    assert s.header_offset_for_slot(5) == (5 // 2 % 4) * slot_bytes
+    assert s.payload_offset_for_slot(5) == s.header_offset_for_slot(5) + 131072
+    assert s.ready_slots == 8  # first file group materialised at open
+    assert os.path.getsize(s.slot_path(0)) == 4 * slot_bytes
+    s.close()
+
+
+def test_reserve_commit_header_and_recover(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    keys = [bytes([i]) * 18 for i in range(5)]
+    acc, rej = s.reserve(keys)
+    assert rej == 0 and len(acc) == 5
+    assert s.contains_prefix(keys) == 0
+    s.commit(keys)
+    assert s.contains_prefix(keys) == 5
+    # header bytes on media
+    _, uri, off, slot, gen = acc[2]
+    path = uri[len("file://"):]
+    with open(path, "rb") as f:
+        f.seek(s.header_offset_for_slot(slot))
+        h = f.read(4096)
+    assert h[:8] == b"TUTTIOBJ"
+    assert struct.unpack_from("<I", h, 56)[0] == core().crc32c(h[:56])
+    assert struct.unpack_from("<Q", h, 16)[0] == core().object_identity(keys[2])
+    assert h[64:64 + 18] == keys[2]
+    s.close()
+    s2 = core().ObjectStore()
+    s2.open(cfg(tmp_path))
+    rec = s2.recover()
+    assert sorted(rec) == sorted(keys)
+    assert s2.lookup(keys[2])[2] == slot
+    s2.close()
+
+
+def test_uncommitted_is_never_written_and_release_invalidates(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    a, b = b"a" * 18, b"b" * 18
+    s.reserve([a, b])
+    s.commit([a])
+    s.pin([a])
+    assert s.release([a]) == 0  # pinned
+    s.unpin([a])
+    assert s.release([a]) == 1
+    s.close()
+    s2 = core().ObjectStore()
+    s2.open(cfg(tmp_path))
+    assert s2.recover() == []
+    s2.close()
+
+
+def test_fingerprint_mismatch_fails_closed(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    s.close()
+    s2 = core().ObjectStore()
+    with pytest.raises(ValueError):
+        s2.open(cfg(tmp_path, fingerprint="other"))
+
+
+def test_capacity_partial_acceptance_and_precreate(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path, capacity_slots=16))
+    keys = [bytes([i]) * 18 for i in range(12)]
+    acc, rej = s.reserve(keys)
+    assert len(acc) == 8 and rej == 4  # only the first group is ready
+    assert s.precreate_step(100) == 8
+    acc2, rej2 = s.reserve(keys)
+    assert rej2 == 0 and len(acc2) == 12
+    s.close()
+
+
+def test_read_only_refuses_mutation(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    s.reserve([b"k" * 18])
+    s.commit([b"k" * 18])
+    s.close()
+    ro = core().ObjectStore()
+    ro.open(cfg(tmp_path, read_only=True))
+    assert ro.recover() == [b"k" * 18]
+    with pytest.raises(RuntimeError):
+        ro.reserve([b"z" * 18])
+    ro.close()
+
+
+def test_residency_bitmaps_all_ranks(tmp_path):
+    stores = []
+    for r in range(2):
+        s = core().ObjectStore()
+        s.open(cfg(tmp_path, rank_id=r, rank_count=2))
+        stores.append(s)
+    # reopen rank 0 so it maps rank 1's bitmap
+    keys = [b"x" * 18, b"y" * 18]
+    for s in stores:
+        s.reserve(keys)
+    stores[0].commit(keys)
+    stores[1].commit(keys[:1])
+    stores[0].close()
+    s0 = core().ObjectStore()
+    s0.open(cfg(tmp_path, rank_id=0, rank_count=2))
+    s0.recover()
+    assert s0.contains_prefix(keys) == 2
+    assert s0.contains_prefix(keys, True) == 1
+    s0.close()
+    stores[1].close()

@@ -1,0 +1,650 @@
+#include "gpu_nvme_data_path.h"
+
+#include <algorithm>
+#include <cstring>
+
+#include <cuda_runtime.h>
+
+#include "../runtime/device_guard.h"
+
+namespace tutti {
+
+namespace {
+constexpr std::uint32_t kApiVersion = 1;
+
+std::size_t align_up(std::size_t v, std::size_t a) { return (v + a - 1) / a * a; }
+
+Status cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return Status::Ok();
+    cudaGetLastError();
+    return {StatusCode::DEVICE_ERROR, std::string(what) + ": " + cudaGetErrorString(e)};
+}
+
+double percentile(std::vector<double>& v, double q) {
+    if (v.empty()) return 0.0;
+    std::size_t k = static_cast<std::size_t>(q * (v.size() - 1));
+    std::nth_element(v.begin(), v.begin() + k, v.end());
+    return v[k];
+}
+}  // namespace
+
+GpuNvmeDataPath::GpuNvmeDataPath(GpuNvmeConfig config, std::vector<GpuNvmeDevice> devices)
+    : cfg_(config), devs_(std::move(devices)) {
+    caps_.name = "nvme-gpu";
+    caps_.source_api_version = kApiVersion;
+    caps_.supports_device_execution = true;
+    caps_.supports_host_execution = false;
+    caps_.supports_device_memory = true;
+    caps_.supports_host_memory = true;  // page-locked, device-mapped host memory
+    caps_.supports_direct = false;
+    caps_.supports_staged = true;
+    caps_.supports_read = true;
+    caps_.supports_write = true;
+    std::uint32_t lba = 512;
+    for (auto& d : devs_)
+        if (d.controller) lba = std::max(lba, d.controller->info().lba_bytes);
+    caps_.target_alignment_bytes = lba;
+    caps_.memory_alignment_bytes = 16;
+    caps_.length_alignment_bytes = lba;
+    caps_.max_single_io_bytes = 0;
+    caps_.max_batch_requests = 1u << 26;
+    caps_.supports_scatter_gather = true;
+    caps_.max_scatter_gather_entries = cfg_.max_pieces_per_cmd;
+    caps_.registration_scope = RegistrationScope::GLOBAL;
+    caps_.progress_model = ProgressModel::HOST_POLL;
+    caps_.device_completion_fence_on_caller_stream = true;
+    caps_.device_execution_autonomous = true;
+    caps_.supports_multi_stream = true;
+    caps_.max_concurrent_streams = 0;
+    caps_.bound_accel_id = cfg_.accel_id;
+    caps_.supports_multi_gpu = false;
+    caps_.optional_target_features = {"fused-paged-scatter", "striped", "raid0-members"};
+}
+
+GpuNvmeDataPath::~GpuNvmeDataPath() { shutdown(0); }
+
+Status GpuNvmeDataPath::initialize(const DataPathConfig&, ResourceProvider*) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (initialized_) return {StatusCode::INVALID_ARGUMENT, "already initialized"};
+    if (devs_.empty() || devs_.size() > io::kMaxDevices)
+        return {StatusCode::INVALID_ARGUMENT, "device table must hold 1..8 controllers"};
+    if (cfg_.slots_per_lease == 0 || cfg_.slots_per_lease > io::kMaxSlots)
+        return {StatusCode::INVALID_ARGUMENT, "slots_per_lease must be in [1, 16]"};
+    if (cfg_.slot_bytes < 4096 || cfg_.slot_bytes > (2u << 20) || cfg_.slot_bytes % 4096)
+        return {StatusCode::INVALID_ARGUMENT, "slot_bytes must be a 4 KiB multiple <= 2 MiB"};
+    if (cfg_.leases == 0) return {StatusCode::INVALID_ARGUMENT, "leases must be > 0"};
+    for (auto& d : devs_) {
+        if (!d.controller) return {StatusCode::INVALID_ARGUMENT, "null controller"};
+        const auto& inf = d.controller->info();
+        if (inf.num_io_queues < cfg_.leases)
+            return {StatusCode::RESOURCE_EXHAUSTED,
+                    inf.name + " has " + std::to_string(inf.num_io_queues) + " queues < leases"};
+        if (cfg_.slots_per_lease * io::kMaxSub >= inf.queue_depth)
+            return {StatusCode::INVALID_ARGUMENT, "slots_per_lease x 8 must be < queue depth"};
+    }
+    // A command must split into <= kMaxSub NVMe commands: half the budget for
+    // MDTS splits, half for extent boundaries.
+    cmd_bytes_ = cfg_.slot_bytes;
+    for (auto& d : devs_)
+        cmd_bytes_ = std::min<std::uint32_t>(cmd_bytes_, d.controller->info().mdts_bytes * (io::kMaxSub / 2));
+    DeviceGuard guard(cfg_.accel_id);
+    TUTTI_RETURN_IF_ERROR(guard.status());
+    TUTTI_RETURN_IF_ERROR(init_device_side());
+    initialized_ = true;
+    return Status::Ok();
+}
+
+Status GpuNvmeDataPath::init_device_side() {
+    const std::uint64_t nslots = std::uint64_t(cfg_.leases) * cfg_.slots_per_lease;
+    auto st = host_mapped_alloc(nslots * cfg_.slot_bytes);
+    if (!st.ok()) return st.status();
+    staging_ = st.value();
+    auto pr = host_mapped_alloc(nslots * nvme::kMemoryPageBytes);
+    if (!pr.ok()) return pr.status();
+    prp_ = pr.value();
+    if (!staging_.device || !prp_.device)
+        return {StatusCode::UNSUPPORTED, "nvme-gpu needs a CUDA device (device-mapped host memory)"};
+    // Same bus address on every controller (identity IOMMU / pass-through).
+    for (std::size_t d = 0; d < devs_.size(); ++d) {
+        auto a = devs_[d].controller->map_dma(staging_.host, staging_.bytes);
+        auto b = devs_[d].controller->map_dma(prp_.host, prp_.bytes);
+        if (!a.ok()) return a.status();
+        if (!b.ok()) return b.status();
+        if (d == 0) {
+            staging_iova_ = a.value();
+            prp_iova_ = b.value();
+        } else if (a.value() != staging_iova_ || b.value() != prp_iova_) {
+            return {StatusCode::UNSUPPORTED, "controllers disagree on DMA addresses of the staging arena"};
+        }
+    }
+    // Prebuilt PRP lists: page j of slot i.
+    auto* lists = static_cast<std::uint64_t*>(prp_.host);
+    const std::uint64_t pages_per_slot = cfg_.slot_bytes / nvme::kMemoryPageBytes;
+    for (std::uint64_t i = 0; i < nslots; ++i)
+        for (std::uint64_t j = 0; j < pages_per_slot; ++j)
+            lists[i * 512 + j] = staging_iova_ + i * cfg_.slot_bytes + j * nvme::kMemoryPageBytes;
+
+    std::vector<io::DevDevice> rows(devs_.size());
+    for (std::size_t d = 0; d < devs_.size(); ++d) {
+        auto& ctl = *devs_[d].controller;
+        std::vector<nvme::QueuePairView> views(cfg_.leases);
+        for (std::uint32_t l = 0; l < cfg_.leases; ++l) views[l] = ctl.device_queue(l);
+        nvme::QueuePairView* dv = nullptr;
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&dv, views.size() * sizeof(views[0])), "cudaMalloc queues"));
+        TUTTI_RETURN_IF_ERROR(cuda_status(
+            cudaMemcpy(dv, views.data(), views.size() * sizeof(views[0]), cudaMemcpyHostToDevice), "upload queues"));
+        d_queue_views_.push_back(dv);
+        std::vector<io::QueueCursor> curs(cfg_.leases, io::QueueCursor{0, 0, 1, 0});
+        io::QueueCursor* dc = nullptr;
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&dc, curs.size() * sizeof(curs[0])), "cudaMalloc cursors"));
+        TUTTI_RETURN_IF_ERROR(cuda_status(
+            cudaMemcpy(dc, curs.data(), curs.size() * sizeof(curs[0]), cudaMemcpyHostToDevice), "upload cursors"));
+        d_cursors_.push_back(dc);
+        std::uint32_t lba = ctl.info().lba_bytes, shift = 0;
+        while ((1u << shift) < lba) ++shift;
+        rows[d] = io::DevDevice{dv, dc, shift, ctl.info().mdts_bytes, cfg_.leases, ctl.info().nsid};
+    }
+    TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_devices_, rows.size() * sizeof(rows[0])), "cudaMalloc devices"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(
+        cudaMemcpy(d_devices_, rows.data(), rows.size() * sizeof(rows[0]), cudaMemcpyHostToDevice), "upload devices"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_targets_, std::size_t(cfg_.max_targets) * sizeof(io::DevTarget)),
+                                      "cudaMalloc targets"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(
+        cudaMemset(d_targets_, 0, std::size_t(cfg_.max_targets) * sizeof(io::DevTarget)), "memset targets"));
+    for (std::uint32_t l = cfg_.leases; l-- > 0;) free_leases_.push_back(l);
+    return Status::Ok();
+}
+
+Status GpuNvmeDataPath::shutdown(std::uint64_t) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (!initialized_) return Status::Ok();
+    DeviceGuard guard(cfg_.accel_id);
+    for (auto& kv : ops_)
+        if (kv.second->arena && kv.second->arena->event) cudaEventSynchronize(kv.second->arena->event);
+    for (auto& kv : ops_)
+        if (kv.second->arena) arena_pool_.push_back(std::move(kv.second->arena));
+    ops_.clear();
+    for (auto& a : arena_pool_) {
+        if (a->event) cudaEventDestroy(a->event);
+        if (a->host) cudaFreeHost(a->host);
+        if (a->dev) cudaFree(a->dev);
+    }
+    arena_pool_.clear();
+    for (auto* p : d_queue_views_) cudaFree(p);
+    for (auto* p : d_cursors_) cudaFree(p);
+    for (auto* p : extent_chunks_) cudaFree(p);
+    d_queue_views_.clear();
+    d_cursors_.clear();
+    extent_chunks_.clear();
+    if (d_devices_) cudaFree(d_devices_);
+    if (d_targets_) cudaFree(d_targets_);
+    d_devices_ = nullptr;
+    d_targets_ = nullptr;
+    for (auto& d : devs_) {
+        if (staging_.host) d.controller->unmap_dma(staging_iova_);
+        if (prp_.host) d.controller->unmap_dma(prp_iova_);
+    }
+    host_mapped_free(staging_);
+    host_mapped_free(prp_);
+    initialized_ = false;
+    return Status::Ok();
+}
+
+Result<DataPathTarget> GpuNvmeDataPath::open(const ResolvedTarget& target) {
+    using R = Result<DataPathTarget>;
+    auto pv = target.view<FileExtentPayload>(kFileExtentPayloadType, kFileExtentPayloadVersion);
+    if (!pv.ok()) return R::Failure(pv.status());
+    const FileExtentPayload& p = *pv.value();
+    std::lock_guard<std::mutex> g(mu_);
+    if (!initialized_) return R::Failure({StatusCode::NOT_READY, "not initialized"});
+    if (p.extents.empty() && p.file_size > 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "no extents"});
+    for (const auto& e : p.extents)
+        if (e.device >= devs_.size())
+            return R::Failure({StatusCode::INVALID_ARGUMENT, "extent names device " + std::to_string(e.device) +
+                                                                 " beyond the device table"});
+    DeviceGuard guard(cfg_.accel_id);
+    // Back the namespace ranges on emulated controllers.
+    for (std::size_t d = 0; d < devs_.size(); ++d) {
+        auto* emu = dynamic_cast<nvme::EmulatedNvmeController*>(devs_[d].controller.get());
+        if (!emu) continue;
+        std::vector<nvme::BackingRange> ranges;
+        for (const auto& e : p.extents)
+            if (e.device == d) ranges.push_back({e.physical, e.length, e.logical});
+        if (!ranges.empty()) TUTTI_RETURN_IF_ERROR_R(R, emu->attach_file(p.path, ranges));
+    }
+    std::uint32_t row;
+    if (!free_target_rows_.empty()) {
+        row = free_target_rows_.back();
+        free_target_rows_.pop_back();
+    } else {
+        if (targets_.size() >= cfg_.max_targets) return R::Failure({StatusCode::RESOURCE_EXHAUSTED, "target table full"});
+        row = static_cast<std::uint32_t>(targets_.size());
+        targets_.emplace_back();
+    }
+    // Extents into the HBM pool (bump allocation in 16 MiB chunks).
+    std::vector<io::DevExtent> ex(p.extents.size());
+    for (std::size_t i = 0; i < ex.size(); ++i)
+        ex[i] = io::DevExtent{p.extents[i].logical, p.extents[i].physical, p.extents[i].length, p.extents[i].device, 0};
+    const std::size_t need = align_up(std::max<std::size_t>(1, ex.size()) * sizeof(io::DevExtent), 256);
+    if (need > kExtentChunkBytes) return R::Failure({StatusCode::RESOURCE_EXHAUSTED, "too many extents"});
+    if (extent_chunks_.empty() || extent_chunk_used_ + need > kExtentChunkBytes) {
+        char* c = nullptr;
+        Status s = cuda_status(cudaMalloc(&c, kExtentChunkBytes), "cudaMalloc extents");
+        if (!s.ok()) return R::Failure(s);
+        extent_chunks_.push_back(c);
+        extent_chunk_used_ = 0;
+    }
+    auto* dex = reinterpret_cast<io::DevExtent*>(extent_chunks_.back() + extent_chunk_used_);
+    extent_chunk_used_ += need;
+    if (!ex.empty()) {
+        Status s = cuda_status(cudaMemcpy(dex, ex.data(), ex.size() * sizeof(ex[0]), cudaMemcpyHostToDevice),
+                               "upload extents");
+        if (!s.ok()) return R::Failure(s);
+    }
+    TargetRec& tr = targets_[row];
+    tr.generation = next_token_++;
+    tr.row = row;
+    tr.size = p.file_size;
+    tr.path = p.path;
+    tr.open = true;
+    io::DevTarget dt{dex, p.file_size, static_cast<std::uint32_t>(ex.size()),
+                     static_cast<std::uint32_t>(tr.generation), 0};
+    Status s = cuda_status(cudaMemcpy(d_targets_ + row, &dt, sizeof(dt), cudaMemcpyHostToDevice), "upload target");
+    if (!s.ok()) return R::Failure(s);
+    return DataPathTarget{row, tr.generation};
+}
+
+Status GpuNvmeDataPath::close(DataPathTarget t) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (t.token >= targets_.size() || targets_[t.token].generation != t.generation || !targets_[t.token].open)
+        return {StatusCode::NOT_FOUND, "unknown target"};
+    targets_[t.token].open = false;
+    targets_[t.token].generation = 0;
+    free_target_rows_.push_back(static_cast<std::uint32_t>(t.token));
+    DeviceGuard guard(cfg_.accel_id);
+    io::DevTarget zero{};
+    return cuda_status(cudaMemcpy(d_targets_ + t.token, &zero, sizeof(zero), cudaMemcpyHostToDevice), "clear target");
+}
+
+Result<RegistrationDomainKey> GpuNvmeDataPath::registration_domain(DataPathTarget) const {
+    return RegistrationDomainKey{"nvme-gpu:" + std::to_string(cfg_.accel_id)};
+}
+
+Result<DataPathMemory> GpuNvmeDataPath::register_memory(const DataPathMemoryView& v, const RegistrationDomainKey&) {
+    using R = Result<DataPathMemory>;
+    if (!v.base || v.size_bytes == 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "empty memory"});
+    if (reinterpret_cast<std::uintptr_t>(v.base) % 16)
+        return R::Failure({StatusCode::INVALID_ARGUMENT, "memory base must be 16-byte aligned"});
+    std::lock_guard<std::mutex> g(mu_);
+    if (v.kind == DataPathMemoryKind::DEVICE && v.expected_accel_id >= 0 && v.expected_accel_id != cfg_.accel_id)
+        return R::Failure({StatusCode::INVALID_ARGUMENT, "memory belongs to another accelerator"});
+    std::uint64_t tok = next_token_++;
+    memories_[tok] = MemoryRec{tok, static_cast<char*>(v.base), v.size_bytes, v.kind};
+    return DataPathMemory{tok, tok};
+}
+
+Status GpuNvmeDataPath::unregister_memory(DataPathMemory m) {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = memories_.find(m.token);
+    if (it == memories_.end() || it->second.generation != m.generation) return {StatusCode::NOT_FOUND, "unknown memory"};
+    memories_.erase(it);
+    return Status::Ok();
+}
+
+Result<std::unique_ptr<GpuNvmeDataPath::Arena>> GpuNvmeDataPath::take_arena(std::size_t bytes) {
+    using R = Result<std::unique_ptr<Arena>>;
+    for (std::size_t i = 0; i < arena_pool_.size(); ++i) {
+        if (arena_pool_[i]->capacity >= bytes) {
+            auto a = std::move(arena_pool_[i]);
+            arena_pool_.erase(arena_pool_.begin() + i);
+            return R(std::move(a));
+        }
+    }
+    auto a = std::make_unique<Arena>();
+    a->capacity = align_up(std::max<std::size_t>(bytes, 1u << 20), 1u << 20);
+    Status s = cuda_status(cudaHostAlloc(reinterpret_cast<void**>(&a->host), a->capacity, cudaHostAllocDefault),
+                           "cudaHostAlloc arena");
+    if (!s.ok()) return R::Failure(s);
+    s = cuda_status(cudaMalloc(&a->dev, a->capacity), "cudaMalloc arena");
+    if (!s.ok()) {
+        cudaFreeHost(a->host);
+        return R::Failure(s);
+    }
+    s = cuda_status(cudaEventCreateWithFlags(&a->event, cudaEventDisableTiming), "cudaEventCreate");
+    if (!s.ok()) {
+        cudaFreeHost(a->host);
+        cudaFree(a->dev);
+        return R::Failure(s);
+    }
+    return R(std::move(a));
+}
+
+void GpuNvmeDataPath::return_arena(std::unique_ptr<Arena> a) {
+    if (a) arena_pool_.push_back(std::move(a));
+}
+
+SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t count, const HostSubmitContext& ctx) {
+    SubmitOutcome out;
+    out.initial_states.resize(count);
+    if (count == 0) return out;
+    std::lock_guard<std::mutex> g(mu_);
+    auto reject_all = [&](Status s) {
+        for (auto& st : out.initial_states) st = {IoRequestState::REJECTED, s};
+        out.status = s;
+        return out;
+    };
+    if (!initialized_) return reject_all({StatusCode::NOT_READY, "not initialized"});
+    if (ctx.execution_domain != ExecutionDomain::DEVICE_EXECUTION)
+        return reject_all({StatusCode::UNSUPPORTED, "nvme-gpu executes on the device"});
+
+    const std::uint64_t lba = caps_.length_alignment_bytes;
+    auto op = std::make_unique<OpRec>();
+    std::vector<io::IoCommand> cmds;
+    std::vector<io::IoPiece> pieces;
+    cmds.reserve(count / 8 + 1);
+    pieces.reserve(count + 16);
+    op->cmd_first_piece.reserve(count / 8 + 1);
+    op->piece_req.reserve(count + 16);
+    Status first_reject;
+    std::size_t accepted = 0;
+
+    for (std::size_t i = 0; i < count; ++i) {
+        const DataPathRequest& r = reqs[i];
+        const IoRequest& in = r.intent;
+        auto mit = memories_.find(r.memory.token);
+        Status bad;
+        if (mit == memories_.end() || mit->second.generation != r.memory.generation)
+            bad = {StatusCode::NOT_FOUND, "unknown memory"};
+        else if (r.target.token >= targets_.size() || targets_[r.target.token].generation != r.target.generation ||
+                 !targets_[r.target.token].open)
+            bad = {StatusCode::NOT_FOUND, "unknown target"};
+        else if (in.length == 0 || in.length % lba || in.target_offset % lba)
+            bad = {StatusCode::INVALID_ARGUMENT, "offset/length must be LBA aligned"};
+        else if (in.memory_offset + in.length > mit->second.size)
+            bad = {StatusCode::OUT_OF_RANGE, "memory range"};
+        else if (in.target_offset + in.length > targets_[r.target.token].size)
+            bad = {StatusCode::OUT_OF_RANGE, "target range"};
+        else if ((reinterpret_cast<std::uintptr_t>(mit->second.base) + in.memory_offset) % 16)
+            bad = {StatusCode::INVALID_ARGUMENT, "memory address must be 16-byte aligned"};
+        if (!bad.ok()) {
+            out.initial_states[i] = {IoRequestState::REJECTED, bad};
+            if (first_reject.ok()) first_reject = bad;
+            continue;
+        }
+        out.initial_states[i] = {IoRequestState::ACCEPTED, Status::Ok()};
+        const std::uint32_t req_idx = static_cast<std::uint32_t>(accepted++);
+        op->req_input_index.push_back(static_cast<std::uint32_t>(i));
+        op->req_bytes.push_back(in.length);
+        const std::uint32_t opcode = in.direction == IoDirection::READ ? nvme::kOpRead : nvme::kOpWrite;
+        std::uint64_t done = 0;
+        while (done < in.length) {
+            const std::uint64_t lo = in.target_offset + done;
+            bool extend = false;
+            if (!cmds.empty()) {
+                const io::IoCommand& c = cmds.back();
+                extend = c.opcode == opcode && c.target == r.target.token && c.logical + c.bytes == lo &&
+                         c.bytes < cmd_bytes_ && c.n_pieces < cfg_.max_pieces_per_cmd;
+            }
+            if (!extend) {
+                io::IoCommand c{};
+                c.logical = lo;
+                c.target = static_cast<std::uint32_t>(r.target.token);
+                c.bytes = 0;
+                c.first_piece = static_cast<std::uint32_t>(pieces.size());
+                c.n_pieces = 0;
+                c.opcode = opcode;
+                cmds.push_back(c);
+                op->cmd_first_piece.push_back(c.first_piece);
+            }
+            io::IoCommand& c = cmds.back();
+            const std::uint64_t n = std::min<std::uint64_t>(in.length - done, cmd_bytes_ - c.bytes);
+            pieces.push_back(io::IoPiece{reinterpret_cast<std::uint64_t>(mit->second.base + in.memory_offset + done),
+                                         c.bytes, static_cast<std::uint32_t>(n)});
+            op->piece_req.push_back(req_idx);
+            c.bytes += static_cast<std::uint32_t>(n);
+            c.n_pieces += 1;
+            done += n;
+        }
+        op->bytes += in.length;
+    }
+    if (accepted == 0) {
+        out.status = first_reject;
+        return out;
+    }
+    const std::uint32_t n_cmds = static_cast<std::uint32_t>(cmds.size());
+    std::uint32_t want = std::min<std::uint32_t>(cfg_.max_ctas_per_op, n_cmds);
+    std::uint32_t take = std::min<std::uint32_t>(want, static_cast<std::uint32_t>(free_leases_.size()));
+    if (take == 0) return reject_all({StatusCode::BUSY, "all queue leases are held by in-flight operations"});
+
+    DeviceGuard guard(cfg_.accel_id);
+    // Arena layout: cmds | pieces | lease ids | cursor | status | timing
+    const std::size_t off_cmds = 0;
+    const std::size_t off_pieces = align_up(off_cmds + cmds.size() * sizeof(io::IoCommand), 256);
+    const std::size_t off_leases = align_up(off_pieces + pieces.size() * sizeof(io::IoPiece), 256);
+    const std::size_t off_cursor = align_up(off_leases + take * sizeof(std::uint32_t), 256);
+    const std::size_t off_status = align_up(off_cursor + 16, 256);
+    const std::size_t off_timing = align_up(off_status + n_cmds * sizeof(std::uint32_t), 256);
+    const bool timing = cfg_.timing;
+    const std::size_t total = off_timing + (timing ? n_cmds * 4 * sizeof(std::uint64_t) : 0);
+    auto ar = take_arena(total);
+    if (!ar.ok()) return reject_all(ar.status());
+    std::unique_ptr<Arena> arena = std::move(ar).value();
+    char* h = arena->host;
+    std::memcpy(h + off_cmds, cmds.data(), cmds.size() * sizeof(io::IoCommand));
+    std::memcpy(h + off_pieces, pieces.data(), pieces.size() * sizeof(io::IoPiece));
+    for (std::uint32_t k = 0; k < take; ++k) {
+        op->leases.push_back(free_leases_.back());
+        free_leases_.pop_back();
+    }
+    std::memcpy(h + off_leases, op->leases.data(), take * sizeof(std::uint32_t));
+    std::memset(h + off_cursor, 0, 16);
+    auto* hst = reinterpret_cast<std::uint32_t*>(h + off_status);
+    for (std::uint32_t k = 0; k < n_cmds; ++k) hst[k] = io::kCmdNotRun;
+
+    io::IoKernelParams kp{};
+    char* d = arena->dev;
+    kp.cmds = reinterpret_cast<const io::IoCommand*>(d + off_cmds);
+    kp.pieces = reinterpret_cast<const io::IoPiece*>(d + off_pieces);
+    kp.n_cmds = n_cmds;
+    kp.n_devices = static_cast<std::uint32_t>(devs_.size());
+    kp.cursor = reinterpret_cast<std::uint32_t*>(d + off_cursor);
+    kp.cmd_status = reinterpret_cast<std::uint32_t*>(d + off_status);
+    kp.targets = d_targets_;
+    kp.devices = d_devices_;
+    kp.lease_ids = reinterpret_cast<const std::uint32_t*>(d + off_leases);
+    kp.staging_dev = static_cast<char*>(staging_.device);
+    kp.staging_iova = staging_iova_;
+    kp.prp_iova = prp_iova_;
+    kp.slot_bytes = cfg_.slot_bytes;
+    kp.slots_per_lease = cfg_.slots_per_lease;
+    kp.timeout_ns = cfg_.timeout_ns;
+    kp.timing = timing ? reinterpret_cast<std::uint64_t*>(d + off_timing) : nullptr;
+
+    cudaStream_t s = ctx.stream;
+    Status cs = cuda_status(cudaMemcpyAsync(d, h, off_timing, cudaMemcpyHostToDevice, s), "H2D commands");
+    if (cs.ok()) cs = cuda_status(io::launch_nvme_io(kp, take, s), "io kernel launch");
+    if (cs.ok())
+        cs = cuda_status(cudaMemcpyAsync(h + off_status, d + off_status, total - off_status, cudaMemcpyDeviceToHost, s),
+                         "D2H status");
+    if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->event, s), "event record");
+    if (!cs.ok()) {
+        // Nothing irreversible is known to have happened if the launch failed;
+        // report every request rejected and return the leases.
+        cudaStreamSynchronize(s);
+        for (auto l : op->leases) free_leases_.push_back(l);
+        return_arena(std::move(arena));
+        return reject_all(cs);
+    }
+    op->arena = std::move(arena);
+    op->n_cmds = n_cmds;
+    op->status_off = off_status;
+    op->timing_off = off_timing;
+    op->timing = timing;
+    op->generation = next_token_++;
+    const std::uint64_t tok = op->generation;
+    ops_[tok] = std::move(op);
+    out.op = DataPathOp{tok, tok};
+    out.status = first_reject;  // non-OK when partially rejected
+    return out;
+}
+
+Status GpuNvmeDataPath::reset_dirty_queues(const std::vector<std::uint32_t>& leases) {
+    for (std::size_t d = 0; d < devs_.size(); ++d) {
+        for (auto l : leases) {
+            io::QueueCursor c{};
+            TUTTI_RETURN_IF_ERROR(
+                cuda_status(cudaMemcpy(&c, d_cursors_[d] + l, sizeof(c), cudaMemcpyDeviceToHost), "read cursor"));
+            if (!c.dirty) continue;
+            TUTTI_RETURN_IF_ERROR(devs_[d].controller->reset_queue(l));
+            io::QueueCursor fresh{0, 0, 1, 0};
+            TUTTI_RETURN_IF_ERROR(
+                cuda_status(cudaMemcpy(d_cursors_[d] + l, &fresh, sizeof(fresh), cudaMemcpyHostToDevice), "reset cursor"));
+        }
+    }
+    return Status::Ok();
+}
+
+void GpuNvmeDataPath::finish_op(OpRec& op) {
+    const auto* st = reinterpret_cast<const std::uint32_t*>(op.arena->host + op.status_off);
+    std::vector<char> req_failed(op.req_bytes.size(), 0);
+    IoCompletionDetail det;
+    bool any_fail = false, any_timeout_or_notrun = false;
+    for (std::uint32_t c = 0; c < op.n_cmds; ++c) {
+        const std::uint32_t code = st[c];
+        if (code == io::kCmdOk) continue;
+        any_fail = true;
+        const std::uint32_t kind = code & 0xFFFF0000u;
+        if (det.first_failed_entry == UINT32_MAX) {
+            det.first_failed_entry = c;
+            det.failure_kind = kind == io::kCmdResolve || kind == io::kCmdBadDevice ? IoFailureKind::RESOLVE_LBA
+                               : kind == io::kCmdTimeout                           ? IoFailureKind::CQ_TIMEOUT
+                               : kind == io::kCmdNvme                              ? IoFailureKind::NVME_CQ_ERROR
+                                                                                   : IoFailureKind::UNKNOWN;
+            det.raw_cq_status = code & 0xFFFFu;
+        }
+        if (kind == io::kCmdTimeout || kind == io::kCmdNotRun) any_timeout_or_notrun = true;
+        if (kind == io::kCmdTimeout) det.timeout_seen = true;
+        const std::uint32_t p0 = op.cmd_first_piece[c];
+        const std::uint32_t p1 = c + 1 < op.n_cmds ? op.cmd_first_piece[c + 1] : static_cast<std::uint32_t>(op.piece_req.size());
+        for (std::uint32_t p = p0; p < p1; ++p) req_failed[op.piece_req[p]] = 1;
+    }
+    for (std::size_t r = 0; r < req_failed.size(); ++r) {
+        if (req_failed[r])
+            det.failed_request_indices.push_back(op.req_input_index[r]);
+        else
+            det.confirmed_bytes += op.req_bytes[r];
+    }
+    if (any_fail) det.failure_scope = IoFailureScope::REQUEST_INDICES;
+    op.detail = std::move(det);
+    if (any_timeout_or_notrun) {
+        Status rs = reset_dirty_queues(op.leases);
+        (void)rs;
+    }
+    for (auto l : op.leases) free_leases_.push_back(l);
+    op.leases.clear();
+    op.state = any_fail ? IoState::FAILED : IoState::COMPLETED;
+    op.status = any_fail ? Status(StatusCode::DEVICE_ERROR,
+                                  std::to_string(op.detail.failed_request_indices.size()) + " request(s) failed")
+                         : Status::Ok();
+    if (op.timing) {
+        const auto* t = reinterpret_cast<const std::uint64_t*>(op.arena->host + op.timing_off);
+        std::vector<double> qw, dev, mv, tot;
+        for (std::uint32_t c = 0; c < op.n_cmds; ++c) {
+            const std::uint64_t* s = t + 4ull * c;
+            if (!s[0] || !s[3]) continue;
+            qw.push_back((s[1] - s[0]) / 1e3);
+            dev.push_back((s[2] - s[1]) / 1e3);
+            mv.push_back((s[3] - s[2]) / 1e3);
+            tot.push_back((s[3] - s[0]) / 1e3);
+        }
+        IoTimingSummary ts;
+        ts.commands = tot.size();
+        ts.queue_wait_us_p50 = percentile(qw, 0.5);
+        ts.move_us_p50 = percentile(mv, 0.5);
+        std::vector<double> dev2 = dev, tot2 = tot;
+        ts.device_us_p50 = percentile(dev, 0.5);
+        ts.device_us_p99 = percentile(dev2, 0.99);
+        ts.total_us_p50 = percentile(tot, 0.5);
+        ts.total_us_p99 = percentile(tot2, 0.99);
+        last_timing_ = ts;
+    }
+}
+
+Result<ProgressResult> GpuNvmeDataPath::progress(ProgressBudget budget) {
+    std::lock_guard<std::mutex> g(mu_);
+    ProgressResult pr;
+    DeviceGuard guard(cfg_.accel_id);
+    for (auto& kv : ops_) {
+        OpRec& op = *kv.second;
+        if (op.state != IoState::IN_FLIGHT) continue;
+        if (budget.max_work_units && pr.work_units_consumed >= budget.max_work_units) {
+            pr.more_work_likely = true;
+            break;
+        }
+        ++pr.work_units_consumed;
+        cudaError_t e = cudaEventQuery(op.arena->event);
+        if (e == cudaErrorNotReady) {
+            pr.more_work_likely = true;
+            continue;
+        }
+        ++pr.operations_advanced;
+        ++pr.operations_terminal;
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            op.state = IoState::FAILED;
+            op.status = {StatusCode::DEVICE_ERROR, std::string("event query: ") + cudaGetErrorString(e)};
+            op.detail.failure_kind = IoFailureKind::CUDA_QUERY_ERROR;
+            op.detail.failure_scope = IoFailureScope::WHOLE_OPERATION;
+            continue;  // leases stay held: the device state is unknown
+        }
+        finish_op(op);
+    }
+    return pr;
+}
+
+Result<DataPathSnapshot> GpuNvmeDataPath::query(DataPathOp op) const {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = ops_.find(op.token);
+    if (it == ops_.end() || it->second->generation != op.generation)
+        return Result<DataPathSnapshot>::Failure({StatusCode::NOT_FOUND, "unknown op"});
+    DataPathSnapshot s;
+    s.state = it->second->state;
+    s.status = it->second->status;
+    s.bytes_transferred = s.state == IoState::IN_FLIGHT ? 0 : it->second->detail.confirmed_bytes;
+    s.detail = it->second->detail;
+    return s;
+}
+
+Status GpuNvmeDataPath::release(DataPathOp op) {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = ops_.find(op.token);
+    if (it == ops_.end() || it->second->generation != op.generation) return {StatusCode::NOT_FOUND, "unknown op"};
+    if (it->second->state == IoState::IN_FLIGHT) return {StatusCode::BUSY, "op still in flight"};
+    return_arena(std::move(it->second->arena));
+    ops_.erase(it);
+    return Status::Ok();
+}
+
+Status GpuNvmeDataPath::enqueue_wait(const DataPathOp* ops, std::size_t count, cudaStream_t stream) {
+    std::lock_guard<std::mutex> g(mu_);
+    DeviceGuard guard(cfg_.accel_id);
+    for (std::size_t i = 0; i < count; ++i) {
+        auto it = ops_.find(ops[i].token);
+        if (it == ops_.end() || it->second->generation != ops[i].generation) return {StatusCode::NOT_FOUND, "unknown op"};
+        if (!it->second->arena) continue;  // already terminal and released
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaStreamWaitEvent(stream, it->second->arena->event, 0), "stream wait"));
+    }
+    return Status::Ok();
+}
+
+IoTimingSummary GpuNvmeDataPath::last_timing() const {
+    std::lock_guard<std::mutex> g(mu_);
+    return last_timing_;
+}
+
+std::uint32_t GpuNvmeDataPath::free_leases() const {
+    std::lock_guard<std::mutex> g(mu_);
+    return static_cast<std::uint32_t>(free_leases_.size());
+}
+
+}  // namespace tutti

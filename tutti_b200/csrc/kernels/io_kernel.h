@@ -1,0 +1,114 @@
+#pragma once
+// Device-side data structures and launch entry points of the GPU NVMe io path.
+//
+// One launch per submit. Each CTA owns one queue pair per device (its "lease"):
+// no SQ/CQ state is shared between CTAs, so the submit/poll path needs no
+// global atomics except one work-stealing cursor over the command list.
+// A command is a contiguous logical range of one target (<= one staging slot);
+// it carries a list of pieces that say where each byte range of the command
+// lives in caller memory, so the paged-KV scatter (read) and gather (write)
+// happen inside the io kernel, between the staging slot and HBM.
+//
+// Parity: this replaces the reference's fused_submit_kernel_pool
+// (csrc/data_paths/striped_local_nvme/fused_submit_kernel.cuh:171-218) plus its
+// separate single_layer_kv_transfer_kernel (csrc/kv_transfer/src/mem_kernels.cu:66-130);
+// per-entry status codes follow EntryCompletionStatus (0 ok, 1 resolve,
+// 2 timeout, 3 NVMe error) from submit_one.cuh:117-143.
+
+#include <cstdint>
+
+#include <cuda_runtime_api.h>
+
+#include "../nvme/nvme_spec.h"
+#include "../nvme/controller.h"
+
+namespace tutti {
+namespace io {
+
+constexpr int kMaxSlots = 16;     // staging slots per CTA
+constexpr int kMaxSub = 8;        // NVMe commands per staging slot (extent/MDTS splits)
+constexpr int kMaxDevices = 8;    // devices (controllers) one launch can drive
+constexpr int kIoThreads = 512;   // threads per CTA
+
+struct IoCommand {  // 32 B
+    std::uint64_t logical;      // byte offset in the target
+    std::uint32_t target;       // row of the device-resident target table
+    std::uint32_t bytes;        // <= slot_bytes
+    std::uint32_t first_piece;
+    std::uint32_t n_pieces;
+    std::uint32_t opcode;       // nvme::kOpRead / kOpWrite
+    std::uint32_t pad;
+};
+
+struct IoPiece {  // 16 B
+    std::uint64_t mem;     // device-visible address in caller memory
+    std::uint32_t off;     // byte offset within the command
+    std::uint32_t bytes;
+};
+
+struct DevExtent {  // 32 B
+    std::uint64_t logical;
+    std::uint64_t physical;
+    std::uint64_t length;
+    std::uint32_t device;
+    std::uint32_t pad;
+};
+
+struct DevTarget {  // 32 B, device-resident file handle
+    const DevExtent* extents;
+    std::uint64_t size;
+    std::uint32_t n_extents;
+    std::uint32_t generation;
+    std::uint64_t pad;
+};
+
+struct QueueCursor {  // persisted per (device, lease) across launches
+    std::uint32_t sq_tail;
+    std::uint32_t cq_head;
+    std::uint32_t phase;
+    std::uint32_t dirty;  // a launch ended with commands still owned by the controller
+};
+
+struct DevDevice {
+    const nvme::QueuePairView* queues;  // indexed by lease
+    QueueCursor* cursors;               // indexed by lease
+    std::uint32_t lba_shift;
+    std::uint32_t mdts_bytes;
+    std::uint32_t n_queues;
+    std::uint32_t nsid;
+};
+
+// Per-command status words written by the kernel.
+enum : std::uint32_t {
+    kCmdOk = 0,
+    kCmdResolve = 1u << 16,
+    kCmdTimeout = 2u << 16,
+    kCmdNvme = 3u << 16,      // | raw NVMe status field
+    kCmdNotRun = 4u << 16,
+    kCmdBadDevice = 5u << 16,
+};
+
+struct IoKernelParams {
+    const IoCommand* cmds;
+    const IoPiece* pieces;
+    std::uint32_t n_cmds;
+    std::uint32_t n_devices;
+    std::uint32_t* cursor;        // work-stealing index, zero at launch
+    std::uint32_t* cmd_status;    // n_cmds words, preset to kCmdNotRun
+    const DevTarget* targets;
+    const DevDevice* devices;     // n_devices rows (device memory)
+    const std::uint32_t* lease_ids;  // gridDim.x leases
+    char* staging_dev;            // device address of the staging arena
+    std::uint64_t staging_iova;   // bus address of the same arena
+    std::uint64_t prp_iova;       // bus address of the PRP-list pages (one page per slot)
+    std::uint32_t slot_bytes;     // <= 2 MiB (one PRP-list page per slot)
+    std::uint32_t slots_per_lease;
+    std::uint64_t timeout_ns;     // per command, from submission
+    std::uint64_t* timing;        // optional: 4 %globaltimer stamps per command
+};
+
+// Launches the fused io kernel on `stream` with one CTA per lease.
+cudaError_t launch_nvme_io(const IoKernelParams& p, std::uint32_t n_leases, cudaStream_t stream);
+
+}  // namespace io
+}  // namespace tutti

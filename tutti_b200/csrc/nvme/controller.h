@@ -1,0 +1,183 @@
+#pragma once
+// NVMe controller providers behind one queue protocol.
+//
+// The GPU io kernel always speaks NVMe: it writes 64-byte SQEs into an SQ ring,
+// rings the SQ tail doorbell, polls CQE phase bits and rings the CQ head
+// doorbell. Which "drive" answers is a provider:
+//   * EmulatedNvmeController: host threads own the rings (page-locked, mapped
+//     into the GPU), execute READ/WRITE/FLUSH against file-backed namespace
+//     ranges with pread/pwrite and post CQEs. Used where no user-owned NVMe
+//     queues exist (no queue-leasing kernel driver, no bindable drives).
+//   * A real controller leased from the queue broker would expose the same
+//     QueuePairView with BAR0 doorbells; it needs a queue-owning kernel driver
+//     and is reported UNSUPPORTED when none is present.
+//
+// Parity: queue memory layout and doorbell stride follow the reference's
+// libnvm queue structs (csrc/device_manager/nvme/libnvm/include/nvm_types.h) and
+// NvmeQueueGroup (csrc/data_paths/local_nvme/io/nvme_queue_group.cu:131-217).
+
+#include <atomic>
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <tutti/status.h>
+
+#include "host_memory.h"
+#include "nvme_spec.h"
+
+namespace tutti {
+namespace nvme {
+
+// Device-visible view of one I/O queue pair; POD, copied into GPU memory.
+struct QueuePairView {
+    Sqe* sq;                    // SQ ring (depth entries)
+    const Cqe* cq;              // CQ ring (depth entries)
+    std::uint32_t* sq_doorbell;
+    std::uint32_t* cq_doorbell;
+    std::uint32_t depth;
+    std::uint32_t qid;
+    std::uint32_t nsid;
+    std::uint32_t pad;
+};
+
+struct ControllerInfo {
+    std::string name;
+    std::string kind;            // "emulated" | "snvme"
+    std::uint32_t lba_bytes = 512;
+    std::uint32_t mdts_bytes = 1u << 20;
+    std::uint32_t queue_depth = 256;  // CAP.MQES + 1
+    std::uint32_t num_io_queues = 0;
+    std::uint32_t nsid = 1;
+    std::uint64_t namespace_bytes = 0;
+};
+
+// One backing range of an emulated namespace: namespace bytes
+// [ns_offset, ns_offset + length) hold file bytes [file_offset, ...).
+struct BackingRange {
+    std::uint64_t ns_offset;
+    std::uint64_t length;
+    std::uint64_t file_offset;
+};
+
+struct ControllerStats {
+    std::uint64_t commands = 0;
+    std::uint64_t read_bytes = 0;
+    std::uint64_t write_bytes = 0;
+    std::uint64_t errors = 0;
+    std::uint64_t injected = 0;
+};
+
+// Fault seams for failure-detection tests (host side only; nothing faults a GPU).
+enum class InjectKind : std::uint32_t {
+    NONE = 0,
+    MEDIA_ERROR = 1,    // complete the next N commands with an unrecovered read error
+    DROP_COMPLETION = 2,  // execute but never post a CQE for the next N commands
+    DELAY = 3,          // delay the next N commands by delay_us
+};
+
+class NvmeController {
+public:
+    virtual ~NvmeController() = default;
+    virtual const ControllerInfo& info() const = 0;
+    // Device-side pointers (GPU submitter).
+    virtual QueuePairView device_queue(std::uint32_t i) const = 0;
+    // Host-side pointers (host submitter, tests).
+    virtual QueuePairView host_queue(std::uint32_t i) const = 0;
+    // Make [ptr, ptr+bytes) DMA-reachable by the controller; returns its bus address.
+    virtual Result<std::uint64_t> map_dma(void* host_ptr, std::uint64_t bytes) = 0;
+    virtual Status unmap_dma(std::uint64_t iova) = 0;
+    // Quiesce queue i and reset its head/tail/phase (after a timeout).
+    virtual Status reset_queue(std::uint32_t i) = 0;
+    virtual ControllerStats stats() const = 0;
+};
+
+struct EmulatedControllerConfig {
+    std::string name = "emu0";
+    std::uint32_t num_io_queues = 64;
+    std::uint32_t queue_depth = 256;
+    std::uint32_t lba_bytes = 512;
+    std::uint32_t mdts_bytes = 1u << 20;
+    std::uint32_t worker_threads = 4;
+    bool direct_io = false;            // O_DIRECT on backing files
+    std::uint64_t namespace_bytes = 1ull << 46;
+    std::uint32_t idle_spin_iters = 2000;  // polls before a worker sleeps
+    std::uint32_t idle_sleep_us = 20;
+};
+
+class EmulatedNvmeController final : public NvmeController {
+public:
+    static Result<std::unique_ptr<EmulatedNvmeController>> create(const EmulatedControllerConfig& cfg);
+    ~EmulatedNvmeController() override;
+
+    const ControllerInfo& info() const override { return info_; }
+    QueuePairView device_queue(std::uint32_t i) const override;
+    QueuePairView host_queue(std::uint32_t i) const override;
+    Result<std::uint64_t> map_dma(void* host_ptr, std::uint64_t bytes) override;
+    Status unmap_dma(std::uint64_t iova) override;
+    Status reset_queue(std::uint32_t i) override;
+    ControllerStats stats() const override;
+
+    // Back namespace ranges with a file (opened by the controller itself).
+    // Idempotent for identical ranges; overlapping ranges of another file fail.
+    Status attach_file(const std::string& path, const std::vector<BackingRange>& ranges);
+    Status detach_file(const std::string& path);
+
+    void inject(InjectKind kind, std::uint32_t count, std::uint32_t delay_us = 0);
+
+    // Stop workers (idempotent). Outstanding SQEs are left unexecuted.
+    void stop();
+
+private:
+    explicit EmulatedNvmeController(const EmulatedControllerConfig& cfg);
+    Status start();
+    void worker_main(std::uint32_t worker);
+    bool service_queue(std::uint32_t q);
+    std::uint32_t execute(const Sqe& sqe, bool* drop_cqe);
+    bool collect_iov(std::uint64_t prp1, std::uint64_t prp2, std::uint64_t bytes,
+                     std::vector<std::pair<char*, std::uint64_t>>& iov) const;
+    bool dma_ok(std::uint64_t addr, std::uint64_t bytes) const;
+
+    struct QueueState {
+        std::uint32_t sq_head = 0;
+        std::uint32_t cq_tail = 0;
+        std::uint32_t phase = 1;
+        std::atomic<std::uint32_t> reset_request{0};
+        std::atomic<std::uint32_t> fatal{0};
+    };
+    struct Backing {
+        std::string path;
+        int fd = -1;
+        std::vector<BackingRange> ranges;
+    };
+    struct Window {
+        std::uint64_t base;
+        std::uint64_t bytes;
+    };
+
+    EmulatedControllerConfig cfg_;
+    ControllerInfo info_;
+    HostMappedBuffer sq_mem_, cq_mem_, bar_mem_;
+    std::vector<std::unique_ptr<QueueState>> qstate_;
+    std::vector<std::thread> workers_;
+    std::atomic<bool> stop_{false};
+
+    mutable std::mutex map_mu_;  // guards backings_ / windows_ (workers take it shared-ish: short)
+    std::vector<Backing> backings_;
+    // flattened, sorted by ns_offset: (ns_offset, length, file_offset, fd)
+    struct Span { std::uint64_t ns, len, foff; int fd; };
+    std::shared_ptr<const std::vector<Span>> spans_;
+    std::shared_ptr<const std::vector<Window>> windows_;
+
+    std::atomic<std::uint32_t> inject_kind_{0};
+    std::atomic<std::uint32_t> inject_count_{0};
+    std::atomic<std::uint32_t> inject_delay_us_{0};
+
+    std::atomic<std::uint64_t> st_commands_{0}, st_read_{0}, st_write_{0}, st_errors_{0}, st_injected_{0};
+};
+
+}  // namespace nvme
+}  // namespace tutti

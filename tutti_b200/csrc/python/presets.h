@@ -1,0 +1,59 @@
+#pragma once
+// Daemon-less preset assembly used by the Python package (reference
+// csrc/presets/local_nvme_preset.cpp:71,141 and include/tutti/presets/local_nvme.h):
+// one emulated controller per backing mount (or per RAID0 member), a
+// multi-mount FIEMAP resolver, and the GPU NVMe DataPath; or the POSIX
+// host-execution DataPath over the same resolvers.
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <tutti/storage_runtime.h>
+
+#include "../datapaths/gpu_nvme_data_path.h"
+#include "../datapaths/posix_data_path.h"
+#include "../nvme/controller.h"
+
+namespace tutti {
+
+struct EmulatedPresetOptions {
+    int accel_id = 0;
+    std::vector<std::string> mounts;   // one emulated drive per mount
+    std::uint32_t queues = 0;          // 0: = leases
+    std::uint32_t queue_depth = 256;
+    std::uint32_t mdts_bytes = 1u << 20;
+    std::uint32_t lba_bytes = 512;
+    std::uint32_t controller_threads = 4;
+    bool direct_io = false;
+    std::string mapping = "auto";      // fiemap | synthetic | auto
+    std::string raid0_md;              // non-empty: mounts[0] is an md RAID0 array
+    std::string sysfs_root = "/sys";
+    std::uint64_t max_terminal_results = 64;
+    GpuNvmeConfig gpu;
+};
+
+struct PosixPresetOptions {
+    int accel_id = -1;
+    std::vector<std::string> mounts;
+    std::uint64_t max_terminal_results = 64;
+    PosixConfig posix;
+};
+
+struct PresetExtras {
+    std::vector<std::shared_ptr<nvme::NvmeController>> controllers;
+    std::shared_ptr<GpuNvmeDataPath> gpu_path;
+    std::shared_ptr<PosixDataPath> posix_path;
+};
+
+struct PresetResult {
+    std::unique_ptr<StorageRuntime> runtime;
+    PresetExtras extras;
+    std::uint32_t runtime_id = 0;
+};
+
+Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o);
+Result<PresetResult> make_posix_runtime(const PosixPresetOptions& o);
+std::uint32_t probe_runtime_id(const StorageRuntime& rt);
+
+}  // namespace tutti
