@@ -35,6 +35,7 @@ CORE_SOURCES = [
     src("datapaths", "gpu_nvme_data_path.cpp"),
     src("datapaths", "posix_data_path.cpp"),
     src("kernels", "io_kernel.cu"),
+    src("kernels", "io_noalloc.cu"),
     src("objects", "object_store.cpp"),
     src("python", "presets.cpp"),
     src("python", "core_module.cpp"),

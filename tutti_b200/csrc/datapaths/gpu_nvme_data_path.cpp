@@ -647,4 +647,68 @@ std::uint32_t GpuNvmeDataPath::free_leases() const {
     return static_cast<std::uint32_t>(free_leases_.size());
 }
 
+std::uint32_t GpuNvmeDataPath::noalloc_acquire_leases(std::uint32_t max, std::uint32_t* out) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (!initialized_) return 0;
+    std::uint32_t n = 0;
+    while (n < max && !free_leases_.empty()) {
+        out[n++] = free_leases_.back();
+        free_leases_.pop_back();
+    }
+    return n;
+}
+
+void GpuNvmeDataPath::noalloc_release_leases(const std::uint32_t* leases, std::uint32_t n, bool reset_dirty) {
+    std::lock_guard<std::mutex> g(mu_);
+    DeviceGuard guard(cfg_.accel_id);
+    for (std::uint32_t i = 0; i < n; ++i) {
+        const std::uint32_t l = leases[i];
+        if (reset_dirty) {
+            for (std::size_t d = 0; d < devs_.size(); ++d) {
+                io::QueueCursor c{};
+                if (cudaMemcpy(&c, d_cursors_[d] + l, sizeof(c), cudaMemcpyDeviceToHost) != cudaSuccess) {
+                    cudaGetLastError();
+                    continue;
+                }
+                if (!c.dirty) continue;
+                if (!devs_[d].controller->reset_queue(l).ok()) continue;
+                const io::QueueCursor fresh{0, 0, 1, 0};
+                if (cudaMemcpy(d_cursors_[d] + l, &fresh, sizeof(fresh), cudaMemcpyHostToDevice) != cudaSuccess)
+                    cudaGetLastError();
+            }
+        }
+        // The vector held every lease at initialize, so its capacity covers this push: no reallocation.
+        free_leases_.push_back(l);
+    }
+}
+
+bool GpuNvmeDataPath::noalloc_memory_ok(std::uint64_t addr, std::uint64_t bytes) const {
+    std::lock_guard<std::mutex> g(mu_);
+    for (const auto& kv : memories_) {
+        const auto base = reinterpret_cast<std::uint64_t>(kv.second.base);
+        if (addr >= base && bytes <= kv.second.size && addr - base <= kv.second.size - bytes) return true;
+    }
+    return false;
+}
+
+bool GpuNvmeDataPath::noalloc_target_ok(std::uint32_t row, std::uint64_t logical, std::uint64_t bytes) const {
+    std::lock_guard<std::mutex> g(mu_);
+    if (row >= targets_.size() || !targets_[row].open) return false;
+    return bytes <= targets_[row].size && logical <= targets_[row].size - bytes;
+}
+
+void GpuNvmeDataPath::noalloc_fill_params(io::IoKernelParams& p) const {
+    std::lock_guard<std::mutex> g(mu_);
+    p.n_devices = static_cast<std::uint32_t>(devs_.size());
+    p.targets = d_targets_;
+    p.devices = d_devices_;
+    p.staging_dev = static_cast<char*>(staging_.device);
+    p.staging_iova = staging_iova_;
+    p.prp_iova = prp_iova_;
+    p.slot_bytes = cfg_.slot_bytes;
+    p.slots_per_lease = cfg_.slots_per_lease;
+    p.timeout_ns = cfg_.timeout_ns;
+    p.timing = nullptr;
+}
+
 }  // namespace tutti

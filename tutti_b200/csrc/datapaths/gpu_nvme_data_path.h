@@ -81,6 +81,18 @@ public:
     IoTimingSummary last_timing() const;
     std::uint32_t free_leases() const;
 
+    // Support for the allocation-free C entry point (kernels/io_noalloc.cu).
+    // None of these allocate: leases come from and return to a vector whose
+    // capacity already covers every lease.
+    std::int32_t accel_id() const { return cfg_.accel_id; }
+    std::uint32_t noalloc_acquire_leases(std::uint32_t max, std::uint32_t* out);
+    void noalloc_release_leases(const std::uint32_t* leases, std::uint32_t n, bool reset_dirty);
+    void noalloc_fill_params(io::IoKernelParams& p) const;
+    // True when [addr, addr+bytes) lies inside one registered memory.
+    bool noalloc_memory_ok(std::uint64_t addr, std::uint64_t bytes) const;
+    // True when `row` is an open target and [logical, logical+bytes) is inside it.
+    bool noalloc_target_ok(std::uint32_t row, std::uint64_t logical, std::uint64_t bytes) const;
+
 private:
     struct TargetRec {
         std::uint64_t generation = 0;

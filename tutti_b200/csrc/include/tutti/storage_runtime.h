@@ -176,6 +176,10 @@ public:
     // Test seam: number of terminal results not yet released.
     std::size_t unreleased_terminal_results() const;
 
+    // The DataPath-level identity an open target maps to (for callers that
+    // drive a DataPath directly, e.g. the allocation-free C entry point).
+    Result<DataPathTarget> data_path_target(const TargetHandle& handle) const;
+
     struct Impl;
 
 private:

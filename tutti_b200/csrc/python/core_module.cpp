@@ -356,6 +356,13 @@ PYBIND11_MODULE(_core, m) {
              })
         .def("free_leases", [](PyRuntime& r) {
             return r.extras.gpu_path ? r.extras.gpu_path->free_leases() : 0u;
+        })
+        // For the allocation-free C entry point: the GPU DataPath's address and
+        // the DataPath target row behind a target handle.
+        .def("gpu_path_address",
+             [](PyRuntime& r) { return reinterpret_cast<std::uintptr_t>(r.extras.gpu_path.get()); })
+        .def("target_row", [](PyRuntime& r, std::uint64_t h) {
+            return unwrap(r.rt->data_path_target(unpack<TargetHandle>(r.rid_, h))).token;
         });
 
     m.def(

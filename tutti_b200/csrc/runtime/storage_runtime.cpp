@@ -840,6 +840,13 @@ Status StorageRuntime::release_io(const IoHandle& h) {
     return Status::Ok();
 }
 
+Result<DataPathTarget> StorageRuntime::data_path_target(const TargetHandle& h) const {
+    std::lock_guard<std::mutex> g(impl_->mu);
+    auto* t = const_cast<Impl&>(*impl_).tgt(h);
+    if (!t) return Result<DataPathTarget>::Failure({StatusCode::NOT_FOUND, "unknown target handle"});
+    return t->dpt;
+}
+
 std::size_t StorageRuntime::unreleased_terminal_results() const {
     std::lock_guard<std::mutex> g(impl_->mu);
     return impl_->terminal_unreleased;
