@@ -48,6 +48,12 @@ def parse():
     p.add_argument("--controller-threads", type=int, default=0, help="0: auto")
     p.add_argument("--direct-io", action="store_true", help="O_DIRECT backing reads (drive-bound)")
     p.add_argument("--no-verify", action="store_true")
+    p.add_argument("--timing", action="store_true", help="per-command %globaltimer breakdown (stderr)")
+    p.add_argument("--leases", type=int, default=128, help="queue leases (CTAs) per GPU")
+    p.add_argument("--ctas", type=int, default=64, help="CTAs one restore may use")
+    p.add_argument("--slots", type=int, default=8)
+    p.add_argument("--inflight", type=int, default=2, help="restores submitted ahead")
+    p.add_argument("--emulator-skip-data", action="store_true", help="diagnostic: controllers move no data")
     return p.parse_args()
 
 
@@ -188,10 +194,11 @@ def main():
     shutil.rmtree(root, ignore_errors=True)
     mounts = [os.path.join(root, f"nvme{d}") for d in range(args.drives)]
     ncpu = os.cpu_count() or 8
-    threads = args.controller_threads or max(2, min(8, ncpu // max(1, world) // max(1, args.drives)))
-    opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": 128,
-            "max_ctas_per_op": 128, "slots_per_lease": 4, "slot_bytes": 1 << 20, "queue_depth": 256,
-            "mdts_bytes": 1 << 20}
+    threads = args.controller_threads or max(2, min(8, (ncpu // max(1, world) - 2) // max(1, args.drives)))
+    opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": args.leases,
+            "max_ctas_per_op": args.ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20,
+            "queue_depth": 256, "mdts_bytes": 1 << 20, "timing": bool(args.timing),
+            "emulator_skip_data": bool(args.emulator_skip_data)}
     backend = "nvme-gpu" if args.impl == "tutti" else "posix"
     if backend == "posix":
         opts = {"threads": max(4, ncpu // max(1, world)), "direct_io": bool(args.direct_io)}
@@ -227,19 +234,29 @@ def main():
     stream = torch.cuda.current_stream(dev)
     launches = [0]
 
-    def step(i, e2e: bool):
-        if e2e:
-            dev_table.copy_(pinned_tables[i], non_blocking=True)  # H2D: this step's block table
-        comp = store.get_paged(keys, perms[i], stream=stream)
-        launches[0] += len(comp._ios)
-        comp.wait()
-        if e2e:
-            # D2H: the step's result (a checksum of the restored first block)
-            checksum.copy_(pool[0, 0, dev_table[0]].float().sum().reshape(1), non_blocking=True)
-            stream.synchronize()
+    def run_steps(first: int, count: int, e2e: bool) -> None:
+        """``count`` restores with up to ``args.inflight`` submitted ahead (host work overlaps IO)."""
+        pending = []
+        for i in range(first, first + count):
+            if e2e:
+                dev_table.copy_(pinned_tables[i], non_blocking=True)  # H2D: this step's block table
+            comp = store.get_paged(keys, perms[i], stream=stream)
+            launches[0] += len(comp._ios)
+            pending.append((i, comp))
+            while len(pending) >= args.inflight:
+                j, c = pending.pop(0)
+                c.wait()
+                if e2e:
+                    # D2H: the step's result (a checksum of its first restored block)
+                    checksum.copy_(pool[0, 0, int(perms[j].reshape(-1)[0])].float().sum().reshape(1),
+                                   non_blocking=True)
+        for j, c in pending:
+            c.wait()
+            if e2e:
+                checksum.copy_(pool[0, 0, int(perms[j].reshape(-1)[0])].float().sum().reshape(1), non_blocking=True)
+        stream.synchronize()
 
-    for i in range(args.warmup):
-        step(i, False)
+    run_steps(0, args.warmup, False)
     barrier(world)
     sampler = ClockSampler([local]).start() if rank == 0 else None
     # device-timed: K restores back to back
@@ -247,8 +264,7 @@ def main():
     barrier(world)
     ev0.record(stream)
     launches[0] = 0
-    for i in range(args.warmup, args.warmup + args.steps):
-        step(i, False)
+    run_steps(args.warmup, args.steps, False)
     ev1.record(stream)
     torch.cuda.synchronize()
     dev_ms = ev0.elapsed_time(ev1) / args.steps
@@ -257,8 +273,7 @@ def main():
     # end to end: + H2D block table from pinned memory + D2H result readback every step
     ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev2.record(stream)
-    for i in range(args.warmup, args.warmup + args.steps):
-        step(i, True)
+    run_steps(args.warmup, args.steps, True)
     ev3.record(stream)
     torch.cuda.synchronize()
     e2e_ms = ev2.elapsed_time(ev3) / args.steps
@@ -273,8 +288,10 @@ def main():
     ms = max_over_ranks(world, dev_ms)
     e2e = max_over_ranks(world, e2e_ms)
     total_bytes = sum_over_ranks(world, float(bytes_per_step))
-    timing = store.runtime.io_timing() if store.runtime else {}
+    timing = store.runtime.io_timing() if store.runtime and args.timing else {}
     stats = store.runtime.controller_stats() if store.runtime else []
+    if args.timing and rank == 0:
+        print(json.dumps({"io_timing": timing, "controllers": stats}), file=sys.stderr)
     store.close()
     if rank == 0:
         value = total_bytes / (ms / 1e3) / 1e9
@@ -287,7 +304,7 @@ def main():
                        "seq_len": args.prefix_tokens, "parallelism": f"dp{world} (one prefix per rank)",
                        "pool_blocks": args.pool_blocks, "drives_per_rank": args.drives,
                        "backing": "O_DIRECT" if args.direct_io else "page cache",
-                       "controller_threads": threads, "impl": args.impl,
+                       "controller_threads": threads, "impl": args.impl, "inflight": args.inflight,
                        "l2": "inputs (4.29 GB/step) larger than L2"},
             "e2e": {"value": round(total_bytes / (e2e / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": nblk * 8, "d2h_bytes_per_step": 4},

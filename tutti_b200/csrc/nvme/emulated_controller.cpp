@@ -331,6 +331,10 @@ std::uint32_t EmulatedNvmeController::execute(const Sqe& sqe, bool* drop_cqe) {
         st_errors_.fetch_add(1);
         return make_status(0, kScDataTransferError);
     }
+    if (cfg_.skip_data) {
+        (op == kOpRead ? st_read_ : st_write_).fetch_add(bytes, std::memory_order_relaxed);
+        return 0;
+    }
     auto spans = std::atomic_load(&spans_);
     // Walk namespace spans and iov segments together.
     std::uint64_t pos = off, end = off + bytes;

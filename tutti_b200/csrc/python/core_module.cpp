@@ -7,6 +7,9 @@
 #include <execinfo.h>
 #include <fcntl.h>
 #include <signal.h>
+
+#include <chrono>
+#include <cstdlib>
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -247,11 +250,23 @@ PYBIND11_MODULE(_core, m) {
                 ctx.accel_id = -1;
                 ctx.stream = reinterpret_cast<cudaStream_t>(stream);
                 IoSubmitOutcome o;
+                const auto t_built = std::chrono::steady_clock::now();
                 {
                     py::gil_scoped_release nogil;
                     o = r.rt->submit(reqs.data(), n, ctx);
                 }
+                const auto t_sub = std::chrono::steady_clock::now();
                 py::dict d;
+                if (std::getenv("TUTTI_SUBMIT_PROFILE")) {
+                    d["runtime_submit_ms"] =
+                        std::chrono::duration<double, std::milli>(t_sub - t_built).count();
+                    if (r.extras.gpu_path) {
+                        const auto sp = r.extras.gpu_path->last_submit_profile();
+                        d["dp_coalesce_ms"] = sp.coalesce_ms;
+                        d["dp_launch_ms"] = sp.launch_ms;
+                        d["dp_commands"] = sp.commands;
+                    }
+                }
                 d["io"] = o.io ? py::cast(pack(*o.io)) : py::none();
                 d["status"] = o.status.to_string();
                 d["ok"] = o.status.ok();
@@ -268,6 +283,84 @@ PYBIND11_MODULE(_core, m) {
             },
             py::arg("direction"), py::arg("mem"), py::arg("mem_offsets"), py::arg("targets"),
             py::arg("target_offsets"), py::arg("lengths"), py::arg("stream") = 0, py::arg("host_exec") = false)
+        .def(
+            "submit_paged",
+            [](PyRuntime& r, const std::string& direction, std::uint64_t mem,
+               py::array_t<std::uint64_t, py::array::c_style> chunk_targets,
+               py::array_t<std::uint64_t, py::array::c_style> chunk_offsets,
+               py::array_t<std::int64_t, py::array::c_style> block_ids, py::array_t<std::int64_t, py::array::c_style> layers,
+               py::dict geo, std::uintptr_t stream, bool host_exec) {
+                // Requests of a paged restore/store in (chunk, layer, block, plane) order:
+                //   target_offset = chunk_offset + layer*segment + j*block_layer + plane*plane_bytes
+                //   memory_offset = ((layer*planes + plane)*num_blocks + block) * plane_bytes
+                const std::uint64_t planes = geo["planes"].cast<std::uint64_t>();
+                const std::uint64_t plane_bytes = geo["plane_bytes"].cast<std::uint64_t>();
+                const std::uint64_t segment = geo["segment_bytes"].cast<std::uint64_t>();
+                const std::uint64_t block_layer = geo["block_layer_bytes"].cast<std::uint64_t>();
+                const std::uint64_t num_blocks = geo["num_blocks"].cast<std::uint64_t>();
+                const std::size_t n = static_cast<std::size_t>(chunk_targets.size());
+                if (chunk_offsets.size() != static_cast<py::ssize_t>(n) || block_ids.ndim() != 2 ||
+                    block_ids.shape(0) != static_cast<py::ssize_t>(n))
+                    throw py::value_error("chunk arrays / block table shape mismatch");
+                const std::size_t bpc = static_cast<std::size_t>(block_ids.shape(1));
+                const std::size_t nl = static_cast<std::size_t>(layers.size());
+                if (direction != "read" && direction != "write") throw py::value_error("direction read|write");
+                const IoDirection dir = direction == "read" ? IoDirection::READ : IoDirection::WRITE;
+                auto ct = chunk_targets.unchecked<1>();
+                auto co = chunk_offsets.unchecked<1>();
+                auto bt = block_ids.unchecked<2>();
+                auto ly = layers.unchecked<1>();
+                std::vector<IoRequest> reqs(n * nl * bpc * planes);
+                const MemoryHandle mh = unpack<MemoryHandle>(r.rid_, mem);
+                std::size_t k = 0;
+                for (std::size_t c = 0; c < n; ++c) {
+                    const TargetHandle th = unpack<TargetHandle>(r.rid_, ct(c));
+                    for (std::size_t l = 0; l < nl; ++l) {
+                        const std::uint64_t L = static_cast<std::uint64_t>(ly(l));
+                        for (std::size_t j = 0; j < bpc; ++j) {
+                            const std::int64_t b = bt(c, j);
+                            if (b < 0 || static_cast<std::uint64_t>(b) >= num_blocks)
+                                throw py::value_error("block id out of range");
+                            for (std::uint64_t p = 0; p < planes; ++p) {
+                                IoRequest& q = reqs[k++];
+                                q.direction = dir;
+                                q.memory = mh;
+                                q.memory_offset = ((L * planes + p) * num_blocks + static_cast<std::uint64_t>(b)) * plane_bytes;
+                                q.target = th;
+                                q.target_offset = co(c) + L * segment + j * block_layer + p * plane_bytes;
+                                q.length = plane_bytes;
+                            }
+                        }
+                    }
+                }
+                HostSubmitContext ctx;
+                ctx.execution_domain = host_exec ? ExecutionDomain::HOST_EXECUTION : ExecutionDomain::DEVICE_EXECUTION;
+                ctx.accel_id = -1;
+                ctx.stream = reinterpret_cast<cudaStream_t>(stream);
+                IoSubmitOutcome o;
+                {
+                    py::gil_scoped_release nogil;
+                    o = r.rt->submit(reqs.data(), reqs.size(), ctx);
+                }
+                py::dict d;
+                d["io"] = o.io ? py::cast(pack(*o.io)) : py::none();
+                d["status"] = o.status.to_string();
+                d["ok"] = o.status.ok();
+                d["count"] = reqs.size();
+                std::vector<std::uint32_t> rejected;
+                std::vector<std::string> reasons;
+                for (std::size_t i = 0; i < reqs.size(); ++i)
+                    if (o.initial_states[i].state == IoRequestState::REJECTED) {
+                        rejected.push_back(static_cast<std::uint32_t>(i));
+                        if (reasons.size() < 8) reasons.push_back(o.initial_states[i].status.to_string());
+                    }
+                d["rejected"] = rejected;
+                d["reasons"] = reasons;
+                return d;
+            },
+            py::arg("direction"), py::arg("mem"), py::arg("chunk_targets"), py::arg("chunk_offsets"),
+            py::arg("block_ids"), py::arg("layers"), py::arg("geometry"), py::arg("stream") = 0,
+            py::arg("host_exec") = false)
         .def("query_io",
              [](PyRuntime& r, std::uint64_t io) {
                  auto s = unwrap(r.rt->query(unpack<IoHandle>(r.rid_, io)));
@@ -377,6 +470,7 @@ PYBIND11_MODULE(_core, m) {
             if (opts.contains("lba_bytes")) o.lba_bytes = opts["lba_bytes"].cast<std::uint32_t>();
             if (opts.contains("controller_threads")) o.controller_threads = opts["controller_threads"].cast<std::uint32_t>();
             if (opts.contains("direct_io")) o.direct_io = opts["direct_io"].cast<bool>();
+            if (opts.contains("emulator_skip_data")) o.skip_data = opts["emulator_skip_data"].cast<bool>();
             if (opts.contains("leases")) o.gpu.leases = opts["leases"].cast<std::uint32_t>();
             if (opts.contains("max_ctas_per_op")) o.gpu.max_ctas_per_op = opts["max_ctas_per_op"].cast<std::uint32_t>();
             if (opts.contains("slots_per_lease")) o.gpu.slots_per_lease = opts["slots_per_lease"].cast<std::uint32_t>();

@@ -26,6 +26,7 @@ struct EmulatedPresetOptions {
     std::uint32_t lba_bytes = 512;
     std::uint32_t controller_threads = 4;
     bool direct_io = false;
+    bool skip_data = false;  // diagnostic: controllers move no data
     std::string mapping = "auto";      // fiemap | synthetic | auto
     std::string raid0_md;              // non-empty: mounts[0] is an md RAID0 array
     std::string sysfs_root = "/sys";

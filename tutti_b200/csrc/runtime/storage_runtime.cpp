@@ -66,6 +66,7 @@ struct StorageRuntime::Impl {
         bool live = false;
         std::string uri;
         std::string dp_key;
+        struct DpEntry* dpe = nullptr;  // stable: DataPaths are fixed after create
         DataPathTarget dpt;
         std::uint64_t size = 0;
         int inflight = 0;
@@ -82,7 +83,8 @@ struct StorageRuntime::Impl {
         bool live = false;
         IoState state = IoState::IN_FLIGHT;
         std::vector<OpPart> parts;
-        std::vector<std::uint32_t> mem_slots, tgt_slots;  // references held while in flight
+        // (slot, count) references held on memories / targets while in flight
+        std::vector<std::pair<std::uint32_t, std::uint32_t>> mem_refs, tgt_refs;
         IoResult result;
         bool refs_released = false;
     };
@@ -214,10 +216,10 @@ struct StorageRuntime::Impl {
 
     void release_refs(IoEntry& e) {
         if (e.refs_released) return;
-        for (auto s : e.mem_slots)
-            if (s < mems.size()) --mems[s].inflight;
-        for (auto s : e.tgt_slots)
-            if (s < tgts.size()) --tgts[s].inflight;
+        for (auto& r : e.mem_refs)
+            if (r.first < mems.size()) mems[r.first].inflight -= static_cast<int>(r.second);
+        for (auto& r : e.tgt_refs)
+            if (r.first < tgts.size()) tgts[r.first].inflight -= static_cast<int>(r.second);
         e.refs_released = true;
     }
 
@@ -611,6 +613,7 @@ std::vector<Result<TargetHandle>> StorageRuntime::open_batch(const std::vector<s
         e.live = true;
         e.uri = uris[i];
         e.dp_key = key;
+        e.dpe = d;
         e.dpt = dpt.value();
         e.size = t.logical_size();
         out.push_back(TargetHandle::from_raw(im.id, slot, e.generation));
@@ -671,11 +674,34 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
         std::vector<std::uint32_t> idx;
     };
     std::vector<Group> groups;
+    groups.reserve(im.dps.size());
     Status first_reject;
+    // Batches address few memories and targets: cache the last lookups so the
+    // per-request cost is arithmetic, not registry searches.
+    MemoryHandle last_mh;
+    TargetHandle last_th;
+    Impl::MemoryEntry* last_m = nullptr;
+    Impl::TargetEntry* last_t = nullptr;
+    Impl::MemoryEntry* reg_m = nullptr;
+    Impl::DpEntry* reg_d = nullptr;
+    DataPathMemory reg_dpm;
+    Status reg_status;
+    Impl::DpEntry* caps_d = nullptr;
+    const DataPathCapabilities* caps = nullptr;
+    Group* last_gp = nullptr;
+    std::vector<std::uint32_t> mem_count(im.mems.size(), 0), tgt_count(im.tgts.size(), 0);
     for (std::size_t i = 0; i < count; ++i) {
         const IoRequest& r = reqs[i];
-        auto* m = im.mem(r.memory);
-        auto* t = im.tgt(r.target);
+        if (!last_m || r.memory != last_mh) {
+            last_m = im.mem(r.memory);
+            last_mh = r.memory;
+        }
+        if (!last_t || r.target != last_th) {
+            last_t = im.tgt(r.target);
+            last_th = r.target;
+        }
+        auto* m = last_m;
+        auto* t = last_t;
         Status bad;
         if (!m)
             bad = {StatusCode::NOT_FOUND, "invalid memory handle"};
@@ -689,11 +715,15 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
             bad = {StatusCode::OUT_OF_RANGE, "target range exceeds logical size"};
         Impl::DpEntry* d = nullptr;
         if (bad.ok()) {
-            d = im.dp(t->dp_key);
+            d = t->dpe;
             if (!d) bad = {StatusCode::INTERNAL, "target's DataPath missing"};
         }
         if (bad.ok()) {
-            const auto& c = d->dp->capabilities();
+            if (d != caps_d) {
+                caps_d = d;
+                caps = &d->dp->capabilities();
+            }
+            const auto& c = *caps;
             if ((r.direction == IoDirection::READ && !c.supports_read) ||
                 (r.direction == IoDirection::WRITE && !c.supports_write))
                 bad = {StatusCode::UNSUPPORTED, "direction not supported by " + d->key};
@@ -708,23 +738,34 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
         }
         DataPathMemory dpm;
         if (bad.ok()) {
-            auto reg = im.registration_for(*m, *d);
-            if (!reg.ok())
-                bad = reg.status();
+            if (m != reg_m || d != reg_d) {
+                auto reg = im.registration_for(*m, *d);
+                reg_m = m;
+                reg_d = d;
+                reg_status = reg.ok() ? Status::Ok() : reg.status();
+                if (reg.ok()) reg_dpm = reg.value();
+            }
+            if (!reg_status.ok())
+                bad = reg_status;
             else
-                dpm = reg.value();
+                dpm = reg_dpm;
         }
         if (!bad.ok()) {
             out.initial_states[i] = {IoRequestState::REJECTED, bad};
             if (first_reject.ok()) first_reject = bad;
             continue;
         }
-        Group* gp = nullptr;
-        for (auto& x : groups)
-            if (x.d == d) gp = &x;
+        Group* gp = (last_gp && last_gp->d == d) ? last_gp : nullptr;
         if (!gp) {
-            groups.push_back({d, {}, {}});
-            gp = &groups.back();
+            for (auto& x : groups)
+                if (x.d == d) gp = &x;
+            if (!gp) {
+                groups.push_back({d, {}, {}});
+                gp = &groups.back();
+                gp->reqs.reserve(count);
+                gp->idx.reserve(count);
+            }
+            last_gp = gp;
         }
         gp->reqs.push_back({r, dpm, t->dpt});
         gp->idx.push_back(static_cast<std::uint32_t>(i));
@@ -745,8 +786,8 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
                 continue;
             }
             const IoRequest& r = reqs[gp.idx[k]];
-            entry.mem_slots.push_back(r.memory.slot());
-            entry.tgt_slots.push_back(r.target.slot());
+            ++mem_count[r.memory.slot()];
+            ++tgt_count[r.target.slot()];
         }
         if (so.op) {
             part.op = *so.op;
@@ -757,8 +798,16 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
     }
     out.status = first_reject;
     if (entry.parts.empty()) return out;
-    for (auto s : entry.mem_slots) ++im.mems[s].inflight;
-    for (auto s : entry.tgt_slots) ++im.tgts[s].inflight;
+    for (std::uint32_t s = 0; s < mem_count.size(); ++s)
+        if (mem_count[s]) {
+            im.mems[s].inflight += static_cast<int>(mem_count[s]);
+            entry.mem_refs.emplace_back(s, mem_count[s]);
+        }
+    for (std::uint32_t s = 0; s < tgt_count.size(); ++s)
+        if (tgt_count[s]) {
+            im.tgts[s].inflight += static_cast<int>(tgt_count[s]);
+            entry.tgt_refs.emplace_back(s, tgt_count[s]);
+        }
     const std::uint32_t slot = Impl::alloc_slot(im.ios);
     entry.generation = im.next_gen++;
     entry.live = true;

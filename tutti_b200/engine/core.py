@@ -1,0 +1,295 @@
+"""KVEngine: the semantic index plus the execution of restores and stores.
+
+Planning state lives in the ``ChunkIndex`` (residency, pins, pending writes,
+LRU eviction). Execution goes through a store:
+
+* direct (``TuttiKVStore`` with the engine's paged pool registered once): a
+  restore is one ``get_paged`` per layer whose fused io kernel scatters into
+  the pool's blocks; a store is one ``put_paged`` whose io kernel gathers them;
+* staged (any ``KVStore``, e.g. ``MemoryKVStore``): chunk bytes move through a
+  staging buffer with the bulk-copy gather/scatter kernels.
+
+Layerwise restores (``start_read_plan``): a feeder thread submits layer
+l's restore on a high-priority IO stream and records an event per layer;
+``wait_layer(l)`` makes the *current* stream wait on that event on the
+device, so attention of layer l starts as soon as its KV is in HBM while
+layers l+1.. are still being read. Writes are queued behind a compute event
+and settled (index confirm, object commit) when they complete.
+Parity: reference tutti/engine/core.py:53-2842 (_ReadPlan, _AsyncReadPlan,
+_DirectAllLayerReadPlan with its feeder thread, _QueuedWrite, KVEngine).
+"""
+from __future__ import annotations
+
+import collections
+import logging
+import threading
+import time
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from ..index.chunk_index import ChunkIndex, StorePlan
+from ..models.kv_geometry import KVGeometry
+from .completion import AggregateCompletion, LoadGateError, PostCompletion
+
+LOG = logging.getLogger("tutti_b200.engine")
+FEEDER_WAIT_S = 120.0
+
+
+class LayerwiseReadPlan:
+    """Per-layer restore of ``keys`` into ``block_table`` rows, fed by a thread."""
+
+    def __init__(self, engine: "KVEngine", keys: Sequence[bytes], block_table: np.ndarray,
+                 layers: Sequence[int], io_stream: torch.cuda.Stream, window: int = 4):
+        self.engine = engine
+        self.keys = list(keys)
+        self.block_table = block_table
+        self.layers = list(layers)
+        self.io_stream = io_stream
+        self.window = max(1, window)
+        self._events: dict[int, torch.cuda.Event] = {}
+        self._comps: list = []
+        self._cv = threading.Condition()
+        self._error: BaseException | None = None
+        self._closed = False
+        self.t_submit0 = time.perf_counter()
+        self.read_done_s: float | None = None
+        self._thread = threading.Thread(target=self._feed, name="tutti-feeder", daemon=True)
+        self._thread.start()
+
+    def _feed(self) -> None:
+        store = self.engine.store
+        dev = self.engine.device
+        try:
+            torch.cuda.set_device(dev)
+            for li, layer in enumerate(self.layers):
+                if self._closed:
+                    break
+                comp = store.get_paged(self.keys, self.block_table, layers=[layer], stream=self.io_stream)
+                ev = torch.cuda.Event()
+                ev.record(self.io_stream)
+                with self._cv:
+                    self._comps.append(comp)
+                    self._events[layer] = ev
+                    self._cv.notify_all()
+                # bound the layers in flight (queue leases are shared)
+                if li >= self.window:
+                    self._comps[li - self.window].wait()
+        except BaseException as e:  # noqa: BLE001 - surfaced by wait_layer / finish
+            with self._cv:
+                self._error = e
+                self._cv.notify_all()
+
+    def wait_layer(self, layer: int) -> None:
+        """Order the current stream after layer ``layer``'s restore (device-side wait)."""
+        deadline = time.monotonic() + FEEDER_WAIT_S
+        with self._cv:
+            while layer not in self._events and self._error is None:
+                left = deadline - time.monotonic()
+                if left <= 0:
+                    raise LoadGateError(f"feeder did not submit layer {layer} within {FEEDER_WAIT_S}s")
+                self._cv.wait(timeout=left)
+            if layer not in self._events:
+                raise LoadGateError(f"restore of layer {layer} failed: {self._error}")
+            ev = self._events[layer]
+        torch.cuda.current_stream().wait_event(ev)
+
+    def finish(self) -> None:
+        """Host-wait for every layer; raises LoadGateError listing the failed chunks."""
+        self._thread.join(timeout=FEEDER_WAIT_S)
+        failed: set[int] = set()
+        err = self._error
+        for comp in self._comps:
+            try:
+                comp.wait()
+            except Exception as e:  # noqa: BLE001
+                err = err or e
+                per_layer = len(self.keys) * self.engine.geometry.blocks_per_chunk * self.engine.geometry.planes
+                for i in getattr(e, "failed", []):
+                    failed.add((i % per_layer) // (self.engine.geometry.blocks_per_chunk * self.engine.geometry.planes))
+        self.read_done_s = time.perf_counter() - self.t_submit0
+        if err is not None:
+            raise LoadGateError(f"restore failed: {err}", failed or range(len(self.keys)))
+
+    def abort(self) -> None:
+        self._closed = True
+        try:
+            self.finish()
+        except LoadGateError:
+            pass
+
+
+class KVEngine:
+    def __init__(self, store, geometry: KVGeometry, *, capacity_chunks: int | None = None,
+                 namespace: bytes = b"", device: int | torch.device = 0, staged: bool | None = None,
+                 io_priority: int = -1, checkpoint_interval_s: float = 60.0):
+        self.store = store
+        self.geometry = geometry
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        cap = capacity_chunks or getattr(store, "capacity_chunks", 1 << 20)
+        self.index = ChunkIndex(cap, geometry.chunk_tokens, namespace)
+        self.staged = (not hasattr(store, "get_paged")) if staged is None else staged
+        self.pool: torch.Tensor | None = None
+        self._io_stream: torch.cuda.Stream | None = None
+        self._io_priority = io_priority
+        self._writes: collections.deque = collections.deque()
+        self._checkpoint_interval = checkpoint_interval_s
+        self._last_checkpoint = time.monotonic()
+        self.stats = collections.Counter()
+
+    # -- index forwarding ---------------------------------------------------
+    def hash_keys(self, tokens: Sequence[int], **kw):
+        return self.index.hash_keys(tokens, **kw)
+
+    def lookup_prefix(self, tokens: Sequence[int]) -> int:
+        return self.index.lookup_prefix(tokens)
+
+    def lookup_prefix_keys(self, keys: Sequence[bytes]) -> int:
+        return self.index.lookup_prefix_keys(keys)
+
+    def pin(self, keys) -> None:
+        self.index.pin(keys)
+
+    def unpin(self, keys) -> None:
+        self.index.unpin(keys)
+
+    def begin_step(self, max_pending_age: int = 64) -> int:
+        """Advance the index epoch; reclaim reservations no rank ever settled."""
+        self.index.advance_epoch()
+        stale = self.index.reclaim_stale_pending(max_pending_age)
+        if stale:
+            LOG.warning("reclaimed %d stale pending reservation(s)", len(stale))
+        self.poll_writes()
+        return self.index.epoch
+
+    def restore_from_store(self) -> int:
+        """Cold start: publish chunks the store already holds."""
+        if hasattr(self.store, "scan"):
+            keys = list(self.store.scan())
+            self.index.restore(keys)
+            return len(keys)
+        return 0
+
+    # -- binding --------------------------------------------------------------
+    @property
+    def io_stream(self) -> torch.cuda.Stream:
+        if self._io_stream is None:
+            self._io_stream = torch.cuda.Stream(device=self.device, priority=self._io_priority)
+        return self._io_stream
+
+    def bind(self, pool: torch.Tensor) -> None:
+        """Bind the engine's paged KV pool (direct mode registers it with the store once)."""
+        self.pool = pool
+        if not self.staged:
+            self.store.register_pool(pool)
+
+    # -- restores -------------------------------------------------------------
+    def _table(self, block_table) -> np.ndarray:
+        bt = block_table.cpu().numpy() if isinstance(block_table, torch.Tensor) else np.asarray(block_table)
+        return bt.reshape(-1, self.geometry.blocks_per_chunk).astype(np.int64)
+
+    def start_read_plan(self, keys: Sequence[bytes], block_table, layers: Sequence[int] | None = None,
+                        window: int = 4) -> LayerwiseReadPlan:
+        """Restore ``keys`` (chunk order) into ``block_table`` rows, layer by layer."""
+        if self.pool is None:
+            raise RuntimeError("bind() the KV pool first")
+        layers = list(range(self.geometry.num_layers)) if layers is None else list(layers)
+        if self.staged:
+            raise NotImplementedError("layerwise plans need a direct (paged) store")
+        self.stats["read_chunks"] += len(keys)
+        return LayerwiseReadPlan(self, keys, self._table(block_table), layers, self.io_stream, window)
+
+    def load(self, keys: Sequence[bytes], block_table, layers: Sequence[int] | None = None):
+        """Restore all (or ``layers``) of ``keys`` in one submission; returns a completion."""
+        bt = self._table(block_table)
+        if not self.staged:
+            self.stats["read_chunks"] += len(keys)
+            return self.store.get_paged(keys, bt, layers=layers, stream=self.io_stream)
+        return self._staged_load(keys, bt)
+
+    def _staged_load(self, keys, bt):
+        from .. import ops
+
+        g = self.geometry
+        staging = torch.empty(len(keys) * g.chunk_bytes, dtype=torch.uint8, device=self.device)
+        comp = self.store.get_batch([(k, self._staging_id(staging), i * g.chunk_bytes) for i, k in enumerate(keys)])
+        comp.wait()
+        ops.scatter_blocks(staging, self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
+        return comp
+
+    def _staging_id(self, staging: torch.Tensor) -> int:
+        bid = self.store.register_buffer(staging, self.geometry.chunk_bytes)
+        if bid is None:
+            raise RuntimeError("store refused the staging buffer")
+        return bid
+
+    # -- stores ---------------------------------------------------------------
+    def plan_store(self, keys: Sequence[bytes]) -> StorePlan | None:
+        plan = self.index.plan_store(keys)
+        if plan is not None and plan.evicted_keys and hasattr(self.store, "drop"):
+            self.store.drop(plan.evicted_keys)  # capacity closure: the index decided, the store executes
+            self.stats["evicted_chunks"] += len(plan.evicted_keys)
+        return plan
+
+    def store_chunks(self, keys: Sequence[bytes], block_table, *, after: torch.cuda.Event | None = None):
+        """Persist chunks ``keys`` from ``block_table`` rows once ``after`` (compute) has happened."""
+        keys = [bytes(k) for k in keys]
+        plan = self.plan_store(keys)
+        if plan is None:
+            self.stats["store_refused"] += 1
+            return None
+        new = set(plan.new_keys)
+        idx = [i for i, k in enumerate(keys) if k in new]
+        if not idx:
+            return None
+        bt = self._table(block_table)[idx]
+        wkeys = [keys[i] for i in idx]
+        stream = self.io_stream
+        if after is not None:
+            stream.wait_event(after)
+        else:
+            stream.wait_stream(torch.cuda.current_stream(self.device))
+        if not self.staged:
+            inner = self.store.put_paged(wkeys, bt, stream=stream)
+        else:
+            from .. import ops
+
+            g = self.geometry
+            with torch.cuda.stream(stream):
+                staging = ops.gather_blocks(self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
+            stream.synchronize()
+            bid = self._staging_id(staging)
+            inner = self.store.put_batch([(k, bid, i * g.chunk_bytes) for i, k in enumerate(wkeys)])
+        comp = PostCompletion(inner, after=lambda: self.index.confirm_store(wkeys, True),
+                              on_error=lambda: self.index.confirm_store(wkeys, False))
+        self._writes.append(comp)
+        self.stats["write_chunks"] += len(wkeys)
+        return comp
+
+    def poll_writes(self) -> int:
+        done = 0
+        while self._writes and self._writes[0].query():
+            try:
+                self._writes.popleft().wait()
+            except Exception as e:  # noqa: BLE001
+                LOG.warning("write failed: %s", e)
+            done += 1
+        self._maybe_checkpoint()
+        return done
+
+    def wait_idle(self) -> None:
+        while self._writes:
+            try:
+                self._writes.popleft().wait()
+            except Exception as e:  # noqa: BLE001
+                LOG.warning("write failed: %s", e)
+        self._maybe_checkpoint(force=False)
+
+    def _maybe_checkpoint(self, force: bool = False) -> None:
+        if not hasattr(self.store, "objects") or self.store.objects is None:
+            return
+        now = time.monotonic()
+        if force or now - self._last_checkpoint >= self._checkpoint_interval:
+            self.store.objects.checkpoint()
+            self._last_checkpoint = now

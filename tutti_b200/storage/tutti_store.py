@@ -107,6 +107,7 @@ class TuttiKVStore:
         self._targets: dict[str, int] = {}
         self._pool = None  # (tensor, handle, num_blocks)
         self._inflight: collections.deque[NativeCompletion] = collections.deque()
+        self.last_submit_profile: dict = {}
 
     # -- lifecycle ------------------------------------------------------------
     @property
@@ -236,6 +237,8 @@ class TuttiKVStore:
         for attempt in range(self.max_retries):
             r = self.runtime.submit_arrays(direction, mem, mem_off[idx], tgts[idx], tgt_off[idx], lens[idx],
                                            sptr, host)
+            if "runtime_submit_ms" in r:
+                self.last_submit_profile = {k: v for k, v in r.items() if k.endswith("_ms") or k == "dp_commands"}
             if r["io"] is not None:
                 ios.append(r["io"])
             rej = np.asarray(r["rejected"], dtype=np.int64)
@@ -256,6 +259,32 @@ class TuttiKVStore:
                 time.sleep(0.0005)
         raise StoreIOError("submit retries exhausted", idx.tolist(), "busy")
 
+    def _submit_paged(self, direction: str, placements, block_ids: np.ndarray, layers: np.ndarray, stream):
+        """Paged requests generated natively (no per-request Python work); retried while leases are busy."""
+        g = self.geometry
+        handles = np.asarray(self.targets_for([p for p, _ in placements]), dtype=np.uint64)
+        offsets = np.asarray([o for _, o in placements], dtype=np.uint64)
+        geo = {"planes": g.planes, "plane_bytes": g.plane_block_bytes, "segment_bytes": g.segment_bytes,
+               "block_layer_bytes": g.block_layer_bytes, "num_blocks": int(self._pool[2])}
+        bt = np.ascontiguousarray(block_ids, dtype=np.int64)
+        ly = np.ascontiguousarray(layers, dtype=np.int64)
+        sptr = self._stream_ptr(stream)
+        host = self.backend != "nvme-gpu"
+        for _ in range(self.max_retries):
+            r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host)
+            if not r["rejected"]:
+                return [r["io"]], int(r["count"]) * g.plane_block_bytes
+            reasons = " ".join(r["reasons"])
+            if r["io"] is not None or ("BUSY" not in reasons and "RESOURCE_EXHAUSTED" not in reasons):
+                if r["io"] is not None:
+                    NativeCompletion(self.runtime, [r["io"]]).wait()
+                raise StoreIOError(f"{len(r['rejected'])} request(s) rejected: {reasons}", r["rejected"], "rejected")
+            if self._inflight:
+                self._inflight.popleft().wait()
+            else:
+                time.sleep(0.0005)
+        raise StoreIOError("submit retries exhausted", kind="busy")
+
     def get_paged(self, keys: Sequence[bytes], block_ids, layers=None, stream=None) -> NativeCompletion:
         """Restore chunks ``keys`` into pool blocks ``block_ids[i]`` for ``layers`` (default all)."""
         g = self.geometry
@@ -268,9 +297,8 @@ class TuttiKVStore:
                 raise StoreIOError(f"chunk {bytes(k).hex()} is not committed", kind="not_found")
             uri, off, _slot, _gen = p
             placements.append((uri[len("file://"):], off))
-        tgts, toff, moff, lens = self.page_requests(placements, block_ids, layers)
-        ios = self._submit_retry("read", tgts, toff, moff, lens, stream)
-        comp = NativeCompletion(self.runtime, ios, nbytes=int(lens.sum()))
+        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream)
+        comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
         self._track(comp)
         return comp
 
@@ -287,17 +315,16 @@ class TuttiKVStore:
             raise StoreIOError(f"{rejected} chunk(s) did not fit (capacity)", kind="capacity")
         placements = [(uri[len("file://"):], off) for (_k, uri, off, _s, _g) in accepted]
         wkeys = [a[0] for a in accepted]
-        tgts, toff, moff, lens = self.page_requests(placements, block_ids[fresh], np.arange(g.num_layers))
         if self.backend == "nvme-gpu" and stream is None:
             # The gather reads the pool: order it after work queued on the current stream.
             stream = torch.cuda.current_stream(self.device)
         try:
-            ios = self._submit_retry("write", tgts, toff, moff, lens, stream)
+            ios, nbytes = self._submit_paged("write", placements, block_ids[fresh], np.arange(g.num_layers), stream)
         except Exception:
             self.objects.abort(wkeys)
             raise
         comp = NativeCompletion(self.runtime, ios, on_success=lambda: self.objects.commit(wkeys),
-                                on_failure=lambda: self.objects.abort(wkeys), nbytes=int(lens.sum()))
+                                on_failure=lambda: self.objects.abort(wkeys), nbytes=nbytes)
         self._track(comp)
         return comp
 
