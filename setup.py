@@ -37,6 +37,11 @@ CORE_SOURCES = [
     src("kernels", "io_kernel.cu"),
     src("kernels", "io_noalloc.cu"),
     src("objects", "object_store.cpp"),
+    src("config", "yaml_lite.cpp"),
+    src("config", "runtime_spec.cpp"),
+    src("daemon", "lease_ledger.cpp"),
+    src("daemon", "daemon_client.cpp"),
+    src("runtime", "tutti_runtime.cpp"),
     src("python", "presets.cpp"),
     src("python", "core_module.cpp"),
 ]

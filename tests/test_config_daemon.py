@@ -1,0 +1,215 @@
+"""Native runtime configuration (YAML spec, validation, assembly) and tutti_daemon leases."""
+import os
+import signal
+import socket
+import subprocess
+import sys
+import textwrap
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from tutti_b200._native import core
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+DAEMON = os.path.join(ROOT, "tutti_b200", "bin", "tutti_daemon")
+
+DEVICE_GROUP = """
+# nvme-device-group over two emulated drives
+accelerator:
+  profile: CUDA
+runtime:
+  accel_id: 0
+storage:
+  resources:
+    - id: nvme-group
+      type: nvme
+      provider: {type: emulated}
+      allocation:
+        selection: device-group
+        device_ids: [0, 1]
+        queues_per_controller: 16
+      config:
+        mounts: ["{m0}", "{m1}"]
+        controller_threads: 2
+  resolvers:
+    - id: file-resolver
+      type: local-file
+      scheme: file
+      config: {topology: multi-mount}
+  datapaths:
+    - id: dg
+      type: nvme-device-group
+      config: {leases: 16, slots_per_lease: 4}
+  backends:
+    - id: storage
+      contract: nvme-device-group
+      resolver: file-resolver
+      datapath: dg
+      resource: nvme-group
+      config: {}
+"""
+
+POSIX = """
+storage:
+  resolvers:
+    - {id: r, type: local-file, config: {topology: multi-mount}}
+  resources:
+    - id: mem
+      type: memory
+      config: {mounts: ["{m0}"]}
+  datapaths:
+    - {id: p, type: posix, config: {threads: 2, direct_io: false}}
+  backends:
+    - {id: b, contract: posix, resolver: r, datapath: p, resource: mem}
+"""
+
+
+def test_parse_device_group_spec(tmp_path):
+    d = core().parse_runtime_config(DEVICE_GROUP.replace("{m0}", "/a").replace("{m1}", "/b"))
+    assert d["resources"][0]["device_ids"] == [0, 1]
+    assert d["resources"][0]["mounts"] == ["/a", "/b"]
+    assert d["resolvers"][0]["topology"] == "multi-mount"
+    assert d["backends"][0]["contract"] == "nvme-device-group"
+    assert d["datapaths"][0]["leases"] == 16
+
+
+@pytest.mark.parametrize("mutation,needle", [
+    (lambda s: s.replace("topology: multi-mount", "topology: multi-mount, bogus: 1"),
+     "storage.resolvers[0].config.bogus: unknown field"),
+    (lambda s: s.replace("contract: nvme-device-group", "contract: nfs"), "unknown contract"),
+    (lambda s: s.replace("datapath: dg", "datapath: nope"), "unknown datapath"),
+    (lambda s: s.replace("id: dg", "id: file-resolver"), "duplicate id"),
+    (lambda s: s.replace("type: nvme-device-group\n", "type: posix\n"), "needs an nvme datapath"),
+    (lambda s: s.replace("slots_per_lease: 4", "slots_per_lease: 99"), "slots_per_lease"),
+    (lambda s: s.replace("profile: CUDA", "profile: MUSA"), "CUDA"),
+])
+def test_spec_validation_fails_closed_with_paths(mutation, needle):
+    text = mutation(DEVICE_GROUP.replace("{m0}", "/a").replace("{m1}", "/b"))
+    with pytest.raises(ValueError) as e:
+        core().parse_runtime_config(text)
+    assert needle in str(e.value)
+
+
+def test_yaml_errors_name_lines():
+    with pytest.raises(ValueError) as e:
+        core().parse_runtime_config("storage:\n  resolvers:\n    - id: x\n      type: [unclosed\n")
+    assert "line 4" in str(e.value)
+    with pytest.raises(ValueError):
+        core().parse_runtime_config("storage:\n  a: 1\n  a: 2\n")
+
+
+def test_posix_runtime_assembled_from_config_roundtrip(tmp_path):
+    m0 = tmp_path / "m0"
+    m0.mkdir()
+    f = m0 / "obj.bin"
+    f.write_bytes(bytes(range(256)) * 64)
+    rt = core().make_runtime_from_config(POSIX.replace("{m0}", str(m0)))
+    try:
+        buf = torch.zeros(16384, dtype=torch.uint8)
+        mh = rt.register_memory(buf.data_ptr(), buf.numel(), "host", -1)
+        th = rt.open(str(f))
+        assert rt.query_target(th)["size"] == 16384
+        r = rt.submit_arrays("read", np.array([mh], np.uint64), np.array([0], np.uint64), np.array([th], np.uint64),
+                             np.array([0], np.uint64), np.array([16384], np.uint64), 0, True)
+        res = rt.wait(r["io"], 10000)
+        rt.release_io(r["io"])
+        assert res["ok"] and res["confirmed_bytes"] == 16384
+        assert bytes(buf.numpy()) == f.read_bytes()
+    finally:
+        rt.shutdown(5000)
+
+
+def test_daemon_protocol_in_process():
+    out = core().daemon_handle_request_selftest(
+        ["HELLO client=t pid=0", "ACQUIRE session=1 devices=0,1 queues=8", "LIST",
+         "ACQUIRE session=1 devices=1 queues=60", "RELEASE lease=2", "ACQUIRE session=1 devices=1 queues=60",
+         "NOPE"],
+        [{"id": 0, "mount": "/m0", "queues": 64}, {"id": 1, "mount": "/m1", "queues": 64}])
+    assert out[0].startswith("OK") and "session=1" in out[0]
+    assert "lease=2" in out[1] and "mounts=/m0,/m1" in out[1] and "first_queue=0,0" in out[1]
+    assert "free_queues=56,56" in out[2]
+    assert out[3].startswith("ERR") and "RESOURCE_EXHAUSTED" in out[3]  # all-or-nothing budget
+    assert out[4].startswith("OK")
+    assert out[5].startswith("OK")
+    assert out[6].startswith("ERR")
+
+
+class Client:
+    def __init__(self, path):
+        self.s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        self.s.connect(path)
+        self.f = self.s.makefile("rwb")
+
+    def __call__(self, line):
+        self.f.write((line + "\n").encode())
+        self.f.flush()
+        return self.f.readline().decode().strip()
+
+    def kv(self, line):
+        rsp = self(line)
+        assert rsp.startswith("OK"), rsp
+        return dict(t.split("=", 1) for t in rsp.split()[1:])
+
+
+@pytest.fixture
+def daemon(tmp_path):
+    if not os.path.exists(DAEMON):
+        pytest.skip("tutti_daemon not built")
+    sock = str(tmp_path / "d.sock")
+    cfg = tmp_path / "daemon.yaml"
+    cfg.write_text(textwrap.dedent(f"""
+        service: {{socket: {sock}}}
+        lease: {{heartbeat_timeout_s: 1, reap_interval_ms: 100}}
+        devices:
+          - {{id: 0, kind: emulated, mount: {tmp_path}/nvme0, queues: 32}}
+          - {{id: 1, kind: emulated, mount: {tmp_path}/nvme1, queues: 32}}
+        """))
+    p = subprocess.Popen([DAEMON, "--config", str(cfg)], stderr=subprocess.PIPE)
+    for _ in range(100):
+        if os.path.exists(sock):
+            break
+        time.sleep(0.05)
+    yield sock
+    p.send_signal(signal.SIGTERM)
+    p.wait(timeout=10)
+
+
+def test_daemon_lease_heartbeat_expiry(daemon):
+    c = Client(daemon)
+    sess = c.kv(f"HELLO client=test pid={os.getpid()}")["session"]
+    lease = c.kv(f"ACQUIRE session={sess} devices=0,1 queues=16")["lease"]
+    assert c.kv("LIST")["free_queues"] == "16,16"
+    for _ in range(3):
+        time.sleep(0.5)
+        c.kv(f"HEARTBEAT lease={lease}")
+    assert c.kv("STATUS")["leases"] == "1"
+    time.sleep(2.0)  # no heartbeat for > 1 s: reaped
+    assert c.kv("STATUS")["leases"] == "0"
+    assert c.kv("LIST")["free_queues"] == "32,32"
+
+
+def test_daemon_reaps_a_crashed_client(daemon):
+    code = textwrap.dedent(f"""
+        import socket, os, time
+        s = socket.socket(socket.AF_UNIX); s.connect({daemon!r}); f = s.makefile('rwb')
+        def rq(l):
+            f.write((l + '\\n').encode()); f.flush(); return f.readline().decode()
+        sess = rq('HELLO client=victim pid=%d' % os.getpid()).split('session=')[1].split()[0]
+        print(rq('ACQUIRE session=%s devices=0 queues=32' % sess), flush=True)
+        while True:
+            rq('HEARTBEAT lease=2'); time.sleep(0.2)
+        """)
+    child = subprocess.Popen([sys.executable, "-c", code], stdout=subprocess.PIPE)
+    assert child.stdout.readline().decode().startswith("OK")
+    c = Client(daemon)
+    assert c.kv("LIST")["free_queues"].startswith("0,")
+    child.kill()  # the client dies holding a lease (a host process, no GPU involved)
+    child.wait()
+    deadline = time.time() + 5
+    while time.time() < deadline and c.kv("STATUS")["leases"] != "0":
+        time.sleep(0.1)
+    assert c.kv("STATUS")["leases"] == "0"
+    assert c.kv("LIST")["free_queues"] == "32,32"

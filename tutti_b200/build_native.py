@@ -1,0 +1,50 @@
+"""Builds the standalone native executables next to the package:
+
+* ``tutti_b200/bin/tutti_daemon``        - the device-manager daemon (queue leases);
+* ``tutti_b200/bin/tutti_native_tests``  - C++ contract tests of the runtime
+  (StorageRuntime against the mock DataPath kit, object store, config spec).
+
+    python -m tutti_b200.build_native
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(PKG, "csrc")
+BIN = os.path.join(PKG, "bin")
+CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+
+CXX = ["g++", "-O2", "-std=c++17", "-pthread", "-I", os.path.join(CSRC, "include"), "-I", CSRC,
+       "-I", os.path.join(CUDA, "include")]
+
+TARGETS = {
+    "tutti_daemon": (["daemon/daemon_main.cpp", "daemon/lease_ledger.cpp", "config/yaml_lite.cpp"], []),
+    "tutti_native_tests": ([
+        "tests/native_tests.cpp", "runtime/storage_runtime.cpp", "objects/object_store.cpp",
+        "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
+        "resolvers/file_resolvers.cpp",
+    ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
+}
+
+
+def build(names=None) -> None:
+    os.makedirs(BIN, exist_ok=True)
+    for name, (srcs, libs) in TARGETS.items():
+        if names and name not in names:
+            continue
+        paths = [os.path.join(CSRC, s) for s in srcs]
+        if not all(os.path.exists(p) for p in paths):
+            continue
+        out = os.path.join(BIN, name)
+        newest = max(os.path.getmtime(os.path.join(d, f)) for d, _, fs in os.walk(CSRC) for f in fs
+                     if f.endswith((".h", ".cpp", ".cuh")))
+        if os.path.exists(out) and newest <= os.path.getmtime(out):
+            continue
+        subprocess.run(CXX + paths + ["-o", out] + libs, check=True)
+
+
+if __name__ == "__main__":
+    build(sys.argv[1:] or None)

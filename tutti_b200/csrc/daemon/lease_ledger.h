@@ -1,0 +1,108 @@
+#pragma once
+// Queue-lease ledger of the device-manager daemon.
+//
+// The daemon is the host-level owner of the NVMe devices: it knows each
+// device's mount and queue budget, and GPU processes lease queues from it.
+// A lease names a client session and, per device, a number of I/O queues.
+// Leases end by explicit release, by heartbeat expiry, or when the reaper
+// finds the client process gone (its PID no longer exists, or exists with a
+// different start time, i.e. the PID was reused).
+// Parity: reference csrc/device_manager/nvme/nvmeservice (ServiceState
+// queue-reservation ledger, leases with heartbeat, PID/starttime reaper:
+// nvmeservice_state.h:190, nvmeservice_state.cpp:29-46,138).
+
+#include <chrono>
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <tutti/status.h>
+
+namespace tutti {
+namespace daemon {
+
+struct DeviceInfo {
+    std::int64_t id = 0;
+    std::string kind = "emulated";  // emulated | nvme
+    std::string mount;
+    std::string pci;
+    std::uint32_t queues = 64;      // queue budget offered to clients
+    std::uint32_t namespace_id = 1;
+    std::uint32_t lba_bytes = 512;
+};
+
+struct Grant {
+    std::int64_t device = 0;
+    std::uint32_t queues = 0;
+    std::uint32_t first_queue = 0;  // the device's queue range [first, first+queues)
+};
+
+struct Lease {
+    std::uint64_t id = 0;
+    std::uint64_t session = 0;
+    std::vector<Grant> grants;
+    std::chrono::steady_clock::time_point last_heartbeat;
+};
+
+struct Session {
+    std::uint64_t id = 0;
+    std::string client;
+    std::int64_t pid = 0;
+    std::uint64_t start_time = 0;  // /proc/<pid>/stat field 22 at HELLO
+};
+
+// Reads /proc/<pid>/stat start time (clock ticks since boot); 0 if the process is gone.
+std::uint64_t process_start_time(std::int64_t pid);
+
+class LeaseLedger {
+public:
+    explicit LeaseLedger(std::vector<DeviceInfo> devices);
+
+    Result<std::uint64_t> open_session(const std::string& client, std::int64_t pid, std::uint64_t start_time);
+    Status close_session(std::uint64_t session);  // releases its leases
+
+    // All-or-nothing: either every device gets `queues` queues or nothing changes.
+    Result<Lease> acquire(std::uint64_t session, const std::vector<std::int64_t>& devices, std::uint32_t queues);
+    Status heartbeat(std::uint64_t lease);
+    Status release(std::uint64_t lease);
+
+    // Releases leases whose heartbeat is older than `timeout`, and sessions
+    // whose process is gone according to `alive(pid, start_time)`.
+    std::vector<std::uint64_t> reap(std::chrono::steady_clock::duration timeout,
+                                    const std::function<bool(std::int64_t, std::uint64_t)>& alive);
+
+    std::vector<DeviceInfo> devices() const;
+    std::uint32_t free_queues(std::int64_t device) const;
+    std::size_t lease_count() const;
+    const DeviceInfo* device(std::int64_t id) const;
+
+private:
+    void release_locked(std::uint64_t lease);
+    mutable std::mutex mu_;
+    std::vector<DeviceInfo> devices_;
+    std::map<std::int64_t, std::vector<bool>> used_;  // device -> queue slot in use
+    std::map<std::uint64_t, Session> sessions_;
+    std::map<std::uint64_t, Lease> leases_;
+    std::uint64_t next_ = 1;
+};
+
+// Line protocol: "VERB key=value key=value\n" -> "OK key=value ...\n" | "ERR message\n".
+struct Message {
+    std::string verb;
+    std::map<std::string, std::string> kv;
+    std::string get(const std::string& k, const std::string& def = "") const {
+        auto it = kv.find(k);
+        return it == kv.end() ? def : it->second;
+    }
+};
+Message parse_message(const std::string& line);
+std::string format_message(const Message& m);
+
+// Handles one request against the ledger (used by the server and by tests).
+std::string handle_request(LeaseLedger& ledger, const std::string& line);
+
+}  // namespace daemon
+}  // namespace tutti

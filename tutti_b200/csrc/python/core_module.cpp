@@ -24,7 +24,10 @@
 #include "../nvme/controller.h"
 #include "../objects/digest.h"
 #include "../objects/object_store.h"
+#include "../config/runtime_spec.h"
+#include "../daemon/lease_ledger.h"
 #include "../resolvers/file_resolvers.h"
+#include "../runtime/tutti_runtime.h"
 #include "presets.h"
 
 namespace py = pybind11;
@@ -94,6 +97,7 @@ MemoryKind parse_kind(const std::string& k) {
 
 // Python-facing runtime: owns the StorageRuntime and anything its components need.
 struct PyRuntime {
+    std::shared_ptr<TuttiRuntime> assembly;  // spec-assembled runtimes: lease + controllers (outlive rt)
     std::unique_ptr<StorageRuntime> rt;
     PresetExtras extras;
     std::uint32_t rid() const {
@@ -505,6 +509,101 @@ PYBIND11_MODULE(_core, m) {
             return wrap(unwrap(make_posix_runtime(o)));
         },
         py::arg("accel_id"), py::arg("mounts"), py::arg("options") = py::dict());
+
+    m.def(
+        "parse_runtime_config",
+        [](const std::string& text, bool validate) {
+            auto s = unwrap(parse_runtime_config_text(text));
+            if (validate) check(validate_runtime_spec(s));
+            py::dict d;
+            d["profile"] = s.profile;
+            d["accel_id"] = s.accel_id;
+            py::list res, rsl, dps, bes;
+            for (auto& r : s.resources) {
+                py::dict x;
+                x["id"] = r.id;
+                x["type"] = r.type;
+                x["provider"] = r.provider;
+                x["endpoint"] = r.endpoint;
+                x["device_ids"] = r.device_ids;
+                x["queues_per_controller"] = r.queues_per_controller;
+                x["mounts"] = r.mounts;
+                res.append(x);
+            }
+            for (auto& r : s.resolvers) {
+                py::dict x;
+                x["id"] = r.id;
+                x["type"] = r.type;
+                x["scheme"] = r.scheme;
+                x["topology"] = r.topology;
+                x["mapping"] = r.mapping;
+                x["md"] = r.md;
+                rsl.append(x);
+            }
+            for (auto& p : s.datapaths) {
+                py::dict x;
+                x["id"] = p.id;
+                x["type"] = p.type;
+                x["leases"] = p.leases;
+                x["slots_per_lease"] = p.slots_per_lease;
+                dps.append(x);
+            }
+            for (auto& b : s.backends) {
+                py::dict x;
+                x["id"] = b.id;
+                x["contract"] = b.contract;
+                x["resolver"] = b.resolver;
+                x["datapath"] = b.datapath;
+                x["resource"] = b.resource;
+                bes.append(x);
+            }
+            d["resources"] = res;
+            d["resolvers"] = rsl;
+            d["datapaths"] = dps;
+            d["backends"] = bes;
+            return d;
+        },
+        py::arg("text"), py::arg("validate") = true);
+
+    m.def(
+        "make_runtime_from_config",
+        [](const std::string& text_or_path, bool is_path) {
+            Result<TuttiRuntimeSpec> spec = is_path ? parse_runtime_config_file(text_or_path)
+                                                    : parse_runtime_config_text(text_or_path);
+            if (!spec.ok()) raise(spec.status());
+            Result<std::unique_ptr<TuttiRuntime>> tr = Result<std::unique_ptr<TuttiRuntime>>::Failure({StatusCode::INTERNAL, "unset"});
+            {
+                py::gil_scoped_release nogil;
+                tr = TuttiRuntime::create(spec.value());
+            }
+            std::shared_ptr<TuttiRuntime> asmbl(unwrap(std::move(tr)).release());
+            auto r = std::make_shared<PyRuntime>();
+            r->assembly = asmbl;
+            r->extras.controllers = asmbl->controllers;
+            r->extras.gpu_path = asmbl->gpu_path;
+            r->extras.posix_path = asmbl->posix_path;
+            r->rt = asmbl->take_storage();
+            r->rid_ = r->rt->runtime_id();
+            return r;
+        },
+        py::arg("config"), py::arg("is_path") = false);
+
+    m.def("daemon_handle_request_selftest", [](const std::vector<std::string>& lines, py::list devices) {
+        // Runs lines through an in-process ledger (protocol tests without a socket).
+        std::vector<tutti::daemon::DeviceInfo> devs;
+        for (auto item : devices) {
+            auto d = item.cast<py::dict>();
+            tutti::daemon::DeviceInfo info;
+            info.id = d["id"].cast<std::int64_t>();
+            info.mount = d["mount"].cast<std::string>();
+            info.queues = d["queues"].cast<std::uint32_t>();
+            devs.push_back(info);
+        }
+        tutti::daemon::LeaseLedger ledger(devs);
+        std::vector<std::string> out;
+        for (auto& l : lines) out.push_back(tutti::daemon::handle_request(ledger, l));
+        return out;
+    });
 
     m.def("make_stub_runtime", [](int accel_id) {
         RuntimeConfig c;

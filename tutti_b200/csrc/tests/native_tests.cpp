@@ -1,0 +1,322 @@
+// C++ contract tests of the native runtime (no GPU, no NVMe).
+// Suites: StorageRuntime against the mock DataPath kit (partial commit,
+// lifecycle, budgets, failure attribution), stub runtime, object store
+// format and recovery, config spec validation.
+// Parity: reference tests/storage_runtime/contract/storage_runtime_contract_test.cpp,
+// tests/storage_objects/*, tests/config/{parser,spec}.
+//
+//   tutti_native_tests [--filter substring]
+
+#include <unistd.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <string>
+#include <vector>
+
+#include <tutti/storage_runtime.h>
+
+#include "../config/runtime_spec.h"
+#include "../objects/digest.h"
+#include "../objects/object_store.h"
+#include "../testing/mock_data_path.h"
+
+using namespace tutti;
+using namespace tutti::testing;
+
+namespace {
+struct TestCase {
+    const char* name;
+    std::function<void()> fn;
+};
+std::vector<TestCase>& registry() {
+    static std::vector<TestCase> r;
+    return r;
+}
+struct Reg {
+    Reg(const char* n, std::function<void()> f) { registry().push_back({n, std::move(f)}); }
+};
+int g_failures = 0;
+#define TEST(name)                   \
+    void name();                     \
+    Reg reg_##name(#name, name);     \
+    void name()
+#define CHECK(cond)                                                                   \
+    do {                                                                              \
+        if (!(cond)) {                                                                \
+            std::fprintf(stderr, "  CHECK failed %s:%d: %s\n", __FILE__, __LINE__, #cond); \
+            ++g_failures;                                                             \
+            return;                                                                   \
+        }                                                                             \
+    } while (0)
+
+struct Fixture {
+    MemResolver resolver;
+    MockDataPath dp;
+    std::unique_ptr<StorageRuntime> rt;
+    std::vector<char> buf = std::vector<char>(1 << 16, 0);
+    MemoryHandle mem;
+    TargetHandle tgt;
+    explicit Fixture(std::uint64_t budget = 64) {
+        auto blob = std::make_shared<std::string>(1 << 16, '\0');
+        for (std::size_t i = 0; i < blob->size(); ++i) (*blob)[i] = static_cast<char>(i * 7);
+        resolver.objects["a"] = blob;
+        RuntimeConfig c;
+        c.accel_id = 0;
+        c.max_terminal_results = budget;
+        RuntimeComponents comps;
+        comps.resolvers.push_back({"mem", &resolver});
+        comps.data_paths.push_back({"mock", &dp, DataPathConfig{"mock"}});
+        rt = StorageRuntime::create(c, comps).value();
+        MemoryView v;
+        v.address = buf.data();
+        v.size = buf.size();
+        v.expected_kind = MemoryKind::HOST;
+        mem = rt->register_memory(v).value();
+        tgt = rt->open("mem://a").value();
+    }
+    IoRequest req(std::uint64_t off, std::uint64_t len, IoDirection d = IoDirection::READ) {
+        return IoRequest{d, mem, off, tgt, off, len};
+    }
+    HostSubmitContext ctx() { return HostSubmitContext{ExecutionDomain::HOST_EXECUTION, -1, nullptr}; }
+};
+}  // namespace
+
+TEST(runtime_read_write_roundtrip) {
+    Fixture f;
+    IoRequest r[2] = {f.req(0, 4096), f.req(8192, 4096)};
+    auto o = f.rt->submit(r, 2, f.ctx());
+    CHECK(o.status.ok() && o.io.has_value());
+    auto w = f.rt->wait(*o.io, 1000);
+    CHECK(w.observation_status.ok() && w.result->state == IoState::COMPLETED);
+    CHECK(w.result->detail.confirmed_bytes == 8192);
+    CHECK(f.buf[100] == static_cast<char>(100 * 7));
+    CHECK(f.rt->release_io(*o.io).ok());
+}
+
+TEST(runtime_partial_commit) {
+    Fixture f;
+    f.dp.set_reject_at_index(1);
+    IoRequest r[3] = {f.req(0, 512), f.req(512, 512), f.req(1024, 512)};
+    auto o = f.rt->submit(r, 3, f.ctx());
+    CHECK(o.io.has_value());
+    CHECK(!o.status.ok());
+    CHECK(o.initial_states[0].state == IoRequestState::ACCEPTED);
+    CHECK(o.initial_states[1].state == IoRequestState::REJECTED);
+    CHECK(o.initial_states[2].state == IoRequestState::ACCEPTED);
+    auto w = f.rt->wait(*o.io, 1000);
+    CHECK(w.result->detail.confirmed_bytes == 1024);
+}
+
+TEST(runtime_all_rejected_has_no_io) {
+    Fixture f;
+    IoRequest r[1] = {f.req(0, 1 << 20)};  // beyond the target
+    auto o = f.rt->submit(r, 1, f.ctx());
+    CHECK(!o.io.has_value());
+    CHECK(o.initial_states[0].status.code() == StatusCode::OUT_OF_RANGE);
+    auto o2 = f.rt->submit(r, 0, f.ctx());
+    CHECK(!o2.io.has_value() && o2.status.ok() && o2.initial_states.empty());
+}
+
+TEST(runtime_wait_timeout_and_release_busy) {
+    Fixture f;
+    f.dp.set_manual_mode(true);
+    IoRequest r[1] = {f.req(0, 4096)};
+    auto o = f.rt->submit(r, 1, f.ctx());
+    auto w = f.rt->wait(*o.io, 10);
+    CHECK(w.observation_status.code() == StatusCode::TIMEOUT && !w.result);
+    CHECK(f.rt->release_io(*o.io).code() == StatusCode::BUSY);
+    CHECK(f.rt->close(f.tgt).code() == StatusCode::BUSY);
+    CHECK(f.rt->unregister_memory(f.mem).code() == StatusCode::BUSY);
+    f.dp.complete_all();
+    CHECK(f.rt->wait(*o.io, 1000).observation_status.ok());
+    CHECK(f.rt->release_io(*o.io).ok());
+    CHECK(f.rt->close(f.tgt).ok());
+}
+
+TEST(runtime_terminal_result_budget) {
+    Fixture f(2);
+    IoRequest r[1] = {f.req(0, 512)};
+    auto a = f.rt->submit(r, 1, f.ctx());
+    auto b = f.rt->submit(r, 1, f.ctx());
+    f.rt->wait(*a.io, 1000);
+    f.rt->wait(*b.io, 1000);
+    auto c = f.rt->submit(r, 1, f.ctx());
+    CHECK(!c.io && c.status.code() == StatusCode::RESOURCE_EXHAUSTED);
+    CHECK(f.rt->release_io(*a.io).ok());
+    auto d = f.rt->submit(r, 1, f.ctx());
+    CHECK(d.io.has_value());
+}
+
+TEST(runtime_failure_attribution) {
+    Fixture f;
+    f.dp.set_fail_request(2);
+    IoRequest r[4] = {f.req(0, 512), f.req(512, 512), f.req(1024, 512), f.req(1536, 512)};
+    auto o = f.rt->submit(r, 4, f.ctx());
+    auto res = f.rt->wait_detail(*o.io, 1000);
+    CHECK(res.ok());
+    CHECK(res.value().state == IoState::FAILED);
+    CHECK(res.value().detail.failure_scope == IoFailureScope::REQUEST_INDICES);
+    CHECK(res.value().detail.failed_request_indices.size() == 1 && res.value().detail.failed_request_indices[0] == 2);
+    CHECK(res.value().detail.confirmed_bytes == 1536);
+}
+
+TEST(runtime_handles_are_runtime_scoped_and_generational) {
+    Fixture f, g;
+    IoRequest r[1] = {IoRequest{IoDirection::READ, g.mem, 0, f.tgt, 0, 512}};
+    auto o = f.rt->submit(r, 1, f.ctx());
+    CHECK(!o.io && o.initial_states[0].status.code() == StatusCode::NOT_FOUND);
+    CHECK(f.rt->close(f.tgt).ok());
+    CHECK(f.rt->close(f.tgt).code() == StatusCode::NOT_FOUND);  // stale generation
+    auto t2 = f.rt->open("mem://a");
+    CHECK(t2.ok() && t2.value() != f.tgt);
+}
+
+TEST(runtime_execution_domain_and_accel_checks) {
+    Fixture f;
+    IoRequest r[1] = {f.req(0, 512)};
+    HostSubmitContext dev{ExecutionDomain::DEVICE_EXECUTION, -1, nullptr};
+    auto o = f.rt->submit(r, 1, dev);
+    CHECK(!o.io && o.initial_states[0].status.code() == StatusCode::UNSUPPORTED);
+    HostSubmitContext other{ExecutionDomain::HOST_EXECUTION, 3, nullptr};
+    auto o2 = f.rt->submit(r, 1, other);
+    CHECK(!o2.io && o2.status.code() == StatusCode::INVALID_ARGUMENT);
+}
+
+TEST(runtime_open_batch_per_item_results) {
+    Fixture f;
+    auto v = f.rt->open_batch({"mem://a", "mem://missing", "nfs://x", "mem://a"});
+    CHECK(v.size() == 4);
+    CHECK(v[0].ok() && v[3].ok() && v[0].value() != v[3].value());
+    CHECK(!v[1].ok() && v[1].status().code() == StatusCode::NOT_FOUND);
+    CHECK(!v[2].ok());
+}
+
+TEST(runtime_overlapping_registration_refused) {
+    Fixture f;
+    MemoryView v;
+    v.address = f.buf.data() + 100;
+    v.size = 10;
+    v.expected_kind = MemoryKind::HOST;
+    CHECK(f.rt->register_memory(v).status().code() == StatusCode::INVALID_ARGUMENT);
+}
+
+TEST(runtime_shutdown_drains_and_stops) {
+    Fixture f;
+    IoRequest r[1] = {f.req(0, 512)};
+    auto o = f.rt->submit(r, 1, f.ctx());
+    CHECK(o.io.has_value());
+    CHECK(f.rt->shutdown(1000).ok());
+    CHECK(f.rt->state() == RuntimeState::STOPPED);
+    CHECK(f.dp.shut_down);
+    MemoryView v;
+    v.address = f.buf.data();
+    v.size = 16;
+    CHECK(f.rt->register_memory(v).status().code() == StatusCode::NOT_READY);
+}
+
+TEST(runtime_shutdown_times_out_with_inflight_io) {
+    Fixture f;
+    f.dp.set_manual_mode(true);
+    IoRequest r[1] = {f.req(0, 512)};
+    auto o = f.rt->submit(r, 1, f.ctx());
+    CHECK(f.rt->shutdown(20).code() == StatusCode::TIMEOUT);
+    f.dp.complete_all();
+    CHECK(f.rt->shutdown(1000).ok());
+}
+
+TEST(stub_runtime_memory_only) {
+    RuntimeConfig c;
+    auto rt = StorageRuntime::create_stub(c);
+    std::vector<char> b(64);
+    MemoryView v;
+    v.address = b.data();
+    v.size = b.size();
+    v.expected_kind = MemoryKind::HOST;
+    auto h = rt->register_memory(v);
+    CHECK(h.ok());
+    CHECK(rt->query_memory(h.value()).value().size == 64);
+    CHECK(rt->open("file:///x").status().code() == StatusCode::NOT_FOUND);
+    CHECK(rt->unregister_memory(h.value()).ok());
+}
+
+TEST(digest_check_values) {
+    CHECK(crc32c("123456789", 9) == 0xE3069283u);
+    CHECK(object_identity(nullptr, 0) == object_identity("", 0));
+    CHECK(object_identity("a", 1) != object_identity("b", 1));
+}
+
+TEST(object_store_commit_recover) {
+    char tmpl[] = "/tmp/tutti_native_XXXXXX";
+    const char* dir = mkdtemp(tmpl);
+    CHECK(dir != nullptr);
+    StoreConfig c;
+    c.uri = dir;
+    c.layout.segment_bytes = 8192;
+    c.layout.segment_count = 2;
+    c.segment_file_slots = 4;
+    c.segment_header_bytes = 4096;
+    c.capacity_slots = 8;
+    {
+        SegmentFileObjectStore s;
+        CHECK(s.open(c).ok());
+        ObjectKey k{{1, 2, 3}};
+        CHECK(s.reserve(&k, 1).ok());
+        CHECK(s.commit(&k, 1).ok());
+        CHECK(s.contains(k));
+        CHECK(s.close().ok());
+    }
+    {
+        SegmentFileObjectStore s;
+        CHECK(s.open(c).ok());
+        auto keys = s.recover();
+        CHECK(keys.ok() && keys.value().size() == 1 && keys.value()[0].bytes == std::vector<std::uint8_t>({1, 2, 3}));
+        CHECK(s.close().ok());
+    }
+    c.namespace_fingerprint = {9};
+    SegmentFileObjectStore s3;
+    CHECK(s3.open(c).code() == StatusCode::INVALID_ARGUMENT);
+    std::string cmd = std::string("rm -rf ") + dir;
+    CHECK(std::system(cmd.c_str()) == 0);
+}
+
+TEST(config_spec_contract_matrix) {
+    const char* ok = R"(
+storage:
+  resources:
+    - {id: r, type: nvme, provider: {type: emulated}, config: {mounts: [/a]}}
+  resolvers:
+    - {id: f, type: local-file, config: {topology: single}}
+  datapaths:
+    - {id: d, type: local-nvme}
+  backends:
+    - {id: b, contract: ext4-local-nvme, resolver: f, datapath: d, resource: r}
+)";
+    auto s = parse_runtime_config_text(ok);
+    CHECK(s.ok());
+    CHECK(validate_runtime_spec(s.value()).ok());
+    std::string two = ok;
+    two.replace(two.find("[/a]"), 4, "[/a, /b]");
+    auto s2 = parse_runtime_config_text(two);
+    CHECK(s2.ok() && !validate_runtime_spec(s2.value()).ok());
+    auto s3 = parse_runtime_config_text(std::string(ok) + "  extra: 1\n");
+    CHECK(!s3.ok());
+}
+
+int main(int argc, char** argv) {
+    const char* filter = nullptr;
+    for (int i = 1; i + 1 < argc; ++i)
+        if (std::string(argv[i]) == "--filter") filter = argv[i + 1];
+    int run = 0;
+    for (auto& t : registry()) {
+        if (filter && !std::strstr(t.name, filter)) continue;
+        const int before = g_failures;
+        t.fn();
+        ++run;
+        std::printf("%s %s\n", g_failures == before ? "PASS" : "FAIL", t.name);
+    }
+    std::printf("%d test(s), %d failure(s)\n", run, g_failures);
+    return g_failures ? 1 : 0;
+}
