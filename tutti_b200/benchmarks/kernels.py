@@ -1,0 +1,153 @@
+"""Microbenchmarks of the sm_100a kernels, each on a case sized for an ncu capture.
+
+    python -m tutti_b200.benchmarks.kernels copy     # batched bulk page copy (HBM -> HBM, 32 KiB pages)
+    python -m tutti_b200.benchmarks.kernels fp8      # block-scaled fp8 quantise of bf16 rows
+    python -m tutti_b200.benchmarks.kernels hash     # chained BLAKE2b-128 prefix keys
+    python -m tutti_b200.benchmarks.kernels checksum # KV block checksums
+    python -m tutti_b200.benchmarks.kernels io       # fused NVMe io kernel restore (emulated controllers)
+
+Each prints one JSON line: kernel time (CUDA events, after warm-up, inputs
+larger than L2 where the kernel is bandwidth-bound) and achieved rates.
+``--iters`` sets timed launches; ``--warmup`` untimed ones.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import tempfile
+
+import numpy as np
+import torch
+
+
+def _time(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_copy(args) -> dict:
+    from .. import ops
+
+    nbytes = args.mib << 20
+    page = 32768
+    a = torch.empty(nbytes, dtype=torch.uint8, device="cuda").random_()
+    b = torch.empty_like(a)
+    n = nbytes // page
+    src = a.data_ptr() + torch.arange(n, device="cuda", dtype=torch.int64) * page
+    dst = b.data_ptr() + torch.randperm(n, device="cuda") * page
+    items = torch.stack([src, dst, torch.full_like(src, page)], 1).contiguous()
+    from .._native import ops as _ops
+
+    ms = _time(lambda: _ops().copy_items(items, True), args.iters, args.warmup)
+    ok = True
+    if args.verify:
+        ops.page_copy(src[:1], dst[:1], page)
+        ok = bool(torch.equal(b[int(dst[0] - b.data_ptr()):][:page], a[:page]))
+    return {"kernel": "bulk_copy_kernel", "bytes": nbytes, "ms": ms, "GBps_rw": 2 * nbytes / ms / 1e6,
+            "pages": n, "ok": ok}
+
+
+def bench_fp8(args) -> dict:
+    from .._native import ops as _ops
+
+    rows = (args.mib << 20) // 256
+    x = torch.randn(rows, 128, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(rows, 128, dtype=torch.uint8, device="cuda")
+    ms = _time(lambda: _ops().fp8_quant(x, 128), args.iters, args.warmup)
+    moved = x.numel() * 2 + q.numel() + rows * 4
+    return {"kernel": "quant_kernel", "rows": rows, "ms": ms, "GBps": moved / ms / 1e6}
+
+
+def bench_hash(args) -> dict:
+    from .. import ops
+    from ..index.chunk_index import chunk_keys_for_tokens
+
+    rng = np.random.default_rng(0)
+    reqs = [rng.integers(0, 150000, size=args.tokens).tolist() for _ in range(args.requests)]
+    import time
+
+    t0 = time.perf_counter()
+    ops.prefix_hash(reqs, args.chunk)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    for _ in range(args.iters):
+        keys = ops.prefix_hash(reqs, args.chunk)
+    torch.cuda.synchronize()
+    gpu_ms = (time.perf_counter() - t1) / args.iters * 1e3
+    t2 = time.perf_counter()
+    ref = [chunk_keys_for_tokens(r, args.chunk) for r in reqs]
+    cpu_ms = (time.perf_counter() - t2) * 1e3
+    return {"kernel": "prefix_hash_kernel", "requests": args.requests, "tokens": args.tokens, "gpu_ms": gpu_ms,
+            "cpu_hashlib_ms": cpu_ms, "ok": keys == ref, "first_call_ms": (t1 - t0) * 1e3}
+
+
+def bench_checksum(args) -> dict:
+    from .. import ops
+
+    nb = (args.mib << 20) // (2 * 2 * 16 * 8 * 128 * 2)
+    pool = torch.randn(2, 2, nb, 16, 8, 128, dtype=torch.bfloat16, device="cuda")
+    blocks = torch.arange(nb, device="cuda")
+    ms = _time(lambda: ops.kv_checksum(pool, blocks), args.iters, args.warmup)
+    nbytes = pool.numel() * 2
+    return {"kernel": "checksum_kernel", "bytes": nbytes, "ms": ms, "GBps": nbytes / ms / 1e6}
+
+
+def bench_io(args) -> dict:
+    from ..index.chunk_index import chunk_keys_for_tokens
+    from ..models.kv_geometry import LLAMA3_8B as g
+    from ..storage.tutti_store import TuttiKVStore
+
+    root = tempfile.mkdtemp(prefix="tutti_kio_")
+    try:
+        tokens = args.tokens
+        nblk = tokens // g.block_size
+        nch = tokens // g.chunk_tokens
+        st = TuttiKVStore(root, g, capacity_chunks=max(16, nch), mounts=[os.path.join(root, f"nvme{d}") for d in range(4)],
+                          device=0, segment_file_slots=max(4, nch // 4 + 1),
+                          runtime_options={"controller_threads": 3, "leases": 64, "max_ctas_per_op": 64,
+                                           "slots_per_lease": 8})
+        st.open()
+        nb = 2 * nblk + 64
+        pool = torch.randn(g.pool_shape(nb), dtype=g.dtype, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(tokens)), g.chunk_tokens)
+        src = np.arange(nblk).reshape(nch, g.blocks_per_chunk)
+        st.put_paged(keys, src).wait()
+        dst = (np.arange(nblk) + nblk).reshape(nch, g.blocks_per_chunk)
+        ms = _time(lambda: st.get_paged(keys, dst).wait(), args.iters, args.warmup)
+        ok = bool(torch.equal(pool[:, :, nblk:2 * nblk], pool[:, :, :nblk]))
+        nbytes = nblk * g.num_layers * g.block_layer_bytes
+        st.close()
+        return {"kernel": "nvme_io_kernel", "bytes": nbytes, "ms": ms, "GBps": nbytes / ms / 1e6, "ok": ok}
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("which", choices=["copy", "fp8", "hash", "checksum", "io"])
+    p.add_argument("--mib", type=int, default=1024)
+    p.add_argument("--iters", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--tokens", type=int, default=4096)
+    p.add_argument("--requests", type=int, default=256)
+    p.add_argument("--chunk", type=int, default=256)
+    p.add_argument("--verify", action="store_true")
+    args = p.parse_args(argv)
+    torch.cuda.set_device(0)
+    fn = {"copy": bench_copy, "fp8": bench_fp8, "hash": bench_hash, "checksum": bench_checksum, "io": bench_io}
+    print(json.dumps(fn[args.which](args)))
+
+
+if __name__ == "__main__":
+    main()
