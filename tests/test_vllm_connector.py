@@ -1,0 +1,198 @@
+"""vLLM connector: scheduler planning, worker load/save cycles, TP failure consensus (CPU)."""
+import os
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tutti_b200.integration.vllm.metadata import LoadSpec, SaveSpec, TuttiConnectorMetadata, TuttiWorkerMetadata
+from tutti_b200.integration.vllm.scheduler import SchedulerSide
+from tutti_b200.integration.vllm.worker import WorkerSide
+from tutti_b200.integration.vllm.factory import ConnectorConfig, make_engine, parse_bytes
+from tutti_b200.parallel.tp_consensus import ChunkFailure, TpFailureConsensus, encode_row, merge_rows
+
+BS, CHUNK = 4, 8  # 2 blocks per chunk
+
+
+def req(rid, n, base=0):
+    return SimpleNamespace(request_id=rid, prompt_token_ids=list(range(base, base + n)), num_computed_tokens=0)
+
+
+def test_scheduler_match_alignment_and_one_token_rule():
+    s = SchedulerSide(BS, CHUNK, capacity_chunks=64)
+    r = req("a", 24)
+    assert s.get_num_new_matched_tokens(r, 0) == (0, False)
+    keys = s.requests["a"].keys
+    assert len(keys) == 3
+    s.index.plan_store(keys)
+    s.index.confirm_store(keys)
+    # 24 tokens fully resident: still leave one token to compute -> 16
+    assert s.get_num_new_matched_tokens(r, 0) == (16, False)
+    # already computed 8 -> 8 more
+    assert s.get_num_new_matched_tokens(r, 8)[0] == 8
+    # mid-chunk computed -> no load
+    assert s.get_num_new_matched_tokens(r, 5)[0] == 0
+
+
+def test_scheduler_saves_published_only_when_all_ranks_commit():
+    s = SchedulerSide(BS, CHUNK, capacity_chunks=64, tp_size=2)
+    r = req("a", 17)
+    s.get_num_new_matched_tokens(r, 0)
+    s.update_state_after_alloc(r, list(range(10, 15)), 0)
+    meta = s.build_meta([("a", list(range(10, 15)), 0, 17)])
+    assert len(meta.saves) == 1 and len(meta.saves[0].keys) == 2
+    assert meta.saves[0].block_ids == [10, 11, 12, 13]
+    k0, k1 = meta.saves[0].keys
+    s.update_from_workers(TuttiWorkerMetadata({k0: 1, k1: 2}))
+    assert not s.index.is_resident(k0) and s.index.is_resident(k1)
+    s.update_from_workers(TuttiWorkerMetadata({k0: 1}).aggregate(TuttiWorkerMetadata({k0: 1})))
+    assert s.index.is_resident(k0)
+    # nothing new to save for the same request
+    assert s.build_meta([("a", list(range(10, 15)), 17, 1)]).saves == []
+
+
+def test_scheduler_load_spec_pins_until_finished():
+    s = SchedulerSide(BS, CHUNK, capacity_chunks=2)
+    r = req("a", 17)
+    s.get_num_new_matched_tokens(r, 0)
+    keys = s.requests["a"].keys
+    s.index.plan_store(keys)
+    s.index.confirm_store(keys)
+    ext, _ = s.get_num_new_matched_tokens(r, 0)
+    s.update_state_after_alloc(r, [7, 8, 9, 10, 11], ext)
+    meta = s.build_meta([])
+    assert meta.loads[0].keys == keys and meta.loads[0].block_ids == [7, 8, 9, 10]
+    assert s.index.is_pinned(keys[0])
+    assert s.index.plan_store([b"x" * 16, b"y" * 16]) is None  # pinned keys are never evicted
+    s.load_finished("a", keys, ok=True)
+    assert not s.index.is_pinned(keys[0])
+
+
+def make_worker(layers):
+    cfg = ConnectorConfig.from_extra({"chunk_tokens": CHUNK, "store": {"type": "memory", "capacity_chunks": 64}})
+    w = WorkerSide(lambda t: make_engine(cfg, t, 0, 0, 1), block_size=BS, chunk_tokens=CHUNK)
+    w.register_kv_caches({f"model.layers.{i}.self_attn.attn": t for i, t in enumerate(layers)})
+    return w
+
+
+def test_worker_save_then_load_roundtrip_cpu():
+    layers = [torch.randn(2, 32, BS, 2, 16) for _ in range(3)]
+    w = make_worker(layers)
+    keys = [bytes([i]) * 16 for i in range(2)]
+    wm = w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, [0, 1, 2, 3])]))
+    assert wm.committed == {keys[0]: 1, keys[1]: 1}
+    ref = [t[:, 0:4].clone() for t in layers]
+    meta = TuttiConnectorMetadata(2, [LoadSpec("b", keys, [20, 21, 22, 23], 16)], [])
+    w.start_load_kv(meta)
+    for i in range(3):
+        w.wait_for_layer_load(f"model.layers.{i}.self_attn.attn")
+    w.wait_for_save(meta)
+    for i in range(3):
+        assert torch.equal(layers[i][:, 20:24], ref[i])
+    assert w.get_block_ids_with_load_errors() == set()
+
+
+def test_worker_reports_load_error_blocks():
+    layers = [torch.randn(2, 32, BS, 2, 16) for _ in range(2)]
+    w = make_worker(layers)
+    missing = [b"m" * 16, b"n" * 16]
+    meta = TuttiConnectorMetadata(5, [LoadSpec("r", missing, [8, 9, 10, 11], 16)], [])
+    w.start_load_kv(meta)
+    wm = w.wait_for_save(meta)
+    assert wm.failed_loads == {"r": 0}
+    assert w.get_block_ids_with_load_errors() == {8, 9, 10, 11}
+
+
+def test_consensus_merge_rows():
+    rows = [encode_row(7, 3, [ChunkFailure(1, 4, 2)]), encode_row(7, 3, [ChunkFailure(1, 2, 1), ChunkFailure(2, 0, 1)]),
+            encode_row(7, 3, [])]
+    c = merge_rows(7, 3, rows)
+    assert c.failed and c.consistent
+    assert list(c.failed_chunks(1)) == [2, 3, 4, 5] and list(c.failed_chunks(2)) == [0]
+    assert not merge_rows(7, 3, [encode_row(7, 3, [])] * 2).failed
+    assert merge_rows(7, 3, [encode_row(7, 3, []), encode_row(8, 3, [])]).failed  # generation skew
+
+
+def _consensus_rank(rank, world, port, q, absent):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        if rank == absent:
+            q.put((rank, "absent"))
+            return  # this rank never joins the collective
+        c = TpFailureConsensus(timeout_s=3.0)
+        try:
+            failures = [ChunkFailure(0, 3, 2)] if rank == 1 else []
+            res = c.coordinate(11, 2, failures)
+            ok = c.drain_barrier(11, True) if res.failed else True
+            q.put((rank, (res.failed, tuple(res.failed_chunks(0)), ok)))
+        except Exception as e:  # noqa: BLE001
+            q.put((rank, type(e).__name__))
+    finally:
+        pass
+
+
+def _run(world, absent):
+    import socket
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_consensus_rank, args=(r, world, port, q, absent)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = dict(q.get(timeout=60) for _ in range(world))
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_consensus_two_gloo_ranks_agree():
+    out = _run(2, absent=-1)
+    assert out[0] == out[1] == (True, (3, 4), True)
+
+
+def test_consensus_missing_rank_times_out():
+    out = _run(2, absent=1)
+    assert out[1] == "absent"
+    assert out[0] in ("TimeoutError", "RuntimeError", "DistBackendError")
+
+
+def test_config_parsing():
+    c = ConnectorConfig.from_extra({"chunk_tokens": 512, "load_mode": "auto",
+                                    "store": {"root": "/r/{LOCAL_RANK}", "capacity": "2GiB"}})
+    assert c.chunk_tokens == 512 and c.capacity_bytes == 2 << 30
+    assert parse_bytes("1.5 GB") == 1_500_000_000
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"bogus": 1})
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"store": {"type": "s3"}})
+
+
+def test_connector_class_with_vllm_base():
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+
+    from tutti_b200.integration.vllm.connector import TuttiConnectorV1
+
+    cfg = SimpleNamespace(kv_transfer_config=SimpleNamespace(kv_connector_extra_config={"chunk_tokens": CHUNK}),
+                          cache_config=SimpleNamespace(block_size=BS),
+                          parallel_config=SimpleNamespace(tensor_parallel_size=1))
+    sch = TuttiConnectorV1(cfg, KVConnectorRole.SCHEDULER, None)
+    r = req("q", 20)
+    assert sch.get_num_new_matched_tokens(r, 0) == (0, False)
+    out = SimpleNamespace(scheduled_new_reqs=[SimpleNamespace(req_id="q", block_ids=([0, 1, 2, 3, 4],),
+                                                              num_computed_tokens=0)],
+                          num_scheduled_tokens={"q": 20}, scheduled_cached_reqs=None)
+    meta = sch.build_connector_meta(out)
+    assert len(meta.saves) == 1 and len(meta.saves[0].keys) == 2

@@ -181,8 +181,42 @@ class KVEngine:
     def bind(self, pool: torch.Tensor) -> None:
         """Bind the engine's paged KV pool (direct mode registers it with the store once)."""
         self.pool = pool
+        self.layers = None
         if not self.staged:
             self.store.register_pool(pool)
+
+    def bind_layers(self, layers: Sequence[torch.Tensor]) -> None:
+        """Bind one KV tensor per layer, ``[planes, num_blocks, block, heads, dim]`` (vLLM's layout)."""
+        self.layers = list(layers)
+        self.pool = self.layers[0]
+        if not self.staged:
+            self.store.register_layers(self.layers)
+
+    # -- staged (host-side) gather/scatter ------------------------------------
+    def _layer_views(self):
+        if getattr(self, "layers", None):
+            return self.layers
+        return [self.pool[i] for i in range(self.pool.shape[0])]
+
+    def _gather_chunks(self, bt: np.ndarray) -> torch.Tensor:
+        """Blocks -> bytes laid out like chunk segments: [chunk][layer][block][plane]."""
+        layers = self._layer_views()
+        idx = torch.from_numpy(bt.reshape(-1)).to(layers[0].device)
+        per_layer = [t[:, idx] for t in layers]  # [P, n*bpc, ...]
+        x = torch.stack(per_layer, 0)  # [L, P, n*bpc, ...]
+        n, bpc = bt.shape
+        x = x.reshape(x.shape[0], x.shape[1], n, bpc, *x.shape[3:]).permute(2, 0, 3, 1, *range(4, x.dim() + 1))
+        return x.contiguous().view(torch.uint8).reshape(n, -1)
+
+    def _scatter_chunks(self, data: torch.Tensor, bt: np.ndarray) -> None:
+        layers = self._layer_views()
+        n, bpc = bt.shape
+        P = layers[0].shape[0]
+        tail = layers[0].shape[2:]
+        x = data.reshape(-1).view(layers[0].dtype).reshape(n, len(layers), bpc, P, *tail)
+        idx = torch.from_numpy(bt.reshape(-1)).to(layers[0].device)
+        for li, t in enumerate(layers):
+            t[:, idx] = x[:, li].permute(2, 0, 1, *range(3, x.dim() - 1)).reshape(P, n * bpc, *tail).to(t.device)
 
     # -- restores -------------------------------------------------------------
     def _table(self, block_table) -> np.ndarray:
@@ -209,13 +243,17 @@ class KVEngine:
         return self._staged_load(keys, bt)
 
     def _staged_load(self, keys, bt):
-        from .. import ops
-
         g = self.geometry
-        staging = torch.empty(len(keys) * g.chunk_bytes, dtype=torch.uint8, device=self.device)
+        dev = self.pool.device
+        staging = torch.empty(len(keys) * g.chunk_bytes, dtype=torch.uint8, device=dev)
         comp = self.store.get_batch([(k, self._staging_id(staging), i * g.chunk_bytes) for i, k in enumerate(keys)])
         comp.wait()
-        ops.scatter_blocks(staging, self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
+        if dev.type == "cuda" and not getattr(self, "layers", None):
+            from .. import ops
+
+            ops.scatter_blocks(staging, self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
+        else:
+            self._scatter_chunks(staging, bt)
         return comp
 
     def _staging_id(self, staging: torch.Tensor) -> int:
@@ -245,20 +283,27 @@ class KVEngine:
             return None
         bt = self._table(block_table)[idx]
         wkeys = [keys[i] for i in idx]
-        stream = self.io_stream
-        if after is not None:
-            stream.wait_event(after)
-        else:
-            stream.wait_stream(torch.cuda.current_stream(self.device))
+        on_gpu = self.pool is not None and self.pool.device.type == "cuda"
+        stream = self.io_stream if on_gpu else None
+        if stream is not None:
+            if after is not None:
+                stream.wait_event(after)
+            else:
+                stream.wait_stream(torch.cuda.current_stream(self.device))
         if not self.staged:
             inner = self.store.put_paged(wkeys, bt, stream=stream)
         else:
-            from .. import ops
-
             g = self.geometry
-            with torch.cuda.stream(stream):
-                staging = ops.gather_blocks(self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
-            stream.synchronize()
+            if on_gpu and not getattr(self, "layers", None):
+                from .. import ops
+
+                with torch.cuda.stream(stream):
+                    staging = ops.gather_blocks(self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
+                stream.synchronize()
+            else:
+                if on_gpu:
+                    stream.synchronize()
+                staging = self._gather_chunks(bt).reshape(-1)
             bid = self._staging_id(staging)
             inner = self.store.put_batch([(k, bid, i * g.chunk_bytes) for i, k in enumerate(wkeys)])
         comp = PostCompletion(inner, after=lambda: self.index.confirm_store(wkeys, True),

@@ -1,0 +1,128 @@
+"""Connector configuration -> scheduler/worker components.
+
+``kv_connector_extra_config`` keys:
+  chunk_tokens             reuse unit in tokens (multiple of the engine block size; default 256)
+  namespace                key-chain namespace (default: model name + dtype)
+  load_mode                sync | async | auto (default sync: layerwise restore inside the forward)
+  kv_load_failure_policy   recompute | fail (default recompute)
+  store:
+    type                   tutti | memory
+    root                   namespace root (per-rank segment files under <mount>/r<rank>)
+    mounts                 backing mounts, one emulated NVMe drive each (default [root])
+    capacity_chunks        capacity in chunks (or capacity: "64GiB")
+    segment_file_slots     slots per segment file (default 2048)
+    runtime_options        options of the native runtime (leases, slots_per_lease, ...)
+Placeholders ``{LOCAL_RANK}`` / ``{RANK}`` in paths are expanded per worker.
+Parity: reference tutti/integration/vllm/factory.py:31-202 and
+config/integration/vllm/kv_transfer.json.
+"""
+from __future__ import annotations
+
+import os
+import re
+from dataclasses import dataclass, field
+
+import torch
+
+from ...models.kv_geometry import KVGeometry
+
+_UNITS = {"": 1, "b": 1, "kib": 1 << 10, "mib": 1 << 20, "gib": 1 << 30, "tib": 1 << 40,
+          "kb": 10 ** 3, "mb": 10 ** 6, "gb": 10 ** 9, "tb": 10 ** 12}
+
+
+def parse_bytes(s) -> int:
+    if isinstance(s, int):
+        return s
+    m = re.fullmatch(r"\s*([0-9.]+)\s*([a-zA-Z]*)\s*", str(s))
+    if not m or m.group(2).lower() not in _UNITS:
+        raise ValueError(f"bad capacity {s!r}")
+    return int(float(m.group(1)) * _UNITS[m.group(2).lower()])
+
+
+def expand(path: str, rank: int, local_rank: int) -> str:
+    return path.replace("{LOCAL_RANK}", str(local_rank)).replace("{RANK}", str(rank))
+
+
+@dataclass
+class ConnectorConfig:
+    chunk_tokens: int = 256
+    namespace: str = ""
+    load_mode: str = "sync"
+    failure_policy: str = "recompute"
+    store_type: str = "tutti"
+    root: str = "/tmp/tutti_kv"
+    mounts: list[str] = field(default_factory=list)
+    capacity_chunks: int = 0
+    capacity_bytes: int = 0
+    segment_file_slots: int = 2048
+    runtime_options: dict = field(default_factory=dict)
+
+    @classmethod
+    def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
+        extra = dict(extra or {})
+        known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store"}
+        unknown = set(extra) - known
+        if unknown:
+            raise ValueError(f"unknown connector options: {sorted(unknown)}")
+        c = cls()
+        c.chunk_tokens = int(extra.get("chunk_tokens", c.chunk_tokens))
+        c.namespace = str(extra.get("namespace", ""))
+        c.load_mode = extra.get("load_mode", c.load_mode)
+        c.failure_policy = extra.get("kv_load_failure_policy", c.failure_policy)
+        st = dict(extra.get("store", {}))
+        c.store_type = st.pop("type", c.store_type)
+        c.root = st.pop("root", c.root)
+        c.mounts = list(st.pop("mounts", []))
+        c.capacity_chunks = int(st.pop("capacity_chunks", 0))
+        if "capacity" in st:
+            c.capacity_bytes = parse_bytes(st.pop("capacity"))
+        c.segment_file_slots = int(st.pop("segment_file_slots", c.segment_file_slots))
+        c.runtime_options = dict(st.pop("runtime_options", {}))
+        if st:
+            raise ValueError(f"unknown store options: {sorted(st)}")
+        if c.store_type not in ("tutti", "memory"):
+            raise ValueError("store.type must be tutti or memory")
+        return c
+
+    def capacity_for(self, geometry: KVGeometry) -> int:
+        if self.capacity_chunks:
+            return self.capacity_chunks
+        if self.capacity_bytes:
+            return max(1, self.capacity_bytes // geometry.chunk_bytes)
+        return 4096
+
+
+def geometry_from_layers(tensors: list[torch.Tensor], chunk_tokens: int, name: str = "vllm") -> KVGeometry:
+    """KV geometry of one rank from vLLM's per-layer tensors ``[2, blocks, block_size, heads, dim]``."""
+    t = tensors[0]
+    if t.dim() != 5:
+        raise ValueError(f"unsupported KV tensor layout {tuple(t.shape)} (expected [2, blocks, block, heads, dim])")
+    planes, _, bs, heads, dim = t.shape
+    return KVGeometry(name, num_layers=len(tensors), num_kv_heads=heads, head_dim=dim, block_size=bs,
+                      planes=planes, dtype=t.dtype, chunk_tokens=chunk_tokens)
+
+
+def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, local_rank: int, world: int):
+    from ...engine.core import KVEngine
+    from ...storage.memory import MemoryKVStore
+    from ...storage.tutti_store import TuttiKVStore
+
+    g = geometry_from_layers(tensors, cfg.chunk_tokens, cfg.namespace or "vllm")
+    cap = cfg.capacity_for(g)
+    ns = (cfg.namespace or g.fingerprint()).encode()
+    device = tensors[0].device
+    if cfg.store_type == "memory" or device.type != "cuda":
+        store = MemoryKVStore(g.chunk_bytes, capacity_chunks=cap)
+        store.open()
+        eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device, staged=True)
+    else:
+        root = expand(cfg.root, rank, local_rank)
+        mounts = [expand(m, rank, local_rank) for m in cfg.mounts] or [os.path.join(root, "nvme0")]
+        store = TuttiKVStore(root, g, capacity_chunks=cap, mounts=mounts, device=device.index, rank=rank,
+                             rank_count=world, segment_file_slots=min(cfg.segment_file_slots, max(16, cap)),
+                             runtime_options=cfg.runtime_options, namespace=ns)
+        store.open()
+        eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device)
+        eng.restore_from_store()
+    eng.bind_layers(tensors)
+    return eng

@@ -1,0 +1,193 @@
+"""Worker side of the vLLM connector: per-step loads and saves on one TP rank.
+
+* ``register_kv_caches``: binds vLLM's per-layer KV tensors
+  (``[2, num_blocks, block_size, kv_heads, head_dim]``) to the engine once.
+* ``start_load_kv``: one layerwise read plan for all synchronous loads of the
+  step (layer l's restore overlaps layer l-1's attention); asynchronous loads
+  are submitted as whole-prefix restores and reported by ``get_finished``.
+* ``wait_for_layer_load``: device-side wait of the current stream on layer l.
+* ``wait_for_save``: settles the loads (TP failure consensus: every rank
+  agrees on the failed chunk range), then persists this step's new full
+  chunks behind the forward's compute event and reports them committed.
+Parity: reference tutti/integration/vllm/worker.py:461-1822 (WorkerImpl,
+start_load_kv, wait_for_layer_load, save_kv_layer, wait_for_save,
+_synchronize_load_failure, async loads).
+"""
+from __future__ import annotations
+
+import logging
+import re
+import time
+from typing import Callable
+
+import numpy as np
+import torch
+
+from ...engine.completion import LoadGateError
+from ...engine.core import KVEngine
+from ...parallel.tp_consensus import ChunkFailure, TpFailureConsensus
+from .metadata import LoadSpec, TuttiConnectorMetadata, TuttiWorkerMetadata
+
+LOG = logging.getLogger("tutti_b200.vllm")
+_LAYER_RE = re.compile(r"(\d+)")
+
+
+class _FailedLoad:
+    """A load that failed at submission; raises when settled."""
+
+    def __init__(self, error: BaseException):
+        self.error = error
+
+    def wait(self) -> None:
+        raise self.error
+
+
+def layer_index(name: str) -> int:
+    m = _LAYER_RE.findall(name)
+    if not m:
+        raise ValueError(f"cannot find a layer index in {name!r}")
+    return int(m[0])
+
+
+class WorkerSide:
+    def __init__(self, make_engine: Callable[[list[torch.Tensor]], KVEngine], *, block_size: int,
+                 chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
+                 consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute"):
+        if failure_policy not in ("recompute", "fail"):
+            raise ValueError("kv_load_failure_policy must be recompute or fail")
+        self.make_engine = make_engine
+        self.block_size = block_size
+        self.chunk_tokens = chunk_tokens
+        self.blocks_per_chunk = chunk_tokens // block_size
+        self.tp_rank = tp_rank
+        self.tp_size = tp_size
+        self.consensus = consensus or TpFailureConsensus()
+        self.failure_policy = failure_policy
+        self.engine: KVEngine | None = None
+        self.layer_of: dict[str, int] = {}
+        self._plan = None
+        self._plan_loads: list[LoadSpec] = []
+        self._async: dict[str, tuple[object, LoadSpec, float]] = {}
+        self._finished_recv: set[str] = set()
+        self._load_error_blocks: set[int] = set()
+        self._meta = TuttiWorkerMetadata()
+
+    # -- binding --------------------------------------------------------------
+    def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
+        names = sorted(kv_caches, key=layer_index)
+        self.layer_of = {n: i for i, n in enumerate(names)}
+        tensors = [kv_caches[n] for n in names]
+        self.engine = self.make_engine(tensors)
+
+    # -- loads ----------------------------------------------------------------
+    def start_load_kv(self, meta: TuttiConnectorMetadata) -> None:
+        self._meta = TuttiWorkerMetadata()
+        sync = [l for l in meta.loads if not l.is_async]
+        for spec in meta.loads:
+            if spec.is_async:
+                comp = self.engine.load(spec.keys, np.asarray(spec.block_ids, dtype=np.int64))
+                self._async[spec.request_id] = (comp, spec, time.perf_counter())
+        self._plan_loads = sync
+        self._plan = None
+        if sync:
+            keys = [k for s in sync for k in s.keys]
+            blocks = np.asarray([b for s in sync for b in s.block_ids], dtype=np.int64)
+            try:
+                if self.engine.staged:
+                    self._plan = self.engine.load(keys, blocks)
+                else:
+                    self._plan = self.engine.start_read_plan(keys, blocks)
+            except Exception as e:  # noqa: BLE001 - settled (with TP consensus) in wait_for_save
+                self._plan = _FailedLoad(e)
+
+    def wait_for_layer_load(self, layer_name: str) -> None:
+        if self._plan is not None and hasattr(self._plan, "wait_layer"):
+            self._plan.wait_layer(self.layer_of[layer_name])
+
+    def _settle_sync_loads(self, generation: int) -> None:
+        if self._plan is None:
+            return
+        local: list[ChunkFailure] = []
+        try:
+            if hasattr(self._plan, "finish"):
+                self._plan.finish()
+            else:
+                self._plan.wait()
+        except (LoadGateError, Exception) as e:  # noqa: BLE001 - mapped to chunk failures below
+            failed = getattr(e, "failed_chunks", None) or range(sum(len(s.keys) for s in self._plan_loads))
+            base = 0
+            for ordinal, spec in enumerate(self._plan_loads):
+                mine = [c - base for c in failed if base <= c < base + len(spec.keys)]
+                if mine:
+                    local.append(ChunkFailure(ordinal, min(mine), max(mine) - min(mine) + 1))
+                base += len(spec.keys)
+        cons = self.consensus.coordinate(generation, len(self._plan_loads), local)
+        if cons.failed:
+            if self.failure_policy == "fail":
+                raise LoadGateError(f"KV load failed on some TP rank: {cons.failures}")
+            self.consensus.drain_barrier(generation, True)
+            for f in cons.failures:
+                spec = self._plan_loads[f.request]
+                first_tok = f.first_chunk * self.chunk_tokens
+                self._meta.failed_loads[spec.request_id] = first_tok
+                # every block from the first failed chunk on must be recomputed
+                self._load_error_blocks.update(spec.block_ids[f.first_chunk * self.blocks_per_chunk:])
+        self._plan = None
+
+    # -- saves ----------------------------------------------------------------
+    def wait_for_save(self, meta: TuttiConnectorMetadata) -> TuttiWorkerMetadata:
+        self._settle_sync_loads(meta.generation)
+        if meta.saves:
+            ev = torch.cuda.Event() if torch.cuda.is_available() and not self.engine.staged else None
+            if ev is not None:
+                ev.record()
+            comps = []
+            for spec in meta.saves:
+                comp = self.engine.store_chunks(spec.keys, np.asarray(spec.block_ids, dtype=np.int64), after=ev)
+                comps.append((spec, comp))
+            for spec, comp in comps:
+                if comp is None:
+                    continue
+                try:
+                    comp.wait()
+                except Exception as e:  # noqa: BLE001 - a failed save only costs a future recompute
+                    LOG.warning("save of %d chunk(s) for %s failed: %s", len(spec.keys), spec.request_id, e)
+                    continue
+                for k in spec.keys:
+                    self._meta.committed[k] = self._meta.committed.get(k, 0) + 1
+            # chunks already resident in this rank's store count as committed too
+            for spec in meta.saves:
+                for k in spec.keys:
+                    if k not in self._meta.committed and self.engine.index.is_resident(k):
+                        self._meta.committed[k] = 1
+        return self._meta
+
+    # -- completion reporting -------------------------------------------------
+    def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
+        done = set()
+        for rid, (comp, spec, t0) in list(self._async.items()):
+            if comp.query():
+                try:
+                    comp.wait()
+                except Exception:  # noqa: BLE001
+                    self._load_error_blocks.update(spec.block_ids)
+                    self._meta.failed_loads[rid] = 0
+                done.add(rid)
+                del self._async[rid]
+        return None, (done or None)
+
+    def get_block_ids_with_load_errors(self) -> set[int]:
+        out, self._load_error_blocks = self._load_error_blocks, set()
+        return out
+
+    def shutdown(self) -> None:
+        for comp, _, _ in self._async.values():
+            try:
+                comp.wait()
+            except Exception:  # noqa: BLE001
+                pass
+        self._async.clear()
+        if self.engine is not None:
+            self.engine.wait_idle()
+            if hasattr(self.engine.store, "close"):
+                self.engine.store.close()

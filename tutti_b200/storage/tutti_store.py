@@ -108,6 +108,7 @@ class TuttiKVStore:
         self._pool = None  # (tensor, handle, num_blocks)
         self._inflight: collections.deque[NativeCompletion] = collections.deque()
         self.last_submit_profile: dict = {}
+        self._layer_mems = np.zeros(0, dtype=np.uint64)  # per-layer registrations, if any
 
     # -- lifecycle ------------------------------------------------------------
     @property
@@ -167,6 +168,22 @@ class TuttiKVStore:
                                          pool.device.index if pool.is_cuda else -1)
         self._pool = (pool, h, pool.shape[2])
         return h
+
+    def register_layers(self, layers: Sequence[torch.Tensor]) -> list[int]:
+        """Register per-layer KV tensors ``[planes, num_blocks, block, heads, dim]`` (one allocation each)."""
+        g = self.geometry
+        if len(layers) != g.num_layers:
+            raise ValueError(f"expected {g.num_layers} layer tensors, got {len(layers)}")
+        handles = []
+        for t in layers:
+            if t.dim() != 5 or t.shape[0] != g.planes or not t.is_contiguous():
+                raise ValueError(f"layer tensor shape {tuple(t.shape)} does not match {g.name}")
+            kind = "device" if t.is_cuda else ("pinned" if t.is_pinned() else "host")
+            handles.append(self.runtime.register_memory(t.data_ptr(), t.numel() * t.element_size(), kind,
+                                                        t.device.index if t.is_cuda else -1))
+        self._layer_mems = np.asarray(handles, dtype=np.uint64)
+        self._pool = (layers[0], int(handles[0]), layers[0].shape[1])
+        return handles
 
     def targets_for(self, paths: Sequence[str]) -> list[int]:
         missing = sorted({p for p in paths if p not in self._targets})
@@ -271,7 +288,8 @@ class TuttiKVStore:
         sptr = self._stream_ptr(stream)
         host = self.backend != "nvme-gpu"
         for _ in range(self.max_retries):
-            r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host)
+            r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host,
+                                          self._layer_mems)
             if not r["rejected"]:
                 return [r["io"]], int(r["count"]) * g.plane_block_bytes
             reasons = " ".join(r["reasons"])
