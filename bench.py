@@ -49,8 +49,8 @@ def parse():
     p.add_argument("--direct-io", action="store_true", help="O_DIRECT backing reads (drive-bound)")
     p.add_argument("--no-verify", action="store_true")
     p.add_argument("--timing", action="store_true", help="per-command %globaltimer breakdown (stderr)")
-    p.add_argument("--leases", type=int, default=128, help="queue leases (CTAs) per GPU")
-    p.add_argument("--ctas", type=int, default=64, help="CTAs one restore may use")
+    p.add_argument("--leases", type=int, default=192, help="queue leases (CTAs) per GPU")
+    p.add_argument("--ctas", type=int, default=96, help="CTAs one restore may use")
     p.add_argument("--slots", type=int, default=8)
     p.add_argument("--inflight", type=int, default=2, help="restores submitted ahead")
     p.add_argument("--emulator-skip-data", action="store_true", help="diagnostic: controllers move no data")
