@@ -1,0 +1,130 @@
+"""Drive-affine fan-out restore: placement exchange and share selection (gloo, CPU)
+and the fused NVLink fan-out on two GPUs (local vs fan-out pools byte-equal)."""
+import datetime
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tutti_b200.parallel.fanout import FanoutRestorer, RestoreItem, owner_of
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_owner_of_is_le64_prefix_mod_group():
+    k = bytes(range(16))
+    assert owner_of(k, 8) == int.from_bytes(k[:8], "little") % 8
+    assert owner_of(b"\x05" + b"\0" * 15, 4) == 1
+
+
+class _Objects:
+    def __init__(self, table):
+        self.table = table
+
+    def lookup(self, key):
+        return self.table.get(key)
+
+
+class _Store:
+    """Stands in for TuttiKVStore: chunk i of rank r sits in slot i of r's files."""
+
+    def __init__(self, rank, keys):
+        self.rank = rank
+        self._pool = (None, 100 + rank, 64)
+        self.objects = _Objects({k: (f"file:///r{rank}/seg{i % 2}", 4096 * i, i, 1) for i, k in enumerate(keys)})
+        self.calls = []
+
+    def register_peer_pool(self, ptr, nbytes, device):
+        return 1000 + device
+
+    def restore_placements(self, todo, blocks, mems, layers=None, stream=None):
+        self.calls.append((list(todo), blocks.tolist(), [int(m) for m in mems]))
+        return "completion"
+
+
+class _Peers:
+    def __init__(self, rank, world):
+        self.rank, self.world = rank, world
+        self.ptrs = [0x1000 * (r + 1) for r in range(world)]
+        self.nbytes = [1 << 20] * world
+        self.devices = list(range(world))
+
+
+def _fanout_rank(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        keys = [bytes([i]) * 16 for i in range(4)]
+        store = _Store(rank, keys)
+        fan = FanoutRestorer(store, _Peers(rank, world))
+        items = [RestoreItem(rank=r, key=k, block_ids=[10 * r + i, 10 * r + i + 1]) for r in range(world)
+                 for i, k in enumerate(keys)]
+        # slot i lives on drive i % 2; drive d belongs to GPU d
+        comp = fan.restore(items, n_drives=2, affine_gpus=[0, 1])
+        # replicated cache: rank 0 owns every chunk, all ranks receive it
+        rep = [RestoreItem(rank=r, key=k, block_ids=[r, i], source=0) for r in range(world) for i, k in enumerate(keys)]
+        comp2 = fan.restore(rep, n_drives=2, affine_gpus=[0, 1])
+        q.put((rank, (comp, comp2, store.calls)))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fanout_selects_drive_affine_share_for_all_ranks():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_fanout_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in range(2))
+    for p in ps:
+        p.join(timeout=30)
+    for r in range(2):
+        assert not isinstance(out[r], str), out[r]
+        comp, comp2, calls = out[r]
+        assert comp == comp2 == "completion"
+        todo, blocks, mems = calls[0]
+        # GPU r reads slots {r, r+2} of BOTH ranks' files and lands each in its owner's pool
+        want = [(f"/r{o}/seg{i % 2}", 4096 * i) for o in range(2) for i in (r, r + 2)]
+        assert todo == want
+        assert mems == [100 + r if o == r else 1000 + o for o in range(2) for _ in (r, r + 2)]
+        assert blocks == [[10 * o + i, 10 * o + i + 1] for o in range(2) for i in (r, r + 2)]
+        rtodo, _rblocks, rmems = calls[1]
+        # one placement (rank 0's file) per destination rank: the data path merges them into one read
+        assert rtodo == [(f"/r0/seg{i % 2}", 4096 * i) for o in range(2) for i in (r, r + 2)]
+        assert rmems == [100 + r if o == r else 1000 + o for o in range(2) for _ in (r, r + 2)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["tp", "mla"])
+def test_two_gpu_fanout_restore_matches_local(tmp_path, mode):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+           "-m", "tutti_b200.benchmarks.fanout", "--mode", mode, "--prefix-tokens", "4096", "--steps", "2",
+           "--warmup", "1", "--root", str(tmp_path / "fan"), "--leases", "32", "--ctas", "16"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=460)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1]
+    import json
+
+    res = json.loads(line)
+    assert res["ok"] and res["results"]["fanout"]["verified"] and res["results"]["local"]["verified"]

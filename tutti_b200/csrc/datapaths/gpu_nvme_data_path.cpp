@@ -21,6 +21,76 @@ Status cuda_status(cudaError_t e, const char* what) {
     return {StatusCode::DEVICE_ERROR, std::string(what) + ": " + cudaGetErrorString(e)};
 }
 
+// Reads of the same target range into several memories (same piece tiling)
+// become one command with replica groups: the bytes cross PCIe once and the
+// kernel stores them to every destination (e.g. each TP rank's pool).
+void merge_replicas(std::vector<io::IoCommand>& cmds, std::vector<io::IoPiece>& pieces,
+                    std::vector<std::uint32_t>& cmd_first_piece, std::vector<std::uint32_t>& piece_req) {
+    struct Key {
+        std::uint64_t logical;
+        std::uint32_t target, bytes, n;
+        bool operator==(const Key& o) const {
+            return logical == o.logical && target == o.target && bytes == o.bytes && n == o.n;
+        }
+    };
+    struct KeyHash {
+        std::size_t operator()(const Key& k) const {
+            return std::hash<std::uint64_t>()(k.logical * 0x9E3779B97F4A7C15ull ^ (std::uint64_t(k.target) << 32 | k.bytes) ^ k.n);
+        }
+    };
+    std::unordered_map<Key, std::uint32_t, KeyHash> group_of;
+    std::vector<std::vector<std::uint32_t>> groups;
+    bool merged = false;
+    auto same_tiling = [&](const io::IoCommand& a, const io::IoCommand& b) {
+        for (std::uint32_t i = 0; i < a.n_pieces; ++i) {
+            const auto& x = pieces[a.first_piece + i];
+            const auto& y = pieces[b.first_piece + i];
+            if (x.off != y.off || x.bytes != y.bytes) return false;
+        }
+        return true;
+    };
+    groups.reserve(cmds.size());
+    for (std::uint32_t i = 0; i < cmds.size(); ++i) {
+        const auto& c = cmds[i];
+        if (c.opcode == nvme::kOpRead) {
+            const Key k{c.logical, c.target, c.bytes, c.n_pieces};
+            auto it = group_of.find(k);
+            if (it != group_of.end() && same_tiling(cmds[groups[it->second][0]], c)) {
+                groups[it->second].push_back(i);
+                merged = true;
+                continue;
+            }
+            group_of[k] = static_cast<std::uint32_t>(groups.size());
+        }
+        groups.push_back({i});
+    }
+    if (!merged) return;
+    std::vector<io::IoCommand> nc;
+    std::vector<io::IoPiece> np;
+    std::vector<std::uint32_t> nfirst, nreq;
+    nc.reserve(groups.size());
+    np.reserve(pieces.size());
+    nreq.reserve(piece_req.size());
+    for (const auto& g : groups) {
+        io::IoCommand c = cmds[g[0]];
+        c.first_piece = static_cast<std::uint32_t>(np.size());
+        c.replicas = g.size() > 1 ? static_cast<std::uint32_t>(g.size()) : 0u;
+        nfirst.push_back(c.first_piece);
+        for (auto idx : g) {
+            const auto& o = cmds[idx];
+            for (std::uint32_t p = 0; p < o.n_pieces; ++p) {
+                np.push_back(pieces[o.first_piece + p]);
+                nreq.push_back(piece_req[o.first_piece + p]);
+            }
+        }
+        nc.push_back(c);
+    }
+    cmds.swap(nc);
+    pieces.swap(np);
+    cmd_first_piece.swap(nfirst);
+    piece_req.swap(nreq);
+}
+
 double percentile(std::vector<double>& v, double q) {
     if (v.empty()) return 0.0;
     std::size_t k = static_cast<std::size_t>(q * (v.size() - 1));
@@ -277,8 +347,15 @@ Result<DataPathMemory> GpuNvmeDataPath::register_memory(const DataPathMemoryView
     if (reinterpret_cast<std::uintptr_t>(v.base) % 16)
         return R::Failure({StatusCode::INVALID_ARGUMENT, "memory base must be 16-byte aligned"});
     std::lock_guard<std::mutex> g(mu_);
-    if (v.kind == DataPathMemoryKind::DEVICE && v.expected_accel_id >= 0 && v.expected_accel_id != cfg_.accel_id)
-        return R::Failure({StatusCode::INVALID_ARGUMENT, "memory belongs to another accelerator"});
+    if (v.kind == DataPathMemoryKind::DEVICE && v.expected_accel_id >= 0 && v.expected_accel_id != cfg_.accel_id) {
+        // Another GPU's memory (e.g. a TP peer's KV pool mapped through CUDA IPC):
+        // usable when this GPU can reach it over NVLink/P2P.
+        int can = 0;
+        if (cudaDeviceCanAccessPeer(&can, cfg_.accel_id, v.expected_accel_id) != cudaSuccess || !can) {
+            cudaGetLastError();
+            return R::Failure({StatusCode::INVALID_ARGUMENT, "memory belongs to an accelerator without peer access"});
+        }
+    }
     std::uint64_t tok = next_token_++;
     memories_[tok] = MemoryRec{tok, static_cast<char*>(v.base), v.size_bytes, v.kind};
     return DataPathMemory{tok, tok};
@@ -421,6 +498,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         out.status = first_reject;
         return out;
     }
+    merge_replicas(cmds, pieces, op->cmd_first_piece, op->piece_req);
     const std::uint32_t n_cmds = static_cast<std::uint32_t>(cmds.size());
     const auto t_coalesced = std::chrono::steady_clock::now();
     std::uint32_t want = std::min<std::uint32_t>(cfg_.max_ctas_per_op, n_cmds);

@@ -161,6 +161,7 @@ __device__ void move_slot(const IoKernelParams& p, const IoCommand& c, char* sta
             }
         }
         const IoPiece first = pcs[pi];
+        const std::uint32_t groups = (to_memory && c.replicas > 1) ? c.replicas : 1u;
         if (first.off <= co && first.off + first.bytes >= ce) {
             char* mem = reinterpret_cast<char*>(first.mem) + (co - first.off);
             const std::uint32_t units = (ce - co) >> 4;
@@ -171,10 +172,14 @@ __device__ void move_slot(const IoKernelParams& p, const IoCommand& c, char* sta
                     const std::uint32_t u = lane + 32 * k;
                     if (u < units) v[k] = ld_cv_v4(stage + co + (u << 4));
                 }
+                for (std::uint32_t g = 0; g < groups; ++g) {
+                    char* gm = g == 0 ? mem
+                                      : reinterpret_cast<char*>(pcs[g * c.n_pieces + pi].mem) + (co - first.off);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const std::uint32_t u = lane + 32 * k;
-                    if (u < units) st_cs_v4(mem + (u << 4), v[k]);
+                    for (int k = 0; k < 8; ++k) {
+                        const std::uint32_t u = lane + 32 * k;
+                        if (u < units) st_cs_v4(gm + (u << 4), v[k]);
+                    }
                 }
             } else {
 #pragma unroll
@@ -192,12 +197,15 @@ __device__ void move_slot(const IoKernelParams& p, const IoCommand& c, char* sta
             for (int q = pi; q < static_cast<int>(c.n_pieces) && pcs[q].off < ce; ++q) {
                 const IoPiece pc = pcs[q];
                 const std::uint32_t a = max(co, pc.off), b = min(ce, pc.off + pc.bytes);
-                char* mem = reinterpret_cast<char*>(pc.mem);
                 for (std::uint32_t o = a + (lane << 4); o < b; o += 512) {
-                    if (to_memory)
-                        st_cs_v4(mem + (o - pc.off), ld_cv_v4(stage + o));
-                    else
-                        *reinterpret_cast<uint4*>(stage + o) = *reinterpret_cast<const uint4*>(mem + (o - pc.off));
+                    if (to_memory) {
+                        const uint4 v = ld_cv_v4(stage + o);
+                        for (std::uint32_t g = 0; g < groups; ++g)
+                            st_cs_v4(reinterpret_cast<char*>(pcs[g * c.n_pieces + q].mem) + (o - pc.off), v);
+                    } else {
+                        *reinterpret_cast<uint4*>(stage + o) =
+                            *reinterpret_cast<const uint4*>(reinterpret_cast<char*>(pc.mem) + (o - pc.off));
+                    }
                 }
             }
         }

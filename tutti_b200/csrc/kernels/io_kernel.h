@@ -35,9 +35,13 @@ struct IoCommand {  // 32 B
     std::uint32_t target;       // row of the device-resident target table
     std::uint32_t bytes;        // <= slot_bytes
     std::uint32_t first_piece;
-    std::uint32_t n_pieces;
+    std::uint32_t n_pieces;     // pieces per destination group
     std::uint32_t opcode;       // nvme::kOpRead / kOpWrite
-    std::uint32_t pad;
+    // Reads only: number of destination groups (0 or 1: one). Group g's pieces
+    // are [first_piece + g*n_pieces, +n_pieces) with the same offsets as group 0;
+    // the command's bytes are read once and stored to every group (e.g. the
+    // TP ranks that all need a replicated latent cache, over NVLink).
+    std::uint32_t replicas;
 };
 
 struct IoPiece {  // 16 B

@@ -88,6 +88,7 @@ extern "C" int tutti_nvme_io_noalloc(void* data_path, const tutti_noalloc_comman
         const tutti_noalloc_command& k = commands[c];
         if (k.opcode != tutti::nvme::kOpRead && k.opcode != tutti::nvme::kOpWrite)
             return fail(TUTTI_NOALLOC_E_ARGS, "command opcode must be 1 (write) or 2 (read)");
+        if (k.reserved > 1) return fail(TUTTI_NOALLOC_E_ARGS, "command.reserved must be 0 or 1");
         if (k.bytes == 0 || k.n_pieces == 0 || k.first_piece > n_pieces || k.n_pieces > n_pieces - k.first_piece)
             return fail(TUTTI_NOALLOC_E_ARGS, "command piece range out of bounds");
         if (!dp->noalloc_target_ok(k.target_row, k.logical, k.bytes))

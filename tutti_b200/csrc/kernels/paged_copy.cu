@@ -5,7 +5,8 @@
 // 16 KiB chunks through a 4-stage shared-memory ring with bulk-async copies
 // (cp.async.bulk global->shared completing on an mbarrier, then
 // cp.async.bulk shared->global in bulk groups), so each CTA keeps 64 KiB in
-// flight with one issuing thread and no register traffic. No multicast.
+// flight with one issuing thread and no register traffic. Each copy targets
+// the issuing CTA's own shared memory only.
 // Peer memory (simt path): 16-byte vector loads/stores by all threads; used
 // when a source or destination is another GPU's memory reached over NVLink.
 //

@@ -74,7 +74,7 @@ __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-// ---- bulk async copies (no multicast anywhere) ------------------------------
+// ---- bulk async copies (single-CTA destinations only) -----------------------
 // global -> shared, completion counted on `bar` (bytes % 16 == 0, both 16 B aligned)
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, std::uint32_t bytes,
                                          std::uint64_t* bar) {

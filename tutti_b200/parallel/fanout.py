@@ -1,0 +1,143 @@
+"""Multi-GPU restore: drive-affine reads fanned out to TP peers over NVLink.
+
+An NVMe drive hangs off one GPU's PCIe switch, while every TP rank needs its
+own KV-head slice of each chunk. The drive-affine GPU reads the chunks stored
+on its drives for *all* ranks and its fused io kernel stores each rank's
+slice straight into that rank's paged pool (CUDA-IPC-mapped peer pointers,
+P2P stores over NVLink 5/NVSwitch): no staging copy on the peer, no separate
+scatter kernel, no NCCL all-gather. Replicated caches (an MLA latent cache is
+identical on every TP rank) are read once and stored to every rank's pool by
+the same kernel (replica groups). A collective after the restore orders the
+peers' subsequent work after the stores.
+
+Control plane: pool IPC handles and per-rank placements are exchanged with
+``torch.distributed`` object collectives (no data crosses it).
+Parity: reference tutti/storage/tutti_nvme/replica_direct.py:43-1190 (owner =
+le64(key[:8]) % group, owner reads, consumers pull pages through IPC with
+replica_page_scatter_kernel) and the replica-sharded IO design notes; here the
+owner pushes inside the io kernel instead of consumers pulling afterwards.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+def owner_of(key: bytes, group_size: int) -> int:
+    """Replica owner of a chunk: its first 8 key bytes, little-endian, modulo the group."""
+    return int.from_bytes(bytes(key[:8]), "little") % group_size
+
+
+class PeerPools:
+    """Every rank's KV pool, mapped into this process through CUDA IPC."""
+
+    def __init__(self, pool: torch.Tensor, group=None):
+        self.pool = pool
+        self.device = pool.device.index
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        handle, offset, _size = ops.ipc_export(pool)
+        mine = (handle, offset, self.device, pool.numel() * pool.element_size())
+        everyone: list = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.ptrs: list[int] = []
+        self.devices: list[int] = []
+        self.nbytes: list[int] = []
+        self._opened: list[int] = []
+        for r, (h, off, devi, nb) in enumerate(everyone):
+            if r == self.rank:
+                self.ptrs.append(pool.data_ptr())
+            else:
+                ops.enable_peer_access(self.device, devi)
+                base = ops.ipc_open(h, self.device)
+                self._opened.append(base)
+                self.ptrs.append(base + off)
+            self.devices.append(devi)
+            self.nbytes.append(nb)
+
+    def close(self) -> None:
+        for p in self._opened:
+            ops.ipc_close(p, self.device)
+        self._opened.clear()
+
+
+@dataclass
+class RestoreItem:
+    """Restore chunk ``key`` into rank ``rank``'s pool blocks ``block_ids``.
+
+    ``source`` is the rank whose namespace holds the chunk: ``rank`` itself for a
+    TP-sliced cache, the replica owner for a cache that is identical on every
+    rank (all ranks' items of one key then share one read).
+    """
+
+    rank: int
+    key: bytes
+    block_ids: Sequence[int]
+    source: int | None = None
+
+    @property
+    def src(self) -> int:
+        return self.rank if self.source is None else self.source
+
+
+class FanoutRestorer:
+    """Restores chunks for all ranks from the drives this GPU owns (drive-affine)."""
+
+    def __init__(self, store, peers: PeerPools, group=None):
+        self.store = store
+        self.peers = peers
+        self.group = group
+        self.mems = [store._pool[1] if r == peers.rank else store.register_peer_pool(p, peers.nbytes[r], peers.devices[r])
+                     for r, p in enumerate(peers.ptrs)]
+
+    def placements(self, keys_by_rank: dict[int, Sequence[bytes]]) -> dict[tuple[int, bytes], tuple[str, int, int]]:
+        """Every rank looks up its own chunks; the (path, offset, slot) map is shared by all."""
+        mine = {}
+        for k in keys_by_rank.get(self.peers.rank, []):
+            p = self.store.objects.lookup(bytes(k))
+            if p is not None:
+                uri, off, slot, _gen = p
+                mine[(self.peers.rank, bytes(k))] = (uri[len("file://"):], off, slot)
+        allmaps: list = [None] * self.peers.world
+        dist.all_gather_object(allmaps, mine, group=self.group)
+        out = {}
+        for m in allmaps:
+            out.update(m)
+        return out
+
+    def restore(self, items: Sequence[RestoreItem], n_drives: int, affine_gpus: Sequence[int],
+                layers=None, stream=None, placements=None):
+        """Submit this GPU's share: items whose chunk lives on a drive this GPU is affine to.
+
+        Drive d (= slot % n_drives) belongs to GPU ``affine_gpus[d % len(affine_gpus)]``.
+        Returns this rank's completion (None if it owns no drive); call ``barrier()`` after
+        waiting so peers see the stores.
+        """
+        pl = placements if placements is not None else self.placements(
+            {r: sorted({bytes(it.key) for it in items if it.src == r}) for r in range(self.peers.world)})
+        todo, mems, blocks = [], [], []
+        for it in items:
+            p = pl.get((it.src, bytes(it.key)))
+            if p is None:
+                raise KeyError(f"rank {it.src} has no committed chunk {bytes(it.key).hex()}")
+            path, off, slot = p
+            if affine_gpus[(slot % n_drives) % len(affine_gpus)] != self.peers.rank:
+                continue
+            todo.append((path, off))
+            mems.append(self.mems[it.rank])
+            blocks.append(list(it.block_ids))
+        if not todo:
+            return None
+        return self.store.restore_placements(todo, np.asarray(blocks, dtype=np.int64), np.asarray(mems, np.uint64),
+                                             layers=layers, stream=stream)
+
+    def barrier(self) -> None:
+        """Orders every rank after all ranks' restores (their kernels completed before this)."""
+        torch.cuda.current_stream().synchronize()
+        dist.barrier(group=self.group)

@@ -276,7 +276,27 @@ class TuttiKVStore:
                 time.sleep(0.0005)
         raise StoreIOError("submit retries exhausted", idx.tolist(), "busy")
 
-    def _submit_paged(self, direction: str, placements, block_ids: np.ndarray, layers: np.ndarray, stream):
+    def register_peer_pool(self, ptr: int, nbytes: int, device: int) -> int:
+        """Register another GPU's whole KV pool (CUDA-IPC mapped) as a restore destination."""
+        return self.runtime.register_memory(int(ptr), int(nbytes), "device", int(device))
+
+    def restore_placements(self, placements, block_ids, chunk_mems=None, layers=None, stream=None):
+        """Restore chunks given by explicit (segment file path, payload offset) placements.
+
+        ``chunk_mems[i]`` names the pool (this rank's or a peer's) chunk i lands in;
+        placements may belong to other ranks' namespaces (the files are opened here).
+        """
+        g = self.geometry
+        block_ids = np.asarray(block_ids, dtype=np.int64).reshape(len(placements), g.blocks_per_chunk)
+        layers = np.arange(g.num_layers) if layers is None else np.asarray(layers, dtype=np.int64).reshape(-1)
+        cm = None if chunk_mems is None else np.asarray(chunk_mems, dtype=np.uint64)
+        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream, chunk_mems=cm)
+        comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
+        self._track(comp)
+        return comp
+
+    def _submit_paged(self, direction: str, placements, block_ids: np.ndarray, layers: np.ndarray, stream,
+                      chunk_mems: np.ndarray | None = None):
         """Paged requests generated natively (no per-request Python work); retried while leases are busy."""
         g = self.geometry
         handles = np.asarray(self.targets_for([p for p, _ in placements]), dtype=np.uint64)
@@ -289,7 +309,8 @@ class TuttiKVStore:
         host = self.backend != "nvme-gpu"
         for _ in range(self.max_retries):
             r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host,
-                                          self._layer_mems)
+                                          self._layer_mems,
+                                          chunk_mems if chunk_mems is not None else np.zeros(0, dtype=np.uint64))
             if not r["rejected"]:
                 return [r["io"]], int(r["count"]) * g.plane_block_bytes
             reasons = " ".join(r["reasons"])
