@@ -30,6 +30,7 @@ import json
 import os
 import shutil
 import sys
+import time
 
 import numpy as np
 import torch
@@ -54,6 +55,7 @@ def parse(argv=None):
     p.add_argument("--controller-threads", type=int, default=0)
     p.add_argument("--leases", type=int, default=128)
     p.add_argument("--ctas", type=int, default=64)
+    p.add_argument("--timing", action="store_true", help="per-command %%globaltimer breakdown of the last mode")
     return p.parse_args(argv)
 
 
@@ -79,7 +81,8 @@ def main(argv=None) -> int:
     ncpu = os.cpu_count() or 8
     threads = args.controller_threads or max(2, min(8, (ncpu // world - 2) // max(1, drives)))
     opts = {"controller_threads": threads, "leases": args.leases, "max_ctas_per_op": args.ctas,
-            "slots_per_lease": 8, "slot_bytes": 1 << 20, "queue_depth": 256, "mdts_bytes": 1 << 20}
+            "slots_per_lease": 8, "slot_bytes": 1 << 20, "queue_depth": 256, "mdts_bytes": 1 << 20,
+            "timing": bool(args.timing)}
     spf = max(16, (nchunks + drives - 1) // drives)
     store = TuttiKVStore(args.root, g, capacity_chunks=spf * drives, mounts=mounts, device=local,
                          rank=rank, rank_count=world, runtime_options=opts, segment_file_slots=spf,
@@ -120,11 +123,15 @@ def main(argv=None) -> int:
         store.targets_for([path])
     stream = torch.cuda.current_stream(dev)
 
+    host_ms = {"local": [], "fanout": []}
+
     def step(mode: str) -> None:
+        t0 = time.perf_counter()
         if mode == "local":
             c = store.restore_placements(local_pl, local_blocks, stream=stream)
         else:
             c = fan.restore(items, drives, affine, stream=stream, placements=placements)
+        host_ms[mode].append((time.perf_counter() - t0) * 1e3)
         if c is not None:
             c.wait()
 
@@ -163,6 +170,8 @@ def main(argv=None) -> int:
     for mode, r in results.items():
         r["GBps_into_hbm"] = round(hbm_bytes / (r["ms"] / 1e3) / 1e9, 3)
         r["storage_bytes_per_step"] = read_bytes[mode]
+        r["host_submit_ms_p50"] = round(float(np.median(host_ms[mode])), 3)
+    timing = store.runtime.io_timing() if args.timing else None
     peers_stats = store.runtime.controller_stats()
     dist.barrier(group=ctl)
     # teardown: nobody reads a peer pool after this barrier
@@ -174,7 +183,7 @@ def main(argv=None) -> int:
         print(json.dumps({"bench": "fanout", "mode": args.mode, "n_gpus": world, "model": g.fingerprint(),
                           "prefix_tokens": args.prefix_tokens, "drives": drives, "affine_gpus": affine,
                           "steps": args.steps, "warmup": args.warmup, "results": results,
-                          "controllers": len(peers_stats), "ok": ok}))
+                          "controllers": len(peers_stats), "ok": ok, "io_timing": timing}))
     del pool
     dist.destroy_process_group()
     if rank == 0:

@@ -133,7 +133,9 @@ Status SegmentFileObjectStore::save_namespace_meta() {
         static_cast<unsigned long long>(cfg_.segment_header_bytes), cfg_.devices.size(), cfg_.rank_count,
         static_cast<unsigned long long>(fingerprint_digest_));
     const std::string path = join(join(cfg_.uri, "meta"), "namespace");
-    const std::string tmp = path + ".tmp";
+    // Every rank of a namespace writes the same meta file: a private temporary
+    // name per rank and process keeps concurrent opens from racing on it.
+    const std::string tmp = path + ".tmp." + std::to_string(cfg_.rank_id) + "." + std::to_string(::getpid());
     int fd = ::open(tmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC | O_CLOEXEC, 0644);
     if (fd < 0) return errno_status("write " + tmp);
     const bool ok = pwrite_full(fd, buf, static_cast<std::size_t>(n), 0) && ::fsync(fd) == 0;

@@ -37,7 +37,10 @@ struct MountBinding {
     std::uint64_t expected_st_dev = 0;    // 0: not checked
     std::string mapping = "auto";         // "fiemap" | "synthetic" | "auto"
     std::string datapath_key = "nvme-gpu";
-    std::uint32_t max_extents = 124;
+    // The device-side file handle is a binary-searched extent array of any
+    // length, so the cap only guards against pathological fragmentation (the
+    // reference's fixed-size handle capped it at 124).
+    std::uint32_t max_extents = 65536;
 };
 
 // Raw FIEMAP walk (exposed for tests and the RAID0 resolver).

@@ -487,7 +487,11 @@ Result<MemoryHandle> StorageRuntime::register_memory(const MemoryView& view) {
         }
         if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
             return R::Failure({StatusCode::INVALID_ARGUMENT, "address is not device memory"});
-        if (view.expected_accel_id >= 0 && a.device != view.expected_accel_id)
+        // Memory imported through CUDA IPC reports the importing device, not the
+        // one it lives on: a caller that names a peer device is taken at its word
+        // (the data path then checks that the peer is reachable).
+        if (view.expected_accel_id >= 0 && a.device != view.expected_accel_id &&
+            !(view.expected_accel_id != im.cfg.accel_id && a.device == im.cfg.accel_id))
             return R::Failure({StatusCode::INVALID_ARGUMENT, "device memory belongs to another accelerator"});
     }
     // Overlapping registrations are refused: one owner per byte.
