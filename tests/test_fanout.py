@@ -24,11 +24,30 @@ def test_owner_of_is_le64_prefix_mod_group():
 
 
 class _Objects:
-    def __init__(self, table):
+    def __init__(self, table, rank=0):
         self.table = table
+        self.rank = rank
+        self.reserved, self.committed, self.aborted = [], [], []
 
     def lookup(self, key):
         return self.table.get(key)
+
+    def contains(self, key):
+        return key in self.committed
+
+    def reserve(self, keys):
+        out = []
+        for k in keys:
+            i = k[0]
+            out.append((k, f"file:///w{self.rank}/seg{i % 2}", 8192 * i, i, 1))
+            self.reserved.append(k)
+        return out, 0
+
+    def commit(self, keys):
+        self.committed += list(keys)
+
+    def abort(self, keys):
+        self.aborted += list(keys)
 
 
 class _Store:
@@ -37,8 +56,22 @@ class _Store:
     def __init__(self, rank, keys):
         self.rank = rank
         self._pool = (None, 100 + rank, 64)
-        self.objects = _Objects({k: (f"file:///r{rank}/seg{i % 2}", 4096 * i, i, 1) for i, k in enumerate(keys)})
+        self.objects = _Objects({k: (f"file:///r{rank}/seg{i % 2}", 4096 * i, i, 1) for i, k in enumerate(keys)},
+                                rank)
         self.calls = []
+        self.writes = []
+        self.fail_writes = False
+
+    def write_placements(self, todo, blocks, mems, stream=None):
+        if self.fail_writes:
+            raise OSError("injected write failure")
+        self.writes.append((list(todo), blocks.tolist(), [int(m) for m in mems]))
+
+        class _Done:
+            def wait(self):
+                return None
+
+        return _Done()
 
     def register_peer_pool(self, ptr, nbytes, device):
         return 1000 + device
@@ -56,7 +89,7 @@ class _Peers:
         self.devices = list(range(world))
 
 
-def _fanout_rank(rank, world, port, q):
+def _fanout_rank_q(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
@@ -78,19 +111,73 @@ def _fanout_rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_fanout_selects_drive_affine_share_for_all_ranks():
+def _spawn(fn, world=2, *extra):
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_fanout_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=fn, args=(r, world, port, q, *extra)) for r in range(world)]
     for p in ps:
         p.start()
-    out = dict(q.get(timeout=120) for _ in range(2))
+    out = dict(q.get(timeout=120) for _ in range(world))
     for p in ps:
         p.join(timeout=30)
+    return out
+
+
+def _store_rank(rank, world, port, q, failing_rank):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        keys = [bytes([i]) * 16 for i in range(4)]
+        store = _Store(rank, keys)
+        store.fail_writes = rank == failing_rank
+        fan = FanoutRestorer(store, _Peers(rank, world))
+        items = [RestoreItem(rank=r, key=k, block_ids=[10 * r + i, 10 * r + i + 1]) for r in range(world)
+                 for i, k in enumerate(keys)]
+        try:
+            n = fan.store(items, n_drives=2, affine_gpus=[0, 1])
+            res = ("ok", n)
+        except RuntimeError as e:
+            res = ("error", str(e))
+        o = store.objects
+        q.put((rank, (res, store.writes, o.committed, o.aborted)))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fanin_store_writes_drive_affine_share_and_commits_own_keys():
+    out = _spawn(_store_rank, 2, -1)
+    keys = [bytes([i]) * 16 for i in range(4)]
+    for r in range(2):
+        assert not isinstance(out[r], str), out[r]
+        res, writes, committed, aborted = out[r]
+        assert res == ("ok", 4)
+        # GPU r writes slots {r, r+2} of BOTH ranks' namespaces, gathering from the owner's pool
+        todo, blocks, mems = writes[0]
+        assert todo == [(f"/w{o}/seg{i % 2}", 8192 * i) for o in range(2) for i in (r, r + 2)]
+        assert mems == [100 + r if o == r else 1000 + o for o in range(2) for _ in (r, r + 2)]
+        assert blocks == [[10 * o + i, 10 * o + i + 1] for o in range(2) for i in (r, r + 2)]
+        assert committed == keys and aborted == []
+
+
+def test_fanin_store_failure_on_one_gpu_aborts_every_rank():
+    out = _spawn(_store_rank, 2, 1)
+    keys = [bytes([i]) * 16 for i in range(4)]
+    for r in range(2):
+        res, _writes, committed, aborted = out[r]
+        assert res[0] == "error" and committed == [] and aborted == keys
+    assert "injected write failure" in out[1][0][1]
+    assert "peer" in out[0][0][1]
+
+
+def test_fanout_selects_drive_affine_share_for_all_ranks():
+    out = _spawn(_fanout_rank_q, 2)
     for r in range(2):
         assert not isinstance(out[r], str), out[r]
         comp, comp2, calls = out[r]
@@ -108,8 +195,8 @@ def test_fanout_selects_drive_affine_share_for_all_ranks():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["tp", "mla"])
-def test_two_gpu_fanout_restore_matches_local(tmp_path, mode):
+@pytest.mark.parametrize("mode,store", [("tp", "local"), ("mla", "local"), ("tp", "fanout")])
+def test_two_gpu_fanout_restore_matches_local(tmp_path, mode, store):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     s = socket.socket()
@@ -119,7 +206,7 @@ def test_two_gpu_fanout_restore_matches_local(tmp_path, mode):
     cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(port),
            "-m", "tutti_b200.benchmarks.fanout", "--mode", mode, "--prefix-tokens", "4096", "--steps", "2",
-           "--warmup", "1", "--root", str(tmp_path / "fan"), "--leases", "32", "--ctas", "16"]
+           "--warmup", "1", "--root", str(tmp_path / "fan"), "--leases", "32", "--ctas", "16", "--store", store]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=460)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -55,6 +55,8 @@ def parse(argv=None):
     p.add_argument("--controller-threads", type=int, default=0)
     p.add_argument("--leases", type=int, default=128)
     p.add_argument("--ctas", type=int, default=64)
+    p.add_argument("--store", choices=["local", "fanout"], default="local",
+                   help="persist the prefix with each rank's own writes or through the drive-affine GPUs")
     p.add_argument("--timing", action="store_true", help="per-command %%globaltimer breakdown of the last mode")
     return p.parse_args(argv)
 
@@ -103,9 +105,17 @@ def main(argv=None) -> int:
         mine = list(range(nchunks))
     else:
         mine = [i for i, k in enumerate(keys) if owner_of(k, world) == rank]
-    if mine:
+    torch.cuda.synchronize()
+    dist.barrier(group=ctl)
+    t_store = time.perf_counter()
+    if args.store == "fanout":
+        src_items = [RestoreItem(rank=r, key=keys[i], block_ids=src[i].tolist()) for r in range(world)
+                     for i in range(nchunks) if args.mode == "tp" or owner_of(keys[i], world) == r]
+        fan.store(src_items, drives, affine)
+    elif mine:
         store.put_paged([keys[i] for i in mine], src[mine]).wait()
     dist.barrier(group=ctl)
+    store_ms = (time.perf_counter() - t_store) * 1e3
 
     # Destination blocks: a seeded permutation of the upper half, one per rank.
     dst = {r: (nblk + np.random.default_rng(r).permutation(pool_blocks - nblk)[:nblk]).reshape(
@@ -183,6 +193,7 @@ def main(argv=None) -> int:
         print(json.dumps({"bench": "fanout", "mode": args.mode, "n_gpus": world, "model": g.fingerprint(),
                           "prefix_tokens": args.prefix_tokens, "drives": drives, "affine_gpus": affine,
                           "steps": args.steps, "warmup": args.warmup, "results": results,
+                          "store": {"mode": args.store, "wall_ms": round(store_ms, 1)},
                           "controllers": len(peers_stats), "ok": ok, "io_timing": timing}))
     del pool
     dist.destroy_process_group()

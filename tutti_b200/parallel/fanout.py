@@ -87,10 +87,10 @@ class RestoreItem:
 
 
 class FanoutRestorer:
-    """Restores chunks for all ranks from the drives this GPU owns (drive-affine)."""
+    """Restores (and stores) chunks for all ranks through the drives this GPU owns (drive-affine)."""
 
     def __init__(self, store, peers: PeerPools, group=None):
-        self.store = store
+        self.kv = store
         self.peers = peers
         self.group = group
         self.mems = [store._pool[1] if r == peers.rank else store.register_peer_pool(p, peers.nbytes[r], peers.devices[r])
@@ -100,7 +100,7 @@ class FanoutRestorer:
         """Every rank looks up its own chunks; the (path, offset, slot) map is shared by all."""
         mine = {}
         for k in keys_by_rank.get(self.peers.rank, []):
-            p = self.store.objects.lookup(bytes(k))
+            p = self.kv.objects.lookup(bytes(k))
             if p is not None:
                 uri, off, slot, _gen = p
                 mine[(self.peers.rank, bytes(k))] = (uri[len("file://"):], off, slot)
@@ -134,10 +134,71 @@ class FanoutRestorer:
             blocks.append(list(it.block_ids))
         if not todo:
             return None
-        return self.store.restore_placements(todo, np.asarray(blocks, dtype=np.int64), np.asarray(mems, np.uint64),
+        return self.kv.restore_placements(todo, np.asarray(blocks, dtype=np.int64), np.asarray(mems, np.uint64),
                                              layers=layers, stream=stream)
+
+    def store(self, items: Sequence[RestoreItem], n_drives: int, affine_gpus: Sequence[int],
+              stream=None) -> int:
+        """Persist every rank's chunks through the drive-affine GPUs (gather over NVLink).
+
+        Collective over the group. Each rank reserves slots for its own new chunks in its
+        own namespace; the GPU affine to a slot's drive gathers the chunk's blocks from the
+        owner's pool (P2P loads inside the io kernel) and writes them; once every rank's
+        writes have completed, each rank commits its own chunks (or aborts them all if
+        any write failed anywhere). Returns how many chunks this rank committed.
+        """
+        me = self.peers.rank
+        objects = self.kv.objects
+        mine = [it for it in items if it.rank == me and not objects.contains(bytes(it.key))]
+        reserved, err = {}, ""
+        if mine:
+            accepted, rejected = objects.reserve([bytes(it.key) for it in mine])
+            for k, uri, off, slot, _gen in accepted:
+                reserved[(me, bytes(k))] = (uri[len("file://"):], off, slot)
+            if rejected:
+                err = f"rank {me}: {rejected} chunk(s) did not fit"
+        # the owners' pools must hold the blocks before any GPU gathers them
+        if torch.cuda.is_available():
+            torch.cuda.current_stream().synchronize()
+        allmaps: list = [None] * self.peers.world
+        dist.all_gather_object(allmaps, (reserved, err), group=self.group)
+        placements, errors = {}, [e for _, e in allmaps if e]
+        for m, _ in allmaps:
+            placements.update(m)
+        ok = not errors
+        if ok:
+            todo, mems, blocks = [], [], []
+            for it in items:
+                p = placements.get((it.rank, bytes(it.key)))
+                if p is None:
+                    continue  # already stored
+                path, off, slot = p
+                if affine_gpus[(slot % n_drives) % len(affine_gpus)] != me:
+                    continue
+                todo.append((path, off))
+                mems.append(self.mems[it.rank])
+                blocks.append(list(it.block_ids))
+            try:
+                if todo:
+                    self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64),
+                                                np.asarray(mems, np.uint64), stream=stream).wait()
+            except Exception as e:  # noqa: BLE001  (reported through the collective below)
+                errors.append(f"rank {me}: {e}")
+                ok = False
+        flags: list = [None] * self.peers.world
+        dist.all_gather_object(flags, ok, group=self.group)
+        keys = [k for (r, k) in reserved]
+        if all(flags):
+            objects.commit(keys)
+            return len(keys)
+        if keys:
+            objects.abort(keys)
+        if errors:
+            raise RuntimeError("; ".join(errors))
+        raise RuntimeError("a peer's drive-affine write failed; this rank's chunks were aborted")
 
     def barrier(self) -> None:
         """Orders every rank after all ranks' restores (their kernels completed before this)."""
-        torch.cuda.current_stream().synchronize()
+        if torch.cuda.is_available():
+            torch.cuda.current_stream().synchronize()
         dist.barrier(group=self.group)

@@ -295,6 +295,23 @@ class TuttiKVStore:
         self._track(comp)
         return comp
 
+    def write_placements(self, placements, block_ids, chunk_mems=None, stream=None) -> NativeCompletion:
+        """Write all layers of chunks to explicit (segment file path, payload offset) placements.
+
+        The slots must already be reserved (by this rank or by the rank that owns them);
+        committing them is the caller's job. ``chunk_mems[i]`` names the pool the chunk is
+        gathered from (a peer's pool is read over NVLink by the io kernel).
+        """
+        g = self.geometry
+        block_ids = np.asarray(block_ids, dtype=np.int64).reshape(len(placements), g.blocks_per_chunk)
+        cm = None if chunk_mems is None else np.asarray(chunk_mems, dtype=np.uint64)
+        if stream is None and self.backend == "nvme-gpu":
+            stream = torch.cuda.current_stream(self.device)
+        ios, nbytes = self._submit_paged("write", placements, block_ids, np.arange(g.num_layers), stream, chunk_mems=cm)
+        comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
+        self._track(comp)
+        return comp
+
     def _submit_paged(self, direction: str, placements, block_ids: np.ndarray, layers: np.ndarray, stream,
                       chunk_mems: np.ndarray | None = None):
         """Paged requests generated natively (no per-request Python work); retried while leases are busy."""
