@@ -131,3 +131,54 @@ def test_enqueue_wait_orders_consumer_stream(tmp_path):
         assert torch.equal(out, ref)
     finally:
         st.close()
+
+
+def _fp8_roundtrip_pages(pages: torch.Tensor) -> torch.Tensor:
+    """Standalone block-scaling kernels on whole pages: the bytes the fused path must reproduce."""
+    from tutti_b200 import ops
+
+    rows = pages.reshape(-1, pages[0, 0, 0].numel())
+    q, s = ops.fp8_quant(rows)
+    return ops.fp8_dequant(q, s).reshape(pages.shape)
+
+
+@pytest.mark.parametrize("drives", [1, 3])
+def test_fp8_stored_format_quantises_on_store_and_dequantises_on_restore(tmp_path, drives):
+    st = TuttiKVStore(tmp_path, G, capacity_chunks=64, mounts=[str(tmp_path / f"nvme{d}") for d in range(drives)],
+                      device=0, segment_file_slots=16, stored_format="fp8_block128",
+                      runtime_options={"leases": 8, "max_ctas_per_op": 8, "timeout_ms": 2000})
+    st.open()
+    try:
+        nb = 256
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda") * 3
+        pool[:, :, 5].zero_()  # an all-zero page: scale 1, zeros back
+        st.register_pool(pool)
+        n = 10
+        keys = chunk_keys_for_tokens(list(range(n * 64)), 64, namespace=b"f8")
+        rng = np.random.default_rng(1)
+        src = rng.permutation(nb)[: n * 4].reshape(n, 4)
+        src[0, 0] = 5
+        st.put_paged(keys, src).wait()
+        sidx = torch.from_numpy(src.reshape(-1)).cuda()
+        orig = pool[:, :, sidx].clone()
+        want = _fp8_roundtrip_pages(orig)
+        # stored bytes are 33/64 of the pool bytes
+        stats = st.runtime.controller_stats()
+        assert sum(x["write_bytes"] for x in stats) == n * G.num_layers * 4 * G.planes * st.stored["plane_bytes"]
+        dst = rng.permutation(nb)[: n * 4].reshape(n, 4)
+        pool.zero_()
+        st.get_paged(keys, dst).wait()
+        got = pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()]
+        assert torch.equal(got, want)  # identical to the standalone kernels
+        # and within E4M3 precision of the fp32 source: |err| <= amax(group) / 16
+        ref = orig.float().reshape(-1, 128)
+        amax = ref.abs().amax(dim=1, keepdim=True)
+        assert torch.all((got.float().reshape(-1, 128) - ref).abs() <= amax / 16 + 1e-6)
+        # layer subset restore of the transformed format
+        pool.zero_()
+        st.get_paged(keys[:2], dst[:2], layers=[1]).wait()
+        d2 = torch.from_numpy(dst[:2].reshape(-1)).cuda()
+        assert torch.equal(pool[1, :, d2], want[1, :, :8])
+        assert torch.count_nonzero(pool[0]) == 0
+    finally:
+        st.close()

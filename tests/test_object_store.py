@@ -136,3 +136,17 @@ def test_residency_bitmaps_all_ranks(tmp_path):
     assert s0.contains_prefix(keys, True) == 1
     s0.close()
     stores[1].close()
+
+
+def test_stored_geometry_fp8_sizes():
+    from tutti_b200.models.kv_geometry import DEEPSEEK_V3_MLA, LLAMA3_8B
+    from tutti_b200.storage.tutti_store import stored_geometry
+
+    s = stored_geometry(LLAMA3_8B, "fp8_block128")
+    assert s["plane_bytes"] == LLAMA3_8B.plane_block_bytes * 33 // 64
+    assert s["segment_bytes"] % 4096 == 0 and s["transform"] == 1
+    m = stored_geometry(DEEPSEEK_V3_MLA, "fp8_block128")
+    assert m["segment_bytes"] == 155648  # 4 x 38016 padded to 4 KiB
+    assert stored_geometry(LLAMA3_8B)["segment_bytes"] == LLAMA3_8B.segment_bytes
+    with pytest.raises(ValueError):
+        stored_geometry(LLAMA3_8B, "int4")

@@ -53,7 +53,7 @@ void merge_replicas(std::vector<io::IoCommand>& cmds, std::vector<io::IoPiece>& 
     for (std::uint32_t i = 0; i < cmds.size(); ++i) {
         const auto& c = cmds[i];
         if (c.opcode == nvme::kOpRead) {
-            const Key k{c.logical, c.target, c.bytes, c.n_pieces};
+            const Key k{c.logical, c.target | (std::uint32_t(c.transform) << 31), c.bytes, c.n_pieces};
             auto it = group_of.find(k);
             if (it != group_of.end() && same_tiling(cmds[groups[it->second][0]], c)) {
                 groups[it->second].push_back(i);
@@ -111,6 +111,7 @@ GpuNvmeDataPath::GpuNvmeDataPath(GpuNvmeConfig config, std::vector<GpuNvmeDevice
     caps_.supports_staged = true;
     caps_.supports_read = true;
     caps_.supports_write = true;
+    caps_.supports_fp8_block_transform = true;  // fused into the movers
     std::uint32_t lba = 512;
     for (auto& d : devs_)
         if (d.controller) lba = std::max(lba, d.controller->info().lba_bytes);
@@ -417,6 +418,12 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         return reject_all({StatusCode::UNSUPPORTED, "nvme-gpu executes on the device"});
 
     const std::uint64_t lba = caps_.length_alignment_bytes;
+    const bool xform = ctx.transform != IoTransform::NONE;
+    if (xform && ctx.transform != IoTransform::FP8_E4M3_BLOCK128)
+        return reject_all({StatusCode::INVALID_ARGUMENT, "unknown IoTransform"});
+    // Soft size of a transformed command: it may grow past this (up to one
+    // slot) to reach an LBA-aligned end.
+    const std::uint32_t xform_budget = cmd_bytes_ > (256u << 10) ? cmd_bytes_ - (256u << 10) : cmd_bytes_ / 2;
     auto op = std::make_unique<OpRec>();
     std::vector<io::IoCommand> cmds;
     std::vector<io::IoPiece> pieces;
@@ -445,11 +452,14 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         else if (r.target.token >= targets_.size() || targets_[r.target.token].generation != r.target.generation ||
                  !targets_[r.target.token].open)
             bad = {StatusCode::NOT_FOUND, "unknown target"};
-        else if (in.length == 0 || in.length % lba || in.target_offset % lba)
+        else if (!xform && (in.length == 0 || in.length % lba || in.target_offset % lba))
             bad = {StatusCode::INVALID_ARGUMENT, "offset/length must be LBA aligned"};
+        else if (xform && (in.length == 0 || in.length % 1024 || in.target_offset % 16 ||
+                           stored_bytes(ctx.transform, in.length) > cmd_bytes_))
+            bad = {StatusCode::INVALID_ARGUMENT, "fp8 transform: 1024-byte lengths, 16-byte offsets, one slot at most"};
         else if (in.memory_offset + in.length > mit->second.size)
             bad = {StatusCode::OUT_OF_RANGE, "memory range"};
-        else if (in.target_offset + in.length > targets_[r.target.token].size)
+        else if (in.target_offset + stored_bytes(ctx.transform, in.length) > targets_[r.target.token].size)
             bad = {StatusCode::OUT_OF_RANGE, "target range"};
         else if ((reinterpret_cast<std::uintptr_t>(mit->second.base) + in.memory_offset) % 16)
             bad = {StatusCode::INVALID_ARGUMENT, "memory address must be 16-byte aligned"};
@@ -463,13 +473,47 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         op->req_input_index.push_back(static_cast<std::uint32_t>(i));
         op->req_bytes.push_back(in.length);
         const std::uint32_t opcode = in.direction == IoDirection::READ ? nvme::kOpRead : nvme::kOpWrite;
+        if (xform) {
+            // A transformed request is one piece ([values][scales]) and is never
+            // split. A command closes only where the stored stream is LBA-aligned:
+            // past the soft budget it keeps growing until such a boundary.
+            const std::uint64_t sb = stored_bytes(ctx.transform, in.length);
+            bool extend = false;
+            if (!cmds.empty()) {
+                const io::IoCommand& c = cmds.back();
+                const bool aligned_end = (c.logical + c.bytes) % lba == 0;
+                extend = c.opcode == opcode && c.transform == io::kXformFp8Block128 &&
+                         c.target == r.target.token && c.logical + c.bytes == in.target_offset &&
+                         c.bytes + sb <= cmd_bytes_ && c.n_pieces < cfg_.max_pieces_per_cmd &&
+                         (c.bytes < xform_budget || !aligned_end);
+            }
+            if (!extend) {
+                io::IoCommand c{};
+                c.logical = in.target_offset;
+                c.target = static_cast<std::uint32_t>(r.target.token);
+                c.first_piece = static_cast<std::uint32_t>(pieces.size());
+                c.opcode = static_cast<std::uint16_t>(opcode);
+                c.transform = io::kXformFp8Block128;
+                cmds.push_back(c);
+                op->cmd_first_piece.push_back(c.first_piece);
+            }
+            io::IoCommand& c = cmds.back();
+            pieces.push_back(io::IoPiece{reinterpret_cast<std::uint64_t>(mit->second.base + in.memory_offset), c.bytes,
+                                         static_cast<std::uint32_t>(sb)});
+            op->piece_req.push_back(req_idx);
+            c.bytes += static_cast<std::uint32_t>(sb);
+            c.n_pieces += 1;
+            op->bytes += in.length;
+            continue;
+        }
         std::uint64_t done = 0;
         while (done < in.length) {
             const std::uint64_t lo = in.target_offset + done;
             bool extend = false;
             if (!cmds.empty()) {
                 const io::IoCommand& c = cmds.back();
-                extend = c.opcode == opcode && c.target == r.target.token && c.logical + c.bytes == lo &&
+                extend = c.opcode == opcode && c.transform == io::kXformNone && c.target == r.target.token &&
+                         c.logical + c.bytes == lo &&
                          c.bytes < cmd_bytes_ && c.n_pieces < cfg_.max_pieces_per_cmd;
             }
             if (!extend) {
@@ -479,7 +523,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
                 c.bytes = 0;
                 c.first_piece = static_cast<std::uint32_t>(pieces.size());
                 c.n_pieces = 0;
-                c.opcode = opcode;
+                c.opcode = static_cast<std::uint16_t>(opcode);
                 cmds.push_back(c);
                 op->cmd_first_piece.push_back(c.first_piece);
             }
@@ -497,6 +541,12 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     if (accepted == 0) {
         out.status = first_reject;
         return out;
+    }
+    if (xform) {
+        for (const auto& c : cmds)
+            if (c.logical % lba || c.bytes % lba)
+                return reject_all({StatusCode::INVALID_ARGUMENT,
+                                   "fp8-transformed requests must tile LBA-aligned runs of the target"});
     }
     merge_replicas(cmds, pieces, op->cmd_first_piece, op->piece_req);
     const std::uint32_t n_cmds = static_cast<std::uint32_t>(cmds.size());

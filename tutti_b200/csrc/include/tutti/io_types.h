@@ -81,10 +81,25 @@ enum class ExecutionDomain {
     DEVICE_EXECUTION,
 };
 
+// Stored format of the bytes a submit moves (one per submit). With
+// FP8_E4M3_BLOCK128 the memory side holds bf16 and each request is stored as
+// [E4M3 values][one fp32 scale per 128 values]: `length` stays the memory
+// length (a multiple of 1024), the target range is stored_bytes(length) long
+// and starts 16-byte aligned; consecutive requests must tile LBA-aligned runs.
+enum class IoTransform : std::uint32_t {
+    NONE = 0,
+    FP8_E4M3_BLOCK128 = 1,
+};
+
+inline std::uint64_t stored_bytes(IoTransform t, std::uint64_t memory_bytes) {
+    return t == IoTransform::FP8_E4M3_BLOCK128 ? memory_bytes / 64 * 33 : memory_bytes;
+}
+
 struct HostSubmitContext {
     ExecutionDomain execution_domain = ExecutionDomain::DEVICE_EXECUTION;
     std::int32_t accel_id = -1;  // -1: the owning runtime's accelerator
     cudaStream_t stream = nullptr;
+    IoTransform transform = IoTransform::NONE;
 };
 
 }  // namespace tutti

@@ -100,6 +100,7 @@ struct DataPathCapabilities {
     std::int32_t bound_accel_id = -1;  // -1: host-only / unbound
     bool supports_multi_gpu = false;
     bool supports_cross_device = false;
+    bool supports_fp8_block_transform = false;  // IoTransform::FP8_E4M3_BLOCK128
     std::vector<std::string> optional_target_features;
 };
 

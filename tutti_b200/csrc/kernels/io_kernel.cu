@@ -26,6 +26,10 @@
 // csrc/kv_transfer/src/mem_kernels.cu:66-130 scatter; status words follow
 // submit_one.cuh:117-143 (0 ok, 1 resolve, 2 timeout, 3 NVMe error).
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
 #include "io_kernel.h"
 
 namespace tutti {
@@ -67,6 +71,96 @@ __device__ __forceinline__ uint4 ld_cv_v4(const void* p) {
 __device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
     asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
+}
+
+__device__ __forceinline__ float ld_cv_f32(const void* p) {
+    float v;
+    asm volatile("ld.global.cv.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+constexpr float kE4M3Max = 448.0f;
+
+// 16 E4M3 values (one uint4) times `scale` -> 16 bf16 values (two uint4).
+__device__ __forceinline__ void fp8x16_dequant(uint4 q, float scale, uint4 out[2]) {
+    const std::uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    std::uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float f[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const __half_raw h =
+                __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>((w[i] >> (8 * b)) & 0xFFu), __NV_E4M3);
+            f[b] = __half2float(__half(h)) * scale;
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(f[0], f[1]), hi = __floats2bfloat162_rn(f[2], f[3]);
+        o[2 * i] = *reinterpret_cast<std::uint32_t*>(&lo);
+        o[2 * i + 1] = *reinterpret_cast<std::uint32_t*>(&hi);
+    }
+    out[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    out[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// Moves one fp8-transformed command: warps take pieces; within a piece a lane
+// handles 16 consecutive values, so 8 lanes share one 128-value scale group
+// (pieces hold a multiple of 512 values, so every lane of the warp takes part
+// in every iteration and the shuffles are full-warp).
+__device__ void move_slot_fp8(const IoKernelParams& p, const IoCommand& c, char* stage, bool to_memory, int gwarp,
+                              int lane) {
+    const IoPiece* pcs = p.pieces + c.first_piece;
+    const std::uint32_t groups = (to_memory && c.replicas > 1) ? c.replicas : 1u;
+    for (std::uint32_t q = gwarp; q < c.n_pieces; q += kWarpsPerGroup) {
+        const IoPiece pc = pcs[q];
+        const std::uint32_t k = pc.bytes / 33u;  // memory bytes / 64
+        const std::uint32_t units = 2u * k;      // 16-value units
+        char* vals = stage + pc.off;
+        char* scl = vals + 32u * k;
+        if (to_memory) {
+            for (std::uint32_t u = lane; u < units; u += 32) {
+                uint4 o[2];
+                fp8x16_dequant(ld_cv_v4(vals + 16u * u), ld_cv_f32(scl + 4u * (u >> 3)), o);
+                for (std::uint32_t g = 0; g < groups; ++g) {
+                    char* m = reinterpret_cast<char*>(g == 0 ? pc.mem : pcs[g * c.n_pieces + q].mem) + 32u * u;
+                    st_cs_v4(m, o[0]);
+                    st_cs_v4(m + 16, o[1]);
+                }
+            }
+        } else {
+            const char* mem = reinterpret_cast<const char*>(pc.mem);
+            for (std::uint32_t u = lane; u < units; u += 32) {
+                const uint4 a = *reinterpret_cast<const uint4*>(mem + 32u * u);
+                const uint4 b = *reinterpret_cast<const uint4*>(mem + 32u * u + 16);
+                const std::uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                float v[16];
+                float amax = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+                    v[2 * i] = f.x;
+                    v[2 * i + 1] = f.y;
+                    amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                const float sc = amax > 0.f ? amax / kE4M3Max : 1.f;
+                const float inv = 1.f / sc;
+                std::uint32_t packed[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    std::uint32_t x = 0;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const __nv_fp8_storage_t e = __nv_cvt_float_to_fp8(v[4 * i + b] * inv, __NV_SATFINITE, __NV_E4M3);
+                        x |= static_cast<std::uint32_t>(e) << (8 * b);
+                    }
+                    packed[i] = x;
+                }
+                *reinterpret_cast<uint4*>(vals + 16u * u) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                if ((lane & 7) == 0) *reinterpret_cast<float*>(scl + 4u * (u >> 3)) = sc;
+            }
+        }
+    }
 }
 
 // Non-aligned named barrier (threads of a warp may arrive after diverging);
@@ -145,6 +239,10 @@ __device__ int resolve_cmd(const IoKernelParams& p, const IoCommand& c, SubCmd* 
 // One mover group moves one slot: warps take 4 KiB chunks of the command.
 __device__ void move_slot(const IoKernelParams& p, const IoCommand& c, char* stage, bool to_memory, int gwarp,
                           int lane) {
+    if (c.transform == kXformFp8Block128) {
+        move_slot_fp8(p, c, stage, to_memory, gwarp, lane);
+        return;
+    }
     const IoPiece* pcs = p.pieces + c.first_piece;
     const std::uint32_t nchunks = (c.bytes + 4095u) >> 12;
     for (std::uint32_t ch = gwarp; ch < nchunks; ch += kWarpsPerGroup) {

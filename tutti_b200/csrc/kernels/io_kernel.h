@@ -30,13 +30,23 @@ constexpr int kMaxSub = 8;        // NVMe commands per staging slot (extent/MDTS
 constexpr int kMaxDevices = 8;    // devices (controllers) one launch can drive
 constexpr int kIoThreads = 512;   // threads per CTA
 
+// Stored-format transforms done by the movers while they move a slot.
+// kXformFp8Block128: memory holds bf16; each piece is stored as
+// [E4M3 values, n bytes][fp32 scale per 128 values, n/32 bytes] for the
+// piece's n bf16 values, i.e. 33/64 of the memory bytes. The scale is
+// amax/448 (1 for an all-zero group) and values saturate, as in the
+// standalone block-scaling kernels, so both produce identical bytes.
+constexpr std::uint16_t kXformNone = 0;
+constexpr std::uint16_t kXformFp8Block128 = 1;
+
 struct IoCommand {  // 32 B
     std::uint64_t logical;      // byte offset in the target
     std::uint32_t target;       // row of the device-resident target table
     std::uint32_t bytes;        // <= slot_bytes
     std::uint32_t first_piece;
     std::uint32_t n_pieces;     // pieces per destination group
-    std::uint32_t opcode;       // nvme::kOpRead / kOpWrite
+    std::uint16_t opcode;       // nvme::kOpRead / kOpWrite
+    std::uint16_t transform;    // kXformNone / kXformFp8Block128
     // Reads only: number of destination groups (0 or 1: one). Group g's pieces
     // are [first_piece + g*n_pieces, +n_pieces) with the same offsets as group 0;
     // the command's bytes are read once and stored to every group (e.g. the

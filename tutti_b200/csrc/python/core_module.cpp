@@ -314,6 +314,14 @@ PYBIND11_MODULE(_core, m) {
                 const std::uint64_t segment = geo["segment_bytes"].cast<std::uint64_t>();
                 const std::uint64_t block_layer = geo["block_layer_bytes"].cast<std::uint64_t>();
                 const std::uint64_t num_blocks = geo["num_blocks"].cast<std::uint64_t>();
+                // Stored format (optional): with the fp8 block transform the target-side
+                // plane and block strides are the stored (33/64) sizes.
+                const std::uint32_t transform = geo.contains("transform") ? geo["transform"].cast<std::uint32_t>() : 0u;
+                const std::uint64_t splane =
+                    geo.contains("stored_plane_bytes") ? geo["stored_plane_bytes"].cast<std::uint64_t>() : plane_bytes;
+                const std::uint64_t sblock = geo.contains("stored_block_layer_bytes")
+                                                 ? geo["stored_block_layer_bytes"].cast<std::uint64_t>()
+                                                 : block_layer;
                 const std::size_t n = static_cast<std::size_t>(chunk_targets.size());
                 if (chunk_offsets.size() != static_cast<py::ssize_t>(n) || block_ids.ndim() != 2 ||
                     block_ids.shape(0) != static_cast<py::ssize_t>(n))
@@ -349,7 +357,7 @@ PYBIND11_MODULE(_core, m) {
                                 q.memory = lmh;
                                 q.memory_offset = ((lterm + p) * num_blocks + static_cast<std::uint64_t>(b)) * plane_bytes;
                                 q.target = th;
-                                q.target_offset = co(c) + L * segment + j * block_layer + p * plane_bytes;
+                                q.target_offset = co(c) + L * segment + j * sblock + p * splane;
                                 q.length = plane_bytes;
                             }
                         }
@@ -359,6 +367,8 @@ PYBIND11_MODULE(_core, m) {
                 ctx.execution_domain = host_exec ? ExecutionDomain::HOST_EXECUTION : ExecutionDomain::DEVICE_EXECUTION;
                 ctx.accel_id = -1;
                 ctx.stream = reinterpret_cast<cudaStream_t>(stream);
+                if (transform > 1) throw py::value_error("transform: 0 (none) or 1 (fp8 e4m3, 1x128 scales)");
+                ctx.transform = static_cast<IoTransform>(transform);
                 IoSubmitOutcome o;
                 {
                     py::gil_scoped_release nogil;

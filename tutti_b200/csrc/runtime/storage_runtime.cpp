@@ -694,6 +694,9 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
     const DataPathCapabilities* caps = nullptr;
     Group* last_gp = nullptr;
     std::vector<std::uint32_t> mem_count(im.mems.size(), 0), tgt_count(im.tgts.size(), 0);
+    const bool xform = ctx.transform != IoTransform::NONE;
+    if (xform && ctx.transform != IoTransform::FP8_E4M3_BLOCK128)
+        return reject_all({StatusCode::INVALID_ARGUMENT, "unknown IoTransform"});
     for (std::size_t i = 0; i < count; ++i) {
         const IoRequest& r = reqs[i];
         if (!last_m || r.memory != last_mh) {
@@ -715,8 +718,10 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
             bad = {StatusCode::INVALID_ARGUMENT, "zero length"};
         else if (r.memory_offset > m->view.size || r.length > m->view.size - r.memory_offset)
             bad = {StatusCode::OUT_OF_RANGE, "memory range exceeds registration"};
-        else if (r.target_offset > t->size || r.length > t->size - r.target_offset)
+        else if (r.target_offset > t->size || stored_bytes(ctx.transform, r.length) > t->size - r.target_offset)
             bad = {StatusCode::OUT_OF_RANGE, "target range exceeds logical size"};
+        else if (xform && (r.length % 1024 || r.target_offset % 16))
+            bad = {StatusCode::INVALID_ARGUMENT, "fp8 block transform needs 1024-byte lengths, 16-byte target offsets"};
         Impl::DpEntry* d = nullptr;
         if (bad.ok()) {
             d = t->dpe;
@@ -734,7 +739,9 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
             else if ((ctx.execution_domain == ExecutionDomain::DEVICE_EXECUTION && !c.supports_device_execution) ||
                      (ctx.execution_domain == ExecutionDomain::HOST_EXECUTION && !c.supports_host_execution))
                 bad = {StatusCode::UNSUPPORTED, "execution domain not supported by " + d->key};
-            else if (r.target_offset % c.target_alignment_bytes || r.length % c.length_alignment_bytes ||
+            else if (xform && !c.supports_fp8_block_transform)
+                bad = {StatusCode::UNSUPPORTED, d->key + " cannot apply the fp8 block transform"};
+            else if ((!xform && (r.target_offset % c.target_alignment_bytes || r.length % c.length_alignment_bytes)) ||
                      (reinterpret_cast<std::uintptr_t>(m->view.address) + r.memory_offset) % c.memory_alignment_bytes)
                 bad = {StatusCode::INVALID_ARGUMENT, "alignment violates " + d->key + " capabilities"};
             else if (c.max_single_io_bytes && r.length > c.max_single_io_bytes)

@@ -34,6 +34,33 @@ from .base import StoreIOError
 from .object_layout import DEFAULT_SEGMENT_FILE_SLOTS, DEFAULT_SEGMENT_HEADER_BYTES, ObjectLayout
 
 
+STORED_FORMATS = ("native", "fp8_block128")
+
+
+def stored_geometry(g: KVGeometry, stored_format: str = "native") -> dict:
+    """On-disk sizes of one rank's chunk slice in ``stored_format``.
+
+    ``native`` stores the pool's bytes as they are. ``fp8_block128`` stores each
+    bf16 (layer, plane, block) page as E4M3 values followed by one fp32 scale per
+    128 values (33/64 of the bytes; the io kernel quantises on store and
+    dequantises on restore); each layer segment is padded to 4 KiB.
+    """
+    if stored_format == "native":
+        return {"plane_bytes": g.plane_block_bytes, "block_layer_bytes": g.block_layer_bytes,
+                "segment_bytes": g.segment_bytes, "transform": 0}
+    if stored_format != "fp8_block128":
+        raise ValueError(f"stored_format must be one of {STORED_FORMATS}")
+    if g.dtype != torch.bfloat16 or g.plane_block_bytes % 1024:
+        raise ValueError("fp8_block128 needs bf16 pages of a multiple of 512 values")
+    plane = g.plane_block_bytes // 64 * 33
+    block_layer = g.planes * plane
+    payload = g.blocks_per_chunk * block_layer
+    if payload % 512:
+        raise ValueError("fp8_block128: a layer segment must be a whole number of 512-byte sectors")
+    return {"plane_bytes": plane, "block_layer_bytes": block_layer,
+            "segment_bytes": (payload + 4095) // 4096 * 4096, "transform": 1}
+
+
 class NativeCompletion:
     """Completion of one or more runtime IOs; ``wait`` raises StoreIOError on failure."""
 
@@ -90,16 +117,20 @@ class TuttiKVStore:
                  backend: str = "nvme-gpu", runtime_options: dict | None = None,
                  segment_file_slots: int = DEFAULT_SEGMENT_FILE_SLOTS,
                  segment_header_bytes: int = DEFAULT_SEGMENT_HEADER_BYTES, namespace: bytes = b"",
-                 materialize: str = "zeros", max_retries: int = 1000):
+                 materialize: str = "zeros", max_retries: int = 1000, stored_format: str = "native"):
         self.root = Path(root)
         self.geometry = geometry
         self.device = device
         self.backend = backend
         self.mounts = [str(m) for m in (mounts or [self.root / "dev0"])]
         self.runtime_options = dict(runtime_options or {})
-        self.layout = ObjectLayout(self.root, segment_bytes=geometry.segment_bytes,
+        self.stored = stored_geometry(geometry, stored_format)
+        if stored_format != "native" and backend != "nvme-gpu":
+            raise ValueError(f"stored_format {stored_format!r} needs the nvme-gpu backend (fused in its io kernel)")
+        fp = geometry.fingerprint() + ("" if stored_format == "native" else ":" + stored_format)
+        self.layout = ObjectLayout(self.root, segment_bytes=self.stored["segment_bytes"],
                                    segment_count=geometry.num_layers, capacity_chunks=capacity_chunks,
-                                   mounts=self.mounts, namespace=namespace or geometry.fingerprint().encode(),
+                                   mounts=self.mounts, namespace=namespace or fp.encode(),
                                    rank=rank, rank_count=rank_count, segment_file_slots=segment_file_slots,
                                    segment_header_bytes=segment_header_bytes, materialize=materialize)
         self.max_retries = max_retries
@@ -221,6 +252,8 @@ class TuttiKVStore:
                       layers: np.ndarray) -> tuple[np.ndarray, ...]:
         """(target handles, target offsets, memory offsets, lengths) in (chunk, layer, block, plane) order."""
         g = self.geometry
+        if self.stored["transform"]:
+            raise NotImplementedError("transformed stores submit through submit_paged (get_paged/put_paged)")
         if self._pool is None:
             raise RuntimeError("register_pool() first")
         nb = self._pool[2]
@@ -318,8 +351,11 @@ class TuttiKVStore:
         g = self.geometry
         handles = np.asarray(self.targets_for([p for p, _ in placements]), dtype=np.uint64)
         offsets = np.asarray([o for _, o in placements], dtype=np.uint64)
-        geo = {"planes": g.planes, "plane_bytes": g.plane_block_bytes, "segment_bytes": g.segment_bytes,
-               "block_layer_bytes": g.block_layer_bytes, "num_blocks": int(self._pool[2])}
+        st = self.stored
+        geo = {"planes": g.planes, "plane_bytes": g.plane_block_bytes, "segment_bytes": st["segment_bytes"],
+               "block_layer_bytes": g.block_layer_bytes, "num_blocks": int(self._pool[2]),
+               "stored_plane_bytes": st["plane_bytes"], "stored_block_layer_bytes": st["block_layer_bytes"],
+               "transform": st["transform"]}
         bt = np.ascontiguousarray(block_ids, dtype=np.int64)
         ly = np.ascontiguousarray(layers, dtype=np.int64)
         sptr = self._stream_ptr(stream)
