@@ -182,3 +182,27 @@ def test_fp8_stored_format_quantises_on_store_and_dequantises_on_restore(tmp_pat
         assert torch.count_nonzero(pool[0]) == 0
     finally:
         st.close()
+
+
+def test_subsector_index_pages_pack_into_aligned_commands(tmp_path):
+    # DeepSeek-V3.2-style index cache: 132 bytes per token, 8,448-byte pages (not a sector multiple)
+    gi = KVGeometry("t-idx", num_layers=3, num_kv_heads=1, head_dim=132, block_size=64, planes=1,
+                    dtype=torch.uint8, chunk_tokens=256)
+    st = TuttiKVStore(tmp_path, gi, capacity_chunks=32, mounts=[str(tmp_path / f"nvme{d}") for d in range(2)],
+                      device=0, segment_file_slots=16, runtime_options={"leases": 8, "max_ctas_per_op": 8})
+    st.open()
+    try:
+        nb = 64
+        pool = torch.randint(0, 256, gi.pool_shape(nb), dtype=torch.uint8, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(5 * 256)), 256, namespace=b"idx")
+        rng = np.random.default_rng(2)
+        src = rng.permutation(nb)[:20].reshape(5, 4)
+        st.put_paged(keys, src).wait()
+        ref = pool[:, :, torch.from_numpy(src.reshape(-1)).cuda()].clone()
+        dst = rng.permutation(nb)[:20].reshape(5, 4)
+        pool.zero_()
+        st.get_paged(keys, dst).wait()
+        assert torch.equal(pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()], ref)
+    finally:
+        st.close()

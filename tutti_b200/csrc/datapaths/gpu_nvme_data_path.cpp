@@ -115,9 +115,13 @@ GpuNvmeDataPath::GpuNvmeDataPath(GpuNvmeConfig config, std::vector<GpuNvmeDevice
     std::uint32_t lba = 512;
     for (auto& d : devs_)
         if (d.controller) lba = std::max(lba, d.controller->info().lba_bytes);
-    caps_.target_alignment_bytes = lba;
+    // Requests need only 16-byte alignment: sub-sector pieces (e.g. 8,448-byte
+    // index-cache pages) are packed into commands, and it is the commands that
+    // must start and end on LBA boundaries (checked per submit).
+    lba_ = lba;
+    caps_.target_alignment_bytes = 16;
     caps_.memory_alignment_bytes = 16;
-    caps_.length_alignment_bytes = lba;
+    caps_.length_alignment_bytes = 16;
     caps_.max_single_io_bytes = 0;
     caps_.max_batch_requests = 1u << 26;
     caps_.supports_scatter_gather = true;
@@ -417,7 +421,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     if (ctx.execution_domain != ExecutionDomain::DEVICE_EXECUTION)
         return reject_all({StatusCode::UNSUPPORTED, "nvme-gpu executes on the device"});
 
-    const std::uint64_t lba = caps_.length_alignment_bytes;
+    const std::uint64_t lba = lba_;
     const bool xform = ctx.transform != IoTransform::NONE;
     if (xform && ctx.transform != IoTransform::FP8_E4M3_BLOCK128)
         return reject_all({StatusCode::INVALID_ARGUMENT, "unknown IoTransform"});
@@ -452,11 +456,12 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         else if (r.target.token >= targets_.size() || targets_[r.target.token].generation != r.target.generation ||
                  !targets_[r.target.token].open)
             bad = {StatusCode::NOT_FOUND, "unknown target"};
-        else if (!xform && (in.length == 0 || in.length % lba || in.target_offset % lba))
-            bad = {StatusCode::INVALID_ARGUMENT, "offset/length must be LBA aligned"};
-        else if (xform && (in.length == 0 || in.length % 1024 || in.target_offset % 16 ||
-                           stored_bytes(ctx.transform, in.length) > cmd_bytes_))
-            bad = {StatusCode::INVALID_ARGUMENT, "fp8 transform: 1024-byte lengths, 16-byte offsets, one slot at most"};
+        else if (in.length == 0 || in.length % 16 || in.target_offset % 16)
+            bad = {StatusCode::INVALID_ARGUMENT, "offset/length must be 16-byte aligned"};
+        else if (xform && (in.length % 1024 || stored_bytes(ctx.transform, in.length) > cmd_bytes_))
+            bad = {StatusCode::INVALID_ARGUMENT, "fp8 transform: 1024-byte lengths, one slot at most"};
+        else if (!xform && (in.length % lba || in.target_offset % lba) && in.length > cmd_bytes_)
+            bad = {StatusCode::INVALID_ARGUMENT, "a request that is not LBA aligned must fit one slot"};
         else if (in.memory_offset + in.length > mit->second.size)
             bad = {StatusCode::OUT_OF_RANGE, "memory range"};
         else if (in.target_offset + stored_bytes(ctx.transform, in.length) > targets_[r.target.token].size)
@@ -473,16 +478,18 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         op->req_input_index.push_back(static_cast<std::uint32_t>(i));
         op->req_bytes.push_back(in.length);
         const std::uint32_t opcode = in.direction == IoDirection::READ ? nvme::kOpRead : nvme::kOpWrite;
-        if (xform) {
-            // A transformed request is one piece ([values][scales]) and is never
-            // split. A command closes only where the stored stream is LBA-aligned:
-            // past the soft budget it keeps growing until such a boundary.
+        if (xform || in.length % lba || in.target_offset % lba) {
+            // A transformed or sub-sector request is one piece (for the transform:
+            // [values][scales]) and is never split. A command closes only where the
+            // stored stream is LBA-aligned: past the soft budget it keeps growing
+            // until such a boundary.
+            const std::uint16_t kind = xform ? io::kXformFp8Block128 : io::kXformNone;
             const std::uint64_t sb = stored_bytes(ctx.transform, in.length);
             bool extend = false;
             if (!cmds.empty()) {
                 const io::IoCommand& c = cmds.back();
                 const bool aligned_end = (c.logical + c.bytes) % lba == 0;
-                extend = c.opcode == opcode && c.transform == io::kXformFp8Block128 &&
+                extend = c.opcode == opcode && c.transform == kind &&
                          c.target == r.target.token && c.logical + c.bytes == in.target_offset &&
                          c.bytes + sb <= cmd_bytes_ && c.n_pieces < cfg_.max_pieces_per_cmd &&
                          (c.bytes < xform_budget || !aligned_end);
@@ -493,7 +500,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
                 c.target = static_cast<std::uint32_t>(r.target.token);
                 c.first_piece = static_cast<std::uint32_t>(pieces.size());
                 c.opcode = static_cast<std::uint16_t>(opcode);
-                c.transform = io::kXformFp8Block128;
+                c.transform = kind;
                 cmds.push_back(c);
                 op->cmd_first_piece.push_back(c.first_piece);
             }
@@ -542,12 +549,10 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         out.status = first_reject;
         return out;
     }
-    if (xform) {
-        for (const auto& c : cmds)
-            if (c.logical % lba || c.bytes % lba)
-                return reject_all({StatusCode::INVALID_ARGUMENT,
-                                   "fp8-transformed requests must tile LBA-aligned runs of the target"});
-    }
+    for (const auto& c : cmds)
+        if (c.logical % lba || c.bytes % lba)
+            return reject_all({StatusCode::INVALID_ARGUMENT,
+                               "requests that are not LBA aligned (or transformed) must tile LBA-aligned runs"});
     merge_replicas(cmds, pieces, op->cmd_first_piece, op->piece_req);
     const std::uint32_t n_cmds = static_cast<std::uint32_t>(cmds.size());
     const auto t_coalesced = std::chrono::steady_clock::now();

@@ -166,6 +166,7 @@ private:
     // staging arena + PRP-list pages (host mapped), one per lease x slot
     HostMappedBuffer staging_, prp_;
     std::uint64_t staging_iova_ = 0, prp_iova_ = 0;
+    std::uint32_t lba_ = 512;  // largest LBA size of the device table
 
     std::vector<TargetRec> targets_;
     std::vector<std::uint32_t> free_target_rows_;

@@ -40,14 +40,18 @@ STORED_FORMATS = ("native", "fp8_block128")
 def stored_geometry(g: KVGeometry, stored_format: str = "native") -> dict:
     """On-disk sizes of one rank's chunk slice in ``stored_format``.
 
-    ``native`` stores the pool's bytes as they are. ``fp8_block128`` stores each
+    ``native`` stores the pool's bytes as they are (a layer segment padded to
+    4 KiB). ``fp8_block128`` stores each
     bf16 (layer, plane, block) page as E4M3 values followed by one fp32 scale per
     128 values (33/64 of the bytes; the io kernel quantises on store and
     dequantises on restore); each layer segment is padded to 4 KiB.
     """
     if stored_format == "native":
+        # sub-sector pages (e.g. 8,448-byte index-cache pages) are fine; the segment is padded to 4 KiB
+        if g.segment_bytes % 512:
+            raise ValueError("a layer segment must be a whole number of 512-byte sectors")
         return {"plane_bytes": g.plane_block_bytes, "block_layer_bytes": g.block_layer_bytes,
-                "segment_bytes": g.segment_bytes, "transform": 0}
+                "segment_bytes": (g.segment_bytes + 4095) // 4096 * 4096, "transform": 0}
     if stored_format != "fp8_block128":
         raise ValueError(f"stored_format must be one of {STORED_FORMATS}")
     if g.dtype != torch.bfloat16 or g.plane_block_bytes % 1024:
