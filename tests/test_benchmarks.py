@@ -1,0 +1,42 @@
+"""Pure-host parts of the benchmark drivers: trace generation and the compute model."""
+import argparse
+
+from tutti_b200.benchmarks.serving_trace import FALLBACK_PEAKS, make_trace, prefill_seconds
+
+
+def _args(**kw):
+    base = dict(seed=0, distinct=512, zipf=1.1, min_prefix=8192, max_prefix=65536, length_scale=1.0,
+                requests=400, reuse=0.8)
+    base.update(kw)
+    return argparse.Namespace(**base)
+
+
+def test_trace_is_seeded_and_shaped():
+    a = make_trace(_args(), 256)
+    assert a == make_trace(_args(), 256)
+    assert all(r["tokens"] % 256 == 0 and 8192 - 256 <= r["tokens"] <= 65536 for r in a)
+    reused = sum(r["prefix"] < 512 for r in a) / len(a)
+    assert 0.7 < reused < 0.9
+    # Zipf: the most popular prefix recurs
+    counts = {}
+    for r in a:
+        counts[r["prefix"]] = counts.get(r["prefix"], 0) + 1
+    assert max(counts.values()) >= 10
+    # the same prefix id always has the same length
+    lens = {}
+    for r in a:
+        assert lens.setdefault(r["prefix"], r["tokens"]) == r["tokens"]
+
+
+def test_length_scale_shrinks_prefixes():
+    a = make_trace(_args(length_scale=0.125), 256)
+    assert all(256 <= r["tokens"] <= 8192 for r in a)
+
+
+def test_prefill_model_grows_with_tokens_and_shrinks_with_tp():
+    pk = dict(FALLBACK_PEAKS)
+    assert prefill_seconds(0, 1000, 8, pk, 0.5) == 0.0
+    one = prefill_seconds(4096, 0, 1, pk, 0.5)
+    assert prefill_seconds(8192, 0, 1, pk, 0.5) > 2 * one * 0.99
+    assert abs(prefill_seconds(4096, 0, 8, pk, 0.5) - one / 8) < 1e-12
+    assert prefill_seconds(512, 32768, 1, pk, 0.5) < prefill_seconds(32768 + 512, 0, 1, pk, 0.5)

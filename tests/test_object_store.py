@@ -150,3 +150,32 @@ def test_stored_geometry_fp8_sizes():
     assert stored_geometry(LLAMA3_8B)["segment_bytes"] == LLAMA3_8B.segment_bytes
     with pytest.raises(ValueError):
         stored_geometry(LLAMA3_8B, "int4")
+
+
+def test_store_grows_segment_files_on_demand(tmp_path):
+    """put_paged beyond the first file group materialises more groups instead of failing (posix, host pool)."""
+    import numpy as np
+    import torch
+
+    from tutti_b200.index.chunk_index import chunk_keys_for_tokens
+    from tutti_b200.models.kv_geometry import KVGeometry
+    from tutti_b200.storage.tutti_store import TuttiKVStore
+
+    g = KVGeometry("t-grow", num_layers=2, num_kv_heads=1, head_dim=128, chunk_tokens=64)
+    st = TuttiKVStore(tmp_path, g, capacity_chunks=64, mounts=[str(tmp_path / "d0"), str(tmp_path / "d1")],
+                      device=-1, backend="posix", segment_file_slots=4, runtime_options={"threads": 2})
+    st.open()
+    try:
+        assert st.objects.ready_slots < 40
+        pool = torch.randn(g.pool_shape(256), dtype=torch.bfloat16)
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(40 * 64)), 64, namespace=b"grow")
+        src = np.arange(160).reshape(40, 4)
+        st.put_paged(keys, src).wait()
+        assert st.objects.ready_slots >= 40
+        ref = pool[:, :, :160].clone()
+        pool.zero_()
+        st.get_paged(keys, src).wait()
+        assert torch.equal(pool[:, :, :160], ref)
+    finally:
+        st.close()

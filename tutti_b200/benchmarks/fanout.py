@@ -57,6 +57,8 @@ def parse(argv=None):
     p.add_argument("--ctas", type=int, default=64)
     p.add_argument("--store", choices=["local", "fanout"], default="local",
                    help="persist the prefix with each rank's own writes or through the drive-affine GPUs")
+    p.add_argument("--stored-format", choices=["native", "fp8_block128"], default="native",
+                   help="fp8_block128: the io kernel quantises on store and dequantises on restore")
     p.add_argument("--timing", action="store_true", help="per-command %%globaltimer breakdown of the last mode")
     return p.parse_args(argv)
 
@@ -88,7 +90,7 @@ def main(argv=None) -> int:
     spf = max(16, (nchunks + drives - 1) // drives)
     store = TuttiKVStore(args.root, g, capacity_chunks=spf * drives, mounts=mounts, device=local,
                          rank=rank, rank_count=world, runtime_options=opts, segment_file_slots=spf,
-                         namespace=b"fanout-" + args.mode.encode())
+                         namespace=b"fanout-" + args.mode.encode(), stored_format=args.stored_format)
     store.open()
     pool = torch.zeros(g.pool_shape(pool_blocks), dtype=g.dtype, device=dev)
     store.register_pool(pool)
@@ -163,7 +165,13 @@ def main(argv=None) -> int:
     def verify() -> bool:
         s = torch.from_numpy(src.reshape(-1)).to(dev)
         d = torch.from_numpy(dst[rank].reshape(-1)).to(dev)
-        ok = torch.tensor([1.0 if torch.equal(pool[:, :, d], pool[:, :, s]) else 0.0], device=dev)
+        want = pool[:, :, s]
+        if args.stored_format == "fp8_block128":
+            from .. import ops
+
+            q, sc = ops.fp8_quant(want.reshape(-1, 128))
+            want = ops.fp8_dequant(q, sc).reshape(want.shape)
+        ok = torch.tensor([1.0 if torch.equal(pool[:, :, d], want) else 0.0], device=dev)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         return bool(ok.item() == 1.0)
 

@@ -152,7 +152,8 @@ class FanoutRestorer:
         mine = [it for it in items if it.rank == me and not objects.contains(bytes(it.key))]
         reserved, err = {}, ""
         if mine:
-            accepted, rejected = objects.reserve([bytes(it.key) for it in mine])
+            reserve = getattr(self.kv, "reserve", objects.reserve)  # the store grows its files on demand
+            accepted, rejected = reserve([bytes(it.key) for it in mine])
             for k, uri, off, slot, _gen in accepted:
                 reserved[(me, bytes(k))] = (uri[len("file://"):], off, slot)
             if rejected:

@@ -398,6 +398,22 @@ class TuttiKVStore:
         self._track(comp)
         return comp
 
+    def reserve(self, keys: Sequence[bytes]):
+        """Reserve slots for ``keys``, materialising more segment-file groups when the ready ones run out.
+
+        Returns the object store's ``(accepted, rejected_count)``; accepted rows are
+        ``(key, uri, offset, slot, generation)``.
+        """
+        keys = [bytes(k) for k in keys]
+        accepted, rejected = self.objects.reserve(keys)
+        if rejected:
+            got = {bytes(a[0]) for a in accepted}
+            rest = [k for k in keys if k not in got]
+            self.layout.precreate_until(self.objects.ready_slots + len(rest))
+            more, rejected = self.objects.reserve(rest)
+            accepted = list(accepted) + list(more)
+        return accepted, rejected
+
     def put_paged(self, keys: Sequence[bytes], block_ids, stream=None) -> NativeCompletion:
         """Persist all layers of chunks ``keys`` from pool blocks ``block_ids[i]``; commit on wait."""
         g = self.geometry
@@ -406,9 +422,13 @@ class TuttiKVStore:
         fresh = [i for i, k in enumerate(keys) if not self.objects.contains(k)]
         if not fresh:
             return NativeCompletion(self.runtime, [])
-        accepted, rejected = self.objects.reserve([keys[i] for i in fresh])
+        accepted, rejected = self.reserve([keys[i] for i in fresh])
         if rejected:
+            self.objects.abort([a[0] for a in accepted])
             raise StoreIOError(f"{rejected} chunk(s) did not fit (capacity)", kind="capacity")
+        # reserve() may return rows out of input order after growing: follow the input order
+        by_key = {bytes(a[0]): a for a in accepted}
+        accepted = [by_key[keys[i]] for i in fresh]
         placements = [(uri[len("file://"):], off) for (_k, uri, off, _s, _g) in accepted]
         wkeys = [a[0] for a in accepted]
         if self.backend == "nvme-gpu" and stream is None:
