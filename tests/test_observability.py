@@ -1,0 +1,51 @@
+"""Metrics counters, health lines and the NVTX switch (host only)."""
+import logging
+
+from tutti_b200.common import observability as obs
+from tutti_b200.storage.tutti_store import NativeCompletion
+
+
+class _Rt:
+    def __init__(self, ok=True):
+        self.ok = ok
+
+    def wait(self, io, timeout_ms):
+        return {"ok": self.ok, "failed_request_indices": [] if self.ok else [0, 3], "failure_kind": "cq_timeout"}
+
+    def release_io(self, io):
+        pass
+
+
+def test_completion_counts_bytes_and_failures():
+    m = obs.metrics()
+    before = m.snapshot()
+    NativeCompletion(_Rt(), [1], nbytes=4096).wait()
+    NativeCompletion(_Rt(), [2], nbytes=100, kind="store").wait()
+    try:
+        NativeCompletion(_Rt(ok=False), [3], nbytes=7).wait()
+    except Exception:
+        pass
+    after = m.snapshot()
+    assert after["restore_bytes"] - before["restore_bytes"] == 4096
+    assert after["store_bytes"] - before["store_bytes"] == 100
+    assert after["restore_ops"] - before["restore_ops"] == 2
+    assert after["failed_ops"] - before["failed_ops"] == 1
+    assert after["failed_requests"] - before["failed_requests"] == 2
+
+
+def test_health_line_rate_limited_and_reports_bandwidth(caplog):
+    t = [100.0]
+    h = obs.HealthReporter(store=None, interval_s=30, clock=lambda: t[0])
+    assert h.maybe_log() is None
+    obs.metrics().add("restore_bytes", 3 * 10**9)
+    t[0] += 30.0
+    with caplog.at_level(logging.INFO, logger="tutti_b200"):
+        r = h.maybe_log()
+    assert r is not None and abs(r["restore_GBps"] - 0.1) < 1e-9
+    assert any("[tutti] health" in rec.message for rec in caplog.records)
+
+
+def test_nvtx_range_is_free_when_disabled():
+    assert not obs.nvtx_enabled()
+    with obs.nvtx_range("x"):
+        pass

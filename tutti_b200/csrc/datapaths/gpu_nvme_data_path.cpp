@@ -2,9 +2,12 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "../runtime/device_guard.h"
 
@@ -89,6 +92,15 @@ void merge_replicas(std::vector<io::IoCommand>& cmds, std::vector<io::IoPiece>& 
     pieces.swap(np);
     cmd_first_piece.swap(nfirst);
     piece_req.swap(nreq);
+}
+
+// NVTX ranges around each submit, opt-in with TUTTI_NVTX=1 (read once).
+bool nvtx_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("TUTTI_NVTX");
+        return e && *e && std::strcmp(e, "0") != 0;
+    }();
+    return on;
 }
 
 double percentile(std::vector<double>& v, double q) {
@@ -228,6 +240,12 @@ Status GpuNvmeDataPath::init_device_side() {
     TUTTI_RETURN_IF_ERROR(cuda_status(
         cudaMemset(d_targets_, 0, std::size_t(cfg_.max_targets) * sizeof(io::DevTarget)), "memset targets"));
     for (std::uint32_t l = cfg_.leases; l-- > 0;) free_leases_.push_back(l);
+    if (const char* v = std::getenv("TUTTI_VERBOSE"); v && *v && std::strcmp(v, "0") != 0)
+        std::fprintf(stderr,
+                     "[tutti] nvme-gpu accel %d: %zu controller(s), %u leases x %u slots x %u KiB staging, "
+                     "commands up to %u KiB, LBA %u, timeout %.1f s\n",
+                     cfg_.accel_id, devs_.size(), cfg_.leases, cfg_.slots_per_lease, cfg_.slot_bytes >> 10,
+                     cmd_bytes_ >> 10, lba_, cfg_.timeout_ns / 1e9);
     return Status::Ok();
 }
 
@@ -605,8 +623,16 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     kp.timing = timing ? reinterpret_cast<std::uint64_t*>(d + off_timing) : nullptr;
 
     cudaStream_t s = ctx.stream;
+    const bool nvtx = nvtx_enabled();
+    if (nvtx) {
+        char name[128];
+        std::snprintf(name, sizeof(name), "tutti.nvme_gpu.submit|op=%s|cmds=%u|ctas=%u%s",
+                      cmds[0].opcode == nvme::kOpRead ? "read" : "write", n_cmds, take, xform ? "|fp8" : "");
+        nvtxRangePushA(name);
+    }
     Status cs = cuda_status(cudaMemcpyAsync(d, h, off_timing, cudaMemcpyHostToDevice, s), "H2D commands");
     if (cs.ok()) cs = cuda_status(io::launch_nvme_io(kp, take, s), "io kernel launch");
+    if (nvtx) nvtxRangePop();
     if (cs.ok())
         cs = cuda_status(cudaMemcpyAsync(h + off_status, d + off_status, total - off_status, cudaMemcpyDeviceToHost, s),
                          "D2H status");

@@ -29,6 +29,7 @@ from typing import Sequence
 import numpy as np
 import torch
 
+from ..common.observability import nvtx_range
 from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
 from .completion import AggregateCompletion, LoadGateError, PostCompletion
@@ -66,7 +67,8 @@ class LayerwiseReadPlan:
             for li, layer in enumerate(self.layers):
                 if self._closed:
                     break
-                comp = store.get_paged(self.keys, self.block_table, layers=[layer], stream=self.io_stream)
+                with nvtx_range(f"tutti.layer_load|layer={layer}|chunks={len(self.keys)}"):
+                    comp = store.get_paged(self.keys, self.block_table, layers=[layer], stream=self.io_stream)
                 ev = torch.cuda.Event()
                 ev.record(self.io_stream)
                 with self._cv:
@@ -93,7 +95,8 @@ class LayerwiseReadPlan:
             if layer not in self._events:
                 raise LoadGateError(f"restore of layer {layer} failed: {self._error}")
             ev = self._events[layer]
-        torch.cuda.current_stream().wait_event(ev)
+        with nvtx_range(f"tutti.layer_wait|layer={layer}"):
+            torch.cuda.current_stream().wait_event(ev)
 
     def finish(self) -> None:
         """Host-wait for every layer; raises LoadGateError listing the failed chunks."""

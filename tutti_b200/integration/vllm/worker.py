@@ -23,6 +23,7 @@ from typing import Callable
 import numpy as np
 import torch
 
+from ...common.observability import HealthReporter
 from ...engine.completion import LoadGateError
 from ...engine.core import KVEngine
 from ...parallel.tp_consensus import ChunkFailure, TpFailureConsensus
@@ -64,6 +65,7 @@ class WorkerSide:
         self.consensus = consensus or TpFailureConsensus()
         self.failure_policy = failure_policy
         self.engine: KVEngine | None = None
+        self.health: HealthReporter | None = None
         self.layer_of: dict[str, int] = {}
         self._plan = None
         self._plan_loads: list[LoadSpec] = []
@@ -82,6 +84,10 @@ class WorkerSide:
     # -- loads ----------------------------------------------------------------
     def start_load_kv(self, meta: TuttiConnectorMetadata) -> None:
         self._meta = TuttiWorkerMetadata()
+        if self.engine is not None:
+            if self.health is None:
+                self.health = HealthReporter(self.engine.store)
+            self.health.maybe_log()
         sync = [l for l in meta.loads if not l.is_async]
         for spec in meta.loads:
             if spec.is_async:

@@ -29,6 +29,7 @@ import numpy as np
 import torch
 
 from .._native import core
+from ..common.observability import metrics, nvtx_range
 from ..models.kv_geometry import KVGeometry
 from .base import StoreIOError
 from .object_layout import DEFAULT_SEGMENT_FILE_SLOTS, DEFAULT_SEGMENT_HEADER_BYTES, ObjectLayout
@@ -68,8 +69,10 @@ def stored_geometry(g: KVGeometry, stored_format: str = "native") -> dict:
 class NativeCompletion:
     """Completion of one or more runtime IOs; ``wait`` raises StoreIOError on failure."""
 
-    def __init__(self, runtime, ios: list[int], on_success=None, on_failure=None, nbytes: int = 0):
+    def __init__(self, runtime, ios: list[int], on_success=None, on_failure=None, nbytes: int = 0,
+                 kind: str = "restore"):
         self._rt = runtime
+        self.kind = kind
         self._ios = list(ios)
         self._on_success = on_success
         self._on_failure = on_failure
@@ -102,6 +105,13 @@ class NativeCompletion:
                 failed.extend(r["failed_request_indices"])
                 kinds.add(r["failure_kind"])
         self._done = True
+        m = metrics()
+        m.add(f"{self.kind}_ops")
+        if failed:
+            m.add("failed_ops")
+            m.add("failed_requests", len(failed))
+        else:
+            m.add(f"{self.kind}_bytes", self.nbytes)
         if failed:
             if self._on_failure:
                 self._on_failure()
@@ -345,7 +355,7 @@ class TuttiKVStore:
         if stream is None and self.backend == "nvme-gpu":
             stream = torch.cuda.current_stream(self.device)
         ios, nbytes = self._submit_paged("write", placements, block_ids, np.arange(g.num_layers), stream, chunk_mems=cm)
-        comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
+        comp = NativeCompletion(self.runtime, ios, nbytes=nbytes, kind="store")
         self._track(comp)
         return comp
 
@@ -375,6 +385,7 @@ class TuttiKVStore:
                 if r["io"] is not None:
                     NativeCompletion(self.runtime, [r["io"]]).wait()
                 raise StoreIOError(f"{len(r['rejected'])} request(s) rejected: {reasons}", r["rejected"], "rejected")
+            metrics().add("submit_retries")
             if self._inflight:
                 self._inflight.popleft().wait()
             else:
@@ -393,7 +404,8 @@ class TuttiKVStore:
                 raise StoreIOError(f"chunk {bytes(k).hex()} is not committed", kind="not_found")
             uri, off, _slot, _gen = p
             placements.append((uri[len("file://"):], off))
-        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream)
+        with nvtx_range(f"tutti.restore|chunks={len(keys)}|layers={len(layers)}"):
+            ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream)
         comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
         self._track(comp)
         return comp
@@ -435,12 +447,14 @@ class TuttiKVStore:
             # The gather reads the pool: order it after work queued on the current stream.
             stream = torch.cuda.current_stream(self.device)
         try:
-            ios, nbytes = self._submit_paged("write", placements, block_ids[fresh], np.arange(g.num_layers), stream)
+            with nvtx_range(f"tutti.store|chunks={len(fresh)}"):
+                ios, nbytes = self._submit_paged("write", placements, block_ids[fresh], np.arange(g.num_layers),
+                                                 stream)
         except Exception:
             self.objects.abort(wkeys)
             raise
         comp = NativeCompletion(self.runtime, ios, on_success=lambda: self.objects.commit(wkeys),
-                                on_failure=lambda: self.objects.abort(wkeys), nbytes=nbytes)
+                                on_failure=lambda: self.objects.abort(wkeys), nbytes=nbytes, kind="store")
         self._track(comp)
         return comp
 
