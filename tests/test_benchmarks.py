@@ -6,7 +6,7 @@ from tutti_b200.benchmarks.serving_trace import FALLBACK_PEAKS, make_trace, pref
 
 def _args(**kw):
     base = dict(seed=0, distinct=512, zipf=1.1, min_prefix=8192, max_prefix=65536, length_scale=1.0,
-                requests=400, reuse=0.8)
+                requests=400, reuse=0.8, warm=16)
     base.update(kw)
     return argparse.Namespace(**base)
 

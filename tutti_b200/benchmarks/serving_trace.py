@@ -68,6 +68,8 @@ def parse(argv=None):
     p.add_argument("--restore", choices=["fanout", "local"], default="fanout")
     p.add_argument("--drives", type=int, default=0, help="0: one per rank")
     p.add_argument("--affine", default="", help="drive d belongs to GPU affine[d %% len]; default all ranks")
+    p.add_argument("--warm", type=int, default=16,
+                   help="persist the N most popular prefixes before the trace (a warm SSD cache)")
     p.add_argument("--mfu", type=float, default=0.5)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--root", default=os.environ.get("TUTTI_BENCH_ROOT", "/tmp/tutti_trace"))
@@ -89,6 +91,13 @@ def peaks() -> dict:
         return dict(FALLBACK_PEAKS, source="fallback")
 
 
+def prefix_lengths(args, chunk: int) -> np.ndarray:
+    """Token length of each distinct prefix (prefix id = Zipf popularity rank - 1)."""
+    rng = np.random.default_rng(args.seed + 7)
+    lo, hi = int(args.min_prefix * args.length_scale), int(args.max_prefix * args.length_scale)
+    return (rng.integers(lo, hi + 1, args.distinct) // chunk).clip(1) * chunk
+
+
 def make_trace(args, chunk: int) -> list[dict]:
     """Seeded request list: prefix id, prefix tokens (chunk multiple), whether it reuses a prefix."""
     rng = np.random.default_rng(args.seed)
@@ -96,7 +105,7 @@ def make_trace(args, chunk: int) -> list[dict]:
     zipf = ranks ** -args.zipf
     zipf /= zipf.sum()
     lo, hi = int(args.min_prefix * args.length_scale), int(args.max_prefix * args.length_scale)
-    lengths = (rng.integers(lo, hi + 1, args.distinct) // chunk).clip(1) * chunk
+    lengths = prefix_lengths(args, chunk)
     out, fresh = [], args.distinct
     for _ in range(args.requests):
         if rng.random() < args.reuse:
@@ -146,6 +155,9 @@ def main(argv=None) -> int:
     distinct_tokens = {}
     for r in trace:
         distinct_tokens[r["prefix"]] = r["tokens"]
+    warm = [{"prefix": pid, "tokens": int(t)} for pid, t in enumerate(prefix_lengths(args, g.chunk_tokens)[:args.warm])]
+    for r in warm:
+        distinct_tokens[r["prefix"]] = r["tokens"]
     chunks_total = sum(t // g.chunk_tokens for t in distinct_tokens.values())
     spf = 64
     cap = ((chunks_total + spf * drives - 1) // (spf * drives) + 1) * spf * drives
@@ -154,7 +166,8 @@ def main(argv=None) -> int:
                          rank=rank, rank_count=world, runtime_options=opts, segment_file_slots=spf,
                          namespace=b"trace")
     store.open()
-    max_blocks = max(r["tokens"] for r in trace) // g.block_size
+    store.layout.precreate_until(cap)  # materialise the segment files up front (untimed setup)
+    max_blocks = max(r["tokens"] for r in trace + warm) // g.block_size
     pool = torch.zeros(g.pool_shape(2 * max_blocks), dtype=g.dtype, device=dev)
     store.register_pool(pool)
     peers = PeerPools(pool, group=ctl)
@@ -172,6 +185,19 @@ def main(argv=None) -> int:
     gen = torch.Generator(device=dev).manual_seed(rank)
     digests: dict[bytes, torch.Tensor] = {}  # this rank's slice of every persisted chunk
     mismatches = 0
+    # warm cache: the most popular prefixes are already on SSD when the trace starts
+    for r in warm:
+        keys = chunk_keys_for_tokens(prefix_tokens(r["prefix"], r["tokens"]), g.chunk_tokens)
+        blocks = np.arange(len(keys) * g.blocks_per_chunk).reshape(len(keys), -1)
+        bidx = torch.from_numpy(blocks.reshape(-1)).to(dev)
+        pool[:, :, bidx] = torch.randn((g.num_layers, g.planes, bidx.numel()) + tuple(pool.shape[3:]), dtype=g.dtype,
+                                       device=dev, generator=gen)
+        store.put_paged(keys, blocks).wait()
+        dg = ops.kv_checksum(pool, bidx).cpu().reshape(len(keys), g.blocks_per_chunk, g.num_layers, g.planes)
+        for c, k in enumerate(keys):
+            digests[k] = dg[c]
+    dist.barrier(group=ctl)
+
     for i, req in enumerate(trace):
         n = req["tokens"]
         keys = chunk_keys_for_tokens(prefix_tokens(req["prefix"], n), g.chunk_tokens)
@@ -262,7 +288,7 @@ def main(argv=None) -> int:
                "model": g.fingerprint(), "requests": len(records),
                "prefix_tokens": [int(args.min_prefix * args.length_scale), int(args.max_prefix * args.length_scale)],
                "length_scale": args.length_scale, "reuse": args.reuse, "zipf": args.zipf,
-               "distinct": args.distinct, "hit_requests": len(hits),
+               "distinct": args.distinct, "warm_prefixes": args.warm, "hit_requests": len(hits),
                "restore_GBps": round(rest_bytes / rest_s / 1e9, 3) if rest_s else None,
                "restore_ms_p50": round(float(np.median([r["restore_ms"] for r in hits])), 3) if hits else None,
                "write_GBps": round(sum(world * (r["tokens"] - r["hit_tokens"]) // g.block_size * g.num_layers
