@@ -206,3 +206,57 @@ def test_subsector_index_pages_pack_into_aligned_commands(tmp_path):
         assert torch.equal(pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()], ref)
     finally:
         st.close()
+
+
+@pytest.mark.parametrize("consumer_drain", [False, True])
+def test_split_completion_restores_exactly(tmp_path, consumer_drain):
+    # submit-phase launch queues the reads and exits; the drain runs on the
+    # consumer stream (enqueue_wait) or, without one, from the host fallback
+    st = make(tmp_path, drives=2, async_completion=True, slots_per_lease=8)
+    try:
+        nb = 256
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(10 * 64)), 64, namespace=b"split")
+        rng = np.random.default_rng(4)
+        src = rng.permutation(nb)[:40].reshape(10, 4)
+        st.put_paged(keys, src).wait()
+        ref = pool[:, :, torch.from_numpy(src.reshape(-1)).cuda()].clone()
+        for it in range(2):
+            dst = rng.permutation(nb)[:40].reshape(10, 4)
+            pool.zero_()
+            io_stream = torch.cuda.Stream()
+            comp = st.get_paged(keys, dst, stream=io_stream)
+            didx = torch.from_numpy(dst.reshape(-1)).cuda()
+            if consumer_drain:
+                consumer = torch.cuda.Stream()
+                comp.enqueue_wait(consumer)
+                with torch.cuda.stream(consumer):
+                    out = pool[:, :, didx].clone()
+                consumer.synchronize()
+                comp.wait()
+            else:
+                comp.wait()
+                out = pool[:, :, didx]
+            assert torch.equal(out, ref), it
+    finally:
+        st.close()
+
+
+def test_split_completion_deadline_runs_from_submission(tmp_path):
+    st = make(tmp_path, async_completion=True, timeout_ms=500)
+    try:
+        nb = 64
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(2 * 64)), 64)
+        st.put_paged(keys, np.arange(8).reshape(2, 4)).wait()
+        ref = pool[:, :, 0:8].clone()
+        st.runtime.inject(0, "drop_completion", 1)
+        with pytest.raises(StoreIOError) as ei:
+            st.get_paged(keys, (np.arange(8) + 8).reshape(2, 4)).wait()
+        assert "cq_timeout" in ei.value.kind
+        st.get_paged(keys, (np.arange(8) + 16).reshape(2, 4)).wait()
+        assert torch.equal(pool[:, :, 16:24], ref)
+    finally:
+        st.close()

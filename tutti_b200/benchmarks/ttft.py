@@ -47,7 +47,8 @@ def run(args) -> dict:
     store = TuttiKVStore(root, g, capacity_chunks=spf * args.drives, mounts=mounts, device=args.device,
                          segment_file_slots=spf, namespace=b"ttft",
                          runtime_options={"controller_threads": args.controller_threads, "leases": 128,
-                                          "max_ctas_per_op": args.ctas_per_layer, "slots_per_lease": 8})
+                                          "max_ctas_per_op": args.ctas_per_layer, "slots_per_lease": 8,
+                                          "async_completion": bool(args.async_completion)})
     store.open()
     model = LlamaModel(cfg, dev)
     pool = torch.zeros(g.pool_shape(nb), dtype=g.dtype, device=dev)
@@ -121,6 +122,8 @@ def main(argv=None):
     p.add_argument("--controller-threads", type=int, default=3)
     p.add_argument("--ctas-per-layer", type=int, default=32)
     p.add_argument("--window", type=int, default=4)
+    p.add_argument("--async-completion", action="store_true",
+                   help="split submit/drain launches: each layer's drain runs on the compute stream")
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--device", type=int, default=0)

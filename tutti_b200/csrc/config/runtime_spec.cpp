@@ -125,7 +125,7 @@ Status parse_datapath(const Node& n, const std::string& p, DataPathSpec& d) {
     if (const Node* c = n.get("config")) {
         const std::string cp = p + ".config";
         TUTTI_RETURN_IF_ERROR(only_fields(*c, cp, {"leases", "max_ctas_per_op", "slots_per_lease", "slot_bytes",
-                                                   "timeout_ms", "threads", "direct_io"}));
+                                                   "timeout_ms", "threads", "direct_io", "async_completion"}));
         TUTTI_RETURN_IF_ERROR(get_uint(*c, "leases", cp, d.leases));
         TUTTI_RETURN_IF_ERROR(get_uint(*c, "max_ctas_per_op", cp, d.max_ctas_per_op));
         TUTTI_RETURN_IF_ERROR(get_uint(*c, "slots_per_lease", cp, d.slots_per_lease));
@@ -133,6 +133,7 @@ Status parse_datapath(const Node& n, const std::string& p, DataPathSpec& d) {
         TUTTI_RETURN_IF_ERROR(get_uint(*c, "timeout_ms", cp, d.timeout_ms));
         TUTTI_RETURN_IF_ERROR(get_uint(*c, "threads", cp, d.threads));
         TUTTI_RETURN_IF_ERROR(get_bool(*c, "direct_io", cp, d.direct_io));
+        TUTTI_RETURN_IF_ERROR(get_bool(*c, "async_completion", cp, d.async_completion));
     }
     return Status::Ok();
 }

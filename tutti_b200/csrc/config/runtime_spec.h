@@ -59,6 +59,7 @@ struct DataPathSpec {
     std::uint32_t leases = 64;
     std::uint32_t max_ctas_per_op = 64;
     std::uint32_t slots_per_lease = 8;
+    bool async_completion = false;  // nvme-gpu: split submit / drain launches for reads
     std::uint32_t slot_bytes = 1u << 20;
     std::uint64_t timeout_ms = 5000;
     std::uint32_t threads = 8;  // posix

@@ -254,12 +254,15 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
     if (!initialized_) return Status::Ok();
     DeviceGuard guard(cfg_.accel_id);
     for (auto& kv : ops_)
+        if (kv.second->drain_pending) launch_drain(*kv.second, kv.second->stream);
+    for (auto& kv : ops_)
         if (kv.second->arena && kv.second->arena->event) cudaEventSynchronize(kv.second->arena->event);
     for (auto& kv : ops_)
         if (kv.second->arena) arena_pool_.push_back(std::move(kv.second->arena));
     ops_.clear();
     for (auto& a : arena_pool_) {
         if (a->event) cudaEventDestroy(a->event);
+        if (a->submitted) cudaEventDestroy(a->submitted);
         if (a->host) cudaFreeHost(a->host);
         if (a->dev) cudaFree(a->dev);
     }
@@ -412,7 +415,9 @@ Result<std::unique_ptr<GpuNvmeDataPath::Arena>> GpuNvmeDataPath::take_arena(std:
         return R::Failure(s);
     }
     s = cuda_status(cudaEventCreateWithFlags(&a->event, cudaEventDisableTiming), "cudaEventCreate");
+    if (s.ok()) s = cuda_status(cudaEventCreateWithFlags(&a->submitted, cudaEventDisableTiming), "cudaEventCreate");
     if (!s.ok()) {
+        if (a->event) cudaEventDestroy(a->event);
         cudaFreeHost(a->host);
         cudaFree(a->dev);
         return R::Failure(s);
@@ -587,7 +592,12 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     const std::size_t off_status = align_up(off_cursor + 16, 256);
     const std::size_t off_timing = align_up(off_status + n_cmds * sizeof(std::uint32_t), 256);
     const bool timing = cfg_.timing;
-    const std::size_t total = off_timing + (timing ? n_cmds * 4 * sizeof(std::uint64_t) : 0);
+    const std::size_t copy_end = off_timing + (timing ? n_cmds * 4 * sizeof(std::uint64_t) : 0);
+    // Split completion when every command is a read and the leased slots hold them all.
+    bool split = cfg_.async_completion && n_cmds <= std::uint64_t(take) * cfg_.slots_per_lease;
+    for (std::size_t k = 0; split && k < cmds.size(); ++k) split = cmds[k].opcode == nvme::kOpRead;
+    const std::size_t off_carry = align_up(copy_end, 256);
+    const std::size_t total = split ? off_carry + take * sizeof(io::LeaseCarry) : copy_end;
     auto ar = take_arena(total);
     if (!ar.ok()) return reject_all(ar.status());
     std::unique_ptr<Arena> arena = std::move(ar).value();
@@ -621,6 +631,8 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     kp.slots_per_lease = cfg_.slots_per_lease;
     kp.timeout_ns = cfg_.timeout_ns;
     kp.timing = timing ? reinterpret_cast<std::uint64_t*>(d + off_timing) : nullptr;
+    kp.carry = split ? reinterpret_cast<io::LeaseCarry*>(d + off_carry) : nullptr;
+    kp.phase = split ? io::kPhaseSubmit : io::kPhaseFull;
 
     cudaStream_t s = ctx.stream;
     const bool nvtx = nvtx_enabled();
@@ -633,10 +645,15 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     Status cs = cuda_status(cudaMemcpyAsync(d, h, off_timing, cudaMemcpyHostToDevice, s), "H2D commands");
     if (cs.ok()) cs = cuda_status(io::launch_nvme_io(kp, take, s), "io kernel launch");
     if (nvtx) nvtxRangePop();
-    if (cs.ok())
-        cs = cuda_status(cudaMemcpyAsync(h + off_status, d + off_status, total - off_status, cudaMemcpyDeviceToHost, s),
-                         "D2H status");
-    if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->event, s), "event record");
+    if (split) {
+        if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->submitted, s), "event record");
+    } else {
+        if (cs.ok())
+            cs = cuda_status(
+                cudaMemcpyAsync(h + off_status, d + off_status, copy_end - off_status, cudaMemcpyDeviceToHost, s),
+                "D2H status");
+        if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->event, s), "event record");
+    }
     if (!cs.ok()) {
         // Nothing irreversible is known to have happened if the launch failed;
         // report every request rejected and return the leases.
@@ -646,6 +663,15 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         return reject_all(cs);
     }
     op->arena = std::move(arena);
+    if (split) {
+        op->drain_pending = true;
+        op->kp = kp;
+        op->kp.phase = io::kPhaseDrain;
+        op->ctas = take;
+        op->copy_back_bytes = copy_end - off_status;
+        op->stream = s;
+        op->submitted_at = std::chrono::steady_clock::now();
+    }
     op->n_cmds = n_cmds;
     op->status_off = off_status;
     op->timing_off = off_timing;
@@ -745,6 +771,23 @@ void GpuNvmeDataPath::finish_op(OpRec& op) {
     }
 }
 
+Status GpuNvmeDataPath::launch_drain(OpRec& op, cudaStream_t stream) {
+    // Caller holds mu_. Orders the drain after the submit-phase kernel, then
+    // copies the statuses back and marks the op's completion event.
+    DeviceGuard guard(cfg_.accel_id);
+    char* h = op.arena->host;
+    char* d = op.arena->dev;
+    Status cs = cuda_status(cudaStreamWaitEvent(stream, op.arena->submitted, 0), "stream wait");
+    if (cs.ok()) cs = cuda_status(io::launch_nvme_io(op.kp, op.ctas, stream), "drain launch");
+    if (cs.ok())
+        cs = cuda_status(cudaMemcpyAsync(h + op.status_off, d + op.status_off, op.copy_back_bytes,
+                                         cudaMemcpyDeviceToHost, stream),
+                         "D2H status");
+    if (cs.ok()) cs = cuda_status(cudaEventRecord(op.arena->event, stream), "event record");
+    op.drain_pending = false;
+    return cs;
+}
+
 Result<ProgressResult> GpuNvmeDataPath::progress(ProgressBudget budget) {
     std::lock_guard<std::mutex> g(mu_);
     ProgressResult pr;
@@ -757,6 +800,23 @@ Result<ProgressResult> GpuNvmeDataPath::progress(ProgressBudget budget) {
             break;
         }
         ++pr.work_units_consumed;
+        if (op.drain_pending) {
+            // Nobody enqueued the drain on a consumer stream in time: launch it here.
+            const auto waited = std::chrono::steady_clock::now() - op.submitted_at;
+            if (waited >= std::chrono::microseconds(cfg_.async_fallback_us)) {
+                Status ds = launch_drain(op, op.stream);
+                if (!ds.ok()) {
+                    op.state = IoState::FAILED;
+                    op.status = ds;
+                    op.detail.failure_kind = IoFailureKind::UNKNOWN;
+                    op.detail.failure_scope = IoFailureScope::WHOLE_OPERATION;
+                    ++pr.operations_terminal;
+                    continue;  // leases stay held: queues hold submitted commands
+                }
+            }
+            pr.more_work_likely = true;
+            continue;
+        }
         cudaError_t e = cudaEventQuery(op.arena->event);
         if (e == cudaErrorNotReady) {
             pr.more_work_likely = true;
@@ -807,6 +867,11 @@ Status GpuNvmeDataPath::enqueue_wait(const DataPathOp* ops, std::size_t count, c
         auto it = ops_.find(ops[i].token);
         if (it == ops_.end() || it->second->generation != ops[i].generation) return {StatusCode::NOT_FOUND, "unknown op"};
         if (!it->second->arena) continue;  // already terminal and released
+        if (it->second->drain_pending) {
+            // Split completion: the drain runs on the consumer's stream, right where it is needed.
+            TUTTI_RETURN_IF_ERROR(launch_drain(*it->second, stream));
+            continue;
+        }
         TUTTI_RETURN_IF_ERROR(cuda_status(cudaStreamWaitEvent(stream, it->second->arena->event, 0), "stream wait"));
     }
     return Status::Ok();

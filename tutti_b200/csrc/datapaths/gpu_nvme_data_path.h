@@ -17,6 +17,7 @@
 //   enqueue_wait -> cudaStreamWaitEvent on a consumer stream
 
 #include <cstdint>
+#include <chrono>
 #include <memory>
 #include <mutex>
 #include <unordered_map>
@@ -41,6 +42,13 @@ struct GpuNvmeConfig {
     std::uint32_t max_targets = 1u << 20;
     std::uint32_t max_pieces_per_cmd = 256;
     bool timing = false;                  // per-command %globaltimer stamps
+    // Split completion for reads: submit() launches only a one-warp-per-lease
+    // kernel that queues the SQEs and exits; the waiting, data movement and
+    // deadlines run in a drain launch that enqueue_wait() puts on the consumer's
+    // stream, or that progress() launches itself once `async_fallback_us` have
+    // passed without one (a host fallback). Off: one kernel does everything.
+    bool async_completion = false;
+    std::uint32_t async_fallback_us = 1000;
 };
 
 // One row of the device table: a controller and the identity string the
@@ -121,7 +129,8 @@ private:
         std::size_t capacity = 0;    // bytes
         char* host = nullptr;        // pinned
         char* dev = nullptr;
-        cudaEvent_t event = nullptr;
+        cudaEvent_t event = nullptr;      // after the (drain) kernel and the status copy-back
+        cudaEvent_t submitted = nullptr;  // split completion: after the submit-phase kernel
     };
     struct OpRec {
         std::uint64_t generation = 0;
@@ -140,12 +149,20 @@ private:
         IoCompletionDetail detail;
         std::uint64_t bytes = 0;
         bool timing = false;
+        // split completion: the drain launch still to be issued
+        bool drain_pending = false;
+        io::IoKernelParams kp{};
+        std::uint32_t ctas = 0;
+        std::size_t copy_back_bytes = 0;
+        cudaStream_t stream = nullptr;
+        std::chrono::steady_clock::time_point submitted_at{};
     };
 
     Status init_device_side();
     Result<std::unique_ptr<Arena>> take_arena(std::size_t bytes);
     void return_arena(std::unique_ptr<Arena> a);
     void finish_op(OpRec& op);
+    Status launch_drain(OpRec& op, cudaStream_t stream);
     Status reset_dirty_queues(const std::vector<std::uint32_t>& leases);
 
     GpuNvmeConfig cfg_;

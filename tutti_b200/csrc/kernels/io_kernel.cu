@@ -332,9 +332,84 @@ __device__ void push_ready(Shared& sh, int s, int slots) {
     sh.rq_tail = sh.rq_tail + 1;
 }
 
+// Resolves command `ci` into slot `s` and writes its SQEs (one per device /
+// extent / MDTS piece) into this lease's queues; the slot becomes INFLIGHT.
+// Returns false (and the status in *err) when the command cannot be resolved.
+__device__ bool issue_cmd(const IoKernelParams& p, Shared& sh, int ci, int s, std::uint32_t lease,
+                          unsigned long long now, std::uint32_t* touched, std::uint32_t* err) {
+    const std::uint64_t lease_slot0 = static_cast<std::uint64_t>(lease) * p.slots_per_lease;
+    const IoCommand c = p.cmds[ci];
+    SubCmd sub[kMaxSub];
+    const int n = resolve_cmd(p, c, sub, err);
+    if (n == 0) return false;
+    const std::uint64_t slot_index = lease_slot0 + s;
+    const std::uint64_t slot_iova = p.staging_iova + slot_index * p.slot_bytes;
+    const std::uint64_t list_iova = p.prp_iova + slot_index * nvme::kMemoryPageBytes;
+    for (int k = 0; k < n; ++k) {
+        const std::uint32_t dv = sub[k].device;
+        const DevDevice& d = p.devices[dv];
+        const nvme::QueuePairView& q = d.queues[lease];
+        const std::uint64_t prp1 = slot_iova + sub[k].off;
+        const std::uint32_t page0 = sub[k].off >> 12;
+        const std::uint32_t extra = nvme::prp_extra_pages(prp1 & 4095u, sub[k].bytes);
+        std::uint64_t prp2 = 0;
+        if (extra == 1)
+            prp2 = slot_iova + (static_cast<std::uint64_t>(page0 + 1) << 12);
+        else if (extra > 1)
+            prp2 = list_iova + 8ull * (page0 + 1);
+        nvme::Sqe e;
+        nvme::build_rw_sqe(e, static_cast<std::uint8_t>(c.opcode), static_cast<std::uint16_t>(s * kMaxSub + k), d.nsid,
+                           sub[k].lba, sub[k].bytes >> d.lba_shift, prp1, prp2);
+        uint4* dst = reinterpret_cast<uint4*>(q.sq + sh.cur[dv].sq_tail);
+        const uint4* src = reinterpret_cast<const uint4*>(&e);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) dst[w] = src[w];
+        sh.cur[dv].sq_tail = (sh.cur[dv].sq_tail + 1) % q.depth;
+        sh.inflight_dev[dv] += 1;
+        *touched |= 1u << dv;
+    }
+    sh.pending[s] = n;
+    sh.t0[s] = now;
+    sh.state[s] = S_INFLIGHT;
+    if (p.timing) p.timing[4ull * ci + 1] = now;
+    return true;
+}
+
+// SQEs before the tail doorbells (system scope: the controller is a peer).
+__device__ void ring_doorbells(const IoKernelParams& p, Shared& sh, std::uint32_t lease, std::uint32_t touched) {
+    if (!touched) return;
+    __threadfence_system();
+    for (std::uint32_t d = 0; d < p.n_devices; ++d)
+        if (touched & (1u << d)) st_release_sys(p.devices[d].queues[lease].sq_doorbell, sh.cur[d].sq_tail);
+}
+
+// Split completion, submit phase: fill this lease's slots with read commands,
+// ring the doorbells once and return without waiting.
+__device__ void engine_submit_phase(const IoKernelParams& p, Shared& sh, std::uint32_t lease, int S) {
+    const unsigned long long now = globaltimer_ns();
+    std::uint32_t touched = 0;
+    bool exhausted = false;
+    for (int s = 0; s < S && !exhausted; ++s) {
+        for (;;) {
+            const std::uint32_t ci = atomicAdd(p.cursor, 1u);
+            if (ci >= p.n_cmds) {
+                exhausted = true;
+                break;
+            }
+            if (p.timing) p.timing[4ull * ci + 0] = now;
+            sh.cmd[s] = static_cast<int>(ci);
+            sh.status[s] = 0;
+            std::uint32_t err = 0;
+            if (issue_cmd(p, sh, static_cast<int>(ci), s, lease, now, &touched, &err)) break;
+            p.cmd_status[ci] = err;  // unresolvable: report it and claim another for this slot
+            sh.cmd[s] = -1;
+        }
+    }
+    ring_doorbells(p, sh, lease, touched);
+}
+
 // Engine: everything that touches the queues. Runs on warp 0, lane 0.
 __device__ void engine_loop(const IoKernelParams& p, Shared& sh, std::uint32_t lease, int S) {
-    const std::uint64_t lease_slot0 = static_cast<std::uint64_t>(lease) * p.slots_per_lease;
     bool exhausted = false;
     unsigned idle = 0;
     unsigned long long last_progress = globaltimer_ns();
@@ -364,54 +439,17 @@ __device__ void engine_loop(const IoKernelParams& p, Shared& sh, std::uint32_t l
             }
             if (st != S_SUBMIT) continue;
             const int ci = sh.cmd[s];
-            const IoCommand c = p.cmds[ci];
-            SubCmd sub[kMaxSub];
             std::uint32_t err = 0;
-            const int n = resolve_cmd(p, c, sub, &err);
-            if (n == 0) {
+            if (!issue_cmd(p, sh, ci, s, lease, now, &touched, &err)) {
                 p.cmd_status[ci] = err;
                 sh.state[s] = S_FREE;
                 progressed = true;
                 --s;  // refill this slot
                 continue;
             }
-            const std::uint64_t slot_index = lease_slot0 + s;
-            const std::uint64_t slot_iova = p.staging_iova + slot_index * p.slot_bytes;
-            const std::uint64_t list_iova = p.prp_iova + slot_index * nvme::kMemoryPageBytes;
-            for (int k = 0; k < n; ++k) {
-                const std::uint32_t dv = sub[k].device;
-                const DevDevice& d = p.devices[dv];
-                const nvme::QueuePairView& q = d.queues[lease];
-                const std::uint64_t prp1 = slot_iova + sub[k].off;
-                const std::uint32_t page0 = sub[k].off >> 12;
-                const std::uint32_t extra = nvme::prp_extra_pages(prp1 & 4095u, sub[k].bytes);
-                std::uint64_t prp2 = 0;
-                if (extra == 1)
-                    prp2 = slot_iova + (static_cast<std::uint64_t>(page0 + 1) << 12);
-                else if (extra > 1)
-                    prp2 = list_iova + 8ull * (page0 + 1);
-                nvme::Sqe e;
-                nvme::build_rw_sqe(e, static_cast<std::uint8_t>(c.opcode), static_cast<std::uint16_t>(s * kMaxSub + k),
-                                   d.nsid, sub[k].lba, sub[k].bytes >> d.lba_shift, prp1, prp2);
-                uint4* dst = reinterpret_cast<uint4*>(q.sq + sh.cur[dv].sq_tail);
-                const uint4* src = reinterpret_cast<const uint4*>(&e);
-#pragma unroll
-                for (int w = 0; w < 4; ++w) dst[w] = src[w];
-                sh.cur[dv].sq_tail = (sh.cur[dv].sq_tail + 1) % q.depth;
-                sh.inflight_dev[dv] += 1;
-                touched |= 1u << dv;
-            }
-            sh.pending[s] = n;
-            sh.t0[s] = now;
-            sh.state[s] = S_INFLIGHT;
             progressed = true;
-            if (p.timing) p.timing[4ull * ci + 1] = now;
         }
-        if (touched) {
-            __threadfence_system();
-            for (std::uint32_t d = 0; d < p.n_devices; ++d)
-                if (touched & (1u << d)) st_release_sys(p.devices[d].queues[lease].sq_doorbell, sh.cur[d].sq_tail);
-        }
+        ring_doorbells(p, sh, lease, touched);
         // (b) drain completions
         for (std::uint32_t d = 0; d < p.n_devices; ++d) {
             if (sh.inflight_dev[d] == 0) continue;
@@ -556,7 +594,41 @@ __global__ void __launch_bounds__(kIoThreads, 1) nvme_io_kernel(const IoKernelPa
         sh.done = 0;
         sh.error = 0;
     }
+    if (tid == 0 && p.phase == kPhaseDrain) {
+        const LeaseCarry& k = p.carry[blockIdx.x];
+        for (int s = 0; s < S; ++s) {
+            if (k.cmd[s] < 0) continue;
+            sh.cmd[s] = k.cmd[s];
+            sh.pending[s] = k.pending[s];
+            sh.status[s] = k.status[s];
+            sh.t0[s] = k.t0[s];
+            sh.state[s] = S_INFLIGHT;
+        }
+        for (std::uint32_t d = 0; d < p.n_devices; ++d) sh.inflight_dev[d] = k.inflight_dev[d];
+    }
     __syncthreads();
+    if (p.phase == kPhaseSubmit) {
+        if (tid == 0) {
+            engine_submit_phase(p, sh, lease, S);
+            LeaseCarry& k = p.carry[blockIdx.x];
+            for (int s = 0; s < kMaxSlots; ++s) {
+                const bool used = s < S && sh.state[s] == S_INFLIGHT;
+                k.cmd[s] = used ? sh.cmd[s] : -1;
+                k.pending[s] = used ? sh.pending[s] : 0;
+                k.status[s] = 0;
+                k.t0[s] = used ? sh.t0[s] : 0;
+            }
+            for (std::uint32_t d = 0; d < static_cast<std::uint32_t>(kMaxDevices); ++d)
+                k.inflight_dev[d] = d < p.n_devices ? sh.inflight_dev[d] : 0;
+            // the queues stay owned by the commands in flight until the drain phase
+            for (std::uint32_t d = 0; d < p.n_devices; ++d) {
+                QueueCursor c = sh.cur[d];
+                c.dirty = 0;
+                p.devices[d].cursors[lease] = c;
+            }
+        }
+        return;
+    }
     if (warp == 0) {
         if (lane == 0) engine_loop(p, sh, lease, S);
     } else {
@@ -582,7 +654,8 @@ __global__ void __launch_bounds__(kIoThreads, 1) nvme_io_kernel(const IoKernelPa
 
 cudaError_t launch_nvme_io(const IoKernelParams& p, std::uint32_t n_leases, cudaStream_t stream) {
     if (n_leases == 0 || p.n_cmds == 0) return cudaSuccess;
-    nvme_io_kernel<<<n_leases, kIoThreads, 0, stream>>>(p);
+    if (p.phase != kPhaseFull && !p.carry) return cudaErrorInvalidValue;
+    nvme_io_kernel<<<n_leases, p.phase == kPhaseSubmit ? 32 : kIoThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -102,6 +102,21 @@ enum : std::uint32_t {
     kCmdBadDevice = 5u << 16,
 };
 
+// Split completion: a submit-phase launch (one warp per lease) claims commands
+// into its slots, writes their SQEs, rings the doorbells and exits; a later
+// drain-phase launch of full CTAs on the same leases takes over the slots from
+// this hand-over record, polls the CQs, moves the data and enforces the
+// deadlines (which run from submission). Reads only.
+enum IoPhase : std::uint32_t { kPhaseFull = 0, kPhaseSubmit = 1, kPhaseDrain = 2 };
+
+struct LeaseCarry {  // one per CTA of a split launch
+    int cmd[kMaxSlots];                // -1: slot unused
+    std::uint32_t pending[kMaxSlots];  // sub-commands not yet completed
+    std::uint32_t status[kMaxSlots];
+    unsigned long long t0[kMaxSlots];  // %globaltimer at submission
+    std::uint32_t inflight_dev[kMaxDevices];
+};
+
 struct IoKernelParams {
     const IoCommand* cmds;
     const IoPiece* pieces;
@@ -119,9 +134,12 @@ struct IoKernelParams {
     std::uint32_t slots_per_lease;
     std::uint64_t timeout_ns;     // per command, from submission
     std::uint64_t* timing;        // optional: 4 %globaltimer stamps per command
+    LeaseCarry* carry;            // split completion: gridDim.x records (else unused)
+    std::uint32_t phase;          // IoPhase
 };
 
-// Launches the fused io kernel on `stream` with one CTA per lease.
+// Launches the fused io kernel on `stream` with one CTA per lease (one warp
+// per lease for kPhaseSubmit).
 cudaError_t launch_nvme_io(const IoKernelParams& p, std::uint32_t n_leases, cudaStream_t stream);
 
 }  // namespace io

@@ -10,6 +10,7 @@
 
 #include <chrono>
 #include <cstdlib>
+#include <cstring>
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -510,6 +511,13 @@ PYBIND11_MODULE(_core, m) {
             if (opts.contains("slot_bytes")) o.gpu.slot_bytes = opts["slot_bytes"].cast<std::uint32_t>();
             if (opts.contains("timeout_ms")) o.gpu.timeout_ns = opts["timeout_ms"].cast<std::uint64_t>() * 1000000ull;
             if (opts.contains("timing")) o.gpu.timing = opts["timing"].cast<bool>();
+            {
+                const char* env = std::getenv("TUTTI_ASYNC_COMPLETION");
+                o.gpu.async_completion = env && *env && std::strcmp(env, "0") != 0;
+            }
+            if (opts.contains("async_completion")) o.gpu.async_completion = opts["async_completion"].cast<bool>();
+            if (opts.contains("async_fallback_us"))
+                o.gpu.async_fallback_us = opts["async_fallback_us"].cast<std::uint32_t>();
             if (opts.contains("mapping")) o.mapping = opts["mapping"].cast<std::string>();
             if (opts.contains("raid0_md")) o.raid0_md = opts["raid0_md"].cast<std::string>();
             if (opts.contains("sysfs_root")) o.sysfs_root = opts["sysfs_root"].cast<std::string>();

@@ -109,6 +109,7 @@ Result<std::unique_ptr<TuttiRuntime>> TuttiRuntime::create(const TuttiRuntimeSpe
         for (auto& r : rows) g.leases = std::min(g.leases, std::max<std::uint32_t>(r.queues, 1));
         g.max_ctas_per_op = std::min(ds.max_ctas_per_op, g.leases);
         g.slots_per_lease = ds.slots_per_lease;
+        g.async_completion = ds.async_completion;
         g.slot_bytes = ds.slot_bytes;
         g.timeout_ns = ds.timeout_ms * 1000000ull;
         rt->gpu_path = std::make_shared<GpuNvmeDataPath>(g, devs);

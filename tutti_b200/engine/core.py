@@ -50,6 +50,7 @@ class LayerwiseReadPlan:
         self.io_stream = io_stream
         self.window = max(1, window)
         self._events: dict[int, torch.cuda.Event] = {}
+        self._comp_of: dict[int, object] = {}
         self._comps: list = []
         self._cv = threading.Condition()
         self._error: BaseException | None = None
@@ -73,6 +74,7 @@ class LayerwiseReadPlan:
                 ev.record(self.io_stream)
                 with self._cv:
                     self._comps.append(comp)
+                    self._comp_of[layer] = comp
                     self._events[layer] = ev
                     self._cv.notify_all()
                 # bound the layers in flight (queue leases are shared)
@@ -95,8 +97,14 @@ class LayerwiseReadPlan:
             if layer not in self._events:
                 raise LoadGateError(f"restore of layer {layer} failed: {self._error}")
             ev = self._events[layer]
+            comp = self._comp_of.get(layer)
         with nvtx_range(f"tutti.layer_wait|layer={layer}"):
-            torch.cuda.current_stream().wait_event(ev)
+            if comp is not None and hasattr(comp, "enqueue_wait"):
+                # device-side wait on the restore itself; with split completion this
+                # launches the drain here, on the consumer's stream
+                comp.enqueue_wait(torch.cuda.current_stream())
+            else:
+                torch.cuda.current_stream().wait_event(ev)
 
     def finish(self) -> None:
         """Host-wait for every layer; raises LoadGateError listing the failed chunks."""

@@ -21,6 +21,7 @@ layerwise_direct.py:45-181 (block table -> page requests).
 from __future__ import annotations
 
 import collections
+import threading
 import time
 from pathlib import Path
 from typing import Sequence
@@ -79,6 +80,9 @@ class NativeCompletion:
         self._done = False
         self._results: list[dict] = []
         self.nbytes = nbytes
+        # enqueue_wait may race a host wait on another thread (e.g. a feeder's
+        # window bound): handles are released, and _done set, only under this lock
+        self._mu = threading.Lock()
 
     def query(self) -> bool:
         if self._done:
@@ -88,23 +92,33 @@ class NativeCompletion:
     def enqueue_wait(self, stream: torch.cuda.Stream | None = None) -> None:
         """Order ``stream`` after this batch's io kernels (no host wait)."""
         s = stream or torch.cuda.current_stream()
-        self._rt.enqueue_wait(self._ios, s.cuda_stream)
+        with self._mu:
+            if self._done:
+                return  # host-waited: the data is in place
+            self._rt.enqueue_wait(self._ios, s.cuda_stream)
 
     def wait(self, timeout_ms: int = 600_000) -> None:
         if self._done:
             return
         failed: list[int] = []
         kinds = set()
+        results = []
         for io in self._ios:
             r = self._rt.wait(io, timeout_ms)
             if r is None:
                 raise StoreIOError(f"io {io} still in flight after {timeout_ms} ms", kind="timeout")
-            self._rt.release_io(io)
+            results.append(r)
+        with self._mu:
+            if self._done:
+                return
+            for io in self._ios:
+                self._rt.release_io(io)
+            self._done = True
+        for r in results:
             self._results.append(r)
             if not r["ok"]:
                 failed.extend(r["failed_request_indices"])
                 kinds.add(r["failure_kind"])
-        self._done = True
         m = metrics()
         m.add(f"{self.kind}_ops")
         if failed:
