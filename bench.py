@@ -194,7 +194,9 @@ def main():
     shutil.rmtree(root, ignore_errors=True)
     mounts = [os.path.join(root, f"nvme{d}") for d in range(args.drives)]
     ncpu = os.cpu_count() or 8
-    threads = args.controller_threads or max(2, min(8, (ncpu // max(1, world) - 2) // max(1, args.drives)))
+    # 3 workers per emulated drive measured best at 1 and 4 GPUs (16 and 32 host cores);
+    # fewer when the box has under two cores per worker
+    threads = args.controller_threads or max(1, min(3, (2 * ncpu // max(1, world)) // max(1, args.drives)))
     opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": args.leases,
             "max_ctas_per_op": args.ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20,
             "queue_depth": 256, "mdts_bytes": 1 << 20, "timing": bool(args.timing),

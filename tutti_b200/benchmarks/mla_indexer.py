@@ -91,7 +91,7 @@ def main(argv=None) -> int:
     dev = torch.device("cuda", 0)
     shutil.rmtree(args.root, ignore_errors=True)
     ncpu = os.cpu_count() or 8
-    threads = max(2, min(8, (ncpu - 2) // max(1, args.drives)))
+    threads = max(1, min(3, (2 * ncpu) // max(1, args.drives)))
     opts = {"controller_threads": threads, "leases": args.leases, "max_ctas_per_op": args.ctas,
             "slots_per_lease": 8, "slot_bytes": 1 << 20, "queue_depth": 256, "mdts_bytes": 1 << 20}
     ob = open_batch_vs_serial(args.root, args.files, opts)

@@ -149,7 +149,7 @@ def main(argv=None) -> int:
         shutil.rmtree(args.root, ignore_errors=True)
     dist.barrier(group=ctl)
     ncpu = os.cpu_count() or 8
-    threads = max(2, min(8, (ncpu // world - 2) // max(1, drives)))
+    threads = max(1, min(3, (2 * ncpu // world) // max(1, drives)))
     opts = {"controller_threads": threads, "leases": args.leases, "max_ctas_per_op": args.ctas,
             "slots_per_lease": 8, "slot_bytes": 1 << 20, "queue_depth": 256, "mdts_bytes": 1 << 20}
     distinct_tokens = {}
