@@ -260,3 +260,26 @@ def test_split_completion_deadline_runs_from_submission(tmp_path):
         assert torch.equal(pool[:, :, 16:24], ref)
     finally:
         st.close()
+
+
+def test_restore_on_a_green_context_io_stream(tmp_path):
+    # io kernels on a stream confined to a 16-SM partition of the GPU
+    from tutti_b200.parallel.green_context import GreenIoStream
+
+    g = GreenIoStream(16, 0)
+    st = make(tmp_path, max_ctas_per_op=8)
+    try:
+        assert 16 <= g.sms < torch.cuda.get_device_properties(0).multi_processor_count
+        nb = 64
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(4 * 64)), 64, namespace=b"green")
+        st.put_paged(keys, np.arange(16).reshape(4, 4)).wait()
+        ref = pool[:, :, 0:16].clone()
+        comp = st.get_paged(keys, (np.arange(16) + 32).reshape(4, 4), stream=g.stream)
+        comp.wait()
+        g.stream.synchronize()
+        assert torch.equal(pool[:, :, 32:48], ref)
+    finally:
+        st.close()
+        g.close()

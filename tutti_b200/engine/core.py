@@ -32,6 +32,7 @@ import torch
 from ..common.observability import nvtx_range
 from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
+from ..parallel.green_context import configured_io_sms, io_stream_on_sms
 from .completion import AggregateCompletion, LoadGateError, PostCompletion
 
 LOG = logging.getLogger("tutti_b200.engine")
@@ -186,7 +187,13 @@ class KVEngine:
     @property
     def io_stream(self) -> torch.cuda.Stream:
         if self._io_stream is None:
-            self._io_stream = torch.cuda.Stream(device=self.device, priority=self._io_priority)
+            sms = configured_io_sms()
+            if sms:
+                # io kernels confined to a green-context SM partition (TUTTI_GREEN_CTX_IO_SMS)
+                dev = self.device.index if isinstance(self.device, torch.device) else int(self.device)
+                self._io_stream = io_stream_on_sms(sms, dev or 0)
+            else:
+                self._io_stream = torch.cuda.Stream(device=self.device, priority=self._io_priority)
         return self._io_stream
 
     def bind(self, pool: torch.Tensor) -> None:
