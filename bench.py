@@ -32,7 +32,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "kv_restore_GBps"
-BASELINE_GBPS = None  # BASELINE.md publishes no B200 number for this config
+BASELINE_GBPS = None  # the reference publishes no B200 number for this config
 
 
 def parse():
