@@ -25,7 +25,7 @@ TARGETS = {
     "tutti_native_tests": ([
         "tests/native_tests.cpp", "runtime/storage_runtime.cpp", "objects/object_store.cpp",
         "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
-        "resolvers/file_resolvers.cpp",
+        "resolvers/file_resolvers.cpp", "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",
     ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
 }
 

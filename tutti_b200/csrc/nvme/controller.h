@@ -109,6 +109,9 @@ struct EmulatedControllerConfig {
     // Diagnostic: complete READ/WRITE commands without moving data (measures
     // the queue protocol and the GPU side alone; payloads are not valid).
     bool skip_data = false;
+    // Page-cached mode: serve READs by copying from a shared mapping of the
+    // backing file instead of pread (measured no faster on the GPU boxes).
+    bool map_reads = false;
 };
 
 class EmulatedNvmeController final : public NvmeController {
@@ -155,6 +158,8 @@ private:
         std::string path;
         int fd = -1;
         std::vector<BackingRange> ranges;
+        const char* map = nullptr;  // page-cached mode only; unmapped at destruction
+        std::uint64_t map_len = 0;
     };
     struct Window {
         std::uint64_t base;
@@ -171,7 +176,9 @@ private:
     mutable std::mutex map_mu_;  // guards backings_ / windows_ (workers take it shared-ish: short)
     std::vector<Backing> backings_;
     // flattened, sorted by ns_offset: (ns_offset, length, file_offset, fd)
-    struct Span { std::uint64_t ns, len, foff; int fd; };
+    // map: a read-only shared mapping of the whole backing file (page-cached
+    // mode), so READs copy straight from the page cache without a syscall.
+    struct Span { std::uint64_t ns, len, foff; int fd; const char* map; std::uint64_t map_len; };
     std::shared_ptr<const std::vector<Span>> spans_;
     std::shared_ptr<const std::vector<Window>> windows_;
 

@@ -12,6 +12,8 @@
 
 #include <fcntl.h>
 #include <immintrin.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
 #include <sys/uio.h>
 #include <unistd.h>
 
@@ -77,8 +79,10 @@ Status EmulatedNvmeController::start() {
 
 EmulatedNvmeController::~EmulatedNvmeController() {
     stop();
-    for (auto& b : backings_)
+    for (auto& b : backings_) {
+        if (b.map) ::munmap(const_cast<char*>(b.map), b.map_len);
         if (b.fd >= 0) ::close(b.fd);
+    }
     host_mapped_free(sq_mem_);
     host_mapped_free(cq_mem_);
     host_mapped_free(bar_mem_);
@@ -178,12 +182,25 @@ Status EmulatedNvmeController::attach_file(const std::string& path, const std::v
         int fd = ::open(path.c_str(), flags | (cfg_.direct_io ? O_DIRECT : 0));
         if (fd < 0 && cfg_.direct_io) fd = ::open(path.c_str(), flags);  // e.g. tmpfs rejects O_DIRECT
         if (fd < 0) return {StatusCode::NOT_FOUND, "emulated namespace cannot open " + path};
-        backings_.push_back(Backing{path, fd, ranges});
+        Backing nb{path, fd, ranges};
+        if (!cfg_.direct_io && cfg_.map_reads) {
+            // Page-cached mode: READs copy from a shared read-only mapping (the page
+            // cache itself) instead of pread; WRITEs keep pwrite, which the mapping sees.
+            struct stat st {};
+            if (::fstat(fd, &st) == 0 && st.st_size > 0) {
+                void* m = ::mmap(nullptr, static_cast<std::size_t>(st.st_size), PROT_READ, MAP_SHARED, fd, 0);
+                if (m != MAP_FAILED) {
+                    nb.map = static_cast<const char*>(m);
+                    nb.map_len = static_cast<std::uint64_t>(st.st_size);
+                }
+            }
+        }
+        backings_.push_back(std::move(nb));
     }
 rebuild: {
     auto spans = std::make_shared<std::vector<Span>>();
     for (auto& b : backings_)
-        for (auto& r : b.ranges) spans->push_back({r.ns_offset, r.length, r.file_offset, b.fd});
+        for (auto& r : b.ranges) spans->push_back({r.ns_offset, r.length, r.file_offset, b.fd, b.map, b.map_len});
     std::sort(spans->begin(), spans->end(), [](const Span& a, const Span& b) { return a.ns < b.ns; });
     for (std::size_t i = 1; i < spans->size(); ++i) {
         const Span& p = (*spans)[i - 1];
@@ -208,7 +225,7 @@ Status EmulatedNvmeController::detach_file(const std::string& path) {
     it->ranges.clear();
     auto spans = std::make_shared<std::vector<Span>>();
     for (auto& b : backings_)
-        for (auto& r : b.ranges) spans->push_back({r.ns_offset, r.length, r.file_offset, b.fd});
+        for (auto& r : b.ranges) spans->push_back({r.ns_offset, r.length, r.file_offset, b.fd, b.map, b.map_len});
     std::sort(spans->begin(), spans->end(), [](const Span& a, const Span& b) { return a.ns < b.ns; });
     std::atomic_store(&spans_, std::shared_ptr<const std::vector<Span>>(spans));
     return Status::Ok();
@@ -357,6 +374,10 @@ std::uint32_t EmulatedNvmeController::execute(const Sqe& sqe, bool* drop_cqe) {
             std::uint64_t n = std::min(chunk, seg_left);
             char* buf = iov[seg].first + seg_off;
             std::uint64_t done = 0;
+            if (op == kOpRead && it->map && foff + n <= it->map_len) {
+                std::memcpy(buf, it->map + foff, n);
+                done = n;
+            }
             while (done < n) {
                 ssize_t r = (op == kOpRead) ? ::pread(it->fd, buf + done, n - done, foff + done)
                                             : ::pwrite(it->fd, buf + done, n - done, foff + done);

@@ -505,6 +505,11 @@ PYBIND11_MODULE(_core, m) {
             if (opts.contains("controller_threads")) o.controller_threads = opts["controller_threads"].cast<std::uint32_t>();
             if (opts.contains("direct_io")) o.direct_io = opts["direct_io"].cast<bool>();
             if (opts.contains("emulator_skip_data")) o.skip_data = opts["emulator_skip_data"].cast<bool>();
+            if (opts.contains("emulator_reads")) {
+                const std::string how = opts["emulator_reads"].cast<std::string>();
+                if (how != "mmap" && how != "pread") throw py::value_error("emulator_reads: mmap|pread");
+                o.map_reads = how == "mmap";
+            }
             if (opts.contains("leases")) o.gpu.leases = opts["leases"].cast<std::uint32_t>();
             if (opts.contains("max_ctas_per_op")) o.gpu.max_ctas_per_op = opts["max_ctas_per_op"].cast<std::uint32_t>();
             if (opts.contains("slots_per_lease")) o.gpu.slots_per_lease = opts["slots_per_lease"].cast<std::uint32_t>();

@@ -29,6 +29,7 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
         c.worker_threads = o.controller_threads;
         c.direct_io = o.direct_io;
         c.skip_data = o.skip_data;
+        c.map_reads = o.map_reads;
         auto ctl = nvme::EmulatedNvmeController::create(c);
         if (!ctl.ok()) return R::Failure(ctl.status());
         std::shared_ptr<nvme::NvmeController> sp(std::move(ctl).value());

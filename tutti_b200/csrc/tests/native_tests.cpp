@@ -1,7 +1,8 @@
 // C++ contract tests of the native runtime (no GPU, no NVMe).
 // Suites: StorageRuntime against the mock DataPath kit (partial commit,
 // lifecycle, budgets, failure attribution), stub runtime, object store
-// format and recovery, config spec validation.
+// format and recovery, config spec validation, and the emulated NVMe
+// controller's queue protocol driven by a host submitter.
 // Parity: reference tests/storage_runtime/contract/storage_runtime_contract_test.cpp,
 // tests/storage_objects/*, tests/config/{parser,spec}.
 //
@@ -19,6 +20,7 @@
 #include <tutti/storage_runtime.h>
 
 #include "../config/runtime_spec.h"
+#include "../nvme/controller.h"
 #include "../objects/digest.h"
 #include "../objects/object_store.h"
 #include "../testing/mock_data_path.h"
@@ -304,6 +306,103 @@ storage:
     auto s3 = parse_runtime_config_text(std::string(ok) + "  extra: 1\n");
     CHECK(!s3.ok());
 }
+
+
+// ---- emulated NVMe controller, host submitter ----
+namespace {
+struct HostSubmitter {
+    nvme::QueuePairView q;
+    std::uint32_t tail = 0, head = 0, phase = 1;
+    // Submits one SQE and waits (bounded) for its CQE; returns the status field or -1 on timeout.
+    int run(const nvme::Sqe& e) {
+        q.sq[tail] = e;
+        tail = (tail + 1) % q.depth;
+        __atomic_store_n(q.sq_doorbell, tail, __ATOMIC_RELEASE);
+        for (int i = 0; i < 200000; ++i) {
+            const std::uint32_t dw3 = __atomic_load_n(&q.cq[head].dw3, __ATOMIC_ACQUIRE);
+            if (nvme::cqe_phase(dw3) == phase) {
+                head = (head + 1) % q.depth;
+                if (head == 0) phase ^= 1u;
+                __atomic_store_n(q.cq_doorbell, head, __ATOMIC_RELEASE);
+                return static_cast<int>(nvme::cqe_status(dw3));
+            }
+            usleep(10);
+        }
+        return -1;
+    }
+};
+
+void controller_roundtrip(bool direct_io, bool map_reads = false) {
+    char path[] = "/tmp/tutti_emu_XXXXXX";
+    const int fd = mkstemp(path);
+    CHECK(fd >= 0);
+    const std::size_t fbytes = 4u << 20;
+    std::vector<unsigned char> pattern(fbytes);
+    for (std::size_t i = 0; i < fbytes; ++i) pattern[i] = static_cast<unsigned char>((i * 131u + 7u) >> 3);
+    CHECK(::pwrite(fd, pattern.data(), fbytes, 0) == static_cast<ssize_t>(fbytes));
+    ::fsync(fd);
+    ::close(fd);
+    nvme::EmulatedControllerConfig cfg;
+    cfg.num_io_queues = 2;
+    cfg.queue_depth = 16;
+    cfg.worker_threads = 1;
+    cfg.direct_io = direct_io;
+    cfg.map_reads = map_reads;
+    auto ctl = nvme::EmulatedNvmeController::create(cfg);
+    CHECK(ctl.ok());
+    auto& c = *ctl.value();
+    // namespace [1 MiB, 5 MiB) is the file
+    CHECK(c.attach_file(path, {{1u << 20, fbytes, 0}}).ok());
+    void* buf = nullptr;
+    void* lst = nullptr;
+    CHECK(posix_memalign(&buf, 4096, 256 << 10) == 0 && posix_memalign(&lst, 4096, 4096) == 0);
+    auto iova = c.map_dma(buf, 256 << 10);
+    auto liova = c.map_dma(lst, 4096);
+    CHECK(iova.ok() && liova.ok());
+    HostSubmitter hs{c.host_queue(0)};
+    // 8 KiB read: PRP1 + PRP2 page
+    nvme::Sqe e{};
+    const std::uint64_t lba = 512;
+    nvme::build_rw_sqe(e, nvme::kOpRead, 1, 1, ((1u << 20) + 8192) / lba, 8192 / lba, iova.value(),
+                       iova.value() + 4096);
+    CHECK(hs.run(e) == 0);
+    CHECK(std::memcmp(buf, pattern.data() + 8192, 8192) == 0);
+    // 64 KiB read through a PRP list (pages in reverse order)
+    auto* l = static_cast<std::uint64_t*>(lst);
+    for (int k = 0; k < 15; ++k) l[k] = iova.value() + (15 - k) * 4096ull;
+    nvme::build_rw_sqe(e, nvme::kOpRead, 2, 1, ((1u << 20) + 65536) / lba, 65536 / lba, iova.value(), liova.value());
+    CHECK(hs.run(e) == 0);
+    auto* b = static_cast<unsigned char*>(buf);
+    CHECK(std::memcmp(b, pattern.data() + 65536, 4096) == 0);
+    for (int k = 0; k < 15; ++k) CHECK(std::memcmp(b + (15 - k) * 4096, pattern.data() + 65536 + (k + 1) * 4096, 4096) == 0);
+    // write 4 KiB, then read it back through the controller
+    std::memset(buf, 0xA5, 4096);
+    nvme::build_rw_sqe(e, nvme::kOpWrite, 3, 1, ((1u << 20) + 12288) / lba, 8, iova.value(), 0);
+    CHECK(hs.run(e) == 0);
+    std::memset(buf, 0, 8192);
+    nvme::build_rw_sqe(e, nvme::kOpRead, 4, 1, ((1u << 20) + 12288) / lba, 8, iova.value(), 0);
+    CHECK(hs.run(e) == 0);
+    CHECK(b[0] == 0xA5 && b[4095] == 0xA5);
+    // outside the backed namespace range, an unmapped buffer, an injected media error
+    nvme::build_rw_sqe(e, nvme::kOpRead, 5, 1, 0, 8, iova.value(), 0);
+    CHECK(hs.run(e) == nvme::make_status(0, nvme::kScLbaOutOfRange));
+    nvme::build_rw_sqe(e, nvme::kOpRead, 6, 1, (1u << 20) / lba, 8, 0x1000, 0);
+    CHECK(hs.run(e) == nvme::make_status(0, nvme::kScDataTransferError));
+    c.inject(nvme::InjectKind::MEDIA_ERROR, 1);
+    nvme::build_rw_sqe(e, nvme::kOpRead, 7, 1, (1u << 20) / lba, 8, iova.value(), 0);
+    CHECK(hs.run(e) == nvme::make_status(nvme::kSctMedia, nvme::kScUnrecoveredRead));
+    nvme::build_rw_sqe(e, nvme::kOpRead, 8, 1, (1u << 20) / lba, 8, iova.value(), 0);
+    CHECK(hs.run(e) == 0);
+    c.stop();
+    free(buf);
+    free(lst);
+    ::unlink(path);
+}
+}  // namespace
+
+TEST(emulated_controller_page_cached_reads_writes_and_errors) { controller_roundtrip(false); }
+TEST(emulated_controller_mapped_reads_writes_and_errors) { controller_roundtrip(false, true); }
+TEST(emulated_controller_direct_io_reads_writes_and_errors) { controller_roundtrip(true); }
 
 int main(int argc, char** argv) {
     const char* filter = nullptr;
