@@ -54,6 +54,7 @@ def parse():
     p.add_argument("--slots", type=int, default=8)
     p.add_argument("--inflight", type=int, default=2, help="restores submitted ahead")
     p.add_argument("--emulator-skip-data", action="store_true", help="diagnostic: controllers move no data")
+    p.add_argument("--staging-wc", action="store_true", help="write-combined staging slots")
     p.add_argument("--emulator-reads", choices=["mmap", "pread"], default="pread",
                    help="how the emulated drives read page-cached segment files")
     return p.parse_args()
@@ -202,7 +203,8 @@ def main():
     opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": args.leases,
             "max_ctas_per_op": args.ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20,
             "queue_depth": 256, "mdts_bytes": 1 << 20, "timing": bool(args.timing),
-            "emulator_skip_data": bool(args.emulator_skip_data), "emulator_reads": args.emulator_reads}
+            "emulator_skip_data": bool(args.emulator_skip_data), "emulator_reads": args.emulator_reads,
+            "staging_write_combined": bool(args.staging_wc)}
     backend = "nvme-gpu" if args.impl == "tutti" else "posix"
     if backend == "posix":
         opts = {"threads": max(4, ncpu // max(1, world)), "direct_io": bool(args.direct_io)}
@@ -309,7 +311,7 @@ def main():
                        "pool_blocks": args.pool_blocks, "drives_per_rank": args.drives,
                        "backing": "O_DIRECT" if args.direct_io else "page cache",
                        "controller_threads": threads, "impl": args.impl, "inflight": args.inflight,
-                       "emulator_reads": args.emulator_reads,
+                       "emulator_reads": args.emulator_reads, "staging_write_combined": bool(args.staging_wc),
                        "l2": "inputs (4.29 GB/step) larger than L2"},
             "e2e": {"value": round(total_bytes / (e2e / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": nblk * 8, "d2h_bytes_per_step": 4},

@@ -184,7 +184,7 @@ Status GpuNvmeDataPath::initialize(const DataPathConfig&, ResourceProvider*) {
 
 Status GpuNvmeDataPath::init_device_side() {
     const std::uint64_t nslots = std::uint64_t(cfg_.leases) * cfg_.slots_per_lease;
-    auto st = host_mapped_alloc(nslots * cfg_.slot_bytes);
+    auto st = host_mapped_alloc(nslots * cfg_.slot_bytes, cfg_.staging_write_combined);
     if (!st.ok()) return st.status();
     staging_ = st.value();
     auto pr = host_mapped_alloc(nslots * nvme::kMemoryPageBytes);

@@ -48,6 +48,9 @@ struct GpuNvmeConfig {
     // stream, or that progress() launches itself once `async_fallback_us` have
     // passed without one (a host fallback). Off: one kernel does everything.
     bool async_completion = false;
+    // Staging slots in write-combined host memory (drives stream into them, the
+    // GPU reads them without snoops); writes that the drive reads back are slower.
+    bool staging_write_combined = false;
     std::uint32_t async_fallback_us = 1000;
 };
 

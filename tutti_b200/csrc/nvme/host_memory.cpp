@@ -16,13 +16,15 @@ bool cuda_device_present() {
     return n > 0;
 }
 
-Result<HostMappedBuffer> host_mapped_alloc(std::size_t bytes) {
+Result<HostMappedBuffer> host_mapped_alloc(std::size_t bytes, bool write_combined) {
     HostMappedBuffer b;
     b.bytes = (bytes + 4095) & ~std::size_t(4095);
     if (b.bytes == 0) b.bytes = 4096;
     if (cuda_device_present()) {
         void* p = nullptr;
-        cudaError_t e = cudaHostAlloc(&p, b.bytes, cudaHostAllocMapped | cudaHostAllocPortable);
+        cudaError_t e = cudaHostAlloc(&p, b.bytes,
+                                      cudaHostAllocMapped | cudaHostAllocPortable |
+                                          (write_combined ? cudaHostAllocWriteCombined : 0u));
         if (e != cudaSuccess) {
             cudaGetLastError();
             return Result<HostMappedBuffer>::Failure(

@@ -29,7 +29,9 @@ bool cuda_device_present();
 
 // Allocates `bytes` (rounded up to 4 KiB) zero-filled. With a CUDA device the
 // memory is cudaHostAllocMapped|Portable; otherwise 4 KiB-aligned heap memory.
-Result<HostMappedBuffer> host_mapped_alloc(std::size_t bytes);
+// write_combined: CPU stores stream without reading the lines first and the
+// GPU reads them without snooping the CPU caches; CPU reads of it are slow.
+Result<HostMappedBuffer> host_mapped_alloc(std::size_t bytes, bool write_combined = false);
 void host_mapped_free(HostMappedBuffer& buf);
 
 }  // namespace tutti

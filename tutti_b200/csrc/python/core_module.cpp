@@ -521,6 +521,8 @@ PYBIND11_MODULE(_core, m) {
                 o.gpu.async_completion = env && *env && std::strcmp(env, "0") != 0;
             }
             if (opts.contains("async_completion")) o.gpu.async_completion = opts["async_completion"].cast<bool>();
+            if (opts.contains("staging_write_combined"))
+                o.gpu.staging_write_combined = opts["staging_write_combined"].cast<bool>();
             if (opts.contains("async_fallback_us"))
                 o.gpu.async_fallback_us = opts["async_fallback_us"].cast<std::uint32_t>();
             if (opts.contains("mapping")) o.mapping = opts["mapping"].cast<std::string>();
