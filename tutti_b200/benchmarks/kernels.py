@@ -103,6 +103,7 @@ def bench_checksum(args) -> dict:
 
 
 def bench_io(args) -> dict:
+    from .. import ops
     from ..index.chunk_index import chunk_keys_for_tokens
     from ..models.kv_geometry import LLAMA3_8B as g
     from ..storage.tutti_store import TuttiKVStore
@@ -113,7 +114,7 @@ def bench_io(args) -> dict:
         nblk = tokens // g.block_size
         nch = tokens // g.chunk_tokens
         st = TuttiKVStore(root, g, capacity_chunks=max(16, nch), mounts=[os.path.join(root, f"nvme{d}") for d in range(4)],
-                          device=0, segment_file_slots=max(4, nch // 4 + 1),
+                          device=0, segment_file_slots=max(4, nch // 4 + 1), stored_format=args.stored_format,
                           runtime_options={"controller_threads": 3, "leases": 64, "max_ctas_per_op": 64,
                                            "slots_per_lease": 8})
         st.open()
@@ -125,10 +126,15 @@ def bench_io(args) -> dict:
         st.put_paged(keys, src).wait()
         dst = (np.arange(nblk) + nblk).reshape(nch, g.blocks_per_chunk)
         ms = _time(lambda: st.get_paged(keys, dst).wait(), args.iters, args.warmup)
-        ok = bool(torch.equal(pool[:, :, nblk:2 * nblk], pool[:, :, :nblk]))
+        want = pool[:, :, :nblk]
+        if args.stored_format == "fp8_block128":
+            q, sc = ops.fp8_quant(want.reshape(-1, 128))
+            want = ops.fp8_dequant(q, sc).reshape(want.shape)
+        ok = bool(torch.equal(pool[:, :, nblk:2 * nblk], want))
         nbytes = nblk * g.num_layers * g.block_layer_bytes
         st.close()
-        return {"kernel": "nvme_io_kernel", "bytes": nbytes, "ms": ms, "GBps": nbytes / ms / 1e6, "ok": ok}
+        return {"kernel": "nvme_io_kernel", "stored_format": args.stored_format, "bytes": nbytes, "ms": ms,
+                "GBps": nbytes / ms / 1e6, "ok": ok}
     finally:
         shutil.rmtree(root, ignore_errors=True)
 
@@ -143,6 +149,7 @@ def main(argv=None):
     p.add_argument("--requests", type=int, default=256)
     p.add_argument("--chunk", type=int, default=256)
     p.add_argument("--verify", action="store_true")
+    p.add_argument("--stored-format", choices=["native", "fp8_block128"], default="native")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     fn = {"copy": bench_copy, "fp8": bench_fp8, "hash": bench_hash, "checksum": bench_checksum, "io": bench_io}
