@@ -505,6 +505,7 @@ PYBIND11_MODULE(_core, m) {
             if (opts.contains("controller_threads")) o.controller_threads = opts["controller_threads"].cast<std::uint32_t>();
             if (opts.contains("direct_io")) o.direct_io = opts["direct_io"].cast<bool>();
             if (opts.contains("emulator_skip_data")) o.skip_data = opts["emulator_skip_data"].cast<bool>();
+            if (opts.contains("emulator_idle_spins")) o.idle_spin_iters = opts["emulator_idle_spins"].cast<std::uint32_t>();
             if (opts.contains("emulator_reads")) {
                 const std::string how = opts["emulator_reads"].cast<std::string>();
                 if (how != "mmap" && how != "pread") throw py::value_error("emulator_reads: mmap|pread");

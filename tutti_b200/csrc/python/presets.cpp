@@ -30,6 +30,7 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
         c.direct_io = o.direct_io;
         c.skip_data = o.skip_data;
         c.map_reads = o.map_reads;
+        c.idle_spin_iters = o.idle_spin_iters;
         auto ctl = nvme::EmulatedNvmeController::create(c);
         if (!ctl.ok()) return R::Failure(ctl.status());
         std::shared_ptr<nvme::NvmeController> sp(std::move(ctl).value());

@@ -28,6 +28,7 @@ struct EmulatedPresetOptions {
     bool direct_io = false;
     bool skip_data = false;  // diagnostic: controllers move no data
     bool map_reads = false;  // page-cached reads copy from a file mapping (default: pread)
+    std::uint32_t idle_spin_iters = 2000;  // queue scans before an idle worker starts sleeping
     std::string mapping = "auto";      // fiemap | synthetic | auto
     std::string raid0_md;              // non-empty: mounts[0] is an md RAID0 array
     std::string sysfs_root = "/sys";
