@@ -34,3 +34,10 @@ def test_fiemap_and_raid0_probe(tmp_path, capsys):
     capsys.readouterr()
     assert main(["probe-raid0", "md9", "--sysfs", str(tmp_path)]) == 0
     assert json.loads(capsys.readouterr().out)["chunk_bytes"] == 65536
+
+
+def test_topology_command_on_empty_sysfs(tmp_path, capsys):
+    from tutti_b200.cli import main
+
+    assert main(["topology", "--sysfs", str(tmp_path)]) == 0
+    assert json.loads(capsys.readouterr().out) == {"gpus": [], "drives": [], "affine_gpus": []}

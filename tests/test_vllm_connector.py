@@ -178,6 +178,11 @@ def test_config_parsing():
         ConnectorConfig.from_extra({"bogus": 1})
     with pytest.raises(ValueError):
         ConnectorConfig.from_extra({"store": {"type": "s3"}})
+    c = ConnectorConfig.from_extra({"store": {"stored_format": "fp8_block128",
+                                              "runtime_options": {"async_completion": True}}})
+    assert c.stored_format == "fp8_block128" and c.runtime_options["async_completion"]
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"store": {"stored_format": "int4"}})
 
 
 def test_connector_class_with_vllm_base():

@@ -6,10 +6,12 @@
     python -m tutti_b200 selftest              # C++ contract suite (no GPU needed)
     python -m tutti_b200 fiemap FILE           # extents the FIEMAP resolver sees
     python -m tutti_b200 probe-raid0 md0 [--sysfs /sys]
+    python -m tutti_b200 topology [--sysfs /sys]   # NVMe drive -> affine GPU over the PCIe tree
     python -m tutti_b200 bench {kernels,ttft,fanout,mla,trace} [args...]
 
 Parity: reference scripts/tutti-env.sh (build, build-ext, test, daemon, status
-subcommands) and scripts/tutti-md (md RAID0 inspection).
+subcommands), scripts/tutti-md (md RAID0 inspection) and
+scripts/pci_topology_check.sh (drive / GPU switch affinity).
 """
 from __future__ import annotations
 
@@ -104,6 +106,18 @@ def cmd_probe_raid0(args) -> int:
     return 0
 
 
+def cmd_topology(args) -> int:
+    from .parallel.topology import affinity, discover
+
+    devs = discover(args.sysfs)
+    gpus = [d for d in devs if d.kind == "gpu"]
+    drives = [d for d in devs if d.kind == "nvme"]
+    aff = affinity(drives, gpus) if drives and gpus else []
+    out = {"gpus": [d.bdf for d in gpus], "drives": [d.bdf for d in drives], "affine_gpus": aff}
+    print(json.dumps(out))
+    return 0
+
+
 def cmd_bench(args) -> int:
     mod = importlib.import_module(f"tutti_b200.benchmarks.{BENCHES[args.which]}")
     rc = mod.main(list(args.rest))
@@ -129,6 +143,9 @@ def main(argv=None) -> int:
     r.add_argument("md")
     r.add_argument("--sysfs", default="/sys")
     r.set_defaults(fn=cmd_probe_raid0)
+    t = sub.add_parser("topology")
+    t.add_argument("--sysfs", default="/sys")
+    t.set_defaults(fn=cmd_topology)
     b = sub.add_parser("bench")
     b.add_argument("which", choices=sorted(BENCHES))
     b.add_argument("rest", nargs=argparse.REMAINDER)

@@ -56,6 +56,7 @@ class ConnectorConfig:
     capacity_bytes: int = 0
     segment_file_slots: int = 2048
     runtime_options: dict = field(default_factory=dict)
+    stored_format: str = "native"  # or "fp8_block128": E4M3 + 1x128 scales on disk, fused in the io kernel
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
@@ -78,6 +79,9 @@ class ConnectorConfig:
             c.capacity_bytes = parse_bytes(st.pop("capacity"))
         c.segment_file_slots = int(st.pop("segment_file_slots", c.segment_file_slots))
         c.runtime_options = dict(st.pop("runtime_options", {}))
+        c.stored_format = str(st.pop("stored_format", c.stored_format))
+        if c.stored_format not in ("native", "fp8_block128"):
+            raise ValueError("store.stored_format must be native or fp8_block128")
         if st:
             raise ValueError(f"unknown store options: {sorted(st)}")
         if c.store_type not in ("tutti", "memory"):
@@ -120,7 +124,7 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
         mounts = [expand(m, rank, local_rank) for m in cfg.mounts] or [os.path.join(root, "nvme0")]
         store = TuttiKVStore(root, g, capacity_chunks=cap, mounts=mounts, device=device.index, rank=rank,
                              rank_count=world, segment_file_slots=min(cfg.segment_file_slots, max(16, cap)),
-                             runtime_options=cfg.runtime_options, namespace=ns)
+                             runtime_options=cfg.runtime_options, namespace=ns, stored_format=cfg.stored_format)
         store.open()
         eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device)
         eng.restore_from_store()
