@@ -179,3 +179,31 @@ def test_store_grows_segment_files_on_demand(tmp_path):
         assert torch.equal(pool[:, :, :160], ref)
     finally:
         st.close()
+
+
+def test_read_only_view_adopts_the_namespace_layout(tmp_path):
+    """A view opened without the model's geometry lists exactly the committed chunks."""
+    import numpy as np
+    import torch
+
+    from tutti_b200.index.chunk_index import chunk_keys_for_tokens
+    from tutti_b200.models.kv_geometry import KVGeometry
+    from tutti_b200.storage.object_layout import ObjectLayout
+    from tutti_b200.storage.tutti_store import TuttiKVStore
+
+    g = KVGeometry("t-view", num_layers=3, num_kv_heads=2, head_dim=128, chunk_tokens=64)
+    mounts = [str(tmp_path / "d0"), str(tmp_path / "d1")]
+    st = TuttiKVStore(tmp_path, g, capacity_chunks=64, mounts=mounts, device=-1, backend="posix",
+                      segment_file_slots=4, runtime_options={"threads": 2})
+    st.open()
+    pool = torch.randn(g.pool_shape(64), dtype=torch.bfloat16)
+    st.register_pool(pool)
+    keys = chunk_keys_for_tokens(list(range(12 * 64)), 64, namespace=b"view")
+    st.put_paged(keys, np.arange(48).reshape(12, 4)).wait()
+    st.close()
+    v = ObjectLayout.open_view(tmp_path, mounts)
+    assert sorted(v.recover()) == sorted(keys)
+    assert v.contains_prefix(keys, False) == 12
+    v.close()
+    with pytest.raises(Exception):
+        ObjectLayout.open_view(tmp_path, mounts[:1])  # the namespace has two devices

@@ -201,3 +201,19 @@ def test_connector_class_with_vllm_base():
                           num_scheduled_tokens={"q": 20}, scheduled_cached_reqs=None)
     meta = sch.build_connector_meta(out)
     assert len(meta.saves) == 1 and len(meta.saves[0].keys) == 2
+
+
+def test_kv_layer_layouts_normalise_to_planes_first():
+    from tutti_b200.integration.vllm.worker import normalize_kv_layer
+
+    a = torch.zeros(2, 8, 16, 4, 64)
+    assert normalize_kv_layer(a) is a
+    b = torch.arange(8 * 2 * 16 * 4 * 64, dtype=torch.float32).reshape(8, 2, 16, 4, 64)
+    nb = normalize_kv_layer(b)
+    assert nb.shape == (1, 8, 16, 8, 64) and nb.data_ptr() == b.data_ptr()
+    # block 3's bytes (its K and V) are block 3 of the single plane
+    assert torch.equal(nb[0, 3].reshape(-1), b[3].reshape(-1))
+    m = normalize_kv_layer(torch.zeros(8, 64, 576))
+    assert m.shape == (1, 8, 64, 1, 576)
+    with pytest.raises(ValueError):
+        normalize_kv_layer(torch.zeros(8, 2, 16, 4, 64).transpose(0, 1).contiguous().transpose(0, 1))

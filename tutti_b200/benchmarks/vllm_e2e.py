@@ -1,0 +1,107 @@
+"""vLLM end to end: persist a long prompt's KV through TuttiConnectorV1, reload it in a new engine.
+
+    python -m tutti_b200.benchmarks.vllm_e2e [--model DIR] [--prompt-tokens 2048]
+
+Three fresh vLLM processes share one store (vLLM's own prefix cache is off):
+  1. ``store``: the prompt is prefilled and its full chunks are saved;
+  2. ``reload``: the scheduler's cold start finds the chunks, the worker loads
+     them layer by layer, and only the tail is computed
+     (``num_cached_tokens`` counts the loaded tokens);
+  3. ``recompute``: the same prompt without the connector, as a reference.
+Without ``--model`` a small random-init Llama is written to a temporary
+directory (no tokenizer: prompts are token ids). Prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def make_tiny_llama(path: str, seed: int = 0) -> None:
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=4,
+                      num_attention_heads=8, num_key_value_heads=4, head_dim=64, max_position_embeddings=8192,
+                      initializer_range=0.1, torch_dtype="bfloat16", tie_word_embeddings=False)
+    model = LlamaForCausalLM(cfg).to(torch.bfloat16)
+    model.save_pretrained(path, safe_serialization=True)
+
+
+def run_phase(args) -> dict:
+    from vllm import LLM, SamplingParams
+    from vllm.config import KVTransferConfig
+    from vllm.inputs import TokensPrompt
+
+    kw = dict(model=args.model, dtype="bfloat16", enforce_eager=True, gpu_memory_utilization=args.gpu_mem,
+              max_model_len=args.prompt_tokens + 64, enable_prefix_caching=False, skip_tokenizer_init=True,
+              block_size=16)
+    if args.phase != "recompute":
+        kw["kv_transfer_config"] = KVTransferConfig(
+            kv_connector="TuttiConnectorV1", kv_connector_module_path="tutti_b200.integration.vllm.connector",
+            kv_role="kv_both",
+            kv_connector_extra_config={"chunk_tokens": 256, "store": {
+                "root": args.root, "capacity_chunks": 256, "segment_file_slots": 32}})
+    llm = LLM(**kw)
+    import numpy as np
+
+    ids = np.random.default_rng(1).integers(0, 2048, args.prompt_tokens).tolist()
+    sp = SamplingParams(temperature=0.0, max_tokens=16)
+    t0 = time.perf_counter()
+    out = llm.generate([TokensPrompt(prompt_token_ids=ids)], sp, use_tqdm=False)[0]
+    wall = time.perf_counter() - t0
+    return {"phase": args.phase, "tokens": list(out.outputs[0].token_ids),
+            "num_cached_tokens": int(getattr(out, "num_cached_tokens", 0) or 0), "wall_s": round(wall, 3)}
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser()
+    p.add_argument("--model", default="")
+    p.add_argument("--prompt-tokens", type=int, default=2048)
+    p.add_argument("--root", default="")
+    p.add_argument("--gpu-mem", type=float, default=0.15)
+    p.add_argument("--phase", default="", choices=["", "store", "reload", "recompute"])
+    args = p.parse_args(argv)
+    if args.phase:
+        print("RESULT " + json.dumps(run_phase(args)), flush=True)
+        return 0
+    work = tempfile.mkdtemp(prefix="tutti_vllm_")
+    model = args.model or os.path.join(work, "tiny-llama")
+    if not args.model:
+        make_tiny_llama(model)
+    root = args.root or os.path.join(work, "kv")
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    res = {}
+    for phase in ("store", "reload", "recompute"):
+        cmd = [sys.executable, "-m", "tutti_b200.benchmarks.vllm_e2e", "--phase", phase, "--model", model,
+               "--root", root, "--prompt-tokens", str(args.prompt_tokens), "--gpu-mem", str(args.gpu_mem)]
+        r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("RESULT ")]
+        if r.returncode or not line:
+            print(json.dumps({"bench": "vllm_e2e", "ok": False, "phase": phase,
+                              "tail": (r.stdout[-1500:] + r.stderr[-3000:])}))
+            return 1
+        res[phase] = json.loads(line[-1][7:])
+    expect = (args.prompt_tokens - 1) // 256 * 256
+    agree = sum(a == b for a, b in zip(res["reload"]["tokens"], res["recompute"]["tokens"]))
+    out = {"bench": "vllm_e2e", "prompt_tokens": args.prompt_tokens,
+           "reload_cached_tokens": res["reload"]["num_cached_tokens"], "expected_cached_tokens": expect,
+           "store_cached_tokens": res["store"]["num_cached_tokens"],
+           "tokens_agree_with_recompute": f"{agree}/{len(res['recompute']['tokens'])}",
+           "first_token_agrees": res["reload"]["tokens"][:1] == res["recompute"]["tokens"][:1],
+           "wall_s": {k: v["wall_s"] for k, v in res.items()},
+           "ok": res["reload"]["num_cached_tokens"] == expect and res["store"]["num_cached_tokens"] == 0}
+    print(json.dumps(out))
+    return 0 if out["ok"] else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -9,6 +9,7 @@
 #include <cerrno>
 #include <cstring>
 #include <cstdio>
+#include <map>
 #include <set>
 
 #include "digest.h"
@@ -168,11 +169,63 @@ Status SegmentFileObjectStore::check_namespace_meta(bool* exists) {
     return Status::Ok();
 }
 
+Status SegmentFileObjectStore::adopt_namespace_meta() {
+    const std::string path = join(join(cfg_.uri, "meta"), "namespace");
+    std::FILE* f = std::fopen(path.c_str(), "r");
+    if (!f) return {StatusCode::NOT_FOUND, "no namespace at " + cfg_.uri};
+    std::map<std::string, std::string> kv;
+    char line[256];
+    while (std::fgets(line, sizeof(line), f)) {
+        char k[128], v[128];
+        if (std::sscanf(line, "%127s %127s", k, v) == 2) kv[k] = v;
+    }
+    std::fclose(f);
+    for (const char* key : {"segment_bytes", "segment_count", "segment_file_slots", "segment_header_bytes", "devices",
+                            "rank_count", "fingerprint"})
+        if (!kv.count(key)) return {StatusCode::DATA_LOSS, std::string("namespace meta lacks ") + key};
+    cfg_.layout.segment_bytes = std::stoull(kv["segment_bytes"]);
+    cfg_.layout.segment_count = static_cast<std::uint32_t>(std::stoul(kv["segment_count"]));
+    cfg_.segment_file_slots = std::stoull(kv["segment_file_slots"]);
+    cfg_.segment_header_bytes = std::stoull(kv["segment_header_bytes"]);
+    cfg_.rank_count = static_cast<std::uint32_t>(std::stoul(kv["rank_count"]));
+    if (std::stoull(kv["devices"]) != cfg_.devices.size())
+        return {StatusCode::INVALID_ARGUMENT, "namespace has " + kv["devices"] + " devices, view names " +
+                                                  std::to_string(cfg_.devices.size())};
+    adopted_fingerprint_ = std::stoull(kv["fingerprint"]);
+    // capacity: every complete file group on media
+    const std::uint64_t group = cfg_.segment_file_slots * cfg_.devices.size();
+    const std::uint64_t file_b = cfg_.segment_file_slots * (cfg_.segment_header_bytes + cfg_.layout.payload_bytes());
+    std::uint64_t groups = 0;
+    for (;; ++groups) {
+        bool all = true;
+        for (std::uint64_t d = 0; d < cfg_.devices.size() && all; ++d) {
+            // file g of every device holds file group g
+            const std::string p = join(join(cfg_.devices[d].mount_path, "r" + std::to_string(cfg_.rank_id) + "/segments"),
+                                       std::to_string(groups) + ".seg");
+            struct stat st {};
+            if (::stat(p.c_str(), &st) != 0 || static_cast<std::uint64_t>(st.st_size) < file_b) all = false;
+        }
+        if (!all) break;
+    }
+    cfg_.capacity_slots = std::max<std::uint64_t>(groups, 1) * group;
+    return Status::Ok();
+}
+
 Status SegmentFileObjectStore::open(const StoreConfig& config) {
     std::lock_guard<std::mutex> g(mu_);
     if (open_) return {StatusCode::INVALID_ARGUMENT, "already open"};
     cfg_ = config;
     if (cfg_.uri.empty()) return {StatusCode::INVALID_ARGUMENT, "uri required"};
+    adopted_fingerprint_ = 0;
+    if (cfg_.adopt_namespace_meta) {
+        if (!cfg_.read_only) return {StatusCode::INVALID_ARGUMENT, "adopt_namespace_meta needs a read-only view"};
+        if (cfg_.devices.empty()) {
+            StoreDevice d;
+            d.mount_path = cfg_.uri;
+            cfg_.devices.push_back(d);
+        }
+        TUTTI_RETURN_IF_ERROR(adopt_namespace_meta());
+    }
     if (cfg_.layout.segment_bytes == 0 || cfg_.layout.segment_count == 0)
         return {StatusCode::INVALID_ARGUMENT, "layout must be non-empty"};
     if (cfg_.layout.segment_bytes % 4096) return {StatusCode::INVALID_ARGUMENT, "segment_bytes must be 4096-aligned"};
@@ -197,7 +250,9 @@ Status SegmentFileObjectStore::open(const StoreConfig& config) {
         total_slots_ = cfg_.segment_file_slots * cfg_.devices.size();
     if (total_slots_ == 0) return {StatusCode::INVALID_ARGUMENT, "capacity too small to hold a single object"};
     group_slots_ = cfg_.segment_file_slots * cfg_.devices.size();
-    fingerprint_digest_ = object_identity(cfg_.namespace_fingerprint.data(), cfg_.namespace_fingerprint.size());
+    fingerprint_digest_ = cfg_.adopt_namespace_meta
+                              ? adopted_fingerprint_
+                              : object_identity(cfg_.namespace_fingerprint.data(), cfg_.namespace_fingerprint.size());
     bool exists = false;
     TUTTI_RETURN_IF_ERROR(check_namespace_meta(&exists));
     if (!cfg_.read_only) {

@@ -78,6 +78,10 @@ struct StoreConfig {
     // device IO); "fallocate" reserves blocks (unwritten extents, host IO only).
     std::string materialize = "zeros";
     bool recover_full_scan = false;
+    // Read-only views only: take segment geometry, fingerprint and capacity from
+    // the namespace's own meta file and media instead of checking them (a
+    // scheduler that knows the namespace's location but not the model).
+    bool adopt_namespace_meta = false;
 };
 
 struct ObjectPlacement {
@@ -159,6 +163,7 @@ private:
     void set_bit(std::uint64_t slot, bool v);
     Status save_namespace_meta();
     Status check_namespace_meta(bool* exists);
+    Status adopt_namespace_meta();
 
     StoreConfig cfg_;
     bool open_ = false;
@@ -181,6 +186,7 @@ private:
     std::uint8_t* bitmap_ = nullptr;
     std::size_t bitmap_bytes_ = 0;
     std::vector<std::pair<const std::uint8_t*, std::size_t>> peer_bitmaps_;
+    std::uint64_t adopted_fingerprint_ = 0;
     bool bitmaps_usable_ = false;
 };
 

@@ -688,6 +688,8 @@ PYBIND11_MODULE(_core, m) {
                 if (c.contains("read_only")) cfg.read_only = c["read_only"].cast<bool>();
                 if (c.contains("materialize")) cfg.materialize = c["materialize"].cast<std::string>();
                 if (c.contains("recover_full_scan")) cfg.recover_full_scan = c["recover_full_scan"].cast<bool>();
+                if (c.contains("adopt_namespace_meta"))
+                    cfg.adopt_namespace_meta = c["adopt_namespace_meta"].cast<bool>();
                 Status st;
                 {
                     py::gil_scoped_release nogil;

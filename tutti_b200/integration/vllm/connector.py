@@ -59,6 +59,7 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                         namespace=self.cfg.namespace.encode(),
                                         policy=LoadPolicy(self.cfg.load_mode, bytes_per_token=max(1, bytes_per_token)))
             self._async_pending: dict[str, bool] = {}
+            self._cold_start()
         else:
             rank, world, cpu_group = _tp_info()
             from ...parallel.tp_consensus import TpFailureConsensus
@@ -68,6 +69,29 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                       block_size=self.block_size, chunk_tokens=self.cfg.chunk_tokens,
                                       tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group),
                                       failure_policy=self.cfg.failure_policy)
+
+    def _cold_start(self) -> None:
+        """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""
+        if self.cfg.store_type != "tutti":
+            return
+        from ...storage.object_layout import ObjectLayout
+        from .factory import expand
+
+        root = expand(self.cfg.root, 0, 0)
+        if not os.path.exists(os.path.join(root, "meta", "namespace")):
+            return
+        mounts = [expand(m, 0, 0) for m in self.cfg.mounts] or [os.path.join(root, "nvme0")]
+        try:
+            view = ObjectLayout.open_view(root, mounts, rank=0)
+            keys = view.recover()
+            if self.tp_size > 1:  # resident only where every TP rank holds its slice
+                keys = [k for k in keys if view.contains_prefix([k], True) == 1]
+            view.close()
+        except Exception as e:  # noqa: BLE001 - a cold store only costs recomputation
+            LOG.warning("[tutti] cold start skipped: %s", e)
+            return
+        self._sched.restore(keys)
+        LOG.info("[tutti] cold start: %d resident chunk(s)", len(keys))
 
     # ---------------- scheduler role ----------------
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int):

@@ -43,6 +43,28 @@ class _FailedLoad:
         raise self.error
 
 
+def normalize_kv_layer(t: torch.Tensor) -> torch.Tensor:
+    """A view of one layer's KV cache as ``[planes, num_blocks, block, heads, dim]``.
+
+    vLLM attention backends lay the cache out as ``[2, num_blocks, block, heads,
+    dim]`` (K and V planes first), ``[num_blocks, 2, block, heads, dim]`` (K and V
+    of a block together) or ``[num_blocks, block, dim]`` (MLA latents). Only
+    bytes move, so a block-major layout becomes one plane whose block holds K and
+    V together.
+    """
+    if not t.is_contiguous():
+        raise ValueError(f"KV cache layer with shape {tuple(t.shape)} is not contiguous")
+    if t.dim() == 5 and t.shape[0] == 2:
+        return t
+    if t.dim() == 5 and t.shape[1] == 2:
+        nb, _, bs, heads, dim = t.shape
+        return t.view(1, nb, bs, 2 * heads, dim)
+    if t.dim() == 3:
+        nb, bs, dim = t.shape
+        return t.view(1, nb, bs, 1, dim)
+    raise ValueError(f"unsupported KV cache layout {tuple(t.shape)}")
+
+
 def layer_index(name: str) -> int:
     m = _LAYER_RE.findall(name)
     if not m:
@@ -78,7 +100,7 @@ class WorkerSide:
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
         names = sorted(kv_caches, key=layer_index)
         self.layer_of = {n: i for i, n in enumerate(names)}
-        tensors = [kv_caches[n] for n in names]
+        tensors = [normalize_kv_layer(kv_caches[n]) for n in names]
         self.engine = self.make_engine(tensors)
 
     # -- loads ----------------------------------------------------------------

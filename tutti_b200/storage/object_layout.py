@@ -84,6 +84,21 @@ class ObjectLayout:
         self.store = s
         return s
 
+    @staticmethod
+    def open_view(root: str | os.PathLike, mounts: list[str] | None = None, rank: int = 0):
+        """A read-only view of an existing namespace that takes its layout from the namespace itself.
+
+        For a process that knows where the store lives but not the model (the vLLM
+        scheduler at cold start): ``recover()`` lists the committed chunk keys,
+        ``contains_prefix(keys, True)`` checks them on every rank's bitmap.
+        """
+        s = core().ObjectStore()
+        mounts = [str(m) for m in (mounts or [root])]
+        s.open({"uri": str(root), "segment_bytes": 4096, "segment_count": 1, "segment_file_slots": 1,
+                "segment_header_bytes": 4096, "mounts": mounts, "rank_id": int(rank), "rank_count": int(rank) + 1,
+                "read_only": True, "adopt_namespace_meta": True})
+        return s
+
     def close(self) -> None:
         self.stop_background_precreate()
         if self.store is not None:
