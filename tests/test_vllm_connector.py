@@ -207,7 +207,14 @@ def test_kv_layer_layouts_normalise_to_planes_first():
     from tutti_b200.integration.vllm.worker import normalize_kv_layer
 
     a = torch.zeros(2, 8, 16, 4, 64)
-    assert normalize_kv_layer(a) is a
+    na = normalize_kv_layer(a)
+    assert na.shape == a.shape and na.data_ptr() == a.data_ptr() and na.is_contiguous()
+    # heads-before-tokens inside each block (a permuted, still block-dense layout)
+    raw = torch.arange(8 * 2 * 4 * 16 * 64, dtype=torch.float32).reshape(8, 2, 4, 16, 64)
+    hnd = raw.permute(0, 1, 3, 2, 4)
+    assert not hnd.is_contiguous()
+    nh = normalize_kv_layer(hnd)
+    assert nh.shape == (1, 8, 16, 8, 64) and torch.equal(nh[0, 5].reshape(-1), raw[5].reshape(-1))
     b = torch.arange(8 * 2 * 16 * 4 * 64, dtype=torch.float32).reshape(8, 2, 16, 4, 64)
     nb = normalize_kv_layer(b)
     assert nb.shape == (1, 8, 16, 8, 64) and nb.data_ptr() == b.data_ptr()
@@ -215,5 +222,5 @@ def test_kv_layer_layouts_normalise_to_planes_first():
     assert torch.equal(nb[0, 3].reshape(-1), b[3].reshape(-1))
     m = normalize_kv_layer(torch.zeros(8, 64, 576))
     assert m.shape == (1, 8, 64, 1, 576)
-    with pytest.raises(ValueError):
-        normalize_kv_layer(torch.zeros(8, 2, 16, 4, 64).transpose(0, 1).contiguous().transpose(0, 1))
+    with pytest.raises(ValueError):  # blocks interleaved with planes: not one range per block
+        normalize_kv_layer(torch.zeros(2, 8, 16, 4, 64).transpose(0, 1))

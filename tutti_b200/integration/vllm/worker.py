@@ -43,26 +43,51 @@ class _FailedLoad:
         raise self.error
 
 
+def _dense(x: torch.Tensor) -> bool:
+    """True when ``x`` covers a gap-free range of its storage (any dimension order)."""
+    expected = 1
+    for stride, size in sorted(zip(x.stride(), x.shape)):
+        if size == 1:
+            continue
+        if stride != expected:
+            return False
+        expected *= size
+    return True
+
+
+def _contiguous_view(t: torch.Tensor, shape: tuple[int, ...]) -> torch.Tensor:
+    strides, acc = [], 1
+    for n in reversed(shape):
+        strides.append(acc)
+        acc *= n
+    return torch.as_strided(t, shape, tuple(reversed(strides)), t.storage_offset())
+
+
 def normalize_kv_layer(t: torch.Tensor) -> torch.Tensor:
-    """A view of one layer's KV cache as ``[planes, num_blocks, block, heads, dim]``.
+    """A contiguous ``[planes, num_blocks, block, heads, dim]`` view of one layer's KV cache bytes.
 
     vLLM attention backends lay the cache out as ``[2, num_blocks, block, heads,
     dim]`` (K and V planes first), ``[num_blocks, 2, block, heads, dim]`` (K and V
-    of a block together) or ``[num_blocks, block, dim]`` (MLA latents). Only
-    bytes move, so a block-major layout becomes one plane whose block holds K and
-    V together.
+    of a block together) or ``[num_blocks, block, dim]`` (MLA latents), and may
+    permute the dimensions inside a block (e.g. heads before tokens). Only bytes
+    move: each block (or plane-block) must be one gap-free range at a fixed
+    stride, and the view below addresses exactly those bytes; a block-major
+    layout becomes one plane whose block holds K and V together.
     """
-    if not t.is_contiguous():
-        raise ValueError(f"KV cache layer with shape {tuple(t.shape)} is not contiguous")
-    if t.dim() == 5 and t.shape[0] == 2:
-        return t
-    if t.dim() == 5 and t.shape[1] == 2:
+    if t.dim() == 5 and t.shape[0] == 2 and t.shape[1] != 2:
+        nb = t.shape[1]
+        per = t[0, 0].numel()
+        if _dense(t[0, 0]) and t.stride(1) == per and t.stride(0) == nb * per:
+            return _contiguous_view(t, tuple(t.shape))
+    elif t.dim() == 5 and t.shape[1] == 2:
         nb, _, bs, heads, dim = t.shape
-        return t.view(1, nb, bs, 2 * heads, dim)
-    if t.dim() == 3:
+        if _dense(t[0]) and t.stride(0) == t[0].numel():
+            return _contiguous_view(t, (1, nb, bs, 2 * heads, dim))
+    elif t.dim() == 3:
         nb, bs, dim = t.shape
-        return t.view(1, nb, bs, 1, dim)
-    raise ValueError(f"unsupported KV cache layout {tuple(t.shape)}")
+        if _dense(t[0]) and t.stride(0) == t[0].numel():
+            return _contiguous_view(t, (1, nb, bs, 1, dim))
+    raise ValueError(f"unsupported KV cache layout {tuple(t.shape)} with strides {t.stride()}")
 
 
 def layer_index(name: str) -> int:
