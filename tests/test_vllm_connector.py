@@ -224,3 +224,24 @@ def test_kv_layer_layouts_normalise_to_planes_first():
     assert m.shape == (1, 8, 64, 1, 576)
     with pytest.raises(ValueError):  # blocks interleaved with planes: not one range per block
         normalize_kv_layer(torch.zeros(2, 8, 16, 4, 64).transpose(0, 1))
+
+
+def test_reference_config_schema_and_import_path():
+    import json as _json
+    import os as _os
+
+    ref_cfg = {"chunk_tokens": 512, "store": {"type": "tutti_nvme", "options": {
+        "root": "/mnt/kv/tutti-kv-{LOCAL_RANK}", "capacity": "64 GiB",
+        "preset": {"type": "raid0", "daemon_config": ["d.yaml"], "gpu_id": "{LOCAL_RANK}",
+                   "device_groups": [[0, 1]]}}}}
+    c = ConnectorConfig.from_extra(ref_cfg)
+    assert c.store_type == "tutti" and c.root == "/mnt/kv/tutti-kv-{LOCAL_RANK}" and c.capacity_bytes == 64 << 30
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"store": {"type": "tutti_nvme", "options": {"bogus": 1}}})
+    # vLLM resolves the connector class from the reference's module path
+    import importlib
+
+    mod = importlib.import_module("tutti.integration.vllm.connector")
+    from tutti_b200.integration.vllm.connector import TuttiConnectorV1
+
+    assert mod.TuttiConnectorV1 is TuttiConnectorV1

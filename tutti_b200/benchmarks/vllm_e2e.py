@@ -2,7 +2,9 @@
 
     python -m tutti_b200.benchmarks.vllm_e2e [--model DIR] [--prompt-tokens 2048]
 
-Three fresh vLLM processes share one store (vLLM's own prefix cache is off):
+Three fresh vLLM processes share one store (vLLM's own prefix cache is off); the
+connector is named by the same module path and store schema as a Tutti
+deployment (``tutti.integration.vllm.connector``, ``store.type: tutti_nvme``):
   1. ``store``: the prompt is prefilled and its full chunks are saved;
   2. ``reload``: the scheduler's cold start finds the chunks, the worker loads
      them layer by layer, and only the tail is computed
@@ -45,11 +47,12 @@ def run_phase(args) -> dict:
               max_model_len=args.prompt_tokens + 64, enable_prefix_caching=False, skip_tokenizer_init=True,
               block_size=16)
     if args.phase != "recompute":
+        # configured exactly as a Tutti deployment is (module path and store schema)
         kw["kv_transfer_config"] = KVTransferConfig(
-            kv_connector="TuttiConnectorV1", kv_connector_module_path="tutti_b200.integration.vllm.connector",
+            kv_connector="TuttiConnectorV1", kv_connector_module_path="tutti.integration.vllm.connector",
             kv_role="kv_both",
-            kv_connector_extra_config={"chunk_tokens": 256, "store": {
-                "root": args.root, "capacity_chunks": 256, "segment_file_slots": 32}})
+            kv_connector_extra_config={"chunk_tokens": 256, "store": {"type": "tutti_nvme", "options": {
+                "root": args.root, "capacity_chunks": 256, "segment_file_slots": 32}}})
     llm = LLM(**kw)
     import numpy as np
 

@@ -6,18 +6,21 @@
   load_mode                sync | async | auto (default sync: layerwise restore inside the forward)
   kv_load_failure_policy   recompute | fail (default recompute)
   store:
-    type                   tutti | memory
+    type                   tutti | memory (tutti_nvme: the reference's name for tutti)
+    options                the reference's nesting of root / capacity / preset (accepted)
     root                   namespace root (per-rank segment files under <mount>/r<rank>)
     mounts                 backing mounts, one emulated NVMe drive each (default [root])
     capacity_chunks        capacity in chunks (or capacity: "64GiB")
     segment_file_slots     slots per segment file (default 2048)
     runtime_options        options of the native runtime (leases, slots_per_lease, ...)
+    stored_format          native | fp8_block128
 Placeholders ``{LOCAL_RANK}`` / ``{RANK}`` in paths are expanded per worker.
 Parity: reference tutti/integration/vllm/factory.py:31-202 and
 config/integration/vllm/kv_transfer.json.
 """
 from __future__ import annotations
 
+import logging
 import os
 import re
 from dataclasses import dataclass, field
@@ -25,6 +28,8 @@ from dataclasses import dataclass, field
 import torch
 
 from ...models.kv_geometry import KVGeometry
+
+LOG = logging.getLogger("tutti_b200.vllm")
 
 _UNITS = {"": 1, "b": 1, "kib": 1 << 10, "mib": 1 << 20, "gib": 1 << 30, "tib": 1 << 40,
           "kb": 10 ** 3, "mb": 10 ** 6, "gb": 10 ** 9, "tb": 10 ** 12}
@@ -72,6 +77,23 @@ class ConnectorConfig:
         c.failure_policy = extra.get("kv_load_failure_policy", c.failure_policy)
         st = dict(extra.get("store", {}))
         c.store_type = st.pop("type", c.store_type)
+        if c.store_type == "tutti_nvme":
+            # the reference connector's schema: store {type: tutti_nvme, options: {root, capacity, preset}}
+            c.store_type = "tutti"
+        opts = dict(st.pop("options", {}))
+        preset = opts.pop("preset", None)
+        if preset is not None:
+            # drive presets (raid0 / device groups / daemon configs) name real NVMe devices; this
+            # build's drives are the emulated controllers over `mounts`, so only the layout is kept
+            LOG.info("[tutti] store preset %r: drives are emulated over the store's mounts",
+                     preset.get("type") if isinstance(preset, dict) else preset)
+        for k in ("root", "capacity", "capacity_chunks", "mounts", "segment_file_slots", "runtime_options",
+                  "stored_format"):
+            if k in opts:
+                st.setdefault(k, opts.pop(k))
+        opts.pop("io_stream", None)
+        if opts:
+            raise ValueError(f"unknown store options: {sorted(opts)}")
         c.root = st.pop("root", c.root)
         c.mounts = list(st.pop("mounts", []))
         c.capacity_chunks = int(st.pop("capacity_chunks", 0))
