@@ -64,7 +64,7 @@ def parse():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons during the timed region."""
+    """Samples nvidia-smi clocks/throttle reasons every 100 ms during the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -73,34 +73,39 @@ class ClockSampler:
     def __init__(self, gpus):
         self.gpus = set(gpus)
         self.rows = []
-        self._stop = threading.Event()
+        self._proc = None
         self._t = None
 
     def start(self):
         if shutil.which("nvidia-smi") is None:
             return self
+        # one long-running sampler (-lms) instead of a process per sample
+        self._proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
 
         def run():
-            while not self._stop.is_set():
+            for line in self._proc.stdout:
+                f = [x.strip() for x in line.split(",")]
                 try:
-                    out = subprocess.run(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits"],
-                                         capture_output=True, text=True, timeout=5).stdout
-                    for line in out.strip().splitlines():
-                        f = [x.strip() for x in line.split(",")]
-                        if int(f[0]) in self.gpus:
-                            self.rows.append(f)
-                except Exception:
-                    pass
-                self._stop.wait(0.2)
+                    if len(f) >= 8 and int(f[0]) in self.gpus:
+                        self.rows.append(f)
+                except ValueError:
+                    continue
 
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
+        time.sleep(0.3)  # first sample before the timed region starts
         return self
 
     def stop(self):
-        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
         if self._t:
-            self._t.join(timeout=10)
+            self._t.join(timeout=5)
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
@@ -268,7 +273,7 @@ def main():
 
     run_steps(0, args.warmup, False)
     barrier(world)
-    sampler = ClockSampler([local]).start() if rank == 0 else None
+    sampler = ClockSampler(list(range(world))).start() if rank == 0 else None  # every GPU of the job
     # device-timed: K restores back to back
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
