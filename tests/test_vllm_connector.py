@@ -245,3 +245,31 @@ def test_reference_config_schema_and_import_path():
     from tutti_b200.integration.vllm.connector import TuttiConnectorV1
 
     assert mod.TuttiConnectorV1 is TuttiConnectorV1
+
+
+def test_worker_with_main_kv_and_index_cache_entities():
+    # 3 attention layers, each with a main KV [2, nb, block, heads, dim] and an index cache [nb, block, 132] (uint8)
+    cfg = ConnectorConfig.from_extra({"chunk_tokens": CHUNK, "store": {"type": "memory", "capacity_chunks": 64}})
+    w = WorkerSide(lambda t, entity="": make_engine(cfg, t, 0, 0, 1, entity), block_size=BS, chunk_tokens=CHUNK)
+    main = [torch.randn(2, 32, BS, 2, 16) for _ in range(3)]
+    index = [torch.randint(0, 256, (32, BS, 132), dtype=torch.uint8) for _ in range(3)]
+    caches = {}
+    for i in range(3):
+        caches[f"model.layers.{i}.self_attn.attn"] = main[i]
+        caches[f"model.layers.{i}.self_attn.indexer.k_cache"] = index[i]
+    w.register_kv_caches(caches)
+    assert w.engine.names == ["self_attn.attn", "self_attn.indexer.k_cache"] or len(w.engine.engines) == 2
+    keys = [bytes([i + 40]) * 16 for i in range(2)]
+    wm = w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, [0, 1, 2, 3])]))
+    assert wm.committed == {keys[0]: 1, keys[1]: 1}
+    ref_m = [t[:, 0:4].clone() for t in main]
+    ref_i = [t[0:4].clone() for t in index]
+    meta = TuttiConnectorMetadata(2, [LoadSpec("b", keys, [20, 21, 22, 23], 16)], [])
+    w.start_load_kv(meta)
+    for name in caches:
+        w.wait_for_layer_load(name)
+    w.wait_for_save(meta)
+    for i in range(3):
+        assert torch.equal(main[i][:, 20:24], ref_m[i])
+        assert torch.equal(index[i][20:24], ref_i[i])
+    assert w.get_block_ids_with_load_errors() == set()

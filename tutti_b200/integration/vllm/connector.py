@@ -65,7 +65,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
             from ...parallel.tp_consensus import TpFailureConsensus
 
             local_rank = int(os.environ.get("LOCAL_RANK", rank))
-            self._worker = WorkerSide(lambda tensors: make_engine(self.cfg, tensors, rank, local_rank, world),
+            self._worker = WorkerSide(lambda tensors, entity="": make_engine(self.cfg, tensors, rank, local_rank,
+                                                                             world, entity),
                                       block_size=self.block_size, chunk_tokens=self.cfg.chunk_tokens,
                                       tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group),
                                       failure_policy=self.cfg.failure_policy)

@@ -128,14 +128,16 @@ def geometry_from_layers(tensors: list[torch.Tensor], chunk_tokens: int, name: s
                       planes=planes, dtype=t.dtype, chunk_tokens=chunk_tokens)
 
 
-def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, local_rank: int, world: int):
+def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, local_rank: int, world: int,
+                entity: str = ""):
+    """The engine of one KV entity (``entity`` "" is the main KV; others get their own namespace and root)."""
     from ...engine.core import KVEngine
     from ...storage.memory import MemoryKVStore
     from ...storage.tutti_store import TuttiKVStore
 
     g = geometry_from_layers(tensors, cfg.chunk_tokens, cfg.namespace or "vllm")
     cap = cfg.capacity_for(g)
-    ns = (cfg.namespace or g.fingerprint()).encode()
+    ns = (cfg.namespace or g.fingerprint()).encode() + (b"/" + entity.encode() if entity else b"")
     device = tensors[0].device
     if cfg.store_type == "memory" or device.type != "cuda":
         store = MemoryKVStore(g.chunk_bytes, capacity_chunks=cap)
@@ -144,6 +146,9 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
     else:
         root = expand(cfg.root, rank, local_rank)
         mounts = [expand(m, rank, local_rank) for m in cfg.mounts] or [os.path.join(root, "nvme0")]
+        if entity:
+            root = os.path.join(root, "entities", entity)
+            mounts = [os.path.join(m, "entities", entity) for m in mounts]
         store = TuttiKVStore(root, g, capacity_chunks=cap, mounts=mounts, device=device.index, rank=rank,
                              rank_count=world, segment_file_slots=min(cfg.segment_file_slots, max(16, cap)),
                              runtime_options=cfg.runtime_options, namespace=ns, stored_format=cfg.stored_format)

@@ -26,6 +26,7 @@ import torch
 from ...common.observability import HealthReporter
 from ...engine.completion import LoadGateError
 from ...engine.core import KVEngine
+from ...engine.entities import EntityEngines
 from ...parallel.tp_consensus import ChunkFailure, TpFailureConsensus
 from .metadata import LoadSpec, TuttiConnectorMetadata, TuttiWorkerMetadata
 
@@ -90,6 +91,13 @@ def normalize_kv_layer(t: torch.Tensor) -> torch.Tensor:
     raise ValueError(f"unsupported KV cache layout {tuple(t.shape)} with strides {t.stride()}")
 
 
+def entity_tag(name: str) -> str:
+    """The part of a layer name after its layer number (``self_attn.indexer.k_cache``)."""
+    m = re.search(r"\d+\.(.*)$", name)
+    tag = (m.group(1) if m else name) or "entity"
+    return re.sub(r"[^A-Za-z0-9_.-]", "_", tag)
+
+
 def layer_index(name: str) -> int:
     m = _LAYER_RE.findall(name)
     if not m:
@@ -98,7 +106,7 @@ def layer_index(name: str) -> int:
 
 
 class WorkerSide:
-    def __init__(self, make_engine: Callable[[list[torch.Tensor]], KVEngine], *, block_size: int,
+    def __init__(self, make_engine: Callable[..., KVEngine], *, block_size: int,
                  chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
                  consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute"):
         if failure_policy not in ("recompute", "fail"):
@@ -123,10 +131,25 @@ class WorkerSide:
 
     # -- binding --------------------------------------------------------------
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
-        names = sorted(kv_caches, key=layer_index)
+        names = sorted(kv_caches, key=lambda n: (layer_index(n), n))
         self.layer_of = {n: i for i, n in enumerate(names)}
-        tensors = [normalize_kv_layer(kv_caches[n]) for n in names]
-        self.engine = self.make_engine(tensors)
+        views = {n: normalize_kv_layer(kv_caches[n]) for n in names}
+        # entities: layers whose pages share one shape and dtype (main KV, index cache, ...)
+        groups: dict[tuple, list[str]] = {}
+        for n in names:
+            t = views[n]
+            groups.setdefault((t.shape[0],) + tuple(t.shape[2:]) + (t.dtype,), []).append(n)
+        if len(groups) == 1:
+            self.engine = self.make_engine([views[n] for n in names])
+            return
+        ordered = sorted(groups.values(), key=len, reverse=True)  # the main KV has the most layers
+        engines, where = [], {}
+        for e, members in enumerate(ordered):
+            tag = "" if e == 0 else entity_tag(members[0])
+            engines.append(self.make_engine([views[n] for n in members], tag))
+            for li, n in enumerate(members):
+                where[n] = (e, li)
+        self.engine = EntityEngines(engines, [where[n] for n in names], [entity_tag(g[0]) for g in ordered])
 
     # -- loads ----------------------------------------------------------------
     def start_load_kv(self, meta: TuttiConnectorMetadata) -> None:
