@@ -248,6 +248,7 @@ def main():
     checksum = torch.zeros(1, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream(dev)
     launches = [0]
+    io_bytes = [0, 0]  # per e2e run: H2D command arenas, D2H statuses
 
     def run_steps(first: int, count: int, e2e: bool) -> None:
         """``count`` restores with up to ``args.inflight`` submitted ahead (host work overlaps IO)."""
@@ -257,6 +258,10 @@ def main():
                 dev_table.copy_(pinned_tables[i], non_blocking=True)  # H2D: this step's block table
             comp = store.get_paged(keys, perms[i], stream=stream)
             launches[0] += len(comp._ios)
+            if e2e and backend == "nvme-gpu":
+                prof = store.runtime.last_submit_profile()  # the command arena this step copied, and back
+                io_bytes[0] += prof.get("h2d_bytes", 0)
+                io_bytes[1] += prof.get("d2h_bytes", 0)
             pending.append((i, comp))
             while len(pending) >= args.inflight:
                 j, c = pending.pop(0)
@@ -324,7 +329,10 @@ def main():
                        "emulator_idle_spins": idle_spins,
                        "l2": "inputs (4.29 GB/step) larger than L2"},
             "e2e": {"value": round(total_bytes / (e2e / 1e3) / 1e9, 3), "unit": "GB/s",
-                    "h2d_bytes_per_step": nblk * 8, "d2h_bytes_per_step": 4},
+                    # the block table (pinned) and the command arena the runtime copies to the
+                    # device each step; back: the result checksum and the per-command statuses
+                    "h2d_bytes_per_step": nblk * 8 + io_bytes[0] // args.steps,
+                    "d2h_bytes_per_step": 4 + io_bytes[1] // args.steps},
             "gpu_launches": n_launch,
             # The restore's roofline term on one GPU is the PCIe read of the staging
             # slots (a GPU zero-copy read of pinned host memory measured 51.4 GB/s on

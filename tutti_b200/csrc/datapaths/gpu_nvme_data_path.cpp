@@ -682,6 +682,8 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_coalesced).count();
     last_submit_profile_.commands = n_cmds;
     last_submit_profile_.requests = count;
+    last_submit_profile_.h2d_bytes = off_timing;
+    last_submit_profile_.d2h_bytes = copy_end - off_status;
     const std::uint64_t tok = op->generation;
     ops_[tok] = std::move(op);
     out.op = DataPathOp{tok, tok};

@@ -65,6 +65,8 @@ struct SubmitProfile {
     double coalesce_ms = 0;  // validation + coalescing into commands/pieces
     double launch_ms = 0;    // arena fill, H2D, launch, D2H enqueue
     std::uint64_t commands = 0, requests = 0;
+    std::uint64_t h2d_bytes = 0;  // command/piece/lease arena copied to the device
+    std::uint64_t d2h_bytes = 0;  // statuses (and timing stamps) copied back
 };
 
 struct IoTimingSummary {

@@ -467,6 +467,19 @@ PYBIND11_MODULE(_core, m) {
                 emu->inject(k, count, delay_us);
             },
             py::arg("device"), py::arg("kind"), py::arg("count") = 1, py::arg("delay_us") = 0)
+        .def("last_submit_profile",
+             [](PyRuntime& r) {
+                 py::dict d;
+                 if (!r.extras.gpu_path) return d;
+                 const auto sp = r.extras.gpu_path->last_submit_profile();
+                 d["coalesce_ms"] = sp.coalesce_ms;
+                 d["launch_ms"] = sp.launch_ms;
+                 d["commands"] = sp.commands;
+                 d["requests"] = sp.requests;
+                 d["h2d_bytes"] = sp.h2d_bytes;
+                 d["d2h_bytes"] = sp.d2h_bytes;
+                 return d;
+             })
         .def("io_timing",
              [](PyRuntime& r) {
                  py::dict d;
