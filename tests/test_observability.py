@@ -49,3 +49,18 @@ def test_nvtx_range_is_free_when_disabled():
     assert not obs.nvtx_enabled()
     with obs.nvtx_range("x"):
         pass
+
+
+def test_environment_switches(monkeypatch):
+    from tutti_b200.common.env import runtime_option_defaults
+    from tutti_b200.integration.vllm.factory import ConnectorConfig
+
+    monkeypatch.setenv("TUTTI_IO_TIMING", "1")
+    monkeypatch.setenv("TUTTI_POOL_WORKERS", "48")
+    assert runtime_option_defaults() == {"timing": True, "max_ctas_per_op": 48}
+    monkeypatch.setenv("TUTTI_LOAD_MODE", "auto")
+    assert ConnectorConfig.from_extra({}).load_mode == "auto"
+    assert ConnectorConfig.from_extra({"load_mode": "sync"}).load_mode == "sync"
+    monkeypatch.delenv("TUTTI_IO_TIMING")
+    monkeypatch.delenv("TUTTI_POOL_WORKERS")
+    assert runtime_option_defaults() == {}

@@ -29,6 +29,7 @@ from typing import Sequence
 import numpy as np
 import torch
 
+from ..common.env import number
 from ..common.observability import nvtx_range
 from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
@@ -135,7 +136,7 @@ class LayerwiseReadPlan:
 class KVEngine:
     def __init__(self, store, geometry: KVGeometry, *, capacity_chunks: int | None = None,
                  namespace: bytes = b"", device: int | torch.device = 0, staged: bool | None = None,
-                 io_priority: int = -1, checkpoint_interval_s: float = 60.0):
+                 io_priority: int = -1, checkpoint_interval_s: float | None = None):
         self.store = store
         self.geometry = geometry
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
@@ -146,7 +147,8 @@ class KVEngine:
         self._io_stream: torch.cuda.Stream | None = None
         self._io_priority = io_priority
         self._writes: collections.deque = collections.deque()
-        self._checkpoint_interval = checkpoint_interval_s
+        self._checkpoint_interval = (checkpoint_interval_s if checkpoint_interval_s is not None
+                                     else number("TUTTI_CHECKPOINT_INTERVAL_S", 60.0))
         self._last_checkpoint = time.monotonic()
         self.stats = collections.Counter()
 

@@ -27,6 +27,7 @@ from dataclasses import dataclass, field
 
 import torch
 
+from ...common.env import text
 from ...models.kv_geometry import KVGeometry
 
 LOG = logging.getLogger("tutti_b200.vllm")
@@ -73,7 +74,7 @@ class ConnectorConfig:
         c = cls()
         c.chunk_tokens = int(extra.get("chunk_tokens", c.chunk_tokens))
         c.namespace = str(extra.get("namespace", ""))
-        c.load_mode = extra.get("load_mode", c.load_mode)
+        c.load_mode = extra.get("load_mode", text("TUTTI_LOAD_MODE", c.load_mode))
         c.failure_policy = extra.get("kv_load_failure_policy", c.failure_policy)
         st = dict(extra.get("store", {}))
         c.store_type = st.pop("type", c.store_type)

@@ -30,6 +30,7 @@ import numpy as np
 import torch
 
 from .._native import core
+from ..common.env import integer, runtime_option_defaults
 from ..common.observability import metrics, nvtx_range
 from ..models.kv_geometry import KVGeometry
 from .base import StoreIOError
@@ -151,7 +152,7 @@ class TuttiKVStore:
         self.device = device
         self.backend = backend
         self.mounts = [str(m) for m in (mounts or [self.root / "dev0"])]
-        self.runtime_options = dict(runtime_options or {})
+        self.runtime_options = {**runtime_option_defaults(), **dict(runtime_options or {})}
         self.stored = stored_geometry(geometry, stored_format)
         if stored_format != "native" and backend != "nvme-gpu":
             raise ValueError(f"stored_format {stored_format!r} needs the nvme-gpu backend (fused in its io kernel)")
@@ -160,7 +161,8 @@ class TuttiKVStore:
                                    segment_count=geometry.num_layers, capacity_chunks=capacity_chunks,
                                    mounts=self.mounts, namespace=namespace or fp.encode(),
                                    rank=rank, rank_count=rank_count, segment_file_slots=segment_file_slots,
-                                   segment_header_bytes=segment_header_bytes, materialize=materialize)
+                                   segment_header_bytes=segment_header_bytes, materialize=materialize,
+                                   precreate_min_free_bytes=integer("TUTTI_PRECREATE_MIN_FREE_BYTES"))
         self.max_retries = max_retries
         self.runtime = None
         self._targets: dict[str, int] = {}
