@@ -65,7 +65,10 @@ def bench_fp8(args) -> dict:
     q = torch.empty(rows, 128, dtype=torch.uint8, device="cuda")
     ms = _time(lambda: _ops().fp8_quant(x, 128), args.iters, args.warmup)
     moved = x.numel() * 2 + q.numel() + rows * 4
-    return {"kernel": "quant_kernel", "rows": rows, "ms": ms, "GBps": moved / ms / 1e6}
+    qq, ss = _ops().fp8_quant(x, 128)
+    ms_d = _time(lambda: _ops().fp8_dequant(qq, ss, torch.bfloat16), args.iters, args.warmup)
+    return {"kernel": "quant16_bf16_kernel", "rows": rows, "ms": ms, "GBps": moved / ms / 1e6,
+            "dequant": {"kernel": "dequant16_bf16_kernel", "ms": ms_d, "GBps": moved / ms_d / 1e6}}
 
 
 def bench_hash(args) -> dict:

@@ -148,6 +148,83 @@ __global__ void __launch_bounds__(256) dequant_scatter_kernel(const std::uint8_t
     }
 }
 
+// bf16 fast path: a lane owns 16 consecutive values (two 16-byte loads), so 8
+// lanes share a 128-value group, a warp covers 4 groups per iteration, the
+// group maximum needs 3 shuffles, and the E4M3 conversions are done in pairs.
+// The arithmetic (scale = amax/448, values * (1/scale), saturating E4M3) is the
+// same as the per-value kernels above, so both produce identical bytes.
+__global__ void __launch_bounds__(256) quant16_bf16_kernel(const __nv_bfloat16* x, std::uint8_t* q, float* scale,
+                                                           std::uint64_t groups) {
+    const int lane = threadIdx.x & 31;
+    const std::uint64_t warps = std::uint64_t(gridDim.x) * (blockDim.x >> 5);
+    for (std::uint64_t w = std::uint64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w * 4 < groups;
+         w += warps) {
+        const std::uint64_t g = w * 4 + (lane >> 3);
+        const bool live = g < groups;
+        const std::uint64_t e = g * 128 + (lane & 7) * 16;
+        uint4 a = make_uint4(0, 0, 0, 0), b = a;
+        if (live) {
+            a = *reinterpret_cast<const uint4*>(x + e);
+            b = *reinterpret_cast<const uint4*>(x + e + 8);
+        }
+        const std::uint32_t raw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float2 v[8];
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            v[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw[i]));
+            amax = fmaxf(amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        const float s = amax > 0.f ? amax / kE4M3Max : 1.f;
+        const float inv = 1.f / s;
+        std::uint32_t out[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_fp8x2_storage_t lo =
+                __nv_cvt_float2_to_fp8x2(make_float2(v[2 * i].x * inv, v[2 * i].y * inv), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+                make_float2(v[2 * i + 1].x * inv, v[2 * i + 1].y * inv), __NV_SATFINITE, __NV_E4M3);
+            out[i] = static_cast<std::uint32_t>(lo) | (static_cast<std::uint32_t>(hi) << 16);
+        }
+        if (live) {
+            *reinterpret_cast<uint4*>(q + e) = make_uint4(out[0], out[1], out[2], out[3]);
+            if ((lane & 7) == 0) scale[g] = s;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) dequant16_bf16_kernel(const std::uint8_t* q, const float* scale,
+                                                             __nv_bfloat16* x, std::uint64_t groups) {
+    const int lane = threadIdx.x & 31;
+    const std::uint64_t warps = std::uint64_t(gridDim.x) * (blockDim.x >> 5);
+    for (std::uint64_t w = std::uint64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w * 4 < groups;
+         w += warps) {
+        const std::uint64_t g = w * 4 + (lane >> 3);
+        if (g >= groups) continue;
+        const std::uint64_t e = g * 128 + (lane & 7) * 16;
+        const uint4 p = *reinterpret_cast<const uint4*>(q + e);
+        const float s = scale[g];
+        const std::uint32_t raw[4] = {p.x, p.y, p.z, p.w};
+        std::uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const __half2_raw hr =
+                    __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(raw[i] >> (16 * h)), __NV_E4M3);
+                const float2 f = __half22float2(__half2(hr));
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(f.x * s, f.y * s);
+                out[2 * i + h] = *reinterpret_cast<std::uint32_t*>(&b2);
+            }
+        }
+        *reinterpret_cast<uint4*>(x + e) = make_uint4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<uint4*>(x + e + 8) = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+}
+
 unsigned grid_for(std::uint64_t groups, int sm_count) {
     const std::uint64_t want = (groups + 7) / 8;
     const std::uint64_t cap = static_cast<std::uint64_t>(sm_count > 0 ? sm_count : 148) * 8;
@@ -161,6 +238,11 @@ cudaError_t launch_fp8_quant(const void* x, int in_dtype, std::uint8_t* q, float
     if (group != 128 || cols % 128) return cudaErrorInvalidValue;
     const std::uint64_t groups = rows * (cols / 128);
     if (!groups) return cudaSuccess;
+    if (in_dtype == 0) {
+        quant16_bf16_kernel<<<grid_for((groups + 3) / 4, sm_count), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), q, scale, groups);
+        return cudaGetLastError();
+    }
     quant_kernel<<<grid_for(groups, sm_count), 256, 0, stream>>>(x, in_dtype, q, scale, groups);
     return cudaGetLastError();
 }
@@ -170,6 +252,11 @@ cudaError_t launch_fp8_dequant(const std::uint8_t* q, const float* scale, void* 
     if (group != 128 || cols % 128) return cudaErrorInvalidValue;
     const std::uint64_t groups = rows * (cols / 128);
     if (!groups) return cudaSuccess;
+    if (out_dtype == 0) {
+        dequant16_bf16_kernel<<<grid_for((groups + 3) / 4, sm_count), 256, 0, stream>>>(
+            q, scale, static_cast<__nv_bfloat16*>(x), groups);
+        return cudaGetLastError();
+    }
     dequant_kernel<<<grid_for(groups, sm_count), 256, 0, stream>>>(q, scale, x, out_dtype, groups);
     return cudaGetLastError();
 }
