@@ -111,3 +111,16 @@ def test_kv_checksum_matches_numpy_reference():
                     assert got[bi, l, p] == ref
     pool[0, 1, 7, 0, 0, 0] += 1
     assert ops.kv_checksum(pool, blocks)[1, 0, 1].item() != int(got[1, 0, 1].astype(np.int64))
+
+
+def test_checksum_segment_parallel_path_equals_per_item_path():
+    # 33,280-byte pages: two full 16 KiB segments and a partial one
+    from tutti_b200._native import ops as _ops
+
+    pool = torch.randn(3, 2, 10, 16, 8, 130, dtype=torch.bfloat16, device="cuda")
+    blocks = torch.tensor([0, 4, 9], device="cuda")
+    fast = ops.kv_checksum(pool, blocks)
+    ptrs = ops._block_ptrs(pool, blocks, torch.arange(3))
+    items = ops._items(ptrs, torch.zeros_like(ptrs), pool[0, 0, 0].numel() * 2)
+    slow = _ops().checksum(items, 0).reshape(ptrs.shape)
+    assert torch.equal(fast, slow)

@@ -102,7 +102,7 @@ def bench_checksum(args) -> dict:
     blocks = torch.arange(nb, device="cuda")
     ms = _time(lambda: ops.kv_checksum(pool, blocks), args.iters, args.warmup)
     nbytes = pool.numel() * 2
-    return {"kernel": "checksum_kernel", "bytes": nbytes, "ms": ms, "GBps": nbytes / ms / 1e6}
+    return {"kernel": "checksum_uniform_kernel", "bytes": nbytes, "ms": ms, "GBps": nbytes / ms / 1e6}
 
 
 def bench_io(args) -> dict:

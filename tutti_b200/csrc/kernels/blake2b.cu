@@ -167,7 +167,63 @@ __global__ void __launch_bounds__(256) checksum_kernel(const CopyItem* items, st
     }
 }
 
+// Items of one size: warps take 16 KiB segments of items (all warps busy
+// however few or large the items are), read them with 16-byte loads four deep
+// and add each segment's sum into its item's digest. Sums commute, so the
+// digest equals checksum_kernel's.
+constexpr std::uint64_t kSegBytes = 16384;
+
+__global__ void __launch_bounds__(256) checksum_uniform_kernel(const CopyItem* items, std::uint32_t n,
+                                                               std::uint64_t bytes, std::uint64_t* out) {
+    const int lane = threadIdx.x & 31;
+    const std::uint64_t segs = (bytes + kSegBytes - 1) / kSegBytes;
+    const std::uint64_t units = std::uint64_t(n) * segs;
+    const std::uint64_t warps = std::uint64_t(gridDim.x) * (blockDim.x >> 5);
+    const std::uint64_t words = bytes / 8;
+    for (std::uint64_t u = std::uint64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units;
+         u += warps) {
+        const std::uint64_t i = u / segs, seg = u % segs;
+        const std::uint64_t* p = reinterpret_cast<const std::uint64_t*>(items[i].src);
+        const std::uint64_t w0 = seg * (kSegBytes / 8);
+        const std::uint64_t w1 = min(words, w0 + kSegBytes / 8);
+        std::uint64_t acc = 0;
+        // pairs of words (16 bytes) per lane, 4 in flight
+        std::uint64_t w = w0 + 2 * lane;
+        for (; w + 2 * 32 * 3 + 1 < w1; w += 2 * 32 * 4) {
+            uint4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const uint4*>(p + w + 64 * k);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const std::uint64_t a = (std::uint64_t(v[k].y) << 32) | v[k].x;
+                const std::uint64_t b = (std::uint64_t(v[k].w) << 32) | v[k].z;
+                const std::uint64_t wi = w + 64 * k;
+                acc += fmix64(a ^ (wi * 0x9E3779B97F4A7C15ull)) + fmix64(b ^ ((wi + 1) * 0x9E3779B97F4A7C15ull));
+            }
+        }
+        for (; w < w1; w += 64) {
+            acc += fmix64(p[w] ^ (w * 0x9E3779B97F4A7C15ull));
+            if (w + 1 < w1) acc += fmix64(p[w + 1] ^ ((w + 1) * 0x9E3779B97F4A7C15ull));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) atomicAdd(reinterpret_cast<unsigned long long*>(out + i), static_cast<unsigned long long>(acc));
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_checksum_uniform(const CopyItem* items, std::uint32_t n, std::uint64_t bytes, std::uint64_t* out,
+                                    cudaStream_t stream) {
+    if (!n) return cudaSuccess;
+    if (bytes % 16) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(out, 0, std::size_t(n) * sizeof(std::uint64_t), stream);
+    if (e != cudaSuccess) return e;
+    const std::uint64_t units = std::uint64_t(n) * ((bytes + kSegBytes - 1) / kSegBytes);
+    const unsigned grid = static_cast<unsigned>(std::max<std::uint64_t>(1, std::min<std::uint64_t>((units + 7) / 8, 148 * 8)));
+    checksum_uniform_kernel<<<grid, 256, 0, stream>>>(items, n, bytes, out);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_prefix_hash(const std::int64_t* tokens, const std::int64_t* starts, const std::int64_t* lengths,
                                const std::uint8_t* parents, const std::int32_t* parent_len,

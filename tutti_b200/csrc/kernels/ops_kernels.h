@@ -47,6 +47,9 @@ cudaError_t launch_prefix_hash(const std::int64_t* tokens, const std::int64_t* s
 
 // 64-bit order-sensitive checksum of each item (bytes multiple of 8).
 cudaError_t launch_checksum(const CopyItem* items, std::uint32_t n, std::uint64_t* out, cudaStream_t stream);
+// Same digests when every item has `bytes` bytes (a multiple of 16, 16-byte aligned sources).
+cudaError_t launch_checksum_uniform(const CopyItem* items, std::uint32_t n, std::uint64_t bytes, std::uint64_t* out,
+                                    cudaStream_t stream);
 
 }  // namespace ops
 }  // namespace tutti

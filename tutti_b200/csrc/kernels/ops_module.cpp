@@ -117,16 +117,20 @@ at::Tensor prefix_hash(const at::Tensor& tokens, const at::Tensor& starts, const
     return keys;
 }
 
-at::Tensor checksum(const at::Tensor& items) {
+at::Tensor checksum(const at::Tensor& items, int64_t uniform_bytes) {
     TORCH_CHECK(items.is_cuda() && items.scalar_type() == at::kLong && items.dim() == 2 && items.size(1) == 3,
                 "items: int64 CUDA [n, 3]");
     const c10::cuda::CUDAGuard guard(items.device());
     auto out = at::empty({items.size(0)}, items.options());
-    check_cuda(launch_checksum(reinterpret_cast<const CopyItem*>(items.data_ptr<int64_t>()),
-                               static_cast<std::uint32_t>(items.size(0)),
-                               reinterpret_cast<std::uint64_t*>(out.data_ptr<int64_t>()),
-                               at::cuda::getCurrentCUDAStream()),
-               "checksum");
+    const auto* it = reinterpret_cast<const CopyItem*>(items.data_ptr<int64_t>());
+    auto* o = reinterpret_cast<std::uint64_t*>(out.data_ptr<int64_t>());
+    const auto n = static_cast<std::uint32_t>(items.size(0));
+    if (uniform_bytes > 0 && uniform_bytes % 16 == 0)
+        check_cuda(launch_checksum_uniform(it, n, static_cast<std::uint64_t>(uniform_bytes), o,
+                                           at::cuda::getCurrentCUDAStream()),
+                   "checksum");
+    else
+        check_cuda(launch_checksum(it, n, o, at::cuda::getCurrentCUDAStream()), "checksum");
     return out;
 }
 
@@ -195,7 +199,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("fp8_gather_quant", &fp8_gather_quant);
     m.def("fp8_dequant_scatter", &fp8_dequant_scatter);
     m.def("prefix_hash", &prefix_hash);
-    m.def("checksum", &checksum);
+    m.def("checksum", &checksum, py::arg("items"), py::arg("uniform_bytes") = 0);
     m.def("ipc_export", &ipc_export);
     m.def("ipc_open", &ipc_open);
     m.def("ipc_close", &ipc_close);

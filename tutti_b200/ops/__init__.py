@@ -165,7 +165,8 @@ def kv_checksum(pool: torch.Tensor, block_ids: torch.Tensor, layers: Sequence[in
     plane_bytes = pool[0, 0, 0].numel() * pool.element_size()
     ptrs = _block_ptrs(pool, block_ids, layers_t)
     items = _items(ptrs, torch.zeros_like(ptrs), plane_bytes)
-    return _ops().checksum(items).reshape(ptrs.shape)
+    # every item is one plane page: the segment-parallel kernel applies when pages are 16-byte multiples
+    return _ops().checksum(items, plane_bytes if plane_bytes % 16 == 0 else 0).reshape(ptrs.shape)
 
 
 def ipc_export(t: torch.Tensor):
