@@ -28,12 +28,21 @@ __constant__ std::uint64_t kIV[8] = {0x6a09e667f3bcc908ull, 0xbb67ae8584caa73bul
                                      0xa54ff53a5f1d36f1ull, 0x510e527fade682d1ull, 0x9b05688c2b3e6c1full,
                                      0x1f83d9abfb41bd6bull, 0x5be0cd19137e2179ull};
 
-__constant__ std::uint8_t kSigma[10][16] = {
+// The message schedule, evaluated at compile time: with every round unrolled,
+// each m[...] index is a constant and the message block stays in registers.
+__host__ __device__ constexpr std::uint8_t sigma_of(int r, int i) {
+    constexpr std::uint8_t t[10][16] = {
     {0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15}, {14, 10, 4, 8, 9, 15, 13, 6, 1, 12, 0, 2, 11, 7, 5, 3},
     {11, 8, 12, 0, 5, 2, 15, 13, 10, 14, 3, 6, 7, 1, 9, 4}, {7, 9, 3, 1, 13, 12, 11, 14, 2, 6, 5, 10, 4, 0, 15, 8},
     {9, 0, 5, 7, 2, 4, 10, 15, 14, 1, 11, 12, 6, 8, 3, 13}, {2, 12, 6, 10, 0, 11, 8, 3, 4, 13, 7, 5, 15, 14, 1, 9},
     {12, 5, 1, 15, 14, 13, 4, 10, 0, 7, 6, 3, 9, 2, 8, 11}, {13, 11, 7, 14, 12, 1, 3, 9, 5, 0, 15, 4, 8, 6, 2, 10},
     {6, 15, 14, 9, 11, 3, 0, 8, 12, 2, 13, 7, 1, 4, 10, 5}, {10, 2, 8, 4, 7, 6, 1, 5, 15, 11, 9, 14, 3, 12, 13, 0}};
+    return t[r][i];
+}
+template <int R, int I>
+struct Sig {
+    static constexpr int value = sigma_of(R % 10, I);
+};
 
 __device__ __forceinline__ std::uint64_t rotr(std::uint64_t x, int n) { return (x >> n) | (x << (64 - n)); }
 
@@ -48,6 +57,18 @@ __device__ __forceinline__ void mix(std::uint64_t* v, int a, int b, int c, int d
     v[b] = rotr(v[b] ^ v[c], 63);
 }
 
+template <int R>
+__device__ __forceinline__ void round_of(std::uint64_t* v, const std::uint64_t* m) {
+    mix(v, 0, 4, 8, 12, m[Sig<R, 0>::value], m[Sig<R, 1>::value]);
+    mix(v, 1, 5, 9, 13, m[Sig<R, 2>::value], m[Sig<R, 3>::value]);
+    mix(v, 2, 6, 10, 14, m[Sig<R, 4>::value], m[Sig<R, 5>::value]);
+    mix(v, 3, 7, 11, 15, m[Sig<R, 6>::value], m[Sig<R, 7>::value]);
+    mix(v, 0, 5, 10, 15, m[Sig<R, 8>::value], m[Sig<R, 9>::value]);
+    mix(v, 1, 6, 11, 12, m[Sig<R, 10>::value], m[Sig<R, 11>::value]);
+    mix(v, 2, 7, 8, 13, m[Sig<R, 12>::value], m[Sig<R, 13>::value]);
+    mix(v, 3, 4, 9, 14, m[Sig<R, 14>::value], m[Sig<R, 15>::value]);
+}
+
 __device__ void compress(std::uint64_t h[8], const std::uint64_t m[16], std::uint64_t t, bool last) {
     std::uint64_t v[16];
 #pragma unroll
@@ -57,18 +78,18 @@ __device__ void compress(std::uint64_t h[8], const std::uint64_t m[16], std::uin
     }
     v[12] ^= t;  // byte counter (messages here are far below 2^64 bytes)
     if (last) v[14] = ~v[14];
-#pragma unroll 1
-    for (int r = 0; r < 12; ++r) {
-        const std::uint8_t* s = kSigma[r % 10];
-        mix(v, 0, 4, 8, 12, m[s[0]], m[s[1]]);
-        mix(v, 1, 5, 9, 13, m[s[2]], m[s[3]]);
-        mix(v, 2, 6, 10, 14, m[s[4]], m[s[5]]);
-        mix(v, 3, 7, 11, 15, m[s[6]], m[s[7]]);
-        mix(v, 0, 5, 10, 15, m[s[8]], m[s[9]]);
-        mix(v, 1, 6, 11, 12, m[s[10]], m[s[11]]);
-        mix(v, 2, 7, 8, 13, m[s[12]], m[s[13]]);
-        mix(v, 3, 4, 9, 14, m[s[14]], m[s[15]]);
-    }
+    round_of<0>(v, m);
+    round_of<1>(v, m);
+    round_of<2>(v, m);
+    round_of<3>(v, m);
+    round_of<4>(v, m);
+    round_of<5>(v, m);
+    round_of<6>(v, m);
+    round_of<7>(v, m);
+    round_of<8>(v, m);
+    round_of<9>(v, m);
+    round_of<10>(v, m);
+    round_of<11>(v, m);
 #pragma unroll
     for (int i = 0; i < 8; ++i) h[i] ^= v[i] ^ v[i + 8];
 }
@@ -92,6 +113,7 @@ __device__ void hash_chunk(const std::uint64_t* parent, int parent_words, const 
     while (w < total_words) {
         const std::uint64_t remaining = total_words - w;
         const int take = remaining > 16 ? 16 : static_cast<int>(remaining);
+#pragma unroll
         for (int i = 0; i < 16; ++i) {
             const std::uint64_t k = w + i;
             if (i < take)
