@@ -2,8 +2,8 @@
 //
 // prefix_hash: the chained chunk keys of the semantic index,
 //   key_i = BLAKE2b-128(parent_{i-1} || le64(tokens of chunk i)),
-// computed on the GPU from token ids already in HBM, one request per thread
-// (the chain is sequential; requests are independent). BLAKE2b follows
+// computed on the GPU from token ids already in HBM, one request per quad of
+// lanes (the chain is sequential; the four G functions of a round step are not). BLAKE2b follows
 // RFC 7693 (unkeyed, digest length 16): the SHA-512 initial values, the
 // ten-row message schedule, rotations 32/24/16/63, 12 rounds, the final-block
 // flag, and a little-endian byte counter. The parent is 0 bytes (empty
@@ -46,114 +46,150 @@ struct Sig {
 
 __device__ __forceinline__ std::uint64_t rotr(std::uint64_t x, int n) { return (x >> n) | (x << (64 - n)); }
 
-__device__ __forceinline__ void mix(std::uint64_t* v, int a, int b, int c, int d, std::uint64_t x, std::uint64_t y) {
-    v[a] = v[a] + v[b] + x;
-    v[d] = rotr(v[d] ^ v[a], 32);
-    v[c] = v[c] + v[d];
-    v[b] = rotr(v[b] ^ v[c], 24);
-    v[a] = v[a] + v[b] + y;
-    v[d] = rotr(v[d] ^ v[a], 16);
-    v[c] = v[c] + v[d];
-    v[b] = rotr(v[b] ^ v[c], 63);
+// One request per quad of lanes. Lane q of the quad holds column q of the
+// 4x4 state (v[q], v[4+q], v[8+q], v[12+q]), so the four G functions of a
+// column step run in parallel; for the diagonal step b, c and d are rotated
+// across the quad by 1, 2 and 3 lanes with shuffles and rotated back after.
+// The 128-byte message block sits in shared memory (one block per quad), and
+// the schedule row of each round is a compile-time constant packed in nibbles.
+__host__ __device__ constexpr std::uint64_t sigma_row(int r) {
+    std::uint64_t v = 0;
+    for (int i = 0; i < 16; ++i) v |= static_cast<std::uint64_t>(sigma_of(r, i)) << (4 * i);
+    return v;
 }
+template <int R>
+struct Row {
+    static constexpr std::uint64_t value = sigma_row(R % 10);
+};
+
+__device__ __forceinline__ void g(std::uint64_t& a, std::uint64_t& b, std::uint64_t& c, std::uint64_t& d,
+                                  std::uint64_t x, std::uint64_t y) {
+    a = a + b + x;
+    d = rotr(d ^ a, 32);
+    c = c + d;
+    b = rotr(b ^ c, 24);
+    a = a + b + y;
+    d = rotr(d ^ a, 16);
+    c = c + d;
+    b = rotr(b ^ c, 63);
+}
+
+struct Quad {
+    unsigned mask;  // the quad's four lanes
+    int base;       // lane index of the quad's lane 0
+    int q;          // this lane's column
+};
 
 template <int R>
-__device__ __forceinline__ void round_of(std::uint64_t* v, const std::uint64_t* m) {
-    mix(v, 0, 4, 8, 12, m[Sig<R, 0>::value], m[Sig<R, 1>::value]);
-    mix(v, 1, 5, 9, 13, m[Sig<R, 2>::value], m[Sig<R, 3>::value]);
-    mix(v, 2, 6, 10, 14, m[Sig<R, 4>::value], m[Sig<R, 5>::value]);
-    mix(v, 3, 7, 11, 15, m[Sig<R, 6>::value], m[Sig<R, 7>::value]);
-    mix(v, 0, 5, 10, 15, m[Sig<R, 8>::value], m[Sig<R, 9>::value]);
-    mix(v, 1, 6, 11, 12, m[Sig<R, 10>::value], m[Sig<R, 11>::value]);
-    mix(v, 2, 7, 8, 13, m[Sig<R, 12>::value], m[Sig<R, 13>::value]);
-    mix(v, 3, 4, 9, 14, m[Sig<R, 14>::value], m[Sig<R, 15>::value]);
+__device__ __forceinline__ void round_quad(std::uint64_t& a, std::uint64_t& b, std::uint64_t& c, std::uint64_t& d,
+                                           const std::uint64_t* m, const Quad& k) {
+    constexpr std::uint64_t row = Row<R>::value;
+    g(a, b, c, d, m[(row >> (8 * k.q)) & 15], m[(row >> (8 * k.q + 4)) & 15]);
+    std::uint64_t b1 = __shfl_sync(k.mask, b, k.base + ((k.q + 1) & 3));
+    std::uint64_t c1 = __shfl_sync(k.mask, c, k.base + ((k.q + 2) & 3));
+    std::uint64_t d1 = __shfl_sync(k.mask, d, k.base + ((k.q + 3) & 3));
+    g(a, b1, c1, d1, m[(row >> (32 + 8 * k.q)) & 15], m[(row >> (36 + 8 * k.q)) & 15]);
+    b = __shfl_sync(k.mask, b1, k.base + ((k.q + 3) & 3));
+    c = __shfl_sync(k.mask, c1, k.base + ((k.q + 2) & 3));
+    d = __shfl_sync(k.mask, d1, k.base + ((k.q + 1) & 3));
 }
 
-__device__ void compress(std::uint64_t h[8], const std::uint64_t m[16], std::uint64_t t, bool last) {
-    std::uint64_t v[16];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        v[i] = h[i];
-        v[i + 8] = kIV[i];
-    }
-    v[12] ^= t;  // byte counter (messages here are far below 2^64 bytes)
-    if (last) v[14] = ~v[14];
-    round_of<0>(v, m);
-    round_of<1>(v, m);
-    round_of<2>(v, m);
-    round_of<3>(v, m);
-    round_of<4>(v, m);
-    round_of<5>(v, m);
-    round_of<6>(v, m);
-    round_of<7>(v, m);
-    round_of<8>(v, m);
-    round_of<9>(v, m);
-    round_of<10>(v, m);
-    round_of<11>(v, m);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] ^= v[i] ^ v[i + 8];
+// h0 = h[q], h1 = h[4+q] of this lane.
+__device__ __forceinline__ void compress_quad(std::uint64_t& h0, std::uint64_t& h1, const std::uint64_t* m,
+                                              std::uint64_t t, bool last, const Quad& k) {
+    std::uint64_t a = h0, b = h1, c = kIV[k.q], d = kIV[4 + k.q];
+    if (k.q == 0) d ^= t;           // v[12]: byte counter (far below 2^64 bytes here)
+    if (k.q == 2 && last) d = ~d;   // v[14]: final-block flag
+    round_quad<0>(a, b, c, d, m, k);
+    round_quad<1>(a, b, c, d, m, k);
+    round_quad<2>(a, b, c, d, m, k);
+    round_quad<3>(a, b, c, d, m, k);
+    round_quad<4>(a, b, c, d, m, k);
+    round_quad<5>(a, b, c, d, m, k);
+    round_quad<6>(a, b, c, d, m, k);
+    round_quad<7>(a, b, c, d, m, k);
+    round_quad<8>(a, b, c, d, m, k);
+    round_quad<9>(a, b, c, d, m, k);
+    round_quad<10>(a, b, c, d, m, k);
+    round_quad<11>(a, b, c, d, m, k);
+    h0 ^= a ^ c;
+    h1 ^= b ^ d;
 }
 
-// BLAKE2b-128 of parent (0 or 2 words) followed by `n` little-endian int64 tokens.
-__device__ void hash_chunk(const std::uint64_t* parent, int parent_words, const std::int64_t* tok, std::uint32_t n,
-                           std::uint64_t out[2]) {
-    std::uint64_t h[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = kIV[i];
-    h[0] ^= 0x01010000ull ^ 16ull;  // depth 1, fanout 1, no key, 16-byte digest
+// BLAKE2b-128 of the parent (0 or 2 words p0, p1) followed by `n` little-endian
+// int64 tokens; every lane of the quad returns the digest.
+__device__ void hash_chunk_quad(std::uint64_t p0, std::uint64_t p1, int parent_words, const std::int64_t* tok,
+                                std::uint32_t n, std::uint64_t* m, const Quad& k, std::uint64_t out[2]) {
+    std::uint64_t h0 = kIV[k.q], h1 = kIV[4 + k.q];
+    if (k.q == 0) h0 ^= 0x01010000ull ^ 16ull;  // depth 1, fanout 1, no key, 16-byte digest
     const std::uint64_t total_words = parent_words + n;
     const std::uint64_t total_bytes = total_words * 8;
-    std::uint64_t m[16];
     std::uint64_t w = 0;
     if (total_words == 0) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) m[i] = 0;
-        compress(h, m, 0, true);
+        for (int j = 0; j < 4; ++j) m[k.q + 4 * j] = 0;
+        __syncwarp(k.mask);
+        compress_quad(h0, h1, m, 0, true, k);
     }
     while (w < total_words) {
         const std::uint64_t remaining = total_words - w;
         const int take = remaining > 16 ? 16 : static_cast<int>(remaining);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const std::uint64_t k = w + i;
+        for (int j = 0; j < 4; ++j) {
+            const int i = k.q + 4 * j;
+            const std::uint64_t idx = w + i;
+            std::uint64_t val = 0;
             if (i < take)
-                m[i] = k < static_cast<std::uint64_t>(parent_words) ? parent[k]
-                                                                     : static_cast<std::uint64_t>(tok[k - parent_words]);
-            else
-                m[i] = 0;
+                val = idx < static_cast<std::uint64_t>(parent_words)
+                          ? (idx == 0 ? p0 : p1)
+                          : static_cast<std::uint64_t>(tok[idx - parent_words]);
+            m[i] = val;
         }
+        __syncwarp(k.mask);
         w += take;
         const bool last = w == total_words;
-        compress(h, m, last ? total_bytes : w * 8, last);
+        compress_quad(h0, h1, m, last ? total_bytes : w * 8, last, k);
+        __syncwarp(k.mask);  // the block is read by every lane before the next one overwrites it
     }
-    out[0] = h[0];
-    out[1] = h[1];
+    out[0] = __shfl_sync(k.mask, h0, k.base);      // h[0]: lane 0's h[q]
+    out[1] = __shfl_sync(k.mask, h0, k.base + 1);  // h[1]: lane 1's h[q]
 }
 
-__global__ void prefix_hash_kernel(const std::int64_t* tokens, const std::int64_t* starts, const std::int64_t* lengths,
-                                   const std::uint8_t* parents, const std::int32_t* parent_len,
-                                   const std::int64_t* key_offsets, std::uint8_t* keys, std::uint32_t requests,
-                                   std::uint32_t chunk_tokens) {
-    const std::uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= requests) return;
+constexpr int kHashThreads = 128;  // 32 requests per CTA
+
+__global__ void __launch_bounds__(kHashThreads) prefix_hash_kernel(
+    const std::int64_t* tokens, const std::int64_t* starts, const std::int64_t* lengths, const std::uint8_t* parents,
+    const std::int32_t* parent_len, const std::int64_t* key_offsets, std::uint8_t* keys, std::uint32_t requests,
+    std::uint32_t chunk_tokens) {
+    __shared__ std::uint64_t msg[kHashThreads / 4][16];
+    const int lane = threadIdx.x & 31;
+    Quad k;
+    k.q = lane & 3;
+    k.base = lane & ~3;
+    k.mask = 0xFu << k.base;
+    const std::uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+    if (r >= requests) return;  // the whole quad leaves together
+    std::uint64_t* m = msg[threadIdx.x >> 2];
     const std::int64_t* tok = tokens + starts[r];
     const std::int64_t nchunks = lengths[r] / chunk_tokens;
-    std::uint64_t parent[2] = {0, 0};
+    std::uint64_t p0 = 0, p1 = 0;
     int pw = 0;
     if (parent_len[r] == 16) {
         const std::uint64_t* p = reinterpret_cast<const std::uint64_t*>(parents + 16ull * r);
-        parent[0] = p[0];
-        parent[1] = p[1];
+        p0 = p[0];
+        p1 = p[1];
         pw = 2;
     }
     std::uint64_t* out = reinterpret_cast<std::uint64_t*>(keys + 16ull * key_offsets[r]);
     for (std::int64_t c = 0; c < nchunks; ++c) {
         std::uint64_t d[2];
-        hash_chunk(parent, pw, tok + c * chunk_tokens, chunk_tokens, d);
-        out[2 * c] = d[0];
-        out[2 * c + 1] = d[1];
-        parent[0] = d[0];
-        parent[1] = d[1];
+        hash_chunk_quad(p0, p1, pw, tok + c * chunk_tokens, chunk_tokens, m, k, d);
+        if (k.q == 0) {
+            out[2 * c] = d[0];
+            out[2 * c + 1] = d[1];
+        }
+        p0 = d[0];
+        p1 = d[1];
         pw = 2;
     }
 }
@@ -252,8 +288,8 @@ cudaError_t launch_prefix_hash(const std::int64_t* tokens, const std::int64_t* s
                                const std::int64_t* key_offsets, std::uint8_t* keys, std::uint32_t requests,
                                std::uint32_t chunk_tokens, cudaStream_t stream) {
     if (!requests) return cudaSuccess;
-    const unsigned threads = 64;
-    prefix_hash_kernel<<<(requests + threads - 1) / threads, threads, 0, stream>>>(
+    const std::uint64_t threads = 4ull * requests;  // a quad of lanes per request
+    prefix_hash_kernel<<<static_cast<unsigned>((threads + kHashThreads - 1) / kHashThreads), kHashThreads, 0, stream>>>(
         tokens, starts, lengths, parents, parent_len, key_offsets, keys, requests, chunk_tokens);
     return cudaGetLastError();
 }
