@@ -40,3 +40,12 @@ def test_prefill_model_grows_with_tokens_and_shrinks_with_tp():
     assert prefill_seconds(8192, 0, 1, pk, 0.5) > 2 * one * 0.99
     assert abs(prefill_seconds(4096, 0, 8, pk, 0.5) - one / 8) < 1e-12
     assert prefill_seconds(512, 32768, 1, pk, 0.5) < prefill_seconds(32768 + 512, 0, 1, pk, 0.5)
+
+
+def test_io_sweep_shapes_cover_the_reference_batches():
+    from tutti_b200.benchmarks.io_sweep import shape_for
+
+    for target in (128, 486, 972, 1944, 3888):
+        chunks, layers = shape_for(target)
+        pages = chunks * 16 * layers
+        assert layers <= 32 and abs(pages - target) / target < 0.02

@@ -68,3 +68,32 @@ def test_layerwise_restore_then_prefill_matches_recompute(tmp_path, staged):
         torch.testing.assert_close(out.float(), full.float(), atol=3e-2, rtol=3e-2)
     finally:
         store.close()
+
+
+def test_writes_on_their_own_stream_overlap_reads(tmp_path):
+    """defer_writes_after_reads=False: a store on the write stream runs beside a restore on the IO stream."""
+    g = CFG.geometry(block_size=16, chunk_tokens=64)
+    store = TuttiKVStore(tmp_path, g, capacity_chunks=64, mounts=[str(tmp_path / "nvme0")], device=0,
+                         segment_file_slots=16, runtime_options={"leases": 16, "max_ctas_per_op": 4})
+    store.open()
+    try:
+        pool = torch.randn(g.pool_shape(128), device="cuda").to(torch.bfloat16)
+        eng = KVEngine(store, g, device=0, defer_writes_after_reads=False)
+        eng.bind(pool)
+        assert eng.write_stream is not eng.io_stream
+        keys_a = chunk_keys_for_tokens(list(range(256)), 64)
+        keys_b = chunk_keys_for_tokens(list(range(1000, 1256)), 64)
+        ta, tb, ta2, tb2 = (torch.arange(s, s + 16) for s in (0, 16, 32, 48))
+        eng.store_chunks(keys_a, ta).wait()
+        read = eng.load(keys_a, ta2)  # IO stream
+        write = eng.store_chunks(keys_b, tb)  # write stream, concurrently
+        read.wait()
+        write.wait()
+        eng.wait_idle()
+        torch.cuda.synchronize()
+        assert torch.equal(pool[:, :, ta2], pool[:, :, ta])
+        eng.load(keys_b, tb2).wait()
+        torch.cuda.synchronize()
+        assert torch.equal(pool[:, :, tb2], pool[:, :, tb])
+    finally:
+        store.close()

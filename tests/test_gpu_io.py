@@ -283,3 +283,57 @@ def test_restore_on_a_green_context_io_stream(tmp_path):
     finally:
         st.close()
         g.close()
+
+
+def test_data_path_host_fault_seams(tmp_path):
+    """Launch failure: nothing issued, all rejected; event-record failure: settled from statuses; query error: FAILED."""
+    st = make(tmp_path, max_ctas_per_op=2)  # the op failed by a query error keeps its (at most 2) leases
+    try:
+        nb = 64
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(2 * 64)), 64, namespace=b"seams")
+        st.put_paged(keys, np.arange(8).reshape(2, 4)).wait()
+        ref = pool[:, :, 0:8].clone()
+        free = st.runtime.free_leases()
+
+        st.runtime.testing_inject_data_path("launch_failure", 1)
+        with pytest.raises(StoreIOError) as ei:
+            st.get_paged(keys, (np.arange(8) + 8).reshape(2, 4)).wait()
+        assert ei.value.kind == "rejected" and "injected" in str(ei.value)
+        assert st.runtime.free_leases() == free  # nothing was issued, every lease came back
+
+        pool[:, :, 16:24].zero_()
+        st.runtime.testing_inject_data_path("event_record_failure", 1)
+        st.get_paged(keys, (np.arange(8) + 16).reshape(2, 4)).wait()  # the IO ran: settled synchronously
+        assert torch.equal(pool[:, :, 16:24], ref)
+
+        st.runtime.testing_inject_data_path("query_error", 1)
+        with pytest.raises(StoreIOError):
+            st.get_paged(keys, (np.arange(8) + 24).reshape(2, 4)).wait()
+        # the path still serves restores (the failed op keeps its leases: its device state is unknown)
+        pool[:, :, 32:40].zero_()
+        st.get_paged(keys, (np.arange(8) + 32).reshape(2, 4)).wait()
+        assert torch.equal(pool[:, :, 32:40], ref)
+    finally:
+        st.close()
+
+
+def test_event_record_failure_on_a_split_read_settles_after_the_drain(tmp_path):
+    st = make(tmp_path, async_completion=True)
+    try:
+        nb = 64
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(2 * 64)), 64, namespace=b"seams2")
+        st.put_paged(keys, np.arange(8).reshape(2, 4)).wait()
+        ref = pool[:, :, 0:8].clone()
+        pool[:, :, 8:16].zero_()
+        st.runtime.testing_inject_data_path("event_record_failure", 1)
+        comp = st.get_paged(keys, (np.arange(8) + 8).reshape(2, 4))
+        consumer = torch.cuda.Stream()
+        comp.enqueue_wait(consumer)  # a settled op needs no drain: nothing is launched
+        comp.wait()
+        assert torch.equal(pool[:, :, 8:16], ref)
+    finally:
+        st.close()

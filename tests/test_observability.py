@@ -64,3 +64,31 @@ def test_environment_switches(monkeypatch):
     monkeypatch.delenv("TUTTI_IO_TIMING")
     monkeypatch.delenv("TUTTI_POOL_WORKERS")
     assert runtime_option_defaults() == {}
+
+
+def test_write_ordering_and_prp_mode_switches(monkeypatch):
+    import pytest
+
+    from tutti_b200.common.env import prp_mode
+    from tutti_b200.engine.core import resolve_defer_writes
+    from tutti_b200.integration.vllm.factory import ConnectorConfig
+
+    monkeypatch.delenv("TUTTI_DEFER_WRITES_AFTER_READS", raising=False)
+    assert resolve_defer_writes(None) is True
+    monkeypatch.setenv("TUTTI_DEFER_WRITES_AFTER_READS", "0")
+    assert resolve_defer_writes(None) is False
+    assert resolve_defer_writes(True) is True  # an explicit option wins over the variable
+    with pytest.raises(ValueError):
+        resolve_defer_writes("yes")
+    cfg = ConnectorConfig.from_extra({"store": {"type": "tutti_nvme", "options": {"defer_writes_after_reads": False}}})
+    assert cfg.defer_writes_after_reads is False
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"store": {"options": {"defer_writes_after_reads": 1}}})
+
+    monkeypatch.delenv("TUTTI_PRP_MODE", raising=False)
+    assert prp_mode() == "dynamic"
+    monkeypatch.setenv("TUTTI_PRP_MODE", "FULL_PREBUILD")
+    assert prp_mode() == "full_prebuild"
+    monkeypatch.setenv("TUTTI_PRP_MODE", "lazy")
+    with pytest.raises(ValueError):
+        prp_mode()

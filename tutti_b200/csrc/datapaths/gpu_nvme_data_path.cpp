@@ -643,19 +643,34 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         nvtxRangePushA(name);
     }
     Status cs = cuda_status(cudaMemcpyAsync(d, h, off_timing, cudaMemcpyHostToDevice, s), "H2D commands");
-    if (cs.ok()) cs = cuda_status(io::launch_nvme_io(kp, take, s), "io kernel launch");
+    bool launched = false;
+    if (cs.ok()) {
+        if (take_test_fault(TestFault::LAUNCH_FAILURE)) {
+            cs = {StatusCode::DEVICE_ERROR, "io kernel launch: injected failure"};
+        } else {
+            cs = cuda_status(io::launch_nvme_io(kp, take, s), "io kernel launch");
+            launched = cs.ok();
+        }
+    }
     if (nvtx) nvtxRangePop();
+    auto record = [&](cudaEvent_t ev) {
+        if (take_test_fault(TestFault::EVENT_RECORD_FAILURE))
+            return Status{StatusCode::DEVICE_ERROR, "event record: injected failure"};
+        return cuda_status(cudaEventRecord(ev, s), "event record");
+    };
+    bool d2h_issued = false;
     if (split) {
-        if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->submitted, s), "event record");
+        if (cs.ok()) cs = record(arena->submitted);
     } else {
         if (cs.ok())
             cs = cuda_status(
                 cudaMemcpyAsync(h + off_status, d + off_status, copy_end - off_status, cudaMemcpyDeviceToHost, s),
                 "D2H status");
-        if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->event, s), "event record");
+        d2h_issued = cs.ok();
+        if (cs.ok()) cs = record(arena->event);
     }
-    if (!cs.ok()) {
-        // Nothing irreversible is known to have happened if the launch failed;
+    if (!cs.ok() && !launched) {
+        // The kernel was not issued, so nothing irreversible happened:
         // report every request rejected and return the leases.
         cudaStreamSynchronize(s);
         for (auto l : op->leases) free_leases_.push_back(l);
@@ -663,6 +678,10 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         return reject_all(cs);
     }
     op->arena = std::move(arena);
+    op->n_cmds = n_cmds;
+    op->status_off = off_status;
+    op->timing_off = off_timing;
+    op->timing = timing;
     if (split) {
         op->drain_pending = true;
         op->kp = kp;
@@ -672,10 +691,32 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         op->stream = s;
         op->submitted_at = std::chrono::steady_clock::now();
     }
-    op->n_cmds = n_cmds;
-    op->status_off = off_status;
-    op->timing_off = off_timing;
-    op->timing = timing;
+    if (!cs.ok()) {
+        // The kernel is issued but its completion cannot be tracked by an
+        // event: the IO happens regardless, so the requests count as accepted.
+        // Wait for it here (the one synchronising path of submit), run the
+        // drain phase too when the read was split, then settle the op from
+        // its command statuses.
+        Status ws = cuda_status(cudaStreamSynchronize(s), "stream synchronize");
+        if (ws.ok() && split) {
+            op->kp.phase = io::kPhaseDrain;
+            ws = cuda_status(io::launch_nvme_io(op->kp, op->ctas, s), "drain launch");
+            op->drain_pending = false;
+            if (ws.ok()) ws = cuda_status(cudaStreamSynchronize(s), "stream synchronize");
+        }
+        if (ws.ok() && (split || !d2h_issued))
+            ws = cuda_status(cudaMemcpy(h + off_status, d + off_status, copy_end - off_status, cudaMemcpyDeviceToHost),
+                             "D2H status");
+        if (ws.ok()) {
+            finish_op(*op);
+        } else {
+            cudaGetLastError();
+            op->state = IoState::FAILED;
+            op->status = ws;
+            op->detail.failure_kind = IoFailureKind::UNKNOWN;
+            op->detail.failure_scope = IoFailureScope::WHOLE_OPERATION;  // leases stay held
+        }
+    }
     op->generation = next_token_++;
     last_submit_profile_.coalesce_ms = std::chrono::duration<double, std::milli>(t_coalesced - t_start).count();
     last_submit_profile_.launch_ms =
@@ -819,7 +860,7 @@ Result<ProgressResult> GpuNvmeDataPath::progress(ProgressBudget budget) {
             pr.more_work_likely = true;
             continue;
         }
-        cudaError_t e = cudaEventQuery(op.arena->event);
+        cudaError_t e = take_test_fault(TestFault::QUERY_ERROR) ? cudaErrorUnknown : cudaEventQuery(op.arena->event);
         if (e == cudaErrorNotReady) {
             pr.more_work_likely = true;
             continue;
@@ -869,6 +910,7 @@ Status GpuNvmeDataPath::enqueue_wait(const DataPathOp* ops, std::size_t count, c
         auto it = ops_.find(ops[i].token);
         if (it == ops_.end() || it->second->generation != ops[i].generation) return {StatusCode::NOT_FOUND, "unknown op"};
         if (!it->second->arena) continue;  // already terminal and released
+        if (it->second->state != IoState::IN_FLIGHT) continue;  // settled: its data is in place
         if (it->second->drain_pending) {
             // Split completion: the drain runs on the consumer's stream, right where it is needed.
             TUTTI_RETURN_IF_ERROR(launch_drain(*it->second, stream));

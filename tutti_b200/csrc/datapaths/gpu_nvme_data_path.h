@@ -16,6 +16,7 @@
 //   progress  -> event query; status aggregation into IoCompletionDetail
 //   enqueue_wait -> cudaStreamWaitEvent on a consumer stream
 
+#include <atomic>
 #include <cstdint>
 #include <chrono>
 #include <memory>
@@ -116,7 +117,31 @@ public:
     // True when `row` is an open target and [logical, logical+bytes) is inside it.
     bool noalloc_target_ok(std::uint32_t row, std::uint64_t logical, std::uint64_t bytes) const;
 
+    // Test seams, all on the host (nothing faults on the device). Each arms
+    // the next `count` occurrences:
+    //  LAUNCH_FAILURE        the io kernel launch reports an error and is not
+    //                        issued: every request of the submit is rejected;
+    //  EVENT_RECORD_FAILURE  the completion event cannot be recorded after the
+    //                        kernel was issued: the IO is irreversible, so the
+    //                        submit synchronises and the op ends COMPLETED or
+    //                        FAILED from its command statuses;
+    //  QUERY_ERROR           progress() sees a CUDA error from the event query:
+    //                        the op ends FAILED instead of staying IN_FLIGHT.
+    enum class TestFault : std::uint32_t { LAUNCH_FAILURE = 0, EVENT_RECORD_FAILURE = 1, QUERY_ERROR = 2 };
+    void test_inject(TestFault f, std::uint32_t count) {
+        test_faults_[static_cast<std::uint32_t>(f)].store(count, std::memory_order_relaxed);
+    }
+
 private:
+    bool take_test_fault(TestFault f) {
+        auto& c = test_faults_[static_cast<std::uint32_t>(f)];
+        std::uint32_t v = c.load(std::memory_order_relaxed);
+        while (v && !c.compare_exchange_weak(v, v - 1, std::memory_order_relaxed)) {
+        }
+        return v != 0;
+    }
+    std::atomic<std::uint32_t> test_faults_[3]{};
+
     struct TargetRec {
         std::uint64_t generation = 0;
         std::uint32_t row = 0;

@@ -467,6 +467,18 @@ PYBIND11_MODULE(_core, m) {
                 emu->inject(k, count, delay_us);
             },
             py::arg("device"), py::arg("kind"), py::arg("count") = 1, py::arg("delay_us") = 0)
+        .def(
+            "testing_inject_data_path",
+            [](PyRuntime& r, const std::string& kind, std::uint32_t count) {
+                if (!r.extras.gpu_path) throw py::value_error("data-path injection needs the nvme-gpu data path");
+                using F = GpuNvmeDataPath::TestFault;
+                F f = kind == "launch_failure"         ? F::LAUNCH_FAILURE
+                      : kind == "event_record_failure" ? F::EVENT_RECORD_FAILURE
+                      : kind == "query_error"          ? F::QUERY_ERROR
+                                                       : throw py::value_error("unknown injection " + kind);
+                r.extras.gpu_path->test_inject(f, count);
+            },
+            py::arg("kind"), py::arg("count") = 1)
         .def("last_submit_profile",
              [](PyRuntime& r) {
                  py::dict d;

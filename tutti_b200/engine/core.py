@@ -15,6 +15,13 @@ l's restore on a high-priority IO stream and records an event per layer;
 device, so attention of layer l starts as soon as its KV is in HBM while
 layers l+1.. are still being read. Writes are queued behind a compute event
 and settled (index confirm, object commit) when they complete.
+
+Write ordering (``defer_writes_after_reads``, default on): writes share the IO
+stream with reads, so a write's io kernel starts only after every read
+submitted before it; mixed read/write traffic on one drive slows both. Off,
+writes get their own stream and may overlap reads (useful when writes would
+otherwise starve behind a continuous read stream); ``wait_write_stream_event``
+still lets a caller order one write batch after a given event.
 Parity: reference tutti/engine/core.py:53-2842 (_ReadPlan, _AsyncReadPlan,
 _DirectAllLayerReadPlan with its feeder thread, _QueuedWrite, KVEngine).
 """
@@ -29,7 +36,7 @@ from typing import Sequence
 import numpy as np
 import torch
 
-from ..common.env import number
+from ..common.env import number, text
 from ..common.observability import nvtx_range
 from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
@@ -38,6 +45,19 @@ from .completion import AggregateCompletion, LoadGateError, PostCompletion
 
 LOG = logging.getLogger("tutti_b200.engine")
 FEEDER_WAIT_S = 120.0
+
+
+def resolve_defer_writes(value: bool | None) -> bool:
+    """Explicit option, else ``TUTTI_DEFER_WRITES_AFTER_READS`` ("0" turns it off), else on.
+
+    Parity: reference tutti/storage/tutti_nvme/store.py:1711-1727 (same precedence and default).
+    """
+    if value is None:
+        env = text("TUTTI_DEFER_WRITES_AFTER_READS")
+        return True if env is None else env != "0"
+    if not isinstance(value, bool):
+        raise ValueError(f"defer_writes_after_reads must be a bool, got {value!r}")
+    return value
 
 
 class LayerwiseReadPlan:
@@ -136,7 +156,8 @@ class LayerwiseReadPlan:
 class KVEngine:
     def __init__(self, store, geometry: KVGeometry, *, capacity_chunks: int | None = None,
                  namespace: bytes = b"", device: int | torch.device = 0, staged: bool | None = None,
-                 io_priority: int = -1, checkpoint_interval_s: float | None = None):
+                 io_priority: int = -1, checkpoint_interval_s: float | None = None,
+                 defer_writes_after_reads: bool | None = None):
         self.store = store
         self.geometry = geometry
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
@@ -146,6 +167,8 @@ class KVEngine:
         self.pool: torch.Tensor | None = None
         self._io_stream: torch.cuda.Stream | None = None
         self._io_priority = io_priority
+        self._write_stream: torch.cuda.Stream | None = None
+        self.defer_writes_after_reads = resolve_defer_writes(defer_writes_after_reads)
         self._writes: collections.deque = collections.deque()
         self._checkpoint_interval = (checkpoint_interval_s if checkpoint_interval_s is not None
                                      else number("TUTTI_CHECKPOINT_INTERVAL_S", 60.0))
@@ -197,6 +220,20 @@ class KVEngine:
             else:
                 self._io_stream = torch.cuda.Stream(device=self.device, priority=self._io_priority)
         return self._io_stream
+
+    @property
+    def write_stream(self) -> torch.cuda.Stream:
+        """The stream writes are submitted on: the IO stream (writes after reads) or a stream of their own."""
+        if self.defer_writes_after_reads:
+            return self.io_stream
+        if self._write_stream is None:
+            self._write_stream = torch.cuda.Stream(device=self.device, priority=0)
+        return self._write_stream
+
+    def wait_write_stream_event(self, event: torch.cuda.Event) -> None:
+        """Order later write batches after ``event`` on the device; the host does not block."""
+        if self.pool is not None and self.pool.device.type == "cuda":
+            self.write_stream.wait_event(event)
 
     def bind(self, pool: torch.Tensor) -> None:
         """Bind the engine's paged KV pool (direct mode registers it with the store once)."""
@@ -304,7 +341,7 @@ class KVEngine:
         bt = self._table(block_table)[idx]
         wkeys = [keys[i] for i in idx]
         on_gpu = self.pool is not None and self.pool.device.type == "cuda"
-        stream = self.io_stream if on_gpu else None
+        stream = self.write_stream if on_gpu else None
         if stream is not None:
             if after is not None:
                 stream.wait_event(after)

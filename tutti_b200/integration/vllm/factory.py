@@ -63,6 +63,7 @@ class ConnectorConfig:
     segment_file_slots: int = 2048
     runtime_options: dict = field(default_factory=dict)
     stored_format: str = "native"  # or "fp8_block128": E4M3 + 1x128 scales on disk, fused in the io kernel
+    defer_writes_after_reads: bool | None = None  # None: TUTTI_DEFER_WRITES_AFTER_READS, else on
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
@@ -89,7 +90,7 @@ class ConnectorConfig:
             LOG.info("[tutti] store preset %r: drives are emulated over the store's mounts",
                      preset.get("type") if isinstance(preset, dict) else preset)
         for k in ("root", "capacity", "capacity_chunks", "mounts", "segment_file_slots", "runtime_options",
-                  "stored_format"):
+                  "stored_format", "defer_writes_after_reads"):
             if k in opts:
                 st.setdefault(k, opts.pop(k))
         opts.pop("io_stream", None)
@@ -103,6 +104,10 @@ class ConnectorConfig:
         c.segment_file_slots = int(st.pop("segment_file_slots", c.segment_file_slots))
         c.runtime_options = dict(st.pop("runtime_options", {}))
         c.stored_format = str(st.pop("stored_format", c.stored_format))
+        dw = st.pop("defer_writes_after_reads", None)
+        if dw is not None and not isinstance(dw, bool):
+            raise ValueError(f"store.defer_writes_after_reads must be a bool, got {dw!r}")
+        c.defer_writes_after_reads = dw
         if c.stored_format not in ("native", "fp8_block128"):
             raise ValueError("store.stored_format must be native or fp8_block128")
         if st:
@@ -154,7 +159,8 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
                              rank_count=world, segment_file_slots=min(cfg.segment_file_slots, max(16, cap)),
                              runtime_options=cfg.runtime_options, namespace=ns, stored_format=cfg.stored_format)
         store.open()
-        eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device)
+        eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device,
+                       defer_writes_after_reads=cfg.defer_writes_after_reads)
         eng.restore_from_store()
     eng.bind_layers(tensors)
     return eng

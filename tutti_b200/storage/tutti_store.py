@@ -30,7 +30,7 @@ import numpy as np
 import torch
 
 from .._native import core
-from ..common.env import integer, runtime_option_defaults
+from ..common.env import integer, prp_mode, runtime_option_defaults
 from ..common.observability import metrics, nvtx_range
 from ..models.kv_geometry import KVGeometry
 from .base import StoreIOError
@@ -153,6 +153,7 @@ class TuttiKVStore:
         self.backend = backend
         self.mounts = [str(m) for m in (mounts or [self.root / "dev0"])]
         self.runtime_options = {**runtime_option_defaults(), **dict(runtime_options or {})}
+        self.prp_mode = prp_mode()
         self.stored = stored_geometry(geometry, stored_format)
         if stored_format != "native" and backend != "nvme-gpu":
             raise ValueError(f"stored_format {stored_format!r} needs the nvme-gpu backend (fused in its io kernel)")
