@@ -479,6 +479,19 @@ PYBIND11_MODULE(_core, m) {
                 r.extras.gpu_path->test_inject(f, count);
             },
             py::arg("kind"), py::arg("count") = 1)
+        .def("memfs_usage",
+             [](PyRuntime& r) {
+                 if (!r.extras.memfs_budget) throw py::value_error("not a memfs runtime");
+                 py::dict d;
+                 d["capacity"] = r.extras.memfs_budget->capacity();
+                 d["used"] = r.extras.memfs_budget->used();
+                 return d;
+             })
+        .def("memfs_remove",
+             [](PyRuntime& r, const std::string& name) {
+                 if (!r.extras.memfs_resolver) throw py::value_error("not a memfs runtime");
+                 check(r.extras.memfs_resolver->remove(name));
+             })
         .def("last_submit_profile",
              [](PyRuntime& r) {
                  py::dict d;
@@ -579,6 +592,17 @@ PYBIND11_MODULE(_core, m) {
             return wrap(unwrap(make_posix_runtime(o)));
         },
         py::arg("accel_id"), py::arg("mounts"), py::arg("options") = py::dict());
+
+    m.def(
+        "make_memfs_runtime",
+        [](int accel_id, std::uint64_t capacity_bytes, std::uint64_t max_terminal_results) {
+            MemfsPresetOptions o;
+            o.accel_id = accel_id;
+            o.capacity_bytes = capacity_bytes;
+            o.max_terminal_results = max_terminal_results;
+            return wrap(unwrap(make_memfs_runtime(o)));
+        },
+        py::arg("accel_id") = -1, py::arg("capacity_bytes") = 1ull << 30, py::arg("max_terminal_results") = 64);
 
     m.def(
         "parse_runtime_config",

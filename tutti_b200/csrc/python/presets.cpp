@@ -110,4 +110,26 @@ Result<PresetResult> make_posix_runtime(const PosixPresetOptions& o) {
     return pr;
 }
 
+Result<PresetResult> make_memfs_runtime(const MemfsPresetOptions& o) {
+    using R = Result<PresetResult>;
+    if (!o.capacity_bytes) return R::Failure({StatusCode::INVALID_ARGUMENT, "memfs needs a capacity"});
+    PresetResult pr;
+    OwnedComponents comps;
+    auto budget = std::make_shared<samples::memfs::MemoryResource>(o.capacity_bytes);
+    auto resolver = std::make_unique<samples::memfs::Resolver>(budget);
+    pr.extras.memfs_resolver = resolver.get();
+    pr.extras.memfs_budget = budget;
+    comps.resolvers.push_back({"memfs", std::move(resolver)});
+    comps.data_paths.push_back({samples::memfs::kDataPathKey, std::make_shared<samples::memfs::MemfsDataPath>(),
+                                DataPathConfig{samples::memfs::kDataPathKey}});
+    RuntimeConfig rc;
+    rc.accel_id = o.accel_id < 0 ? 0 : o.accel_id;
+    rc.max_terminal_results = o.max_terminal_results;
+    auto rt = StorageRuntime::create_owning(rc, std::move(comps));
+    if (!rt.ok()) return R::Failure(rt.status());
+    pr.runtime = std::move(rt).value();
+    pr.runtime_id = pr.runtime->runtime_id();
+    return pr;
+}
+
 }  // namespace tutti

@@ -13,6 +13,7 @@
 
 #include "../datapaths/gpu_nvme_data_path.h"
 #include "../datapaths/posix_data_path.h"
+#include "../samples/memfs/memfs.h"
 #include "../nvme/controller.h"
 
 namespace tutti {
@@ -43,10 +44,18 @@ struct PosixPresetOptions {
     PosixConfig posix;
 };
 
+struct MemfsPresetOptions {
+    int accel_id = -1;
+    std::uint64_t capacity_bytes = 1ull << 30;
+    std::uint64_t max_terminal_results = 64;
+};
+
 struct PresetExtras {
     std::vector<std::shared_ptr<nvme::NvmeController>> controllers;
     std::shared_ptr<GpuNvmeDataPath> gpu_path;
     std::shared_ptr<PosixDataPath> posix_path;
+    std::shared_ptr<samples::memfs::MemoryResource> memfs_budget;
+    samples::memfs::Resolver* memfs_resolver = nullptr;  // owned by the runtime's components
 };
 
 struct PresetResult {
@@ -57,6 +66,8 @@ struct PresetResult {
 
 Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o);
 Result<PresetResult> make_posix_runtime(const PosixPresetOptions& o);
+// The memfs sample backend (scheme memfs://, DataPath key memfs) and nothing else.
+Result<PresetResult> make_memfs_runtime(const MemfsPresetOptions& o);
 std::uint32_t probe_runtime_id(const StorageRuntime& rt);
 
 }  // namespace tutti

@@ -23,6 +23,7 @@
 #include "../nvme/controller.h"
 #include "../objects/digest.h"
 #include "../objects/object_store.h"
+#include "../samples/memfs/memfs.h"
 #include "../testing/mock_data_path.h"
 
 using namespace tutti;
@@ -227,6 +228,45 @@ TEST(runtime_shutdown_times_out_with_inflight_io) {
     CHECK(f.rt->shutdown(20).code() == StatusCode::TIMEOUT);
     f.dp.complete_all();
     CHECK(f.rt->shutdown(1000).ok());
+}
+
+TEST(memfs_sample_plugs_into_an_unmodified_runtime) {
+    // a backend written only against the SPI: resolver + payload + DataPath + budget
+    auto budget = std::make_shared<samples::memfs::MemoryResource>(1 << 20);
+    samples::memfs::Resolver resolver(budget);
+    samples::memfs::MemfsDataPath dp;
+    RuntimeConfig c;
+    c.accel_id = 0;
+    RuntimeComponents comps;
+    comps.resolvers.push_back({"memfs", &resolver});
+    comps.data_paths.push_back({"memfs", &dp, DataPathConfig{"memfs"}});
+    auto rt = StorageRuntime::create(c, comps).value();
+    std::vector<char> src(8192), dst(8192, 0);
+    for (std::size_t i = 0; i < src.size(); ++i) src[i] = static_cast<char>(i * 13 + 1);
+    MemoryView v;
+    v.address = src.data();
+    v.size = src.size();
+    v.expected_kind = MemoryKind::HOST;
+    auto ms = rt->register_memory(v).value();
+    v.address = dst.data();
+    auto md = rt->register_memory(v).value();
+    auto t = rt->open("memfs://obj?size=64K");
+    CHECK(t.ok() && budget->used() == 65536);
+    const HostSubmitContext ctx{ExecutionDomain::HOST_EXECUTION, -1, nullptr};
+    IoRequest w{IoDirection::WRITE, ms, 0, t.value(), 4096, 8192};
+    auto o = rt->submit(&w, 1, ctx);
+    CHECK(o.status.ok() && o.io.has_value());
+    CHECK(rt->wait(*o.io, 1000).result->state == IoState::COMPLETED);
+    CHECK(rt->release_io(*o.io).ok());
+    IoRequest r[2] = {{IoDirection::READ, md, 0, t.value(), 4096, 8192},
+                      {IoDirection::READ, md, 0, t.value(), 65536 - 100, 200}};  // past the end
+    o = rt->submit(r, 2, ctx);
+    CHECK(o.io.has_value() && o.initial_states[1].state == IoRequestState::REJECTED);
+    auto res = rt->wait(*o.io, 1000);
+    CHECK(res.result->state == IoState::COMPLETED && res.result->detail.confirmed_bytes == 8192);
+    CHECK(std::memcmp(src.data(), dst.data(), src.size()) == 0);
+    CHECK(rt->release_io(*o.io).ok());
+    CHECK(!rt->open("memfs://big?size=2M").ok());  // over budget
 }
 
 TEST(stub_runtime_memory_only) {
