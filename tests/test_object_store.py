@@ -207,3 +207,29 @@ def test_read_only_view_adopts_the_namespace_layout(tmp_path):
     v.close()
     with pytest.raises(Exception):
         ObjectLayout.open_view(tmp_path, mounts[:1])  # the namespace has two devices
+
+
+def test_ready_markers_bind_segment_files_to_their_inode(tmp_path):
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    path = s.slot_path(0)
+    marker = open(path + ".ready").read().split()
+    st = os.stat(path)
+    assert marker == ["tutti-ready", "v1", str(st.st_size), str(st.st_dev), str(st.st_ino)]
+    assert os.path.exists(os.path.join(str(tmp_path / "d0"), ".tutti_segment_precreate.lock"))
+    s.close()
+    # a replacement file of the same name and size is not a prepared segment file
+    data = open(path, "rb").read()
+    with open(path + ".new", "wb") as f:  # created while the original exists: another inode
+        f.write(data)
+    os.replace(path + ".new", path)
+    ro = core().ObjectStore()
+    ro.open(cfg(tmp_path, read_only=True))
+    assert ro.ready_slots == 0
+    ro.close()
+    # a writable open prepares that file again (new marker for the new inode)
+    s = core().ObjectStore()
+    s.open(cfg(tmp_path))
+    assert s.ready_slots == 8
+    assert open(path + ".ready").read().split()[4] == str(os.stat(path).st_ino)
+    s.close()

@@ -2,6 +2,7 @@
 
 #include <fcntl.h>
 #include <sys/mman.h>
+#include <sys/file.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -269,11 +270,8 @@ Status SegmentFileObjectStore::open(const StoreConfig& config) {
     std::uint64_t ready = 0;
     for (std::uint64_t grp = 0; grp * group_slots_ < total_slots_; ++grp) {
         bool all = true;
-        for (std::uint64_t d = 0; d < cfg_.devices.size(); ++d) {
-            struct stat st {};
-            const std::string p = slot_path(grp * group_slots_ + d);
-            if (::stat(p.c_str(), &st) != 0 || static_cast<std::uint64_t>(st.st_size) < file_bytes()) all = false;
-        }
+        for (std::uint64_t d = 0; d < cfg_.devices.size(); ++d)
+            if (!segment_file_ready(slot_path(grp * group_slots_ + d))) all = false;
         if (!all) break;
         ready = std::min(total_slots_, (grp + 1) * group_slots_);
     }
@@ -293,11 +291,57 @@ Status SegmentFileObjectStore::open(const StoreConfig& config) {
     return Status::Ok();
 }
 
+namespace {
+// The `.ready` marker of a segment file: its size and the (st_dev, st_ino) it
+// was written for, so a replacement file of the same name and size is never
+// taken for a prepared one.
+std::string ready_marker_text(std::uint64_t bytes, const struct stat& st) {
+    return "tutti-ready v1 " + std::to_string(bytes) + " " + std::to_string(static_cast<std::uint64_t>(st.st_dev)) +
+           " " + std::to_string(static_cast<std::uint64_t>(st.st_ino)) + "\n";
+}
+
+// Holds `<mount>/.tutti_segment_precreate.lock` exclusively: ranks that share a
+// mount create their segment files one at a time, which keeps each file's
+// extents long (concurrent zero-fills interleave their blocks).
+class MountCreateLock {
+public:
+    explicit MountCreateLock(const std::string& mount) {
+        const std::string p = mount + "/.tutti_segment_precreate.lock";
+        fd_ = ::open(p.c_str(), O_RDWR | O_CREAT | O_CLOEXEC, 0644);
+        if (fd_ >= 0) {
+            while (::flock(fd_, LOCK_EX) != 0 && errno == EINTR) {
+            }
+        }
+    }
+    ~MountCreateLock() {
+        if (fd_ >= 0) ::close(fd_);  // closing releases the lock
+    }
+    MountCreateLock(const MountCreateLock&) = delete;
+    MountCreateLock& operator=(const MountCreateLock&) = delete;
+
+private:
+    int fd_ = -1;
+};
+}  // namespace
+
+bool SegmentFileObjectStore::segment_file_ready(const std::string& path) const {
+    struct stat st {};
+    if (::stat(path.c_str(), &st) != 0 || static_cast<std::uint64_t>(st.st_size) < file_bytes()) return false;
+    std::FILE* f = std::fopen((path + ".ready").c_str(), "r");
+    if (!f) return false;
+    char line[160] = {0};
+    const bool got = std::fgets(line, sizeof(line), f) != nullptr;
+    std::fclose(f);
+    return got && ready_marker_text(file_bytes(), st) == line;
+}
+
 Status SegmentFileObjectStore::materialize_group(std::uint64_t grp) {
     const std::uint64_t fb = file_bytes();
     for (std::uint64_t d = 0; d < cfg_.devices.size(); ++d) {
         const std::string p = slot_path(grp * group_slots_ + d);
+        if (segment_file_ready(p)) continue;  // prepared by an earlier open
         const std::string tmp = p + ".tmp";
+        MountCreateLock serial(cfg_.devices[d].mount_path);
         int fd = ::open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC | O_CLOEXEC, 0644);
         if (fd < 0) return errno_status("create " + tmp);
         if (cfg_.materialize == "fallocate") {
@@ -322,6 +366,17 @@ Status SegmentFileObjectStore::materialize_group(std::uint64_t grp) {
         }
         ::close(fd);
         if (::rename(tmp.c_str(), p.c_str()) != 0) return errno_status("publish " + p);
+        // The marker goes last (written, synced, renamed into place): a crash
+        // before it leaves a file that the next open prepares again.
+        struct stat st {};
+        if (::stat(p.c_str(), &st) != 0) return errno_status("stat " + p);
+        const std::string mk = ready_marker_text(fb, st), mtmp = p + ".ready.tmp";
+        int mfd = ::open(mtmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC | O_CLOEXEC, 0644);
+        if (mfd < 0) return errno_status("create " + mtmp);
+        const bool ok = pwrite_full(mfd, mk.data(), mk.size(), 0) && ::fsync(mfd) == 0;
+        ::close(mfd);
+        if (!ok) return errno_status("write " + mtmp);
+        if (::rename(mtmp.c_str(), (p + ".ready").c_str()) != 0) return errno_status("publish " + p + ".ready");
     }
     return Status::Ok();
 }

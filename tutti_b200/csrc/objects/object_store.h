@@ -122,6 +122,8 @@ public:
     std::uint64_t ready_slots() const;
     std::string slot_uri(std::uint64_t slot) const;
     std::string slot_path(std::uint64_t slot) const;
+    // True when `path` has its full size and a `.ready` marker bound to its inode.
+    bool segment_file_ready(const std::string& path) const;
     std::uint64_t slot_generation(std::uint64_t slot) const;
     std::uint64_t slot_bytes() const { return slot_bytes_; }
     std::uint64_t total_slots() const { return total_slots_; }
