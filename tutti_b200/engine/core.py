@@ -287,7 +287,9 @@ class KVEngine:
             raise RuntimeError("bind() the KV pool first")
         layers = list(range(self.geometry.num_layers)) if layers is None else list(layers)
         if self.staged:
-            raise NotImplementedError("layerwise plans need a direct (paged) store")
+            from ..common.errors import DirectTransferUnavailable
+
+            raise DirectTransferUnavailable("layerwise plans need a direct (paged) store")
         self.stats["read_chunks"] += len(keys)
         return LayerwiseReadPlan(self, keys, self._table(block_table), layers, self.io_stream, window)
 

@@ -73,17 +73,20 @@ class TuttiConnectorV1(KVConnectorBase_V1):
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""
-        if self.cfg.store_type != "tutti":
-            return
-        from ...storage.object_layout import ObjectLayout
+        from ...storage.registry import create_metadata_store, has_metadata_store
         from .factory import expand
 
-        root = expand(self.cfg.root, 0, 0)
-        if not os.path.exists(os.path.join(root, "meta", "namespace")):
+        if not has_metadata_store(self.cfg.store_type):
             return
-        mounts = [expand(m, 0, 0) for m in self.cfg.mounts] or [os.path.join(root, "nvme0")]
+        if self.cfg.store_type == "tutti":
+            options = {"root": expand(self.cfg.root, 0, 0), "mounts": [expand(m, 0, 0) for m in self.cfg.mounts],
+                       "rank": 0}
+        else:
+            options = {k: expand(v, 0, 0) if isinstance(v, str) else v for k, v in self.cfg.store_options.items()}
         try:
-            view = ObjectLayout.open_view(root, mounts, rank=0)
+            view = create_metadata_store(self.cfg.store_type, options)
+            if view is None:
+                return
             keys = view.recover()
             if self.tp_size > 1:  # resident only where every TP rank holds its slice
                 keys = [k for k in keys if view.contains_prefix([k], True) == 1]

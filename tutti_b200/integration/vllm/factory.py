@@ -21,7 +21,6 @@ config/integration/vllm/kv_transfer.json.
 from __future__ import annotations
 
 import logging
-import os
 import re
 from dataclasses import dataclass, field
 
@@ -64,6 +63,7 @@ class ConnectorConfig:
     runtime_options: dict = field(default_factory=dict)
     stored_format: str = "native"  # or "fp8_block128": E4M3 + 1x128 scales on disk, fused in the io kernel
     defer_writes_after_reads: bool | None = None  # None: TUTTI_DEFER_WRITES_AFTER_READS, else on
+    store_options: dict = field(default_factory=dict)  # a registered third-party store type's own options
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
@@ -83,6 +83,14 @@ class ConnectorConfig:
             # the reference connector's schema: store {type: tutti_nvme, options: {root, capacity, preset}}
             c.store_type = "tutti"
         opts = dict(st.pop("options", {}))
+        if c.store_type not in ("tutti", "memory"):
+            # a store type registered by a plugin: its options are its own business
+            from ...storage.registry import store_types
+
+            if c.store_type not in store_types():
+                raise ValueError(f"store.type must be one of {store_types()}, got {c.store_type!r}")
+            c.store_options = {**st, **opts}
+            return c
         preset = opts.pop("preset", None)
         if preset is not None:
             # drive presets (raid0 / device groups / daemon configs) name real NVMe devices; this
@@ -112,8 +120,6 @@ class ConnectorConfig:
             raise ValueError("store.stored_format must be native or fp8_block128")
         if st:
             raise ValueError(f"unknown store options: {sorted(st)}")
-        if c.store_type not in ("tutti", "memory"):
-            raise ValueError("store.type must be tutti or memory")
         return c
 
     def capacity_for(self, geometry: KVGeometry) -> int:
@@ -136,31 +142,36 @@ def geometry_from_layers(tensors: list[torch.Tensor], chunk_tokens: int, name: s
 
 def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, local_rank: int, world: int,
                 entity: str = ""):
-    """The engine of one KV entity (``entity`` "" is the main KV; others get their own namespace and root)."""
+    """The engine of one KV entity ("" is the main KV; others get their own namespace and root).
+
+    The store comes from the store-type registry (``cfg.store_type``); a store
+    without ``get_paged`` is driven through staging buffers.
+    """
     from ...engine.core import KVEngine
-    from ...storage.memory import MemoryKVStore
-    from ...storage.tutti_store import TuttiKVStore
+    from ...storage.registry import StoreContext, create_store
 
     g = geometry_from_layers(tensors, cfg.chunk_tokens, cfg.namespace or "vllm")
     cap = cfg.capacity_for(g)
     ns = (cfg.namespace or g.fingerprint()).encode() + (b"/" + entity.encode() if entity else b"")
     device = tensors[0].device
-    if cfg.store_type == "memory" or device.type != "cuda":
-        store = MemoryKVStore(g.chunk_bytes, capacity_chunks=cap)
-        store.open()
-        eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device, staged=True)
+    kind = cfg.store_type
+    if kind == "tutti" and device.type != "cuda":
+        kind = "memory"  # the io kernel needs the pool in HBM
+    if kind == "tutti":
+        options = {"root": expand(cfg.root, rank, local_rank),
+                   "mounts": [expand(m, rank, local_rank) for m in cfg.mounts],
+                   "segment_file_slots": cfg.segment_file_slots, "runtime_options": cfg.runtime_options,
+                   "stored_format": cfg.stored_format}
+    elif kind == "memory":
+        options = {}
     else:
-        root = expand(cfg.root, rank, local_rank)
-        mounts = [expand(m, rank, local_rank) for m in cfg.mounts] or [os.path.join(root, "nvme0")]
-        if entity:
-            root = os.path.join(root, "entities", entity)
-            mounts = [os.path.join(m, "entities", entity) for m in mounts]
-        store = TuttiKVStore(root, g, capacity_chunks=cap, mounts=mounts, device=device.index, rank=rank,
-                             rank_count=world, segment_file_slots=min(cfg.segment_file_slots, max(16, cap)),
-                             runtime_options=cfg.runtime_options, namespace=ns, stored_format=cfg.stored_format)
-        store.open()
-        eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device,
-                       defer_writes_after_reads=cfg.defer_writes_after_reads)
-        eng.restore_from_store()
+        options = {k: expand(v, rank, local_rank) if isinstance(v, str) else v for k, v in cfg.store_options.items()}
+    ctx = StoreContext(geometry=g, capacity_chunks=cap, namespace=ns, device=device, rank=rank,
+                       local_rank=local_rank, world=world, entity=entity, options=options)
+    store = create_store(kind, ctx)
+    staged = kind == "memory" or not hasattr(store, "get_paged")
+    eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device, staged=staged,
+                   defer_writes_after_reads=cfg.defer_writes_after_reads)
+    eng.restore_from_store()
     eng.bind_layers(tensors)
     return eng
