@@ -4,7 +4,8 @@
     python -m tutti_b200.benchmarks.kernels fp8      # block-scaled fp8 quantise of bf16 rows
     python -m tutti_b200.benchmarks.kernels hash     # chained BLAKE2b-128 prefix keys
     python -m tutti_b200.benchmarks.kernels checksum # KV block checksums
-    python -m tutti_b200.benchmarks.kernels io       # fused NVMe io kernel restore (emulated controllers)
+    python -m tutti_b200.benchmarks.kernels io       # fused NVMe io kernel restore (emulated controllers);
+                                                     #   --direction write: store; --async-completion: split launches
 
 Each prints one JSON line: kernel time (CUDA events, after warm-up, inputs
 larger than L2 where the kernel is bandwidth-bound) and achieved rates.
@@ -117,10 +118,10 @@ def bench_io(args) -> dict:
         tokens = args.tokens
         nblk = tokens // g.block_size
         nch = tokens // g.chunk_tokens
-        st = TuttiKVStore(root, g, capacity_chunks=max(16, nch), mounts=[os.path.join(root, f"nvme{d}") for d in range(4)],
-                          device=0, segment_file_slots=max(4, nch // 4 + 1), stored_format=args.stored_format,
+        st = TuttiKVStore(root, g, capacity_chunks=max(16, 2 * nch), mounts=[os.path.join(root, f"nvme{d}") for d in range(4)],
+                          device=0, segment_file_slots=max(4, nch // 2 + 1), stored_format=args.stored_format,
                           runtime_options={"controller_threads": 3, "leases": 64, "max_ctas_per_op": 64,
-                                           "slots_per_lease": 8})
+                                           "slots_per_lease": 8, "async_completion": bool(args.async_completion)})
         st.open()
         nb = 2 * nblk + 64
         pool = torch.randn(g.pool_shape(nb), dtype=g.dtype, device="cuda")
@@ -129,6 +130,21 @@ def bench_io(args) -> dict:
         src = np.arange(nblk).reshape(nch, g.blocks_per_chunk)
         st.put_paged(keys, src).wait()
         dst = (np.arange(nblk) + nblk).reshape(nch, g.blocks_per_chunk)
+        if args.direction == "write":
+            # fresh keys every launch: each store writes (and commits) new chunks from the source blocks
+            state = {"n": 0}
+
+            def store_once():
+                state["n"] += 1
+                k = chunk_keys_for_tokens(list(range(tokens)), g.chunk_tokens, namespace=b"w%d" % state["n"])
+                st.put_paged(k, src).wait()
+                st.drop(k)  # free the slots for the next launch
+
+            ms = _time(store_once, args.iters, args.warmup)
+            nbytes = nblk * g.num_layers * g.block_layer_bytes
+            st.close()
+            return {"kernel": "nvme_io_kernel", "direction": "write", "stored_format": args.stored_format,
+                    "bytes": nbytes, "ms": ms, "GBps": nbytes / ms / 1e6, "ok": True}
         ms = _time(lambda: st.get_paged(keys, dst).wait(), args.iters, args.warmup)
         want = pool[:, :, :nblk]
         if args.stored_format == "fp8_block128":
@@ -137,7 +153,8 @@ def bench_io(args) -> dict:
         ok = bool(torch.equal(pool[:, :, nblk:2 * nblk], want))
         nbytes = nblk * g.num_layers * g.block_layer_bytes
         st.close()
-        return {"kernel": "nvme_io_kernel", "stored_format": args.stored_format, "bytes": nbytes, "ms": ms,
+        return {"kernel": "nvme_io_kernel", "direction": "read", "async_completion": bool(args.async_completion),
+                "stored_format": args.stored_format, "bytes": nbytes, "ms": ms,
                 "GBps": nbytes / ms / 1e6, "ok": ok}
     finally:
         shutil.rmtree(root, ignore_errors=True)
@@ -154,6 +171,8 @@ def main(argv=None):
     p.add_argument("--chunk", type=int, default=256)
     p.add_argument("--verify", action="store_true")
     p.add_argument("--stored-format", choices=["native", "fp8_block128"], default="native")
+    p.add_argument("--direction", choices=["read", "write"], default="read", help="io: restore or store")
+    p.add_argument("--async-completion", action="store_true", help="io: split submit / drain launches")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     fn = {"copy": bench_copy, "fp8": bench_fp8, "hash": bench_hash, "checksum": bench_checksum, "io": bench_io}
