@@ -42,6 +42,7 @@ from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
 from ..parallel.green_context import configured_io_sms, io_stream_on_sms
 from .completion import AggregateCompletion, LoadGateError, PostCompletion
+from .staging import StagingBuffer
 
 LOG = logging.getLogger("tutti_b200.engine")
 FEEDER_WAIT_S = 120.0
@@ -170,6 +171,7 @@ class KVEngine:
         self._write_stream: torch.cuda.Stream | None = None
         self.defer_writes_after_reads = resolve_defer_writes(defer_writes_after_reads)
         self._writes: collections.deque = collections.deque()
+        self._staging_bufs: dict[str, StagingBuffer] = {}  # staged stores: one reused buffer per direction
         self._checkpoint_interval = (checkpoint_interval_s if checkpoint_interval_s is not None
                                      else number("TUTTI_CHECKPOINT_INTERVAL_S", 60.0))
         self._last_checkpoint = time.monotonic()
@@ -301,25 +303,25 @@ class KVEngine:
             return self.store.get_paged(keys, bt, layers=layers, stream=self.io_stream)
         return self._staged_load(keys, bt)
 
+    def _staging(self, direction: str) -> StagingBuffer:
+        buf = self._staging_bufs.get(direction)
+        if buf is None:
+            buf = self._staging_bufs[direction] = StagingBuffer(self.store, self.geometry.chunk_bytes, self.pool.device)
+        return buf
+
     def _staged_load(self, keys, bt):
         g = self.geometry
         dev = self.pool.device
-        staging = torch.empty(len(keys) * g.chunk_bytes, dtype=torch.uint8, device=dev)
-        comp = self.store.get_batch([(k, self._staging_id(staging), i * g.chunk_bytes) for i, k in enumerate(keys)])
-        comp.wait()
-        if dev.type == "cuda" and not getattr(self, "layers", None):
-            from .. import ops
+        with self._staging("load").use(len(keys)) as (staging, bid, _):
+            comp = self.store.get_batch([(k, bid, i * g.chunk_bytes) for i, k in enumerate(keys)])
+            comp.wait()
+            if dev.type == "cuda" and not getattr(self, "layers", None):
+                from .. import ops
 
-            ops.scatter_blocks(staging, self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
-        else:
-            self._scatter_chunks(staging, bt)
+                ops.scatter_blocks(staging, self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
+            else:
+                self._scatter_chunks(staging, bt)
         return comp
-
-    def _staging_id(self, staging: torch.Tensor) -> int:
-        bid = self.store.register_buffer(staging, self.geometry.chunk_bytes)
-        if bid is None:
-            raise RuntimeError("store refused the staging buffer")
-        return bid
 
     # -- stores ---------------------------------------------------------------
     def plan_store(self, keys: Sequence[bytes]) -> StorePlan | None:
@@ -349,24 +351,29 @@ class KVEngine:
                 stream.wait_event(after)
             else:
                 stream.wait_stream(torch.cuda.current_stream(self.device))
+
+        def settle(inner):
+            return PostCompletion(inner, after=lambda: self.index.confirm_store(wkeys, True),
+                                  on_error=lambda: self.index.confirm_store(wkeys, False))
+
         if not self.staged:
-            inner = self.store.put_paged(wkeys, bt, stream=stream)
+            comp = settle(self.store.put_paged(wkeys, bt, stream=stream))
         else:
             g = self.geometry
-            if on_gpu and not getattr(self, "layers", None):
-                from .. import ops
+            with self._staging("store").use(len(wkeys)) as (staging, bid, holder):
+                if on_gpu and not getattr(self, "layers", None):
+                    from .. import ops
 
-                with torch.cuda.stream(stream):
-                    staging = ops.gather_blocks(self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk)
-                stream.synchronize()
-            else:
-                if on_gpu:
+                    with torch.cuda.stream(stream):
+                        ops.gather_blocks(self.pool, torch.from_numpy(bt.reshape(-1)), g.blocks_per_chunk,
+                                          out=staging)
                     stream.synchronize()
-                staging = self._gather_chunks(bt).reshape(-1)
-            bid = self._staging_id(staging)
-            inner = self.store.put_batch([(k, bid, i * g.chunk_bytes) for i, k in enumerate(wkeys)])
-        comp = PostCompletion(inner, after=lambda: self.index.confirm_store(wkeys, True),
-                              on_error=lambda: self.index.confirm_store(wkeys, False))
+                else:
+                    if on_gpu:
+                        stream.synchronize()
+                    staging.copy_(self._gather_chunks(bt).reshape(-1))
+                comp = settle(self.store.put_batch([(k, bid, i * g.chunk_bytes) for i, k in enumerate(wkeys)]))
+                holder["pending"] = comp  # the store may read the buffer until this batch completes
         self._writes.append(comp)
         self.stats["write_chunks"] += len(wkeys)
         return comp

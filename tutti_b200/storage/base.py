@@ -28,6 +28,9 @@ class KVStore(Protocol):
 
     def register_buffer(self, buffer, granularity: int) -> int | None: ...
 
+    # optional: drop a registration (engines reuse and replace their staging buffers)
+    def unregister_buffer(self, buffer_id: int) -> None: ...
+
     def put_batch(self, batch: Sequence[tuple[bytes, int, int]]) -> Completion: ...
 
     def get_batch(self, batch: Sequence[tuple[bytes, int, int]]) -> Completion: ...

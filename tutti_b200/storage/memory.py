@@ -42,6 +42,9 @@ class MemoryKVStore:
         self._buffers[bid] = buffer.view(torch.uint8).reshape(-1)
         return bid
 
+    def unregister_buffer(self, bid: int) -> None:
+        self._buffers.pop(bid, None)
+
     def _view(self, bid: int, off: int) -> torch.Tensor:
         buf = self._buffers[bid]
         if off < 0 or off + self.chunk_bytes > buf.numel():
