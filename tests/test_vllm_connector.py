@@ -89,10 +89,12 @@ def test_worker_save_then_load_roundtrip_cpu():
     w.start_load_kv(meta)
     for i in range(3):
         w.wait_for_layer_load(f"model.layers.{i}.self_attn.attn")
-    w.wait_for_save(meta)
+    wm = w.wait_for_save(meta)
     for i in range(3):
         assert torch.equal(layers[i][:, 20:24], ref[i])
     assert w.get_block_ids_with_load_errors() == set()
+    # the finished load is reported to the scheduler's load policy, with the step it ran in
+    assert wm.generation == 2 and len(wm.read_samples) == 1 and wm.read_samples[0][0] == 2
 
 
 def test_worker_reports_load_error_blocks():

@@ -6,6 +6,7 @@
 | ``TUTTI_POOL_WORKERS=<n>`` | CTAs (queue leases) one restore/store may use (the runtime option) |
 | ``TUTTI_ASYNC_COMPLETION=1`` | split submit / drain launches for reads (off; read natively) |
 | ``TUTTI_LOAD_MODE=sync\\|async\\|auto`` | the vLLM connector's load mode (sync) |
+| ``TUTTI_ASYNC_LOAD_FREE_RATIO=<r>`` | share of the blocks running requests leave that asynchronous loads may hold (0.5) |
 | ``TUTTI_CHECKPOINT_INTERVAL_S=<s>`` | object-index checkpoint cadence of the KV engine (60) |
 | ``TUTTI_PRECREATE_MIN_FREE_BYTES=<n>`` | free space kept on each mount by segment-file growth |
 | ``TUTTI_DEFER_WRITES_AFTER_READS=0`` | writes on a stream of their own, free to overlap reads (on: writes queue behind reads) |

@@ -5,6 +5,7 @@ completions, LoadGateError carrying the failed chunk range).
 """
 from __future__ import annotations
 
+import time
 from typing import Callable, Iterable
 
 
@@ -27,6 +28,11 @@ class AggregateCompletion:
 
     def query(self) -> bool:
         return self._done or all(p.query() for p in self._parts)
+
+    def read_ms(self) -> float | None:
+        """The slowest part's read time, once every part knows its own (entities read in parallel)."""
+        times = [p.read_ms() if hasattr(p, "read_ms") else None for p in self._parts]
+        return None if not times or any(t is None for t in times) else max(times)
 
     def wait(self) -> None:
         if self._done:
@@ -71,3 +77,48 @@ class PostCompletion:
         self._done = True
         if self._after:
             self._after()
+
+
+class TimedCompletion:
+    """A restore's completion and its read time.
+
+    Device-timed between two events recorded on the IO stream around the
+    submission (the io kernel runs until its data is in place). When the read
+    finishes elsewhere (split completion: its drain is launched later, on
+    another stream), the read time is the host time from submission to the
+    first observation of completion instead. ``read_ms`` is None until known.
+    """
+
+    def __init__(self, inner, ev_start=None, ev_end=None, device_timed: bool = True, host_ms: float | None = None):
+        self._inner = inner
+        self._ev = (ev_start, ev_end) if device_timed and ev_start is not None else None
+        self._t0 = time.perf_counter()
+        self._host_ms: float | None = host_ms  # given when the read already finished (synchronous stores)
+
+    def __getattr__(self, name):
+        return getattr(self._inner, name)
+
+    def _mark(self) -> None:
+        if self._host_ms is None:
+            self._host_ms = (time.perf_counter() - self._t0) * 1e3
+
+    def query(self) -> bool:
+        done = self._inner.query()
+        if done:
+            self._mark()
+        return done
+
+    def wait(self, *a, **kw) -> None:
+        try:
+            self._inner.wait(*a, **kw)
+        finally:
+            self._mark()
+
+    def enqueue_wait(self, stream=None) -> None:
+        self._inner.enqueue_wait(stream)
+
+    def read_ms(self) -> float | None:
+        if self._ev is not None:
+            start, end = self._ev
+            return float(start.elapsed_time(end)) if end.query() else None
+        return self._host_ms

@@ -36,12 +36,12 @@ from typing import Sequence
 import numpy as np
 import torch
 
-from ..common.env import number, text
+from ..common.env import flag, number, text
 from ..common.observability import nvtx_range
 from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
 from ..parallel.green_context import configured_io_sms, io_stream_on_sms
-from .completion import AggregateCompletion, LoadGateError, PostCompletion
+from .completion import AggregateCompletion, LoadGateError, PostCompletion, TimedCompletion
 from .staging import StagingBuffer
 
 LOG = logging.getLogger("tutti_b200.engine")
@@ -80,6 +80,10 @@ class LayerwiseReadPlan:
         self._closed = False
         self.t_submit0 = time.perf_counter()
         self.read_done_s: float | None = None
+        # read time: the IO stream's events around all layers; with split completion the
+        # last drain runs on the consumer stream, so the end is recorded there instead
+        self._ev_start: torch.cuda.Event | None = None
+        self._ev_end_consumer: torch.cuda.Event | None = None
         self._thread = threading.Thread(target=self._feed, name="tutti-feeder", daemon=True)
         self._thread.start()
 
@@ -88,12 +92,15 @@ class LayerwiseReadPlan:
         dev = self.engine.device
         try:
             torch.cuda.set_device(dev)
+            start = torch.cuda.Event(enable_timing=True)
+            start.record(self.io_stream)
+            self._ev_start = start
             for li, layer in enumerate(self.layers):
                 if self._closed:
                     break
                 with nvtx_range(f"tutti.layer_load|layer={layer}|chunks={len(self.keys)}"):
                     comp = store.get_paged(self.keys, self.block_table, layers=[layer], stream=self.io_stream)
-                ev = torch.cuda.Event()
+                ev = torch.cuda.Event(enable_timing=True)
                 ev.record(self.io_stream)
                 with self._cv:
                     self._comps.append(comp)
@@ -128,6 +135,10 @@ class LayerwiseReadPlan:
                 comp.enqueue_wait(torch.cuda.current_stream())
             else:
                 torch.cuda.current_stream().wait_event(ev)
+            if layer == self.layers[-1] and self.engine.split_completion:
+                end = torch.cuda.Event(enable_timing=True)
+                end.record(torch.cuda.current_stream())
+                self._ev_end_consumer = end
 
     def finish(self) -> None:
         """Host-wait for every layer; raises LoadGateError listing the failed chunks."""
@@ -152,6 +163,14 @@ class LayerwiseReadPlan:
             self.finish()
         except LoadGateError:
             pass
+
+    def read_ms(self) -> float | None:
+        """Device time from the first layer's submission to the last layer's data, once known."""
+        start = self._ev_start
+        end = self._ev_end_consumer if self.engine.split_completion else self._events.get(self.layers[-1])
+        if start is None or end is None or not end.query():
+            return None
+        return float(start.elapsed_time(end))
 
 
 class KVEngine:
@@ -295,13 +314,27 @@ class KVEngine:
         self.stats["read_chunks"] += len(keys)
         return LayerwiseReadPlan(self, keys, self._table(block_table), layers, self.io_stream, window)
 
+    @property
+    def split_completion(self) -> bool:
+        """Reads finish in a drain launched on the consumer's stream (or by the host fallback)."""
+        opts = getattr(self.store, "runtime_options", None) or {}
+        return bool(opts.get("async_completion")) or flag("TUTTI_ASYNC_COMPLETION")
+
     def load(self, keys: Sequence[bytes], block_table, layers: Sequence[int] | None = None):
-        """Restore all (or ``layers``) of ``keys`` in one submission; returns a completion."""
+        """Restore all (or ``layers``) of ``keys`` in one submission; returns a completion with ``read_ms()``."""
         bt = self._table(block_table)
         if not self.staged:
             self.stats["read_chunks"] += len(keys)
-            return self.store.get_paged(keys, bt, layers=layers, stream=self.io_stream)
-        return self._staged_load(keys, bt)
+            s = self.io_stream
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record(s)
+            comp = self.store.get_paged(keys, bt, layers=layers, stream=s)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record(s)
+            return TimedCompletion(comp, ev0, ev1, device_timed=not self.split_completion)
+        t0 = time.perf_counter()
+        comp = self._staged_load(keys, bt)
+        return TimedCompletion(comp, device_timed=False, host_ms=(time.perf_counter() - t0) * 1e3)
 
     def _staging(self, direction: str) -> StagingBuffer:
         buf = self._staging_bufs.get(direction)

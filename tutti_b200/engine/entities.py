@@ -52,6 +52,11 @@ class _MultiPlan:
             if hasattr(p, "abort"):
                 p.abort()
 
+    def read_ms(self) -> float | None:
+        """The slowest entity's read time (entities read in parallel), once every plan knows its own."""
+        times = [p.read_ms() if hasattr(p, "read_ms") else None for p in self._plans]
+        return None if any(t is None for t in times) else max(times)
+
 
 class _Stores:
     def __init__(self, engines):

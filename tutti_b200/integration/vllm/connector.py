@@ -53,11 +53,12 @@ class TuttiConnectorV1(KVConnectorBase_V1):
         self._sched: SchedulerSide | None = None
         self._worker: WorkerSide | None = None
         if role == KVConnectorRole.SCHEDULER:
-            bytes_per_token = 1
             capacity = self.cfg.capacity_chunks or 1 << 20
+            total_blocks = getattr(kv_cache_config, "num_blocks", None) if kv_cache_config is not None else None
             self._sched = SchedulerSide(self.block_size, self.cfg.chunk_tokens, capacity, self.tp_size,
                                         namespace=self.cfg.namespace.encode(),
-                                        policy=LoadPolicy(self.cfg.load_mode, bytes_per_token=max(1, bytes_per_token)))
+                                        policy=LoadPolicy(self.cfg.load_mode, free_ratio=self.cfg.async_load_free_ratio),
+                                        total_blocks=total_blocks)
             self._async_pending: dict[str, bool] = {}
             self._cold_start()
         else:
@@ -124,12 +125,12 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                 if new_blocks:
                     blocks += list(new_blocks[0])
                 scheduled.append((rid, blocks, cached.num_computed_tokens[i], n))
-        return self._sched.build_meta(scheduled)
+        return self._sched.build_meta(scheduled, getattr(scheduler_output, "total_num_scheduled_tokens", None))
 
     def update_connector_output(self, connector_output) -> None:
         wm = getattr(connector_output, "kv_connector_worker_meta", None)
-        if isinstance(wm, TuttiWorkerMetadata):
-            self._sched.update_from_workers(wm)
+        received = getattr(connector_output, "finished_recving", None) or ()
+        self._sched.update_from_workers(wm if isinstance(wm, TuttiWorkerMetadata) else None, received)
 
     def request_finished(self, request, block_ids: list[int]) -> tuple[bool, dict[str, Any] | None]:
         self._sched.request_finished(request.request_id)
@@ -155,7 +156,9 @@ class TuttiConnectorV1(KVConnectorBase_V1):
         self._last_worker_meta = self._worker.wait_for_save(meta)
 
     def build_connector_worker_meta(self):
-        return getattr(self, "_last_worker_meta", None)
+        # once per step: a step without wait_for_save must not resend the last one's commits
+        meta, self._last_worker_meta = getattr(self, "_last_worker_meta", None), None
+        return meta
 
     def get_finished(self, finished_req_ids: set[str]):
         return self._worker.get_finished(finished_req_ids)

@@ -64,11 +64,12 @@ class ConnectorConfig:
     stored_format: str = "native"  # or "fp8_block128": E4M3 + 1x128 scales on disk, fused in the io kernel
     defer_writes_after_reads: bool | None = None  # None: TUTTI_DEFER_WRITES_AFTER_READS, else on
     store_options: dict = field(default_factory=dict)  # a registered third-party store type's own options
+    async_load_free_ratio: float = 0.5  # async loads may hold this share of the blocks running requests leave
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
         extra = dict(extra or {})
-        known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store"}
+        known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio"}
         unknown = set(extra) - known
         if unknown:
             raise ValueError(f"unknown connector options: {sorted(unknown)}")
@@ -77,6 +78,11 @@ class ConnectorConfig:
         c.namespace = str(extra.get("namespace", ""))
         c.load_mode = extra.get("load_mode", text("TUTTI_LOAD_MODE", c.load_mode))
         c.failure_policy = extra.get("kv_load_failure_policy", c.failure_policy)
+        from .load_policy import MODES, resolve_free_ratio
+
+        if c.load_mode not in MODES:
+            raise ValueError(f"load_mode must be one of {MODES}, got {c.load_mode!r}")
+        c.async_load_free_ratio = resolve_free_ratio(extra)
         st = dict(extra.get("store", {}))
         c.store_type = st.pop("type", c.store_type)
         if c.store_type == "tutti_nvme":

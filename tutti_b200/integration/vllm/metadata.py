@@ -41,14 +41,22 @@ class TuttiConnectorMetadata(_MetaBase):
     generation: int = 0
     loads: list[LoadSpec] = field(default_factory=list)
     saves: list[SaveSpec] = field(default_factory=list)
+    step_tokens: int = 0  # tokens this step computes (the workers' step-time samples are per token)
 
 
 @dataclass
 class TuttiWorkerMetadata(_WorkerMetaBase):
-    """Per-key count of ranks that committed it this step, plus failed load keys."""
+    """Per-key count of ranks that committed it this step, failed loads, and the rank's measurements.
+
+    ``read_samples``: (chunks, ms) of this rank's restores that finished (device-timed);
+    ``step_samples``: (tokens, ms) of steps without a synchronous read.
+    """
 
     committed: dict[bytes, int] = field(default_factory=dict)
     failed_loads: dict[str, int] = field(default_factory=dict)  # request id -> first failed token
+    generation: int = 0  # the connector metadata this step ran with
+    read_samples: list[tuple[int, float]] = field(default_factory=list)
+    step_samples: list[tuple[int, float]] = field(default_factory=list)
 
     def aggregate(self, other: "TuttiWorkerMetadata") -> "TuttiWorkerMetadata":
         merged = dict(self.committed)
@@ -57,4 +65,5 @@ class TuttiWorkerMetadata(_WorkerMetaBase):
         failed = dict(self.failed_loads)
         for r, t in other.failed_loads.items():
             failed[r] = min(t, failed.get(r, t))
-        return TuttiWorkerMetadata(merged, failed)
+        return TuttiWorkerMetadata(merged, failed, max(self.generation, other.generation),
+                                   self.read_samples + other.read_samples, self.step_samples + other.step_samples)

@@ -9,6 +9,10 @@
 * ``wait_for_save``: settles the loads (TP failure consensus: every rank
   agrees on the failed chunk range), then persists this step's new full
   chunks behind the forward's compute event and reports them committed.
+* Measurements for the scheduler's load policy, harvested without blocking
+  (a sample whose events have not completed waits for a later step):
+  ``read_samples`` (chunks, device ms) of finished restores and
+  ``step_samples`` (tokens, device ms) of forwards without a synchronous read.
 Parity: reference tutti/integration/vllm/worker.py:461-1822 (WorkerImpl,
 start_load_kv, wait_for_layer_load, save_kv_layer, wait_for_save,
 _synchronize_load_failure, async loads).
@@ -128,6 +132,9 @@ class WorkerSide:
         self._finished_recv: set[str] = set()
         self._load_error_blocks: set[int] = set()
         self._meta = TuttiWorkerMetadata()
+        self._read_timing: list[tuple[int, object]] = []  # (chunks, plan or completion with read_ms())
+        self._step_timing: list[tuple[object, object, int]] = []  # (start, end, tokens) of steps w/o sync reads
+        self._step: tuple[object, int, bool] | None = None  # this step's start event, tokens, had sync loads
 
     # -- binding --------------------------------------------------------------
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
@@ -159,6 +166,10 @@ class WorkerSide:
                 self.health = HealthReporter(self.engine.store)
             self.health.maybe_log()
         sync = [l for l in meta.loads if not l.is_async]
+        if torch.cuda.is_available():
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._step = (ev, int(getattr(meta, "step_tokens", 0)), bool(sync))
         for spec in meta.loads:
             if spec.is_async:
                 comp = self.engine.load(spec.keys, np.asarray(spec.block_ids, dtype=np.int64))
@@ -197,6 +208,8 @@ class WorkerSide:
                 if mine:
                     local.append(ChunkFailure(ordinal, min(mine), max(mine) - min(mine) + 1))
                 base += len(spec.keys)
+        if not local and hasattr(self._plan, "read_ms"):
+            self._read_timing.append((sum(len(s.keys) for s in self._plan_loads), self._plan))
         cons = self.consensus.coordinate(generation, len(self._plan_loads), local)
         if cons.failed:
             if self.failure_policy == "fail":
@@ -211,7 +224,33 @@ class WorkerSide:
         self._plan = None
 
     # -- saves ----------------------------------------------------------------
+    def _harvest_samples(self) -> None:
+        """Move finished read and step timings into this step's metadata (never blocks)."""
+        keep = []
+        for chunks, src in self._read_timing[-64:]:
+            ms = src.read_ms()
+            if ms is None:
+                keep.append((chunks, src))
+            elif chunks > 0 and ms > 0:
+                self._meta.read_samples.append((chunks, ms))
+        self._read_timing = keep
+        pending = []
+        for start, end, tokens in self._step_timing[-64:]:
+            if not end.query():
+                pending.append((start, end, tokens))
+            elif tokens > 0:
+                self._meta.step_samples.append((tokens, float(start.elapsed_time(end))))
+        self._step_timing = pending
+
     def wait_for_save(self, meta: TuttiConnectorMetadata) -> TuttiWorkerMetadata:
+        self._meta.generation = meta.generation
+        if self._step is not None:
+            start, tokens, had_sync = self._step
+            self._step = None
+            if not had_sync:  # a synchronous read's stall says nothing about compute
+                end = torch.cuda.Event(enable_timing=True)
+                end.record()
+                self._step_timing.append((start, end, tokens))
         self._settle_sync_loads(meta.generation)
         if meta.saves:
             ev = torch.cuda.Event() if torch.cuda.is_available() and not self.engine.staged else None
@@ -236,6 +275,7 @@ class WorkerSide:
                 for k in spec.keys:
                     if k not in self._meta.committed and self.engine.index.is_resident(k):
                         self._meta.committed[k] = 1
+        self._harvest_samples()
         return self._meta
 
     # -- completion reporting -------------------------------------------------
@@ -245,6 +285,8 @@ class WorkerSide:
             if comp.query():
                 try:
                     comp.wait()
+                    if hasattr(comp, "read_ms"):
+                        self._read_timing.append((len(spec.keys), comp))
                 except Exception:  # noqa: BLE001
                     self._load_error_blocks.update(spec.block_ids)
                     self._meta.failed_loads[rid] = 0
