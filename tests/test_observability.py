@@ -60,7 +60,10 @@ def test_environment_switches(monkeypatch):
     assert runtime_option_defaults() == {"timing": True, "max_ctas_per_op": 48}
     monkeypatch.setenv("TUTTI_LOAD_MODE", "auto")
     assert ConnectorConfig.from_extra({}).load_mode == "auto"
-    assert ConnectorConfig.from_extra({"load_mode": "sync"}).load_mode == "sync"
+    assert ConnectorConfig.from_extra({"load_mode": "sync"}).load_mode == "auto"  # the variable wins
+    monkeypatch.delenv("TUTTI_LOAD_MODE")
+    assert ConnectorConfig.from_extra({"load_mode": "async"}).load_mode == "async"
+    assert ConnectorConfig.from_extra({}).load_mode == "sync"
     monkeypatch.delenv("TUTTI_IO_TIMING")
     monkeypatch.delenv("TUTTI_POOL_WORKERS")
     assert runtime_option_defaults() == {}

@@ -76,7 +76,8 @@ class ConnectorConfig:
         c = cls()
         c.chunk_tokens = int(extra.get("chunk_tokens", c.chunk_tokens))
         c.namespace = str(extra.get("namespace", ""))
-        c.load_mode = extra.get("load_mode", text("TUTTI_LOAD_MODE", c.load_mode))
+        # TUTTI_LOAD_MODE > load_mode in the connector config > sync
+        c.load_mode = str(text("TUTTI_LOAD_MODE") or extra.get("load_mode") or c.load_mode).strip().lower()
         c.failure_policy = extra.get("kv_load_failure_policy", c.failure_policy)
         from .load_policy import MODES, resolve_free_ratio
 
