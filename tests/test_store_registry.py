@@ -97,7 +97,8 @@ REFERENCE_MODULE_PATHS = {
     "storage.tutti_nvme.store": ["TuttiKVStore"], "storage.tutti_nvme.object_layout": [],
     "storage.tutti_nvme.layerwise_direct": ["page_geometry"],
     "storage.tutti_nvme.replica_direct": ["owner_index"],
-    "storage.tutti_nvme.runtime_factory": ["build_runtime"],
+    "storage.tutti_nvme.runtime_factory": ["build_runtime", "prepare_preset", "preset_mounts"],
+    "storage.tutti_nvme.preset_derive": ["daemon_config_paths"], "engine.staging": [],
 }
 
 

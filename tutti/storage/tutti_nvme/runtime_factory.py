@@ -1,5 +1,6 @@
 """``tutti.storage.tutti_nvme.runtime_factory``: native runtimes from a YAML spec or a preset (tutti_b200's)."""
 from tutti_b200._native import core as _core
+from tutti_b200.storage.preset import normalize_preset, prepare_preset, preset_mounts  # noqa: F401
 
 
 def build_runtime_from_config(text: str):

@@ -65,6 +65,7 @@ class ConnectorConfig:
     defer_writes_after_reads: bool | None = None  # None: TUTTI_DEFER_WRITES_AFTER_READS, else on
     store_options: dict = field(default_factory=dict)  # a registered third-party store type's own options
     async_load_free_ratio: float = 0.5  # async loads may hold this share of the blocks running requests leave
+    preset: dict | None = None  # drives by device id (daemon config, device groups), when mounts are not given
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
@@ -100,10 +101,10 @@ class ConnectorConfig:
             return c
         preset = opts.pop("preset", None)
         if preset is not None:
-            # drive presets (raid0 / device groups / daemon configs) name real NVMe devices; this
-            # build's drives are the emulated controllers over `mounts`, so only the layout is kept
-            LOG.info("[tutti] store preset %r: drives are emulated over the store's mounts",
-                     preset.get("type") if isinstance(preset, dict) else preset)
+            if not isinstance(preset, dict):
+                raise ValueError("store.options.preset must be a mapping")
+            # the drives a rank uses, by device id; mounts are derived per rank (storage/preset.py)
+            c.preset = dict(preset)
         for k in ("root", "capacity", "capacity_chunks", "mounts", "segment_file_slots", "runtime_options",
                   "stored_format", "defer_writes_after_reads"):
             if k in opts:
@@ -147,6 +148,18 @@ def geometry_from_layers(tensors: list[torch.Tensor], chunk_tokens: int, name: s
                       planes=planes, dtype=t.dtype, chunk_tokens=chunk_tokens)
 
 
+def store_mounts(cfg: ConnectorConfig, rank: int, local_rank: int, world: int) -> list[str]:
+    """The store's mounts: explicit ``mounts``, else those of the preset's drives for this rank."""
+    if cfg.mounts or not cfg.preset:
+        return [expand(m, rank, local_rank) for m in cfg.mounts]
+    from ...storage.preset import prepare_preset, preset_mounts
+
+    prepared = prepare_preset(cfg.preset, rank=rank, tp_size=max(1, world))
+    mounts = [expand(m, rank, local_rank) for m in preset_mounts(prepared)]
+    LOG.info("[tutti] rank %d: %s preset -> drives at %s", rank, prepared["type"], mounts)
+    return mounts
+
+
 def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, local_rank: int, world: int,
                 entity: str = ""):
     """The engine of one KV entity ("" is the main KV; others get their own namespace and root).
@@ -166,7 +179,7 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
         kind = "memory"  # the io kernel needs the pool in HBM
     if kind == "tutti":
         options = {"root": expand(cfg.root, rank, local_rank),
-                   "mounts": [expand(m, rank, local_rank) for m in cfg.mounts],
+                   "mounts": store_mounts(cfg, rank, local_rank, world),
                    "segment_file_slots": cfg.segment_file_slots, "runtime_options": cfg.runtime_options,
                    "stored_format": cfg.stored_format}
     elif kind == "memory":
