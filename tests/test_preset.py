@@ -68,3 +68,17 @@ def test_connector_config_takes_its_mounts_from_the_preset(daemons):
     explicit = ConnectorConfig.from_extra({"store": {"type": "tutti_nvme", "options": {
         "root": "/kv", "mounts": ["/a{LOCAL_RANK}"], "preset": {"type": "local", "device_id": 0}}}})
     assert store_mounts(explicit, rank=0, local_rank=5, world=1) == ["/a5"]  # explicit mounts win
+
+
+def test_preset_from_environment_is_parsed_and_checked(monkeypatch, daemons):
+    from tutti_b200.storage.preset import runtime_from_env
+
+    monkeypatch.delenv("TUTTI_NVME_PRESET", raising=False)
+    with pytest.raises(ValueError, match="not set"):
+        runtime_from_env()
+    monkeypatch.setenv("TUTTI_NVME_PRESET", "[1, 2]")
+    with pytest.raises(ValueError, match="mapping"):
+        runtime_from_env()
+    monkeypatch.setenv("TUTTI_NVME_PRESET", '{"type": "local", "device_id": 7, "daemon_config": "%s"}' % daemons)
+    with pytest.raises(ValueError, match="device id 7"):
+        runtime_from_env()

@@ -130,3 +130,27 @@ def preset_mounts(preset: dict) -> list[str]:
         if m not in mounts:
             mounts.append(str(m))
     return mounts
+
+
+def runtime_from_preset(preset: dict, accel_id: int = 0, options: dict | None = None, rank: int = 0,
+                        tp_size: int = 1):
+    """A GPU-initiated NVMe runtime over the preset's drives (one controller per drive mount)."""
+    from .._native import core
+
+    mounts = preset_mounts(prepare_preset(preset, rank=rank, tp_size=tp_size))
+    return core().make_emulated_nvme_runtime(int(accel_id), mounts, dict(options or {}))
+
+
+def runtime_from_env(accel_id: int = 0, options: dict | None = None):
+    """The runtime ``TUTTI_NVME_PRESET`` describes: an inline YAML/JSON mapping or a file holding one."""
+    import os
+
+    import yaml
+
+    raw = os.environ.get("TUTTI_NVME_PRESET", "").strip()
+    if not raw:
+        raise ValueError("TUTTI_NVME_PRESET is not set (an inline YAML/JSON preset or a file path)")
+    preset = yaml.safe_load(Path(raw).read_text() if os.path.isfile(raw) else raw)
+    if not isinstance(preset, dict):
+        raise ValueError("TUTTI_NVME_PRESET must hold a mapping")
+    return runtime_from_preset(preset, accel_id, options)
