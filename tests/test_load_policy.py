@@ -114,3 +114,13 @@ def test_stale_pending_saves_are_reclaimed_by_the_step_loop():
     for _ in range(70):  # no rank ever reports the save
         s.build_meta([])
     assert not any(s.index.is_pending(x) for x in k)
+
+
+def test_retrieve_limits():
+    s = SchedulerSide(BS, CHUNK, capacity_chunks=64, min_retrieve_tokens=17, max_tokens_per_load=20)
+    r, _ = _resident_request(s, "a", 41)  # 5 chunks, 40 loadable
+    assert s.get_num_new_matched_tokens(r, 0)[0] == 16  # capped at 20 -> whole chunks: 16
+    assert s.get_num_new_matched_tokens(r, 24)[0] == 0  # the 16 tokens left are below the minimum
+    s2 = SchedulerSide(BS, CHUNK, capacity_chunks=64, min_retrieve_tokens=17)
+    r2, _ = _resident_request(s2, "b", 17)
+    assert s2.get_num_new_matched_tokens(r2, 0)[0] == 0  # a 16-token hit is below the minimum

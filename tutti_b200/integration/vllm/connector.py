@@ -46,6 +46,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
         ktc = vllm_config.kv_transfer_config
         extra = getattr(ktc, "kv_connector_extra_config", None) or {}
         self.cfg = ConnectorConfig.from_extra(extra)
+        if "kv_load_failure_policy" not in extra and getattr(ktc, "kv_load_failure_policy", None):
+            self.cfg.failure_policy = str(ktc.kv_load_failure_policy)  # vLLM's own field (Tutti's sample config)
         cache = vllm_config.cache_config
         self.block_size = int(cache.block_size)
         par = vllm_config.parallel_config
@@ -58,7 +60,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
             self._sched = SchedulerSide(self.block_size, self.cfg.chunk_tokens, capacity, self.tp_size,
                                         namespace=self.cfg.namespace.encode(),
                                         policy=LoadPolicy(self.cfg.load_mode, free_ratio=self.cfg.async_load_free_ratio),
-                                        total_blocks=total_blocks)
+                                        total_blocks=total_blocks, min_retrieve_tokens=self.cfg.min_retrieve_tokens,
+                                        max_tokens_per_load=self.cfg.max_tokens_per_load)
             self._async_pending: dict[str, bool] = {}
             self._cold_start()
         else:
@@ -69,7 +72,7 @@ class TuttiConnectorV1(KVConnectorBase_V1):
             self._worker = WorkerSide(lambda tensors, entity="": make_engine(self.cfg, tensors, rank, local_rank,
                                                                              world, entity),
                                       block_size=self.block_size, chunk_tokens=self.cfg.chunk_tokens,
-                                      tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group),
+                                      tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group, self.cfg.failure_timeout_s),
                                       failure_policy=self.cfg.failure_policy)
 
     def _cold_start(self) -> None:

@@ -3,11 +3,16 @@
 ``kv_connector_extra_config`` keys:
   chunk_tokens             reuse unit in tokens (multiple of the engine block size; default 256)
   namespace                key-chain namespace (default: model name + dtype)
-  load_mode                sync | async | auto (default sync: layerwise restore inside the forward)
-  kv_load_failure_policy   recompute | fail (default recompute)
+  load_mode                sync | async | auto (default sync: layerwise restore inside the forward;
+                           TUTTI_LOAD_MODE overrides)
+  async_load_free_ratio    share of free blocks asynchronous loads may hold (default 0.5)
+  min_retrieve_tokens      hits shorter than this are computed instead of loaded (default 0)
+  max_tokens_per_load      cap on the tokens one request loads at once (default 0: no cap)
+  failure_collective_timeout_s  TP failure-consensus timeout (default 30)
+  kv_load_failure_policy   recompute | fail (default: the kv_transfer_config's own field, else recompute)
   store:
-    type                   tutti | memory (tutti_nvme: the reference's name for tutti)
-    options                the reference's nesting of root / capacity / preset (accepted)
+    type                   tutti | memory | a registered plugin type (tutti_nvme: Tutti's name for tutti)
+    options                Tutti's nesting of root / capacity / preset (drives by device id)
     root                   namespace root (per-rank segment files under <mount>/r<rank>)
     mounts                 backing mounts, one emulated NVMe drive each (default [root])
     capacity_chunks        capacity in chunks (or capacity: "64GiB")
@@ -66,11 +71,15 @@ class ConnectorConfig:
     store_options: dict = field(default_factory=dict)  # a registered third-party store type's own options
     async_load_free_ratio: float = 0.5  # async loads may hold this share of the blocks running requests leave
     preset: dict | None = None  # drives by device id (daemon config, device groups), when mounts are not given
+    min_retrieve_tokens: int = 0
+    max_tokens_per_load: int = 0
+    failure_timeout_s: float = 30.0
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
         extra = dict(extra or {})
-        known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio"}
+        known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio",
+                 "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s"}
         unknown = set(extra) - known
         if unknown:
             raise ValueError(f"unknown connector options: {sorted(unknown)}")
@@ -80,6 +89,11 @@ class ConnectorConfig:
         # TUTTI_LOAD_MODE > load_mode in the connector config > sync
         c.load_mode = str(text("TUTTI_LOAD_MODE") or extra.get("load_mode") or c.load_mode).strip().lower()
         c.failure_policy = extra.get("kv_load_failure_policy", c.failure_policy)
+        c.min_retrieve_tokens = int(extra.get("min_retrieve_tokens", 0))
+        c.max_tokens_per_load = int(extra.get("max_tokens_per_load", 0))
+        c.failure_timeout_s = float(extra.get("failure_collective_timeout_s", 30.0))
+        if c.min_retrieve_tokens < 0 or c.max_tokens_per_load < 0 or c.failure_timeout_s <= 0:
+            raise ValueError("min_retrieve_tokens and max_tokens_per_load must be >= 0, the timeout > 0")
         from .load_policy import MODES, resolve_free_ratio
 
         if c.load_mode not in MODES:

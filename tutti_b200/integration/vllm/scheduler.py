@@ -61,7 +61,7 @@ def _tokens(request) -> list[int]:
 class SchedulerSide:
     def __init__(self, block_size: int, chunk_tokens: int, capacity_chunks: int, tp_size: int = 1,
                  namespace: bytes = b"", policy: LoadPolicy | None = None, total_blocks: int | None = None,
-                 log_interval_s: float | None = None):
+                 log_interval_s: float | None = None, min_retrieve_tokens: int = 0, max_tokens_per_load: int = 0):
         if chunk_tokens % block_size:
             raise ValueError("chunk_tokens must be a multiple of the engine block size")
         self.block_size = block_size
@@ -74,6 +74,8 @@ class SchedulerSide:
         self.generation = 0
         self._planned: dict[bytes, str] = {}  # pending saves: key -> request
         self.total_blocks = total_blocks  # vLLM's KV pool size, when known
+        self.min_retrieve_tokens = min_retrieve_tokens  # shorter hits are computed instead
+        self.max_tokens_per_load = max_tokens_per_load  # 0: no cap
         self._live: dict[str, object] = {}  # request objects, for the block-usage estimate
         self._async_blocks: dict[str, int] = {}  # asynchronous loads not yet received -> blocks held
         self._sync_loads: dict[int, list[tuple[str, list[bytes]]]] = {}  # generation -> loads dispatched
@@ -128,6 +130,10 @@ class SchedulerSide:
         # loads start on a chunk boundary
         if num_computed_tokens % self.chunk_tokens:
             ext = 0
+        if self.min_retrieve_tokens and ext < self.min_retrieve_tokens:
+            ext = 0
+        if self.max_tokens_per_load:
+            ext = min(ext, self.max_tokens_per_load // self.chunk_tokens * self.chunk_tokens)
         if ext == 0:
             return 0, False
         self.profile["hit_tokens"] += ext
