@@ -46,8 +46,11 @@ class TuttiConnectorV1(KVConnectorBase_V1):
         ktc = vllm_config.kv_transfer_config
         extra = getattr(ktc, "kv_connector_extra_config", None) or {}
         self.cfg = ConnectorConfig.from_extra(extra)
-        if "kv_load_failure_policy" not in extra and getattr(ktc, "kv_load_failure_policy", None):
-            self.cfg.failure_policy = str(ktc.kv_load_failure_policy)  # vLLM's own field (Tutti's sample config)
+        vllm_policy = getattr(ktc, "kv_load_failure_policy", None)
+        if vllm_policy and "kv_load_failure_policy" in extra and extra["kv_load_failure_policy"] != vllm_policy:
+            LOG.warning("[tutti] kv_load_failure_policy %r in the connector config is ignored: vLLM applies "
+                        "its own kv_transfer_config.kv_load_failure_policy (%r)", extra["kv_load_failure_policy"],
+                        vllm_policy)
         cache = vllm_config.cache_config
         self.block_size = int(cache.block_size)
         par = vllm_config.parallel_config
@@ -73,7 +76,9 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                                                              world, entity),
                                       block_size=self.block_size, chunk_tokens=self.cfg.chunk_tokens,
                                       tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group, self.cfg.failure_timeout_s),
-                                      failure_policy=self.cfg.failure_policy)
+                                      # vLLM's scheduler applies kv_load_failure_policy (recompute or fail the
+                                      # requests) to the blocks the worker reports; the worker only reports
+                                      failure_policy="recompute")
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""

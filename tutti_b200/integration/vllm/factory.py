@@ -9,7 +9,8 @@
   min_retrieve_tokens      hits shorter than this are computed instead of loaded (default 0)
   max_tokens_per_load      cap on the tokens one request loads at once (default 0: no cap)
   failure_collective_timeout_s  TP failure-consensus timeout (default 30)
-  kv_load_failure_policy   recompute | fail (default: the kv_transfer_config's own field, else recompute)
+  kv_load_failure_policy   recompute | fail: vLLM's own kv_transfer_config field governs, applied by
+                           vLLM's scheduler to the blocks the worker reports as failed
   store:
     type                   tutti | memory | a registered plugin type (tutti_nvme: Tutti's name for tutti)
     options                Tutti's nesting of root / capacity / preset (drives by device id)
