@@ -202,7 +202,15 @@ def test_connector_class_with_vllm_base():
                                                               num_computed_tokens=0)],
                           num_scheduled_tokens={"q": 20}, scheduled_cached_reqs=None)
     meta = sch.build_connector_meta(out)
-    assert len(meta.saves) == 1 and len(meta.saves[0].keys) == 2
+    assert len(meta.saves) == 1 and len(meta.saves[0].keys) == 2 and meta.step_tokens == 20
+    # the step's output: both ranks' commits, no async receipts
+    wm = TuttiWorkerMetadata({k: 1 for k in meta.saves[0].keys}, generation=meta.generation)
+    sch.update_connector_output(SimpleNamespace(kv_connector_worker_meta=wm, finished_recving=None))
+    assert all(sch._sched.index.is_resident(k) for k in meta.saves[0].keys)
+    sch.update_connector_output(SimpleNamespace(kv_connector_worker_meta=None, finished_recving={"q"}))
+    # vLLM's pool size reaches the load policy's block estimate
+    sch2 = TuttiConnectorV1(cfg, KVConnectorRole.SCHEDULER, SimpleNamespace(num_blocks=1234))
+    assert sch2._sched.total_blocks == 1234
 
 
 def test_kv_layer_layouts_normalise_to_planes_first():
