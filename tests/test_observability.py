@@ -95,3 +95,19 @@ def test_write_ordering_and_prp_mode_switches(monkeypatch):
     monkeypatch.setenv("TUTTI_PRP_MODE", "lazy")
     with pytest.raises(ValueError):
         prp_mode()
+
+
+def test_latency_percentiles_in_the_health_line():
+    import tutti_b200.common.observability as obs
+
+    fresh = obs.Metrics()
+    for v in range(1, 101):
+        fresh.observe("restore_ms", float(v))
+    assert fresh.percentiles("restore_ms") == {"p50": 51.0, "p99": 100.0}
+    assert fresh.percentiles("nothing_ms") is None
+    m = obs.metrics()  # the process-wide one the health line reads
+    m._windows.pop("restore_ms", None)
+    for v in range(1, 101):
+        m.observe("restore_ms", float(v))
+    r = obs.HealthReporter(interval_s=0).report()
+    assert r["restore_ms_p50"] == 51.0 and r["restore_ms_p99"] == 100.0

@@ -14,6 +14,7 @@ tutti/integration/vllm/connector.py:555-677 (health and profile logs).
 """
 from __future__ import annotations
 
+import collections
 import contextlib
 import logging
 import os
@@ -53,6 +54,7 @@ class Metrics:
     def __init__(self):
         self._mu = threading.Lock()
         self._v = {n: 0 for n in self.NAMES}
+        self._windows: dict[str, collections.deque] = {}
         self._prom = None
         port = os.environ.get("TUTTI_METRICS_PORT")
         if port:
@@ -75,6 +77,24 @@ class Metrics:
     def snapshot(self) -> dict:
         with self._mu:
             return dict(self._v)
+
+    # -- latency windows (the last WINDOW samples of each kind) -------------------
+    WINDOW = 2048
+
+    def observe(self, name: str, value_ms: float) -> None:
+        with self._mu:
+            w = self._windows.get(name)
+            if w is None:
+                w = self._windows[name] = collections.deque(maxlen=self.WINDOW)
+            w.append(float(value_ms))
+
+    def percentiles(self, name: str, qs=(0.5, 0.99)) -> dict[str, float] | None:
+        """``{"p50": ..., "p99": ...}`` over the window (nearest rank), or None without samples."""
+        with self._mu:
+            w = sorted(self._windows.get(name, ()))
+        if not w:
+            return None
+        return {f"p{round(q * 100)}": w[min(len(w) - 1, int(q * len(w)))] for q in qs}
 
 
 _metrics: Metrics | None = None
@@ -106,6 +126,10 @@ class HealthReporter:
         out = {"restore_GBps": (cur["restore_bytes"] - self._last["restore_bytes"]) / dt / 1e9,
                "store_GBps": (cur["store_bytes"] - self._last["store_bytes"]) / dt / 1e9,
                "failed_ops": cur["failed_ops"], "ops": cur["restore_ops"] + cur["store_ops"]}
+        for kind in ("restore", "store"):
+            pct = metrics().percentiles(f"{kind}_ms")
+            if pct:  # submit to first observed completion, per op
+                out.update({f"{kind}_ms_{k}": v for k, v in pct.items()})
         st = self.store
         if st is not None:
             out["inflight"] = len(getattr(st, "_inflight", ()))

@@ -81,6 +81,8 @@ class NativeCompletion:
         self._done = False
         self._results: list[dict] = []
         self.nbytes = nbytes
+        self._t0 = time.perf_counter()
+        self._latency_ms: float | None = None
         # enqueue_wait may race a host wait on another thread (e.g. a feeder's
         # window bound): handles are released, and _done set, only under this lock
         self._mu = threading.Lock()
@@ -88,7 +90,10 @@ class NativeCompletion:
     def query(self) -> bool:
         if self._done:
             return True
-        return all(self._rt.query_io(io) != "in_flight" for io in self._ios)
+        done = all(self._rt.query_io(io) != "in_flight" for io in self._ios)
+        if done and self._latency_ms is None:
+            self._latency_ms = (time.perf_counter() - self._t0) * 1e3
+        return done
 
     def enqueue_wait(self, stream: torch.cuda.Stream | None = None) -> None:
         """Order ``stream`` after this batch's io kernels (no host wait)."""
@@ -122,6 +127,9 @@ class NativeCompletion:
                 kinds.add(r["failure_kind"])
         m = metrics()
         m.add(f"{self.kind}_ops")
+        if self._latency_ms is None:
+            self._latency_ms = (time.perf_counter() - self._t0) * 1e3
+        m.observe(f"{self.kind}_ms", self._latency_ms)
         if failed:
             m.add("failed_ops")
             m.add("failed_requests", len(failed))
