@@ -3,6 +3,8 @@ import json
 import subprocess
 import sys
 
+import pytest
+
 
 def test_status_json_reports_native_pieces(capsys):
     from tutti_b200.cli import main
@@ -41,3 +43,30 @@ def test_topology_command_on_empty_sysfs(tmp_path, capsys):
 
     assert main(["topology", "--sysfs", str(tmp_path)]) == 0
     assert json.loads(capsys.readouterr().out) == {"gpus": [], "drives": [], "affine_gpus": []}
+
+
+def test_vllm_config_and_serve_command(capsys):
+    import json
+
+    from tutti_b200.cli import main
+    from tutti_b200.integration.vllm.factory import ConnectorConfig
+
+    assert main(["vllm-config", "--root", "/kv/{LOCAL_RANK}", "--capacity", "64 GiB", "--load-mode", "auto",
+                 "--preset", '{"type": "nvme-device-group", "device_groups": [[0], [1]]}']) == 0
+    ktc = json.loads(capsys.readouterr().out)
+    assert ktc["kv_connector_module_path"] == "tutti.integration.vllm.connector"
+    c = ConnectorConfig.from_extra(ktc["kv_connector_extra_config"])
+    assert c.capacity_bytes == 64 << 30 and c.load_mode == "auto" and c.preset["device_groups"] == [[0], [1]]
+    assert main(["vllm-serve", "/models/llama", "--root", "/kv", "--dry-run", "--", "--tensor-parallel-size", "8"]) == 0
+    out = capsys.readouterr().out
+    assert out.startswith("vllm serve /models/llama --kv-transfer-config '{") and "--tensor-parallel-size 8" in out
+    with pytest.raises(ValueError):  # a bad config fails before vLLM starts
+        main(["vllm-config", "--root", "/kv", "--preset", '["not", "a", "mapping"]'])
+
+
+def test_test_command_runs_the_suites(capsys):
+    from tutti_b200.cli import main
+
+    assert main(["test", "--dry-run", "-k", "cli"]) == 0
+    out = capsys.readouterr().out.splitlines()
+    assert "-m not gpu" in out[0] and out[0].endswith("-k cli") and out[1].endswith("tutti_native_tests")

@@ -7,11 +7,15 @@
     python -m tutti_b200 fiemap FILE           # extents the FIEMAP resolver sees
     python -m tutti_b200 probe-raid0 md0 [--sysfs /sys]
     python -m tutti_b200 topology [--sysfs /sys]   # NVMe drive -> affine GPU over the PCIe tree
-    python -m tutti_b200 bench {kernels,ttft,fanout,mla,trace} [args...]
+    python -m tutti_b200 bench {kernels,ttft,fanout,mla,trace,sweep,plumbing,vllm} [args...]
+    python -m tutti_b200 test [--gpu] [--dry-run] [pytest args...]   # pytest suites + C++ contract suite
+    python -m tutti_b200 vllm-config --root R [--mounts M ...] [--preset JSON] ...   # --kv-transfer-config JSON
+    python -m tutti_b200 vllm-serve MODEL --root R [...] [--dry-run] -- [vllm serve args...]
 
 Parity: reference scripts/tutti-env.sh (build, build-ext, test, daemon, status
-subcommands), scripts/tutti-md (md RAID0 inspection) and
-scripts/pci_topology_check.sh (drive / GPU switch affinity).
+subcommands), scripts/tutti-md (md RAID0 inspection),
+scripts/pci_topology_check.sh (drive / GPU switch affinity) and
+scripts/vllm/run/serve-8gpu-striped.sh (vLLM serve with the connector).
 """
 from __future__ import annotations
 
@@ -24,7 +28,8 @@ import sys
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
-BENCHES = {"kernels": "kernels", "ttft": "ttft", "fanout": "fanout", "mla": "mla_indexer", "trace": "serving_trace"}
+BENCHES = {"kernels": "kernels", "ttft": "ttft", "fanout": "fanout", "mla": "mla_indexer", "trace": "serving_trace",
+           "sweep": "io_sweep", "plumbing": "cpu_plumbing", "vllm": "vllm_e2e"}
 
 
 def _bin(name: str) -> str:
@@ -124,6 +129,67 @@ def cmd_bench(args) -> int:
     return int(rc or 0) if not isinstance(rc, dict) else 0
 
 
+def cmd_test(args) -> int:
+    cmds = [[sys.executable, "-m", "pytest", os.path.join(ROOT, "tests"), "-q", "-m", "gpu" if args.gpu else "not gpu",
+             *args.rest]]
+    if not args.gpu:
+        cmds.append([_bin("tutti_native_tests")])
+    for c in cmds:
+        if args.dry_run:
+            print(" ".join(c))
+            continue
+        rc = subprocess.run(c, cwd=ROOT).returncode
+        if rc:
+            return rc
+    return 0
+
+
+def kv_transfer_config(args) -> dict:
+    """The ``--kv-transfer-config`` of a vLLM deployment with this connector (Tutti's module path and schema)."""
+    options = {"root": args.root}
+    if args.mounts:
+        options["mounts"] = list(args.mounts)
+    if args.capacity:
+        options["capacity"] = args.capacity
+    if args.preset:
+        options["preset"] = json.loads(args.preset)
+    if args.stored_format != "native":
+        options["stored_format"] = args.stored_format
+    extra = {"chunk_tokens": args.chunk_tokens, "load_mode": args.load_mode,
+             "store": {"type": "tutti_nvme", "options": options}}
+    from .integration.vllm.factory import ConnectorConfig
+
+    ConnectorConfig.from_extra(extra)  # fail here, not inside vLLM's workers
+    return {"kv_connector": "TuttiConnectorV1", "kv_connector_module_path": "tutti.integration.vllm.connector",
+            "kv_role": "kv_both", "kv_load_failure_policy": args.failure_policy, "kv_connector_extra_config": extra}
+
+
+def cmd_vllm_config(args) -> int:
+    print(json.dumps(kv_transfer_config(args)))
+    return 0
+
+
+def cmd_vllm_serve(args) -> int:
+    rest = [a for a in args.rest if a != "--"]
+    cmd = ["vllm", "serve", args.model, "--kv-transfer-config", json.dumps(kv_transfer_config(args)), *rest]
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    if args.dry_run:
+        print(" ".join(cmd[:4]) + " '" + cmd[4] + "' " + " ".join(cmd[5:]))
+        return 0
+    return subprocess.run(cmd, env=env).returncode
+
+
+def _vllm_args(q) -> None:
+    q.add_argument("--root", required=True, help="store root ({LOCAL_RANK} / {RANK} expand per worker)")
+    q.add_argument("--mounts", nargs="*", default=[], help="one drive per mount")
+    q.add_argument("--capacity", default="", help='e.g. "64 GiB"')
+    q.add_argument("--preset", default="", help="drives by device id, as JSON (daemon_config, device_groups)")
+    q.add_argument("--chunk-tokens", type=int, default=256)
+    q.add_argument("--load-mode", choices=["sync", "async", "auto"], default="sync")
+    q.add_argument("--failure-policy", choices=["recompute", "fail"], default="recompute")
+    q.add_argument("--stored-format", choices=["native", "fp8_block128"], default="native")
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="python -m tutti_b200")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -150,7 +216,23 @@ def main(argv=None) -> int:
     b.add_argument("which", choices=sorted(BENCHES))
     b.add_argument("rest", nargs=argparse.REMAINDER)
     b.set_defaults(fn=cmd_bench)
-    args = p.parse_args(argv)
+    te = sub.add_parser("test")
+    te.add_argument("--gpu", action="store_true", help="the B200 suite instead of the host suites")
+    te.add_argument("--dry-run", action="store_true")
+    te.set_defaults(fn=cmd_test, passthrough=True)  # other arguments go to pytest
+    vc = sub.add_parser("vllm-config")
+    _vllm_args(vc)
+    vc.set_defaults(fn=cmd_vllm_config)
+    vs = sub.add_parser("vllm-serve")
+    vs.add_argument("model")
+    _vllm_args(vs)
+    vs.add_argument("--dry-run", action="store_true")
+    vs.set_defaults(fn=cmd_vllm_serve, passthrough=True)  # other arguments go to vllm serve
+    args, extra = p.parse_known_args(argv)
+    if extra and not getattr(args, "passthrough", False):
+        p.error(f"unrecognized arguments: {' '.join(extra)}")
+    if getattr(args, "passthrough", False):
+        args.rest = extra
     return args.fn(args)
 
 
