@@ -41,7 +41,7 @@ from ..common.observability import nvtx_range
 from ..index.chunk_index import ChunkIndex, StorePlan
 from ..models.kv_geometry import KVGeometry
 from ..parallel.green_context import configured_io_sms, io_stream_on_sms
-from .completion import AggregateCompletion, LoadGateError, PostCompletion, TimedCompletion
+from .completion import LoadGateError, PostCompletion, TimedCompletion
 from .staging import StagingBuffer
 
 LOG = logging.getLogger("tutti_b200.engine")

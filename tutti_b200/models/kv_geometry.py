@@ -15,7 +15,7 @@ layer l: for each block j of the chunk, plane 0 then plane 1.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 
