@@ -1,0 +1,91 @@
+"""One KV-engine contract over two stores: the staged in-memory store and the direct segment-file store.
+
+The segment-file store runs on the POSIX backend here (host pread/pwrite straight
+into a host-memory pool), so the direct paged path is exercised without a GPU.
+Parity: reference tests/python/storage/test_store_contract.py (one contract, Memory and Tutti stores).
+"""
+import numpy as np
+import pytest
+import torch
+
+from tutti_b200.engine.core import KVEngine
+from tutti_b200.index.chunk_index import chunk_keys_for_tokens
+from tutti_b200.models.kv_geometry import KVGeometry
+from tutti_b200.storage.memory import MemoryKVStore
+from tutti_b200.storage.tutti_store import TuttiKVStore
+
+G = KVGeometry("contract", num_layers=2, num_kv_heads=2, head_dim=64, block_size=16, chunk_tokens=32)
+CAP = 6
+
+
+def open_store(kind, root):
+    if kind == "memory":
+        s = MemoryKVStore(G.chunk_bytes, capacity_chunks=CAP)
+        s.open()
+        return s
+    return TuttiKVStore(root, G, capacity_chunks=CAP, mounts=[str(root / "m0"), str(root / "m1")], backend="posix",
+                        device=-1, segment_file_slots=4, runtime_options={"threads": 2, "direct_io": False}).open()
+
+
+@pytest.fixture(params=["memory", "segment-files"])
+def env(request, tmp_path):
+    store = open_store(request.param, tmp_path)
+    eng = KVEngine(store, G, capacity_chunks=CAP, device=torch.device("cpu"))
+    pool = torch.randn(G.pool_shape(64)).to(torch.bfloat16)
+    eng.bind(pool)
+    yield request.param, store, eng, pool, tmp_path
+    store.close()
+
+
+def keys_for(i, n=1):
+    return chunk_keys_for_tokens(list(range(i * 1000, i * 1000 + 32 * n)), 32)
+
+
+def test_roundtrip_to_other_blocks(env):
+    kind, store, eng, pool, _ = env
+    k = keys_for(0, 3)
+    eng.store_chunks(k, torch.arange(0, 6)).wait()
+    assert eng.lookup_prefix_keys(k) == 96
+    ref = pool[:, :, 0:6].clone()
+    eng.load(k, torch.tensor([40, 41, 50, 51, 60, 61])).wait()
+    got = pool[:, :, torch.tensor([40, 41, 50, 51, 60, 61])]
+    assert torch.equal(got, ref)
+    assert eng.store_chunks(k, torch.arange(0, 6)) is None  # resident chunks are not written again
+
+
+def test_capacity_closure_evicts_lru_but_never_pinned(env):
+    kind, store, eng, pool, _ = env
+    chunks = [keys_for(i) for i in range(CAP)]
+    for i, k in enumerate(chunks):
+        eng.store_chunks(k, torch.arange(2 * i, 2 * i + 2)).wait()
+    eng.pin(chunks[0])
+    eng.store_chunks(keys_for(100), torch.arange(20, 22)).wait()  # full: evicts the oldest unpinned
+    assert eng.lookup_prefix_keys(chunks[0]) == 32 and eng.lookup_prefix_keys(chunks[1]) == 0
+    ref = pool[:, :, 0:2].clone()
+    eng.load(chunks[0], torch.arange(30, 32)).wait()
+    assert torch.equal(pool[:, :, 30:32], ref)
+    with pytest.raises(Exception):  # the evicted chunk is gone from the store too
+        eng.load(chunks[1], torch.arange(32, 34)).wait()
+    eng.unpin(chunks[0])
+
+
+def test_a_fresh_engine_finds_persisted_chunks(env):
+    kind, store, eng, pool, root = env
+    k = keys_for(7, 2)
+    eng.store_chunks(k, torch.arange(4, 8)).wait()
+    eng.wait_idle()
+    if kind == "memory":
+        pytest.skip("the in-memory store does not outlive its process")
+    ref = pool[:, :, 4:8].clone()
+    store.objects.checkpoint()
+    store.close()
+    store2 = open_store(kind, root)
+    try:
+        eng2 = KVEngine(store2, G, capacity_chunks=CAP, device=torch.device("cpu"))
+        pool2 = torch.zeros(G.pool_shape(64), dtype=torch.bfloat16)
+        eng2.bind(pool2)
+        assert eng2.restore_from_store() == 2 and eng2.lookup_prefix_keys(k) == 64
+        eng2.load(k, torch.arange(10, 14)).wait()
+        assert torch.equal(pool2[:, :, 10:14], ref)
+    finally:
+        store2.close()

@@ -323,6 +323,13 @@ class KVEngine:
     def load(self, keys: Sequence[bytes], block_table, layers: Sequence[int] | None = None):
         """Restore all (or ``layers``) of ``keys`` in one submission; returns a completion with ``read_ms()``."""
         bt = self._table(block_table)
+        if not self.staged and self.pool.device.type != "cuda":
+            # a direct store serving host memory (e.g. the POSIX backend): host-executed, host-timed
+            self.stats["read_chunks"] += len(keys)
+            t0 = time.perf_counter()
+            comp = self.store.get_paged(keys, bt, layers=layers, stream=None)
+            comp.wait()
+            return TimedCompletion(comp, device_timed=False, host_ms=(time.perf_counter() - t0) * 1e3)
         if not self.staged:
             self.stats["read_chunks"] += len(keys)
             s = self.io_stream
