@@ -89,3 +89,17 @@ def test_a_fresh_engine_finds_persisted_chunks(env):
         assert torch.equal(pool2[:, :, 10:14], ref)
     finally:
         store2.close()
+
+
+def test_layerwise_plan_on_a_host_pool(env):
+    kind, store, eng, pool, _ = env
+    if kind == "memory":
+        pytest.skip("layerwise plans need a direct store")
+    k = keys_for(3, 2)
+    eng.store_chunks(k, torch.arange(0, 4)).wait()
+    ref = pool[:, :, 0:4].clone()
+    plan = eng.start_read_plan(k, torch.arange(20, 24))
+    for layer in range(G.num_layers):
+        plan.wait_layer(layer)
+    plan.finish()
+    assert torch.equal(pool[:, :, 20:24], ref) and plan.read_ms() is not None

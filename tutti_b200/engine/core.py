@@ -173,6 +173,25 @@ class LayerwiseReadPlan:
         return float(start.elapsed_time(end))
 
 
+class _WholeRestorePlan:
+    """The plan interface over one finished restore (a host-memory pool has no streams to overlap)."""
+
+    def __init__(self, comp):
+        self._comp = comp
+
+    def wait_layer(self, layer: int) -> None:
+        return None
+
+    def finish(self) -> None:
+        self._comp.wait()
+
+    def abort(self) -> None:
+        pass
+
+    def read_ms(self) -> float | None:
+        return self._comp.read_ms()
+
+
 class KVEngine:
     def __init__(self, store, geometry: KVGeometry, *, capacity_chunks: int | None = None,
                  namespace: bytes = b"", device: int | torch.device = 0, staged: bool | None = None,
@@ -311,6 +330,8 @@ class KVEngine:
             from ..common.errors import DirectTransferUnavailable
 
             raise DirectTransferUnavailable("layerwise plans need a direct (paged) store")
+        if self.pool.device.type != "cuda":
+            return _WholeRestorePlan(self.load(keys, block_table, layers))  # host pool: no streams to overlap
         self.stats["read_chunks"] += len(keys)
         return LayerwiseReadPlan(self, keys, self._table(block_table), layers, self.io_stream, window)
 
