@@ -676,6 +676,7 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
         Impl::DpEntry* d;
         std::vector<DataPathRequest> reqs;
         std::vector<std::uint32_t> idx;
+        std::uint64_t bytes = 0;
     };
     std::vector<Group> groups;
     groups.reserve(im.dps.size());
@@ -771,13 +772,24 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
             for (auto& x : groups)
                 if (x.d == d) gp = &x;
             if (!gp) {
-                groups.push_back({d, {}, {}});
+                groups.push_back({d, {}, {}, 0});
                 gp = &groups.back();
                 gp->reqs.reserve(count);
                 gp->idx.reserve(count);
             }
             last_gp = gp;
         }
+        // The DataPath's batch width is a hard limit: requests past it are rejected
+        // as exhausted (resubmit them), the rest of the batch proceeds.
+        const auto& wc = *caps;
+        if ((wc.max_batch_requests && gp->reqs.size() >= wc.max_batch_requests) ||
+            (wc.max_batch_bytes && gp->bytes + r.length > wc.max_batch_bytes)) {
+            const Status full{StatusCode::RESOURCE_EXHAUSTED, "batch width of " + d->key + " reached; resubmit"};
+            out.initial_states[i] = {IoRequestState::REJECTED, full};
+            if (first_reject.ok()) first_reject = full;
+            continue;
+        }
+        gp->bytes += r.length;
         gp->reqs.push_back({r, dpm, t->dpt});
         gp->idx.push_back(static_cast<std::uint32_t>(i));
     }

@@ -113,6 +113,25 @@ TEST(runtime_partial_commit) {
     CHECK(w.result->detail.confirmed_bytes == 1024);
 }
 
+TEST(runtime_enforces_the_data_path_batch_width) {
+    Fixture f;
+    f.dp.mutable_caps().max_batch_requests = 3;
+    IoRequest r[5] = {f.req(0, 4096), f.req(4096, 4096), f.req(8192, 4096), f.req(12288, 4096), f.req(16384, 4096)};
+    auto o = f.rt->submit(r, 5, f.ctx());
+    CHECK(o.io.has_value());
+    CHECK(o.initial_states[2].state == IoRequestState::ACCEPTED);
+    CHECK(o.initial_states[3].state == IoRequestState::REJECTED &&
+          o.initial_states[3].status.code() == StatusCode::RESOURCE_EXHAUSTED);
+    CHECK(f.rt->wait(*o.io, 1000).result->detail.confirmed_bytes == 3 * 4096);
+    CHECK(f.rt->release_io(*o.io).ok());
+    f.dp.mutable_caps().max_batch_requests = 0;
+    f.dp.mutable_caps().max_batch_bytes = 8192;  // by bytes: two 4 KiB requests per batch
+    o = f.rt->submit(r, 3, f.ctx());
+    CHECK(o.initial_states[1].state == IoRequestState::ACCEPTED && o.initial_states[2].state == IoRequestState::REJECTED);
+    CHECK(f.rt->wait(*o.io, 1000).observation_status.ok());
+    CHECK(f.rt->release_io(*o.io).ok());
+}
+
 TEST(runtime_all_rejected_has_no_io) {
     Fixture f;
     IoRequest r[1] = {f.req(0, 1 << 20)};  // beyond the target
