@@ -288,11 +288,61 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
 }
 
 Result<DataPathTarget> GpuNvmeDataPath::open(const ResolvedTarget& target) {
+    std::lock_guard<std::mutex> g(mu_);
+    std::vector<Upload> uploads;
+    auto r = open_locked(target, uploads);
+    if (!r.ok()) return r;
+    Status s = flush_uploads(uploads);
+    if (!s.ok()) return Result<DataPathTarget>::Failure(s);
+    return r;
+}
+
+std::vector<Result<DataPathTarget>> GpuNvmeDataPath::open_many(const ResolvedTarget* const* targets, std::size_t count) {
+    std::lock_guard<std::mutex> g(mu_);
+    std::vector<Result<DataPathTarget>> out;
+    out.reserve(count);
+    std::vector<Upload> uploads;
+    for (std::size_t i = 0; i < count; ++i) out.push_back(open_locked(*targets[i], uploads));
+    Status s = flush_uploads(uploads);
+    if (!s.ok())  // no target of the batch is usable without its device rows
+        for (auto& r : out)
+            if (r.ok()) r = Result<DataPathTarget>::Failure(s);
+    return out;
+}
+
+Status GpuNvmeDataPath::flush_uploads(std::vector<Upload>& uploads) {
+    // Caller holds mu_. Consecutive destinations (bump-allocated extents with
+    // under 256 bytes of alignment padding between them, fresh target rows)
+    // go up in one copy; the padding belongs to no target and is zero-filled.
+    if (uploads.empty()) return Status::Ok();
+    DeviceGuard guard(cfg_.accel_id);
+    std::size_t i = 0;
+    std::vector<char> run;
+    while (i < uploads.size()) {
+        char* start = uploads[i].dst;
+        run.assign(uploads[i].bytes.begin(), uploads[i].bytes.end());
+        std::size_t k = i + 1;
+        while (k < uploads.size() && uploads[k].dst >= start + run.size() &&
+               uploads[k].dst - (start + run.size()) < 256) {
+            run.resize(static_cast<std::size_t>(uploads[k].dst - start), 0);
+            run.insert(run.end(), uploads[k].bytes.begin(), uploads[k].bytes.end());
+            ++k;
+        }
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMemcpy(start, run.data(), run.size(), cudaMemcpyHostToDevice),
+                                          "upload target rows"));
+        i = k;
+    }
+    uploads.clear();
+    return Status::Ok();
+}
+
+Result<DataPathTarget> GpuNvmeDataPath::open_locked(const ResolvedTarget& target, std::vector<Upload>& uploads) {
+    // Caller holds mu_. Host-side work of an open; the device copies it owes are
+    // appended to `uploads` (flush_uploads).
     using R = Result<DataPathTarget>;
     auto pv = target.view<FileExtentPayload>(kFileExtentPayloadType, kFileExtentPayloadVersion);
     if (!pv.ok()) return R::Failure(pv.status());
     const FileExtentPayload& p = *pv.value();
-    std::lock_guard<std::mutex> g(mu_);
     if (!initialized_) return R::Failure({StatusCode::NOT_READY, "not initialized"});
     if (p.extents.empty() && p.file_size > 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "no extents"});
     for (const auto& e : p.extents)
@@ -334,9 +384,8 @@ Result<DataPathTarget> GpuNvmeDataPath::open(const ResolvedTarget& target) {
     auto* dex = reinterpret_cast<io::DevExtent*>(extent_chunks_.back() + extent_chunk_used_);
     extent_chunk_used_ += need;
     if (!ex.empty()) {
-        Status s = cuda_status(cudaMemcpy(dex, ex.data(), ex.size() * sizeof(ex[0]), cudaMemcpyHostToDevice),
-                               "upload extents");
-        if (!s.ok()) return R::Failure(s);
+        const char* b = reinterpret_cast<const char*>(ex.data());
+        uploads.push_back({reinterpret_cast<char*>(dex), std::vector<char>(b, b + ex.size() * sizeof(ex[0]))});
     }
     TargetRec& tr = targets_[row];
     tr.generation = next_token_++;
@@ -346,8 +395,8 @@ Result<DataPathTarget> GpuNvmeDataPath::open(const ResolvedTarget& target) {
     tr.open = true;
     io::DevTarget dt{dex, p.file_size, static_cast<std::uint32_t>(ex.size()),
                      static_cast<std::uint32_t>(tr.generation), 0};
-    Status s = cuda_status(cudaMemcpy(d_targets_ + row, &dt, sizeof(dt), cudaMemcpyHostToDevice), "upload target");
-    if (!s.ok()) return R::Failure(s);
+    const char* b = reinterpret_cast<const char*>(&dt);
+    uploads.push_back({reinterpret_cast<char*>(d_targets_ + row), std::vector<char>(b, b + sizeof(dt))});
     return DataPathTarget{row, tr.generation};
 }
 

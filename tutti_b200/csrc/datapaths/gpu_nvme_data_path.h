@@ -85,6 +85,7 @@ public:
     Status initialize(const DataPathConfig& config, ResourceProvider* resources) override;
     Status shutdown(std::uint64_t timeout_ns) override;
     Result<DataPathTarget> open(const ResolvedTarget& target) override;
+    std::vector<Result<DataPathTarget>> open_many(const ResolvedTarget* const* targets, std::size_t count) override;
     Status close(DataPathTarget target) override;
     Result<RegistrationDomainKey> registration_domain(DataPathTarget target) const override;
     Result<DataPathMemory> register_memory(const DataPathMemoryView& view,
@@ -188,6 +189,13 @@ private:
         std::chrono::steady_clock::time_point submitted_at{};
     };
 
+    // A host->device copy an open still owes (extents, a target row).
+    struct Upload {
+        char* dst;
+        std::vector<char> bytes;
+    };
+    Result<DataPathTarget> open_locked(const ResolvedTarget& target, std::vector<Upload>& uploads);
+    Status flush_uploads(std::vector<Upload>& uploads);
     Status init_device_side();
     Result<std::unique_ptr<Arena>> take_arena(std::size_t bytes);
     void return_arena(std::unique_ptr<Arena> a);

@@ -177,6 +177,15 @@ public:
     virtual Status shutdown(std::uint64_t timeout_ns) = 0;
 
     virtual Result<DataPathTarget> open(const ResolvedTarget& target) = 0;
+    // Several opens at once (StorageRuntime::open_batch): a DataPath may share
+    // per-open costs, e.g. device uploads, across the batch. Same results as
+    // calling open() on each target in order.
+    virtual std::vector<Result<DataPathTarget>> open_many(const ResolvedTarget* const* targets, std::size_t count) {
+        std::vector<Result<DataPathTarget>> out;
+        out.reserve(count);
+        for (std::size_t i = 0; i < count; ++i) out.push_back(open(*targets[i]));
+        return out;
+    }
     virtual Status close(DataPathTarget target) = 0;
     virtual Result<RegistrationDomainKey> registration_domain(DataPathTarget target) const = 0;
 

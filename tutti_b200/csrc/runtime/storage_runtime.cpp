@@ -591,6 +591,38 @@ std::vector<Result<TargetHandle>> StorageRuntime::open_batch(const std::vector<s
         for (auto& t : th) t.join();
     }
     std::lock_guard<std::mutex> g(im.mu);
+    // One open_many per DataPath (it may share per-open costs across the batch),
+    // then handles in input order.
+    std::vector<Impl::DpEntry*> dps(uris.size(), nullptr);
+    std::vector<std::optional<Result<DataPathTarget>>> opened(uris.size());
+    std::vector<std::pair<Impl::DpEntry*, std::vector<std::size_t>>> by_dp;
+    for (std::size_t i = 0; i < uris.size(); ++i) {
+        auto& r = *resolved[i];
+        if (!r.ok()) continue;
+        std::string key(r.value().recommended_data_path_key());
+        dps[i] = im.dp(key);
+        if (!dps[i]) {
+            opened[i] = Result<DataPathTarget>::Failure(
+                {StatusCode::NOT_FOUND, "no DataPath registered for key '" + key + "'"});
+            continue;
+        }
+        auto it = std::find_if(by_dp.begin(), by_dp.end(), [&](const auto& x) { return x.first == dps[i]; });
+        if (it == by_dp.end()) {
+            by_dp.push_back({dps[i], {}});
+            it = by_dp.end() - 1;
+        }
+        it->second.push_back(i);
+    }
+    for (auto& [d, idx] : by_dp) {
+        std::vector<const ResolvedTarget*> ts;
+        ts.reserve(idx.size());
+        for (auto i : idx) ts.push_back(&resolved[i]->value());
+        DeviceGuard dg(d->dp->capabilities().bound_accel_id);
+        auto res = d->dp->open_many(ts.data(), ts.size());
+        for (std::size_t k = 0; k < idx.size(); ++k)
+            opened[idx[k]] = k < res.size() ? std::move(res[k])
+                                            : Result<DataPathTarget>::Failure({StatusCode::INTERNAL, "missing open"});
+    }
     for (std::size_t i = 0; i < uris.size(); ++i) {
         auto& r = *resolved[i];
         if (!r.ok()) {
@@ -598,18 +630,13 @@ std::vector<Result<TargetHandle>> StorageRuntime::open_batch(const std::vector<s
             continue;
         }
         const ResolvedTarget& t = r.value();
-        std::string key(t.recommended_data_path_key());
-        auto* d = im.dp(key);
-        if (!d) {
-            out.push_back(R::Failure({StatusCode::NOT_FOUND, "no DataPath registered for key '" + key + "'"}));
-            continue;
-        }
-        DeviceGuard dg(d->dp->capabilities().bound_accel_id);
-        auto dpt = d->dp->open(t);
+        auto* d = dps[i];
+        auto& dpt = *opened[i];
         if (!dpt.ok()) {
             out.push_back(R::Failure(dpt.status()));
             continue;
         }
+        std::string key(t.recommended_data_path_key());
         const std::uint32_t slot = Impl::alloc_slot(im.tgts);
         auto& e = im.tgts[slot];
         e = Impl::TargetEntry{};
