@@ -213,3 +213,43 @@ def test_daemon_reaps_a_crashed_client(daemon):
         time.sleep(0.1)
     assert c.kv("STATUS")["leases"] == "0"
     assert c.kv("LIST")["free_queues"] == "32,32"
+
+
+def test_daemon_device_acl_by_accelerator():
+    out = core().daemon_handle_request_selftest(
+        ["HELLO client=a pid=0 accel=0", "HELLO client=b pid=0 accel=1", "HELLO client=c pid=0",
+         "ACQUIRE session=1 devices=1 queues=4", "ACQUIRE session=2 devices=1 queues=4",
+         "ACQUIRE session=3 devices=0 queues=4", "ACQUIRE session=3 devices=0,1 queues=4", "LIST"],
+        [{"id": 0, "mount": "/m0", "queues": 64}, {"id": 1, "mount": "/m1", "queues": 64, "accelerators": [1, 2]}])
+    assert out[3].startswith("ERR") and "PERMISSION_DENIED" in out[3] and "accelerator 0" in out[3]
+    assert out[4].startswith("OK")  # accelerator 1 is on device 1's list
+    assert out[5].startswith("OK")  # device 0 has no list: any accelerator
+    assert out[6].startswith("ERR") and "PERMISSION_DENIED" in out[6]  # all-or-nothing
+    assert "accelerators=*,1+2" in out[7] and "free_queues=60,60" in out[7]
+
+
+def test_daemon_reads_accelerator_lists(tmp_path):
+    if not os.path.exists(DAEMON):
+        pytest.skip("tutti_daemon not built")
+    sock = str(tmp_path / "acl.sock")
+    cfg = tmp_path / "daemon.yaml"
+    cfg.write_text(textwrap.dedent(f"""
+        service: {{socket: {sock}}}
+        devices:
+          - {{id: 0, kind: emulated, mount: {tmp_path}/nvme0, queues: 8, accelerators: [3]}}
+        """))
+    p = subprocess.Popen([DAEMON, "--config", str(cfg)], stderr=subprocess.PIPE)
+    try:
+        for _ in range(100):
+            if os.path.exists(sock):
+                break
+            time.sleep(0.05)
+        c = Client(sock)
+        assert c.kv("LIST")["accelerators"] == "3"
+        s_other = c.kv(f"HELLO client=x pid={os.getpid()} accel=1")["session"]
+        assert "PERMISSION_DENIED" in c(f"ACQUIRE session={s_other} devices=0 queues=2")
+        s_mine = c.kv(f"HELLO client=y pid={os.getpid()} accel=3")["session"]
+        assert c.kv(f"ACQUIRE session={s_mine} devices=0 queues=2")["lease"]
+    finally:
+        p.send_signal(signal.SIGTERM)
+        p.wait(timeout=10)

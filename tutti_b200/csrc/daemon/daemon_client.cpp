@@ -29,7 +29,7 @@ std::vector<std::string> split(const std::string& s) {
 
 DaemonClient::~DaemonClient() { close(); }
 
-Status DaemonClient::connect(const std::string& path, const std::string& client_name) {
+Status DaemonClient::connect(const std::string& path, const std::string& client_name, std::int64_t accel) {
     fd_ = ::socket(AF_UNIX, SOCK_STREAM | SOCK_CLOEXEC, 0);
     if (fd_ < 0) return {StatusCode::INTERNAL, "socket failed"};
     sockaddr_un addr{};
@@ -42,7 +42,8 @@ Status DaemonClient::connect(const std::string& path, const std::string& client_
     }
     const long pid = static_cast<long>(::getpid());
     auto r = request("HELLO client=" + client_name + " pid=" + std::to_string(pid) +
-                     " start_time=" + std::to_string(process_start_time(pid)));
+                     " start_time=" + std::to_string(process_start_time(pid)) +
+                     (accel >= 0 ? " accel=" + std::to_string(accel) : std::string()));
     if (!r.ok()) return r.status();
     const Message m = parse_message(r.value());
     session_ = std::strtoull(m.get("session").c_str(), nullptr, 10);

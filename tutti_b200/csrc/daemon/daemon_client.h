@@ -34,7 +34,8 @@ public:
     DaemonClient(const DaemonClient&) = delete;
     DaemonClient& operator=(const DaemonClient&) = delete;
 
-    Status connect(const std::string& socket_path, const std::string& client_name);
+    // `accel`: this process's accelerator, checked against devices' accelerator lists (-1: not given).
+    Status connect(const std::string& socket_path, const std::string& client_name, std::int64_t accel = -1);
     Result<LeaseGrant> acquire(const std::vector<std::int64_t>& devices, std::uint32_t queues);
     // Starts a thread that sends HEARTBEAT every `interval_ms`.
     void start_heartbeat(std::uint32_t interval_ms);

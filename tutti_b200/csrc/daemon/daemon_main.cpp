@@ -7,7 +7,8 @@
 //   service: {socket: /run/tutti/daemon.sock}
 //   lease:   {heartbeat_timeout_s: 30, reap_interval_ms: 1000}
 //   devices:
-//     - {id: 0, kind: emulated, mount: /mnt/nvme0, queues: 128, pci: "0000:1b:00.0", nsid: 1, lba_bytes: 512}
+//     - {id: 0, kind: emulated, mount: /mnt/nvme0, queues: 128, pci: "0000:1b:00.0", nsid: 1, lba_bytes: 512,
+//        accelerators: [0, 1]}   # optional: only these GPUs may lease its queues
 //
 // Protocol: one request per line (see lease_ledger.h); a connection that
 // closes ends nothing by itself - leases end by RELEASE, BYE, heartbeat
@@ -103,6 +104,14 @@ int main(int argc, char** argv) {
         if (auto q = d.get("queues")) info.queues = static_cast<std::uint32_t>(yaml::as_int(*q, p + ".queues").value());
         if (auto q = d.get("nsid")) info.namespace_id = static_cast<std::uint32_t>(yaml::as_int(*q, p + ".nsid").value());
         if (auto q = d.get("lba_bytes")) info.lba_bytes = static_cast<std::uint32_t>(yaml::as_int(*q, p + ".lba_bytes").value());
+        if (auto a = d.get("accelerators")) {
+            if (!a->is_seq()) return fail(p + ".accelerators: expected a list of accelerator ids");
+            for (std::size_t k = 0; k < a->seq.size(); ++k) {
+                auto v = yaml::as_int(*a->seq[k], p + ".accelerators[" + std::to_string(k) + "]");
+                if (!v.ok()) return fail(v.status().to_string());
+                info.accelerators.push_back(v.value());
+            }
+        }
         if (info.kind != "emulated" && info.kind != "nvme") return fail(p + ".kind must be emulated or nvme");
         devices.push_back(info);
     }

@@ -64,13 +64,15 @@ std::size_t LeaseLedger::lease_count() const {
     return leases_.size();
 }
 
-Result<std::uint64_t> LeaseLedger::open_session(const std::string& client, std::int64_t pid, std::uint64_t start) {
+Result<std::uint64_t> LeaseLedger::open_session(const std::string& client, std::int64_t pid, std::uint64_t start,
+                                                std::int64_t accel) {
     std::lock_guard<std::mutex> g(mu_);
     Session s;
     s.id = next_++;
     s.client = client;
     s.pid = pid;
     s.start_time = start;
+    s.accel = accel;
     sessions_[s.id] = s;
     return s.id;
 }
@@ -90,8 +92,21 @@ Result<Lease> LeaseLedger::acquire(std::uint64_t session, const std::vector<std:
                                    std::uint32_t queues) {
     using R = Result<Lease>;
     std::lock_guard<std::mutex> g(mu_);
-    if (!sessions_.count(session)) return R::Failure({StatusCode::NOT_FOUND, "unknown session"});
+    auto sit = sessions_.find(session);
+    if (sit == sessions_.end()) return R::Failure({StatusCode::NOT_FOUND, "unknown session"});
     if (devices.empty() || queues == 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "empty request"});
+    const std::int64_t accel = sit->second.accel;
+    for (auto dev : devices) {
+        for (const auto& d : devices_) {
+            if (d.id != dev || d.accelerators.empty()) continue;
+            bool allowed = false;
+            for (auto a : d.accelerators) allowed = allowed || a == accel;
+            if (!allowed)
+                return R::Failure({StatusCode::PERMISSION_DENIED,
+                                   "accelerator " + (accel < 0 ? std::string("(not given)") : std::to_string(accel)) +
+                                       " may not use device " + std::to_string(dev)});
+        }
+    }
     // Contiguous queue ranges per device, all-or-nothing.
     std::vector<Grant> grants;
     for (auto dev : devices) {
@@ -224,16 +239,20 @@ std::string handle_request(LeaseLedger& ledger, const std::string& line) {
         const std::int64_t pid = std::strtoll(req.get("pid", "0").c_str(), nullptr, 10);
         std::uint64_t start = std::strtoull(req.get("start_time", "0").c_str(), nullptr, 10);
         if (start == 0) start = process_start_time(pid);
-        auto s = ledger.open_session(req.get("client", "anonymous"), pid, start);
+        const std::int64_t accel = std::strtoll(req.get("accel", "-1").c_str(), nullptr, 10);
+        auto s = ledger.open_session(req.get("client", "anonymous"), pid, start, accel);
         if (!s.ok()) return err(s.status());
         rsp.kv["session"] = std::to_string(s.value());
     } else if (req.verb == "BYE") {
         Status s = ledger.close_session(std::strtoull(req.get("session").c_str(), nullptr, 10));
         if (!s.ok()) return err(s);
     } else if (req.verb == "LIST") {
-        std::string ids, mounts, free, kinds;
+        std::string ids, mounts, free, kinds, acl;
         for (auto& d : ledger.devices()) {
             const std::string sep = ids.empty() ? "" : ",";
+            std::string who;
+            for (auto a : d.accelerators) who += (who.empty() ? "" : "+") + std::to_string(a);
+            acl += sep + (who.empty() ? "*" : who);  // "*": any accelerator
             ids += sep + std::to_string(d.id);
             mounts += sep + d.mount;
             kinds += sep + d.kind;
@@ -243,6 +262,7 @@ std::string handle_request(LeaseLedger& ledger, const std::string& line) {
         rsp.kv["mounts"] = mounts;
         rsp.kv["kinds"] = kinds;
         rsp.kv["free_queues"] = free;
+        rsp.kv["accelerators"] = acl;
     } else if (req.verb == "ACQUIRE") {
         auto l = ledger.acquire(std::strtoull(req.get("session").c_str(), nullptr, 10), parse_ids(req.get("devices")),
                                 static_cast<std::uint32_t>(std::strtoul(req.get("queues", "0").c_str(), nullptr, 10)));

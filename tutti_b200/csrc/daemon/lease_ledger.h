@@ -32,6 +32,7 @@ struct DeviceInfo {
     std::uint32_t queues = 64;      // queue budget offered to clients
     std::uint32_t namespace_id = 1;
     std::uint32_t lba_bytes = 512;
+    std::vector<std::int64_t> accelerators;  // who may lease its queues; empty: any accelerator
 };
 
 struct Grant {
@@ -52,6 +53,7 @@ struct Session {
     std::string client;
     std::int64_t pid = 0;
     std::uint64_t start_time = 0;  // /proc/<pid>/stat field 22 at HELLO
+    std::int64_t accel = -1;       // the client's accelerator (HELLO accel=...), -1 if not given
 };
 
 // Reads /proc/<pid>/stat start time (clock ticks since boot); 0 if the process is gone.
@@ -61,10 +63,13 @@ class LeaseLedger {
 public:
     explicit LeaseLedger(std::vector<DeviceInfo> devices);
 
-    Result<std::uint64_t> open_session(const std::string& client, std::int64_t pid, std::uint64_t start_time);
+    Result<std::uint64_t> open_session(const std::string& client, std::int64_t pid, std::uint64_t start_time,
+                                       std::int64_t accel = -1);
     Status close_session(std::uint64_t session);  // releases its leases
 
     // All-or-nothing: either every device gets `queues` queues or nothing changes.
+    // A device with an accelerator list is leased only to sessions of those
+    // accelerators (PERMISSION_DENIED otherwise).
     Result<Lease> acquire(std::uint64_t session, const std::vector<std::int64_t>& devices, std::uint32_t queues);
     Status heartbeat(std::uint64_t lease);
     Status release(std::uint64_t lease);

@@ -23,6 +23,7 @@ enum class StatusCode {
     DEVICE_ERROR,
     DATA_LOSS,
     INTERNAL,
+    PERMISSION_DENIED,
 };
 
 inline const char* status_code_name(StatusCode c) noexcept {
@@ -39,6 +40,7 @@ inline const char* status_code_name(StatusCode c) noexcept {
         case StatusCode::DEVICE_ERROR: return "DEVICE_ERROR";
         case StatusCode::DATA_LOSS: return "DATA_LOSS";
         case StatusCode::INTERNAL: return "INTERNAL";
+        case StatusCode::PERMISSION_DENIED: return "PERMISSION_DENIED";
     }
     return "?";
 }

@@ -691,6 +691,7 @@ PYBIND11_MODULE(_core, m) {
             info.id = d["id"].cast<std::int64_t>();
             info.mount = d["mount"].cast<std::string>();
             info.queues = d["queues"].cast<std::uint32_t>();
+            if (d.contains("accelerators")) info.accelerators = d["accelerators"].cast<std::vector<std::int64_t>>();
             devs.push_back(info);
         }
         tutti::daemon::LeaseLedger ledger(devs);

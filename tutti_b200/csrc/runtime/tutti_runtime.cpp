@@ -38,7 +38,7 @@ Result<std::unique_ptr<TuttiRuntime>> TuttiRuntime::create(const TuttiRuntimeSpe
                 rows.push_back({m, res->queues_per_controller ? res->queues_per_controller : ds.leases, res->lba_bytes});
         } else {  // nvme-service
             auto client = std::make_shared<daemon::DaemonClient>();
-            TUTTI_RETURN_IF_ERROR_R(R, client->connect(res->endpoint, res->client));
+            TUTTI_RETURN_IF_ERROR_R(R, client->connect(res->endpoint, res->client, spec.accel_id));
             const std::uint32_t want = res->queues_per_controller ? res->queues_per_controller : ds.leases;
             auto grant = client->acquire(res->device_ids, want);
             if (!grant.ok()) return R::Failure(grant.status());
