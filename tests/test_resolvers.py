@@ -57,3 +57,45 @@ def test_raid0_map_matches_striping_oracle():
         assert members[m][moff] == image[off]
         k = min(contig, md_bytes - off)
         assert np.array_equal(members[m][moff: moff + k], image[off: off + k])
+
+
+def test_md_array_found_from_a_mount(tmp_path):
+    import os
+
+    mnt = tmp_path / "mnt"
+    mnt.mkdir()
+    st = os.stat(mnt)
+    sysfs = tmp_path / "sys"
+    _fake_md(sysfs, name="md7")
+    (sysfs / "devices" / "virtual" / "block" / "md7").mkdir(parents=True)
+    (sysfs / "dev" / "block").mkdir(parents=True)
+    os.symlink("../../devices/virtual/block/md7", sysfs / "dev" / "block" / f"{os.major(st.st_dev)}:{os.minor(st.st_dev)}")
+    assert core().find_md_array(str(sysfs), str(mnt)) == "md7"
+    other = tmp_path / "sys2"
+    (other / "dev" / "block").mkdir(parents=True)
+    os.symlink("../../devices/pci/nvme0n1", other / "dev" / "block" / f"{os.major(st.st_dev)}:{os.minor(st.st_dev)}")
+    with pytest.raises(Exception, match="not on an md array"):
+        core().find_md_array(str(other), str(mnt))
+
+
+def test_tutti_style_runtime_config_validates():
+    # Tutti's runtime YAML conventions: an explicit device selection, and a raid0
+    # resolver that finds its md array from the mount instead of naming it
+    text = """
+accelerator: {profile: CUDA}
+runtime: {accel_id: 0}
+storage:
+  resources:
+    - id: nvme-local-0
+      type: nvme
+      provider: {type: nvme-service, endpoint: "127.0.0.1:50051"}
+      allocation: {selection: explicit, device_ids: [0, 1], queues_per_controller: 4}
+  resolvers:
+    - {id: raid0-resolver, type: local-file, scheme: file, config: {topology: raid0}}
+  datapaths:
+    - {id: dp, type: nvme-device-group, config: {}}
+  backends:
+    - {id: storage, contract: nvme-device-group, resolver: raid0-resolver, datapath: dp, resource: nvme-local-0, config: {}}
+"""
+    spec = core().parse_runtime_config(text, True)
+    assert spec["resources"][0]["provider"] == "nvme-service" and spec["backends"]

@@ -236,8 +236,9 @@ Status validate_runtime_spec(const TuttiRuntimeSpec& s) {
                 return bad("resource " + r.id + ": emulated provider needs config.mounts");
             if (r.provider == "emulated" && !r.device_ids.empty() && r.device_ids.size() != r.mounts.size())
                 return bad("resource " + r.id + ": one mount per device id");
-            if (r.selection != "device-group" && r.selection != "single")
-                return bad("resource " + r.id + ": selection must be device-group or single");
+            // "explicit" is Tutti's name for an explicit list of device ids
+            if (r.selection != "device-group" && r.selection != "single" && r.selection != "explicit")
+                return bad("resource " + r.id + ": selection must be device-group, single or explicit");
         }
     }
     for (auto& r : s.resolvers) {
@@ -245,7 +246,6 @@ Status validate_runtime_spec(const TuttiRuntimeSpec& s) {
         if (r.type != "local-file") return bad("resolver " + r.id + ": type must be local-file");
         if (r.topology != "single" && r.topology != "multi-mount" && r.topology != "raid0")
             return bad("resolver " + r.id + ": topology must be single, multi-mount or raid0");
-        if (r.topology == "raid0" && r.md.empty()) return bad("resolver " + r.id + ": raid0 needs config.md");
         if (r.mapping != "auto" && r.mapping != "fiemap" && r.mapping != "synthetic")
             return bad("resolver " + r.id + ": mapping must be auto, fiemap or synthetic");
     }

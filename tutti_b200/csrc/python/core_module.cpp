@@ -927,6 +927,9 @@ PYBIND11_MODULE(_core, m) {
               return d;
           },
           py::arg("path"), py::arg("mapping") = "auto", py::arg("device_index") = 0, py::arg("block_bytes") = 512);
+    m.def("find_md_array", [](const std::string& sysfs_root, const std::string& path) {
+        return unwrap(find_md_array(sysfs_root, path));
+    });
     m.def("probe_md_raid0", [](const std::string& sysfs_root, const std::string& md) {
         auto g = unwrap(probe_md_raid0(sysfs_root, md));
         py::dict d;

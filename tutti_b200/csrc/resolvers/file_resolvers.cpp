@@ -5,6 +5,7 @@
 #include <linux/fs.h>
 #include <sys/ioctl.h>
 #include <sys/stat.h>
+#include <sys/sysmacros.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -249,6 +250,23 @@ Result<Raid0Geometry> probe_md_raid0(const std::string& sysfs_root, const std::s
         g.members[s].name = "rd" + std::to_string(i);
     }
     return g;
+}
+
+Result<std::string> find_md_array(const std::string& sysfs_root, const std::string& path) {
+    using R = Result<std::string>;
+    struct stat st {};
+    if (::stat(path.c_str(), &st) != 0) return R::Failure({StatusCode::NOT_FOUND, "stat " + path + " failed"});
+    const std::string link = sysfs_root + "/dev/block/" + std::to_string(major(st.st_dev)) + ":" +
+                             std::to_string(minor(st.st_dev));
+    char buf[4096];
+    const ssize_t n = ::readlink(link.c_str(), buf, sizeof(buf) - 1);
+    if (n <= 0) return R::Failure({StatusCode::NOT_FOUND, "no block device entry " + link + " for " + path});
+    std::string target(buf, static_cast<std::size_t>(n));
+    const std::string name = target.substr(target.find_last_of('/') + 1);
+    struct stat md {};
+    if (::stat((sysfs_root + "/block/" + name + "/md").c_str(), &md) != 0)
+        return R::Failure({StatusCode::NOT_FOUND, path + " is on " + name + ", not on an md array"});
+    return name;
 }
 
 Raid0Location raid0_map(const Raid0Geometry& g, std::uint64_t md_offset) {

@@ -92,6 +92,10 @@ struct Raid0Geometry {
 // Probes <sysfs_root>/block/<md>/md: level must be raid0; chunk_size; raid_disks;
 // rd<N>/{slot,offset} -> members in slot order. `sysfs_root` is "/sys" normally.
 Result<Raid0Geometry> probe_md_raid0(const std::string& sysfs_root, const std::string& md_name);
+// The md array (e.g. "md0") whose block device holds `path`'s filesystem:
+// st_dev -> <sysfs_root>/dev/block/MAJ:MIN -> that device's name, which must
+// have an md/ directory. Lets a raid0 resolver find its array from the mount.
+Result<std::string> find_md_array(const std::string& sysfs_root, const std::string& path);
 
 // md byte offset -> (member index, member byte offset).
 struct Raid0Location {

@@ -76,7 +76,14 @@ Result<std::unique_ptr<TuttiRuntime>> TuttiRuntime::create(const TuttiRuntimeSpe
     // 2) resolver
     const std::string key = gpu ? "nvme-gpu" : "posix";
     if (rs.topology == "raid0") {
-        auto geo = probe_md_raid0(rs.sysfs_root, rs.md);
+        std::string md = rs.md;
+        if (md.empty()) {  // the array behind the resource's mount
+            if (rows.empty()) return R::Failure({StatusCode::INVALID_ARGUMENT, "raid0 resolver has no mount"});
+            auto found = find_md_array(rs.sysfs_root, rows[0].mount);
+            if (!found.ok()) return R::Failure(found.status());
+            md = found.value();
+        }
+        auto geo = probe_md_raid0(rs.sysfs_root, md);
         if (!geo.ok()) return R::Failure(geo.status());
         MountBinding mb;
         mb.mount_path = rows.empty() ? "/" : rows[0].mount;
