@@ -253,3 +253,52 @@ def test_daemon_reads_accelerator_lists(tmp_path):
     finally:
         p.send_signal(signal.SIGTERM)
         p.wait(timeout=10)
+
+
+def test_daemon_reads_tutti_schema(tmp_path):
+    if not os.path.exists(DAEMON):
+        pytest.skip("tutti_daemon not built")
+    sock = str(tmp_path / "t.sock")
+    cfg = tmp_path / "nvme_daemon.yaml"
+    cfg.write_text(textwrap.dedent(f"""
+        service: {{socket: {sock}}}
+        grpc: {{endpoint: "127.0.0.1:50051"}}
+        accelerators:
+          - {{accel_id: 0, view_root: {tmp_path}/gpu0}}
+        nvmes:
+          - device_id: 0
+            pci_addr: "0000:08:00.0"
+            backing_mount_path: {tmp_path}/nvme0
+            namespace_id: 1
+            kernel_ioq_cap: 32
+            allowed_accel_ids: [0]
+            auto_mount: true
+          - device_id: 1
+            pci_addr: "0000:4b:00.0"
+            backing_mount_path: {tmp_path}/nvme1
+            namespace_id: 1
+            kernel_ioq_cap: 32
+            allowed_accel_ids: [1]
+            auto_mount: true
+        queue_pool: {{default_per_client: 16, max_per_client: 24}}
+        lease: {{heartbeat_interval_sec: 10, timeout_sec: 30}}
+        unmount_retry: {{interval_ms: 1000, max: 30}}
+        """))
+    p = subprocess.Popen([DAEMON, "--config", str(cfg)], stderr=subprocess.PIPE)
+    try:
+        for _ in range(100):
+            if os.path.exists(sock):
+                break
+            time.sleep(0.05)
+        c = Client(sock)
+        lst = c.kv("LIST")
+        assert lst["devices"] == "0,1" and lst["kinds"] == "nvme,nvme" and lst["accelerators"] == "0,1"
+        assert lst["free_queues"] == "32,32" and lst["mounts"].endswith("nvme1")
+        s0 = c.kv(f"HELLO client=g0 pid={os.getpid()} accel=0")["session"]
+        assert "RESOURCE_EXHAUSTED" in c(f"ACQUIRE session={s0} devices=0 queues=30")  # above max_per_client
+        assert "PERMISSION_DENIED" in c(f"ACQUIRE session={s0} devices=1 queues=8")
+        c.kv(f"ACQUIRE session={s0} devices=0 queues=0")  # 0: the pool's default
+        assert c.kv("LIST")["free_queues"] == "16,32"
+    finally:
+        p.send_signal(signal.SIGTERM)
+        p.wait(timeout=10)

@@ -6,6 +6,9 @@
 // Config:
 //   service: {socket: /run/tutti/daemon.sock}
 //   lease:   {heartbeat_timeout_s: 30, reap_interval_ms: 1000}
+//   devices:             (or Tutti's nvmes: [{device_id, backing_mount_path, pci_addr, namespace_id,
+//                         kernel_ioq_cap, allowed_accel_ids}])
+//   queue_pool: {default_per_client: 16, max_per_client: 32}   (optional)
 //   devices:
 //     - {id: 0, kind: emulated, mount: /mnt/nvme0, queues: 128, pci: "0000:1b:00.0", nsid: 1, lba_bytes: 512,
 //        accelerators: [0, 1]}   # optional: only these GPUs may lease its queues
@@ -80,42 +83,82 @@ int main(int argc, char** argv) {
     const yaml::Node& r = *root.value();
     std::string socket_path = "/tmp/tutti_daemon.sock";
     std::int64_t hb_timeout = 30, reap_ms = 1000;
+    std::uint32_t pool_default = 0, pool_max = 0;
+    auto int_of = [](const yaml::Node* n, const std::string& path, std::int64_t& out) -> Status {
+        if (!n) return Status::Ok();
+        auto v = yaml::as_int(*n, path);
+        if (!v.ok()) return v.status();
+        out = v.value();
+        return Status::Ok();
+    };
+    Status st;
     if (const auto* s = r.get("service"))
         if (const auto* p = s->get("socket")) socket_path = p->scalar;
     if (const auto* l = r.get("lease")) {
-        if (const auto* t = l->get("heartbeat_timeout_s")) hb_timeout = yaml::as_int(*t, "lease.heartbeat_timeout_s").value();
-        if (const auto* t = l->get("reap_interval_ms")) reap_ms = yaml::as_int(*t, "lease.reap_interval_ms").value();
+        if (st.ok()) st = int_of(l->get("heartbeat_timeout_s"), "lease.heartbeat_timeout_s", hb_timeout);
+        if (st.ok()) st = int_of(l->get("timeout_sec"), "lease.timeout_sec", hb_timeout);  // Tutti's key
+        if (st.ok()) st = int_of(l->get("reap_interval_ms"), "lease.reap_interval_ms", reap_ms);
     }
+    if (const auto* q = r.get("queue_pool")) {  // Tutti's per-client queue policy
+        std::int64_t d = 0, m = 0;
+        if (st.ok()) st = int_of(q->get("default_per_client"), "queue_pool.default_per_client", d);
+        if (st.ok()) st = int_of(q->get("max_per_client"), "queue_pool.max_per_client", m);
+        pool_default = static_cast<std::uint32_t>(d);
+        pool_max = static_cast<std::uint32_t>(m);
+    }
+    if (!st.ok()) return fail(st.to_string());
+    if (r.get("grpc") && !r.get("service"))
+        std::fprintf(stderr, "tutti_daemon: grpc.endpoint is not served (line protocol on %s)\n", socket_path.c_str());
+
+    // Devices: this daemon's schema (devices: [{id, kind, mount, pci, queues, nsid, lba_bytes,
+    // accelerators}]) or Tutti's (nvmes: [{device_id, backing_mount_path, pci_addr, namespace_id,
+    // kernel_ioq_cap, allowed_accel_ids}]).
     std::vector<DeviceInfo> devices;
-    const auto* devs = r.get("devices");
-    if (!devs || !devs->is_seq()) return fail("config: devices: expected a list");
-    for (std::size_t i = 0; i < devs->seq.size(); ++i) {
-        const yaml::Node& d = *devs->seq[i];
-        const std::string p = "devices[" + std::to_string(i) + "]";
-        DeviceInfo info;
-        auto id = d.get("id");
-        if (!id) return fail(p + ".id: required");
-        auto idv = yaml::as_int(*id, p + ".id");
-        if (!idv.ok()) return fail(idv.status().to_string());
-        info.id = idv.value();
-        if (auto k = d.get("kind")) info.kind = k->scalar;
-        if (auto m = d.get("mount")) info.mount = m->scalar;
-        if (auto c = d.get("pci")) info.pci = c->scalar;
-        if (auto q = d.get("queues")) info.queues = static_cast<std::uint32_t>(yaml::as_int(*q, p + ".queues").value());
-        if (auto q = d.get("nsid")) info.namespace_id = static_cast<std::uint32_t>(yaml::as_int(*q, p + ".nsid").value());
-        if (auto q = d.get("lba_bytes")) info.lba_bytes = static_cast<std::uint32_t>(yaml::as_int(*q, p + ".lba_bytes").value());
-        if (auto a = d.get("accelerators")) {
-            if (!a->is_seq()) return fail(p + ".accelerators: expected a list of accelerator ids");
-            for (std::size_t k = 0; k < a->seq.size(); ++k) {
-                auto v = yaml::as_int(*a->seq[k], p + ".accelerators[" + std::to_string(k) + "]");
-                if (!v.ok()) return fail(v.status().to_string());
-                info.accelerators.push_back(v.value());
+    auto parse_list = [&](const yaml::Node& list, const std::string& name, bool tutti) -> Status {
+        if (!list.is_seq()) return {StatusCode::INVALID_ARGUMENT, "config: " + name + ": expected a list"};
+        for (std::size_t i = 0; i < list.seq.size(); ++i) {
+            const yaml::Node& d = *list.seq[i];
+            const std::string p = name + "[" + std::to_string(i) + "]";
+            DeviceInfo info;
+            info.kind = tutti ? "nvme" : "emulated";
+            const yaml::Node* id = d.get(tutti ? "device_id" : "id");
+            if (!id) return {StatusCode::INVALID_ARGUMENT, p + ": id required"};
+            std::int64_t v = 0;
+            TUTTI_RETURN_IF_ERROR(int_of(id, p + ".id", v));
+            info.id = v;
+            if (auto k = d.get("kind")) info.kind = k->scalar;
+            if (auto m = d.get(tutti ? "backing_mount_path" : "mount")) info.mount = m->scalar;
+            if (auto c = d.get(tutti ? "pci_addr" : "pci")) info.pci = c->scalar;
+            v = info.queues;
+            TUTTI_RETURN_IF_ERROR(int_of(d.get(tutti ? "kernel_ioq_cap" : "queues"), p + ".queues", v));
+            info.queues = static_cast<std::uint32_t>(v);
+            v = info.namespace_id;
+            TUTTI_RETURN_IF_ERROR(int_of(d.get(tutti ? "namespace_id" : "nsid"), p + ".nsid", v));
+            info.namespace_id = static_cast<std::uint32_t>(v);
+            v = info.lba_bytes;
+            TUTTI_RETURN_IF_ERROR(int_of(d.get("lba_bytes"), p + ".lba_bytes", v));
+            info.lba_bytes = static_cast<std::uint32_t>(v);
+            if (auto a = d.get(tutti ? "allowed_accel_ids" : "accelerators")) {
+                if (!a->is_seq()) return {StatusCode::INVALID_ARGUMENT, p + ".accelerators: expected a list of ids"};
+                for (std::size_t k = 0; k < a->seq.size(); ++k) {
+                    TUTTI_RETURN_IF_ERROR(int_of(a->seq[k].get(), p + ".accelerators[" + std::to_string(k) + "]", v));
+                    info.accelerators.push_back(v);
+                }
             }
+            if (info.kind != "emulated" && info.kind != "nvme")
+                return {StatusCode::INVALID_ARGUMENT, p + ".kind must be emulated or nvme"};
+            devices.push_back(info);
         }
-        if (info.kind != "emulated" && info.kind != "nvme") return fail(p + ".kind must be emulated or nvme");
-        devices.push_back(info);
-    }
+        return Status::Ok();
+    };
+    const auto* devs = r.get("devices");
+    const auto* nvmes = r.get("nvmes");
+    if (!devs && !nvmes) return fail("config: devices (or nvmes): expected a list");
+    if (devs) st = parse_list(*devs, "devices", false);
+    if (st.ok() && nvmes) st = parse_list(*nvmes, "nvmes", true);
+    if (!st.ok()) return fail(st.to_string());
     LeaseLedger ledger(devices);
+    ledger.set_queue_pool(pool_default, pool_max);
 
     const int srv = ::socket(AF_UNIX, SOCK_STREAM | SOCK_CLOEXEC, 0);
     if (srv < 0) return fail("socket failed");

@@ -94,7 +94,11 @@ Result<Lease> LeaseLedger::acquire(std::uint64_t session, const std::vector<std:
     std::lock_guard<std::mutex> g(mu_);
     auto sit = sessions_.find(session);
     if (sit == sessions_.end()) return R::Failure({StatusCode::NOT_FOUND, "unknown session"});
+    if (queues == 0) queues = pool_default_;
     if (devices.empty() || queues == 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "empty request"});
+    if (pool_max_ && queues > pool_max_)
+        return R::Failure({StatusCode::RESOURCE_EXHAUSTED, std::to_string(queues) + " queues asked, at most " +
+                                                               std::to_string(pool_max_) + " per client"});
     const std::int64_t accel = sit->second.accel;
     for (auto dev : devices) {
         for (const auto& d : devices_) {

@@ -72,6 +72,13 @@ public:
     // accelerators (PERMISSION_DENIED otherwise).
     Result<Lease> acquire(std::uint64_t session, const std::vector<std::int64_t>& devices, std::uint32_t queues);
     Status heartbeat(std::uint64_t lease);
+    // Per-client queue policy: a request for 0 queues gets `default_queues`;
+    // one for more than `max_queues` is refused (0: no default / no cap).
+    void set_queue_pool(std::uint32_t default_queues, std::uint32_t max_queues) {
+        std::lock_guard<std::mutex> g(mu_);
+        pool_default_ = default_queues;
+        pool_max_ = max_queues;
+    }
     Status release(std::uint64_t lease);
 
     // Releases leases whose heartbeat is older than `timeout`, and sessions
@@ -92,6 +99,7 @@ private:
     std::map<std::uint64_t, Session> sessions_;
     std::map<std::uint64_t, Lease> leases_;
     std::uint64_t next_ = 1;
+    std::uint32_t pool_default_ = 0, pool_max_ = 0;
 };
 
 // Line protocol: "VERB key=value key=value\n" -> "OK key=value ...\n" | "ERR message\n".
