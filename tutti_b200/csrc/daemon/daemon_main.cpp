@@ -6,10 +6,9 @@
 // Config:
 //   service: {socket: /run/tutti/daemon.sock}
 //   lease:   {heartbeat_timeout_s: 30, reap_interval_ms: 1000}
-//   devices:             (or Tutti's nvmes: [{device_id, backing_mount_path, pci_addr, namespace_id,
-//                         kernel_ioq_cap, allowed_accel_ids}])
-//   queue_pool: {default_per_client: 16, max_per_client: 32}   (optional)
-//   devices:
+//   queue_pool: {default_per_client: 16, max_per_client: 32}   # optional
+//   devices:   # or Tutti's nvmes: [{device_id, backing_mount_path, pci_addr, namespace_id,
+//              #                     kernel_ioq_cap, allowed_accel_ids}]
 //     - {id: 0, kind: emulated, mount: /mnt/nvme0, queues: 128, pci: "0000:1b:00.0", nsid: 1, lba_bytes: 512,
 //        accelerators: [0, 1]}   # optional: only these GPUs may lease its queues
 //
