@@ -76,7 +76,7 @@ if all(os.path.exists(os.path.join(ROOT, s)) for s in OPS_SOURCES):
 setup(
     name="tutti_b200",
     version="0.1.0",
-    packages=["tutti_b200"],
+    packages=["tutti_b200", "tutti", "tutti_runtime"],  # tutti / tutti_runtime: Tutti's import paths
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -230,20 +230,27 @@ PYBIND11_MODULE(_core, m) {
                py::array_t<std::uint64_t, py::array::c_style> mem_off,
                py::array_t<std::uint64_t, py::array::c_style> tgt,
                py::array_t<std::uint64_t, py::array::c_style> tgt_off,
-               py::array_t<std::uint64_t, py::array::c_style> len, std::uintptr_t stream, bool host_exec) {
+               py::array_t<std::uint64_t, py::array::c_style> len, std::uintptr_t stream, bool host_exec,
+               py::array_t<std::uint8_t, py::array::c_style> directions) {
                 const std::size_t n = static_cast<std::size_t>(len.size());
                 if (mem_off.size() != static_cast<py::ssize_t>(n) || tgt_off.size() != static_cast<py::ssize_t>(n) ||
                     (mem.size() != 1 && mem.size() != static_cast<py::ssize_t>(n)) ||
                     (tgt.size() != 1 && tgt.size() != static_cast<py::ssize_t>(n)))
                     throw py::value_error("array lengths differ");
+                // "mixed": directions[i] is 0 (read) or 1 (write) per request
+                const bool mixed = direction == "mixed";
                 const IoDirection dir = direction == "read" ? IoDirection::READ : IoDirection::WRITE;
-                if (direction != "read" && direction != "write") throw py::value_error("direction read|write");
+                if (direction != "read" && direction != "write" && !mixed)
+                    throw py::value_error("direction read|write|mixed");
+                if (mixed && directions.size() != static_cast<py::ssize_t>(n))
+                    throw py::value_error("mixed: one direction per request");
                 std::vector<IoRequest> reqs(n);
                 auto pm = mem.unchecked<1>(), pmo = mem_off.unchecked<1>(), pt = tgt.unchecked<1>(),
                      pto = tgt_off.unchecked<1>(), pl = len.unchecked<1>();
                 const bool one_mem = mem.size() == 1, one_tgt = tgt.size() == 1;
+                const std::uint8_t* pd = mixed ? directions.data() : nullptr;
                 for (std::size_t i = 0; i < n; ++i) {
-                    reqs[i].direction = dir;
+                    reqs[i].direction = mixed ? (pd[i] ? IoDirection::WRITE : IoDirection::READ) : dir;
                     reqs[i].memory = unpack<MemoryHandle>(r.rid_, pm(one_mem ? 0 : i));
                     reqs[i].memory_offset = pmo(i);
                     reqs[i].target = unpack<TargetHandle>(r.rid_, pt(one_tgt ? 0 : i));
@@ -287,7 +294,8 @@ PYBIND11_MODULE(_core, m) {
                 return d;
             },
             py::arg("direction"), py::arg("mem"), py::arg("mem_offsets"), py::arg("targets"),
-            py::arg("target_offsets"), py::arg("lengths"), py::arg("stream") = 0, py::arg("host_exec") = false)
+            py::arg("target_offsets"), py::arg("lengths"), py::arg("stream") = 0, py::arg("host_exec") = false,
+            py::arg("directions") = py::array_t<std::uint8_t>())
         .def(
             "submit_paged",
             [](PyRuntime& r, const std::string& direction, std::uint64_t mem,
