@@ -42,3 +42,28 @@ def test_factories_take_tutti_presets(tmp_path):
     assert isinstance(stub, tutti_runtime.Runtime)
     with pytest.raises(ValueError, match="raid0"):
         tutti_runtime.make_raid0_nvme_runtime({"devices": [{"mount_path": str(tmp_path / "a")}]})
+
+
+def test_object_store_with_tutti_config(tmp_path):
+    s = tutti_runtime.ObjectStore()
+    cfg = {"uri": str(tmp_path), "devices": [{"mount_path": str(tmp_path / "d0"), "namespace_id": 1},
+                                             {"mount_path": str(tmp_path / "d1")}],
+           "segment_bytes": 8192, "segment_count": 2, "segment_file_slots": 4, "segment_header_bytes": 131072,
+           "capacity_slots": 16, "namespace_fingerprint": b"\x01geometry", "rank_id": 0, "rank_count": 1,
+           "background_reclaim": True, "residency_sync_interval_ms": 100}
+    with pytest.raises(ValueError):
+        s.open("local_nvme_file", cfg)  # one device only
+    s.open("striped_local_nvme_file", cfg)
+    assert s.is_open() and s.ready_slots() == 8
+    keys = [bytes([i]) * 18 for i in range(3)]
+    acc, rej = s.reserve(keys)
+    s.commit([a[0] for a in acc])
+    assert s.contains_prefix(keys) == 3 and s.contains_prefix_all_ranks(keys) == 3
+    s.close()
+    again = tutti_runtime.ObjectStore()
+    with pytest.raises(Exception):  # another geometry fingerprint fails closed
+        again.open("striped_local_nvme_file", dict(cfg, namespace_fingerprint=b"other"))
+    again = tutti_runtime.ObjectStore()
+    again.open("striped_local_nvme_file", cfg)
+    assert sorted(again.recover()) == sorted(keys)
+    again.close()

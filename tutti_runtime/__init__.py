@@ -7,6 +7,7 @@
              unregister_memory / submit / enqueue_wait / release_io / query_io /
              open_io_count / wait / wait_result / wait_detail / shutdown
     SubmitResult, WaitResult
+    ObjectStore: open(scheme, config) / contains_prefix_all_ranks / lookup / usage / ...
 
 Presets take Tutti's form (``tutti_b200.storage.preset``): the drives' mounts are
 given in the preset or derived from its daemon configuration, and each mount is
@@ -27,7 +28,7 @@ import numpy as np
 from tutti_b200._native import core as _core
 from tutti_b200.storage.preset import prepare_preset, preset_mounts
 
-__all__ = ["Runtime", "SubmitResult", "WaitResult", "make_stub_runtime", "make_local_nvme_runtime",
+__all__ = ["Runtime", "ObjectStore", "SubmitResult", "WaitResult", "make_stub_runtime", "make_local_nvme_runtime",
            "make_nvme_device_group_runtime", "make_raid0_nvme_runtime"]
 
 
@@ -188,3 +189,75 @@ class Runtime:
 
     def shutdown(self, timeout_ms: int) -> None:
         self.native.shutdown(int(timeout_ms))
+
+
+OBJECT_STORE_SCHEMES = ("local_nvme_file", "striped_local_nvme_file")  # one mount / slots rotating over mounts
+_STORE_KEYS = ("uri", "segment_bytes", "segment_count", "segment_file_slots", "segment_header_bytes",
+               "capacity_slots", "capacity_bytes", "rank_id", "rank_count")
+
+
+class ObjectStore:
+    """Tutti's ``ObjectStore`` binding: ``open(scheme, config)`` with Tutti's config keys.
+
+    ``devices`` is a list of ``{"mount_path": ...}`` (other device facts are
+    accepted); ``namespace_fingerprint`` (bytes) guards the namespace's geometry.
+    ``background_reclaim`` and ``residency_sync_interval_ms`` are accepted and
+    have no effect here (residency bitmaps are memory-mapped and always current).
+    """
+
+    def __init__(self):
+        self.native = None
+
+    def open(self, scheme: str, config: dict) -> None:
+        if self.native is not None:
+            raise RuntimeError("object_store.open: store already open")
+        if scheme not in OBJECT_STORE_SCHEMES:
+            raise ValueError(f"unknown storage object store scheme {scheme!r} (one of {OBJECT_STORE_SCHEMES})")
+        c = dict(config)
+        mounts = [d["mount_path"] if isinstance(d, dict) else str(d) for d in c.get("devices") or []]
+        if not mounts:
+            raise ValueError("object store config needs devices (mount_path)")
+        if scheme == "local_nvme_file" and len(mounts) != 1:
+            raise ValueError("local_nvme_file takes exactly one device; striped_local_nvme_file takes several")
+        ours = {k: c[k] for k in _STORE_KEYS if k in c}
+        ours["mounts"] = mounts
+        if c.get("namespace_fingerprint") is not None:
+            ours["fingerprint"] = c["namespace_fingerprint"]
+        store = _core().ObjectStore()
+        store.open(ours)
+        self.native = store
+
+    def is_open(self) -> bool:
+        return self.native is not None
+
+    def close(self) -> None:
+        if self.native is not None:
+            store, self.native = self.native, None
+            store.close()
+
+    def _store(self):
+        if self.native is None:
+            raise RuntimeError("object store is not open")
+        return self.native
+
+    def contains_prefix(self, keys) -> int:
+        return self._store().contains_prefix(list(keys), False)
+
+    def contains_prefix_all_ranks(self, keys) -> int:
+        return self._store().contains_prefix(list(keys), True)
+
+    def ready_slots(self) -> int:
+        return self._store().ready_slots
+
+    def precreated_slots(self) -> int:
+        return self._store().precreated_slots
+
+    def precreate_target(self) -> int:
+        return self._store().precreate_target
+
+    def __getattr__(self, name):
+        # contains, lookup, usage, reserve, commit, abort, release, pin, unpin, recover,
+        # checkpoint, precreate_step, slot_uri, slot_generation: the same calls
+        if name == "native":
+            raise AttributeError(name)
+        return getattr(self._store(), name)
