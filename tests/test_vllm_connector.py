@@ -283,3 +283,11 @@ def test_worker_with_main_kv_and_index_cache_entities():
         assert torch.equal(main[i][:, 20:24], ref_m[i])
         assert torch.equal(index[i][20:24], ref_i[i])
     assert w.get_block_ids_with_load_errors() == set()
+
+
+def test_lookahead_option():
+    assert ConnectorConfig.from_extra({"lookahead_k": 2}).lookahead_k == 2
+    assert ConnectorConfig.from_extra({}).lookahead_k == 4
+    for bad in (0, -1, True, "3"):
+        with pytest.raises(ValueError):
+            ConnectorConfig.from_extra({"lookahead_k": bad})

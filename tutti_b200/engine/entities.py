@@ -91,8 +91,8 @@ class EntityEngines:
     def load(self, keys, block_table):
         return AggregateCompletion([e.load(keys, block_table) for e in self.engines])
 
-    def start_read_plan(self, keys, block_table):
-        return _MultiPlan([e.start_read_plan(keys, block_table) for e in self.engines], self.layer_map)
+    def start_read_plan(self, keys, block_table, window: int = 4):
+        return _MultiPlan([e.start_read_plan(keys, block_table, window=window) for e in self.engines], self.layer_map)
 
     def store_chunks(self, keys, block_table, *, after=None):
         parts = [e.store_chunks(keys, block_table, after=after) for e in self.engines]

@@ -78,7 +78,7 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                       tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group, self.cfg.failure_timeout_s),
                                       # vLLM's scheduler applies kv_load_failure_policy (recompute or fail the
                                       # requests) to the blocks the worker reports; the worker only reports
-                                      failure_policy="recompute")
+                                      failure_policy="recompute", lookahead=self.cfg.lookahead_k)
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""

@@ -9,6 +9,7 @@
   min_retrieve_tokens      hits shorter than this are computed instead of loaded (default 0)
   max_tokens_per_load      cap on the tokens one request loads at once (default 0: no cap)
   failure_collective_timeout_s  TP failure-consensus timeout (default 30)
+  lookahead_k              layers a synchronous load reads ahead of attention (default 4)
   kv_load_failure_policy   recompute | fail: vLLM's own kv_transfer_config field governs, applied by
                            vLLM's scheduler to the blocks the worker reports as failed
   store:
@@ -75,12 +76,13 @@ class ConnectorConfig:
     min_retrieve_tokens: int = 0
     max_tokens_per_load: int = 0
     failure_timeout_s: float = 30.0
+    lookahead_k: int = 4  # layers restored ahead of the layer attention is waiting for
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
         extra = dict(extra or {})
         known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio",
-                 "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s"}
+                 "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s", "lookahead_k"}
         unknown = set(extra) - known
         if unknown:
             raise ValueError(f"unknown connector options: {sorted(unknown)}")
@@ -93,6 +95,9 @@ class ConnectorConfig:
         c.min_retrieve_tokens = int(extra.get("min_retrieve_tokens", 0))
         c.max_tokens_per_load = int(extra.get("max_tokens_per_load", 0))
         c.failure_timeout_s = float(extra.get("failure_collective_timeout_s", 30.0))
+        c.lookahead_k = extra.get("lookahead_k", c.lookahead_k)
+        if not isinstance(c.lookahead_k, int) or isinstance(c.lookahead_k, bool) or c.lookahead_k <= 0:
+            raise ValueError(f"lookahead_k must be a positive integer, got {c.lookahead_k!r}")
         if c.min_retrieve_tokens < 0 or c.max_tokens_per_load < 0 or c.failure_timeout_s <= 0:
             raise ValueError("min_retrieve_tokens and max_tokens_per_load must be >= 0, the timeout > 0")
         from .load_policy import MODES, resolve_free_ratio

@@ -112,7 +112,8 @@ def layer_index(name: str) -> int:
 class WorkerSide:
     def __init__(self, make_engine: Callable[..., KVEngine], *, block_size: int,
                  chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
-                 consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute"):
+                 consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute",
+                 lookahead: int = 4):
         if failure_policy not in ("recompute", "fail"):
             raise ValueError("kv_load_failure_policy must be recompute or fail")
         self.make_engine = make_engine
@@ -123,6 +124,7 @@ class WorkerSide:
         self.tp_size = tp_size
         self.consensus = consensus or TpFailureConsensus()
         self.failure_policy = failure_policy
+        self.lookahead = max(1, int(lookahead))  # layers read ahead of the layer attention waits for
         self.engine: KVEngine | None = None
         self.health: HealthReporter | None = None
         self.layer_of: dict[str, int] = {}
@@ -183,7 +185,7 @@ class WorkerSide:
                 if self.engine.staged:
                     self._plan = self.engine.load(keys, blocks)
                 else:
-                    self._plan = self.engine.start_read_plan(keys, blocks)
+                    self._plan = self.engine.start_read_plan(keys, blocks, window=self.lookahead)
             except Exception as e:  # noqa: BLE001 - settled (with TP consensus) in wait_for_save
                 self._plan = _FailedLoad(e)
 
