@@ -291,3 +291,22 @@ def test_lookahead_option():
     for bad in (0, -1, True, "3"):
         with pytest.raises(ValueError):
             ConnectorConfig.from_extra({"lookahead_k": bad})
+
+
+def test_tutti_geometry_keys_are_checked():
+    layers = [torch.zeros(2, 8, BS, 2, 16) for _ in range(3)]
+    ok = ConnectorConfig.from_extra({"chunk_tokens": CHUNK, "num_layers": 3, "physical_chunk_tokens": CHUNK,
+                                     "max_chunks_per_wave": 64, "replica_io": True,
+                                     "store": {"type": "memory", "capacity_chunks": 8}})
+    make_engine(ok, layers, 0, 0, 1)
+    bad = ConnectorConfig.from_extra({"chunk_tokens": CHUNK, "num_layers": 4, "store": {"type": "memory"}})
+    with pytest.raises(ValueError, match="num_layers"):
+        make_engine(bad, layers, 0, 0, 1)
+    direct = ConnectorConfig.from_extra({"chunk_tokens": CHUNK, "direct_transfer": True, "store": {"type": "memory"}})
+    with pytest.raises(ValueError, match="direct_transfer"):
+        make_engine(direct, layers, 0, 0, 1)
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"chunk_tokens": CHUNK, "physical_chunk_tokens": 2 * CHUNK})
+    with pytest.raises(ValueError):
+        ConnectorConfig.from_extra({"store": {"type": "tutti_nvme", "options": {"segment_header_bytes": 100}}})
+    assert ConnectorConfig.from_extra({"store": {"options": {"segment_header_bytes": 8192}}}).segment_header_bytes == 8192

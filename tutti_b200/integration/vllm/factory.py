@@ -10,6 +10,11 @@
   max_tokens_per_load      cap on the tokens one request loads at once (default 0: no cap)
   failure_collective_timeout_s  TP failure-consensus timeout (default 30)
   lookahead_k              layers a synchronous load reads ahead of attention (default 4)
+  num_layers, chunk_kv_bytes, segment_bytes   optional; checked against vLLM's KV caches
+  physical_chunk_tokens    must equal chunk_tokens (one object per chunk)
+  direct_transfer          true: refuse a store that moves chunks through staging buffers
+  max_chunks_per_wave      accepted; a restore is one submission the io kernel pipelines
+  replica_io               accepted with a warning: the worker restores each rank's own slice
   kv_load_failure_policy   recompute | fail: vLLM's own kv_transfer_config field governs, applied by
                            vLLM's scheduler to the blocks the worker reports as failed
   store:
@@ -20,6 +25,7 @@
     capacity_chunks        capacity in chunks (or capacity: "64GiB")
     segment_file_slots     slots per segment file (default 2048)
     runtime_options        options of the native runtime (leases, slots_per_lease, ...)
+    segment_header_bytes   per-slot prefix bytes (a multiple of 4096; part of the on-disk layout)
     stored_format          native | fp8_block128
 Placeholders ``{LOCAL_RANK}`` / ``{RANK}`` in paths are expanded per worker.
 Parity: reference tutti/integration/vllm/factory.py:31-202 and
@@ -77,12 +83,18 @@ class ConnectorConfig:
     max_tokens_per_load: int = 0
     failure_timeout_s: float = 30.0
     lookahead_k: int = 4  # layers restored ahead of the layer attention is waiting for
+    expect: dict = field(default_factory=dict)  # num_layers / chunk_kv_bytes / segment_bytes given in the config
+    direct_transfer: bool = False  # require the direct (paged) path
+    segment_header_bytes: int = 0  # 0: the store's default
 
     @classmethod
     def from_extra(cls, extra: dict | None) -> "ConnectorConfig":
         extra = dict(extra or {})
         known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio",
-                 "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s", "lookahead_k"}
+                 "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s", "lookahead_k",
+                 # Tutti's keys for facts derived here from vLLM's tensors (checked, not required)
+                 "num_layers", "chunk_kv_bytes", "segment_bytes", "physical_chunk_tokens",
+                 "direct_transfer", "max_chunks_per_wave", "replica_io"}
         unknown = set(extra) - known
         if unknown:
             raise ValueError(f"unknown connector options: {sorted(unknown)}")
@@ -95,6 +107,15 @@ class ConnectorConfig:
         c.min_retrieve_tokens = int(extra.get("min_retrieve_tokens", 0))
         c.max_tokens_per_load = int(extra.get("max_tokens_per_load", 0))
         c.failure_timeout_s = float(extra.get("failure_collective_timeout_s", 30.0))
+        c.expect = {k: int(extra[k]) for k in ("num_layers", "chunk_kv_bytes", "segment_bytes") if k in extra}
+        if int(extra.get("physical_chunk_tokens", c.chunk_tokens)) != c.chunk_tokens:
+            raise ValueError("physical_chunk_tokens must equal chunk_tokens here (one object per chunk)")
+        c.direct_transfer = bool(extra.get("direct_transfer", False))
+        if "max_chunks_per_wave" in extra and int(extra["max_chunks_per_wave"]) <= 0:
+            raise ValueError("max_chunks_per_wave must be positive")
+        if extra.get("replica_io"):
+            LOG.warning("[tutti] replica_io is not wired into the vLLM worker here: each TP rank restores its "
+                        "own slice (the NVLink fan-out is available as parallel.fanout.FanoutRestorer)")
         c.lookahead_k = extra.get("lookahead_k", c.lookahead_k)
         if not isinstance(c.lookahead_k, int) or isinstance(c.lookahead_k, bool) or c.lookahead_k <= 0:
             raise ValueError(f"lookahead_k must be a positive integer, got {c.lookahead_k!r}")
@@ -126,7 +147,7 @@ class ConnectorConfig:
             # the drives a rank uses, by device id; mounts are derived per rank (storage/preset.py)
             c.preset = dict(preset)
         for k in ("root", "capacity", "capacity_chunks", "mounts", "segment_file_slots", "runtime_options",
-                  "stored_format", "defer_writes_after_reads"):
+                  "stored_format", "defer_writes_after_reads", "segment_header_bytes"):
             if k in opts:
                 st.setdefault(k, opts.pop(k))
         opts.pop("io_stream", None)
@@ -138,6 +159,9 @@ class ConnectorConfig:
         if "capacity" in st:
             c.capacity_bytes = parse_bytes(st.pop("capacity"))
         c.segment_file_slots = int(st.pop("segment_file_slots", c.segment_file_slots))
+        c.segment_header_bytes = int(st.pop("segment_header_bytes", 0))
+        if c.segment_header_bytes and (c.segment_header_bytes < 4096 or c.segment_header_bytes % 4096):
+            raise ValueError("segment_header_bytes must be a multiple of 4096 (at least 4096)")
         c.runtime_options = dict(st.pop("runtime_options", {}))
         c.stored_format = str(st.pop("stored_format", c.stored_format))
         dw = st.pop("defer_writes_after_reads", None)
@@ -191,6 +215,10 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
     from ...storage.registry import StoreContext, create_store
 
     g = geometry_from_layers(tensors, cfg.chunk_tokens, cfg.namespace or "vllm")
+    derived = {"num_layers": g.num_layers, "chunk_kv_bytes": g.chunk_bytes, "segment_bytes": g.segment_bytes}
+    for k, v in cfg.expect.items():
+        if not entity and derived[k] != v:
+            raise ValueError(f"{k}={v} in the connector config, but vLLM's KV caches give {derived[k]}")
     cap = cfg.capacity_for(g)
     ns = (cfg.namespace or g.fingerprint()).encode() + (b"/" + entity.encode() if entity else b"")
     device = tensors[0].device
@@ -201,7 +229,7 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
         options = {"root": expand(cfg.root, rank, local_rank),
                    "mounts": store_mounts(cfg, rank, local_rank, world),
                    "segment_file_slots": cfg.segment_file_slots, "runtime_options": cfg.runtime_options,
-                   "stored_format": cfg.stored_format}
+                   "stored_format": cfg.stored_format, "segment_header_bytes": cfg.segment_header_bytes}
     elif kind == "memory":
         options = {}
     else:
@@ -210,6 +238,8 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
                        local_rank=local_rank, world=world, entity=entity, options=options)
     store = create_store(kind, ctx)
     staged = kind == "memory" or not hasattr(store, "get_paged")
+    if staged and cfg.direct_transfer:
+        raise ValueError(f"direct_transfer: the {kind} store on {device} moves chunks through staging buffers")
     eng = KVEngine(store, g, capacity_chunks=cap, namespace=ns, device=device, staged=staged,
                    defer_writes_after_reads=cfg.defer_writes_after_reads)
     eng.restore_from_store()

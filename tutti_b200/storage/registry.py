@@ -112,7 +112,9 @@ def _tutti_store(ctx: StoreContext):
                          device=ctx.device.index, rank=ctx.rank, rank_count=ctx.world,
                          segment_file_slots=min(int(o.get("segment_file_slots", 2048)), max(16, ctx.capacity_chunks)),
                          runtime_options=dict(o.get("runtime_options") or {}), namespace=ctx.namespace,
-                         stored_format=o.get("stored_format", "native"))
+                         stored_format=o.get("stored_format", "native"),
+                         **({"segment_header_bytes": int(o["segment_header_bytes"])}
+                            if o.get("segment_header_bytes") else {}))
     return store.open()
 
 
