@@ -109,3 +109,31 @@ def test_reference_module_paths_resolve():
         m = importlib.import_module("tutti." + mod)
         for n in names:
             assert hasattr(m, n), f"tutti.{mod}.{n}"
+
+
+def test_tutti_store_factory_passes_the_config_through(monkeypatch):
+    """The tutti store's constructor arguments, checked with a stand-in class (the real one needs a GPU)."""
+    import tutti_b200.storage.tutti_store as ts
+    from tutti_b200.models.kv_geometry import KVGeometry
+
+    seen = {}
+
+    class FakeStore:
+        def __init__(self, root, geometry, **kw):
+            seen.update(root=root, **kw)
+
+        def open(self):
+            return self
+
+    monkeypatch.setattr(ts, "TuttiKVStore", FakeStore)
+    g = KVGeometry("t", num_layers=2, num_kv_heads=2, head_dim=64, chunk_tokens=32)
+    ctx = registry.StoreContext(geometry=g, capacity_chunks=100, namespace=b"ns", device=torch.device("cuda", 3),
+                                rank=1, world=2, entity="idx",
+                                options={"root": "/kv", "mounts": ["/m0", "/m1"], "segment_file_slots": 64,
+                                         "runtime_options": {"leases": 8}, "stored_format": "fp8_block128",
+                                         "segment_header_bytes": 8192})
+    registry.create_store("tutti_nvme", ctx)
+    assert seen["root"] == "/kv/entities/idx" and seen["mounts"] == ["/m0/entities/idx", "/m1/entities/idx"]
+    assert seen["device"] == 3 and seen["rank"] == 1 and seen["rank_count"] == 2
+    assert seen["segment_file_slots"] == 64 and seen["runtime_options"] == {"leases": 8}
+    assert seen["stored_format"] == "fp8_block128" and seen["segment_header_bytes"] == 8192
