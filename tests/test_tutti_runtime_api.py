@@ -67,3 +67,17 @@ def test_object_store_with_tutti_config(tmp_path):
     again.open("striped_local_nvme_file", cfg)
     assert sorted(again.recover()) == sorted(keys)
     again.close()
+
+
+def test_memory_store_with_tutti_names_and_host_buffers():
+    from tutti.storage.memory import MemoryKVStore
+
+    s = MemoryKVStore(segment_bytes=4096, num_chunks=4)
+    s.open()
+    src, dst = bytearray(range(256)) * 16, bytearray(4096)
+    a, b = s.register_buffer(src, 4096), s.register_buffer(memoryview(dst), 4096)
+    s.put_batch([(b"k" * 18, a, 0)]).wait()
+    s.get_batch([(b"k" * 18, b, 0)]).wait()
+    assert dst == src
+    with pytest.raises(ValueError):
+        MemoryKVStore(num_chunks=4)
