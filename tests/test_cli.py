@@ -70,3 +70,15 @@ def test_test_command_runs_the_suites(capsys):
     assert main(["test", "--dry-run", "-k", "cli"]) == 0
     out = capsys.readouterr().out.splitlines()
     assert "-m not gpu" in out[0] and out[0].endswith("-k cli") and out[1].endswith("tutti_native_tests")
+
+
+def test_cpp_api_example_round_trip(tmp_path):
+    import os
+
+    exe = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "tutti_b200", "bin",
+                       "tutti_posix_roundtrip")
+    if not os.path.exists(exe):
+        pytest.skip("native examples not built")
+    out = subprocess.run([exe, str(tmp_path)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "OK 1048576"

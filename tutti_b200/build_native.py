@@ -1,6 +1,7 @@
 """Builds the standalone native executables next to the package:
 
 * ``tutti_b200/bin/tutti_daemon``        - the device-manager daemon (queue leases);
+* ``tutti_b200/bin/tutti_posix_roundtrip`` - the public C++ API end to end on the POSIX data path
 * ``tutti_b200/bin/tutti_native_tests``  - C++ contract tests of the runtime
   (StorageRuntime against the mock DataPath kit, object store, config spec).
 
@@ -26,6 +27,11 @@ TARGETS = {
         "tests/native_tests.cpp", "runtime/storage_runtime.cpp", "objects/object_store.cpp",
         "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
         "resolvers/file_resolvers.cpp", "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",
+    ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
+    # the public C++ API without a GPU: runtime assembly, open, register, submit, wait
+    "tutti_posix_roundtrip": ([
+        "examples/posix_roundtrip.cpp", "runtime/storage_runtime.cpp", "resolvers/file_resolvers.cpp",
+        "datapaths/posix_data_path.cpp",
     ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
 }
 
