@@ -426,6 +426,13 @@ void controller_roundtrip(bool direct_io, bool map_reads = false) {
                        iova.value() + 4096);
     CHECK(hs.run(e) == 0);
     CHECK(std::memcmp(buf, pattern.data() + 8192, 8192) == 0);
+    // 40 more single-page reads: the 16-entry CQ wraps and its phase bit flips (2.5 laps)
+    for (std::uint32_t k = 0; k < 40; ++k) {
+        const std::uint64_t off = (k * 7u % 64u) * 4096u;
+        nvme::build_rw_sqe(e, nvme::kOpRead, 1, 1, ((1u << 20) + off) / lba, 4096 / lba, iova.value(), 0);
+        CHECK(hs.run(e) == 0);
+        CHECK(std::memcmp(buf, pattern.data() + off, 4096) == 0);
+    }
     // 64 KiB read through a PRP list (pages in reverse order)
     auto* l = static_cast<std::uint64_t*>(lst);
     for (int k = 0; k < 15; ++k) l[k] = iova.value() + (15 - k) * 4096ull;
