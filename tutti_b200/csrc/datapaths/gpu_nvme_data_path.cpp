@@ -289,7 +289,7 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
 
 Result<DataPathTarget> GpuNvmeDataPath::open(const ResolvedTarget& target) {
     std::lock_guard<std::mutex> g(mu_);
-    std::vector<Upload> uploads;
+    std::vector<DeviceUpload> uploads;
     auto r = open_locked(target, uploads);
     if (!r.ok()) return r;
     Status s = flush_uploads(uploads);
@@ -301,7 +301,7 @@ std::vector<Result<DataPathTarget>> GpuNvmeDataPath::open_many(const ResolvedTar
     std::lock_guard<std::mutex> g(mu_);
     std::vector<Result<DataPathTarget>> out;
     out.reserve(count);
-    std::vector<Upload> uploads;
+    std::vector<DeviceUpload> uploads;
     for (std::size_t i = 0; i < count; ++i) out.push_back(open_locked(*targets[i], uploads));
     Status s = flush_uploads(uploads);
     if (!s.ok())  // no target of the batch is usable without its device rows
@@ -310,33 +310,20 @@ std::vector<Result<DataPathTarget>> GpuNvmeDataPath::open_many(const ResolvedTar
     return out;
 }
 
-Status GpuNvmeDataPath::flush_uploads(std::vector<Upload>& uploads) {
-    // Caller holds mu_. Consecutive destinations (bump-allocated extents with
-    // under 256 bytes of alignment padding between them, fresh target rows)
-    // go up in one copy; the padding belongs to no target and is zero-filled.
+Status GpuNvmeDataPath::flush_uploads(std::vector<DeviceUpload>& uploads) {
+    // Caller holds mu_. One copy per run of nearby destinations in one allocation
+    // (bump-allocated extent arrays, consecutive target rows); see upload_plan.h.
     if (uploads.empty()) return Status::Ok();
     DeviceGuard guard(cfg_.accel_id);
-    std::size_t i = 0;
-    std::vector<char> run;
-    while (i < uploads.size()) {
-        char* start = uploads[i].dst;
-        run.assign(uploads[i].bytes.begin(), uploads[i].bytes.end());
-        std::size_t k = i + 1;
-        while (k < uploads.size() && uploads[k].dst >= start + run.size() &&
-               uploads[k].dst - (start + run.size()) < 256) {
-            run.resize(static_cast<std::size_t>(uploads[k].dst - start), 0);
-            run.insert(run.end(), uploads[k].bytes.begin(), uploads[k].bytes.end());
-            ++k;
-        }
-        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMemcpy(start, run.data(), run.size(), cudaMemcpyHostToDevice),
+    for (const UploadRun& r : coalesce_uploads(std::move(uploads), 255))
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMemcpy(r.dst, r.bytes.data(), r.bytes.size(), cudaMemcpyHostToDevice),
                                           "upload target rows"));
-        i = k;
-    }
     uploads.clear();
     return Status::Ok();
 }
 
-Result<DataPathTarget> GpuNvmeDataPath::open_locked(const ResolvedTarget& target, std::vector<Upload>& uploads) {
+Result<DataPathTarget> GpuNvmeDataPath::open_locked(const ResolvedTarget& target,
+                                                     std::vector<DeviceUpload>& uploads) {
     // Caller holds mu_. Host-side work of an open; the device copies it owes are
     // appended to `uploads` (flush_uploads).
     using R = Result<DataPathTarget>;
@@ -385,7 +372,8 @@ Result<DataPathTarget> GpuNvmeDataPath::open_locked(const ResolvedTarget& target
     extent_chunk_used_ += need;
     if (!ex.empty()) {
         const char* b = reinterpret_cast<const char*>(ex.data());
-        uploads.push_back({reinterpret_cast<char*>(dex), std::vector<char>(b, b + ex.size() * sizeof(ex[0]))});
+        uploads.push_back({extent_chunks_.back(), reinterpret_cast<char*>(dex),
+                           std::vector<char>(b, b + ex.size() * sizeof(ex[0]))});
     }
     TargetRec& tr = targets_[row];
     tr.generation = next_token_++;
@@ -396,7 +384,8 @@ Result<DataPathTarget> GpuNvmeDataPath::open_locked(const ResolvedTarget& target
     io::DevTarget dt{dex, p.file_size, static_cast<std::uint32_t>(ex.size()),
                      static_cast<std::uint32_t>(tr.generation), 0};
     const char* b = reinterpret_cast<const char*>(&dt);
-    uploads.push_back({reinterpret_cast<char*>(d_targets_ + row), std::vector<char>(b, b + sizeof(dt))});
+    uploads.push_back({reinterpret_cast<const char*>(d_targets_), reinterpret_cast<char*>(d_targets_ + row),
+                       std::vector<char>(b, b + sizeof(dt))});
     return DataPathTarget{row, tr.generation};
 }
 

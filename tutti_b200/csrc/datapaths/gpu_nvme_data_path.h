@@ -29,6 +29,7 @@
 #include <tutti/spi/resolver.h>
 
 #include "../kernels/io_kernel.h"
+#include "upload_plan.h"
 #include "../nvme/controller.h"
 
 namespace tutti {
@@ -189,13 +190,9 @@ private:
         std::chrono::steady_clock::time_point submitted_at{};
     };
 
-    // A host->device copy an open still owes (extents, a target row).
-    struct Upload {
-        char* dst;
-        std::vector<char> bytes;
-    };
-    Result<DataPathTarget> open_locked(const ResolvedTarget& target, std::vector<Upload>& uploads);
-    Status flush_uploads(std::vector<Upload>& uploads);
+    // Host->device copies an open still owes (extents, a target row).
+    Result<DataPathTarget> open_locked(const ResolvedTarget& target, std::vector<DeviceUpload>& uploads);
+    Status flush_uploads(std::vector<DeviceUpload>& uploads);
     Status init_device_side();
     Result<std::unique_ptr<Arena>> take_arena(std::size_t bytes);
     void return_arena(std::unique_ptr<Arena> a);

@@ -20,6 +20,7 @@
 #include <tutti/storage_runtime.h>
 
 #include "../config/runtime_spec.h"
+#include "../datapaths/upload_plan.h"
 #include "../nvme/controller.h"
 #include "../objects/digest.h"
 #include "../objects/object_store.h"
@@ -286,6 +287,30 @@ TEST(memfs_sample_plugs_into_an_unmodified_runtime) {
     CHECK(std::memcmp(src.data(), dst.data(), src.size()) == 0);
     CHECK(rt->release_io(*o.io).ok());
     CHECK(!rt->open("memfs://big?size=2M").ok());  // over budget
+}
+
+TEST(upload_runs_merge_within_an_allocation_only) {
+    static char arena[1024];
+    char* a = arena;        // allocation A: [0, 64)
+    char* b = arena + 64;   // allocation B starts right after A
+    auto up = [](const char* alloc, char* dst, std::vector<char> v) { return DeviceUpload{alloc, dst, std::move(v)}; };
+    std::vector<DeviceUpload> ups;
+    ups.push_back(up(b, b + 400, {7, 7}));          // B, far: its own run
+    ups.push_back(up(a, a + 40, {3, 3, 3, 3}));     // A, after the next one (input order does not matter)
+    ups.push_back(up(a, a + 0, {1, 1, 1, 1, 1, 1, 1, 1}));
+    ups.push_back(up(b, b + 0, {5, 5}));            // B at A's end: never merged with A
+    ups.push_back(up(a, a + 42, {9}));              // overlaps an earlier upload: later wins
+    auto runs = coalesce_uploads(ups, 255);
+    CHECK(runs.size() == 3);
+    CHECK(runs[0].dst == a && runs[0].bytes.size() == 44);  // [0, 44) with the gap zero-filled
+    CHECK(runs[0].bytes[0] == 1 && runs[0].bytes[8] == 0 && runs[0].bytes[39] == 0 && runs[0].bytes[40] == 3);
+    CHECK(runs[0].bytes[42] == 9 && runs[0].bytes[43] == 3);
+    CHECK(runs[1].dst == b && runs[1].bytes.size() == 2 && runs[1].bytes[0] == 5);
+    CHECK(runs[2].dst == b + 400 && runs[2].bytes.size() == 2);
+    std::vector<DeviceUpload> rows;  // consecutive 32-byte rows: one run
+    for (int r = 0; r < 5; ++r) rows.push_back(up(a, a + 32 * r, std::vector<char>(32, static_cast<char>(r))));
+    runs = coalesce_uploads(rows, 255);
+    CHECK(runs.size() == 1 && runs[0].bytes.size() == 160 && runs[0].bytes[159] == 4);
 }
 
 TEST(stub_runtime_memory_only) {
