@@ -81,3 +81,10 @@ def test_memory_store_with_tutti_names_and_host_buffers():
     assert dst == src
     with pytest.raises(ValueError):
         MemoryKVStore(num_chunks=4)
+
+
+def test_error_injection_hook_needs_emulated_drives():
+    rt = memfs_runtime()
+    with pytest.raises((IndexError, ValueError)):
+        rt.testing_inject_next_read_nvme_error(0x285)
+    rt.shutdown(1000)

@@ -132,7 +132,8 @@ public:
     Status attach_file(const std::string& path, const std::vector<BackingRange>& ranges);
     Status detach_file(const std::string& path);
 
-    void inject(InjectKind kind, std::uint32_t count, std::uint32_t delay_us = 0);
+    // `status`: for MEDIA_ERROR, the CQE status field (type and code) to post; 0: unrecovered read error.
+    void inject(InjectKind kind, std::uint32_t count, std::uint32_t delay_us = 0, std::uint32_t status = 0);
 
     // Stop workers (idempotent). Outstanding SQEs are left unexecuted.
     void stop();
@@ -185,6 +186,7 @@ private:
     std::atomic<std::uint32_t> inject_kind_{0};
     std::atomic<std::uint32_t> inject_count_{0};
     std::atomic<std::uint32_t> inject_delay_us_{0};
+    std::atomic<std::uint32_t> inject_status_{0};
 
     std::atomic<std::uint64_t> st_commands_{0}, st_read_{0}, st_write_{0}, st_errors_{0}, st_injected_{0};
 };

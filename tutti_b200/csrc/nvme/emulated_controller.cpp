@@ -231,8 +231,10 @@ Status EmulatedNvmeController::detach_file(const std::string& path) {
     return Status::Ok();
 }
 
-void EmulatedNvmeController::inject(InjectKind kind, std::uint32_t count, std::uint32_t delay_us) {
+void EmulatedNvmeController::inject(InjectKind kind, std::uint32_t count, std::uint32_t delay_us,
+                                    std::uint32_t status) {
     inject_delay_us_.store(delay_us);
+    inject_status_.store(status);
     inject_count_.store(count);
     inject_kind_.store(static_cast<std::uint32_t>(kind));
 }
@@ -303,9 +305,11 @@ std::uint32_t EmulatedNvmeController::execute(const Sqe& sqe, bool* drop_cqe) {
             st_injected_.fetch_add(1);
             if (c == 1) inject_kind_.store(0);
             switch (static_cast<InjectKind>(ik)) {
-                case InjectKind::MEDIA_ERROR:
+                case InjectKind::MEDIA_ERROR: {
                     st_errors_.fetch_add(1);
-                    return make_status(kSctMedia, kScUnrecoveredRead);
+                    const std::uint32_t raw = inject_status_.load();
+                    return raw ? raw : make_status(kSctMedia, kScUnrecoveredRead);
+                }
                 case InjectKind::DROP_COMPLETION:
                     *drop_cqe = true;
                     return 0;

@@ -463,7 +463,8 @@ PYBIND11_MODULE(_core, m) {
              })
         .def(
             "inject",
-            [](PyRuntime& r, int device, const std::string& kind, std::uint32_t count, std::uint32_t delay_us) {
+            [](PyRuntime& r, int device, const std::string& kind, std::uint32_t count, std::uint32_t delay_us,
+               std::uint32_t status) {
                 if (device < 0 || device >= static_cast<int>(r.extras.controllers.size()))
                     throw py::index_error("device index");
                 auto* emu = dynamic_cast<nvme::EmulatedNvmeController*>(r.extras.controllers[device].get());
@@ -472,9 +473,9 @@ PYBIND11_MODULE(_core, m) {
                                      : kind == "drop_completion" ? nvme::InjectKind::DROP_COMPLETION
                                      : kind == "delay"           ? nvme::InjectKind::DELAY
                                                                  : nvme::InjectKind::NONE;
-                emu->inject(k, count, delay_us);
+                emu->inject(k, count, delay_us, status);
             },
-            py::arg("device"), py::arg("kind"), py::arg("count") = 1, py::arg("delay_us") = 0)
+            py::arg("device"), py::arg("kind"), py::arg("count") = 1, py::arg("delay_us") = 0, py::arg("status") = 0)
         .def(
             "testing_inject_data_path",
             [](PyRuntime& r, const std::string& kind, std::uint32_t count) {

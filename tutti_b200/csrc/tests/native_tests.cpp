@@ -484,6 +484,12 @@ void controller_roundtrip(bool direct_io, bool map_reads = false) {
     CHECK(hs.run(e) == nvme::make_status(nvme::kSctMedia, nvme::kScUnrecoveredRead));
     nvme::build_rw_sqe(e, nvme::kOpRead, 8, 1, (1u << 20) / lba, 8, iova.value(), 0);
     CHECK(hs.run(e) == 0);
+    // an injected error can carry any CQE status (here: type 2, code 0x85)
+    c.inject(nvme::InjectKind::MEDIA_ERROR, 1, 0, nvme::make_status(2, 0x85));
+    nvme::build_rw_sqe(e, nvme::kOpRead, 9, 1, (1u << 20) / lba, 8, iova.value(), 0);
+    CHECK(hs.run(e) == nvme::make_status(2, 0x85));
+    nvme::build_rw_sqe(e, nvme::kOpRead, 10, 1, (1u << 20) / lba, 8, iova.value(), 0);
+    CHECK(hs.run(e) == 0);
     c.stop();
     free(buf);
     free(lst);

@@ -187,6 +187,12 @@ class Runtime:
     def open_io_count(self) -> int:
         return len(self._open)
 
+    def testing_inject_next_read_nvme_error(self, raw_cq_status: int) -> None:
+        """The next command the first drive serves completes with ``raw_cq_status`` (type and code bits)."""
+        if not hasattr(self.native, "inject"):
+            raise ValueError("error injection needs a runtime with emulated NVMe controllers")
+        self.native.inject(0, "media_error", 1, 0, int(raw_cq_status))
+
     def shutdown(self, timeout_ms: int) -> None:
         self.native.shutdown(int(timeout_ms))
 
