@@ -111,3 +111,14 @@ def test_latency_percentiles_in_the_health_line():
         m.observe("restore_ms", float(v))
     r = obs.HealthReporter(interval_s=0).report()
     assert r["restore_ms_p50"] == 51.0 and r["restore_ms_p99"] == 100.0
+
+
+def test_health_interval_has_a_floor(monkeypatch):
+    from tutti_b200.common.observability import health_interval_s
+
+    monkeypatch.setenv("TUTTI_HEALTH_INTERVAL_S", "0")
+    assert health_interval_s() == 1.0
+    monkeypatch.setenv("TUTTI_HEALTH_INTERVAL_S", "12.5")
+    assert health_interval_s() == 12.5
+    monkeypatch.delenv("TUTTI_HEALTH_INTERVAL_S")
+    assert health_interval_s() == 30.0

@@ -109,12 +109,17 @@ def metrics() -> Metrics:
         return _metrics
 
 
+def health_interval_s() -> float:
+    """``TUTTI_HEALTH_INTERVAL_S`` (default 30, at least 1: the health lines must not flood the log)."""
+    return max(1.0, float(os.environ.get("TUTTI_HEALTH_INTERVAL_S", "30") or 30))
+
+
 class HealthReporter:
     """Logs one ``[tutti] health`` line at most every ``interval_s`` seconds when ``maybe_log`` is called."""
 
     def __init__(self, store=None, interval_s: float | None = None, clock=time.monotonic):
         self.store = store
-        self.interval_s = float(os.environ.get("TUTTI_HEALTH_INTERVAL_S", "30")) if interval_s is None else interval_s
+        self.interval_s = health_interval_s() if interval_s is None else interval_s
         self._clock = clock
         self._last_t = clock()
         self._last = metrics().snapshot()

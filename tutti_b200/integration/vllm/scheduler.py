@@ -28,10 +28,10 @@ Parity: reference tutti/integration/vllm/connector.py:421 (get_num_new_matched_t
 from __future__ import annotations
 
 import logging
-import os
 import time
 from dataclasses import dataclass, field
 
+from ...common.observability import health_interval_s
 from ...index.chunk_index import ChunkIndex
 from .load_policy import LoadPolicy
 from .metadata import LoadSpec, SaveSpec, TuttiConnectorMetadata, TuttiWorkerMetadata
@@ -80,7 +80,7 @@ class SchedulerSide:
         self._async_blocks: dict[str, int] = {}  # asynchronous loads not yet received -> blocks held
         self._sync_loads: dict[int, list[tuple[str, list[bytes]]]] = {}  # generation -> loads dispatched
         self._async_loads: dict[str, list[bytes]] = {}  # request -> keys of its dispatched async load
-        self._log_interval = (float(os.environ.get("TUTTI_HEALTH_INTERVAL_S", "30")) if log_interval_s is None
+        self._log_interval = (health_interval_s() if log_interval_s is None
                               else log_interval_s)
         self._last_log = time.monotonic()
         self.profile = {"lookups": 0, "hit_tokens": 0, "hash_ms": 0.0, "loads_ok": 0, "loads_failed": 0}
