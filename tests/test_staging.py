@@ -72,3 +72,24 @@ def test_store_buffer_is_not_reused_before_the_previous_put_completes():
     assert torch.equal(pool[:, :, 20:24], ref[:, :, 0:4])
     assert torch.equal(pool[:, :, 30:34], ref[:, :, 8:12])
     assert isinstance(DoneCompletion(), DoneCompletion)
+
+
+def test_checkpoint_interval_zero_turns_periodic_checkpoints_off():
+    calls = []
+
+    class Objects:
+        def checkpoint(self):
+            calls.append(1)
+
+    store = MemoryKVStore(G.chunk_bytes, capacity_chunks=8)
+    store.open()
+    store.objects = Objects()
+    off = KVEngine(store, G, capacity_chunks=8, device=torch.device("cpu"), staged=True, checkpoint_interval_s=0)
+    off.poll_writes()
+    off.wait_idle()
+    assert calls == []
+    off._maybe_checkpoint(force=True)  # an explicit checkpoint still happens
+    assert calls == [1]
+    every = KVEngine(store, G, capacity_chunks=8, device=torch.device("cpu"), staged=True, checkpoint_interval_s=1e-9)
+    every.poll_writes()
+    assert calls == [1, 1]

@@ -462,6 +462,7 @@ class KVEngine:
         if not hasattr(self.store, "objects") or self.store.objects is None:
             return
         now = time.monotonic()
-        if force or now - self._last_checkpoint >= self._checkpoint_interval:
+        periodic = self._checkpoint_interval > 0  # 0 turns periodic checkpoints off (TUTTI_CHECKPOINT_INTERVAL_S=0)
+        if force or (periodic and now - self._last_checkpoint >= self._checkpoint_interval):
             self.store.objects.checkpoint()
             self._last_checkpoint = now
