@@ -293,12 +293,12 @@ def test_daemon_reads_tutti_schema(tmp_path):
         c = Client(sock)
         lst = c.kv("LIST")
         assert lst["devices"] == "0,1" and lst["kinds"] == "nvme,nvme" and lst["accelerators"] == "0,1"
-        assert lst["free_queues"] == "32,32" and lst["mounts"].endswith("nvme1")
+        assert lst["free_queues"] == "64,64" and lst["mounts"].endswith("nvme1")  # kernel_ioq_cap is not a budget
         s0 = c.kv(f"HELLO client=g0 pid={os.getpid()} accel=0")["session"]
         assert "RESOURCE_EXHAUSTED" in c(f"ACQUIRE session={s0} devices=0 queues=30")  # above max_per_client
         assert "PERMISSION_DENIED" in c(f"ACQUIRE session={s0} devices=1 queues=8")
         c.kv(f"ACQUIRE session={s0} devices=0 queues=0")  # 0: the pool's default
-        assert c.kv("LIST")["free_queues"] == "16,32"
+        assert c.kv("LIST")["free_queues"] == "48,64"
     finally:
         p.send_signal(signal.SIGTERM)
         p.wait(timeout=10)

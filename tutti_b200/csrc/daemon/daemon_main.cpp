@@ -8,7 +8,7 @@
 //   lease:   {heartbeat_timeout_s: 30, reap_interval_ms: 1000}
 //   queue_pool: {default_per_client: 16, max_per_client: 32}   # optional
 //   devices:   # or Tutti's nvmes: [{device_id, backing_mount_path, pci_addr, namespace_id,
-//              #                     kernel_ioq_cap, allowed_accel_ids}]
+//              #   allowed_accel_ids (empty: every accelerator of Tutti's accelerators: list)}]
 //     - {id: 0, kind: emulated, mount: /mnt/nvme0, queues: 128, pci: "0000:1b:00.0", nsid: 1, lba_bytes: 512,
 //        accelerators: [0, 1]}   # optional: only these GPUs may lease its queues
 //
@@ -106,12 +106,26 @@ int main(int argc, char** argv) {
         pool_max = static_cast<std::uint32_t>(m);
     }
     if (!st.ok()) return fail(st.to_string());
+    if (r.get("nvmes") && !r.get("queue_pool")) {  // Tutti's parser defaults
+        pool_default = 4;
+        pool_max = 32;
+    }
     if (r.get("grpc") && !r.get("service"))
         std::fprintf(stderr, "tutti_daemon: grpc.endpoint is not served (line protocol on %s)\n", socket_path.c_str());
 
     // Devices: this daemon's schema (devices: [{id, kind, mount, pci, queues, nsid, lba_bytes,
     // accelerators}]) or Tutti's (nvmes: [{device_id, backing_mount_path, pci_addr, namespace_id,
     // kernel_ioq_cap, allowed_accel_ids}]).
+    std::vector<std::int64_t> configured_accels;  // Tutti's accelerators: [{accel_id, view_root}]
+    if (const auto* acc = r.get("accelerators")) {
+        if (!acc->is_seq()) return fail("config: accelerators: expected a list");
+        for (std::size_t i = 0; i < acc->seq.size(); ++i) {
+            std::int64_t a = -1;
+            st = int_of(acc->seq[i]->get("accel_id"), "accelerators[" + std::to_string(i) + "].accel_id", a);
+            if (!st.ok()) return fail(st.to_string());
+            if (a >= 0) configured_accels.push_back(a);
+        }
+    }
     std::vector<DeviceInfo> devices;
     auto parse_list = [&](const yaml::Node& list, const std::string& name, bool tutti) -> Status {
         if (!list.is_seq()) return {StatusCode::INVALID_ARGUMENT, "config: " + name + ": expected a list"};
@@ -128,8 +142,9 @@ int main(int argc, char** argv) {
             if (auto k = d.get("kind")) info.kind = k->scalar;
             if (auto m = d.get(tutti ? "backing_mount_path" : "mount")) info.mount = m->scalar;
             if (auto c = d.get(tutti ? "pci_addr" : "pci")) info.pci = c->scalar;
+            // Tutti's kernel_ioq_cap is a kernel block-IO hint, not the queues offered to clients
             v = info.queues;
-            TUTTI_RETURN_IF_ERROR(int_of(d.get(tutti ? "kernel_ioq_cap" : "queues"), p + ".queues", v));
+            if (!tutti) TUTTI_RETURN_IF_ERROR(int_of(d.get("queues"), p + ".queues", v));
             info.queues = static_cast<std::uint32_t>(v);
             v = info.namespace_id;
             TUTTI_RETURN_IF_ERROR(int_of(d.get(tutti ? "namespace_id" : "nsid"), p + ".nsid", v));
@@ -144,6 +159,8 @@ int main(int argc, char** argv) {
                     info.accelerators.push_back(v);
                 }
             }
+            // Tutti: an empty allowed_accel_ids means every accelerator the file configures
+            if (tutti && info.accelerators.empty()) info.accelerators = configured_accels;
             if (info.kind != "emulated" && info.kind != "nvme")
                 return {StatusCode::INVALID_ARGUMENT, p + ".kind must be emulated or nvme"};
             devices.push_back(info);
