@@ -82,3 +82,17 @@ def test_preset_from_environment_is_parsed_and_checked(monkeypatch, daemons):
     monkeypatch.setenv("TUTTI_NVME_PRESET", '{"type": "local", "device_id": 7, "daemon_config": "%s"}' % daemons)
     with pytest.raises(ValueError, match="device id 7"):
         runtime_from_env()
+
+
+def test_raid0_preset_over_a_tutti_style_daemon_file(tmp_path):
+    d = tmp_path / "daemon_kv.yaml"
+    lines = ["nvmes:"]
+    for i in range(4):
+        lines += [f"- device_id: {i}", f'  pci_addr: "0000:0{i}:00.0"', "  backing_mount_path: /mnt/md_kv",
+                  "  namespace_id: 1", "  kernel_ioq_cap: 16", "  allowed_accel_ids: [0, 1, 2, 3]",
+                  "  auto_mount: false"]
+    lines += ["raid0_arrays:", "- name: kv", "  device_ids: [0, 1, 2, 3]", "  mount_path: /mnt/md_kv"]
+    d.write_text("\n".join(lines) + "\n")
+    p = prepare_preset({"type": "raid0", "daemon_config": [str(d)], "gpu_id": "{LOCAL_RANK}",
+                        "device_groups": [[0, 1, 2, 3]]}, rank=5, tp_size=8)
+    assert preset_mounts(p) == ["/mnt/md_kv"] and [x["pci_bdf"] for x in p["devices"]][-1] == "0000:03:00.0"
