@@ -83,6 +83,7 @@ def test_metadata_views_resolve_lazily():
 
 REFERENCE_MODULE_PATHS = {
     "common.errors": ["DirectTransferUnavailable"], "common.nvtx": ["enabled", "range"],
+    "common.utils": ["is_int", "positive_int", "parse_capacity", "flatten_block_ids"],
     "engine.completion": ["LoadGateError"], "engine.core": ["KVEngine"],
     "index.chunk_index": [], "integration.vllm.connector": ["TuttiConnectorV1"],
     "integration.vllm.worker": ["WorkerImpl"], "integration.vllm.worker_meta": ["TuttiWorkerMetadata"],
