@@ -49,3 +49,20 @@ def test_io_sweep_shapes_cover_the_reference_batches():
         chunks, layers = shape_for(target)
         pages = chunks * 16 * layers
         assert layers <= 32 and abs(pages - target) / target < 0.02
+
+
+def test_bench_reference_arm_prints_one_json_line():
+    """The driver's reference arm contract: exactly one JSON line with impl=reference (no GPU needed)."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "1", "--steps", "2",
+                          "--warmup", "3"], cwd=root, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    rec = json.loads(lines[0])
+    assert rec["impl"] == "reference" and ("unavailable" in rec or "value" in rec)
