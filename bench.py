@@ -165,24 +165,198 @@ def sum_over_ranks(world, value: float) -> float:
     return float(t.item())
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+REF_STAGED_NOTE = ("reference staged restore: KVEngine over MemoryKVStore (host DRAM) + RingWindow pinned "
+                   "staging + PagedTransferHooks -> tutti_kv_transfer single_layer_kv_transfer (K7); the "
+                   "reference's snvme SSD path needs drives and a kernel module this pool lacks")
+
+
+def _ensure_reference_kernels() -> str | None:
+    """Build the reference's own ``tutti_kv_transfer`` extension into baseline/_ref if it is missing.
+
+    The sources are the reference's ``csrc/kv_transfer`` tree, built unmodified by
+    its own setup.py with the arch list set for sm_100a. Returns a reason string
+    when the extension cannot be had.
+    """
+    import glob
+
+    if glob.glob(os.path.join(REF_DIR, "tutti_kv_transfer", "_native*.so")):
+        return None
+    src = os.environ.get("TUTTI_REFERENCE_SRC", "/root/reference")
+    if not os.path.isdir(os.path.join(src, "csrc", "kv_transfer")):
+        return "reference kv_transfer extension not built and its sources are not on this machine"
+    import tempfile
+
+    tmp = tempfile.mkdtemp(prefix="refkvt_")
+    shutil.copytree(os.path.join(src, "csrc", "kv_transfer"), os.path.join(tmp, "csrc", "kv_transfer"))
+    shutil.copy(os.path.join(src, "VERSION"), os.path.join(tmp, "VERSION"))
+    env = dict(os.environ, TORCH_CUDA_ARCH_LIST="10.0a", MAX_JOBS="8")
+    r = subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
+                        "--find-links", "/opt/wheelhouse", "--target", REF_DIR,
+                        os.path.join(tmp, "csrc", "kv_transfer")], env=env, capture_output=True, text=True)
+    shutil.rmtree(tmp, ignore_errors=True)
+    if r.returncode != 0:
+        return "building the reference kv_transfer extension failed: " + (r.stderr or r.stdout)[-200:].replace("\n", " ")
+    return None
+
+
 def reference_arm(args):
-    """The reference's stock path cannot run on this pool; say why in one line."""
-    ref = os.path.join(ROOT, "baseline", "_ref")
-    reason = None
-    if not os.path.isdir(os.path.join(ref, "tutti")):
-        reason = "reference package not installed under baseline/_ref"
-    else:
-        sys.path.insert(0, ref)
-        try:
-            import tutti_runtime._core  # noqa: F401  (the reference's native runtime)
-        except ImportError:
-            reason = ("reference SSD->HBM restore needs its native tutti_runtime._core (CMake build needing "
-                      "gRPC/protobuf/yaml-cpp, absent offline) plus the snvme kernel module, tutti_daemon and "
-                      "bindable NVMe drives (none on the GPU box); pip install yields only the pure-Python package")
+    """The reference's own build on the same config: its stock staged restore.
+
+    Path (all reference code, imported from baseline/_ref, nothing of this
+    repository): ``tutti.engine.core.KVEngine`` over ``tutti.storage.memory.MemoryKVStore``
+    (the prefix in host DRAM), staged through a pinned ``RingWindow`` and scattered
+    into the paged pool by ``PagedTransferHooks`` (tutti/integration/vllm/worker.py:256-460)
+    with the reference's K7 kernel (csrc/kv_transfer/src/mem_kernels.cu:66-130).
+    One step restores the 32 layers of the prefix with ``load_layer`` per layer
+    (tutti/engine/core.py:1936) and waits for every layer's scatter.
+    """
     rank = int(os.environ.get("RANK", "0"))
+
+    def unavailable(reason: str) -> int:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": reason}))
+        return 0
+
+    if not os.path.isdir(os.path.join(REF_DIR, "tutti")):
+        return unavailable("reference package not installed under baseline/_ref")
+    why = _ensure_reference_kernels()
+    if why:
+        return unavailable(why)
+    # The reference's packages must win over this repository's `tutti` import path.
+    here = {ROOT, os.path.abspath(os.getcwd())}
+    sys.path[:] = [REF_DIR] + [p for p in sys.path if os.path.abspath(p or ".") not in here]
+    for name in [m for m in sys.modules if m == "tutti" or m.startswith("tutti.")]:
+        del sys.modules[name]
+    import numpy as np
+    import torch
+
+    try:
+        import tutti
+        from tutti.engine.core import KVEngine
+        from tutti.engine.staging import RingWindow
+        from tutti.integration.vllm.worker import PagedTransferHooks
+        from tutti.storage.memory import MemoryKVStore
+        from tutti_kv_transfer import discover_engine_format
+    except Exception as e:  # noqa: BLE001 - one line for the driver
+        return unavailable(f"reference import failed: {type(e).__name__}: {e}")
+    if not os.path.abspath(tutti.__file__).startswith(REF_DIR) or "tutti_b200" in sys.modules:
+        return unavailable("reference import resolved outside baseline/_ref")
+    if not torch.cuda.is_available():
+        return unavailable("no CUDA device on this machine (the reference's K7 scatter needs one)")
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    L, H, D, BS, CT = 32, 8, 128, 16, 256  # Llama-3.1-8B KV, block 16, 256-token chunks
+    nblk = args.prefix_tokens // BS
+    nchunks = args.prefix_tokens // CT
+    bpc = CT // BS
+    seg = CT * 2 * H * D * 2  # one layer of one chunk: K and V rows, bf16
+    layers = [torch.empty((2, args.pool_blocks, BS, H, D), dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    store = MemoryKVStore(seg, nchunks + 16)
+    engine = KVEngine({"chunk_tokens": CT, "chunk_kv_bytes": seg * L, "max_chunks_per_wave": nchunks,
+                       "num_layers": L}, store)
+    # The worker's staged binding (worker.py:2320-2390): two banks of lookahead_k (2) layers each.
+    bank = 2 * nchunks
+    staging = torch.empty(2 * bank * seg, dtype=torch.uint8, pin_memory=True)
+    raw = staging.numpy()
+    read_window = RingWindow(raw, bank, seg, capacity_per_wave=nchunks, slot_base=0)
+    write_window = RingWindow(raw, bank, seg, capacity_per_wave=nchunks, slot_base=bank)
+    fmt = discover_engine_format(layers[0], use_mla=False)
+    hooks = PagedTransferHooks(lambda i: layers[i], staging, seg, CT, BS, fmt)
+    engine.bind({}, read_window, L, bpc, write_window=write_window, gather_fn=hooks.gather,
+                scatter_fn=hooks.scatter, force_staged=True)
+
+    rng = np.random.default_rng(rank)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    src_blocks = rng.permutation(args.pool_blocks)[:nblk].reshape(nchunks, bpc)
+    src_idx = torch.from_numpy(src_blocks.reshape(-1)).to(dev)
+    ref = torch.randn((L, 2, nblk, BS, H, D), dtype=torch.bfloat16, device=dev, generator=gen)
+    for i in range(L):
+        layers[i][:, src_idx] = ref[i]
+    tokens = torch.randint(0, 128_000, (args.prefix_tokens,), generator=torch.Generator().manual_seed(7 + rank))
+    keys, _ = engine.hash_keys(tokens.tolist())
+    t0 = time.perf_counter()
+    plan = engine.plan_store(keys)
+    if plan is None:
+        return unavailable("reference plan_store refused the prefix")
+    for i in range(L):
+        engine.store_layer(keys, i, [list(map(int, b)) for b in src_blocks])
+    engine.wait_idle()
+    engine.confirm_store(keys)
+    store_s = time.perf_counter() - t0
+    bytes_per_step = nblk * L * 2 * BS * H * D * 2
+
+    perms = [rng.permutation(args.pool_blocks)[:nblk].reshape(nchunks, bpc)
+             for _ in range(args.warmup + args.steps)]
+    tables = [[list(map(int, b)) for b in p] for p in perms]
+    pinned_tables = [torch.from_numpy(p.reshape(-1).copy()).pin_memory() for p in perms]
+    dev_table = torch.empty(nblk, dtype=torch.int64, device=dev)
+    checksum = torch.zeros(1, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    launches = [0]
+
+    def run_steps(first: int, count: int, e2e: bool) -> None:
+        for i in range(first, first + count):
+            if e2e:
+                dev_table.copy_(pinned_tables[i], non_blocking=True)
+            handles = [engine.load_layer(keys, layer, tables[i]) for layer in range(L)]
+            for h in handles:
+                h.wait()
+            launches[0] += L  # one K7 scatter launch per layer (the whole prefix is one wave)
+            if e2e:
+                checksum.copy_(layers[0][0, int(perms[i].reshape(-1)[0])].float().sum().reshape(1),
+                               non_blocking=True)
+        stream.synchronize()
+
+    run_steps(0, args.warmup, False)
+    barrier(world)
+    sampler = ClockSampler(list(range(world))).start() if rank == 0 else None
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    ev0.record(stream)
+    launches[0] = 0
+    run_steps(args.warmup, args.steps, False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dev_ms = ev0.elapsed_time(ev1) / args.steps
+    n_launch = launches[0]
+    barrier(world)
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    run_steps(args.warmup, args.steps, True)
+    ev3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev2.elapsed_time(ev3) / args.steps
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    last = torch.from_numpy(perms[-1].reshape(-1)).to(dev)
+    ok = all(bool(torch.equal(layers[i][:, last], ref[i])) for i in range(L))
+    ok_all = max_over_ranks(world, 0.0 if ok else 1.0) == 0.0
+    ms = max_over_ranks(world, dev_ms)
+    e2e = max_over_ranks(world, e2e_ms)
+    total_bytes = sum_over_ranks(world, float(bytes_per_step))
+    engine.close()
     if rank == 0:
-        print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": reason or "unknown"}))
-    return 0
+        value = total_bytes / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (randn KV of the named shape; prefix held by the reference's MemoryKVStore)",
+            "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world,
+                       "seq_len": args.prefix_tokens, "parallelism": f"dp{world} (one prefix per rank)",
+                       "pool_blocks": args.pool_blocks, "path": REF_STAGED_NOTE,
+                       "l2": "inputs (4.29 GB/step) larger than L2"},
+            "e2e": {"value": round(total_bytes / (e2e / 1e3) / 1e9, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": nblk * 8, "d2h_bytes_per_step": 4},
+            "gpu_launches": n_launch, "verified": ok_all, "store_setup_s": round(store_s, 2), "clocks": clocks,
+        }))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0 if ok_all else 1
 
 
 def measure_drive_gbps(store, keys, threads_per_drive: int, piece: int = 1 << 20, repeats: int = 2) -> float:

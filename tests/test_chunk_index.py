@@ -73,3 +73,32 @@ def test_incremental_hash_matches_full():
     a, p = idx.hash_keys(toks[:16])
     b, p2 = idx.hash_keys(toks, start=16, parent=p)
     assert a + b == full and p2 == last
+
+
+def test_eviction_picks_the_coldest_unpinned_key_among_many_pinned():
+    idx = ChunkIndex(capacity=200, chunk_tokens=1)
+    keys = [bytes([i // 256, i % 256]) * 8 for i in range(200)]
+    assert idx.plan_store(keys) is not None
+    idx.confirm_store(keys)
+    idx.pin(keys[:150])  # the 150 coldest are pinned
+    idx.mark_recent(keys[160:])  # keys[150:160] are now the coldest unpinned ones
+    new = [b"\xff" * 16, b"\xfe" * 16]
+    plan = idx.plan_store(new)
+    assert plan.evicted_keys == keys[150:152]
+    assert idx.stats() == {"capacity": 200, "resident": 198, "pending": 2, "pinned": 150, "epoch": 0}
+    # a deficit the unpinned keys cannot cover is refused without a change
+    idx.pin(keys[152:])
+    assert idx.plan_store([bytes([7]) * 16]) is None
+    assert idx.stats()["resident"] == 198
+
+
+def test_lookup_many_matches_lookup_prefix():
+    idx = ChunkIndex(capacity=16, chunk_tokens=4, namespace=b"ns")
+    prompts = [list(range(10)), list(range(100, 117)), list(range(3))]
+    keys, _ = idx.hash_keys(prompts[0])
+    idx.plan_store(keys)
+    idx.confirm_store(keys)
+    hits = idx.lookup_many(prompts)
+    assert [h for h, _ in hits] == [8, 0, 0]
+    assert hits[0][1] == keys and len(hits[1][1]) == 4 and hits[2][1] == []
+    assert [idx.lookup_prefix(p) for p in prompts] == [8, 0, 0]

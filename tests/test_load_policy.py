@@ -3,7 +3,7 @@ from types import SimpleNamespace
 
 import pytest
 
-from tutti_b200.integration.vllm.load_policy import LoadPolicy, resolve_free_ratio
+from tutti_b200.integration.vllm.load_policy import LineFit, LoadPolicy, free_ratio_setting
 from tutti_b200.integration.vllm.metadata import TuttiWorkerMetadata
 from tutti_b200.integration.vllm.scheduler import SchedulerSide
 
@@ -12,43 +12,67 @@ ROOMY = dict(held_blocks=0, need_blocks=10, free_blocks=1000)
 
 
 def test_modes_and_gates():
-    assert not LoadPolicy("sync").decide(chunks=100, compute_tokens=1, others=5, **ROOMY).is_async
+    assert not LoadPolicy("sync").decide(chunks=100, compute_tokens=1, others=5, **ROOMY).asynchronous
     a = LoadPolicy("async")
-    assert a.decide(chunks=1, compute_tokens=1, others=1, **ROOMY).is_async
+    assert a.decide(chunks=1, compute_tokens=1, others=1, **ROOMY).asynchronous
     d = a.decide(chunks=1, compute_tokens=1, others=0, **ROOMY)
-    assert not d.is_async and d.reason == "alone"
+    assert not d.asynchronous and d.basis == "alone"
     d = a.decide(chunks=1, compute_tokens=1, others=3, held_blocks=400, need_blocks=200, free_blocks=500)
-    assert not d.is_async and d.reason == "memory"  # 600 > 0.5 * (500 + 400)
+    assert not d.asynchronous and d.basis == "memory"  # 600 > 0.5 * (500 + 400)
     d = a.decide(chunks=1, compute_tokens=1, others=3, held_blocks=0, need_blocks=1, free_blocks=None)
-    assert d.reason == "memory"  # unknown pool: stay synchronous
-    assert a.decisions == {"async:mode=async": 1, "sync:alone": 1, "sync:memory": 2}
+    assert d.basis == "memory"  # unknown pool: stay synchronous
+    assert a.snapshot()["decisions"] == {"async/mode": 1, "sync/alone": 1, "sync/memory": 2}
     with pytest.raises(ValueError):
         LoadPolicy("sometimes")
 
 
+def test_line_fit_cases():
+    f = LineFit()
+    assert f.line() is None and f.at(3) is None
+    f.add(10, 50.0)  # one x: proportional through the origin
+    assert f.line() == (0.0, 5.0)
+    g = LineFit(half_life=1e9)
+    for x in (100, 1000, 400):
+        g.add(x, 30.0 + x / 90.0)
+    a, b = g.line()
+    assert a == pytest.approx(30.0) and b == pytest.approx(1 / 90.0)
+    h = LineFit(half_life=1e9)
+    h.add(1, 10.0)
+    h.add(5, 2.0)  # cost falling with size is not believed: the mean
+    assert h.line() == pytest.approx((6.0, 0.0))
+    k = LineFit(half_life=1.0)  # the newest sample weighs twice the one before
+    k.add(1, 1.0)
+    k.add(1, 4.0)
+    assert k.at(1) == pytest.approx(3.0)
+
+
 def test_auto_cost_rule_after_calibration():
     p = LoadPolicy("auto")
-    assert p.decide(chunks=10, compute_tokens=100, others=4, **ROOMY).reason == "uncalibrated"
-    p.observe_read(chunks=10, ms=50.0)  # 5 ms per chunk
-    p.observe_step(tokens=100, ms=30.0)  # decode-sized: step time only
-    assert p.compute_ms_per_token.value is None and p.step_ms.value == 30.0
-    p.observe_step(tokens=1000, ms=40.0)  # prefill-sized: 0.04 ms per token
-    assert p.compute_ms_per_token.value == pytest.approx(0.04)
-    # long read (100 chunks = 500 ms) vs T = 0.04*1000 + S: sync would stall 4 others -> async
+    assert p.decide(chunks=10, compute_tokens=100, others=4, **ROOMY).basis == "uncalibrated"
+    p.record_restore(chunks=10, ms=50.0)  # 5 ms per chunk
+    assert p.restore_ms(100) == pytest.approx(500.0)
+    assert p.decide(chunks=10, compute_tokens=100, others=4, **ROOMY).basis == "uncalibrated"  # no steps yet
+    p.record_step(tokens=100, ms=30.0)
+    p.record_step(tokens=1000, ms=40.0)
+    s0, s1 = p.steps.line()
+    assert s1 > 0 and s0 + s1 * 1000 == pytest.approx(40.0, rel=0.05)
+    # 100 chunks (500 ms) against a window of this request's 1000 tokens plus one typical step:
+    # a synchronous read would stall 4 others far longer than waiting costs this request
     d = p.decide(chunks=100, compute_tokens=1000, others=4, **ROOMY)
-    assert d.is_async and d.reason == "cost" and d.read_ms == pytest.approx(500.0)
-    # short read hides under the step -> sync
-    assert not p.decide(chunks=2, compute_tokens=1000, others=4, **ROOMY).is_async
+    assert d.asynchronous and d.basis == "cost" and d.read_ms == pytest.approx(500.0)
+    assert d.window_ms == pytest.approx(s1 * 1000 + p.step_ms(p.steps.mean_x))
+    # a short read hides under the window -> synchronous
+    assert not p.decide(chunks=2, compute_tokens=1000, others=4, **ROOMY).asynchronous
 
 
-def test_free_ratio_resolution(monkeypatch):
+def test_free_ratio_setting(monkeypatch):
     monkeypatch.delenv("TUTTI_ASYNC_LOAD_FREE_RATIO", raising=False)
-    assert resolve_free_ratio({}) == 0.5 and resolve_free_ratio({"async_load_free_ratio": 0.25}) == 0.25
+    assert free_ratio_setting({}) == 0.5 and free_ratio_setting({"async_load_free_ratio": 0.25}) == 0.25
     monkeypatch.setenv("TUTTI_ASYNC_LOAD_FREE_RATIO", "0.75")
-    assert resolve_free_ratio({"async_load_free_ratio": 0.25}) == 0.75
+    assert free_ratio_setting({"async_load_free_ratio": 0.25}) == 0.75
     monkeypatch.setenv("TUTTI_ASYNC_LOAD_FREE_RATIO", "2")
     with pytest.raises(ValueError):
-        resolve_free_ratio({})
+        free_ratio_setting({})
 
 
 def _resident_request(s, rid, n, base=0, status="RUNNING"):
@@ -98,8 +122,8 @@ def test_policy_learns_from_the_slowest_rank():
     a = TuttiWorkerMetadata(read_samples=[(10, 20.0)], step_samples=[(600, 30.0)])
     b = TuttiWorkerMetadata(read_samples=[(10, 50.0)], step_samples=[(600, 45.0)])
     s.update_from_workers(a.aggregate(b))
-    assert s.policy.read_ms_per_chunk.value == pytest.approx(5.0)
-    assert s.policy.step_ms.value == pytest.approx(45.0)
+    assert s.policy.restore_ms(1) == pytest.approx(5.0)  # the slower rank's 50 ms for 10 chunks
+    assert s.policy.step_ms(600) == pytest.approx(45.0)
     assert s.maybe_log(force=True)
 
 

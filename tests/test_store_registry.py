@@ -138,3 +138,19 @@ def test_tutti_store_factory_passes_the_config_through(monkeypatch):
     assert seen["device"] == 3 and seen["rank"] == 1 and seen["rank_count"] == 2
     assert seen["segment_file_slots"] == 64 and seen["runtime_options"] == {"leases": 8}
     assert seen["stored_format"] == "fp8_block128" and seen["segment_header_bytes"] == 8192
+
+
+def test_flatten_block_ids_never_raises():
+    import numpy as np
+
+    from tutti.common.utils import flatten_block_ids
+
+    assert flatten_block_ids(None) == ()
+    assert flatten_block_ids("abc") == ()
+    assert flatten_block_ids(b"\x01\x02") == ()
+    assert flatten_block_ids(7) == (7,)
+    assert flatten_block_ids([[1, 2], (3,), {4}, 5]) == (1, 2, 3, 4, 5)
+    assert flatten_block_ids([[1, [2, 3]], "x", None, np.int64(9)]) == (1, 9)
+    assert flatten_block_ids(np.array([[1, 2], [3, 4]])) == ()  # ndarray rows are neither lists nor ints
+    assert flatten_block_ids([np.array([1, 2])]) == ()
+    assert flatten_block_ids([[np.int32(5), True]]) == (5,)

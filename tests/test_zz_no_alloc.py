@@ -1,9 +1,9 @@
 """The allocation-free C entry point ``tutti_nvme_io_noalloc``.
 
-It serves callers that cannot allocate GPU memory while they move KV (code
-running under CUDA-graph capture, engines that hand all spare HBM to their KV
-pool, C-ABI embedders without a CUDA allocator): its scratch lives in a fixed
-device array inside the library. The test calls the exported C symbol through
+It serves callers that cannot allocate GPU memory while they move KV (engines
+that hand all spare HBM to their KV pool at start-up, so a cudaMalloc mid-step
+could fail; C-ABI embedders that own no CUDA allocator): its scratch lives in
+a fixed device array inside the library. The test calls the exported C symbol through
 ctypes and checks that two calls in a row restore exactly what the runtime's
 ordinary submit path restores. The file is named to be collected last.
 """
@@ -26,8 +26,8 @@ G = KVGeometry("noalloc-llama", num_layers=4, num_kv_heads=8, head_dim=128, chun
 
 class Command(ctypes.Structure):
     _fields_ = [("logical", ctypes.c_uint64), ("target_row", ctypes.c_uint32), ("bytes", ctypes.c_uint32),
-                ("first_piece", ctypes.c_uint32), ("n_pieces", ctypes.c_uint32), ("opcode", ctypes.c_uint32),
-                ("reserved", ctypes.c_uint32)]
+                ("first_piece", ctypes.c_uint32), ("n_pieces", ctypes.c_uint32), ("opcode", ctypes.c_uint16),
+                ("transform", ctypes.c_uint16), ("replicas", ctypes.c_uint32)]
 
 
 class Piece(ctypes.Structure):

@@ -31,12 +31,42 @@ def parse_capacity(value: str) -> int:
     return int(amount)
 
 
+def _block_id(value):
+    """An integer block id (int or NumPy integer, not bool), else None."""
+    if isinstance(value, bool):
+        return None
+    if isinstance(value, int):
+        return value
+    try:
+        import numpy as np
+    except ImportError:  # pragma: no cover - numpy is a dependency of torch
+        return None
+    return int(value) if isinstance(value, np.integer) else None
+
+
 def flatten_block_ids(block_tables) -> tuple[int, ...]:
-    """Block tables (nested sequences of ints) as one flat tuple."""
-    out = []
-    for row in block_tables:
-        if is_int(row):
-            out.append(row)
+    """Block ids of a wave's block tables as one flat tuple, for error reports.
+
+    Used on failure paths, so it never raises: ``None``, strings and bytes give
+    ``()``; a lone integer gives a 1-tuple; rows that are lists, tuples or sets
+    contribute their integer items (one level deep) and every other value is
+    skipped. Parity: tutti/common/utils.py:46-62 of the reference.
+    """
+    if block_tables is None or isinstance(block_tables, (str, bytes, bytearray)):
+        return ()
+    one = _block_id(block_tables)
+    if one is not None:
+        return (one,)
+    try:
+        rows = list(block_tables)
+    except TypeError:
+        return ()
+    out: list[int] = []
+    for row in rows:
+        if isinstance(row, (list, tuple, set)):
+            out.extend(b for b in map(_block_id, row) if b is not None)
         else:
-            out.extend(flatten_block_ids(row))
-    return tuple(int(x) for x in out)
+            b = _block_id(row)
+            if b is not None:
+                out.append(b)
+    return tuple(out)

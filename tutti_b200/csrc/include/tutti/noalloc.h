@@ -2,14 +2,17 @@
 /* Allocation-free entry point of the GPU NVMe io path.
  *
  * This entry point has no counterpart in the reference. It exists for callers
- * that must not allocate GPU memory when they move KV: code that runs while a
- * serving engine captures CUDA graphs (an allocation there breaks the
- * capture), engines that hand every free byte of HBM to their KV pool up
- * front and treat a later cudaMalloc as an out-of-memory risk, and embedders
- * that reach this library through a plain C ABI without a CUDA allocator of
- * their own. The call copies the caller's command list into a fixed device
- * array that is part of the library image, launches the same fused io kernel
- * the runtime uses, and waits for it on the caller's stream.
+ * that cannot allocate GPU memory at the moment they move KV: serving engines
+ * that hand every free byte of HBM to their KV pool at start-up, so that a
+ * later cudaMalloc in the middle of a step can fail with out-of-memory, and
+ * embedders that reach this library through a plain C ABI (a C, C++ or Rust
+ * serving process) and own no CUDA allocator of their own to lend it. The call
+ * copies the caller's command list into a fixed device array that is part of
+ * the library image and launches the same fused io kernel the runtime uses.
+ *
+ * The call is synchronous: it enqueues its copies and the kernel on the
+ * caller's stream, waits for that stream, reads the per-command status words
+ * on the host and only then returns.
  *
  * Limits (per call): at most TUTTI_NOALLOC_MAX_COMMANDS commands and
  * TUTTI_NOALLOC_MAX_PIECES pieces; larger batches are refused with
@@ -41,17 +44,22 @@ extern "C" {
 #define TUTTI_NOALLOC_MAX_PIECES 131072u
 #define TUTTI_NOALLOC_MAX_LEASES 256u
 
-/* Same layout as the io kernel's command: a contiguous logical range of one
- * opened target (row = the DataPath target token), read or written in one
- * staging slot. opcode: 2 = read (restore), 1 = write (store). */
+/* One command: a contiguous logical range of one opened target (target_row =
+ * the DataPath target token), read or written through one staging slot. The
+ * fields sit at the io kernel's own command offsets (checked at compile time),
+ * so the list is copied to the device as is.
+ *   opcode:    2 = read (restore), 1 = write (store);
+ *   transform: must be 0 (stored bytes equal memory bytes);
+ *   replicas:  must be 0 or 1 (the command's bytes go to one destination). */
 typedef struct {
     uint64_t logical;
     uint32_t target_row;
     uint32_t bytes;
     uint32_t first_piece;
     uint32_t n_pieces;
-    uint32_t opcode;
-    uint32_t reserved;
+    uint16_t opcode;
+    uint16_t transform;
+    uint32_t replicas;
 } tutti_noalloc_command;
 
 /* Where bytes [off, off + bytes) of a command live in caller memory

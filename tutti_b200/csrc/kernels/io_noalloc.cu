@@ -2,9 +2,9 @@
 // <tutti/noalloc.h>). This entry point has no counterpart in the reference.
 //
 // Who needs it: callers that cannot allocate GPU memory at the moment they
-// move KV, such as code running while a serving engine captures CUDA graphs,
-// engines that give all spare HBM to their KV pool at start-up, and C-ABI
-// embedders without a CUDA allocator. The runtime's own submit path keeps a
+// move KV, such as engines that give all spare HBM to their KV pool at
+// start-up (a cudaMalloc in the middle of a step could then fail) and C-ABI
+// embedders that own no CUDA allocator. The runtime's own submit path keeps a
 // pool of per-operation arenas obtained with cudaMalloc; this entry point
 // instead puts the launch's scratch (command list, piece list, lease ids, work
 // cursor, per-command status) in one fixed array below, which every GPU that
@@ -13,10 +13,12 @@
 // Limits: TUTTI_NOALLOC_MAX_COMMANDS commands, TUTTI_NOALLOC_MAX_PIECES pieces
 // and TUTTI_NOALLOC_MAX_LEASES CTAs per call (about 2.3 MiB in total);
 // anything larger is refused before launch. Calls that overlap on the GPU race
-// on the shared array. The first call on a device looks up the array's device
-// address with that device current; make it before any stream capture.
-// Nothing here calls cudaMalloc, cudaFree or any allocating routine.
+// on the shared array. The call is synchronous (it waits for its stream). The
+// first call on a device looks up the array's device address with that device
+// current; make it before any stream capture. Nothing here calls cudaMalloc,
+// cudaFree or any allocating routine.
 
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -41,6 +43,23 @@ constexpr std::size_t kOffCursor = align_up(kOffLeases + TUTTI_NOALLOC_MAX_LEASE
 constexpr std::size_t kOffStatus = align_up(kOffCursor + 16);
 constexpr std::size_t kScratchBytes = align_up(kOffStatus + TUTTI_NOALLOC_MAX_COMMANDS * sizeof(std::uint32_t));
 
+// The C structs are copied to the device unchanged, so every field must sit at
+// the io kernel's offset with the io kernel's width.
+#define TUTTI_SAME_FIELD(a, fa, b, fb)                                                   \
+    static_assert(offsetof(a, fa) == offsetof(b, fb) && sizeof(a::fa) == sizeof(b::fb), \
+                  #a "." #fa " must match " #b "." #fb)
+TUTTI_SAME_FIELD(tutti_noalloc_command, logical, tutti::io::IoCommand, logical);
+TUTTI_SAME_FIELD(tutti_noalloc_command, target_row, tutti::io::IoCommand, target);
+TUTTI_SAME_FIELD(tutti_noalloc_command, bytes, tutti::io::IoCommand, bytes);
+TUTTI_SAME_FIELD(tutti_noalloc_command, first_piece, tutti::io::IoCommand, first_piece);
+TUTTI_SAME_FIELD(tutti_noalloc_command, n_pieces, tutti::io::IoCommand, n_pieces);
+TUTTI_SAME_FIELD(tutti_noalloc_command, opcode, tutti::io::IoCommand, opcode);
+TUTTI_SAME_FIELD(tutti_noalloc_command, transform, tutti::io::IoCommand, transform);
+TUTTI_SAME_FIELD(tutti_noalloc_command, replicas, tutti::io::IoCommand, replicas);
+TUTTI_SAME_FIELD(tutti_noalloc_piece, mem, tutti::io::IoPiece, mem);
+TUTTI_SAME_FIELD(tutti_noalloc_piece, off, tutti::io::IoPiece, off);
+TUTTI_SAME_FIELD(tutti_noalloc_piece, bytes, tutti::io::IoPiece, bytes);
+#undef TUTTI_SAME_FIELD
 static_assert(sizeof(tutti_noalloc_command) == sizeof(tutti::io::IoCommand), "command layout");
 static_assert(sizeof(tutti_noalloc_piece) == sizeof(tutti::io::IoPiece), "piece layout");
 
@@ -54,7 +73,8 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 // address, so it is never handed to a kernel.
 void* g_scratch_addr[kMaxGpus] = {};
 std::mutex g_setup_mu;
-char g_last_error[256] = "";
+// Per calling thread: calls on different devices may run at the same time.
+thread_local char g_last_error[256] = "";
 
 int fail(int code, const char* msg) {
     std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
@@ -88,7 +108,8 @@ extern "C" int tutti_nvme_io_noalloc(void* data_path, const tutti_noalloc_comman
         const tutti_noalloc_command& k = commands[c];
         if (k.opcode != tutti::nvme::kOpRead && k.opcode != tutti::nvme::kOpWrite)
             return fail(TUTTI_NOALLOC_E_ARGS, "command opcode must be 1 (write) or 2 (read)");
-        if (k.reserved > 1) return fail(TUTTI_NOALLOC_E_ARGS, "command.reserved must be 0 or 1");
+        if (k.transform != 0) return fail(TUTTI_NOALLOC_E_ARGS, "command.transform must be 0 (no stored-format transform)");
+        if (k.replicas > 1) return fail(TUTTI_NOALLOC_E_ARGS, "command.replicas must be 0 or 1");
         if (k.bytes == 0 || k.n_pieces == 0 || k.first_piece > n_pieces || k.n_pieces > n_pieces - k.first_piece)
             return fail(TUTTI_NOALLOC_E_ARGS, "command piece range out of bounds");
         if (!dp->noalloc_target_ok(k.target_row, k.logical, k.bytes))

@@ -1,90 +1,133 @@
-"""Semantic index: chained chunk keys, residency, pins, pending writes, LRU.
+"""Prefix index of the KV store: chained chunk keys and chunk residency.
 
-Key derivation (fixed by the storage format; the GPU kernel
-``tutti_b200.ops.prefix_hash`` computes the same bytes):
-    key_0 = blake2b(namespace || le64(t_0) ... le64(t_{C-1}), digest_size=16)
-    key_i = blake2b(key_{i-1} || le64(tokens of chunk i), digest_size=16)
-A trailing partial chunk has no key. ``io_key = chunk_key(16) || le16(layer)``.
+Keys (fixed by the storage format; the GPU kernel ``tutti_b200.ops.prefix_hash``
+computes the same bytes, and segment-file headers store them)::
 
-State per key: resident (participates in hits and LRU), pending (a write was
-planned and not yet settled: occupies capacity, never hit, never evicted),
-pin count (> 0 protects from eviction). Eviction happens only in
-``plan_store``. Single-threaded; callers serialise.
-Parity: reference tutti/index/chunk_index.py:54-414.
+    key_0 = blake2b(namespace || le64(t_0) .. le64(t_{C-1}), digest_size=16)
+    key_i = blake2b(key_{i-1} || le64(tokens of chunk i),   digest_size=16)
+    io_key = chunk_key(16) || le16(layer)
+
+A trailing partial chunk has no key.
+
+Residency is a table of ``_Rec`` records, one per chunk key the index knows.
+A record is either PENDING (a write was planned and not yet settled: it takes
+capacity, is never a hit and is never evicted) or RESIDENT. Each record keeps
+its pin count, the epoch it was planned in and a recency stamp from a logical
+clock that every hit advances. Three side structures keep the hot operations
+away from full scans:
+
+* ``_victims``: a min-heap of ``(stamp, key)`` for resident, unpinned
+  records. Entries are invalidated lazily (a hit, a pin or a removal leaves
+  the old entry behind; it is skipped when popped because its stamp no
+  longer matches), and the heap is rebuilt when stale entries outnumber live
+  ones. Choosing k victims costs O(k log n) whatever is pinned.
+* ``_by_epoch``: pending keys bucketed by planning epoch, so reclaiming
+  reservations that no rank ever settled visits only the expired buckets.
+* counters of resident and pending records for the capacity check.
+
+The class is single-threaded; callers serialise (the scheduler and each
+worker engine own one index each).
+
+Parity: the reference keeps the same key chain and the same residency rules
+(plan reserves, confirm publishes, pins protect, pending never hits or is
+evicted, LRU eviction inside plan_store only) in tutti/index/chunk_index.py:54-414;
+this table-and-heap layout is this package's own.
 """
 from __future__ import annotations
 
 import hashlib
-import sys
-from array import array
-from collections import Counter, OrderedDict
-from dataclasses import dataclass
-from typing import Iterable, Sequence
+import heapq
+import struct
+from typing import Iterable, NamedTuple, Sequence
 
 KEY_BYTES = 16
 LAYER_BYTES = 2
 IO_KEY_BYTES = KEY_BYTES + LAYER_BYTES
 
+_PENDING = 1
+_RESIDENT = 2
 
-def _le64(tokens: Sequence[int]) -> bytes:
-    a = array("Q", tokens)
-    if sys.byteorder != "little":
-        a.byteswap()
-    return a.tobytes()
+
+# -- key derivation ----------------------------------------------------------
+
+def _token_bytes(tokens: Sequence[int]) -> bytes:
+    """Little-endian uint64 encoding of token ids."""
+    return struct.pack(f"<{len(tokens)}Q", *tokens)
 
 
 def chunk_digest(parent: bytes, chunk: Sequence[int]) -> bytes:
-    return hashlib.blake2b(parent + _le64(chunk), digest_size=KEY_BYTES).digest()
+    """Key of one chunk given its parent key (or the namespace for the first chunk)."""
+    h = hashlib.blake2b(digest_size=KEY_BYTES)
+    h.update(parent)
+    h.update(_token_bytes(chunk))
+    return h.digest()
 
 
 def chunk_keys_for_tokens(tokens: Sequence[int], chunk_tokens: int, namespace: bytes = b"",
                           parent: bytes | None = None) -> list[bytes]:
     """Chained keys of every complete chunk of ``tokens``."""
-    p = namespace if parent is None else parent
-    out = []
-    for i in range(0, len(tokens) - chunk_tokens + 1, chunk_tokens):
-        p = chunk_digest(p, tokens[i:i + chunk_tokens])
-        out.append(p)
-    return out
+    keys: list[bytes] = []
+    prev = namespace if parent is None else parent
+    whole = len(tokens) // chunk_tokens
+    for c in range(whole):
+        prev = chunk_digest(prev, tokens[c * chunk_tokens:(c + 1) * chunk_tokens])
+        keys.append(prev)
+    return keys
 
 
 def derive_io_key(chunk_key: bytes, layer: int) -> bytes:
+    """Object key of one layer of one chunk."""
     if not isinstance(chunk_key, (bytes, bytearray)) or len(chunk_key) != KEY_BYTES:
         raise ValueError(f"chunk key must be {KEY_BYTES} bytes")
-    if not isinstance(layer, int) or isinstance(layer, bool) or not 0 <= layer < (1 << (8 * LAYER_BYTES)):
+    if isinstance(layer, bool) or not isinstance(layer, int) or not 0 <= layer < (1 << (8 * LAYER_BYTES)):
         raise ValueError(f"layer out of range: {layer!r}")
-    return bytes(chunk_key) + layer.to_bytes(LAYER_BYTES, "little")
+    return bytes(chunk_key) + struct.pack("<H", layer)
 
 
 def decode_io_key(io_key: bytes) -> tuple[bytes, int]:
+    """(chunk key, layer) of an object key (a bare chunk key decodes as layer 0)."""
     if not isinstance(io_key, (bytes, bytearray, memoryview)) or len(io_key) == 0:
         raise ValueError("io_key must be non-empty bytes")
-    io_key = bytes(io_key)
-    return io_key[:KEY_BYTES], int.from_bytes(io_key[KEY_BYTES:], "little")
+    raw = bytes(io_key)
+    return raw[:KEY_BYTES], int.from_bytes(raw[KEY_BYTES:], "little")
+
+
+def _strict_io_key(io_key) -> bytes:
+    if not isinstance(io_key, (bytes, bytearray)) or len(io_key) != IO_KEY_BYTES:
+        raise ValueError(f"io_key must be {IO_KEY_BYTES} bytes")
+    return bytes(io_key)
 
 
 def chunk_key_of(io_key: bytes) -> bytes:
-    _check_io_key(io_key)
-    return bytes(io_key[:KEY_BYTES])
+    return _strict_io_key(io_key)[:KEY_BYTES]
 
 
 def layer_of(io_key: bytes) -> int:
-    _check_io_key(io_key)
-    return int.from_bytes(io_key[KEY_BYTES:], "little")
+    return struct.unpack("<H", _strict_io_key(io_key)[KEY_BYTES:])[0]
 
 
-def _check_io_key(io_key) -> None:
-    if not isinstance(io_key, (bytes, bytearray)) or len(io_key) != IO_KEY_BYTES:
-        raise ValueError(f"io_key must be {IO_KEY_BYTES} bytes")
+# -- residency ----------------------------------------------------------------
 
+class StorePlan(NamedTuple):
+    """Outcome of a write reservation: chunks to write, and chunks to drop first (coldest first)."""
 
-@dataclass
-class StorePlan:
     new_keys: list[bytes]
-    evicted_keys: list[bytes]  # oldest first; the caller drops their data
+    evicted_keys: list[bytes]
+
+
+class _Rec:
+    __slots__ = ("state", "pins", "epoch", "stamp")
+
+    def __init__(self, state: int, epoch: int, stamp: int):
+        self.state = state
+        self.pins = 0
+        self.epoch = epoch
+        self.stamp = stamp
 
 
 class ChunkIndex:
+    """Residency of chunk keys under a fixed capacity, with the key chain of one namespace."""
+
     def __init__(self, capacity: int, chunk_tokens: int, namespace: bytes = b""):
         if capacity <= 0:
             raise ValueError("capacity must be positive")
@@ -95,12 +138,16 @@ class ChunkIndex:
         self._capacity = int(capacity)
         self._chunk_tokens = int(chunk_tokens)
         self._namespace = bytes(namespace)
-        self._resident: OrderedDict[bytes, None] = OrderedDict()  # LRU: oldest first
-        self._pending: dict[bytes, int] = {}  # key -> epoch planned
-        self._pins: Counter[bytes] = Counter()
+        self._recs: dict[bytes, _Rec] = {}
+        self._victims: list[tuple[int, bytes]] = []
+        self._by_epoch: dict[int, set[bytes]] = {}
+        self._n_resident = 0
+        self._n_pending = 0
+        self._n_pinned = 0
+        self._clock = 0
         self._epoch = 0
 
-    # -- properties ---------------------------------------------------------
+    # -- facts ------------------------------------------------------------------
     @property
     def capacity(self) -> int:
         return self._capacity
@@ -118,146 +165,264 @@ class ChunkIndex:
         return self._epoch
 
     def stats(self) -> dict[str, int]:
-        return {"capacity": self._capacity, "resident": len(self._resident), "pending": len(self._pending),
-                "pinned": len(self._pins), "epoch": self._epoch}
+        return {"capacity": self._capacity, "resident": self._n_resident, "pending": self._n_pending,
+                "pinned": self._n_pinned, "epoch": self._epoch}
+
+    def _state(self, key: bytes) -> int:
+        rec = self._recs.get(key)
+        return rec.state if rec is not None else 0
 
     def is_resident(self, key: bytes) -> bool:
-        return key in self._resident
-
-    def is_pinned(self, key: bytes) -> bool:
-        return self._pins.get(key, 0) > 0
+        return self._state(key) == _RESIDENT
 
     def is_pending(self, key: bytes) -> bool:
-        return key in self._pending
+        return self._state(key) == _PENDING
 
-    # -- epochs ---------------------------------------------------------------
+    def is_pinned(self, key: bytes) -> bool:
+        rec = self._recs.get(key)
+        return rec is not None and rec.pins > 0
+
+    # -- recency and victims ------------------------------------------------------
+    def _tick(self) -> int:
+        self._clock += 1
+        return self._clock
+
+    def _offer(self, key: bytes, rec: _Rec) -> None:
+        """Make a resident, unpinned record an eviction candidate at its current stamp."""
+        heapq.heappush(self._victims, (rec.stamp, key))
+        if len(self._victims) > 64 and len(self._victims) > 4 * max(1, self._n_resident):
+            self._victims = [(r.stamp, k) for k, r in self._recs.items() if r.state == _RESIDENT and r.pins == 0]
+            heapq.heapify(self._victims)
+
+    def _touch(self, key: bytes, rec: _Rec) -> None:
+        rec.stamp = self._tick()
+        if rec.pins == 0:
+            self._offer(key, rec)
+
+    def _live_victim(self, stamp: int, key: bytes) -> bool:
+        rec = self._recs.get(key)
+        return rec is not None and rec.state == _RESIDENT and rec.pins == 0 and rec.stamp == stamp
+
+    def _take_victims(self, count: int, spare: set[bytes]) -> list[bytes] | None:
+        """The ``count`` coldest evictable keys outside ``spare``; None (heap unchanged) if too few."""
+        taken: list[tuple[int, bytes]] = []
+        skipped: list[tuple[int, bytes]] = []
+        while len(taken) < count and self._victims:
+            stamp, key = heapq.heappop(self._victims)
+            if not self._live_victim(stamp, key):
+                continue  # stale entry: dropped for good
+            (skipped if key in spare else taken).append((stamp, key))
+        for item in skipped:
+            heapq.heappush(self._victims, item)
+        if len(taken) < count:
+            for item in taken:
+                heapq.heappush(self._victims, item)
+            return None
+        return [k for _s, k in taken]
+
+    def _drop(self, key: bytes) -> None:
+        rec = self._recs.pop(key)
+        if rec.state == _RESIDENT:
+            self._n_resident -= 1
+        else:
+            self._n_pending -= 1
+            bucket = self._by_epoch.get(rec.epoch)
+            if bucket is not None:
+                bucket.discard(key)
+                if not bucket:
+                    del self._by_epoch[rec.epoch]
+        if rec.pins:
+            self._n_pinned -= 1
+
+    def _publish(self, key: bytes) -> None:
+        """Make ``key`` resident as the most recent chunk (new or previously pending)."""
+        rec = self._recs.get(key)
+        if rec is None:
+            rec = self._recs[key] = _Rec(_RESIDENT, self._epoch, self._tick())
+            self._n_resident += 1
+        elif rec.state == _PENDING:
+            self._drop(key)
+            rec = self._recs[key] = _Rec(_RESIDENT, self._epoch, self._tick())
+            self._n_resident += 1
+        else:
+            rec.stamp = self._tick()
+        if rec.pins == 0:
+            self._offer(key, rec)
+
+    # -- epochs -------------------------------------------------------------------
     def advance_epoch(self) -> int:
         self._epoch += 1
         return self._epoch
 
     def reclaim_stale_pending(self, max_age: int) -> list[bytes]:
-        """Drop reservations older than ``max_age`` epochs (a rank that never settled)."""
+        """Release reservations planned ``max_age`` or more epochs ago (nobody settled them)."""
         if max_age <= 0:
             return []
-        cutoff = self._epoch - max_age
-        stale = [k for k, e in self._pending.items() if e <= cutoff]
-        for k in stale:
-            del self._pending[k]
-        return stale
+        horizon = self._epoch - max_age
+        expired = [e for e in self._by_epoch if e <= horizon]
+        freed: list[bytes] = []
+        for e in sorted(expired):
+            for key in sorted(self._by_epoch.get(e, ())):
+                self._drop(key)
+                freed.append(key)
+        return freed
 
-    # -- hashing and lookup -------------------------------------------------
+    # -- hashing and lookup ---------------------------------------------------------
     def hash_keys(self, token_ids: Sequence[int], start: int = 0, parent: bytes | None = None,
                   max_keys: int | None = None) -> tuple[list[bytes], bytes]:
-        """Fold tokens from ``start`` (earlier tokens are already in ``parent``) into keys."""
+        """Keys of the complete chunks of ``token_ids[start:]`` chained from ``parent``.
+
+        ``parent`` is the key of the chunk that ends at ``start`` (the
+        namespace when None), so a caller can hash a growing prompt
+        incrementally. Returns the keys and the last key (the next parent).
+        """
         if start < 0:
             raise ValueError("start must be non-negative")
         if max_keys is not None and max_keys <= 0:
             raise ValueError("max_keys must be positive")
-        p = self._namespace if parent is None else parent
-        step = self._chunk_tokens
-        end = len(token_ids) - step + 1
+        n = (len(token_ids) - start) // self._chunk_tokens if len(token_ids) > start else 0
         if max_keys is not None:
-            end = min(end, start + max_keys * step)
-        keys = []
-        for i in range(start, end, step):
-            p = chunk_digest(p, token_ids[i:i + step])
-            keys.append(p)
-        return keys, p
-
-    def lookup_prefix(self, token_ids: Sequence[int]) -> int:
-        """Tokens of the longest resident chunk prefix; hits refresh the LRU."""
-        matched = 0
-        p = self._namespace
-        step = self._chunk_tokens
-        for i in range(0, len(token_ids) - step + 1, step):
-            p = chunk_digest(p, token_ids[i:i + step])
-            if p not in self._resident:
-                break
-            self._resident.move_to_end(p)
-            matched += step
-        return matched
+            n = min(n, max_keys)
+        tail = self._namespace if parent is None else parent
+        keys = chunk_keys_for_tokens(token_ids[start:start + n * self._chunk_tokens], self._chunk_tokens,
+                                     parent=tail)
+        return keys, (keys[-1] if keys else tail)
 
     def lookup_prefix_keys(self, keys: Sequence[bytes]) -> int:
-        matched = 0
-        for k in keys:
-            if k not in self._resident:
+        """Tokens covered by the longest run of resident keys from the start; hits become most recent."""
+        hits = 0
+        for key in keys:
+            rec = self._recs.get(key)
+            if rec is None or rec.state != _RESIDENT:
                 break
-            self._resident.move_to_end(k)
-            matched += self._chunk_tokens
-        return matched
+            self._touch(key, rec)
+            hits += 1
+        return hits * self._chunk_tokens
 
-    # -- two-phase store ------------------------------------------------------
-    def plan_store(self, keys: Iterable[bytes]) -> StorePlan | None:
-        """Reserve capacity for a write batch, evicting LRU unpinned keys if needed.
+    def lookup_prefix(self, token_ids: Sequence[int]) -> int:
+        """Hash ``token_ids`` chunk by chunk and stop at the first chunk that is not resident."""
+        prev = self._namespace
+        hits = 0
+        step = self._chunk_tokens
+        for c in range(len(token_ids) // step):
+            prev = chunk_digest(prev, token_ids[c * step:(c + 1) * step])
+            rec = self._recs.get(prev)
+            if rec is None or rec.state != _RESIDENT:
+                break
+            self._touch(prev, rec)
+            hits += 1
+        return hits * step
 
-        Returns None (and changes nothing) if any key is already pending or the
-        deficit cannot be covered by evictable keys outside the batch.
+    def lookup_many(self, requests: Sequence[Sequence[int]], device=None) -> list[tuple[int, list[bytes]]]:
+        """Prefix hits of many prompts at once: ``[(hit_tokens, keys)]`` per request.
+
+        With ``device`` (a CUDA device), the keys of every request are hashed
+        in one launch of the GPU prefix-hash kernel, which gives the same bytes
+        as the host chain; otherwise they are hashed on the host.
         """
-        batch = list(dict.fromkeys(keys))
-        in_batch = set(batch)
-        if any(k in self._pending for k in batch):
+        if device is not None:
+            from .. import ops
+
+            all_keys = ops.prefix_hash(requests, self._chunk_tokens, namespace=self._namespace, device=device)
+        else:
+            all_keys = [chunk_keys_for_tokens(r, self._chunk_tokens, namespace=self._namespace) for r in requests]
+        return [(self.lookup_prefix_keys(keys), keys) for keys in all_keys]
+
+    # -- writes -----------------------------------------------------------------------
+    def plan_store(self, keys: Iterable[bytes]) -> StorePlan | None:
+        """Reserve capacity for a batch of chunks about to be written.
+
+        Keys already resident need no write. If the free capacity does not
+        cover the new keys, the coldest resident, unpinned keys outside the
+        batch are evicted (the caller drops their data). Returns None and
+        changes nothing when a key of the batch is already pending or the
+        evictable keys do not cover the deficit.
+        """
+        batch: list[bytes] = []
+        seen: set[bytes] = set()
+        for k in keys:
+            if k not in seen:
+                seen.add(k)
+                batch.append(k)
+        if any(self._state(k) == _PENDING for k in batch):
             return None
-        new = [k for k in batch if k not in self._resident]
-        deficit = len(new) - (self._capacity - len(self._resident) - len(self._pending))
-        evicted: list[bytes] = []
-        if deficit > 0:
-            for k in self._resident:
-                if len(evicted) == deficit:
-                    break
-                if k not in in_batch and self._pins.get(k, 0) == 0:
-                    evicted.append(k)
-            if len(evicted) < deficit:
+        fresh = [k for k in batch if self._state(k) != _RESIDENT]
+        free = self._capacity - self._n_resident - self._n_pending
+        victims: list[bytes] = []
+        if len(fresh) > free:
+            got = self._take_victims(len(fresh) - free, seen)
+            if got is None:
                 return None
-            for k in evicted:
-                del self._resident[k]
-        for k in new:
-            self._pending[k] = self._epoch
-        return StorePlan(new_keys=new, evicted_keys=evicted)
+            victims = got
+            for k in victims:
+                self._drop(k)
+        bucket = self._by_epoch.setdefault(self._epoch, set())
+        for k in fresh:
+            self._recs[k] = _Rec(_PENDING, self._epoch, 0)
+            self._n_pending += 1
+            bucket.add(k)
+        return StorePlan(fresh, victims)
 
     def confirm_store(self, keys: Iterable[bytes], ok: bool = True) -> None:
-        """Settle a planned batch: resident (most recent) on success, else release capacity."""
+        """Settle reservations: published as most recent on success, released on failure."""
         for k in keys:
-            self._pending.pop(k, None)
+            state = self._state(k)
             if ok:
-                self._resident.pop(k, None)
-                self._resident[k] = None
+                self._publish(k)
+            elif state == _PENDING:
+                self._drop(k)
 
-    # -- protection -----------------------------------------------------------
+    # -- protection ---------------------------------------------------------------------
     def pin(self, keys: Iterable[bytes]) -> None:
+        """Protect resident keys from eviction (counted); any key not resident -> KeyError, nothing pinned."""
         batch = list(keys)
-        missing = [k for k in batch if k not in self._resident]
-        if missing:
-            raise KeyError(missing)
+        absent = [k for k in batch if self._state(k) != _RESIDENT]
+        if absent:
+            raise KeyError(absent)
         for k in batch:
-            self._pins[k] += 1
+            rec = self._recs[k]
+            if rec.pins == 0:
+                self._n_pinned += 1
+            rec.pins += 1
 
     def unpin(self, keys: Iterable[bytes]) -> None:
+        """Release one pin per key; a key without pins -> KeyError, nothing released."""
         batch = list(keys)
-        missing = [k for k in batch if self._pins.get(k, 0) <= 0]
-        if missing:
-            raise KeyError(missing)
+        need: dict[bytes, int] = {}
         for k in batch:
-            self._pins[k] -= 1
-            if self._pins[k] == 0:
-                del self._pins[k]
+            need[k] = need.get(k, 0) + 1
+        short = [k for k, n in need.items() if k not in self._recs or self._recs[k].pins < n]
+        if short:
+            raise KeyError(short)
+        for k in batch:
+            rec = self._recs[k]
+            rec.pins -= 1
+            if rec.pins == 0:
+                self._n_pinned -= 1
+                if rec.state == _RESIDENT:
+                    self._offer(k, rec)
 
     def mark_recent(self, keys: Iterable[bytes]) -> None:
         for k in keys:
-            if k in self._resident:
-                self._resident.move_to_end(k)
+            rec = self._recs.get(k)
+            if rec is not None and rec.state == _RESIDENT:
+                self._touch(k, rec)
 
     def restore(self, keys: Iterable[bytes]) -> None:
-        """Cold start: publish keys recovered from the store (oldest first), within capacity."""
+        """Cold start: publish keys recovered from the store, oldest first, while capacity lasts."""
         for k in keys:
-            if len(self._resident) + len(self._pending) >= self._capacity:
+            if self._state(k) == _RESIDENT:
+                continue
+            if self._n_resident + self._n_pending >= self._capacity:
                 break
-            self._resident[k] = None
+            self._publish(k)
 
     def forget(self, keys: Iterable[bytes]) -> list[bytes]:
-        """Drop residency of unpinned keys (data was lost or invalidated); returns those dropped."""
-        dropped = []
+        """Drop residency of unpinned keys whose data was lost; returns the keys dropped."""
+        gone: list[bytes] = []
         for k in keys:
-            if k in self._resident and self._pins.get(k, 0) == 0:
-                del self._resident[k]
-                dropped.append(k)
-        return dropped
+            rec = self._recs.get(k)
+            if rec is not None and rec.state == _RESIDENT and rec.pins == 0:
+                self._drop(k)
+                gone.append(k)
+        return gone

@@ -121,11 +121,11 @@ class ConnectorConfig:
             raise ValueError(f"lookahead_k must be a positive integer, got {c.lookahead_k!r}")
         if c.min_retrieve_tokens < 0 or c.max_tokens_per_load < 0 or c.failure_timeout_s <= 0:
             raise ValueError("min_retrieve_tokens and max_tokens_per_load must be >= 0, the timeout > 0")
-        from .load_policy import MODES, resolve_free_ratio
+        from .load_policy import MODES, free_ratio_setting
 
         if c.load_mode not in MODES:
             raise ValueError(f"load_mode must be one of {MODES}, got {c.load_mode!r}")
-        c.async_load_free_ratio = resolve_free_ratio(extra)
+        c.async_load_free_ratio = free_ratio_setting(extra)
         st = dict(extra.get("store", {}))
         c.store_type = st.pop("type", c.store_type)
         if c.store_type == "tutti_nvme":

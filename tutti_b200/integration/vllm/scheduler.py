@@ -142,7 +142,7 @@ class SchedulerSide:
                                       compute_tokens=len(tokens) - num_computed_tokens - ext, others=others,
                                       held_blocks=held, need_blocks=-(-(num_computed_tokens + ext) // self.block_size),
                                       free_blocks=free)
-        return ext, decision.is_async
+        return ext, decision.asynchronous
 
     def update_state_after_alloc(self, request, block_ids: list[int], num_external_tokens: int,
                                  num_computed_tokens: int = 0, is_async: bool = False) -> None:
@@ -229,10 +229,10 @@ class SchedulerSide:
         # TP ranks advance together: each step follows its slowest rank
         reads = [(int(c), float(ms)) for c, ms in wm.read_samples if c > 0 and ms > 0]
         if reads:
-            self.policy.observe_read(*max(reads, key=lambda x: x[1] / x[0]))
+            self.policy.record_restore(*max(reads, key=lambda x: x[1] / x[0]))
         steps = [(int(t), float(ms)) for t, ms in wm.step_samples if t > 0 and ms > 0]
         if steps:
-            self.policy.observe_step(*max(steps, key=lambda x: x[1]))
+            self.policy.record_step(*max(steps, key=lambda x: x[1]))
         done = [k for k, n in wm.committed.items() if n >= self.tp_size and k in self._planned]
         for k in done:
             self._planned.pop(k, None)
