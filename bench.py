@@ -51,8 +51,12 @@ def parse():
     p.add_argument("--no-verify", action="store_true")
     p.add_argument("--timing", action="store_true", help="per-command %globaltimer breakdown (stderr)")
     p.add_argument("--leases", type=int, default=192, help="queue leases (CTAs) per GPU")
-    p.add_argument("--ctas", type=int, default=96, help="CTAs one restore may use")
-    p.add_argument("--slots", type=int, default=8)
+    p.add_argument("--ctas", type=int, default=0, help="CTAs one restore may use (0: by media)")
+    p.add_argument("--slots", type=int, default=16)
+    p.add_argument("--media", choices=["memory", "files"], default="memory",
+                   help="emulated drive media: in-memory image DMA'd into HBM, or the files (pread)")
+    p.add_argument("--drive-gbps", type=float, default=0.0, help="per-drive transfer cap (0: none)")
+    p.add_argument("--e2e-parts", default="h2d,readback", help=argparse.SUPPRESS)  # diagnostics
     p.add_argument("--inflight", type=int, default=2, help="restores submitted ahead")
     p.add_argument("--emulator-skip-data", action="store_true", help="diagnostic: controllers move no data")
     p.add_argument("--staging-wc", action="store_true", help="write-combined staging slots")
@@ -401,8 +405,42 @@ def measure_drive_gbps(store, keys, threads_per_drive: int, piece: int = 1 << 20
     return best
 
 
+def measure_dma_gbps(dev, piece: int = 1 << 20, total: int = 2 << 30) -> float:
+    """Copy-engine rate of the drives' transfers: 1 MiB copies from page-locked host memory into HBM.
+
+    The same transfer size and direction the emulated drives issue for each
+    READ command, back to back on one stream, timed with CUDA events.
+    """
+    import torch
+
+    src = torch.empty(256 << 20, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    s = torch.cuda.Stream(dev)
+    n = total // piece
+    k = (256 << 20) // piece
+    with torch.cuda.stream(s):
+        for i in range(k):  # warm-up
+            dst[i * piece:(i + 1) * piece].copy_(src[i * piece:(i + 1) * piece], non_blocking=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(n):
+            j = i % k
+            dst[j * piece:(j + 1) * piece].copy_(src[j * piece:(j + 1) * piece], non_blocking=True)
+        e1.record(s)
+    e1.synchronize()
+    return total / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+
 def main():
     args = parse()
+    # More hardware queues (before CUDA starts): the emulated drives' copy
+    # streams then rarely share one with a stream that has work waiting on an
+    # io kernel.
+    os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+    # Load every kernel when CUDA starts: loading one lazily while an io kernel
+    # waits for the drives takes a context-wide lock that also stalls the
+    # drives' copy calls until the io kernel's deadline.
+    os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
     if args.impl == "reference":
         return reference_arm(args)
     import numpy as np
@@ -424,9 +462,16 @@ def main():
     # 3 workers per emulated drive measured best at 1 and 4 GPUs (16 and 32 host cores);
     # fewer when the box has under two cores per worker
     idle_spins = args.idle_spins or 2000  # 64 measured no different, even on 4 cores
-    threads = args.controller_threads or max(1, min(3, (2 * ncpu // max(1, world)) // max(1, args.drives)))
+    memory = args.media == "memory"
+    if memory:
+        # a drive worker only walks PRPs and issues copies: one per drive
+        threads = args.controller_threads or 1
+    else:
+        threads = args.controller_threads or max(1, min(3, (2 * ncpu // max(1, world)) // max(1, args.drives)))
+    ctas = args.ctas or (32 if memory else 96)
     opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": args.leases,
-            "max_ctas_per_op": args.ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20,
+            "emulator_media": args.media, "drive_gbps": args.drive_gbps,
+            "max_ctas_per_op": ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20,
             "queue_depth": 256, "mdts_bytes": 1 << 20, "timing": bool(args.timing),
             "emulator_skip_data": bool(args.emulator_skip_data), "emulator_reads": args.emulator_reads,
             "staging_write_combined": bool(args.staging_wc), "emulator_idle_spins": idle_spins}
@@ -435,6 +480,8 @@ def main():
         opts = {"threads": max(4, ncpu // max(1, world)), "direct_io": bool(args.direct_io)}
     # capacity: the prefix plus one spare file group
     spf = max(16, (nchunks + args.drives - 1) // args.drives)
+    if memory:  # each drive's image arena holds its segment file (allocated when the drive is created)
+        opts["image_budget_bytes"] = spf * (g.chunk_bytes + (128 << 10)) + (128 << 20)
     store = TuttiKVStore(root, g, capacity_chunks=spf * args.drives, mounts=mounts, device=local,
                          backend=backend, runtime_options=opts, segment_file_slots=spf,
                          namespace=b"bench")
@@ -452,30 +499,59 @@ def main():
     tokens = torch.randint(0, 128_000, (args.prefix_tokens,), generator=torch.Generator().manual_seed(7 + rank))
     keys = chunk_keys_for_tokens(tokens.tolist(), g.chunk_tokens)
     t0 = time.perf_counter()
-    store.put_paged(keys, src_blocks).wait()
+    try:
+        store.put_paged(keys, src_blocks).wait()
+    except Exception:
+        print(json.dumps({"controllers": store.runtime.controller_stats()}), file=sys.stderr)
+        raise
     store_s = time.perf_counter() - t0
     store.warm_targets()
     bytes_per_step = nblk * g.num_layers * g.block_layer_bytes
-    # roofline: the emulated drives' own ceiling, all ranks at once (host-only reads)
+    # roofline: the emulated drives' own ceiling, all ranks at once
     barrier(world)
-    drive_gbps = measure_drive_gbps(store, keys, threads) if backend == "nvme-gpu" else 0.0
+    if backend != "nvme-gpu":
+        drive_gbps = 0.0
+    elif memory:
+        drive_gbps = measure_dma_gbps(dev)  # the copies the drives issue, with no protocol around them
+    else:
+        drive_gbps = measure_drive_gbps(store, keys, threads)  # host-only reads of the files
     drive_total = sum_over_ranks(world, drive_gbps)
+    if args.drive_gbps:
+        drive_total = min(drive_total, args.drive_gbps * args.drives * world)
 
     perms = [rng.permutation(args.pool_blocks)[:nblk].reshape(nchunks, g.blocks_per_chunk)
              for _ in range(args.warmup + args.steps)]
     pinned_tables = [torch.from_numpy(p.reshape(-1).copy()).pin_memory() for p in perms]
     dev_table = torch.empty(nblk, dtype=torch.int64, device=dev)
     checksum = torch.zeros(1, dtype=torch.float32).pin_memory()
-    stream = torch.cuda.current_stream(dev)
+    # The restores run on an io stream of their own and the per-step input and
+    # result copies on a copy stream (as a serving engine keeps them), so no
+    # copy is ever queued behind a running io kernel.
+    stream = torch.cuda.Stream(dev)
+    copy_stream = torch.cuda.Stream(dev)
     launches = [0]
     io_bytes = [0, 0]  # per e2e run: H2D command arenas, D2H statuses
+
+    parts = set(args.e2e_parts.split(","))
+
+    def result_readback(j: int) -> None:
+        if "readback" not in parts:
+            return
+        with torch.cuda.stream(copy_stream):  # D2H: the step's result (a checksum of its first restored block)
+            if "nosum" in parts:
+                checksum.view(torch.bfloat16)[:2].copy_(pool[0, 0, int(perms[j].reshape(-1)[0]), 0, 0, :2],
+                                                        non_blocking=True)
+            else:
+                checksum.copy_(pool[0, 0, int(perms[j].reshape(-1)[0])].float().sum().reshape(1), non_blocking=True)
 
     def run_steps(first: int, count: int, e2e: bool) -> None:
         """``count`` restores with up to ``args.inflight`` submitted ahead (host work overlaps IO)."""
         pending = []
         for i in range(first, first + count):
-            if e2e:
-                dev_table.copy_(pinned_tables[i], non_blocking=True)  # H2D: this step's block table
+            if e2e and "h2d" in parts:
+                with torch.cuda.stream(copy_stream):  # H2D: this step's block table
+                    dev_table.copy_(pinned_tables[i], non_blocking=True)
+                stream.wait_stream(copy_stream)
             comp = store.get_paged(keys, perms[i], stream=stream)
             launches[0] += len(comp._ios)
             if e2e and backend == "nvme-gpu":
@@ -487,15 +563,25 @@ def main():
                 j, c = pending.pop(0)
                 c.wait()
                 if e2e:
-                    # D2H: the step's result (a checksum of its first restored block)
-                    checksum.copy_(pool[0, 0, int(perms[j].reshape(-1)[0])].float().sum().reshape(1),
-                                   non_blocking=True)
+                    result_readback(j)
         for j, c in pending:
             c.wait()
             if e2e:
-                checksum.copy_(pool[0, 0, int(perms[j].reshape(-1)[0])].float().sum().reshape(1), non_blocking=True)
+                result_readback(j)
         stream.synchronize()
+        copy_stream.synchronize()
 
+    run_steps_plain = run_steps
+
+    def checked(first: int, count: int, e2e: bool) -> None:
+        try:
+            run_steps_plain(first, count, e2e)
+        except Exception:
+            print(json.dumps({"failed_in": "e2e" if e2e else "device-timed",
+                              "controllers": store.runtime.controller_stats()}), file=sys.stderr)
+            raise
+
+    run_steps = checked  # noqa: F811 - failures report the drives' counters
     run_steps(0, args.warmup, False)
     barrier(world)
     sampler = ClockSampler(list(range(world))).start() if rank == 0 else None  # every GPU of the job
@@ -530,6 +616,7 @@ def main():
     total_bytes = sum_over_ranks(world, float(bytes_per_step))
     timing = store.runtime.io_timing() if store.runtime and args.timing else {}
     stats = store.runtime.controller_stats() if store.runtime else []
+    staging_where = "hbm" if store.runtime and store.runtime.staging_on_device() else "host"
     if args.timing and rank == 0:
         print(json.dumps({"io_timing": timing, "controllers": stats}), file=sys.stderr)
     store.close()
@@ -539,11 +626,16 @@ def main():
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None if BASELINE_GBPS is None else round(value / BASELINE_GBPS, 3),
-            "dtype": "bf16", "data": "synthetic (randn KV of the named shape; emulated NVMe over page-cached segment files)",
+            "dtype": "bf16",
+            "data": ("synthetic (randn KV of the named shape; emulated NVMe drives with in-memory media, "
+                     "copy-engine DMA into HBM staging)" if memory else
+                     "synthetic (randn KV of the named shape; emulated NVMe over page-cached segment files)"),
             "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world,
                        "seq_len": args.prefix_tokens, "parallelism": f"dp{world} (one prefix per rank)",
                        "pool_blocks": args.pool_blocks, "drives_per_rank": args.drives,
-                       "backing": "O_DIRECT" if args.direct_io else "page cache",
+                       "backing": "O_DIRECT" if args.direct_io else "page cache", "media": args.media,
+                       "staging": staging_where,
+                       "drive_gbps_cap": args.drive_gbps or None, "ctas": ctas, "slots": args.slots,
                        "controller_threads": threads, "impl": args.impl, "inflight": args.inflight,
                        "emulator_reads": args.emulator_reads, "staging_write_combined": bool(args.staging_wc),
                        "emulator_idle_spins": idle_spins,
@@ -554,16 +646,20 @@ def main():
                     "h2d_bytes_per_step": nblk * 8 + io_bytes[0] // args.steps,
                     "d2h_bytes_per_step": 4 + io_bytes[1] // args.steps},
             "gpu_launches": n_launch,
-            # The restore's roofline term on one GPU is the PCIe read of the staging
-            # slots (a GPU zero-copy read of pinned host memory measured 51.4 GB/s on
-            # this pool); the emulated drives, which are host threads, usually bind first.
-            # The second term is the emulated drives' ceiling: the same bytes read on the
-            # host by the same threads with no GPU involved (measured before warm-up).
-            "roofline": {"term": "PCIe zero-copy read of staging slots", "per_gpu_gbps": ZERO_COPY_GBPS,
-                         "per_gpu_fraction": round(value / world / ZERO_COPY_GBPS, 3),
-                         "emulated_drive_gbps": round(drive_total, 3),
-                         "bound_gbps": round(min(ZERO_COPY_GBPS * world, drive_total or 1e9), 3),
-                         "fraction_of_bound": round(value / min(ZERO_COPY_GBPS * world, drive_total or 1e9), 3)},
+            # Roofline: the drives' transfers. Memory media: the copy engines' rate for the
+            # 1 MiB host->HBM copies every READ is served with (measured in this run, before
+            # warm-up, no protocol around it), times the ranks; capped by --drive-gbps x drives.
+            # File media: the GPU's zero-copy read of the host staging slots (51.4 GB/s on this
+            # pool) against the host-only read rate of the files by the same threads.
+            "roofline": ({"term": "copy-engine DMA of 1 MiB commands, page-locked host image -> HBM",
+                          "per_gpu_gbps": round(drive_gbps, 3), "bound_gbps": round(drive_total, 3),
+                          "fraction_of_bound": round(value / drive_total, 3) if drive_total else None}
+                         if memory else
+                         {"term": "PCIe zero-copy read of staging slots", "per_gpu_gbps": ZERO_COPY_GBPS,
+                          "per_gpu_fraction": round(value / world / ZERO_COPY_GBPS, 3),
+                          "emulated_drive_gbps": round(drive_total, 3),
+                          "bound_gbps": round(min(ZERO_COPY_GBPS * world, drive_total or 1e9), 3),
+                          "fraction_of_bound": round(value / min(ZERO_COPY_GBPS * world, drive_total or 1e9), 3)}),
             "verified": ok_all,
             "store_setup_s": round(store_s, 2),
             "clocks": clocks,

@@ -4,6 +4,12 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# Before CUDA starts: more hardware queues, so the emulated drives' copy streams
+# rarely share one with a stream whose work waits on an io kernel.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+# Eager kernel loading: a lazy load while an io kernel waits on the drives
+# would stall the drives' copy calls (a context-wide lock) until its deadline.
+os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 

@@ -20,8 +20,15 @@ pytestmark = pytest.mark.gpu
 G = KVGeometry("t-llama", num_layers=3, num_kv_heads=4, head_dim=128, chunk_tokens=64)
 
 
-def make(tmp_path, drives=1, **opts):
-    base = {"leases": 8, "max_ctas_per_op": 8, "timeout_ms": 2000}
+@pytest.fixture(params=["files", "memory"])
+def media(request):
+    """Emulated drive media: the backing files with page-locked host staging, or an
+    in-memory image that the drives DMA from (copy engines) into HBM staging."""
+    return request.param
+
+
+def make(tmp_path, drives=1, media="files", **opts):
+    base = {"leases": 8, "max_ctas_per_op": 8, "timeout_ms": 2000, "emulator_media": media}
     base.update(opts)
     st = TuttiKVStore(tmp_path, G, capacity_chunks=64, mounts=[str(tmp_path / f"nvme{d}") for d in range(drives)],
                       device=0, segment_file_slots=16, runtime_options=base)
@@ -29,9 +36,10 @@ def make(tmp_path, drives=1, **opts):
 
 
 @pytest.mark.parametrize("drives", [1, 4])
-def test_store_restore_roundtrip_random_blocks(tmp_path, drives):
-    st = make(tmp_path, drives=drives)
+def test_store_restore_roundtrip_random_blocks(tmp_path, drives, media):
+    st = make(tmp_path, drives=drives, media=media)
     try:
+        assert st.runtime.staging_on_device() == (media == "memory")
         nb = 512
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
         st.register_pool(pool)
@@ -48,12 +56,14 @@ def test_store_restore_roundtrip_random_blocks(tmp_path, drives):
         assert torch.equal(got, ref)
         stats = st.runtime.controller_stats()
         assert sum(s["read_bytes"] for s in stats) == n * G.chunk_bytes
+        if media == "memory":  # every command DMA'd by the copy engines, both directions
+            assert sum(s["dma_copies"] for s in stats) >= n * G.chunk_bytes // (1 << 20)
     finally:
         st.close()
 
 
-def test_layer_subset_restore(tmp_path):
-    st = make(tmp_path)
+def test_layer_subset_restore(tmp_path, media):
+    st = make(tmp_path, media=media)
     try:
         nb = 64
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
@@ -72,8 +82,8 @@ def test_layer_subset_restore(tmp_path):
         st.close()
 
 
-def test_media_error_reports_failed_requests(tmp_path):
-    st = make(tmp_path)
+def test_media_error_reports_failed_requests(tmp_path, media):
+    st = make(tmp_path, media=media)
     try:
         nb = 64
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
@@ -91,8 +101,8 @@ def test_media_error_reports_failed_requests(tmp_path):
         st.close()
 
 
-def test_lost_completion_times_out_and_queue_recovers(tmp_path):
-    st = make(tmp_path, timeout_ms=500)
+def test_lost_completion_times_out_and_queue_recovers(tmp_path, media):
+    st = make(tmp_path, timeout_ms=500, media=media)
     try:
         nb = 64
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
@@ -111,8 +121,8 @@ def test_lost_completion_times_out_and_queue_recovers(tmp_path):
         st.close()
 
 
-def test_enqueue_wait_orders_consumer_stream(tmp_path):
-    st = make(tmp_path)
+def test_enqueue_wait_orders_consumer_stream(tmp_path, media):
+    st = make(tmp_path, media=media)
     try:
         nb = 64
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
@@ -143,10 +153,11 @@ def _fp8_roundtrip_pages(pages: torch.Tensor) -> torch.Tensor:
 
 
 @pytest.mark.parametrize("drives", [1, 3])
-def test_fp8_stored_format_quantises_on_store_and_dequantises_on_restore(tmp_path, drives):
+def test_fp8_stored_format_quantises_on_store_and_dequantises_on_restore(tmp_path, drives, media):
     st = TuttiKVStore(tmp_path, G, capacity_chunks=64, mounts=[str(tmp_path / f"nvme{d}") for d in range(drives)],
                       device=0, segment_file_slots=16, stored_format="fp8_block128",
-                      runtime_options={"leases": 8, "max_ctas_per_op": 8, "timeout_ms": 2000})
+                      runtime_options={"leases": 8, "max_ctas_per_op": 8, "timeout_ms": 2000,
+                                       "emulator_media": media})
     st.open()
     try:
         nb = 256
@@ -184,12 +195,13 @@ def test_fp8_stored_format_quantises_on_store_and_dequantises_on_restore(tmp_pat
         st.close()
 
 
-def test_subsector_index_pages_pack_into_aligned_commands(tmp_path):
+def test_subsector_index_pages_pack_into_aligned_commands(tmp_path, media):
     # DeepSeek-V3.2-style index cache: 132 bytes per token, 8,448-byte pages (not a sector multiple)
     gi = KVGeometry("t-idx", num_layers=3, num_kv_heads=1, head_dim=132, block_size=64, planes=1,
                     dtype=torch.uint8, chunk_tokens=256)
     st = TuttiKVStore(tmp_path, gi, capacity_chunks=32, mounts=[str(tmp_path / f"nvme{d}") for d in range(2)],
-                      device=0, segment_file_slots=16, runtime_options={"leases": 8, "max_ctas_per_op": 8})
+                      device=0, segment_file_slots=16,
+                      runtime_options={"leases": 8, "max_ctas_per_op": 8, "emulator_media": media})
     st.open()
     try:
         nb = 64
@@ -209,10 +221,10 @@ def test_subsector_index_pages_pack_into_aligned_commands(tmp_path):
 
 
 @pytest.mark.parametrize("consumer_drain", [False, True])
-def test_split_completion_restores_exactly(tmp_path, consumer_drain):
+def test_split_completion_restores_exactly(tmp_path, consumer_drain, media):
     # submit-phase launch queues the reads and exits; the drain runs on the
     # consumer stream (enqueue_wait) or, without one, from the host fallback
-    st = make(tmp_path, drives=2, async_completion=True, slots_per_lease=8)
+    st = make(tmp_path, drives=2, async_completion=True, slots_per_lease=8, media=media)
     try:
         nb = 256
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
@@ -243,8 +255,8 @@ def test_split_completion_restores_exactly(tmp_path, consumer_drain):
         st.close()
 
 
-def test_split_completion_deadline_runs_from_submission(tmp_path):
-    st = make(tmp_path, async_completion=True, timeout_ms=500)
+def test_split_completion_deadline_runs_from_submission(tmp_path, media):
+    st = make(tmp_path, async_completion=True, timeout_ms=500, media=media)
     try:
         nb = 64
         pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")

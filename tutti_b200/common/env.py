@@ -12,6 +12,8 @@
 | ``TUTTI_DEFER_WRITES_AFTER_READS=0`` | writes on a stream of their own, free to overlap reads (on: writes queue behind reads) |
 | ``TUTTI_PRP_MODE=dynamic\\|full_prebuild`` | validated; both name the same thing here: NVMe commands address staging slots, whose PRP lists are built once at init whatever the KV pool's size |
 | ``TUTTI_REPLICA_NO_ACK=1`` | accepted; replica fan-out is push-based (the owner stores into each consumer's pool), so consumers never acknowledge and there is no ACK to skip |
+| ``TUTTI_EMULATOR_MEDIA=files`` or ``memory`` | media of the emulated drives: the backing files, or a page-locked image of them that the drives DMA from into HBM staging (files) |
+| ``TUTTI_DRIVE_GBPS=<x>`` | sustained transfer cap of each emulated drive in GB/s (none) |
 | ``TUTTI_NVME_PRESET=<yaml or path>`` | a runtime over a preset's drives (``storage.preset.runtime_from_env``) |
 | ``TUTTI_GREEN_CTX_IO_SMS``, ``TUTTI_NVTX``, ``TUTTI_METRICS_PORT``, ``TUTTI_HEALTH_INTERVAL_S``, ``TUTTI_VERBOSE`` | see their modules |
 Parity: reference doc/configuration-and-performance.md:117-157 (the same names).
@@ -63,4 +65,12 @@ def runtime_option_defaults() -> dict:
     workers = integer("TUTTI_POOL_WORKERS")
     if workers:
         out["max_ctas_per_op"] = workers
+    media = text("TUTTI_EMULATOR_MEDIA")
+    if media:
+        if media not in ("files", "memory"):
+            raise ValueError("TUTTI_EMULATOR_MEDIA must be 'files' or 'memory'")
+        out["emulator_media"] = media
+    gbps = number("TUTTI_DRIVE_GBPS")
+    if gbps:
+        out["drive_gbps"] = gbps
     return out

@@ -184,17 +184,47 @@ Status GpuNvmeDataPath::initialize(const DataPathConfig&, ResourceProvider*) {
 
 Status GpuNvmeDataPath::init_device_side() {
     const std::uint64_t nslots = std::uint64_t(cfg_.leases) * cfg_.slots_per_lease;
-    auto st = host_mapped_alloc(nslots * cfg_.slot_bytes, cfg_.staging_write_combined);
-    if (!st.ok()) return st.status();
-    staging_ = st.value();
+    bool all_dma = true;
+    for (auto& d : devs_) all_dma = all_dma && d.controller->info().device_dma;
+    if (cfg_.staging == GpuNvmeConfig::Staging::DEVICE && !all_dma)
+        return {StatusCode::UNSUPPORTED, "device staging needs controllers that DMA into GPU memory"};
+    staging_on_device_ = cfg_.staging == GpuNvmeConfig::Staging::DEVICE ||
+                         (cfg_.staging == GpuNvmeConfig::Staging::AUTO && all_dma);
+    if (staging_on_device_) {
+        // The drives' copies are CUDA work in this process, so two process-wide
+        // settings decide whether they can stall behind a running io kernel.
+        const char* loading = std::getenv("CUDA_MODULE_LOADING");
+        const char* conns = std::getenv("CUDA_DEVICE_MAX_CONNECTIONS");
+        if (!loading || std::strcmp(loading, "EAGER") != 0)
+            std::fprintf(stderr,
+                         "[tutti] nvme-gpu: drives DMA into HBM staging but CUDA_MODULE_LOADING is not EAGER: a kernel "
+                         "loaded lazily while a restore runs stalls the drives until the io deadline\n");
+        if (!conns || std::atoi(conns) < 16)
+            std::fprintf(stderr,
+                         "[tutti] nvme-gpu: drives DMA into HBM staging with CUDA_DEVICE_MAX_CONNECTIONS < 16: a copy "
+                         "that waits behind an io kernel can share a hardware queue with a drive's copies\n");
+    }
+    void* arena = nullptr;
+    std::uint64_t arena_bytes = nslots * cfg_.slot_bytes;
+    if (staging_on_device_) {
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&staging_hbm_, arena_bytes), "cudaMalloc staging"));
+        arena = staging_hbm_;
+    } else {
+        auto st = host_mapped_alloc(arena_bytes, cfg_.staging_write_combined);
+        if (!st.ok()) return st.status();
+        staging_ = st.value();
+        if (!staging_.device)
+            return {StatusCode::UNSUPPORTED, "nvme-gpu needs a CUDA device (device-mapped host memory)"};
+        arena = staging_.host;
+        arena_bytes = staging_.bytes;
+    }
     auto pr = host_mapped_alloc(nslots * nvme::kMemoryPageBytes);
     if (!pr.ok()) return pr.status();
     prp_ = pr.value();
-    if (!staging_.device || !prp_.device)
-        return {StatusCode::UNSUPPORTED, "nvme-gpu needs a CUDA device (device-mapped host memory)"};
+    if (!prp_.device) return {StatusCode::UNSUPPORTED, "nvme-gpu needs a CUDA device (device-mapped host memory)"};
     // Same bus address on every controller (identity IOMMU / pass-through).
     for (std::size_t d = 0; d < devs_.size(); ++d) {
-        auto a = devs_[d].controller->map_dma(staging_.host, staging_.bytes);
+        auto a = devs_[d].controller->map_dma(arena, arena_bytes);
         auto b = devs_[d].controller->map_dma(prp_.host, prp_.bytes);
         if (!a.ok()) return a.status();
         if (!b.ok()) return b.status();
@@ -240,11 +270,17 @@ Status GpuNvmeDataPath::init_device_side() {
     TUTTI_RETURN_IF_ERROR(cuda_status(
         cudaMemset(d_targets_, 0, std::size_t(cfg_.max_targets) * sizeof(io::DevTarget)), "memset targets"));
     for (std::uint32_t l = cfg_.leases; l-- > 0;) free_leases_.push_back(l);
+    for (std::uint32_t i = 0; i < cfg_.prealloc_arenas; ++i) {
+        auto a = take_arena(cfg_.prealloc_arena_bytes);
+        if (!a.ok()) return a.status();
+        return_arena(std::move(a).value());
+    }
     if (const char* v = std::getenv("TUTTI_VERBOSE"); v && *v && std::strcmp(v, "0") != 0)
         std::fprintf(stderr,
-                     "[tutti] nvme-gpu accel %d: %zu controller(s), %u leases x %u slots x %u KiB staging, "
+                     "[tutti] nvme-gpu accel %d: %zu controller(s), %u leases x %u slots x %u KiB %s staging, "
                      "commands up to %u KiB, LBA %u, timeout %.1f s\n",
                      cfg_.accel_id, devs_.size(), cfg_.leases, cfg_.slots_per_lease, cfg_.slot_bytes >> 10,
+                     staging_on_device_ ? "HBM" : "host",
                      cmd_bytes_ >> 10, lba_, cfg_.timeout_ns / 1e9);
     return Status::Ok();
 }
@@ -278,11 +314,13 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
     d_devices_ = nullptr;
     d_targets_ = nullptr;
     for (auto& d : devs_) {
-        if (staging_.host) d.controller->unmap_dma(staging_iova_);
+        if (staging_.host || staging_hbm_) d.controller->unmap_dma(staging_iova_);
         if (prp_.host) d.controller->unmap_dma(prp_iova_);
     }
     host_mapped_free(staging_);
     host_mapped_free(prp_);
+    if (staging_hbm_) cudaFree(staging_hbm_);
+    staging_hbm_ = nullptr;
     initialized_ = false;
     return Status::Ok();
 }
@@ -444,9 +482,15 @@ Result<std::unique_ptr<GpuNvmeDataPath::Arena>> GpuNvmeDataPath::take_arena(std:
     }
     auto a = std::make_unique<Arena>();
     a->capacity = align_up(std::max<std::size_t>(bytes, 1u << 20), 1u << 20);
-    Status s = cuda_status(cudaHostAlloc(reinterpret_cast<void**>(&a->host), a->capacity, cudaHostAllocDefault),
+    Status s = cuda_status(cudaHostAlloc(reinterpret_cast<void**>(&a->host), a->capacity, cudaHostAllocMapped),
                            "cudaHostAlloc arena");
     if (!s.ok()) return R::Failure(s);
+    s = cuda_status(cudaHostGetDevicePointer(reinterpret_cast<void**>(&a->host_dev), a->host, 0),
+                    "cudaHostGetDevicePointer arena");
+    if (!s.ok()) {
+        cudaFreeHost(a->host);
+        return R::Failure(s);
+    }
     s = cuda_status(cudaMalloc(&a->dev, a->capacity), "cudaMalloc arena");
     if (!s.ok()) {
         cudaFreeHost(a->host);
@@ -648,6 +692,11 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     }
     std::memcpy(h + off_leases, op->leases.data(), take * sizeof(std::uint32_t));
     std::memset(h + off_cursor, 0, 16);
+    // Status words and timing stamps live in the mapped host half of the arena:
+    // the kernel stores them over PCIe, so no copy is ever queued behind it (a
+    // copy waiting on a running io kernel would also hold up any drive DMA that
+    // shares its hardware queue).
+    if (timing) std::memset(h + off_timing, 0, copy_end - off_timing);
     auto* hst = reinterpret_cast<std::uint32_t*>(h + off_status);
     for (std::uint32_t k = 0; k < n_cmds; ++k) hst[k] = io::kCmdNotRun;
 
@@ -658,17 +707,18 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     kp.n_cmds = n_cmds;
     kp.n_devices = static_cast<std::uint32_t>(devs_.size());
     kp.cursor = reinterpret_cast<std::uint32_t*>(d + off_cursor);
-    kp.cmd_status = reinterpret_cast<std::uint32_t*>(d + off_status);
+    kp.cmd_status = reinterpret_cast<std::uint32_t*>(arena->host_dev + off_status);
     kp.targets = d_targets_;
     kp.devices = d_devices_;
     kp.lease_ids = reinterpret_cast<const std::uint32_t*>(d + off_leases);
-    kp.staging_dev = static_cast<char*>(staging_.device);
+    kp.staging_dev = staging_base();
     kp.staging_iova = staging_iova_;
+    kp.movers = staging_on_device_ ? io::kMoversBulk : io::kMoversSimt;
     kp.prp_iova = prp_iova_;
     kp.slot_bytes = cfg_.slot_bytes;
     kp.slots_per_lease = cfg_.slots_per_lease;
     kp.timeout_ns = cfg_.timeout_ns;
-    kp.timing = timing ? reinterpret_cast<std::uint64_t*>(d + off_timing) : nullptr;
+    kp.timing = timing ? reinterpret_cast<std::uint64_t*>(arena->host_dev + off_timing) : nullptr;
     kp.carry = split ? reinterpret_cast<io::LeaseCarry*>(d + off_carry) : nullptr;
     kp.phase = split ? io::kPhaseSubmit : io::kPhaseFull;
 
@@ -680,7 +730,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
                       cmds[0].opcode == nvme::kOpRead ? "read" : "write", n_cmds, take, xform ? "|fp8" : "");
         nvtxRangePushA(name);
     }
-    Status cs = cuda_status(cudaMemcpyAsync(d, h, off_timing, cudaMemcpyHostToDevice, s), "H2D commands");
+    Status cs = cuda_status(cudaMemcpyAsync(d, h, off_status, cudaMemcpyHostToDevice, s), "H2D commands");
     bool launched = false;
     if (cs.ok()) {
         if (take_test_fault(TestFault::LAUNCH_FAILURE)) {
@@ -696,15 +746,9 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
             return Status{StatusCode::DEVICE_ERROR, "event record: injected failure"};
         return cuda_status(cudaEventRecord(ev, s), "event record");
     };
-    bool d2h_issued = false;
     if (split) {
         if (cs.ok()) cs = record(arena->submitted);
     } else {
-        if (cs.ok())
-            cs = cuda_status(
-                cudaMemcpyAsync(h + off_status, d + off_status, copy_end - off_status, cudaMemcpyDeviceToHost, s),
-                "D2H status");
-        d2h_issued = cs.ok();
         if (cs.ok()) cs = record(arena->event);
     }
     if (!cs.ok() && !launched) {
@@ -742,9 +786,6 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
             op->drain_pending = false;
             if (ws.ok()) ws = cuda_status(cudaStreamSynchronize(s), "stream synchronize");
         }
-        if (ws.ok() && (split || !d2h_issued))
-            ws = cuda_status(cudaMemcpy(h + off_status, d + off_status, copy_end - off_status, cudaMemcpyDeviceToHost),
-                             "D2H status");
         if (ws.ok()) {
             finish_op(*op);
         } else {
@@ -761,7 +802,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_coalesced).count();
     last_submit_profile_.commands = n_cmds;
     last_submit_profile_.requests = count;
-    last_submit_profile_.h2d_bytes = off_timing;
+    last_submit_profile_.h2d_bytes = off_status;
     last_submit_profile_.d2h_bytes = copy_end - off_status;
     const std::uint64_t tok = op->generation;
     ops_[tok] = std::move(op);
@@ -853,17 +894,11 @@ void GpuNvmeDataPath::finish_op(OpRec& op) {
 }
 
 Status GpuNvmeDataPath::launch_drain(OpRec& op, cudaStream_t stream) {
-    // Caller holds mu_. Orders the drain after the submit-phase kernel, then
-    // copies the statuses back and marks the op's completion event.
+    // Caller holds mu_. Orders the drain after the submit-phase kernel and marks
+    // the op's completion event (the kernel writes the statuses to host memory).
     DeviceGuard guard(cfg_.accel_id);
-    char* h = op.arena->host;
-    char* d = op.arena->dev;
     Status cs = cuda_status(cudaStreamWaitEvent(stream, op.arena->submitted, 0), "stream wait");
     if (cs.ok()) cs = cuda_status(io::launch_nvme_io(op.kp, op.ctas, stream), "drain launch");
-    if (cs.ok())
-        cs = cuda_status(cudaMemcpyAsync(h + op.status_off, d + op.status_off, op.copy_back_bytes,
-                                         cudaMemcpyDeviceToHost, stream),
-                         "D2H status");
     if (cs.ok()) cs = cuda_status(cudaEventRecord(op.arena->event, stream), "event record");
     op.drain_pending = false;
     return cs;
@@ -1024,8 +1059,9 @@ void GpuNvmeDataPath::noalloc_fill_params(io::IoKernelParams& p) const {
     p.n_devices = static_cast<std::uint32_t>(devs_.size());
     p.targets = d_targets_;
     p.devices = d_devices_;
-    p.staging_dev = static_cast<char*>(staging_.device);
+    p.staging_dev = staging_base();
     p.staging_iova = staging_iova_;
+    p.movers = staging_on_device_ ? io::kMoversBulk : io::kMoversSimt;
     p.prp_iova = prp_iova_;
     p.slot_bytes = cfg_.slot_bytes;
     p.slots_per_lease = cfg_.slots_per_lease;

@@ -54,6 +54,19 @@ struct GpuNvmeConfig {
     // GPU reads them without snoops); writes that the drive reads back are slower.
     bool staging_write_combined = false;
     std::uint32_t async_fallback_us = 1000;
+    // Where the staging slots live. DEVICE: in HBM; the drives DMA into them
+    // and the io kernel's bulk-copy movers scatter HBM -> HBM. HOST: page-
+    // locked host memory the movers read over PCIe (zero-copy). AUTO: DEVICE
+    // when every controller of the table can DMA into GPU memory.
+    enum class Staging : std::uint32_t { AUTO = 0, HOST = 1, DEVICE = 2 };
+    Staging staging = Staging::AUTO;
+    // Per-op arenas (command list, pieces, statuses) created at initialize.
+    // A submit that finds none large enough allocates one, and a page-locked
+    // or device allocation orders later CUDA work (the drives' copies among
+    // it) behind the kernels already running, so keep these sized for the
+    // largest op in flight: 8 MiB holds a 32k-token Llama-3.1-8B restore.
+    std::uint32_t prealloc_arenas = 4;
+    std::uint32_t prealloc_arena_bytes = 8u << 20;
 };
 
 // One row of the device table: a controller and the identity string the
@@ -102,6 +115,7 @@ public:
     // Telemetry of the last terminal op with timing enabled.
     IoTimingSummary last_timing() const;
     std::uint32_t free_leases() const;
+    bool staging_on_device() const { return staging_on_device_; }
     SubmitProfile last_submit_profile() const {
         std::lock_guard<std::mutex> g(mu_);
         return last_submit_profile_;
@@ -159,7 +173,8 @@ private:
     };
     struct Arena {
         std::size_t capacity = 0;    // bytes
-        char* host = nullptr;        // pinned
+        char* host = nullptr;        // page-locked, mapped: the status words are written here by the kernel
+        char* host_dev = nullptr;    // device address of `host`
         char* dev = nullptr;
         cudaEvent_t event = nullptr;      // after the (drain) kernel and the status copy-back
         cudaEvent_t submitted = nullptr;  // split completion: after the submit-phase kernel
@@ -215,8 +230,12 @@ private:
     std::size_t extent_chunk_used_ = 0;
     static constexpr std::size_t kExtentChunkBytes = 16u << 20;
 
-    // staging arena + PRP-list pages (host mapped), one per lease x slot
+    // staging arena + PRP-list pages (host mapped), one per lease x slot; with
+    // device staging the arena is staging_hbm_ (cudaMalloc) and staging_ is unused
     HostMappedBuffer staging_, prp_;
+    char* staging_hbm_ = nullptr;
+    bool staging_on_device_ = false;
+    char* staging_base() const { return staging_on_device_ ? staging_hbm_ : static_cast<char*>(staging_.device); }
     std::uint64_t staging_iova_ = 0, prp_iova_ = 0;
     std::uint32_t lba_ = 512;  // largest LBA size of the device table
 

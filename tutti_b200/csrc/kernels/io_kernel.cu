@@ -31,6 +31,7 @@
 #include <cuda_fp8.h>
 
 #include "io_kernel.h"
+#include "primitives.cuh"
 
 namespace tutti {
 namespace io {
@@ -40,9 +41,11 @@ namespace {
 enum SlotStateKind : int { S_FREE = 0, S_SUBMIT, S_INFLIGHT, S_READY, S_GATHER, S_POISON, S_MOVING };
 
 constexpr int kMoverGroups = 3;
-constexpr int kWarpsPerGroup = 5;
-constexpr int kGroupThreads = kWarpsPerGroup * 32;
-constexpr unsigned long long kMoverSpinLimit = 1ull << 31;
+// A mover that waits longer than the command deadline plus this margin for
+// the engine (which itself stops once nothing has moved for a deadline) gives
+// up and flags the launch.
+constexpr unsigned long long kMoverGraceNs = 2000000000ull;
+constexpr unsigned long long kEngineGraceNs = 500000000ull;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
@@ -106,11 +109,12 @@ __device__ __forceinline__ void fp8x16_dequant(uint4 q, float scale, uint4 out[2
 // handles 16 consecutive values, so 8 lanes share one 128-value scale group
 // (pieces hold a multiple of 512 values, so every lane of the warp takes part
 // in every iteration and the shuffles are full-warp).
+template <int W>
 __device__ void move_slot_fp8(const IoKernelParams& p, const IoCommand& c, char* stage, bool to_memory, int gwarp,
                               int lane) {
     const IoPiece* pcs = p.pieces + c.first_piece;
     const std::uint32_t groups = (to_memory && c.replicas > 1) ? c.replicas : 1u;
-    for (std::uint32_t q = gwarp; q < c.n_pieces; q += kWarpsPerGroup) {
+    for (std::uint32_t q = gwarp; q < c.n_pieces; q += W) {
         const IoPiece pc = pcs[q];
         const std::uint32_t k = pc.bytes / 33u;  // memory bytes / 64
         const std::uint32_t units = 2u * k;      // 16-value units
@@ -237,15 +241,16 @@ __device__ int resolve_cmd(const IoKernelParams& p, const IoCommand& c, SubCmd* 
 }
 
 // One mover group moves one slot: warps take 4 KiB chunks of the command.
+template <int W>
 __device__ void move_slot(const IoKernelParams& p, const IoCommand& c, char* stage, bool to_memory, int gwarp,
                           int lane) {
     if (c.transform == kXformFp8Block128) {
-        move_slot_fp8(p, c, stage, to_memory, gwarp, lane);
+        move_slot_fp8<W>(p, c, stage, to_memory, gwarp, lane);
         return;
     }
     const IoPiece* pcs = p.pieces + c.first_piece;
     const std::uint32_t nchunks = (c.bytes + 4095u) >> 12;
-    for (std::uint32_t ch = gwarp; ch < nchunks; ch += kWarpsPerGroup) {
+    for (std::uint32_t ch = gwarp; ch < nchunks; ch += W) {
         const std::uint32_t co = ch << 12;
         const std::uint32_t ce = min(co + 4096u, c.bytes);
         int lo = 0, hi = static_cast<int>(c.n_pieces) - 1, pi = 0;
@@ -310,6 +315,95 @@ __device__ void move_slot(const IoKernelParams& p, const IoCommand& c, char* sta
     }
 }
 
+// Bulk-copy mover (HBM staging): lane 0 of the group's warp streams the slot
+// through a ring of kBulkStages shared-memory chunks: cp.async.bulk
+// global->shared completing on the stage's mbarrier, then one
+// cp.async.bulk shared->global per destination (replica groups store the
+// same chunk to every rank's pool). `phase_bits` carries the mbarrier phases
+// from slot to slot. Every wait is bounded by a %globaltimer deadline; on
+// expiry the function drains its own copies in flight and returns false.
+__device__ bool move_slot_bulk(const IoKernelParams& p, const IoCommand& c, char* stage, bool to_memory,
+                               unsigned char* ring, std::uint64_t* bars, std::uint32_t& phase_bits) {
+    const IoPiece* pcs = p.pieces + c.first_piece;
+    const std::uint32_t groups = (to_memory && c.replicas > 1) ? c.replicas : 1u;
+    const unsigned long long deadline = dev::globaltimer_ns() + p.timeout_ns + kMoverGraceNs;
+    // chunk cursor over (piece, offset within piece)
+    std::uint32_t load_q = 0, load_off = 0;
+    std::uint32_t q_of[kBulkStages], off_of[kBulkStages], bytes_of[kBulkStages];
+    auto next_chunk = [&](std::uint32_t& q, std::uint32_t& off, std::uint32_t& bytes) -> bool {
+        while (load_q < c.n_pieces) {
+            const std::uint32_t pb = pcs[load_q].bytes;
+            if (load_off < pb) {
+                q = load_q;
+                off = load_off;
+                bytes = min(kBulkChunk, pb - load_off);
+                load_off += bytes;
+                return true;
+            }
+            ++load_q;
+            load_off = 0;
+        }
+        return false;
+    };
+    auto issue_load = [&](std::uint32_t st, std::uint32_t q, std::uint32_t off, std::uint32_t bytes) {
+        const IoPiece& pc = pcs[q];
+        const char* src = to_memory ? stage + pc.off + off : reinterpret_cast<const char*>(pc.mem) + off;
+        dev::mbar_arrive_expect_tx(&bars[st], bytes);
+        dev::bulk_g2s(ring + st * kBulkChunk, src, bytes, &bars[st]);
+        q_of[st] = q;
+        off_of[st] = off;
+        bytes_of[st] = bytes;
+    };
+    std::uint32_t in_flight = 0, head = 0, tail = 0;
+    while (in_flight < kBulkStages) {
+        std::uint32_t q, off, bytes;
+        if (!next_chunk(q, off, bytes)) break;
+        issue_load(tail, q, off, bytes);
+        tail = (tail + 1) % kBulkStages;
+        ++in_flight;
+    }
+    bool ok = true;
+    while (in_flight > 0) {
+        const std::uint32_t ph = (phase_bits >> head) & 1u;
+        while (!dev::mbar_try_wait(&bars[head], ph)) {
+            if (dev::globaltimer_ns() > deadline) {
+                ok = false;
+                break;
+            }
+        }
+        if (!ok) break;
+        phase_bits ^= 1u << head;
+        const IoPiece& pc = pcs[q_of[head]];
+        for (std::uint32_t g = 0; g < groups; ++g) {
+            char* dst = to_memory ? reinterpret_cast<char*>(pcs[g * c.n_pieces + q_of[head]].mem) + off_of[head]
+                                  : stage + pc.off + off_of[head];
+            dev::bulk_s2g(dst, ring + head * kBulkChunk, bytes_of[head]);
+        }
+        dev::bulk_commit();
+        --in_flight;
+        std::uint32_t q, off, bytes;
+        if (next_chunk(q, off, bytes)) {
+            dev::bulk_wait_read<0>();  // the stage is refilled once its stores have read it
+            issue_load(head, q, off, bytes);
+            ++in_flight;
+        }
+        head = (head + 1) % kBulkStages;
+    }
+    if (!ok) {
+        // Loads still in flight complete on their barriers; wait for them (bounded)
+        // so no copy lands in shared memory after this CTA moves on.
+        for (std::uint32_t k = 0; k < in_flight; ++k) {
+            const std::uint32_t st = (head + k) % kBulkStages;
+            const unsigned long long t = dev::globaltimer_ns();
+            while (!dev::mbar_try_wait(&bars[st], (phase_bits >> st) & 1u) && dev::globaltimer_ns() - t < kMoverGraceNs) {
+            }
+            phase_bits ^= 1u << st;
+        }
+    }
+    dev::bulk_wait<0>();  // the stores are complete (visible) before the slot changes state
+    return ok;
+}
+
 struct Shared {
     volatile int state[kMaxSlots];
     int cmd[kMaxSlots];
@@ -324,6 +418,7 @@ struct Shared {
     volatile int done;
     volatile int group_slot[kMoverGroups];
     std::uint32_t error;
+    alignas(8) std::uint64_t bars[kMoverGroups][kBulkStages];  // bulk movers' ring barriers
 };
 
 __device__ void push_ready(Shared& sh, int s, int slots) {
@@ -509,8 +604,10 @@ __device__ void engine_loop(const IoKernelParams& p, Shared& sh, std::uint32_t l
             last_progress = t1;
         }
         if (exhausted && (!busy || only_poison)) break;
-        // Failsafe: nothing moved for 4 deadlines (e.g. movers wedged): stop.
-        if (t1 - last_progress > 4 * p.timeout_ns + 1000000000ull) {
+        // Failsafe: nothing moved for a whole deadline (every command in flight
+        // reaches its own deadline sooner, which counts as progress), e.g.
+        // movers wedged: stop.
+        if (t1 - last_progress > p.timeout_ns + kEngineGraceNs) {
             atomicOr(&sh.error, 1u);
             break;
         }
@@ -520,15 +617,17 @@ __device__ void engine_loop(const IoKernelParams& p, Shared& sh, std::uint32_t l
     __threadfence_block();
 }
 
+template <int W, bool BULK>
 __device__ void mover_loop(const IoKernelParams& p, Shared& sh, std::uint32_t lease, int S, int group, int gwarp,
-                           int lane) {
+                           int lane, unsigned char* ring) {
     const bool leader = gwarp == 0 && lane == 0;
     const int bar_id = 1 + group;
     const std::uint64_t lease_slot0 = static_cast<std::uint64_t>(lease) * p.slots_per_lease;
+    std::uint32_t phase_bits = 0;  // bulk ring barrier phases (leader lane)
     for (;;) {
         if (leader) {
             int got = -1;
-            unsigned long long spins = 0;
+            const unsigned long long t0 = dev::globaltimer_ns();
             for (;;) {
                 const std::uint32_t h = *reinterpret_cast<volatile std::uint32_t*>(&sh.rq_claim);
                 if (h != sh.rq_tail) {
@@ -539,8 +638,8 @@ __device__ void mover_loop(const IoKernelParams& p, Shared& sh, std::uint32_t le
                     continue;
                 }
                 if (sh.done) break;
-                if (++spins > kMoverSpinLimit) {
-                    atomicOr(&sh.error, 2u);
+                if (dev::globaltimer_ns() - t0 > p.timeout_ns + kMoverGraceNs) {
+                    atomicOr(&sh.error, 2u);  // the engine went quiet past its own failsafe
                     break;
                 }
                 __nanosleep(128);
@@ -549,20 +648,30 @@ __device__ void mover_loop(const IoKernelParams& p, Shared& sh, std::uint32_t le
             __threadfence_block();
         }
         __syncwarp();
-        named_barrier(bar_id, kGroupThreads);
+        if (W > 1) named_barrier(bar_id, W * 32);
         const int s = sh.group_slot[group];
         if (s < 0) break;
         const int ci = sh.cmd[s];
         const bool to_memory = sh.state[s] == S_READY;
         char* stage = p.staging_dev + (lease_slot0 + s) * static_cast<std::uint64_t>(p.slot_bytes);
-        move_slot(p, p.cmds[ci], stage, to_memory, gwarp, lane);
+        const IoCommand c = p.cmds[ci];
+        bool moved = true;
+        if (BULK && c.transform == kXformNone) {
+            if (lane == 0) moved = move_slot_bulk(p, c, stage, to_memory, ring, sh.bars[group], phase_bits);
+        } else {
+            move_slot<W>(p, c, stage, to_memory, gwarp, lane);
+        }
         if (!to_memory) __threadfence_system();  // gathered bytes visible to the controller
         __syncwarp();
-        named_barrier(bar_id, kGroupThreads);
+        if (W > 1) named_barrier(bar_id, W * 32);
         if (leader) {
-            if (to_memory) {
+            if (!moved) {
+                atomicOr(&sh.error, 4u);
+                p.cmd_status[ci] = kCmdTimeout;
+                sh.state[s] = S_FREE;
+            } else if (to_memory) {
                 p.cmd_status[ci] = kCmdOk;
-                if (p.timing) p.timing[4ull * ci + 3] = globaltimer_ns();
+                if (p.timing) p.timing[4ull * ci + 3] = dev::globaltimer_ns();
                 sh.state[s] = S_FREE;
             } else {
                 sh.state[s] = S_SUBMIT;
@@ -574,8 +683,10 @@ __device__ void mover_loop(const IoKernelParams& p, Shared& sh, std::uint32_t le
 
 }  // namespace
 
-__global__ void __launch_bounds__(kIoThreads, 1) nvme_io_kernel(const IoKernelParams p) {
+template <int W, bool BULK>
+__global__ void __launch_bounds__(32 * (1 + kMoverGroups * W), 1) nvme_io_kernel(const IoKernelParams p) {
     __shared__ Shared sh;
+    extern __shared__ __align__(128) unsigned char bulk_ring[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const std::uint32_t lease = p.lease_ids[blockIdx.x];
     const int S = static_cast<int>(p.slots_per_lease);
@@ -593,6 +704,11 @@ __global__ void __launch_bounds__(kIoThreads, 1) nvme_io_kernel(const IoKernelPa
         sh.rq_claim = 0;
         sh.done = 0;
         sh.error = 0;
+        if (BULK) {
+            for (int g = 0; g < kMoverGroups; ++g)
+                for (std::uint32_t k = 0; k < kBulkStages; ++k) dev::mbar_init(&sh.bars[g][k], 1);
+            dev::fence_barrier_init();
+        }
     }
     if (tid == 0 && p.phase == kPhaseDrain) {
         const LeaseCarry& k = p.carry[blockIdx.x];
@@ -632,9 +748,10 @@ __global__ void __launch_bounds__(kIoThreads, 1) nvme_io_kernel(const IoKernelPa
     if (warp == 0) {
         if (lane == 0) engine_loop(p, sh, lease, S);
     } else {
-        const int group = (warp - 1) / kWarpsPerGroup;
-        const int gwarp = (warp - 1) % kWarpsPerGroup;
-        mover_loop(p, sh, lease, S, group, gwarp, lane);
+        const int group = (warp - 1) / W;
+        const int gwarp = (warp - 1) % W;
+        mover_loop<W, BULK>(p, sh, lease, S, group, gwarp, lane,
+                            BULK ? bulk_ring + group * kBulkStages * kBulkChunk : nullptr);
     }
     __syncwarp();
     __syncthreads();
@@ -655,7 +772,16 @@ __global__ void __launch_bounds__(kIoThreads, 1) nvme_io_kernel(const IoKernelPa
 cudaError_t launch_nvme_io(const IoKernelParams& p, std::uint32_t n_leases, cudaStream_t stream) {
     if (n_leases == 0 || p.n_cmds == 0) return cudaSuccess;
     if (p.phase != kPhaseFull && !p.carry) return cudaErrorInvalidValue;
-    nvme_io_kernel<<<n_leases, p.phase == kPhaseSubmit ? 32 : kIoThreads, 0, stream>>>(p);
+    const bool submit_only = p.phase == kPhaseSubmit;
+    if (p.movers == kMoversBulk) {
+        static const cudaError_t attr = cudaFuncSetAttribute(
+            nvme_io_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmemBytes));
+        if (attr != cudaSuccess) return attr;
+        nvme_io_kernel<1, true><<<n_leases, submit_only ? 32 : kIoThreadsBulk, submit_only ? 0 : kBulkSmemBytes,
+                                  stream>>>(p);
+    } else {
+        nvme_io_kernel<5, false><<<n_leases, submit_only ? 32 : kIoThreads, 0, stream>>>(p);
+    }
     return cudaGetLastError();
 }
 

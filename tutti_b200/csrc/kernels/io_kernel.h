@@ -28,7 +28,19 @@ namespace io {
 constexpr int kMaxSlots = 16;     // staging slots per CTA
 constexpr int kMaxSub = 8;        // NVMe commands per staging slot (extent/MDTS splits)
 constexpr int kMaxDevices = 8;    // devices (controllers) one launch can drive
-constexpr int kIoThreads = 512;   // threads per CTA
+constexpr int kIoThreads = 512;   // threads per CTA with SIMT movers (host-memory staging)
+constexpr int kIoThreadsBulk = 128;  // threads per CTA with bulk-copy movers (HBM staging)
+
+// How the movers copy a slot between staging and caller memory.
+//  kMoversSimt: 3 groups x 5 warps of 16-byte loads/stores; hides the latency
+//               of zero-copy reads of page-locked host staging over PCIe.
+//  kMoversBulk: 3 groups x 1 warp; lane 0 of each group streams the slot
+//               through a shared-memory ring with cp.async.bulk (TMA engine),
+//               for staging in HBM that the drive fills by DMA.
+enum MoverKind : std::uint32_t { kMoversSimt = 0, kMoversBulk = 1 };
+constexpr std::uint32_t kBulkStages = 4;
+constexpr std::uint32_t kBulkChunk = 8192;
+constexpr std::uint32_t kBulkSmemBytes = 3 * kBulkStages * kBulkChunk;  // dynamic smem of a bulk CTA
 
 // Stored-format transforms done by the movers while they move a slot.
 // kXformFp8Block128: memory holds bf16; each piece is stored as
@@ -136,6 +148,7 @@ struct IoKernelParams {
     std::uint64_t* timing;        // optional: 4 %globaltimer stamps per command
     LeaseCarry* carry;            // split completion: gridDim.x records (else unused)
     std::uint32_t phase;          // IoPhase
+    std::uint32_t movers;         // MoverKind (matches where the staging arena lives)
 };
 
 // Launches the fused io kernel on `stream` with one CTA per lease (one warp

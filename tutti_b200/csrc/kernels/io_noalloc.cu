@@ -169,6 +169,9 @@ extern "C" int tutti_nvme_io_noalloc(void* data_path, const tutti_noalloc_comman
         p.lease_ids = reinterpret_cast<const std::uint32_t*>(base + kOffLeases);
         e = tutti::io::launch_nvme_io(p, n_leases, stream);
     }
+    // Wait for the kernel before copying its statuses back: a copy queued behind
+    // a running io kernel could hold up drive DMA that shares its hardware queue.
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(cmd_status, base + kOffStatus, n_commands * sizeof(std::uint32_t), cudaMemcpyDeviceToHost,
                             stream);

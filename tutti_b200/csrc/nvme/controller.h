@@ -6,8 +6,15 @@
 // doorbell. Which "drive" answers is a provider:
 //   * EmulatedNvmeController: host threads own the rings (page-locked, mapped
 //     into the GPU), execute READ/WRITE/FLUSH against file-backed namespace
-//     ranges with pread/pwrite and post CQEs. Used where no user-owned NVMe
-//     queues exist (no queue-leasing kernel driver, no bindable drives).
+//     ranges and post CQEs. Its media is either the backing files themselves
+//     (pread/pwrite) or an in-memory image of them (page-locked host memory,
+//     loaded from the files on first touch, written through on WRITE). PRPs
+//     may name host memory or GPU memory: GPU destinations are filled by
+//     copy-engine DMA on the worker's own CUDA stream, and the CQE of such a
+//     command is written by that stream after the copy (the ordering a
+//     drive's posted writes give: data before completion). Used where no
+//     user-owned NVMe queues exist (no queue-leasing kernel driver, no
+//     bindable drives).
 //   * A real controller leased from the queue broker would expose the same
 //     QueuePairView with BAR0 doorbells; it needs a queue-owning kernel driver
 //     and is reported UNSUPPORTED when none is present.
@@ -53,6 +60,7 @@ struct ControllerInfo {
     std::uint32_t num_io_queues = 0;
     std::uint32_t nsid = 1;
     std::uint64_t namespace_bytes = 0;
+    bool device_dma = false;  // PRPs may name GPU memory (the controller DMAs into HBM)
 };
 
 // One backing range of an emulated namespace: namespace bytes
@@ -64,6 +72,12 @@ struct BackingRange {
 };
 
 struct ControllerStats {
+    std::uint64_t dma_copies = 0;  // copy-engine transfers issued for GPU-memory PRPs
+    std::uint64_t image_bytes = 0; // memory media: bytes of the image loaded so far
+    std::uint64_t load_ns = 0;     // time spent loading image chunks from the files
+    std::uint64_t file_ns = 0;     // time spent in pread/pwrite of the backing files
+    std::uint64_t sync_ns = 0;     // time spent waiting for the workers' own copies
+    std::uint64_t max_command_ns = 0;  // longest single command execution
     std::uint64_t commands = 0;
     std::uint64_t read_bytes = 0;
     std::uint64_t write_bytes = 0;
@@ -112,6 +126,26 @@ struct EmulatedControllerConfig {
     // Page-cached mode: serve READs by copying from a shared mapping of the
     // backing file instead of pread (measured no faster on the GPU boxes).
     bool map_reads = false;
+    // Media: the backing files (pread/pwrite) or an in-memory image of them.
+    // The image is one page-locked arena of `image_budget_bytes` (0: 1 GiB),
+    // allocated when the controller is created and handed out in
+    // `image_chunk_bytes` pieces, each loaded from its file on first touch;
+    // WRITEs update the image and are written through to the file before
+    // their CQE, so the files stay the durable copy. Ranges past the arena are
+    // served from the files. (Every CUDA allocation of the controller happens
+    // at creation: a page-locked allocation while an io kernel waits for this
+    // drive would order the drive's copies behind that kernel.)
+    enum class Media : std::uint32_t { FILES = 0, MEMORY = 1 };
+    Media media = Media::FILES;
+    std::uint64_t image_chunk_bytes = 64ull << 20;
+    std::uint64_t image_budget_bytes = 0;
+    // CUDA device whose memory PRPs may name (-1: the current device at create;
+    // ignored without CUDA). GPU destinations are DMA'd by the copy engines.
+    int cuda_device = -1;
+    // Sustained transfer rate of the emulated drive in GB/s (0: as fast as the
+    // host and the copy engines go). Commands start no earlier than the drive
+    // could have finished the bytes before them.
+    double max_gbps = 0.0;
 };
 
 class EmulatedNvmeController final : public NvmeController {
@@ -141,12 +175,22 @@ public:
 private:
     explicit EmulatedNvmeController(const EmulatedControllerConfig& cfg);
     Status start();
+    struct WorkerCtx;
+    struct Backing;
+    struct Seg {
+        char* p;
+        std::uint64_t n;
+        bool device;
+    };
     void worker_main(std::uint32_t worker);
-    bool service_queue(std::uint32_t q);
-    std::uint32_t execute(const Sqe& sqe, bool* drop_cqe);
-    bool collect_iov(std::uint64_t prp1, std::uint64_t prp2, std::uint64_t bytes,
-                     std::vector<std::pair<char*, std::uint64_t>>& iov) const;
-    bool dma_ok(std::uint64_t addr, std::uint64_t bytes) const;
+    bool service_queue(std::uint32_t q, WorkerCtx& w);
+    std::uint32_t execute(const Sqe& sqe, WorkerCtx& w, bool* drop_cqe, bool* on_stream);
+    std::uint32_t move_span(bool read, Backing* b, int fd, const char* map, std::uint64_t map_len,
+                            std::uint64_t foff, char* buf, std::uint64_t n, bool device, WorkerCtx& w);
+    bool collect_iov(std::uint64_t prp1, std::uint64_t prp2, std::uint64_t bytes, std::vector<Seg>& iov) const;
+    int window_kind(std::uint64_t addr, std::uint64_t bytes) const;  // -1 none, 0 host, 1 device
+    char* image_at(Backing* b, std::uint64_t foff, std::uint64_t* avail);
+    void pace(std::uint64_t bytes);
 
     struct QueueState {
         std::uint32_t sq_head = 0;
@@ -161,27 +205,42 @@ private:
         std::vector<BackingRange> ranges;
         const char* map = nullptr;  // page-cached mode only; unmapped at destruction
         std::uint64_t map_len = 0;
+        // memory media: one pointer per image chunk of the file (null until loaded)
+        std::uint64_t file_bytes = 0;
+        std::unique_ptr<std::atomic<char*>[]> chunks;
+        std::size_t n_chunks = 0;
+        std::mutex load_mu;
     };
     struct Window {
         std::uint64_t base;
         std::uint64_t bytes;
+        bool device;
     };
 
     EmulatedControllerConfig cfg_;
     ControllerInfo info_;
+    int cuda_device_ = -1;
     HostMappedBuffer sq_mem_, cq_mem_, bar_mem_;
     std::vector<std::unique_ptr<QueueState>> qstate_;
     std::vector<std::thread> workers_;
     std::atomic<bool> stop_{false};
 
     mutable std::mutex map_mu_;  // guards backings_ / windows_ (workers take it shared-ish: short)
-    std::vector<Backing> backings_;
+    std::vector<std::unique_ptr<Backing>> backings_;
     // flattened, sorted by ns_offset: (ns_offset, length, file_offset, fd)
     // map: a read-only shared mapping of the whole backing file (page-cached
     // mode), so READs copy straight from the page cache without a syscall.
-    struct Span { std::uint64_t ns, len, foff; int fd; const char* map; std::uint64_t map_len; };
+    struct Span { std::uint64_t ns, len, foff; int fd; const char* map; std::uint64_t map_len; Backing* b; };
     std::shared_ptr<const std::vector<Span>> spans_;
     std::shared_ptr<const std::vector<Window>> windows_;
+
+    std::atomic<std::uint64_t> image_bytes_{0};
+    char* image_arena_ = nullptr;
+    std::uint64_t image_arena_bytes_ = 0;
+    bool image_arena_pinned_ = false;
+    std::vector<char*> bounces_;  // one page-locked bounce buffer per worker (null without CUDA)
+    std::atomic<std::uint64_t> st_load_ns_{0}, st_file_ns_{0}, st_sync_ns_{0}, st_max_cmd_ns_{0};
+    std::atomic<std::uint64_t> pace_next_ns_{0};
 
     std::atomic<std::uint32_t> inject_kind_{0};
     std::atomic<std::uint32_t> inject_count_{0};
@@ -189,6 +248,7 @@ private:
     std::atomic<std::uint32_t> inject_status_{0};
 
     std::atomic<std::uint64_t> st_commands_{0}, st_read_{0}, st_write_{0}, st_errors_{0}, st_injected_{0};
+    std::atomic<std::uint64_t> st_dma_copies_{0};
 };
 
 }  // namespace nvme

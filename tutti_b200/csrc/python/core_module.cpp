@@ -457,6 +457,13 @@ PYBIND11_MODULE(_core, m) {
                      d["write_bytes"] = s.write_bytes;
                      d["errors"] = s.errors;
                      d["injected"] = s.injected;
+                     d["dma_copies"] = s.dma_copies;
+                     d["image_bytes"] = s.image_bytes;
+                     d["load_ms"] = s.load_ns / 1e6;
+                     d["file_ms"] = s.file_ns / 1e6;
+                     d["sync_ms"] = s.sync_ns / 1e6;
+                     d["max_command_ms"] = s.max_command_ns / 1e6;
+                     d["device_dma"] = c->info().device_dma;
                      out.append(d);
                  }
                  return out;
@@ -528,6 +535,8 @@ PYBIND11_MODULE(_core, m) {
                  d["total_us_p99"] = t.total_us_p99;
                  return d;
              })
+        .def("staging_on_device",
+             [](PyRuntime& r) { return r.extras.gpu_path ? r.extras.gpu_path->staging_on_device() : false; })
         .def("free_leases", [](PyRuntime& r) {
             return r.extras.gpu_path ? r.extras.gpu_path->free_leases() : 0u;
         })
@@ -557,6 +566,16 @@ PYBIND11_MODULE(_core, m) {
                 const std::string how = opts["emulator_reads"].cast<std::string>();
                 if (how != "mmap" && how != "pread") throw py::value_error("emulator_reads: mmap|pread");
                 o.map_reads = how == "mmap";
+            }
+            if (opts.contains("emulator_media")) o.media = opts["emulator_media"].cast<std::string>();
+            if (opts.contains("image_budget_bytes")) o.image_budget_bytes = opts["image_budget_bytes"].cast<std::uint64_t>();
+            if (opts.contains("drive_gbps")) o.drive_gbps = opts["drive_gbps"].cast<double>();
+            if (opts.contains("staging")) {
+                const std::string where = opts["staging"].cast<std::string>();
+                if (where == "auto") o.gpu.staging = GpuNvmeConfig::Staging::AUTO;
+                else if (where == "host") o.gpu.staging = GpuNvmeConfig::Staging::HOST;
+                else if (where == "device") o.gpu.staging = GpuNvmeConfig::Staging::DEVICE;
+                else throw py::value_error("staging: auto|host|device");
             }
             if (opts.contains("leases")) o.gpu.leases = opts["leases"].cast<std::uint32_t>();
             if (opts.contains("max_ctas_per_op")) o.gpu.max_ctas_per_op = opts["max_ctas_per_op"].cast<std::uint32_t>();

@@ -19,8 +19,15 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
         geo = g.value();
         ndev = geo.members.size();
     }
+    if (o.media != "files" && o.media != "memory")
+        return R::Failure({StatusCode::INVALID_ARGUMENT, "emulated media must be 'files' or 'memory'"});
     for (std::size_t i = 0; i < ndev; ++i) {
         nvme::EmulatedControllerConfig c;
+        c.media = o.media == "memory" ? nvme::EmulatedControllerConfig::Media::MEMORY
+                                      : nvme::EmulatedControllerConfig::Media::FILES;
+        c.image_budget_bytes = o.image_budget_bytes;
+        c.max_gbps = o.drive_gbps;
+        c.cuda_device = o.accel_id;
         c.name = "emu" + std::to_string(i);
         c.num_io_queues = o.queues ? o.queues : o.gpu.leases;
         c.queue_depth = o.queue_depth;
@@ -64,6 +71,12 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
     }
     GpuNvmeConfig g = o.gpu;
     g.accel_id = o.accel_id;
+    // Memory media DMA each command straight into HBM staging; file media keep
+    // page-locked host staging (their device DMA would go through a bounce).
+    if (g.staging == GpuNvmeConfig::Staging::AUTO)
+        g.staging = o.media == "memory" ? GpuNvmeConfig::Staging::DEVICE : GpuNvmeConfig::Staging::HOST;
+    if (g.staging == GpuNvmeConfig::Staging::DEVICE && !cuda_device_present())
+        g.staging = GpuNvmeConfig::Staging::HOST;
     auto path = std::make_shared<GpuNvmeDataPath>(g, devs);
     pr.extras.gpu_path = path;
     comps.data_paths.push_back({"nvme-gpu", path, DataPathConfig{"nvme-gpu"}});

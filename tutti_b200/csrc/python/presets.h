@@ -30,6 +30,11 @@ struct EmulatedPresetOptions {
     bool skip_data = false;  // diagnostic: controllers move no data
     bool map_reads = false;  // page-cached reads copy from a file mapping (default: pread)
     std::uint32_t idle_spin_iters = 2000;  // queue scans before an idle worker starts sleeping
+    // Emulated drives' media: "files" (pread/pwrite) or "memory" (a page-locked
+    // image of the backing files, loaded on first touch, written through).
+    std::string media = "files";
+    std::uint64_t image_budget_bytes = 0;  // 0: no limit
+    double drive_gbps = 0.0;               // per-drive transfer cap (0: none)
     std::string mapping = "auto";      // fiemap | synthetic | auto
     std::string raid0_md;              // non-empty: mounts[0] is an md RAID0 array
     std::string sysfs_root = "/sys";

@@ -8,6 +8,7 @@
 //
 //   tutti_native_tests [--filter substring]
 
+#include <fcntl.h>
 #include <unistd.h>
 
 #include <cstdio>
@@ -416,7 +417,8 @@ struct HostSubmitter {
     }
 };
 
-void controller_roundtrip(bool direct_io, bool map_reads = false) {
+void controller_roundtrip(bool direct_io, bool map_reads = false, bool memory_media = false,
+                          std::uint64_t image_budget = 0) {
     char path[] = "/tmp/tutti_emu_XXXXXX";
     const int fd = mkstemp(path);
     CHECK(fd >= 0);
@@ -432,6 +434,11 @@ void controller_roundtrip(bool direct_io, bool map_reads = false) {
     cfg.worker_threads = 1;
     cfg.direct_io = direct_io;
     cfg.map_reads = map_reads;
+    if (memory_media) {
+        cfg.media = nvme::EmulatedControllerConfig::Media::MEMORY;
+        cfg.image_chunk_bytes = 1u << 20;  // the 4 MiB file is four image chunks
+        cfg.image_budget_bytes = image_budget;
+    }
     auto ctl = nvme::EmulatedNvmeController::create(cfg);
     CHECK(ctl.ok());
     auto& c = *ctl.value();
@@ -474,6 +481,17 @@ void controller_roundtrip(bool direct_io, bool map_reads = false) {
     nvme::build_rw_sqe(e, nvme::kOpRead, 4, 1, ((1u << 20) + 12288) / lba, 8, iova.value(), 0);
     CHECK(hs.run(e) == 0);
     CHECK(b[0] == 0xA5 && b[4095] == 0xA5);
+    {  // a WRITE's CQE means the bytes are in the backing file (memory media write through)
+        unsigned char back[4096];
+        const int rfd = ::open(path, O_RDONLY);
+        CHECK(rfd >= 0 && ::pread(rfd, back, 4096, 12288) == 4096);
+        ::close(rfd);
+        CHECK(back[0] == 0xA5 && back[4095] == 0xA5);
+    }
+    if (memory_media) {
+        const auto st = c.stats();
+        CHECK(image_budget == 0 ? st.image_bytes >= (1u << 20) : st.image_bytes <= image_budget);
+    }
     // outside the backed namespace range, an unmapped buffer, an injected media error
     nvme::build_rw_sqe(e, nvme::kOpRead, 5, 1, 0, 8, iova.value(), 0);
     CHECK(hs.run(e) == nvme::make_status(0, nvme::kScLbaOutOfRange));
@@ -500,6 +518,10 @@ void controller_roundtrip(bool direct_io, bool map_reads = false) {
 TEST(emulated_controller_page_cached_reads_writes_and_errors) { controller_roundtrip(false); }
 TEST(emulated_controller_mapped_reads_writes_and_errors) { controller_roundtrip(false, true); }
 TEST(emulated_controller_direct_io_reads_writes_and_errors) { controller_roundtrip(true); }
+TEST(emulated_controller_memory_media_reads_writes_and_errors) { controller_roundtrip(false, false, true); }
+TEST(emulated_controller_memory_media_over_budget_serves_from_files) {
+    controller_roundtrip(false, false, true, 1u << 20);  // one chunk fits; the rest is read from the file
+}
 
 int main(int argc, char** argv) {
     const char* filter = nullptr;
