@@ -207,10 +207,12 @@ class ChunkIndex:
         """The ``count`` coldest evictable keys outside ``spare``; None (heap unchanged) if too few."""
         taken: list[tuple[int, bytes]] = []
         skipped: list[tuple[int, bytes]] = []
+        seen: set[bytes] = set()
         while len(taken) < count and self._victims:
             stamp, key = heapq.heappop(self._victims)
-            if not self._live_victim(stamp, key):
-                continue  # stale entry: dropped for good
+            if key in seen or not self._live_victim(stamp, key):
+                continue  # stale or duplicate entry (a record is offered again on unpin): dropped for good
+            seen.add(key)
             (skipped if key in spare else taken).append((stamp, key))
         for item in skipped:
             heapq.heappush(self._victims, item)
