@@ -57,6 +57,8 @@ def parse():
                    help="emulated drive media: in-memory image DMA'd into HBM, or the files (pread)")
     p.add_argument("--drive-gbps", type=float, default=0.0, help="per-drive transfer cap (0: none)")
     p.add_argument("--e2e-parts", default="h2d,readback", help=argparse.SUPPRESS)  # diagnostics
+    p.add_argument("--async-completion", action="store_true",
+                   help="split submit/drain: the drain starts once the drives have posted every CQE")
     p.add_argument("--inflight", type=int, default=2, help="restores submitted ahead")
     p.add_argument("--emulator-skip-data", action="store_true", help="diagnostic: controllers move no data")
     p.add_argument("--staging-wc", action="store_true", help="write-combined staging slots")
@@ -471,8 +473,8 @@ def main():
     ctas = args.ctas or (32 if memory else 96)
     opts = {"controller_threads": threads, "direct_io": bool(args.direct_io), "leases": args.leases,
             "emulator_media": args.media, "drive_gbps": args.drive_gbps,
-            "max_ctas_per_op": ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20,
-            "queue_depth": 256, "mdts_bytes": 1 << 20, "timing": bool(args.timing),
+            "async_completion": bool(args.async_completion), "async_fallback_us": 500000, "queue_depth": 1024,
+            "max_ctas_per_op": ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20, "mdts_bytes": 1 << 20, "timing": bool(args.timing),
             "emulator_skip_data": bool(args.emulator_skip_data), "emulator_reads": args.emulator_reads,
             "staging_write_combined": bool(args.staging_wc), "emulator_idle_spins": idle_spins}
     backend = "nvme-gpu" if args.impl == "tutti" else "posix"
@@ -637,6 +639,7 @@ def main():
                        "staging": staging_where,
                        "drive_gbps_cap": args.drive_gbps or None, "ctas": ctas, "slots": args.slots,
                        "controller_threads": threads, "impl": args.impl, "inflight": args.inflight,
+                       "async_completion": bool(args.async_completion),
                        "emulator_reads": args.emulator_reads, "staging_write_combined": bool(args.staging_wc),
                        "emulator_idle_spins": idle_spins,
                        "l2": "inputs (4.29 GB/step) larger than L2"},

@@ -51,6 +51,7 @@ OPS_SOURCES = [
     src("kernels", "paged_copy.cu"),
     src("kernels", "fp8_block.cu"),
     src("kernels", "blake2b.cu"),
+    src("kernels", "probe_kernels.cu"),
 ]
 
 ext_modules = [

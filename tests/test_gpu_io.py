@@ -349,3 +349,31 @@ def test_event_record_failure_on_a_split_read_settles_after_the_drain(tmp_path):
         assert torch.equal(pool[:, :, 8:16], ref)
     finally:
         st.close()
+
+
+def test_split_completion_of_an_op_larger_than_its_leased_slots(tmp_path, media):
+    # 2 CTAs x 2 slots hold 4 commands; the op has 12: the drain takes over the
+    # submitted ones and claims the rest itself
+    st = make(tmp_path, drives=2, async_completion=True, max_ctas_per_op=2, slots_per_lease=2, media=media)
+    try:
+        nb = 256
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        keys = chunk_keys_for_tokens(list(range(12 * 64)), 64, namespace=b"split-big")
+        rng = np.random.default_rng(5)
+        src = rng.permutation(nb)[:48].reshape(12, 4)
+        st.put_paged(keys, src).wait()
+        ref = pool[:, :, torch.from_numpy(src.reshape(-1)).cuda()].clone()
+        dst = rng.permutation(nb)[:48].reshape(12, 4)
+        pool.zero_()
+        comp = st.get_paged(keys, dst, stream=torch.cuda.Stream())
+        assert st.runtime.last_submit_profile()["commands"] > 4
+        consumer = torch.cuda.Stream()
+        comp.enqueue_wait(consumer)
+        with torch.cuda.stream(consumer):
+            out = pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()].clone()
+        consumer.synchronize()
+        comp.wait()
+        assert torch.equal(out, ref)
+    finally:
+        st.close()

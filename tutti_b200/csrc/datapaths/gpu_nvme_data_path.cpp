@@ -157,7 +157,7 @@ Status GpuNvmeDataPath::initialize(const DataPathConfig&, ResourceProvider*) {
     if (devs_.empty() || devs_.size() > io::kMaxDevices)
         return {StatusCode::INVALID_ARGUMENT, "device table must hold 1..8 controllers"};
     if (cfg_.slots_per_lease == 0 || cfg_.slots_per_lease > io::kMaxSlots)
-        return {StatusCode::INVALID_ARGUMENT, "slots_per_lease must be in [1, 16]"};
+        return {StatusCode::INVALID_ARGUMENT, "slots_per_lease must be in [1, 64]"};
     if (cfg_.slot_bytes < 4096 || cfg_.slot_bytes > (2u << 20) || cfg_.slot_bytes % 4096)
         return {StatusCode::INVALID_ARGUMENT, "slot_bytes must be a 4 KiB multiple <= 2 MiB"};
     if (cfg_.leases == 0) return {StatusCode::INVALID_ARGUMENT, "leases must be > 0"};
@@ -252,15 +252,17 @@ Status GpuNvmeDataPath::init_device_side() {
         TUTTI_RETURN_IF_ERROR(cuda_status(
             cudaMemcpy(dv, views.data(), views.size() * sizeof(views[0]), cudaMemcpyHostToDevice), "upload queues"));
         d_queue_views_.push_back(dv);
-        std::vector<io::QueueCursor> curs(cfg_.leases, io::QueueCursor{0, 0, 1, 0});
-        io::QueueCursor* dc = nullptr;
-        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&dc, curs.size() * sizeof(curs[0])), "cudaMalloc cursors"));
-        TUTTI_RETURN_IF_ERROR(cuda_status(
-            cudaMemcpy(dc, curs.data(), curs.size() * sizeof(curs[0]), cudaMemcpyHostToDevice), "upload cursors"));
-        d_cursors_.push_back(dc);
+        // Cursors live in mapped host memory: the kernel reads them when a CTA
+        // starts and writes them when it ends; the host reads them without a copy.
+        auto cm = host_mapped_alloc(std::size_t(cfg_.leases) * sizeof(io::QueueCursor));
+        if (!cm.ok()) return cm.status();
+        cursor_mem_.push_back(cm.value());
+        auto* hc = cursor_mem_.back().host_as<io::QueueCursor>();
+        for (std::uint32_t l = 0; l < cfg_.leases; ++l) hc[l] = io::QueueCursor{0, 0, 1, 0};
+        d_cursors_.push_back(cursor_mem_.back().device_as<io::QueueCursor>());
         std::uint32_t lba = ctl.info().lba_bytes, shift = 0;
         while ((1u << shift) < lba) ++shift;
-        rows[d] = io::DevDevice{dv, dc, shift, ctl.info().mdts_bytes, cfg_.leases, ctl.info().nsid};
+        rows[d] = io::DevDevice{dv, d_cursors_.back(), shift, ctl.info().mdts_bytes, cfg_.leases, ctl.info().nsid};
     }
     TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_devices_, rows.size() * sizeof(rows[0])), "cudaMalloc devices"));
     TUTTI_RETURN_IF_ERROR(cuda_status(
@@ -304,7 +306,8 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
     }
     arena_pool_.clear();
     for (auto* p : d_queue_views_) cudaFree(p);
-    for (auto* p : d_cursors_) cudaFree(p);
+    for (auto& m : cursor_mem_) host_mapped_free(m);
+    cursor_mem_.clear();
     for (auto* p : extent_chunks_) cudaFree(p);
     d_queue_views_.clear();
     d_cursors_.clear();
@@ -675,10 +678,12 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     const std::size_t off_timing = align_up(off_status + n_cmds * sizeof(std::uint32_t), 256);
     const bool timing = cfg_.timing;
     const std::size_t copy_end = off_timing + (timing ? n_cmds * 4 * sizeof(std::uint64_t) : 0);
-    // Split completion when every command is a read and the leased slots hold them all.
-    bool split = cfg_.async_completion && n_cmds <= std::uint64_t(take) * cfg_.slots_per_lease;
+    // Split completion for reads of any size: the submit launch fills every leased
+    // slot and exits; the drain takes those slots over and claims the rest of the
+    // op's commands itself, so the SMs are held only from the drain on.
+    bool split = cfg_.async_completion;
     for (std::size_t k = 0; split && k < cmds.size(); ++k) split = cmds[k].opcode == nvme::kOpRead;
-    const std::size_t off_carry = align_up(copy_end, 256);
+    const std::size_t off_carry = align_up(copy_end, 256);  // in the mapped host half (zero-copy)
     const std::size_t total = split ? off_carry + take * sizeof(io::LeaseCarry) : copy_end;
     auto ar = take_arena(total);
     if (!ar.ok()) return reject_all(ar.status());
@@ -719,7 +724,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     kp.slots_per_lease = cfg_.slots_per_lease;
     kp.timeout_ns = cfg_.timeout_ns;
     kp.timing = timing ? reinterpret_cast<std::uint64_t*>(arena->host_dev + off_timing) : nullptr;
-    kp.carry = split ? reinterpret_cast<io::LeaseCarry*>(d + off_carry) : nullptr;
+    kp.carry = split ? reinterpret_cast<io::LeaseCarry*>(arena->host_dev + off_carry) : nullptr;
     kp.phase = split ? io::kPhaseSubmit : io::kPhaseFull;
 
     cudaStream_t s = ctx.stream;
@@ -770,6 +775,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
         op->kp.phase = io::kPhaseDrain;
         op->ctas = take;
         op->copy_back_bytes = copy_end - off_status;
+        op->carry_off = off_carry;
         op->stream = s;
         op->submitted_at = std::chrono::steady_clock::now();
     }
@@ -812,19 +818,42 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
 }
 
 Status GpuNvmeDataPath::reset_dirty_queues(const std::vector<std::uint32_t>& leases) {
+    // Caller holds mu_; the op is terminal, so its kernels have written the cursors.
     for (std::size_t d = 0; d < devs_.size(); ++d) {
+        auto* cur = cursor_mem_[d].host_as<io::QueueCursor>();
         for (auto l : leases) {
-            io::QueueCursor c{};
-            TUTTI_RETURN_IF_ERROR(
-                cuda_status(cudaMemcpy(&c, d_cursors_[d] + l, sizeof(c), cudaMemcpyDeviceToHost), "read cursor"));
-            if (!c.dirty) continue;
+            if (!reinterpret_cast<volatile io::QueueCursor*>(cur)[l].dirty) continue;
             TUTTI_RETURN_IF_ERROR(devs_[d].controller->reset_queue(l));
-            io::QueueCursor fresh{0, 0, 1, 0};
-            TUTTI_RETURN_IF_ERROR(
-                cuda_status(cudaMemcpy(d_cursors_[d] + l, &fresh, sizeof(fresh), cudaMemcpyHostToDevice), "reset cursor"));
+            cur[l] = io::QueueCursor{0, 0, 1, 0};
         }
     }
     return Status::Ok();
+}
+
+bool GpuNvmeDataPath::split_data_ready(const OpRec& op) const {
+    const cudaError_t e = cudaEventQuery(op.arena->submitted);
+    if (e != cudaSuccess) {
+        if (e != cudaErrorNotReady) cudaGetLastError();
+        return false;
+    }
+    const auto* carry = reinterpret_cast<const volatile io::LeaseCarry*>(op.arena->host + op.carry_off);
+    for (std::size_t i = 0; i < op.leases.size(); ++i) {
+        const std::uint32_t l = op.leases[i];
+        for (std::size_t d = 0; d < devs_.size(); ++d) {
+            const std::uint32_t n = carry[i].inflight_dev[d];
+            if (n == 0) continue;
+            const auto* cur = reinterpret_cast<const volatile io::QueueCursor*>(cursor_mem_[d].host) + l;
+            const std::uint32_t head = cur->cq_head, phase = cur->phase;
+            const nvme::QueuePairView q = devs_[d].controller->host_queue(l);
+            for (std::uint32_t k = 0; k < n; ++k) {
+                const std::uint32_t at = head + k;
+                const std::uint32_t want = (at >= q.depth) ? (phase ^ 1u) : phase;
+                const std::uint32_t dw3 = __atomic_load_n(&q.cq[at % q.depth].dw3, __ATOMIC_ACQUIRE);
+                if (nvme::cqe_phase(dw3) != want) return false;
+            }
+        }
+    }
+    return true;
 }
 
 void GpuNvmeDataPath::finish_op(OpRec& op) {
@@ -917,9 +946,10 @@ Result<ProgressResult> GpuNvmeDataPath::progress(ProgressBudget budget) {
         }
         ++pr.work_units_consumed;
         if (op.drain_pending) {
-            // Nobody enqueued the drain on a consumer stream in time: launch it here.
+            // No consumer has asked for the data yet: launch the drain here once the
+            // drives have completed the submitted wave, or after async_fallback_us.
             const auto waited = std::chrono::steady_clock::now() - op.submitted_at;
-            if (waited >= std::chrono::microseconds(cfg_.async_fallback_us)) {
+            if (split_data_ready(op) || waited >= std::chrono::microseconds(cfg_.async_fallback_us)) {
                 Status ds = launch_drain(op, op.stream);
                 if (!ds.ok()) {
                     op.state = IoState::FAILED;
@@ -1022,16 +1052,10 @@ void GpuNvmeDataPath::noalloc_release_leases(const std::uint32_t* leases, std::u
         const std::uint32_t l = leases[i];
         if (reset_dirty) {
             for (std::size_t d = 0; d < devs_.size(); ++d) {
-                io::QueueCursor c{};
-                if (cudaMemcpy(&c, d_cursors_[d] + l, sizeof(c), cudaMemcpyDeviceToHost) != cudaSuccess) {
-                    cudaGetLastError();
-                    continue;
-                }
-                if (!c.dirty) continue;
+                auto* cur = cursor_mem_[d].host_as<io::QueueCursor>();
+                if (!reinterpret_cast<volatile io::QueueCursor*>(cur)[l].dirty) continue;
                 if (!devs_[d].controller->reset_queue(l).ok()) continue;
-                const io::QueueCursor fresh{0, 0, 1, 0};
-                if (cudaMemcpy(d_cursors_[d] + l, &fresh, sizeof(fresh), cudaMemcpyHostToDevice) != cudaSuccess)
-                    cudaGetLastError();
+                cur[l] = io::QueueCursor{0, 0, 1, 0};
             }
         }
         // The vector held every lease at initialize, so its capacity covers this push: no reallocation.

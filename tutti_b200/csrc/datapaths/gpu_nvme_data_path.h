@@ -38,7 +38,7 @@ struct GpuNvmeConfig {
     std::int32_t accel_id = 0;
     std::uint32_t leases = 64;            // queue pairs used per device (CTAs available)
     std::uint32_t max_ctas_per_op = 64;   // leases one submit may take
-    std::uint32_t slots_per_lease = 4;    // staging slots per CTA (<= 16)
+    std::uint32_t slots_per_lease = 4;    // staging slots per CTA (<= 64; x 8 below the queue depth)
     std::uint32_t slot_bytes = 1u << 20;  // <= 2 MiB
     std::uint64_t timeout_ns = 5ull * 1000 * 1000 * 1000;
     std::uint32_t max_targets = 1u << 20;
@@ -53,6 +53,9 @@ struct GpuNvmeConfig {
     // Staging slots in write-combined host memory (drives stream into them, the
     // GPU reads them without snoops); writes that the drive reads back are slower.
     bool staging_write_combined = false;
+    // A split read's drain is launched by progress() once the drives have posted
+    // every CQE of the submitted wave (its data is in place), or after this
+    // long, whichever comes first; enqueue_wait() launches it at once.
     std::uint32_t async_fallback_us = 1000;
     // Where the staging slots live. DEVICE: in HBM; the drives DMA into them
     // and the io kernel's bulk-copy movers scatter HBM -> HBM. HOST: page-
@@ -201,6 +204,7 @@ private:
         io::IoKernelParams kp{};
         std::uint32_t ctas = 0;
         std::size_t copy_back_bytes = 0;
+        std::size_t carry_off = 0;  // split completion: hand-over records in the mapped host half
         cudaStream_t stream = nullptr;
         std::chrono::steady_clock::time_point submitted_at{};
     };
@@ -213,6 +217,9 @@ private:
     void return_arena(std::unique_ptr<Arena> a);
     void finish_op(OpRec& op);
     Status launch_drain(OpRec& op, cudaStream_t stream);
+    // Split completion: the submit launch has finished and every CQE it waits
+    // for has been posted (read from the host-resident CQs and cursors).
+    bool split_data_ready(const OpRec& op) const;
     Status reset_dirty_queues(const std::vector<std::uint32_t>& leases);
 
     GpuNvmeConfig cfg_;
@@ -225,7 +232,8 @@ private:
     io::DevTarget* d_targets_ = nullptr;
     io::DevDevice* d_devices_ = nullptr;
     std::vector<nvme::QueuePairView*> d_queue_views_;
-    std::vector<io::QueueCursor*> d_cursors_;
+    std::vector<io::QueueCursor*> d_cursors_;   // device addresses of cursor_mem_
+    std::vector<HostMappedBuffer> cursor_mem_;  // per device: one cursor per lease, in mapped host memory
     std::vector<char*> extent_chunks_;
     std::size_t extent_chunk_used_ = 0;
     static constexpr std::size_t kExtentChunkBytes = 16u << 20;

@@ -25,7 +25,7 @@
 namespace tutti {
 namespace io {
 
-constexpr int kMaxSlots = 16;     // staging slots per CTA
+constexpr int kMaxSlots = 64;     // staging slots per CTA (slots x kMaxSub must stay under the queue depth)
 constexpr int kMaxSub = 8;        // NVMe commands per staging slot (extent/MDTS splits)
 constexpr int kMaxDevices = 8;    // devices (controllers) one launch can drive
 constexpr int kIoThreads = 512;   // threads per CTA with SIMT movers (host-memory staging)

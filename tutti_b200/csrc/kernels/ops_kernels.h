@@ -51,5 +51,10 @@ cudaError_t launch_checksum(const CopyItem* items, std::uint32_t n, std::uint64_
 cudaError_t launch_checksum_uniform(const CopyItem* items, std::uint32_t n, std::uint64_t bytes, std::uint64_t* out,
                                     cudaStream_t stream);
 
+// SM-filling compute stand-in for the interference benchmark: `blocks` CTAs of
+// 256 threads, each thread running `iters` x 32 FMAs. `out` (blocks x 256
+// floats) is written only if the chains hit an impossible value.
+cudaError_t launch_persistent_fma(float* out, std::uint64_t iters, std::uint32_t blocks, cudaStream_t stream);
+
 }  // namespace ops
 }  // namespace tutti

@@ -191,9 +191,21 @@ bool enable_peer_access(int64_t device, int64_t peer) {
 
 }  // namespace
 
+// Persistent compute stand-in on the current stream; blocks_per_sm CTAs per SM.
+void persistent_fma(const at::Tensor& out, int64_t iters, int64_t blocks_per_sm) {
+    TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous(), "out: float32 CUDA tensor");
+    const c10::cuda::CUDAGuard guard(out.device());
+    const std::uint32_t blocks = static_cast<std::uint32_t>(sm_count(out.get_device()) * blocks_per_sm);
+    TORCH_CHECK(out.numel() >= static_cast<int64_t>(blocks) * 256, "out needs blocks x 256 floats");
+    check_cuda(launch_persistent_fma(out.data_ptr<float>(), static_cast<std::uint64_t>(iters), blocks,
+                                     at::cuda::getCurrentCUDAStream()),
+               "persistent_fma launch");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "tutti_b200 sm_100a kernels: page copy, fp8 block scaling, prefix hashing, checksums, IPC";
     m.def("copy_items", &copy_items, py::arg("items"), py::arg("tma") = true);
+    m.def("persistent_fma", &persistent_fma, py::arg("out"), py::arg("iters"), py::arg("blocks_per_sm") = 1);
     m.def("fp8_quant", &fp8_quant, py::arg("x"), py::arg("group") = 128);
     m.def("fp8_dequant", &fp8_dequant, py::arg("q"), py::arg("scale"), py::arg("dtype") = at::kBFloat16);
     m.def("fp8_gather_quant", &fp8_gather_quant);
