@@ -14,9 +14,15 @@ the prefix lookup) to the logits of the last prompt token, p50 over iterations.
 """
 from __future__ import annotations
 
+import os
+
+# Before CUDA starts: the emulated drives' in-process DMA needs eager kernel
+# loading and enough hardware queues (see the GPU NVMe data path).
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
+
 import argparse
 import json
-import os
 import shutil
 import statistics
 import time
@@ -47,7 +53,9 @@ def run(args) -> dict:
     store = TuttiKVStore(root, g, capacity_chunks=spf * args.drives, mounts=mounts, device=args.device,
                          segment_file_slots=spf, namespace=b"ttft",
                          runtime_options={"controller_threads": args.controller_threads, "leases": 128,
-                                          "max_ctas_per_op": args.ctas_per_layer, "slots_per_lease": 8,
+                                          "max_ctas_per_op": args.ctas_per_layer, "slots_per_lease": 16,
+                                          "queue_depth": 1024, "emulator_media": args.media,
+                                          "image_budget_bytes": spf * (g.chunk_bytes + (128 << 10)) + (128 << 20),
                                           "async_completion": bool(args.async_completion)})
     store.open()
     model = LlamaModel(cfg, dev)
@@ -56,6 +64,7 @@ def run(args) -> dict:
     engine.bind(pool)
     rng = np.random.default_rng(0)
     prompts = [torch.from_numpy(rng.integers(0, cfg.vocab, size=P + N)) for _ in range(R)]
+    dev_prompts = [p.to(dev) for p in prompts]
     # Persist each request's prefix (its KV from a real prefill of the prefix).
     setup_tables = [torch.arange(r * blocks_per_req, (r + 1) * blocks_per_req) for r in range(R)]
     for r in range(R):
@@ -70,13 +79,16 @@ def run(args) -> dict:
         # fresh, randomly placed blocks for every iteration
         perm = torch.from_numpy(np.random.default_rng(100 + it).permutation(nb)[: R * blocks_per_req])
         tables = [perm[r * blocks_per_req:(r + 1) * blocks_per_req] for r in range(R)]
+        # block tables on the device before the clock starts (a serving engine keeps them
+        # there); no host-to-device copy is then queued behind the layer waits of the prefill
+        dev_tables = [t.to(dev) for t in tables]
         pool.zero_()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         if mode == "recompute":
             for r in range(R):
-                model.prefill([prompts[r]], [0], [tables[r]], pool)
+                model.prefill([dev_prompts[r]], [0], [dev_tables[r]], pool)
         else:
             keys, hit = [], []
             for r in range(R):
@@ -84,17 +96,17 @@ def run(args) -> dict:
                 hit.append(engine.lookup_prefix_keys(k))
                 keys.extend(k[: hit[-1] // g.chunk_tokens])
             table = torch.cat([tables[r][: hit[r] // bs] for r in range(R)])
-            new = [prompts[r][hit[r]:] for r in range(R)]
+            new = [dev_prompts[r][hit[r]:] for r in range(R)]
             if mode == "layerwise":
                 plan = engine.start_read_plan(keys, table, window=args.window)
-                model.prefill(new, hit, tables, pool, wait_layer=plan.wait_layer)
+                model.prefill(new, hit, dev_tables, pool, wait_layer=plan.wait_layer)
                 e.record()
                 plan.finish()
             else:
                 comp = engine.load(keys, table)
                 comp.wait()
                 torch.cuda.current_stream().wait_stream(engine.io_stream)
-                model.prefill(new, hit, tables, pool)
+                model.prefill(new, hit, dev_tables, pool)
         if mode == "recompute" or mode == "restore_then_prefill":
             e.record()
         torch.cuda.synchronize()
@@ -119,7 +131,10 @@ def main(argv=None):
     p.add_argument("--new", type=int, default=512)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--drives", type=int, default=4)
-    p.add_argument("--controller-threads", type=int, default=3)
+    p.add_argument("--controller-threads", type=int, default=1)
+    p.add_argument("--media", choices=["memory", "files"], default="memory")
+    p.add_argument("--reference", action="store_true",
+                   help="also time the reference's staged restore (baseline/_ref) on the same workload")
     p.add_argument("--ctas-per-layer", type=int, default=32)
     p.add_argument("--window", type=int, default=4)
     p.add_argument("--async-completion", action="store_true",
@@ -132,10 +147,21 @@ def main(argv=None):
     args = p.parse_args(argv)
     t0 = time.time()
     res = run(args)
+    if args.reference:
+        import subprocess
+        import sys
+
+        torch.cuda.empty_cache()  # the reference run allocates its own pool and model
+        cmd = [sys.executable, "-m", "tutti_b200.benchmarks.ttft_reference", "--requests", str(args.requests),
+               "--prefix", str(args.prefix), "--new", str(args.new), "--layers", str(args.layers),
+               "--iters", str(args.iters), "--warmup", str(args.warmup), "--device", str(args.device)]
+        out = subprocess.run(cmd, capture_output=True, text=True)
+        lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+        res["reference"] = json.loads(lines[-1]) if lines else {"error": (out.stderr or out.stdout)[-400:]}
     line = {"metric": "ttft_p50_ms", "value": res.get("layerwise", {}).get("p50_ms"), "unit": "ms",
             "higher_is_better": False, "modes": res,
             "config": {"model": "llama-3.1-8b (random init)", "requests": args.requests, "prefix_tokens": args.prefix,
-                       "new_tokens": args.new, "drives": args.drives, "dtype": "bf16"},
+                       "new_tokens": args.new, "drives": args.drives, "media": args.media, "dtype": "bf16"},
             "wall_s": round(time.time() - t0, 1)}
     print(json.dumps(line))
 

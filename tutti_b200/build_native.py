@@ -24,7 +24,8 @@ CXX = ["g++", "-O2", "-std=c++17", "-pthread", "-I", os.path.join(CSRC, "include
 TARGETS = {
     "tutti_daemon": (["daemon/daemon_main.cpp", "daemon/lease_ledger.cpp", "config/yaml_lite.cpp"], []),
     "tutti_native_tests": ([
-        "tests/native_tests.cpp", "runtime/storage_runtime.cpp", "objects/object_store.cpp",
+        "tests/native_tests.cpp", "tests/runtime_contract_tests.cpp", "tests/datapath_contract_tests.cpp",
+        "runtime/storage_runtime.cpp", "datapaths/posix_data_path.cpp", "objects/object_store.cpp",
         "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
         "resolvers/file_resolvers.cpp", "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",
     ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
@@ -46,7 +47,7 @@ def build(names=None) -> None:
             continue
         out = os.path.join(BIN, name)
         newest = max(os.path.getmtime(os.path.join(d, f)) for d, _, fs in os.walk(CSRC) for f in fs
-                     if f.endswith((".h", ".cpp", ".cuh")))
+                     if f.endswith((".h", ".cpp", ".cuh", ".cu")))
         if os.path.exists(out) and newest <= os.path.getmtime(out):
             continue
         subprocess.run(CXX + paths + ["-o", out] + libs, check=True)

@@ -272,6 +272,8 @@ Status GpuNvmeDataPath::init_device_side() {
     TUTTI_RETURN_IF_ERROR(cuda_status(
         cudaMemset(d_targets_, 0, std::size_t(cfg_.max_targets) * sizeof(io::DevTarget)), "memset targets"));
     for (std::uint32_t l = cfg_.leases; l-- > 0;) free_leases_.push_back(l);
+    TUTTI_RETURN_IF_ERROR(
+        cuda_status(cudaStreamCreateWithFlags(&upload_stream_, cudaStreamNonBlocking), "cudaStreamCreate upload"));
     for (std::uint32_t i = 0; i < cfg_.prealloc_arenas; ++i) {
         auto a = take_arena(cfg_.prealloc_arena_bytes);
         if (!a.ok()) return a.status();
@@ -301,10 +303,16 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
     for (auto& a : arena_pool_) {
         if (a->event) cudaEventDestroy(a->event);
         if (a->submitted) cudaEventDestroy(a->submitted);
+        if (a->uploaded) cudaEventDestroy(a->uploaded);
         if (a->host) cudaFreeHost(a->host);
         if (a->dev) cudaFree(a->dev);
     }
     arena_pool_.clear();
+    if (upload_stream_) {
+        cudaStreamSynchronize(upload_stream_);
+        cudaStreamDestroy(upload_stream_);
+        upload_stream_ = nullptr;
+    }
     for (auto* p : d_queue_views_) cudaFree(p);
     for (auto& m : cursor_mem_) host_mapped_free(m);
     cursor_mem_.clear();
@@ -356,9 +364,12 @@ Status GpuNvmeDataPath::flush_uploads(std::vector<DeviceUpload>& uploads) {
     // (bump-allocated extent arrays, consecutive target rows); see upload_plan.h.
     if (uploads.empty()) return Status::Ok();
     DeviceGuard guard(cfg_.accel_id);
-    for (const UploadRun& r : coalesce_uploads(std::move(uploads), 255))
-        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMemcpy(r.dst, r.bytes.data(), r.bytes.size(), cudaMemcpyHostToDevice),
-                                          "upload target rows"));
+    const auto runs = coalesce_uploads(std::move(uploads), 255);
+    for (const UploadRun& r : runs)
+        TUTTI_RETURN_IF_ERROR(cuda_status(
+            cudaMemcpyAsync(r.dst, r.bytes.data(), r.bytes.size(), cudaMemcpyHostToDevice, upload_stream_),
+            "upload target rows"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(cudaStreamSynchronize(upload_stream_), "upload target rows"));
     uploads.clear();
     return Status::Ok();
 }
@@ -439,7 +450,10 @@ Status GpuNvmeDataPath::close(DataPathTarget t) {
     free_target_rows_.push_back(static_cast<std::uint32_t>(t.token));
     DeviceGuard guard(cfg_.accel_id);
     io::DevTarget zero{};
-    return cuda_status(cudaMemcpy(d_targets_ + t.token, &zero, sizeof(zero), cudaMemcpyHostToDevice), "clear target");
+    Status cs = cuda_status(cudaMemcpyAsync(d_targets_ + t.token, &zero, sizeof(zero), cudaMemcpyHostToDevice,
+                                            upload_stream_), "clear target");
+    if (cs.ok()) cs = cuda_status(cudaStreamSynchronize(upload_stream_), "clear target");
+    return cs;
 }
 
 Result<RegistrationDomainKey> GpuNvmeDataPath::registration_domain(DataPathTarget) const {
@@ -501,8 +515,10 @@ Result<std::unique_ptr<GpuNvmeDataPath::Arena>> GpuNvmeDataPath::take_arena(std:
     }
     s = cuda_status(cudaEventCreateWithFlags(&a->event, cudaEventDisableTiming), "cudaEventCreate");
     if (s.ok()) s = cuda_status(cudaEventCreateWithFlags(&a->submitted, cudaEventDisableTiming), "cudaEventCreate");
+    if (s.ok()) s = cuda_status(cudaEventCreateWithFlags(&a->uploaded, cudaEventDisableTiming), "cudaEventCreate");
     if (!s.ok()) {
         if (a->event) cudaEventDestroy(a->event);
+        if (a->submitted) cudaEventDestroy(a->submitted);
         cudaFreeHost(a->host);
         cudaFree(a->dev);
         return R::Failure(s);
@@ -735,7 +751,9 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
                       cmds[0].opcode == nvme::kOpRead ? "read" : "write", n_cmds, take, xform ? "|fp8" : "");
         nvtxRangePushA(name);
     }
-    Status cs = cuda_status(cudaMemcpyAsync(d, h, off_status, cudaMemcpyHostToDevice, s), "H2D commands");
+    Status cs = cuda_status(cudaMemcpyAsync(d, h, off_status, cudaMemcpyHostToDevice, upload_stream_), "H2D commands");
+    if (cs.ok()) cs = cuda_status(cudaEventRecord(arena->uploaded, upload_stream_), "event record");
+    if (cs.ok()) cs = cuda_status(cudaStreamWaitEvent(s, arena->uploaded, 0), "stream wait");
     bool launched = false;
     if (cs.ok()) {
         if (take_test_fault(TestFault::LAUNCH_FAILURE)) {
@@ -759,6 +777,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     if (!cs.ok() && !launched) {
         // The kernel was not issued, so nothing irreversible happened:
         // report every request rejected and return the leases.
+        cudaStreamSynchronize(upload_stream_);
         cudaStreamSynchronize(s);
         for (auto l : op->leases) free_leases_.push_back(l);
         return_arena(std::move(arena));

@@ -181,6 +181,7 @@ private:
         char* dev = nullptr;
         cudaEvent_t event = nullptr;      // after the (drain) kernel and the status copy-back
         cudaEvent_t submitted = nullptr;  // split completion: after the submit-phase kernel
+        cudaEvent_t uploaded = nullptr;   // after the command list's upload (on the upload stream)
     };
     struct OpRec {
         std::uint64_t generation = 0;
@@ -242,6 +243,10 @@ private:
     // device staging the arena is staging_hbm_ (cudaMalloc) and staging_ is unused
     HostMappedBuffer staging_, prp_;
     char* staging_hbm_ = nullptr;
+    // Command lists and target rows go to the device on this stream, never on
+    // a stream where an io kernel may be running: a copy waiting behind a
+    // kernel that waits for the drives could hold up the drives' own copies.
+    cudaStream_t upload_stream_ = nullptr;
     bool staging_on_device_ = false;
     char* staging_base() const { return staging_on_device_ ? staging_hbm_ : static_cast<char*>(staging_.device); }
     std::uint64_t staging_iova_ = 0, prp_iova_ = 0;

@@ -9,6 +9,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <climits>
 #include <cerrno>
 #include <cstring>
 #include <cstdio>
@@ -180,6 +181,20 @@ Result<ResolvedTarget> LocalFileResolver::resolve(std::string_view uri, const Re
     std::string path = uri_to_path(uri);
     if (path.empty() || path[0] != '/')
         return Result<ResolvedTarget>::Failure({StatusCode::INVALID_ARGUMENT, "path must be absolute"});
+    if (!binding_.mount_path.empty()) {
+        // A resolver serves the files of its mount only; compare canonical paths
+        // so that ".." or a symlink cannot step outside it.
+        char real_file[PATH_MAX], real_mount[PATH_MAX];
+        if (!::realpath(path.c_str(), real_file))
+            return Result<ResolvedTarget>::Failure({StatusCode::NOT_FOUND, "cannot resolve " + path});
+        const std::string mount = ::realpath(binding_.mount_path.c_str(), real_mount) ? std::string(real_mount)
+                                                                                      : binding_.mount_path;
+        const std::string file(real_file);
+        if (file.compare(0, mount.size(), mount) != 0 || (file.size() > mount.size() && mount != "/" &&
+                                                          file[mount.size()] != '/'))
+            return Result<ResolvedTarget>::Failure(
+                {StatusCode::INVALID_ARGUMENT, path + " is outside the mount " + binding_.mount_path});
+    }
     auto p = build_payload(path);
     if (!p.ok()) return Result<ResolvedTarget>::Failure(p.status());
     std::uint64_t size = p.value()->file_size;

@@ -161,7 +161,8 @@ private:
                 op.snap.status = {StatusCode::DEVICE_ERROR, "injected request failure"};
                 op.snap.detail.failure_kind = IoFailureKind::NVME_CQ_ERROR;
                 op.snap.detail.failure_scope = IoFailureScope::REQUEST_INDICES;
-                op.snap.detail.failed_request_indices.push_back(static_cast<std::uint32_t>(k));
+                // indices name entries of the DataPath submit's request array
+                op.snap.detail.failed_request_indices.push_back(op.index[k]);
                 continue;
             }
             auto& blob = *targets_[r.target.token];
