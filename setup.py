@@ -31,6 +31,8 @@ CORE_SOURCES = [
     src("runtime", "storage_runtime.cpp"),
     src("nvme", "host_memory.cpp"),
     src("nvme", "emulated_controller.cpp"),
+    src("nvme", "snvme_client.cpp"),
+    src("testing", "fake_snvme.cpp"),
     src("resolvers", "file_resolvers.cpp"),
     src("datapaths", "gpu_nvme_data_path.cpp"),
     src("datapaths", "posix_data_path.cpp"),

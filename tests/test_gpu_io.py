@@ -62,6 +62,36 @@ def test_store_restore_roundtrip_random_blocks(tmp_path, drives, media):
         st.close()
 
 
+def test_restore_through_the_snvme_client_over_a_fake_driver(tmp_path, media):
+    """The real-drive provider's path: the snvme client creates queue groups,
+    maps rings and data buffers per page through the driver, has it create the
+    queue pairs and hands the GPU data path BAR0 doorbells; a fake driver whose
+    hardware is an emulated drive stands in for the kernel module."""
+    st = make(tmp_path, drives=2, media=media, nvme_provider="snvme_fake", leases=40, max_ctas_per_op=16)
+    try:
+        stats = st.runtime.controller_stats()
+        assert [s["kind"] for s in stats] == ["snvme", "snvme"]
+        assert all(s["queues"] == 40 for s in stats)  # two queue groups (32 + 8) per drive
+        nb = 512
+        pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+        st.register_pool(pool)
+        n = 24
+        keys = chunk_keys_for_tokens(list(range(n * 64)), 64, namespace=b"p1")
+        rng = np.random.default_rng(3)
+        src = rng.permutation(nb)[: n * 4].reshape(n, 4)
+        st.put_paged(keys, src).wait()
+        ref = pool[:, :, torch.from_numpy(src.reshape(-1)).cuda()].clone()
+        dst = rng.permutation(nb)[: n * 4].reshape(n, 4)
+        pool.zero_()
+        st.get_paged(keys, dst).wait()
+        got = pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()]
+        assert torch.equal(got, ref)
+        stats = st.runtime.controller_stats()
+        assert sum(s["read_bytes"] for s in stats) == n * G.chunk_bytes
+    finally:
+        st.close()
+
+
 def test_layer_subset_restore(tmp_path, media):
     st = make(tmp_path, media=media)
     try:

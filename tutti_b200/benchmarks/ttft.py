@@ -25,6 +25,7 @@ import argparse
 import json
 import shutil
 import statistics
+import sys
 import time
 
 import numpy as np
@@ -112,11 +113,19 @@ def run(args) -> dict:
         torch.cuda.synchronize()
         return s.elapsed_time(e)
 
+    def checked(mode: str, it: int) -> float:
+        try:
+            return one(mode, it)
+        except Exception:
+            # the drives' counters say whether a restore waited on the media, the copies or the queues
+            print(json.dumps({"failed_in": mode, "controllers": store.runtime.controller_stats()}), file=sys.stderr)
+            raise
+
     out = {}
     for mode in args.modes:
         for w in range(args.warmup):
-            one(mode, 1000 + w)
-        ts = [one(mode, i) for i in range(args.iters)]
+            checked(mode, 1000 + w)
+        ts = [checked(mode, i) for i in range(args.iters)]
         out[mode] = {"p50_ms": round(statistics.median(ts), 2), "samples_ms": [round(t, 2) for t in ts]}
     # correctness: logits from the layerwise path equal those of a full recompute
     store.close()
@@ -149,7 +158,6 @@ def main(argv=None):
     res = run(args)
     if args.reference:
         import subprocess
-        import sys
 
         torch.cuda.empty_cache()  # the reference run allocates its own pool and model
         cmd = [sys.executable, "-m", "tutti_b200.benchmarks.ttft_reference", "--requests", str(args.requests),

@@ -25,6 +25,7 @@ TARGETS = {
     "tutti_daemon": (["daemon/daemon_main.cpp", "daemon/lease_ledger.cpp", "config/yaml_lite.cpp"], []),
     "tutti_native_tests": ([
         "tests/native_tests.cpp", "tests/runtime_contract_tests.cpp", "tests/datapath_contract_tests.cpp",
+        "tests/snvme_client_tests.cpp", "nvme/snvme_client.cpp", "testing/fake_snvme.cpp",
         "runtime/storage_runtime.cpp", "datapaths/posix_data_path.cpp", "objects/object_store.cpp",
         "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
         "resolvers/file_resolvers.cpp", "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",

@@ -222,25 +222,50 @@ Status GpuNvmeDataPath::init_device_side() {
     if (!pr.ok()) return pr.status();
     prp_ = pr.value();
     if (!prp_.device) return {StatusCode::UNSUPPORTED, "nvme-gpu needs a CUDA device (device-mapped host memory)"};
-    // Same bus address on every controller (identity IOMMU / pass-through).
+    // Map both regions on every controller. The prebuilt PRP lists are shared by
+    // all drives, so every controller must report the same bus address for
+    // every page (an identity or pass-through IOMMU does).
+    const std::uint64_t pages_per_slot = cfg_.slot_bytes / nvme::kMemoryPageBytes;
+    std::vector<std::uint64_t> page_bus(nslots * pages_per_slot), list_bus(nslots);
+    char* const arena_va = static_cast<char*>(arena);
+    char* const prp_va = static_cast<char*>(prp_.host);
     for (std::size_t d = 0; d < devs_.size(); ++d) {
         auto a = devs_[d].controller->map_dma(arena, arena_bytes);
-        auto b = devs_[d].controller->map_dma(prp_.host, prp_.bytes);
         if (!a.ok()) return a.status();
+        staging_maps_.push_back(std::move(a).value());
+        auto b = devs_[d].controller->map_dma(prp_.host, prp_.bytes);
         if (!b.ok()) return b.status();
-        if (d == 0) {
-            staging_iova_ = a.value();
-            prp_iova_ = b.value();
-        } else if (a.value() != staging_iova_ || b.value() != prp_iova_) {
-            return {StatusCode::UNSUPPORTED, "controllers disagree on DMA addresses of the staging arena"};
+        prp_maps_.push_back(std::move(b).value());
+        const nvme::DmaMapping& sm = staging_maps_.back();
+        const nvme::DmaMapping& pm = prp_maps_.back();
+        if (!sm.covers(arena, nslots * cfg_.slot_bytes) || !pm.covers(prp_.host, nslots * nvme::kMemoryPageBytes))
+            return {StatusCode::INTERNAL, devs_[d].identity + ": DMA mapping does not cover the buffer"};
+        for (std::uint64_t k = 0; k < page_bus.size(); ++k) {
+            const std::uint64_t bus = sm.bus_at(arena_va + k * nvme::kMemoryPageBytes);
+            if (bus == 0 || (bus & (nvme::kMemoryPageBytes - 1)) != 0)
+                return {StatusCode::UNSUPPORTED, devs_[d].identity + ": staging page without a 4 KiB-aligned bus address"};
+            if (d > 0 && bus != page_bus[k])
+                return {StatusCode::UNSUPPORTED, "controllers disagree on the bus addresses of the staging arena"};
+            page_bus[k] = bus;
+        }
+        for (std::uint64_t i = 0; i < nslots; ++i) {
+            const std::uint64_t bus = pm.bus_at(prp_va + i * nvme::kMemoryPageBytes);
+            if (bus == 0 || (d > 0 && bus != list_bus[i]))
+                return {StatusCode::UNSUPPORTED, "controllers disagree on the bus addresses of the PRP lists"};
+            list_bus[i] = bus;
         }
     }
-    // Prebuilt PRP lists: page j of slot i.
+    // Prebuilt PRP lists: entry j of slot i's page is the bus address of the
+    // slot's page j (a command starting at page j0 points PRP2 at entry j0 + 1).
     auto* lists = static_cast<std::uint64_t*>(prp_.host);
-    const std::uint64_t pages_per_slot = cfg_.slot_bytes / nvme::kMemoryPageBytes;
     for (std::uint64_t i = 0; i < nslots; ++i)
-        for (std::uint64_t j = 0; j < pages_per_slot; ++j)
-            lists[i * 512 + j] = staging_iova_ + i * cfg_.slot_bytes + j * nvme::kMemoryPageBytes;
+        for (std::uint64_t j = 0; j < pages_per_slot; ++j) lists[i * 512 + j] = page_bus[i * pages_per_slot + j];
+    TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_page_bus_, page_bus.size() * 8), "cudaMalloc page table"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_list_bus_, list_bus.size() * 8), "cudaMalloc list table"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(
+        cudaMemcpy(d_page_bus_, page_bus.data(), page_bus.size() * 8, cudaMemcpyHostToDevice), "upload page table"));
+    TUTTI_RETURN_IF_ERROR(cuda_status(
+        cudaMemcpy(d_list_bus_, list_bus.data(), list_bus.size() * 8, cudaMemcpyHostToDevice), "upload list table"));
 
     std::vector<io::DevDevice> rows(devs_.size());
     for (std::size_t d = 0; d < devs_.size(); ++d) {
@@ -272,6 +297,7 @@ Status GpuNvmeDataPath::init_device_side() {
     TUTTI_RETURN_IF_ERROR(cuda_status(
         cudaMemset(d_targets_, 0, std::size_t(cfg_.max_targets) * sizeof(io::DevTarget)), "memset targets"));
     for (std::uint32_t l = cfg_.leases; l-- > 0;) free_leases_.push_back(l);
+    retired_.assign(cfg_.leases, false);
     TUTTI_RETURN_IF_ERROR(
         cuda_status(cudaStreamCreateWithFlags(&upload_stream_, cudaStreamNonBlocking), "cudaStreamCreate upload"));
     for (std::uint32_t i = 0; i < cfg_.prealloc_arenas; ++i) {
@@ -324,10 +350,15 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
     if (d_targets_) cudaFree(d_targets_);
     d_devices_ = nullptr;
     d_targets_ = nullptr;
-    for (auto& d : devs_) {
-        if (staging_.host || staging_hbm_) d.controller->unmap_dma(staging_iova_);
-        if (prp_.host) d.controller->unmap_dma(prp_iova_);
+    for (std::size_t d = 0; d < devs_.size(); ++d) {
+        if (d < staging_maps_.size()) devs_[d].controller->unmap_dma(staging_maps_[d]);
+        if (d < prp_maps_.size()) devs_[d].controller->unmap_dma(prp_maps_[d]);
     }
+    staging_maps_.clear();
+    prp_maps_.clear();
+    if (d_page_bus_) cudaFree(d_page_bus_);
+    if (d_list_bus_) cudaFree(d_list_bus_);
+    d_page_bus_ = d_list_bus_ = nullptr;
     host_mapped_free(staging_);
     host_mapped_free(prp_);
     if (staging_hbm_) cudaFree(staging_hbm_);
@@ -391,8 +422,8 @@ Result<DataPathTarget> GpuNvmeDataPath::open_locked(const ResolvedTarget& target
     DeviceGuard guard(cfg_.accel_id);
     // Back the namespace ranges on emulated controllers.
     for (std::size_t d = 0; d < devs_.size(); ++d) {
-        auto* emu = dynamic_cast<nvme::EmulatedNvmeController*>(devs_[d].controller.get());
-        if (!emu) continue;
+        nvme::EmulatedNvmeController* emu = devs_[d].controller->emulated_drive();
+        if (!emu) continue;  // a real drive: the file system already sits on its namespace
         std::vector<nvme::BackingRange> ranges;
         for (const auto& e : p.extents)
             if (e.device == d) ranges.push_back({e.physical, e.length, e.logical});
@@ -733,9 +764,9 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     kp.devices = d_devices_;
     kp.lease_ids = reinterpret_cast<const std::uint32_t*>(d + off_leases);
     kp.staging_dev = staging_base();
-    kp.staging_iova = staging_iova_;
+    kp.page_bus = d_page_bus_;
+    kp.list_bus = d_list_bus_;
     kp.movers = staging_on_device_ ? io::kMoversBulk : io::kMoversSimt;
-    kp.prp_iova = prp_iova_;
     kp.slot_bytes = cfg_.slot_bytes;
     kp.slots_per_lease = cfg_.slots_per_lease;
     kp.timeout_ns = cfg_.timeout_ns;
@@ -838,15 +869,36 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
 
 Status GpuNvmeDataPath::reset_dirty_queues(const std::vector<std::uint32_t>& leases) {
     // Caller holds mu_; the op is terminal, so its kernels have written the cursors.
+    // A queue the controller cannot reset (a real drive resets whole queue
+    // groups only) retires its lease: it never serves another op.
+    Status first;
     for (std::size_t d = 0; d < devs_.size(); ++d) {
         auto* cur = cursor_mem_[d].host_as<io::QueueCursor>();
         for (auto l : leases) {
             if (!reinterpret_cast<volatile io::QueueCursor*>(cur)[l].dirty) continue;
-            TUTTI_RETURN_IF_ERROR(devs_[d].controller->reset_queue(l));
+            Status s = devs_[d].controller->reset_queue(l);
+            if (!s.ok()) {
+                retire_lease_locked(l, s);
+                if (first.ok()) first = s;
+                continue;
+            }
             cur[l] = io::QueueCursor{0, 0, 1, 0};
         }
     }
-    return Status::Ok();
+    return first;
+}
+
+void GpuNvmeDataPath::retire_lease_locked(std::uint32_t lease, const Status& why) {
+    if (lease < retired_.size() && !retired_[lease]) {
+        retired_[lease] = true;
+        std::fprintf(stderr, "[tutti] nvme-gpu accel %d: lease %u retired (%s)\n", cfg_.accel_id, lease,
+                     why.message().c_str());
+    }
+}
+
+void GpuNvmeDataPath::return_leases_locked(const std::vector<std::uint32_t>& leases) {
+    for (auto l : leases)
+        if (l >= retired_.size() || !retired_[l]) free_leases_.push_back(l);
 }
 
 bool GpuNvmeDataPath::split_data_ready(const OpRec& op) const {
@@ -864,6 +916,7 @@ bool GpuNvmeDataPath::split_data_ready(const OpRec& op) const {
             const auto* cur = reinterpret_cast<const volatile io::QueueCursor*>(cursor_mem_[d].host) + l;
             const std::uint32_t head = cur->cq_head, phase = cur->phase;
             const nvme::QueuePairView q = devs_[d].controller->host_queue(l);
+            if (!q.cq) return false;  // a CQ in GPU memory: the drain waits for the fallback timer
             for (std::uint32_t k = 0; k < n; ++k) {
                 const std::uint32_t at = head + k;
                 const std::uint32_t want = (at >= q.depth) ? (phase ^ 1u) : phase;
@@ -909,9 +962,9 @@ void GpuNvmeDataPath::finish_op(OpRec& op) {
     op.detail = std::move(det);
     if (any_timeout_or_notrun) {
         Status rs = reset_dirty_queues(op.leases);
-        (void)rs;
+        (void)rs;  // a lease whose queue could not be reset is retired
     }
-    for (auto l : op.leases) free_leases_.push_back(l);
+    return_leases_locked(op.leases);
     op.leases.clear();
     op.state = any_fail ? IoState::FAILED : IoState::COMPLETED;
     op.status = any_fail ? Status(StatusCode::DEVICE_ERROR,
@@ -1073,10 +1126,15 @@ void GpuNvmeDataPath::noalloc_release_leases(const std::uint32_t* leases, std::u
             for (std::size_t d = 0; d < devs_.size(); ++d) {
                 auto* cur = cursor_mem_[d].host_as<io::QueueCursor>();
                 if (!reinterpret_cast<volatile io::QueueCursor*>(cur)[l].dirty) continue;
-                if (!devs_[d].controller->reset_queue(l).ok()) continue;
+                Status s = devs_[d].controller->reset_queue(l);
+                if (!s.ok()) {
+                    retire_lease_locked(l, s);
+                    continue;
+                }
                 cur[l] = io::QueueCursor{0, 0, 1, 0};
             }
         }
+        if (l < retired_.size() && retired_[l]) continue;
         // The vector held every lease at initialize, so its capacity covers this push: no reallocation.
         free_leases_.push_back(l);
     }
@@ -1103,9 +1161,9 @@ void GpuNvmeDataPath::noalloc_fill_params(io::IoKernelParams& p) const {
     p.targets = d_targets_;
     p.devices = d_devices_;
     p.staging_dev = staging_base();
-    p.staging_iova = staging_iova_;
+    p.page_bus = d_page_bus_;
+    p.list_bus = d_list_bus_;
     p.movers = staging_on_device_ ? io::kMoversBulk : io::kMoversSimt;
-    p.prp_iova = prp_iova_;
     p.slot_bytes = cfg_.slot_bytes;
     p.slots_per_lease = cfg_.slots_per_lease;
     p.timeout_ns = cfg_.timeout_ns;

@@ -222,6 +222,8 @@ private:
     // for has been posted (read from the host-resident CQs and cursors).
     bool split_data_ready(const OpRec& op) const;
     Status reset_dirty_queues(const std::vector<std::uint32_t>& leases);
+    void retire_lease_locked(std::uint32_t lease, const Status& why);
+    void return_leases_locked(const std::vector<std::uint32_t>& leases);
 
     GpuNvmeConfig cfg_;
     std::vector<GpuNvmeDevice> devs_;
@@ -249,7 +251,14 @@ private:
     cudaStream_t upload_stream_ = nullptr;
     bool staging_on_device_ = false;
     char* staging_base() const { return staging_on_device_ ? staging_hbm_ : static_cast<char*>(staging_.device); }
-    std::uint64_t staging_iova_ = 0, prp_iova_ = 0;
+    // Per controller: the DMA mappings of the staging arena and the PRP-list
+    // pages. Every controller must hand out the same bus addresses (one set of
+    // prebuilt PRP lists serves all drives).
+    std::vector<nvme::DmaMapping> staging_maps_, prp_maps_;
+    // Device copies of the bus-address tables the io kernel builds PRPs from:
+    // one entry per 4 KiB staging page, one per slot's PRP-list page.
+    std::uint64_t* d_page_bus_ = nullptr;
+    std::uint64_t* d_list_bus_ = nullptr;
     std::uint32_t lba_ = 512;  // largest LBA size of the device table
 
     std::vector<TargetRec> targets_;
@@ -258,6 +267,7 @@ private:
     std::unordered_map<std::uint64_t, MemoryRec> memories_;
     std::unordered_map<std::uint64_t, std::unique_ptr<OpRec>> ops_;
     std::vector<std::uint32_t> free_leases_;
+    std::vector<bool> retired_;  // leases whose queues could not be reset after a timeout
     std::vector<std::unique_ptr<Arena>> arena_pool_;
     std::uint64_t next_token_ = 1;
     IoTimingSummary last_timing_;

@@ -438,20 +438,20 @@ __device__ bool issue_cmd(const IoKernelParams& p, Shared& sh, int ci, int s, st
     const int n = resolve_cmd(p, c, sub, err);
     if (n == 0) return false;
     const std::uint64_t slot_index = lease_slot0 + s;
-    const std::uint64_t slot_iova = p.staging_iova + slot_index * p.slot_bytes;
-    const std::uint64_t list_iova = p.prp_iova + slot_index * nvme::kMemoryPageBytes;
+    const std::uint64_t* pages = p.page_bus + slot_index * (p.slot_bytes >> 12);
+    const std::uint64_t list_bus = p.list_bus[slot_index];
     for (int k = 0; k < n; ++k) {
         const std::uint32_t dv = sub[k].device;
         const DevDevice& d = p.devices[dv];
         const nvme::QueuePairView& q = d.queues[lease];
-        const std::uint64_t prp1 = slot_iova + sub[k].off;
         const std::uint32_t page0 = sub[k].off >> 12;
+        const std::uint64_t prp1 = pages[page0] + (sub[k].off & 4095u);
         const std::uint32_t extra = nvme::prp_extra_pages(prp1 & 4095u, sub[k].bytes);
         std::uint64_t prp2 = 0;
         if (extra == 1)
-            prp2 = slot_iova + (static_cast<std::uint64_t>(page0 + 1) << 12);
+            prp2 = pages[page0 + 1];
         else if (extra > 1)
-            prp2 = list_iova + 8ull * (page0 + 1);
+            prp2 = list_bus + 8ull * (page0 + 1);
         nvme::Sqe e;
         nvme::build_rw_sqe(e, static_cast<std::uint8_t>(c.opcode), static_cast<std::uint16_t>(s * kMaxSub + k), d.nsid,
                            sub[k].lba, sub[k].bytes >> d.lba_shift, prp1, prp2);
@@ -470,12 +470,29 @@ __device__ bool issue_cmd(const IoKernelParams& p, Shared& sh, int ci, int s, st
     return true;
 }
 
+// One doorbell write. A doorbell in host memory (emulated drive) takes a
+// system-scope release store. A controller register in BAR0 takes an .mmio
+// store (performed exactly once, never merged or served from a cache), after a
+// system-scope fence that orders the ring accesses before it (a relaxed .mmio
+// store orders nothing by itself).
+__device__ __forceinline__ void write_doorbell(const nvme::QueuePairView& q, std::uint32_t* db, std::uint32_t v) {
+    if (q.flags & nvme::kQueueMmioDoorbells) {
+        asm volatile("fence.sc.sys;" ::: "memory");
+        asm volatile("st.mmio.relaxed.sys.global.u32 [%0], %1;" ::"l"(db), "r"(v) : "memory");
+    } else {
+        st_release_sys(db, v);
+    }
+}
+
 // SQEs before the tail doorbells (system scope: the controller is a peer).
 __device__ void ring_doorbells(const IoKernelParams& p, Shared& sh, std::uint32_t lease, std::uint32_t touched) {
     if (!touched) return;
     __threadfence_system();
     for (std::uint32_t d = 0; d < p.n_devices; ++d)
-        if (touched & (1u << d)) st_release_sys(p.devices[d].queues[lease].sq_doorbell, sh.cur[d].sq_tail);
+        if (touched & (1u << d)) {
+            const nvme::QueuePairView& q = p.devices[d].queues[lease];
+            write_doorbell(q, q.sq_doorbell, sh.cur[d].sq_tail);
+        }
 }
 
 // Split completion, submit phase: fill this lease's slots with read commands,
@@ -565,7 +582,7 @@ __device__ void engine_loop(const IoKernelParams& p, Shared& sh, std::uint32_t l
                 if (sh.cur[d].cq_head == 0) sh.cur[d].phase ^= 1u;
             }
             if (got) {
-                st_release_sys(q.cq_doorbell, sh.cur[d].cq_head);
+                write_doorbell(q, q.cq_doorbell, sh.cur[d].cq_head);
                 progressed = true;
             }
         }

@@ -140,8 +140,12 @@ struct IoKernelParams {
     const DevDevice* devices;     // n_devices rows (device memory)
     const std::uint32_t* lease_ids;  // gridDim.x leases
     char* staging_dev;            // device address of the staging arena
-    std::uint64_t staging_iova;   // bus address of the same arena
-    std::uint64_t prp_iova;       // bus address of the PRP-list pages (one page per slot)
+    // Bus addresses the drives DMA to (device memory): page_bus[k] is the bus
+    // address of 4 KiB page k of the staging arena (slot i covers pages
+    // [i * slot_bytes / 4 KiB, ...)), list_bus[i] that of slot i's prebuilt
+    // PRP-list page. Pages need not be adjacent on the bus.
+    const std::uint64_t* page_bus;
+    const std::uint64_t* list_bus;
     std::uint32_t slot_bytes;     // <= 2 MiB (one PRP-list page per slot)
     std::uint32_t slots_per_lease;
     std::uint64_t timeout_ns;     // per command, from submission

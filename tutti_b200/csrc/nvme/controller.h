@@ -15,9 +15,11 @@
 //     drive's posted writes give: data before completion). Used where no
 //     user-owned NVMe queues exist (no queue-leasing kernel driver, no
 //     bindable drives).
-//   * A real controller leased from the queue broker would expose the same
-//     QueuePairView with BAR0 doorbells; it needs a queue-owning kernel driver
-//     and is reported UNSUPPORTED when none is present.
+//   * SnvmeController (snvme_client.h): a real controller driven through the
+//     snvme queue-leasing driver. The rings live in this process's memory, the
+//     driver creates the queue pairs over them, the doorbells are the
+//     controller's BAR0 (mapped into the process and registered with CUDA as
+//     I/O memory) and PRPs carry the bus addresses the driver pinned.
 //
 // Parity: queue memory layout and doorbell stride follow the reference's
 // libnvm queue structs (csrc/device_manager/nvme/libnvm/include/nvm_types.h) and
@@ -39,6 +41,9 @@
 namespace tutti {
 namespace nvme {
 
+// QueuePairView::flags
+constexpr std::uint32_t kQueueMmioDoorbells = 1u << 0;  // doorbells are device registers (BAR0)
+
 // Device-visible view of one I/O queue pair; POD, copied into GPU memory.
 struct QueuePairView {
     Sqe* sq;                    // SQ ring (depth entries)
@@ -48,7 +53,32 @@ struct QueuePairView {
     std::uint32_t depth;
     std::uint32_t qid;
     std::uint32_t nsid;
-    std::uint32_t pad;
+    std::uint32_t flags;        // kQueue*
+};
+
+// Bus addresses of a buffer made DMA-reachable by a controller. Behind an
+// IOMMU or a GPU peer mapping every page has its own bus address and the
+// pages of one buffer need not be adjacent on the bus.
+struct DmaMapping {
+    std::uint64_t va = 0;          // start of the mapped range (page-aligned when paged)
+    std::uint64_t bytes = 0;       // length of the mapped range
+    std::uint64_t page_bytes = 0;  // 0: the whole range is one bus range at bus[0]
+    std::vector<std::uint64_t> bus;
+    int kind = 0;                  // controller-private (which unmap call releases it)
+
+    bool covers(const void* p, std::uint64_t n) const {
+        const auto a = reinterpret_cast<std::uint64_t>(p);
+        return a >= va && n <= bytes && a - va <= bytes - n;
+    }
+    // Bus address of virtual address `p` inside the range (0 outside it).
+    std::uint64_t bus_at(const void* p) const {
+        const auto a = reinterpret_cast<std::uint64_t>(p);
+        if (a < va || a - va >= bytes || bus.empty()) return 0;
+        const std::uint64_t off = a - va;
+        if (page_bytes == 0) return bus[0] + off;
+        const std::uint64_t pg = off / page_bytes;
+        return pg < bus.size() ? bus[pg] + off % page_bytes : 0;
+    }
 };
 
 struct ControllerInfo {
@@ -101,12 +131,15 @@ public:
     virtual QueuePairView device_queue(std::uint32_t i) const = 0;
     // Host-side pointers (host submitter, tests).
     virtual QueuePairView host_queue(std::uint32_t i) const = 0;
-    // Make [ptr, ptr+bytes) DMA-reachable by the controller; returns its bus address.
-    virtual Result<std::uint64_t> map_dma(void* host_ptr, std::uint64_t bytes) = 0;
-    virtual Status unmap_dma(std::uint64_t iova) = 0;
+    // Make [ptr, ptr+bytes) (host or GPU memory) DMA-reachable by the controller.
+    virtual Result<DmaMapping> map_dma(void* ptr, std::uint64_t bytes) = 0;
+    virtual Status unmap_dma(const DmaMapping& m) = 0;
     // Quiesce queue i and reset its head/tail/phase (after a timeout).
     virtual Status reset_queue(std::uint32_t i) = 0;
     virtual ControllerStats stats() const = 0;
+    // The emulated drive that answers this controller's queues, if any (its
+    // namespace is backed by files and it takes host-side fault injection).
+    virtual class EmulatedNvmeController* emulated_drive() { return nullptr; }
 };
 
 struct EmulatedControllerConfig {
@@ -139,6 +172,10 @@ struct EmulatedControllerConfig {
     Media media = Media::FILES;
     std::uint64_t image_chunk_bytes = 64ull << 20;
     std::uint64_t image_budget_bytes = 0;
+    // Queue pairs are created by a driver over rings it was given
+    // (create_io_queue_pair) instead of existing from the start on the
+    // controller's own rings.
+    bool driver_created_queues = false;
     // CUDA device whose memory PRPs may name (-1: the current device at create;
     // ignored without CUDA). GPU destinations are DMA'd by the copy engines.
     int cuda_device = -1;
@@ -156,10 +193,26 @@ public:
     const ControllerInfo& info() const override { return info_; }
     QueuePairView device_queue(std::uint32_t i) const override;
     QueuePairView host_queue(std::uint32_t i) const override;
-    Result<std::uint64_t> map_dma(void* host_ptr, std::uint64_t bytes) override;
-    Status unmap_dma(std::uint64_t iova) override;
+    Result<DmaMapping> map_dma(void* ptr, std::uint64_t bytes) override;
+    Status unmap_dma(const DmaMapping& m) override;
     Status reset_queue(std::uint32_t i) override;
     ControllerStats stats() const override;
+    EmulatedNvmeController* emulated_drive() override { return this; }
+
+    // A DMA window whose memory kind the caller states (true: GPU memory), as
+    // a driver that pinned the pages knows it. Returns the identity bus address.
+    Result<std::uint64_t> map_window(void* ptr, std::uint64_t bytes, bool device);
+    Status unmap_window(std::uint64_t bus);
+
+    // What a queue-owning driver does with admin commands (driver_created_queues):
+    // Create I/O CQ + SQ `qid` (1..num_io_queues) over host-memory rings of
+    // `depth` entries, and Delete them. The doorbells of `qid` sit at the NVMe
+    // offsets of the register file (bar0_host / bar0_device).
+    Status create_io_queue_pair(std::uint32_t qid, void* sq, void* cq, std::uint32_t depth);
+    Status delete_io_queue_pair(std::uint32_t qid);
+    void* bar0_host() const { return bar_mem_.host; }
+    void* bar0_device() const { return bar_mem_.device; }
+    std::uint64_t bar0_bytes() const { return bar_mem_.bytes; }
 
     // Back namespace ranges with a file (opened by the controller itself).
     // Idempotent for identical ranges; overlapping ranges of another file fail.
@@ -198,7 +251,18 @@ private:
         std::uint32_t phase = 1;
         std::atomic<std::uint32_t> reset_request{0};
         std::atomic<std::uint32_t> fatal{0};
+        // The rings this queue serves (host view) and the device address of its
+        // CQ (completions written by a copy stream); owned by the worker, changed
+        // only through a reset request.
+        QueuePairView view{};
+        char* cq_device = nullptr;
+        bool enabled = true;
+        // A driver's create/delete, applied by the worker with the next reset.
+        QueuePairView pending_view{};
+        char* pending_cq_device = nullptr;
+        bool pending_enabled = true;
     };
+    Status apply_queue_change(std::uint32_t i);
     struct Backing {
         std::string path;
         int fd = -1;

@@ -126,10 +126,18 @@ Status EmulatedNvmeController::start() {
     auto cq = host_mapped_alloc(nq * d * sizeof(Cqe));
     if (!cq.ok()) return cq.status();
     cq_mem_ = cq.value();
-    auto bar = host_mapped_alloc(kDoorbellBase + 8 * nq);
+    // Register file: doorbells of the admin queue (0) and I/O queues 1..nq.
+    auto bar = host_mapped_alloc(kDoorbellBase + 8 * (nq + 1));
     if (!bar.ok()) return bar.status();
     bar_mem_ = bar.value();
-    for (std::uint32_t i = 0; i < nq; ++i) qstate_.emplace_back(new QueueState());
+    for (std::uint32_t i = 0; i < nq; ++i) {
+        qstate_.emplace_back(new QueueState());
+        QueueState& qs = *qstate_.back();
+        qs.view = host_queue(i);
+        if (cq_mem_.device)
+            qs.cq_device = static_cast<char*>(cq_mem_.device) + std::uint64_t(i) * d * sizeof(Cqe);
+        qs.enabled = !cfg_.driver_created_queues;
+    }
     std::uint32_t nw = std::max<std::uint32_t>(1, std::min(cfg_.worker_threads, cfg_.num_io_queues));
     // All CUDA allocations happen here, before any io kernel can wait on this drive.
     if (cfg_.media == EmulatedControllerConfig::Media::MEMORY) {
@@ -195,10 +203,10 @@ static QueuePairView make_view(char* sq, char* cq, char* bar, std::uint32_t i, s
     QueuePairView v{};
     v.sq = reinterpret_cast<Sqe*>(sq) + std::uint64_t(i) * depth;
     v.cq = reinterpret_cast<const Cqe*>(cq) + std::uint64_t(i) * depth;
-    v.sq_doorbell = reinterpret_cast<std::uint32_t*>(bar + sq_doorbell_offset(i));
-    v.cq_doorbell = reinterpret_cast<std::uint32_t*>(bar + cq_doorbell_offset(i));
-    v.depth = depth;
     v.qid = i + 1;  // queue 0 is the admin queue on a real controller
+    v.sq_doorbell = reinterpret_cast<std::uint32_t*>(bar + sq_doorbell_offset(v.qid));
+    v.cq_doorbell = reinterpret_cast<std::uint32_t*>(bar + cq_doorbell_offset(v.qid));
+    v.depth = depth;
     v.nsid = nsid;
     return v;
 }
@@ -214,9 +222,9 @@ QueuePairView EmulatedNvmeController::host_queue(std::uint32_t i) const {
                      static_cast<char*>(bar_mem_.host), i, cfg_.queue_depth, info_.nsid);
 }
 
-Result<std::uint64_t> EmulatedNvmeController::map_dma(void* ptr, std::uint64_t bytes) {
-    if (!ptr || bytes == 0)
-        return Result<std::uint64_t>::Failure({StatusCode::INVALID_ARGUMENT, "empty DMA window"});
+Result<DmaMapping> EmulatedNvmeController::map_dma(void* ptr, std::uint64_t bytes) {
+    using R = Result<DmaMapping>;
+    if (!ptr || bytes == 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "empty DMA window"});
     bool device = false;
     if (cuda_device_ >= 0) {
         cudaPointerAttributes a{};
@@ -224,26 +232,99 @@ Result<std::uint64_t> EmulatedNvmeController::map_dma(void* ptr, std::uint64_t b
             device = a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
         else
             cudaGetLastError();
-        if (device && !info_.device_dma)
-            return Result<std::uint64_t>::Failure(
-                {StatusCode::UNSUPPORTED, "this controller cannot DMA into GPU memory (no stream memory ops)"});
     }
+    auto bus = map_window(ptr, bytes, device);
+    if (!bus.ok()) return R::Failure(bus.status());
+    DmaMapping m;
+    m.va = reinterpret_cast<std::uint64_t>(ptr);
+    m.bytes = bytes;
+    m.bus = {bus.value()};
+    return R(std::move(m));
+}
+
+Status EmulatedNvmeController::unmap_dma(const DmaMapping& m) { return unmap_window(m.va); }
+
+Result<std::uint64_t> EmulatedNvmeController::map_window(void* ptr, std::uint64_t bytes, bool device) {
+    using R = Result<std::uint64_t>;
+    if (!ptr || bytes == 0) return R::Failure({StatusCode::INVALID_ARGUMENT, "empty DMA window"});
+    if (device && !info_.device_dma)
+        return R::Failure({StatusCode::UNSUPPORTED, "this controller cannot DMA into GPU memory (no stream memory ops)"});
     std::lock_guard<std::mutex> g(map_mu_);
     auto next = std::make_shared<std::vector<Window>>(*std::atomic_load(&windows_));
     next->push_back({reinterpret_cast<std::uint64_t>(ptr), bytes, device});
     std::atomic_store(&windows_, std::shared_ptr<const std::vector<Window>>(next));
     // The emulator's IOMMU is the identity: bus address == virtual address.
-    return reinterpret_cast<std::uint64_t>(ptr);
+    return R(reinterpret_cast<std::uint64_t>(ptr));
 }
 
-Status EmulatedNvmeController::unmap_dma(std::uint64_t iova) {
+Status EmulatedNvmeController::unmap_window(std::uint64_t bus) {
     std::lock_guard<std::mutex> g(map_mu_);
     auto next = std::make_shared<std::vector<Window>>(*std::atomic_load(&windows_));
-    auto it = std::find_if(next->begin(), next->end(), [&](const Window& w) { return w.base == iova; });
+    auto it = std::find_if(next->begin(), next->end(), [&](const Window& w) { return w.base == bus; });
     if (it == next->end()) return {StatusCode::NOT_FOUND, "no DMA window at that address"};
     next->erase(it);
     std::atomic_store(&windows_, std::shared_ptr<const std::vector<Window>>(next));
     return Status::Ok();
+}
+
+Status EmulatedNvmeController::apply_queue_change(std::uint32_t i) {
+    QueueState& qs = *qstate_[i];
+    if (workers_.empty()) {
+        // No worker runs (stopped): apply in place.
+        qs.view = qs.pending_view;
+        qs.cq_device = qs.pending_cq_device;
+        qs.enabled = qs.pending_enabled;
+        qs.sq_head = qs.cq_tail = 0;
+        qs.phase = 1;
+        return Status::Ok();
+    }
+    qs.reset_request.store(2, std::memory_order_release);
+    auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(5);
+    while (qs.reset_request.load(std::memory_order_acquire) != 0) {
+        if (std::chrono::steady_clock::now() > deadline)
+            return {StatusCode::TIMEOUT, "queue change not acknowledged by the drive"};
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    return Status::Ok();
+}
+
+Status EmulatedNvmeController::create_io_queue_pair(std::uint32_t qid, void* sq, void* cq, std::uint32_t depth) {
+    if (!cfg_.driver_created_queues) return {StatusCode::UNSUPPORTED, "queues are not driver-created"};
+    if (qid == 0 || qid > qstate_.size()) return {StatusCode::OUT_OF_RANGE, "invalid queue identifier"};
+    if (!sq || !cq) return {StatusCode::INVALID_ARGUMENT, "queue rings are required"};
+    if (depth < 2 || depth > info_.queue_depth) return {StatusCode::INVALID_ARGUMENT, "queue size exceeds CAP.MQES"};
+    QueueState& qs = *qstate_[qid - 1];
+    if (qs.enabled) return {StatusCode::BUSY, "queue identifier in use"};
+    char* bar = static_cast<char*>(bar_mem_.host);
+    QueuePairView v{};
+    v.sq = static_cast<Sqe*>(sq);
+    v.cq = static_cast<const Cqe*>(cq);
+    v.sq_doorbell = reinterpret_cast<std::uint32_t*>(bar + sq_doorbell_offset(qid));
+    v.cq_doorbell = reinterpret_cast<std::uint32_t*>(bar + cq_doorbell_offset(qid));
+    v.depth = depth;
+    v.qid = qid;
+    v.nsid = info_.nsid;
+    void* cq_dev = nullptr;
+    if (cuda_device_ >= 0 && cudaHostGetDevicePointer(&cq_dev, cq, 0) != cudaSuccess) {
+        cudaGetLastError();
+        cq_dev = nullptr;  // not device-mapped: completions are posted by the host
+    }
+    std::memset(cq, 0, std::size_t(depth) * sizeof(Cqe));
+    qs.pending_view = v;
+    qs.pending_cq_device = static_cast<char*>(cq_dev);
+    qs.pending_enabled = true;
+    return apply_queue_change(qid - 1);
+}
+
+Status EmulatedNvmeController::delete_io_queue_pair(std::uint32_t qid) {
+    if (!cfg_.driver_created_queues) return {StatusCode::UNSUPPORTED, "queues are not driver-created"};
+    if (qid == 0 || qid > qstate_.size()) return {StatusCode::OUT_OF_RANGE, "invalid queue identifier"};
+    QueueState& qs = *qstate_[qid - 1];
+    if (!qs.enabled) return {StatusCode::NOT_FOUND, "queue identifier not in use"};
+    qs.pending_view = QueuePairView{};
+    qs.pending_cq_device = nullptr;
+    qs.pending_enabled = false;
+    return apply_queue_change(qid - 1);
 }
 
 Status EmulatedNvmeController::reset_queue(std::uint32_t i) {
@@ -709,26 +790,34 @@ std::uint32_t EmulatedNvmeController::execute(const Sqe& sqe, WorkerCtx& w, bool
 
 bool EmulatedNvmeController::service_queue(std::uint32_t q, WorkerCtx& w) {
     QueueState& qs = *qstate_[q];
-    QueuePairView v = host_queue(q);
     auto drain_stream = [&] {
         if (w.stream_dirty) {
             w.stream_dirty = false;
             if (cudaStreamSynchronize(w.stream) != cudaSuccess) cudaGetLastError();
         }
     };
-    if (qs.reset_request.load(std::memory_order_acquire)) {
+    if (const std::uint32_t req = qs.reset_request.load(std::memory_order_acquire)) {
         drain_stream();  // no CQE write of this queue may land after the reset
         qs.sq_head = 0;
         qs.cq_tail = 0;
         qs.phase = 1;
-        std::memset(const_cast<Cqe*>(v.cq), 0, sizeof(Cqe) * v.depth);
-        store_release(v.sq_doorbell, 0);
-        store_release(v.cq_doorbell, 0);
+        if (req == 2) {  // a driver created or deleted the queue pair
+            qs.view = qs.pending_view;
+            qs.cq_device = qs.pending_cq_device;
+            qs.enabled = qs.pending_enabled;
+        }
+        if (qs.enabled) {
+            const QueuePairView& v = qs.view;
+            std::memset(const_cast<Cqe*>(v.cq), 0, sizeof(Cqe) * v.depth);
+            store_release(v.sq_doorbell, 0);
+            store_release(v.cq_doorbell, 0);
+        }
         qs.fatal.store(0);
         qs.reset_request.store(0, std::memory_order_release);
         return true;
     }
-    if (qs.fatal.load(std::memory_order_relaxed)) return false;
+    if (!qs.enabled || qs.fatal.load(std::memory_order_relaxed)) return false;
+    const QueuePairView v = qs.view;
     std::uint32_t tail = load_acquire(v.sq_doorbell);
     if (tail >= v.depth) {
         qs.fatal.store(1);  // protocol violation: invalid doorbell value
@@ -759,10 +848,10 @@ bool EmulatedNvmeController::service_queue(std::uint32_t q, WorkerCtx& w) {
         slot->dw2 = (qs.sq_head & 0xFFFFu) | ((v.qid & 0xFFFFu) << 16);
         const std::uint32_t dw3 = make_cqe_dw3(sqe_cid(sqe), qs.phase, status);
         bool posted = false;
-        if (on_stream && status == 0) {
+        if (on_stream && status == 0 && qs.cq_device) {
             // After the copies on the same stream: the completion follows the data.
-            const std::uint64_t dev_dw3 = reinterpret_cast<std::uint64_t>(cq_mem_.device) +
-                                          (std::uint64_t(q) * v.depth + qs.cq_tail) * sizeof(Cqe) + 12;
+            const std::uint64_t dev_dw3 =
+                reinterpret_cast<std::uint64_t>(qs.cq_device) + std::uint64_t(qs.cq_tail) * sizeof(Cqe) + 12;
             posted = write_value32()(reinterpret_cast<CUstream>(w.stream), static_cast<CUdeviceptr>(dev_dw3), dw3,
                                      0) == CUDA_SUCCESS;
         }

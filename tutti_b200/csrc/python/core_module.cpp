@@ -452,6 +452,8 @@ PYBIND11_MODULE(_core, m) {
                      auto s = c->stats();
                      py::dict d;
                      d["name"] = c->info().name;
+                     d["kind"] = c->info().kind;
+                     d["queues"] = c->info().num_io_queues;
                      d["commands"] = s.commands;
                      d["read_bytes"] = s.read_bytes;
                      d["write_bytes"] = s.write_bytes;
@@ -474,7 +476,7 @@ PYBIND11_MODULE(_core, m) {
                std::uint32_t status) {
                 if (device < 0 || device >= static_cast<int>(r.extras.controllers.size()))
                     throw py::index_error("device index");
-                auto* emu = dynamic_cast<nvme::EmulatedNvmeController*>(r.extras.controllers[device].get());
+                auto* emu = r.extras.controllers[device]->emulated_drive();
                 if (!emu) throw py::value_error("injection needs an emulated controller");
                 nvme::InjectKind k = kind == "media_error"     ? nvme::InjectKind::MEDIA_ERROR
                                      : kind == "drop_completion" ? nvme::InjectKind::DROP_COMPLETION
@@ -568,6 +570,10 @@ PYBIND11_MODULE(_core, m) {
                 o.map_reads = how == "mmap";
             }
             if (opts.contains("emulator_media")) o.media = opts["emulator_media"].cast<std::string>();
+            if (opts.contains("nvme_provider")) o.provider = opts["nvme_provider"].cast<std::string>();
+            if (opts.contains("snvme_nodes")) o.snvme_nodes = opts["snvme_nodes"].cast<std::vector<std::string>>();
+            if (opts.contains("snvme_rings_in_gpu_memory"))
+                o.snvme_rings_in_gpu_memory = opts["snvme_rings_in_gpu_memory"].cast<bool>();
             if (opts.contains("image_budget_bytes")) o.image_budget_bytes = opts["image_budget_bytes"].cast<std::uint64_t>();
             if (opts.contains("drive_gbps")) o.drive_gbps = opts["drive_gbps"].cast<double>();
             if (opts.contains("staging")) {

@@ -1,6 +1,8 @@
 #include "presets.h"
 
+#include "../nvme/snvme_client.h"
 #include "../resolvers/file_resolvers.h"
+#include "../testing/fake_snvme.h"
 
 namespace tutti {
 
@@ -21,6 +23,10 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
     }
     if (o.media != "files" && o.media != "memory")
         return R::Failure({StatusCode::INVALID_ARGUMENT, "emulated media must be 'files' or 'memory'"});
+    if (o.provider != "emulated" && o.provider != "snvme" && o.provider != "snvme_fake")
+        return R::Failure({StatusCode::INVALID_ARGUMENT, "provider must be 'emulated', 'snvme' or 'snvme_fake'"});
+    if (o.provider == "snvme" && o.snvme_nodes.size() != ndev)
+        return R::Failure({StatusCode::INVALID_ARGUMENT, "provider 'snvme' needs one snvme node per drive"});
     for (std::size_t i = 0; i < ndev; ++i) {
         nvme::EmulatedControllerConfig c;
         c.media = o.media == "memory" ? nvme::EmulatedControllerConfig::Media::MEMORY
@@ -38,9 +44,34 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
         c.skip_data = o.skip_data;
         c.map_reads = o.map_reads;
         c.idle_spin_iters = o.idle_spin_iters;
-        auto ctl = nvme::EmulatedNvmeController::create(c);
-        if (!ctl.ok()) return R::Failure(ctl.status());
-        std::shared_ptr<nvme::NvmeController> sp(std::move(ctl).value());
+        std::shared_ptr<nvme::NvmeController> sp;
+        if (o.provider == "emulated") {
+            auto ctl = nvme::EmulatedNvmeController::create(c);
+            if (!ctl.ok()) return R::Failure(ctl.status());
+            sp = std::move(ctl).value();
+        } else {
+            nvme::SnvmeControllerConfig sc;
+            sc.num_io_queues = c.num_io_queues;
+            sc.rings_in_gpu_memory = o.snvme_rings_in_gpu_memory;
+            sc.max_command_bytes = o.mdts_bytes;
+            sc.namespace_bytes = c.namespace_bytes;
+            sc.cuda_device = o.accel_id;
+            std::shared_ptr<nvme::SnvmeSys> sys;
+            if (o.provider == "snvme") {
+                sc.node = o.snvme_nodes[i];
+                sys = std::shared_ptr<nvme::SnvmeSys>(&nvme::linux_snvme_sys(), [](nvme::SnvmeSys*) {});
+            } else {
+                testing::FakeSnvmeConfig fc;
+                fc.node = sc.node = "/dev/ssnvme" + std::to_string(i);
+                fc.drive = c;
+                auto fake = testing::FakeSnvmeDriver::create(fc);
+                if (!fake.ok()) return R::Failure(fake.status());
+                sys = std::shared_ptr<nvme::SnvmeSys>(std::move(fake).value());
+            }
+            auto ctl = nvme::SnvmeController::create(sc, std::move(sys));
+            if (!ctl.ok()) return R::Failure(ctl.status());
+            sp = std::move(ctl).value();
+        }
         pr.extras.controllers.push_back(sp);
         devs.push_back({sp, c.name});
     }

@@ -20,7 +20,15 @@ namespace tutti {
 
 struct EmulatedPresetOptions {
     int accel_id = 0;
-    std::vector<std::string> mounts;   // one emulated drive per mount
+    std::vector<std::string> mounts;   // one drive per mount
+    // Which controller answers each mount's queues:
+    //   "emulated":   an EmulatedNvmeController (its own rings and doorbells);
+    //   "snvme":      a real controller through the snvme driver, node snvme_nodes[i];
+    //   "snvme_fake": the snvme client over a fake driver whose hardware is an
+    //                 emulated drive (the real-drive code path without the drive).
+    std::string provider = "emulated";
+    std::vector<std::string> snvme_nodes;
+    bool snvme_rings_in_gpu_memory = false;
     std::uint32_t queues = 0;          // 0: = leases
     std::uint32_t queue_depth = 256;
     std::uint32_t mdts_bytes = 1u << 20;

@@ -150,7 +150,7 @@ Status TuttiRuntime::shutdown(std::uint64_t timeout_ms) {
     gpu_path.reset();
     posix_path.reset();
     for (auto& c : controllers)
-        if (auto* e = dynamic_cast<nvme::EmulatedNvmeController*>(c.get())) e->stop();
+        if (auto* e = c->emulated_drive()) e->stop();
     controllers.clear();
     if (lease) {
         Status s = lease->release();

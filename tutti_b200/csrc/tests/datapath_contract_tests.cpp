@@ -182,8 +182,8 @@ struct Drive {
         (void)!posix_memalign(&buf, 4096, 4u << 20);
         (void)!posix_memalign(&lists, 4096, 16 * 4096);
         std::memset(buf, 0, 4u << 20);
-        iova = ctl->map_dma(buf, 4u << 20).value();
-        list_iova = ctl->map_dma(lists, 16 * 4096).value();
+        iova = ctl->map_dma(buf, 4u << 20).value().bus_at(buf);
+        list_iova = ctl->map_dma(lists, 16 * 4096).value().bus_at(lists);
     }
     ~Drive() {
         ctl->stop();

@@ -370,8 +370,8 @@ void controller_roundtrip(bool direct_io, bool map_reads = false, bool memory_me
     void* buf = nullptr;
     void* lst = nullptr;
     CHECK(posix_memalign(&buf, 4096, 256 << 10) == 0 && posix_memalign(&lst, 4096, 4096) == 0);
-    auto iova = c.map_dma(buf, 256 << 10);
-    auto liova = c.map_dma(lst, 4096);
+    auto iova = c.map_window(buf, 256 << 10, false);
+    auto liova = c.map_window(lst, 4096, false);
     CHECK(iova.ok() && liova.ok());
     HostSubmitter hs{c.host_queue(0)};
     // 8 KiB read: PRP1 + PRP2 page
