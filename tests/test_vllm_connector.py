@@ -310,3 +310,91 @@ def test_tutti_geometry_keys_are_checked():
     with pytest.raises(ValueError):
         ConnectorConfig.from_extra({"store": {"type": "tutti_nvme", "options": {"segment_header_bytes": 100}}})
     assert ConnectorConfig.from_extra({"store": {"options": {"segment_header_bytes": 8192}}}).segment_header_bytes == 8192
+
+
+class _SaveGate:
+    """A save's completion whose device work finishes when the test says so."""
+
+    def __init__(self):
+        self.done = False
+        self.waited_before_done = False
+
+    def query(self):
+        return self.done
+
+    def wait(self):
+        if not self.done:  # a real completion would block here until the write finished
+            self.waited_before_done = True
+            self.done = True
+
+
+class _SaveEngine:
+    staged = True  # no CUDA event on a CPU host
+
+    def __init__(self):
+        self.gates = []
+        self.index = SimpleNamespace(is_resident=lambda k: False)
+
+    def store_chunks(self, keys, block_table, after=None):
+        g = _SaveGate()
+        self.gates.append(g)
+        return g
+
+
+def _saving_worker(max_inflight=64):
+    w = WorkerSide(lambda t: None, block_size=BS, chunk_tokens=CHUNK, max_inflight_saves=max_inflight)
+    w.engine = _SaveEngine()
+    return w
+
+
+def test_worker_step_does_not_wait_for_its_own_saves():
+    w = _saving_worker()
+    keys = [b"s" * 16, b"t" * 16]
+    wm = w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, [0, 1, 2, 3])]))
+    gate = w.engine.gates[0]
+    assert not gate.waited_before_done and wm.committed == {} and w.saves_in_flight() == 1
+    # the request finished, but its blocks are held until the save settles
+    assert w.get_finished({"a"}) == (None, None)
+    gate.done = True  # the write finished on the device
+    wm = w.wait_for_save(TuttiConnectorMetadata(2, [], []))
+    assert wm.committed == {keys[0]: 1, keys[1]: 1} and w.saves_in_flight() == 0
+    assert w.get_finished(set()) == ({"a"}, None)
+    assert w.get_finished(set()) == (None, None)  # reported once
+
+
+def test_worker_saves_settle_from_get_finished_and_in_any_order():
+    w = _saving_worker()
+    w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", [b"a" * 16], [0, 1]),
+                                                   SaveSpec("b", [b"b" * 16], [2, 3])]))
+    ga, gb = w.engine.gates
+    gb.done = True
+    assert w.get_finished({"a", "b"}) == ({"b"}, None)  # b settled, a still in flight
+    ga.done = True
+    assert w.get_finished(set()) == ({"a"}, None)
+    assert not ga.waited_before_done and not gb.waited_before_done
+
+
+def test_worker_back_pressure_waits_for_the_oldest_save_only():
+    w = _saving_worker(max_inflight=2)
+    for i in range(3):
+        w.wait_for_save(TuttiConnectorMetadata(i + 1, [], [SaveSpec(f"r{i}", [bytes([i]) * 16], [0, 1])]))
+    g0, g1, g2 = w.engine.gates
+    assert g0.waited_before_done and not g1.waited_before_done and not g2.waited_before_done
+    assert w.saves_in_flight() == 2
+    w.engine.wait_idle = lambda: None
+    w.engine.store = SimpleNamespace()
+    w.shutdown()  # settles everything still in flight
+    assert w.saves_in_flight() == 0 and g2.done
+
+
+def test_scheduler_holds_blocks_of_finished_requests_with_saves():
+    s = SchedulerSide(BS, CHUNK, capacity_chunks=64)
+    for rid in ("a", "b"):
+        r = req(rid, 17 if rid == "a" else 5, base=100 if rid == "b" else 0)
+        s.get_num_new_matched_tokens(r, 0)
+        s.update_state_after_alloc(r, list(range(10, 15)), 0)
+    meta = s.build_meta([("a", list(range(10, 15)), 0, 17), ("b", list(range(20, 22)), 0, 5)])
+    assert [sp.request_id for sp in meta.saves] == ["a"]  # b has no full chunk
+    assert s.request_finished("a") is True  # its blocks wait for the workers' finished_sending
+    assert s.request_finished("b") is False
+    assert s.request_finished("a") is False  # already released

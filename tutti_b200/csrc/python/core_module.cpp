@@ -453,6 +453,7 @@ PYBIND11_MODULE(_core, m) {
                      py::dict d;
                      d["name"] = c->info().name;
                      d["kind"] = c->info().kind;
+                     d["emulated"] = c->emulated_drive() != nullptr;  // the drive's DMA runs in this process
                      d["queues"] = c->info().num_io_queues;
                      d["commands"] = s.commands;
                      d["read_bytes"] = s.read_bytes;

@@ -98,6 +98,9 @@ class LayerwiseReadPlan:
             for li, layer in enumerate(self.layers):
                 if self._closed:
                     break
+                # at most `window` layers in flight (queue leases are shared)
+                if li >= self.window:
+                    self._comps[li - self.window].wait()
                 with nvtx_range(f"tutti.layer_load|layer={layer}|chunks={len(self.keys)}"):
                     comp = store.get_paged(self.keys, self.block_table, layers=[layer], stream=self.io_stream)
                 ev = torch.cuda.Event(enable_timing=True)
@@ -107,9 +110,6 @@ class LayerwiseReadPlan:
                     self._comp_of[layer] = comp
                     self._events[layer] = ev
                     self._cv.notify_all()
-                # bound the layers in flight (queue leases are shared)
-                if li >= self.window:
-                    self._comps[li - self.window].wait()
         except BaseException as e:  # noqa: BLE001 - surfaced by wait_layer / finish
             with self._cv:
                 self._error = e
@@ -129,7 +129,13 @@ class LayerwiseReadPlan:
             ev = self._events[layer]
             comp = self._comp_of.get(layer)
         with nvtx_range(f"tutti.layer_wait|layer={layer}"):
-            if comp is not None and hasattr(comp, "enqueue_wait"):
+            if comp is not None and self.engine.host_gated_layer_waits:
+                try:
+                    comp.wait()  # the host waits; the stream then waits on a finished event
+                except Exception as e:  # noqa: BLE001 - surfaced like a feeder failure
+                    raise LoadGateError(f"restore of layer {layer} failed: {e}") from e
+                torch.cuda.current_stream().wait_event(ev)
+            elif comp is not None and hasattr(comp, "enqueue_wait"):
                 # device-side wait on the restore itself; with split completion this
                 # launches the drain here, on the consumer's stream
                 comp.enqueue_wait(torch.cuda.current_stream())
@@ -334,6 +340,33 @@ class KVEngine:
             return _WholeRestorePlan(self.load(keys, block_table, layers))  # host pool: no streams to overlap
         self.stats["read_chunks"] += len(keys)
         return LayerwiseReadPlan(self, keys, self._table(block_table), layers, self.io_stream, window)
+
+    @property
+    def host_gated_layer_waits(self) -> bool:
+        """Layer waits block the host instead of the consumer stream.
+
+        Needed when the drives' DMA runs in this process (emulated drives that
+        copy into HBM staging on their own CUDA streams): a consumer stream
+        waiting on a restore's event sits at the head of a hardware queue, and a
+        drive stream that shares that queue could not issue the very copies the
+        wait is for until the restore's deadline expired. Real drives DMA on
+        their own, and then the wait stays on the device.
+        ``TUTTI_LAYER_WAIT=host|device`` overrides.
+        """
+        forced = (text("TUTTI_LAYER_WAIT") or "").strip().lower()
+        if forced in ("host", "device"):
+            return forced == "host"
+        cached = getattr(self, "_host_gated", None)
+        if cached is None:
+            rt = getattr(self.store, "runtime", None)
+            cached = False
+            try:
+                if rt is not None and rt.staging_on_device():
+                    cached = any(c.get("emulated") for c in rt.controller_stats())
+            except (AttributeError, RuntimeError):
+                cached = False
+            self._host_gated = cached
+        return cached
 
     @property
     def split_completion(self) -> bool:

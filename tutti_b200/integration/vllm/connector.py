@@ -78,7 +78,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                       tp_rank=rank, tp_size=world, consensus=TpFailureConsensus(cpu_group, self.cfg.failure_timeout_s),
                                       # vLLM's scheduler applies kv_load_failure_policy (recompute or fail the
                                       # requests) to the blocks the worker reports; the worker only reports
-                                      failure_policy="recompute", lookahead=self.cfg.lookahead_k)
+                                      failure_policy="recompute", lookahead=self.cfg.lookahead_k,
+                                      max_inflight_saves=self.cfg.max_inflight_saves)
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""
@@ -141,8 +142,9 @@ class TuttiConnectorV1(KVConnectorBase_V1):
         self._sched.update_from_workers(wm if isinstance(wm, TuttiWorkerMetadata) else None, received)
 
     def request_finished(self, request, block_ids: list[int]) -> tuple[bool, dict[str, Any] | None]:
-        self._sched.request_finished(request.request_id)
-        return False, None
+        # a request whose chunks are being saved keeps its blocks until every
+        # worker reports it in finished_sending (saves run behind the step)
+        return self._sched.request_finished(request.request_id), None
 
     # ---------------- worker role ----------------
     def register_kv_caches(self, kv_caches) -> None:

@@ -10,6 +10,7 @@
   max_tokens_per_load      cap on the tokens one request loads at once (default 0: no cap)
   failure_collective_timeout_s  TP failure-consensus timeout (default 30)
   lookahead_k              layers a synchronous load reads ahead of attention (default 4)
+  max_inflight_saves       saves a worker keeps in flight behind the steps (default 64)
   num_layers, chunk_kv_bytes, segment_bytes   optional; checked against vLLM's KV caches
   physical_chunk_tokens    must equal chunk_tokens (one object per chunk)
   direct_transfer          true: refuse a store that moves chunks through staging buffers
@@ -83,6 +84,7 @@ class ConnectorConfig:
     max_tokens_per_load: int = 0
     failure_timeout_s: float = 30.0
     lookahead_k: int = 4  # layers restored ahead of the layer attention is waiting for
+    max_inflight_saves: int = 64  # saves in flight per worker before a step waits for the oldest
     expect: dict = field(default_factory=dict)  # num_layers / chunk_kv_bytes / segment_bytes given in the config
     direct_transfer: bool = False  # require the direct (paged) path
     segment_header_bytes: int = 0  # 0: the store's default
@@ -92,6 +94,7 @@ class ConnectorConfig:
         extra = dict(extra or {})
         known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio",
                  "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s", "lookahead_k",
+                 "max_inflight_saves",
                  # Tutti's keys for facts derived here from vLLM's tensors (checked, not required)
                  "num_layers", "chunk_kv_bytes", "segment_bytes", "physical_chunk_tokens",
                  "direct_transfer", "max_chunks_per_wave", "replica_io"}
@@ -119,6 +122,10 @@ class ConnectorConfig:
         c.lookahead_k = extra.get("lookahead_k", c.lookahead_k)
         if not isinstance(c.lookahead_k, int) or isinstance(c.lookahead_k, bool) or c.lookahead_k <= 0:
             raise ValueError(f"lookahead_k must be a positive integer, got {c.lookahead_k!r}")
+        c.max_inflight_saves = extra.get("max_inflight_saves", c.max_inflight_saves)
+        if not isinstance(c.max_inflight_saves, int) or isinstance(c.max_inflight_saves, bool) or \
+                c.max_inflight_saves <= 0:
+            raise ValueError(f"max_inflight_saves must be a positive integer, got {c.max_inflight_saves!r}")
         if c.min_retrieve_tokens < 0 or c.max_tokens_per_load < 0 or c.failure_timeout_s <= 0:
             raise ValueError("min_retrieve_tokens and max_tokens_per_load must be >= 0, the timeout > 0")
         from .load_policy import MODES, free_ratio_setting

@@ -73,6 +73,7 @@ class SchedulerSide:
         self.requests: dict[str, _RequestState] = {}
         self.generation = 0
         self._planned: dict[bytes, str] = {}  # pending saves: key -> request
+        self._saving_requests: set[str] = set()  # requests that had a save (their blocks wait for it)
         self.total_blocks = total_blocks  # vLLM's KV pool size, when known
         self.min_retrieve_tokens = min_retrieve_tokens  # shorter hits are computed instead
         self.max_tokens_per_load = max_tokens_per_load  # 0: no cap
@@ -209,6 +210,7 @@ class SchedulerSide:
             for k in plan.new_keys:
                 self._planned[k] = req_id
             meta.saves.append(SaveSpec(req_id, list(plan.new_keys), blocks))
+            self._saving_requests.add(req_id)
         return meta
 
     def update_from_workers(self, wm: TuttiWorkerMetadata | None, finished_recving=()) -> list[bytes]:
@@ -249,9 +251,15 @@ class SchedulerSide:
         if not ok:
             self.index.forget(keys[max(0, first_failed_token) // self.chunk_tokens:])
 
-    def request_finished(self, request_id: str) -> None:
+    def request_finished(self, request_id: str) -> bool:
+        """Forget the request; True when its blocks must wait for the workers' saves of it
+        (every worker reports it in ``finished_sending`` once they settled)."""
         self.requests.pop(request_id, None)
         self._live.pop(request_id, None)
+        if request_id in self._saving_requests:
+            self._saving_requests.discard(request_id)
+            return True
+        return False
 
     def maybe_log(self, force: bool = False) -> bool:
         """``[tutti] index-profile`` and ``[tutti] load-policy`` lines, at most once per interval."""

@@ -7,8 +7,16 @@
   are submitted as whole-prefix restores and reported by ``get_finished``.
 * ``wait_for_layer_load``: device-side wait of the current stream on layer l.
 * ``wait_for_save``: settles the loads (TP failure consensus: every rank
-  agrees on the failed chunk range), then persists this step's new full
-  chunks behind the forward's compute event and reports them committed.
+  agrees on the failed chunk range), then queues this step's new full chunks
+  for persisting behind the forward's compute event and returns: the step
+  does not wait for its saves. Saves that finished since (checked without
+  blocking here and in ``get_finished``) are committed then (payload, then
+  header) and reported committed in that step's metadata. At most
+  ``max_inflight_saves`` saves stay in flight; beyond that the oldest is
+  waited for (back-pressure).
+* ``get_finished``: finished asynchronous loads (``finished_recving``), and
+  finished requests whose saves have all settled (``finished_sending``): the
+  scheduler keeps the blocks of a request that had saves until then.
 * Measurements for the scheduler's load policy, harvested without blocking
   (a sample whose events have not completed waits for a later step):
   ``read_samples`` (chunks, device ms) of finished restores and
@@ -22,6 +30,7 @@ from __future__ import annotations
 import logging
 import re
 import time
+from collections import deque
 from typing import Callable
 
 import numpy as np
@@ -113,7 +122,7 @@ class WorkerSide:
     def __init__(self, make_engine: Callable[..., KVEngine], *, block_size: int,
                  chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
                  consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute",
-                 lookahead: int = 4):
+                 lookahead: int = 4, max_inflight_saves: int = 64):
         if failure_policy not in ("recompute", "fail"):
             raise ValueError("kv_load_failure_policy must be recompute or fail")
         self.make_engine = make_engine
@@ -137,6 +146,11 @@ class WorkerSide:
         self._read_timing: list[tuple[int, object]] = []  # (chunks, plan or completion with read_ms())
         self._step_timing: list[tuple[object, object, int]] = []  # (start, end, tokens) of steps w/o sync reads
         self._step: tuple[object, int, bool] | None = None  # this step's start event, tokens, had sync loads
+        self.max_inflight_saves = max(1, int(max_inflight_saves))
+        self._saves: deque = deque()  # (SaveSpec, completion) in submission order
+        self._saves_of: dict[str, int] = {}  # request id -> saves in flight on this rank
+        self._had_saves: set[str] = set()  # requests with a save on this rank (their blocks wait for it)
+        self._finishing: set[str] = set()  # finished requests whose saves are still in flight
 
     # -- binding --------------------------------------------------------------
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
@@ -258,30 +272,66 @@ class WorkerSide:
             ev = torch.cuda.Event() if torch.cuda.is_available() and not self.engine.staged else None
             if ev is not None:
                 ev.record()
-            comps = []
             for spec in meta.saves:
+                self._had_saves.add(spec.request_id)
                 comp = self.engine.store_chunks(spec.keys, np.asarray(spec.block_ids, dtype=np.int64), after=ev)
-                comps.append((spec, comp))
-            for spec, comp in comps:
-                if comp is None:
+                if comp is None:  # nothing new to write: resident chunks count as committed
+                    self._count_resident(spec.keys)
                     continue
-                try:
-                    comp.wait()
-                except Exception as e:  # noqa: BLE001 - a failed save only costs a future recompute
-                    LOG.warning("save of %d chunk(s) for %s failed: %s", len(spec.keys), spec.request_id, e)
-                    continue
-                for k in spec.keys:
-                    self._meta.committed[k] = self._meta.committed.get(k, 0) + 1
-            # chunks already resident in this rank's store count as committed too
-            for spec in meta.saves:
-                for k in spec.keys:
-                    if k not in self._meta.committed and self.engine.index.is_resident(k):
-                        self._meta.committed[k] = 1
+                self._saves.append((spec, comp))
+                self._saves_of[spec.request_id] = self._saves_of.get(spec.request_id, 0) + 1
+            while len(self._saves) > self.max_inflight_saves:
+                self._settle_save(*self._saves.popleft())
+        self._harvest_saves()
         self._harvest_samples()
         return self._meta
 
+    def _count_resident(self, keys) -> None:
+        for k in keys:
+            if k not in self._meta.committed and self.engine.index.is_resident(k):
+                self._meta.committed[k] = 1
+
+    def _settle_save(self, spec, comp) -> None:
+        """Wait for (or collect) one save, commit it and count its chunks in this step's metadata."""
+        try:
+            comp.wait()
+        except Exception as e:  # noqa: BLE001 - a failed save only costs a future recompute
+            LOG.warning("save of %d chunk(s) for %s failed: %s", len(spec.keys), spec.request_id, e)
+        else:
+            for k in spec.keys:
+                self._meta.committed[k] = self._meta.committed.get(k, 0) + 1
+        self._count_resident(spec.keys)  # chunks another save made resident meanwhile
+        left = self._saves_of.get(spec.request_id, 1) - 1
+        if left > 0:
+            self._saves_of[spec.request_id] = left
+        else:
+            self._saves_of.pop(spec.request_id, None)
+
+    def _harvest_saves(self) -> None:
+        """Commit the saves whose device work has finished; never blocks on one in flight."""
+        if not self._saves:
+            return
+        pending = deque()
+        for spec, comp in self._saves:
+            if comp.query():
+                self._settle_save(spec, comp)
+            else:
+                pending.append((spec, comp))
+        self._saves = pending
+
+    def saves_in_flight(self) -> int:
+        return len(self._saves)
+
     # -- completion reporting -------------------------------------------------
     def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
+        # finished requests hold their blocks until this rank's saves of them settled
+        for rid in finished_req_ids or ():
+            if rid in self._had_saves:
+                self._finishing.add(rid)
+        self._harvest_saves()
+        sending = {rid for rid in self._finishing if rid not in self._saves_of}
+        self._finishing -= sending
+        self._had_saves -= sending
         done = set()
         for rid, (comp, spec, t0) in list(self._async.items()):
             if comp.query():
@@ -294,13 +344,15 @@ class WorkerSide:
                     self._meta.failed_loads[rid] = 0
                 done.add(rid)
                 del self._async[rid]
-        return None, (done or None)
+        return (sending or None), (done or None)
 
     def get_block_ids_with_load_errors(self) -> set[int]:
         out, self._load_error_blocks = self._load_error_blocks, set()
         return out
 
     def shutdown(self) -> None:
+        while self._saves:
+            self._settle_save(*self._saves.popleft())
         for comp, _, _ in self._async.values():
             try:
                 comp.wait()

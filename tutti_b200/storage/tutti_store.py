@@ -86,6 +86,8 @@ class NativeCompletion:
         # enqueue_wait may race a host wait on another thread (e.g. a feeder's
         # window bound): handles are released, and _done set, only under this lock
         self._mu = threading.Lock()
+        self._wait_mu = threading.Lock()
+        self._error: StoreIOError | None = None
 
     def query(self) -> bool:
         if self._done:
@@ -104,8 +106,21 @@ class NativeCompletion:
             self._rt.enqueue_wait(self._ios, s.cuda_stream)
 
     def wait(self, timeout_ms: int = 600_000) -> None:
-        if self._done:
-            return
+        # Waiters on several threads (a feeder's window bound, a layer wait) are
+        # serialised: the first settles the IOs, the others see its outcome.
+        with self._wait_mu:
+            if self._done:
+                if self._error is not None:
+                    raise self._error
+                return
+            try:
+                self._wait_locked(timeout_ms)
+            except StoreIOError as e:
+                if self._done:
+                    self._error = e
+                raise
+
+    def _wait_locked(self, timeout_ms: int) -> None:
         failed: list[int] = []
         kinds = set()
         results = []
