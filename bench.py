@@ -60,6 +60,10 @@ def parse():
     p.add_argument("--async-completion", action="store_true",
                    help="split submit/drain: the drain starts once the drives have posted every CQE")
     p.add_argument("--inflight", type=int, default=2, help="restores submitted ahead")
+    p.add_argument("--direct-reads", action="store_true",
+                   help="drives DMA each read straight into the pool pages (no staging, no movers)")
+    p.add_argument("--provider", choices=["emulated", "snvme_fake"], default="emulated",
+                   help="controller provider: emulated drives, or the snvme client over a fake driver")
     p.add_argument("--emulator-skip-data", action="store_true", help="diagnostic: controllers move no data")
     p.add_argument("--staging-wc", action="store_true", help="write-combined staging slots")
     p.add_argument("--idle-spins", type=int, default=0,
@@ -476,7 +480,8 @@ def main():
             "async_completion": bool(args.async_completion), "async_fallback_us": 500000, "queue_depth": 1024,
             "max_ctas_per_op": ctas, "slots_per_lease": args.slots, "slot_bytes": 1 << 20, "mdts_bytes": 1 << 20, "timing": bool(args.timing),
             "emulator_skip_data": bool(args.emulator_skip_data), "emulator_reads": args.emulator_reads,
-            "staging_write_combined": bool(args.staging_wc), "emulator_idle_spins": idle_spins}
+            "staging_write_combined": bool(args.staging_wc), "emulator_idle_spins": idle_spins,
+            "direct_reads": bool(args.direct_reads), "nvme_provider": args.provider}
     backend = "nvme-gpu" if args.impl == "tutti" else "posix"
     if backend == "posix":
         opts = {"threads": max(4, ncpu // max(1, world)), "direct_io": bool(args.direct_io)}
@@ -640,6 +645,7 @@ def main():
                        "drive_gbps_cap": args.drive_gbps or None, "ctas": ctas, "slots": args.slots,
                        "controller_threads": threads, "impl": args.impl, "inflight": args.inflight,
                        "async_completion": bool(args.async_completion),
+                       "direct_reads": bool(args.direct_reads), "provider": args.provider,
                        "emulator_reads": args.emulator_reads, "staging_write_combined": bool(args.staging_wc),
                        "emulator_idle_spins": idle_spins,
                        "l2": "inputs (4.29 GB/step) larger than L2"},

@@ -92,6 +92,43 @@ def test_restore_through_the_snvme_client_over_a_fake_driver(tmp_path, media):
         st.close()
 
 
+@pytest.mark.parametrize("provider", ["emulated", "snvme_fake"])
+def test_direct_reads_land_in_the_pool_pages(tmp_path, provider):
+    """With direct reads the drives DMA each read straight into the pool's
+    pages (PRPs built by the io kernel from the pool's bus addresses): one
+    copy per contiguous destination run instead of one per staged command."""
+    copies = {}
+    for direct in (False, True):
+        root = tmp_path / f"d{int(direct)}"
+        st = make(root, drives=2, media="memory", nvme_provider=provider, direct_reads=direct)
+        try:
+            nb = 512
+            pool = torch.randn(G.pool_shape(nb), dtype=torch.bfloat16, device="cuda")
+            assert pool.data_ptr() % 4096 == 0
+            st.register_pool(pool)
+            n = 16
+            keys = chunk_keys_for_tokens(list(range(n * 64)), 64, namespace=b"dr")
+            rng = np.random.default_rng(7)
+            src = rng.permutation(nb)[: n * 4].reshape(n, 4)
+            st.put_paged(keys, src).wait()
+            ref = pool[:, :, torch.from_numpy(src.reshape(-1)).cuda()].clone()
+            before = sum(s["dma_copies"] for s in st.runtime.controller_stats())
+            dst = rng.permutation(nb)[: n * 4].reshape(n, 4)
+            pool.zero_()
+            st.get_paged(keys, dst).wait()
+            assert torch.equal(pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()], ref)
+            # a layer subset goes the same way
+            pool.zero_()
+            st.get_paged(keys, dst, layers=[1]).wait()
+            got = pool[:, :, torch.from_numpy(dst.reshape(-1)).cuda()]
+            assert torch.equal(got[1], ref[1]) and torch.count_nonzero(got[0]) == 0
+            copies[direct] = sum(s["dma_copies"] for s in st.runtime.controller_stats()) - before
+        finally:
+            st.close()
+    # staged: about one copy per command; direct: one per destination block plane
+    assert copies[True] > 2 * copies[False]
+
+
 def test_layer_subset_restore(tmp_path, media):
     st = make(tmp_path, media=media)
     try:

@@ -73,4 +73,6 @@ def runtime_option_defaults() -> dict:
     gbps = number("TUTTI_DRIVE_GBPS")
     if gbps:
         out["drive_gbps"] = gbps
+    if flag("TUTTI_DIRECT_READS"):
+        out["direct_reads"] = True
     return out

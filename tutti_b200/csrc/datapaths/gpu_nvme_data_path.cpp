@@ -260,6 +260,29 @@ Status GpuNvmeDataPath::init_device_side() {
     auto* lists = static_cast<std::uint64_t*>(prp_.host);
     for (std::uint64_t i = 0; i < nslots; ++i)
         for (std::uint64_t j = 0; j < pages_per_slot; ++j) lists[i * 512 + j] = page_bus[i * pages_per_slot + j];
+    if (cfg_.direct_reads) {
+        // One PRP-list page per slot for direct commands (the io kernel writes it).
+        auto dl = host_mapped_alloc(nslots * nvme::kMemoryPageBytes);
+        if (!dl.ok()) return dl.status();
+        direct_lists_ = dl.value();
+        if (!direct_lists_.device) return {StatusCode::UNSUPPORTED, "direct reads need device-mapped host memory"};
+        std::vector<std::uint64_t> dbus(nslots);
+        for (std::size_t d = 0; d < devs_.size(); ++d) {
+            auto m = devs_[d].controller->map_dma(direct_lists_.host, direct_lists_.bytes);
+            if (!m.ok()) return m.status();
+            direct_list_maps_.push_back(std::move(m).value());
+            for (std::uint64_t i = 0; i < nslots; ++i) {
+                const std::uint64_t bus =
+                    direct_list_maps_.back().bus_at(static_cast<char*>(direct_lists_.host) + i * nvme::kMemoryPageBytes);
+                if (bus == 0 || (d > 0 && bus != dbus[i]))
+                    return {StatusCode::UNSUPPORTED, "controllers disagree on the bus addresses of the direct PRP lists"};
+                dbus[i] = bus;
+            }
+        }
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_direct_list_bus_, nslots * 8), "cudaMalloc direct lists"));
+        TUTTI_RETURN_IF_ERROR(cuda_status(
+            cudaMemcpy(d_direct_list_bus_, dbus.data(), nslots * 8, cudaMemcpyHostToDevice), "upload direct lists"));
+    }
     TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_page_bus_, page_bus.size() * 8), "cudaMalloc page table"));
     TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&d_list_bus_, list_bus.size() * 8), "cudaMalloc list table"));
     TUTTI_RETURN_IF_ERROR(cuda_status(
@@ -359,6 +382,23 @@ Status GpuNvmeDataPath::shutdown(std::uint64_t) {
     if (d_page_bus_) cudaFree(d_page_bus_);
     if (d_list_bus_) cudaFree(d_list_bus_);
     d_page_bus_ = d_list_bus_ = nullptr;
+    for (auto& kv : direct_regions_) {
+        for (std::size_t d = 0; d < kv.second.maps.size() && d < devs_.size(); ++d)
+            devs_[d].controller->unmap_dma(kv.second.maps[d]);
+        if (kv.second.d_bus) cudaFree(kv.second.d_bus);
+    }
+    direct_regions_.clear();
+    for (void* t : retired_device_tables_) cudaFree(t);
+    retired_device_tables_.clear();
+    if (d_regions_) cudaFree(d_regions_);
+    d_regions_ = nullptr;
+    n_regions_ = 0;
+    for (std::size_t d = 0; d < direct_list_maps_.size() && d < devs_.size(); ++d)
+        devs_[d].controller->unmap_dma(direct_list_maps_[d]);
+    direct_list_maps_.clear();
+    host_mapped_free(direct_lists_);
+    if (d_direct_list_bus_) cudaFree(d_direct_list_bus_);
+    d_direct_list_bus_ = nullptr;
     host_mapped_free(staging_);
     host_mapped_free(prp_);
     if (staging_hbm_) cudaFree(staging_hbm_);
@@ -508,6 +548,15 @@ Result<DataPathMemory> GpuNvmeDataPath::register_memory(const DataPathMemoryView
     }
     std::uint64_t tok = next_token_++;
     memories_[tok] = MemoryRec{tok, static_cast<char*>(v.base), v.size_bytes, v.kind};
+    if (cfg_.direct_reads && initialized_ && v.kind == DataPathMemoryKind::DEVICE &&
+        (v.expected_accel_id < 0 || v.expected_accel_id == cfg_.accel_id)) {
+        // This GPU's own memory: the drives may DMA into it. A region that
+        // cannot be mapped stays registered and is served through staging.
+        Status ms = map_direct_region_locked(tok, static_cast<char*>(v.base), v.size_bytes);
+        if (!ms.ok())
+            std::fprintf(stderr, "[tutti] nvme-gpu accel %d: memory served through staging (%s)\n", cfg_.accel_id,
+                         ms.message().c_str());
+    }
     return DataPathMemory{tok, tok};
 }
 
@@ -516,6 +565,82 @@ Status GpuNvmeDataPath::unregister_memory(DataPathMemory m) {
     auto it = memories_.find(m.token);
     if (it == memories_.end() || it->second.generation != m.generation) return {StatusCode::NOT_FOUND, "unknown memory"};
     memories_.erase(it);
+    if (direct_regions_.count(m.token)) unmap_direct_region_locked(m.token);
+    return Status::Ok();
+}
+
+Status GpuNvmeDataPath::map_direct_region_locked(std::uint64_t token, char* base, std::uint64_t bytes) {
+    DeviceGuard guard(cfg_.accel_id);
+    DirectRegion r;
+    r.base = base;
+    r.bytes = bytes;
+    for (std::size_t d = 0; d < devs_.size(); ++d) {
+        auto m = devs_[d].controller->map_dma(base, bytes);
+        if (!m.ok() || !m.value().covers(base, bytes)) {
+            for (std::size_t k = 0; k < r.maps.size(); ++k) devs_[k].controller->unmap_dma(r.maps[k]);
+            return m.ok() ? Status{StatusCode::INTERNAL, "DMA mapping does not cover the memory"} : m.status();
+        }
+        r.maps.push_back(std::move(m).value());
+        const nvme::DmaMapping& a = r.maps.front();
+        const nvme::DmaMapping& b = r.maps.back();
+        const bool pow2 = a.page_bytes == 0 || (a.page_bytes >= 4096 && (a.page_bytes & (a.page_bytes - 1)) == 0);
+        if (!pow2 || a.va != b.va || a.page_bytes != b.page_bytes || a.bus != b.bus) {
+            for (std::size_t k = 0; k < r.maps.size(); ++k) devs_[k].controller->unmap_dma(r.maps[k]);
+            return {StatusCode::UNSUPPORTED, "controllers disagree on the memory's bus addresses"};
+        }
+    }
+    const nvme::DmaMapping& m = r.maps.front();
+    Status st = cuda_status(cudaMalloc(&r.d_bus, m.bus.size() * 8), "cudaMalloc bus table");
+    if (st.ok())
+        st = cuda_status(cudaMemcpyAsync(r.d_bus, m.bus.data(), m.bus.size() * 8, cudaMemcpyHostToDevice, upload_stream_),
+                         "upload bus table");
+    if (st.ok()) st = cuda_status(cudaStreamSynchronize(upload_stream_), "upload bus table");
+    if (!st.ok()) {
+        for (std::size_t k = 0; k < r.maps.size(); ++k) devs_[k].controller->unmap_dma(r.maps[k]);
+        if (r.d_bus) cudaFree(r.d_bus);
+        return st;
+    }
+    direct_regions_[token] = std::move(r);
+    return publish_regions_locked();
+}
+
+void GpuNvmeDataPath::unmap_direct_region_locked(std::uint64_t token) {
+    auto it = direct_regions_.find(token);
+    if (it == direct_regions_.end()) return;
+    DirectRegion r = std::move(it->second);
+    direct_regions_.erase(it);
+    (void)publish_regions_locked();
+    for (std::size_t d = 0; d < r.maps.size() && d < devs_.size(); ++d) devs_[d].controller->unmap_dma(r.maps[d]);
+    retired_device_tables_.push_back(r.d_bus);  // an op in flight may still hold the old table
+}
+
+Status GpuNvmeDataPath::publish_regions_locked() {
+    // A new device table per change: ops in flight keep reading the one they
+    // were launched with.
+    std::vector<io::DmaRegion> rows;
+    for (const auto& kv : direct_regions_) {
+        const DirectRegion& r = kv.second;
+        const nvme::DmaMapping& m = r.maps.front();
+        io::DmaRegion row{};
+        row.lo = reinterpret_cast<std::uint64_t>(r.base);
+        row.hi = row.lo + r.bytes;
+        row.va = m.va;
+        row.bus = r.d_bus;
+        row.page_shift = m.page_bytes ? static_cast<std::uint32_t>(__builtin_ctzll(m.page_bytes)) : 0u;
+        rows.push_back(row);
+    }
+    std::sort(rows.begin(), rows.end(), [](const io::DmaRegion& a, const io::DmaRegion& b) { return a.lo < b.lo; });
+    io::DmaRegion* table = nullptr;
+    if (!rows.empty()) {
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMalloc(&table, rows.size() * sizeof(io::DmaRegion)), "cudaMalloc regions"));
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaMemcpyAsync(table, rows.data(), rows.size() * sizeof(io::DmaRegion),
+                                                          cudaMemcpyHostToDevice, upload_stream_),
+                                          "upload regions"));
+        TUTTI_RETURN_IF_ERROR(cuda_status(cudaStreamSynchronize(upload_stream_), "upload regions"));
+    }
+    if (d_regions_) retired_device_tables_.push_back(d_regions_);
+    d_regions_ = table;
+    n_regions_ = static_cast<std::uint32_t>(rows.size());
     return Status::Ok();
 }
 
@@ -766,6 +891,10 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
     kp.staging_dev = staging_base();
     kp.page_bus = d_page_bus_;
     kp.list_bus = d_list_bus_;
+    kp.regions = d_regions_;
+    kp.n_regions = n_regions_;
+    kp.direct_lists = direct_lists_.device_as<std::uint64_t>();
+    kp.direct_list_bus = d_direct_list_bus_;
     kp.movers = staging_on_device_ ? io::kMoversBulk : io::kMoversSimt;
     kp.slot_bytes = cfg_.slot_bytes;
     kp.slots_per_lease = cfg_.slots_per_lease;
@@ -1163,6 +1292,10 @@ void GpuNvmeDataPath::noalloc_fill_params(io::IoKernelParams& p) const {
     p.staging_dev = staging_base();
     p.page_bus = d_page_bus_;
     p.list_bus = d_list_bus_;
+    p.regions = d_regions_;
+    p.n_regions = n_regions_;
+    p.direct_lists = direct_lists_.device_as<std::uint64_t>();
+    p.direct_list_bus = d_direct_list_bus_;
     p.movers = staging_on_device_ ? io::kMoversBulk : io::kMoversSimt;
     p.slot_bytes = cfg_.slot_bytes;
     p.slots_per_lease = cfg_.slots_per_lease;

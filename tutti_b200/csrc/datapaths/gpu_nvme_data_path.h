@@ -70,6 +70,13 @@ struct GpuNvmeConfig {
     // largest op in flight: 8 MiB holds a 32k-token Llama-3.1-8B restore.
     std::uint32_t prealloc_arenas = 4;
     std::uint32_t prealloc_arena_bytes = 8u << 20;
+    // Direct reads: device memory registered with this data path is DMA-mapped
+    // on every controller, and a read whose bytes land in whole 4 KiB pages of
+    // it is served by the drive straight into those pages (PRPs built by the io
+    // kernel from the memory's bus addresses); the io kernel moves no data for
+    // it. Other reads (partial pages, fp8 transform, replicas, split
+    // completion) keep the staged path.
+    bool direct_reads = false;
 };
 
 // One row of the device table: a controller and the identity string the
@@ -259,6 +266,27 @@ private:
     // one entry per 4 KiB staging page, one per slot's PRP-list page.
     std::uint64_t* d_page_bus_ = nullptr;
     std::uint64_t* d_list_bus_ = nullptr;
+    // Direct reads: per registered device memory, its mapping on every
+    // controller and the device copy of its bus table; the device region
+    // table the kernels search (a new table per change, the old ones kept
+    // until close since ops in flight may hold them); one PRP-list page per
+    // staging slot for direct commands.
+    struct DirectRegion {
+        char* base = nullptr;
+        std::uint64_t bytes = 0;
+        std::vector<nvme::DmaMapping> maps;  // one per controller
+        std::uint64_t* d_bus = nullptr;
+    };
+    std::unordered_map<std::uint64_t, DirectRegion> direct_regions_;  // memory token ->
+    io::DmaRegion* d_regions_ = nullptr;
+    std::uint32_t n_regions_ = 0;
+    std::vector<void*> retired_device_tables_;
+    HostMappedBuffer direct_lists_;
+    std::vector<nvme::DmaMapping> direct_list_maps_;
+    std::uint64_t* d_direct_list_bus_ = nullptr;
+    Status map_direct_region_locked(std::uint64_t token, char* base, std::uint64_t bytes);
+    void unmap_direct_region_locked(std::uint64_t token);
+    Status publish_regions_locked();
     std::uint32_t lba_ = 512;  // largest LBA size of the device table
 
     std::vector<TargetRec> targets_;

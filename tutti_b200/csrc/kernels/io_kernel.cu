@@ -404,7 +404,64 @@ __device__ bool move_slot_bulk(const IoKernelParams& p, const IoCommand& c, char
     return ok;
 }
 
+// Bus address of [addr, addr + bytes) inside one registered region, 0 if none holds it.
+__device__ std::uint64_t region_bus(const IoKernelParams& p, std::uint64_t addr, std::uint64_t bytes) {
+    int lo = 0, hi = static_cast<int>(p.n_regions) - 1, at = -1;
+    while (lo <= hi) {  // last region starting at or below addr
+        const int mid = (lo + hi) >> 1;
+        if (p.regions[mid].lo <= addr) {
+            at = mid;
+            lo = mid + 1;
+        } else {
+            hi = mid - 1;
+        }
+    }
+    if (at < 0) return 0;
+    const DmaRegion& r = p.regions[at];
+    if (addr >= r.hi || bytes > r.hi - addr) return 0;
+    const std::uint64_t off = addr - r.va;
+    if (r.page_shift == 0) return r.bus[0] + off;
+    const std::uint64_t first = off >> r.page_shift, last = (off + bytes - 1) >> r.page_shift;
+    if (first != last) return 0;  // the range crosses a bus page
+    return r.bus[first] + (off & ((1ull << r.page_shift) - 1));
+}
+
+// Bus address of 4 KiB page `j` of a direct command (its pieces cover the
+// command contiguously in whole pages; checked by fill_direct_list).
+__device__ std::uint64_t direct_page_bus(const IoKernelParams& p, const IoCommand& c, std::uint32_t j) {
+    const IoPiece* pcs = p.pieces + c.first_piece;
+    const std::uint32_t off = j << 12;
+    for (std::uint32_t q = 0; q < c.n_pieces; ++q)
+        if (off >= pcs[q].off && off - pcs[q].off < pcs[q].bytes) return region_bus(p, pcs[q].mem + (off - pcs[q].off), 4096);
+    return 0;
+}
+
+// Decides whether read `c` can be served by drive DMA straight into its
+// destination pages and, if so, writes the bus address of each of its pages
+// into `list` (the slot's direct PRP-list page). Needs: no transform, one
+// destination group, pieces that tile [0, bytes) in order in whole 4 KiB
+// pages at 4 KiB-aligned addresses, each page inside a registered region.
+__device__ bool fill_direct_list(const IoKernelParams& p, const IoCommand& c, std::uint64_t* list) {
+    if (p.n_regions == 0 || p.phase != kPhaseFull || c.opcode != nvme::kOpRead || c.transform != kXformNone ||
+        c.replicas > 1 || (c.bytes & 4095u) != 0 || c.bytes > 512u * 4096u)
+        return false;
+    const IoPiece* pcs = p.pieces + c.first_piece;
+    std::uint32_t next = 0, j = 0;
+    for (std::uint32_t q = 0; q < c.n_pieces; ++q) {
+        const IoPiece pc = pcs[q];
+        if (pc.off != next || (pc.bytes & 4095u) != 0 || (pc.mem & 4095u) != 0) return false;
+        for (std::uint32_t k = 0; k < pc.bytes; k += 4096) {
+            const std::uint64_t bus = region_bus(p, pc.mem + k, 4096);
+            if (bus == 0) return false;
+            list[j++] = bus;
+        }
+        next += pc.bytes;
+    }
+    return next == c.bytes;
+}
+
 struct Shared {
+    bool direct[kMaxSlots];  // the slot's read is DMA'd straight into its destination
     volatile int state[kMaxSlots];
     int cmd[kMaxSlots];
     std::uint32_t pending[kMaxSlots];
@@ -439,17 +496,20 @@ __device__ bool issue_cmd(const IoKernelParams& p, Shared& sh, int ci, int s, st
     if (n == 0) return false;
     const std::uint64_t slot_index = lease_slot0 + s;
     const std::uint64_t* pages = p.page_bus + slot_index * (p.slot_bytes >> 12);
-    const std::uint64_t list_bus = p.list_bus[slot_index];
+    // Direct read: PRPs name the destination pages (list written for this command).
+    const bool direct = p.direct_lists && fill_direct_list(p, c, p.direct_lists + slot_index * 512);
+    const std::uint64_t list_bus = direct ? p.direct_list_bus[slot_index] : p.list_bus[slot_index];
+    sh.direct[s] = direct;
     for (int k = 0; k < n; ++k) {
         const std::uint32_t dv = sub[k].device;
         const DevDevice& d = p.devices[dv];
         const nvme::QueuePairView& q = d.queues[lease];
         const std::uint32_t page0 = sub[k].off >> 12;
-        const std::uint64_t prp1 = pages[page0] + (sub[k].off & 4095u);
+        const std::uint64_t prp1 = (direct ? direct_page_bus(p, c, page0) : pages[page0]) + (sub[k].off & 4095u);
         const std::uint32_t extra = nvme::prp_extra_pages(prp1 & 4095u, sub[k].bytes);
         std::uint64_t prp2 = 0;
         if (extra == 1)
-            prp2 = pages[page0 + 1];
+            prp2 = direct ? direct_page_bus(p, c, page0 + 1) : pages[page0 + 1];
         else if (extra > 1)
             prp2 = list_bus + 8ull * (page0 + 1);
         nvme::Sqe e;
@@ -595,10 +655,10 @@ __device__ void engine_loop(const IoKernelParams& p, Shared& sh, std::uint32_t l
                 const int ci = sh.cmd[s];
                 if (sh.pending[s] == 0) {
                     if (p.timing) p.timing[4ull * ci + 2] = t1;
-                    if (sh.status[s] == 0 && p.cmds[ci].opcode == nvme::kOpRead) {
+                    if (sh.status[s] == 0 && p.cmds[ci].opcode == nvme::kOpRead && !sh.direct[s]) {
                         sh.state[s] = S_READY;
                         push_ready(sh, s, S);
-                    } else {
+                    } else {  // written, failed, or read straight into its destination
                         p.cmd_status[ci] = sh.status[s];
                         if (p.timing) p.timing[4ull * ci + 3] = t1;
                         sh.state[s] = S_FREE;
@@ -716,6 +776,7 @@ __global__ void __launch_bounds__(32 * (1 + kMoverGroups * W), 1) nvme_io_kernel
             sh.state[s] = S_FREE;
             sh.pending[s] = 0;
             sh.cmd[s] = -1;
+            sh.direct[s] = false;
         }
         sh.rq_tail = 0;
         sh.rq_claim = 0;

@@ -121,6 +121,20 @@ enum : std::uint32_t {
 // deadlines (which run from submission). Reads only.
 enum IoPhase : std::uint32_t { kPhaseFull = 0, kPhaseSubmit = 1, kPhaseDrain = 2 };
 
+// A registered memory region the drives may DMA into directly. Addresses in
+// [lo, hi) qualify; byte `off = addr - va` of the mapping (which may start
+// below lo: the driver pins whole pages) has bus address
+// bus[off >> page_shift] + (off & (2^page_shift - 1)), or bus[0] + off when
+// page_shift is 0 (one contiguous bus range).
+struct DmaRegion {  // 48 B
+    std::uint64_t lo;
+    std::uint64_t hi;
+    std::uint64_t va;
+    const std::uint64_t* bus;
+    std::uint32_t page_shift;
+    std::uint32_t pad[3];
+};
+
 struct LeaseCarry {  // one per CTA of a split launch
     int cmd[kMaxSlots];                // -1: slot unused
     std::uint32_t pending[kMaxSlots];  // sub-commands not yet completed
@@ -146,6 +160,17 @@ struct IoKernelParams {
     // PRP-list page. Pages need not be adjacent on the bus.
     const std::uint64_t* page_bus;
     const std::uint64_t* list_bus;
+    // Direct reads: a read whose bytes all land in whole 4 KiB pages of these
+    // regions (sorted by va) gets PRPs that name those pages, so the drive DMAs
+    // into the final memory and no mover touches the data. Its PRP list is
+    // written into direct_lists (one 4 KiB page per slot, device address of
+    // page-locked host memory) whose bus addresses are direct_list_bus.
+    // n_regions == 0: every command is staged.
+    const DmaRegion* regions;
+    std::uint64_t* direct_lists;
+    const std::uint64_t* direct_list_bus;
+    std::uint32_t n_regions;
+    std::uint32_t direct_pad;
     std::uint32_t slot_bytes;     // <= 2 MiB (one PRP-list page per slot)
     std::uint32_t slots_per_lease;
     std::uint64_t timeout_ns;     // per command, from submission

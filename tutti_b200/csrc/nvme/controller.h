@@ -103,6 +103,7 @@ struct BackingRange {
 
 struct ControllerStats {
     std::uint64_t dma_copies = 0;  // copy-engine transfers issued for GPU-memory PRPs
+    std::uint64_t green_streams = 0;  // worker streams in the drives' own (green) context
     std::uint64_t image_bytes = 0; // memory media: bytes of the image loaded so far
     std::uint64_t load_ns = 0;     // time spent loading image chunks from the files
     std::uint64_t file_ns = 0;     // time spent in pread/pwrite of the backing files
@@ -313,6 +314,7 @@ private:
 
     std::atomic<std::uint64_t> st_commands_{0}, st_read_{0}, st_write_{0}, st_errors_{0}, st_injected_{0};
     std::atomic<std::uint64_t> st_dma_copies_{0};
+    std::atomic<std::uint64_t> st_green_streams_{0};
 };
 
 }  // namespace nvme

@@ -32,6 +32,7 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 namespace tutti {
 namespace nvme {
@@ -44,6 +45,89 @@ std::uint64_t now_ns() {
     return static_cast<std::uint64_t>(
         std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch())
             .count());
+}
+
+// The drives' CUDA streams live in a context of their own: a green context
+// over the whole device, which shares the application's address space (copies
+// reach its HBM) but not its hardware queues. On a queue shared with the
+// application, a drive stream sits behind any stream-ordered wait the
+// application queued there (a kernel queued behind a running io kernel, an
+// event wait on a restore) until the io deadline frees it, since that wait
+// depends on the drive's own copies: measured in a layerwise restore, where
+// every command of a layer timed out. Driver entry points are looked up
+// through the runtime (no libcuda link). TUTTI_EMULATOR_STREAMS=plain keeps
+// them in the application's context.
+struct GreenDriveStreams {
+    using DeviceGet = CUresult (*)(CUdevice*, int);
+    using GetResource = CUresult (*)(CUdevice, CUdevResource*, CUdevResourceType);
+    using GenerateDesc = CUresult (*)(CUdevResourceDesc*, CUdevResource*, unsigned int);
+    using CtxCreate = CUresult (*)(CUgreenCtx*, CUdevResourceDesc, CUdevice, unsigned int);
+    using StreamCreate = CUresult (*)(CUstream*, CUgreenCtx, unsigned int, int);
+    DeviceGet device_get = nullptr;
+    GetResource get_resource = nullptr;
+    GenerateDesc generate_desc = nullptr;
+    CtxCreate ctx_create = nullptr;
+    StreamCreate stream_create = nullptr;
+    std::mutex mu;
+    std::vector<std::pair<int, CUgreenCtx>> ctx_of_device;
+
+    template <typename F>
+    static F lookup(const char* name) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<F>(p);
+    }
+    GreenDriveStreams() {
+        device_get = lookup<DeviceGet>("cuDeviceGet");
+        get_resource = lookup<GetResource>("cuDeviceGetDevResource");
+        generate_desc = lookup<GenerateDesc>("cuDevResourceGenerateDesc");
+        ctx_create = lookup<CtxCreate>("cuGreenCtxCreate");
+        stream_create = lookup<StreamCreate>("cuGreenCtxStreamCreate");
+    }
+    // A non-blocking stream in the device's drive context (nullptr: unavailable).
+    cudaStream_t create(int device) {
+        if (!device_get || !get_resource || !generate_desc || !ctx_create || !stream_create) return nullptr;
+        std::lock_guard<std::mutex> g(mu);
+        CUgreenCtx ctx = nullptr;
+        for (auto& kv : ctx_of_device)
+            if (kv.first == device) ctx = kv.second;
+        if (!ctx) {
+            CUdevice dev = 0;
+            CUdevResource all{};
+            CUdevResourceDesc desc = nullptr;
+            if (device_get(&dev, device) != CUDA_SUCCESS || get_resource(dev, &all, CU_DEV_RESOURCE_TYPE_SM) != CUDA_SUCCESS ||
+                generate_desc(&desc, &all, 1) != CUDA_SUCCESS ||
+                ctx_create(&ctx, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM) != CUDA_SUCCESS)
+                return nullptr;
+            ctx_of_device.emplace_back(device, ctx);  // lives as long as the process
+        }
+        CUstream st = nullptr;
+        if (stream_create(&st, ctx, CU_STREAM_NON_BLOCKING, 0) != CUDA_SUCCESS) return nullptr;
+        return reinterpret_cast<cudaStream_t>(st);
+    }
+};
+
+// A stream for a drive worker on `device`; *green tells where it lives.
+cudaStream_t create_drive_stream(int device, bool* green) {
+    static GreenDriveStreams greens;
+    *green = false;
+    const char* how = std::getenv("TUTTI_EMULATOR_STREAMS");
+    if (!how || std::strcmp(how, "plain") != 0) {
+        if (cudaStream_t s = greens.create(device)) {
+            *green = true;
+            return s;
+        }
+    }
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return s;
 }
 
 // cuStreamWriteValue32, looked up through the runtime so the library does not
@@ -348,6 +432,7 @@ ControllerStats EmulatedNvmeController::stats() const {
     s.errors = st_errors_.load();
     s.injected = st_injected_.load();
     s.dma_copies = st_dma_copies_.load();
+    s.green_streams = st_green_streams_.load();
     s.image_bytes = image_bytes_.load();
     s.load_ns = st_load_ns_.load();
     s.file_ns = st_file_ns_.load();
@@ -874,9 +959,11 @@ void EmulatedNvmeController::worker_main(std::uint32_t worker) {
     WorkerCtx w;
     w.bounce = worker < bounces_.size() ? bounces_[worker] : nullptr;
     w.bounce_bytes = cfg_.mdts_bytes;
-    if (cuda_device_ >= 0 && cudaSetDevice(cuda_device_) == cudaSuccess &&
-        cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking) == cudaSuccess) {
-        w.cuda = true;
+    if (cuda_device_ >= 0 && cudaSetDevice(cuda_device_) == cudaSuccess) {
+        bool green = false;
+        w.stream = create_drive_stream(cuda_device_, &green);
+        w.cuda = w.stream != nullptr;
+        if (green) st_green_streams_.fetch_add(1, std::memory_order_relaxed);
     } else {
         cudaGetLastError();
     }

@@ -461,6 +461,7 @@ PYBIND11_MODULE(_core, m) {
                      d["errors"] = s.errors;
                      d["injected"] = s.injected;
                      d["dma_copies"] = s.dma_copies;
+                     d["green_streams"] = s.green_streams;
                      d["image_bytes"] = s.image_bytes;
                      d["load_ms"] = s.load_ns / 1e6;
                      d["file_ms"] = s.file_ns / 1e6;
@@ -595,6 +596,7 @@ PYBIND11_MODULE(_core, m) {
                 o.gpu.async_completion = env && *env && std::strcmp(env, "0") != 0;
             }
             if (opts.contains("async_completion")) o.gpu.async_completion = opts["async_completion"].cast<bool>();
+            if (opts.contains("direct_reads")) o.gpu.direct_reads = opts["direct_reads"].cast<bool>();
             if (opts.contains("staging_write_combined"))
                 o.gpu.staging_write_combined = opts["staging_write_combined"].cast<bool>();
             if (opts.contains("async_fallback_us"))
