@@ -302,3 +302,98 @@ def test_daemon_reads_tutti_schema(tmp_path):
     finally:
         p.send_signal(signal.SIGTERM)
         p.wait(timeout=10)
+
+
+def _kv(rsp):
+    assert rsp.startswith("OK"), rsp
+    from urllib.parse import unquote
+    return {k: unquote(v) for k, v in (t.split("=", 1) for t in rsp.split()[1:])}
+
+
+def test_daemon_service_surface_connect_slices_and_resources():
+    devs = [{"id": 0, "mount": "/mnt/nvme 0", "queues": 32, "accelerators": [0], "pci": "0000:08:00.0",
+             "chrdev": "/dev/ssnvme0", "lba_bytes": 4096},
+            {"id": 1, "mount": "/mnt/nvme1", "queues": 32, "accelerators": [0, 1]},
+            {"id": 2, "mount": "/mnt/nvme2", "queues": 32, "available": False, "diagnostic": "mount: no superblock"}]
+    accs = [{"accel_id": 0, "view_root": "/run/tutti/gpu0"}, {"accel_id": 1, "view_root": "/run/tutti/gpu1"}]
+    out = core().daemon_handle_request_selftest(
+        ["LIST_DEVICES", "LIST_ACCELERATORS",
+         "CONNECT device=0 accel=0 queues=8 pid=0",
+         "ACQUIRE_SLICES accel=1 selection=allowed queues=4 pid=0",
+         "ACQUIRE_SLICES accel=0 selection=striped queues=4 pid=0",
+         "ACQUIRE_SLICES accel=1 selection=explicit devices=0 queues=4 pid=0",
+         "CONNECT device=2 accel=0 queues=4 pid=0",
+         "LIST_RESOURCES", "HEARTBEAT allocation_id=1", "DISCONNECT allocation_id=1",
+         "ACQUIRE_SLICES accel=1 selection=striped queues=4 pid=0", "STATUS"], devs, accs)
+    lst = _kv(out[0])
+    assert lst["devices"] == "3" and lst["d0.pci_addr"] == "0000:08:00.0" and lst["d0.snvme_dev_path"] == "/dev/ssnvme0"
+    assert lst["d0.blk_size_log"] == "12" and lst["d0.backing_mount_path"] == "/mnt/nvme 0"  # spaces survive
+    assert lst["d1.allowed_gpus"] == "0:/run/tutti/gpu0/nvme1;1:/run/tutti/gpu1/nvme1"
+    acc = _kv(out[1])
+    assert acc["accelerators"] == "2" and acc["a1.view_root"] == "/run/tutti/gpu1"
+    con = _kv(out[2])  # the reference's ConnectResponse fields
+    assert con["allocation_id"] == "2" and con["granted_queues"] == "8" and con["mount_path"] == "/run/tutti/gpu0/nvme0"
+    assert con["snvme_dev_path"] == "/dev/ssnvme0" and con["blk_size"] == "4096" and con["lease_timeout_sec"] == "30"
+    sl = _kv(out[3])  # accelerator 1 may use device 1 only
+    assert sl["slices"] == "1" and sl["s0.device_id"] == "1" and sl["s0.view_path"] == "/run/tutti/gpu1/nvme1"
+    st = _kv(out[4])  # striped over the available drives accelerator 0 may use (2 is unavailable)
+    assert st["slices"] == "2" and st["s0.device_id"] == "0" and st["s1.device_id"] == "1"
+    assert out[5].startswith("ERR") and "PERMISSION_DENIED" in out[5]
+    assert out[6].startswith("ERR") and "unavailable" in out[6] and "no superblock" in out[6]
+    res = _kv(out[7])
+    assert res["resources"] == "3" and res["r2.available"] == "false" and res["r2.available_queues"] == "0"
+    assert res["r0.reserved_queues"] == "12" and res["r0.controller_queue_capacity"] == "32"
+    assert out[8].startswith("ERR")  # allocation 1 does not exist (ids count sessions too)
+    assert out[9].startswith("ERR")
+    assert out[10].startswith("ERR") and "RESOURCE_EXHAUSTED" in out[10]  # one drive cannot be striped
+    assert _kv(out[11])["leases"] == "3"
+
+
+def test_daemon_connect_and_disconnect_close_their_session():
+    out = core().daemon_handle_request_selftest(
+        ["CONNECT device=0 accel=0 queues=16 pid=0", "LIST", "DISCONNECT allocation_id=2", "LIST",
+         "DISCONNECT allocation_id=2"],
+        [{"id": 0, "mount": "/m0", "queues": 32}])
+    assert _kv(out[0])["allocation_id"] == "2"
+    assert _kv(out[1])["free_queues"] == "16"
+    assert _kv(out[2])["success"] == "true"
+    assert _kv(out[3])["free_queues"] == "32"
+    assert out[4].startswith("ERR") and "NOT_FOUND" in out[4]
+
+
+def test_daemon_builds_accelerator_view_roots(tmp_path):
+    if not os.path.exists(DAEMON):
+        pytest.skip("tutti_daemon not built")
+    sock = str(tmp_path / "v.sock")
+    (tmp_path / "gpu0").mkdir()
+    (tmp_path / "gpu0" / "nvme1").symlink_to("/stale/target")  # replaced
+    (tmp_path / "gpu0" / "keep.txt").write_text("x")  # left alone
+    cfg = tmp_path / "daemon.yaml"
+    cfg.write_text(textwrap.dedent(f"""
+        service: {{socket: {sock}}}
+        accelerators:
+          - {{accel_id: 0, view_root: {tmp_path}/gpu0}}
+          - {{accel_id: 1, view_root: {tmp_path}/gpu1}}
+        nvmes:
+          - {{device_id: 0, backing_mount_path: {tmp_path}/nvme0, allowed_accel_ids: [0]}}
+          - {{device_id: 1, backing_mount_path: {tmp_path}/nvme1, allowed_accel_ids: [0, 1]}}
+        """))
+    p = subprocess.Popen([DAEMON, "--config", str(cfg)], stderr=subprocess.PIPE)
+    try:
+        for _ in range(100):
+            if os.path.exists(sock):
+                break
+            time.sleep(0.05)
+        assert os.readlink(tmp_path / "gpu0" / "nvme0") == f"{tmp_path}/nvme0"
+        assert os.readlink(tmp_path / "gpu0" / "nvme1") == f"{tmp_path}/nvme1"
+        assert os.readlink(tmp_path / "gpu1" / "nvme1") == f"{tmp_path}/nvme1"
+        assert not (tmp_path / "gpu1" / "nvme0").exists()
+        assert (tmp_path / "gpu0" / "keep.txt").read_text() == "x"
+        c = Client(sock)
+        sl = c.kv("ACQUIRE_SLICES accel=1 selection=allowed queues=4 pid=%d" % os.getpid())
+        assert sl["slices"] == "1" and sl["s0.view_path"] == f"{tmp_path}/gpu1/nvme1"
+        res = c.kv("LIST_RESOURCES")
+        assert res["r0.available"] == "true"  # no block device configured: mounted outside the daemon
+    finally:
+        p.send_signal(signal.SIGTERM)
+        p.wait(timeout=10)

@@ -22,10 +22,14 @@ CXX = ["g++", "-O2", "-std=c++17", "-pthread", "-I", os.path.join(CSRC, "include
        "-I", os.path.join(CUDA, "include")]
 
 TARGETS = {
-    "tutti_daemon": (["daemon/daemon_main.cpp", "daemon/lease_ledger.cpp", "config/yaml_lite.cpp"], []),
+    "tutti_daemon": (["daemon/daemon_main.cpp", "daemon/lease_ledger.cpp", "daemon/host_admin.cpp",
+                      "config/yaml_lite.cpp", "nvme/snvme_client.cpp", "nvme/host_memory.cpp",
+                      "nvme/emulated_controller.cpp"],
+                     ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
     "tutti_native_tests": ([
         "tests/native_tests.cpp", "tests/runtime_contract_tests.cpp", "tests/datapath_contract_tests.cpp",
         "tests/snvme_client_tests.cpp", "nvme/snvme_client.cpp", "testing/fake_snvme.cpp",
+        "tests/host_admin_tests.cpp", "daemon/host_admin.cpp",
         "runtime/storage_runtime.cpp", "datapaths/posix_data_path.cpp", "objects/object_store.cpp",
         "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
         "resolvers/file_resolvers.cpp", "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",

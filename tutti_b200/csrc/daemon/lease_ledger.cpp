@@ -1,5 +1,6 @@
 #include "lease_ledger.h"
 
+#include <cctype>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -65,7 +66,7 @@ std::size_t LeaseLedger::lease_count() const {
 }
 
 Result<std::uint64_t> LeaseLedger::open_session(const std::string& client, std::int64_t pid, std::uint64_t start,
-                                                std::int64_t accel) {
+                                                std::int64_t accel, bool implicit) {
     std::lock_guard<std::mutex> g(mu_);
     Session s;
     s.id = next_++;
@@ -73,8 +74,42 @@ Result<std::uint64_t> LeaseLedger::open_session(const std::string& client, std::
     s.pid = pid;
     s.start_time = start;
     s.accel = accel;
+    s.implicit = implicit;
     sessions_[s.id] = s;
     return s.id;
+}
+
+Status LeaseLedger::release_allocation(std::uint64_t lease) {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = leases_.find(lease);
+    if (it == leases_.end()) return {StatusCode::NOT_FOUND, "unknown allocation"};
+    const std::uint64_t session = it->second.session;
+    release_locked(lease);
+    auto sit = sessions_.find(session);
+    if (sit != sessions_.end() && sit->second.implicit) {
+        bool more = false;
+        for (auto& kv : leases_) more |= kv.second.session == session;
+        if (!more) sessions_.erase(sit);
+    }
+    return Status::Ok();
+}
+
+std::string LeaseLedger::view_root(std::int64_t accel) const {
+    std::lock_guard<std::mutex> g(mu_);
+    for (const auto& a : accels_)
+        if (a.id == accel) return a.view_root;
+    return "";
+}
+
+std::vector<std::int64_t> LeaseLedger::allowed_devices(std::int64_t accel) const {
+    std::lock_guard<std::mutex> g(mu_);
+    std::vector<std::int64_t> out;
+    for (const auto& d : devices_) {
+        bool ok = d.accelerators.empty();
+        for (auto a : d.accelerators) ok = ok || a == accel;
+        if (ok && d.available) out.push_back(d.id);
+    }
+    return out;
 }
 
 Status LeaseLedger::close_session(std::uint64_t session) {
@@ -101,6 +136,10 @@ Result<Lease> LeaseLedger::acquire(std::uint64_t session, const std::vector<std:
                                                                std::to_string(pool_max_) + " per client"});
     const std::int64_t accel = sit->second.accel;
     for (auto dev : devices) {
+        for (const auto& d : devices_)
+            if (d.id == dev && !d.available)
+                return R::Failure({StatusCode::UNSUPPORTED, "device " + std::to_string(dev) +
+                                                                " is unavailable: " + d.diagnostic});
         for (const auto& d : devices_) {
             if (d.id != dev || d.accelerators.empty()) continue;
             bool allowed = false;
@@ -190,6 +229,35 @@ std::vector<std::uint64_t> LeaseLedger::reap(std::chrono::steady_clock::duration
     return reaped;
 }
 
+namespace {
+std::string encode_value(const std::string& v) {
+    std::string out;
+    for (unsigned char c : v) {
+        if (c == '%' || c == ' ' || c == '\t' || c == '\n' || c == '\r') {
+            char b[4];
+            std::snprintf(b, sizeof(b), "%%%02X", c);
+            out += b;
+        } else {
+            out.push_back(static_cast<char>(c));
+        }
+    }
+    return out;
+}
+std::string decode_value(const std::string& v) {
+    std::string out;
+    for (std::size_t i = 0; i < v.size(); ++i) {
+        if (v[i] == '%' && i + 2 < v.size() && std::isxdigit(static_cast<unsigned char>(v[i + 1])) &&
+            std::isxdigit(static_cast<unsigned char>(v[i + 2]))) {
+            out.push_back(static_cast<char>(std::strtol(v.substr(i + 1, 2).c_str(), nullptr, 16)));
+            i += 2;
+        } else {
+            out.push_back(v[i]);
+        }
+    }
+    return out;
+}
+}  // namespace
+
 Message parse_message(const std::string& line) {
     Message m;
     std::vector<std::string> toks;
@@ -209,14 +277,15 @@ Message parse_message(const std::string& line) {
         if (eq == std::string::npos)
             m.kv[tok] = "";
         else
-            m.kv[tok.substr(0, eq)] = tok.substr(eq + 1);
+            m.kv[tok.substr(0, eq)] = decode_value(tok.substr(eq + 1));
     }
     return m;
 }
 
+
 std::string format_message(const Message& m) {
     std::string out = m.verb;
-    for (auto& kv : m.kv) out += " " + kv.first + "=" + kv.second;
+    for (auto& kv : m.kv) out += " " + kv.first + "=" + encode_value(kv.second);
     return out + "\n";
 }
 
@@ -233,6 +302,56 @@ std::vector<std::int64_t> parse_ids(const std::string& s) {
     return out;
 }
 std::string err(const Status& s) { return "ERR " + s.to_string() + "\n"; }
+
+std::string join_ids(const std::vector<std::int64_t>& v, const char* sep = ",") {
+    std::string out;
+    for (auto x : v) out += (out.empty() ? "" : sep) + std::to_string(x);
+    return out;
+}
+
+std::uint32_t log2_of(std::uint32_t v) {
+    std::uint32_t l = 0;
+    while ((1u << (l + 1)) <= v && l < 31) ++l;
+    return l;
+}
+
+// Fields of one device as the service reports it, under `p` (e.g. "d0.").
+void put_device(Message& rsp, const std::string& p, const DeviceInfo& d, const LeaseLedger& ledger) {
+    rsp.kv[p + "device_id"] = std::to_string(d.id);
+    rsp.kv[p + "pci_addr"] = d.pci;
+    rsp.kv[p + "snvme_dev_path"] = d.chrdev;
+    rsp.kv[p + "block_path"] = d.block_device;
+    rsp.kv[p + "backing_mount_path"] = d.mount;
+    rsp.kv[p + "namespace_id"] = std::to_string(d.namespace_id);
+    rsp.kv[p + "blk_size"] = std::to_string(d.lba_bytes);
+    rsp.kv[p + "blk_size_log"] = std::to_string(log2_of(d.lba_bytes));
+    rsp.kv[p + "queue_depth"] = std::to_string(d.queue_depth);
+    rsp.kv[p + "max_data_size"] = std::to_string(d.max_data_size);
+    rsp.kv[p + "max_queues_per_group"] = std::to_string(d.max_queues_per_group);
+    rsp.kv[p + "allowed_accel_ids"] = d.accelerators.empty() ? "*" : join_ids(d.accelerators);
+    rsp.kv[p + "kind"] = d.kind;
+    (void)ledger;
+}
+
+// One lease as the service reports an allocation: one slice per device.
+void put_slices(Message& rsp, const Lease& l, const LeaseLedger& ledger, std::int64_t accel) {
+    rsp.kv["allocation_id"] = std::to_string(l.id);
+    rsp.kv["slices"] = std::to_string(l.grants.size());
+    const std::string root = ledger.view_root(accel);
+    for (std::size_t i = 0; i < l.grants.size(); ++i) {
+        const Grant& gr = l.grants[i];
+        const DeviceInfo* d = ledger.device(gr.device);
+        const std::string p = "s" + std::to_string(i) + ".";
+        if (d) put_device(rsp, p, *d, ledger);
+        rsp.kv[p + "accel_id"] = std::to_string(accel);
+        rsp.kv[p + "granted_queues"] = std::to_string(gr.queues);
+        rsp.kv[p + "first_queue"] = std::to_string(gr.first_queue);
+        rsp.kv[p + "controller_queue_capacity"] = std::to_string(d ? d->queues : 0);
+        rsp.kv[p + "view_path"] = root.empty() ? "" : root + "/nvme" + std::to_string(gr.device);
+    }
+    rsp.kv["heartbeat_interval_sec"] = std::to_string(ledger.heartbeat_interval_s());
+    rsp.kv["lease_timeout_sec"] = std::to_string(ledger.lease_timeout_s());
+}
 }  // namespace
 
 std::string handle_request(LeaseLedger& ledger, const std::string& line) {
@@ -289,11 +408,101 @@ std::string handle_request(LeaseLedger& ledger, const std::string& line) {
         rsp.kv["lba_bytes"] = lbas;
         rsp.kv["nsid"] = nsids;
     } else if (req.verb == "HEARTBEAT") {
-        Status s = ledger.heartbeat(std::strtoull(req.get("lease").c_str(), nullptr, 10));
+        const std::string id = req.get("lease", req.get("allocation_id", req.get("allocation")));
+        Status s = ledger.heartbeat(std::strtoull(id.c_str(), nullptr, 10));
         if (!s.ok()) return err(s);
-    } else if (req.verb == "RELEASE") {
-        Status s = ledger.release(std::strtoull(req.get("lease").c_str(), nullptr, 10));
+        rsp.kv["notice"] = "NONE";
+    } else if (req.verb == "RELEASE" || req.verb == "DISCONNECT") {
+        const std::string id = req.get("lease", req.get("allocation_id", req.get("allocation")));
+        Status s = ledger.release_allocation(std::strtoull(id.c_str(), nullptr, 10));
         if (!s.ok()) return err(s);
+        rsp.kv["success"] = "true";
+    } else if (req.verb == "LIST_DEVICES") {
+        const auto devs = ledger.devices();
+        rsp.kv["devices"] = std::to_string(devs.size());
+        for (std::size_t i = 0; i < devs.size(); ++i) {
+            const std::string p = "d" + std::to_string(i) + ".";
+            put_device(rsp, p, devs[i], ledger);
+            // the mount each allowed accelerator reaches the drive through
+            std::string gpus;
+            for (auto a : devs[i].accelerators.empty() ? std::vector<std::int64_t>{} : devs[i].accelerators) {
+                const std::string root = ledger.view_root(a);
+                gpus += (gpus.empty() ? "" : ";") + std::to_string(a) + ":" +
+                        (root.empty() ? devs[i].mount : root + "/nvme" + std::to_string(devs[i].id));
+            }
+            rsp.kv[p + "allowed_gpus"] = gpus;
+        }
+    } else if (req.verb == "LIST_ACCELERATORS") {
+        const auto acc = ledger.accelerators();
+        rsp.kv["accelerators"] = std::to_string(acc.size());
+        for (std::size_t i = 0; i < acc.size(); ++i) {
+            rsp.kv["a" + std::to_string(i) + ".accel_id"] = std::to_string(acc[i].id);
+            rsp.kv["a" + std::to_string(i) + ".view_root"] = acc[i].view_root;
+        }
+    } else if (req.verb == "LIST_RESOURCES") {
+        const auto devs = ledger.devices();
+        rsp.kv["resources"] = std::to_string(devs.size());
+        for (std::size_t i = 0; i < devs.size(); ++i) {
+            const std::string p = "r" + std::to_string(i) + ".";
+            put_device(rsp, p, devs[i], ledger);
+            const std::uint32_t freeq = ledger.free_queues(devs[i].id);
+            rsp.kv[p + "controller_queue_capacity"] = std::to_string(devs[i].queues);
+            rsp.kv[p + "available_queues"] = std::to_string(devs[i].available ? freeq : 0);
+            rsp.kv[p + "reserved_queues"] = std::to_string(devs[i].queues - freeq);
+            rsp.kv[p + "available"] = devs[i].available ? "true" : "false";
+            rsp.kv[p + "diagnostic"] = devs[i].diagnostic;
+        }
+        rsp.kv["heartbeat_interval_sec"] = std::to_string(ledger.heartbeat_interval_s());
+        rsp.kv["lease_timeout_sec"] = std::to_string(ledger.lease_timeout_s());
+    } else if (req.verb == "CONNECT" || req.verb == "ACQUIRE_SLICES") {
+        // A session of its own (closed with the allocation) unless one is named.
+        const std::int64_t accel = std::strtoll(req.get("accel", req.get("cuda_device", req.get("accel_id", "-1"))).c_str(),
+                                                nullptr, 10);
+        const std::int64_t pid = std::strtoll(req.get("pid", req.get("client_pid", "0")).c_str(), nullptr, 10);
+        std::vector<std::int64_t> devs;
+        if (req.verb == "CONNECT") {
+            devs.push_back(std::strtoll(req.get("device", req.get("device_id", "-1")).c_str(), nullptr, 10));
+        } else {
+            const std::string mode = req.get("selection", "allowed");
+            if (mode == "explicit") {
+                devs = parse_ids(req.get("devices", req.get("device_ids")));
+                if (devs.empty()) return err({StatusCode::INVALID_ARGUMENT, "explicit selection names no devices"});
+            } else if (mode == "allowed" || mode == "striped") {
+                devs = ledger.allowed_devices(accel);
+                if (mode == "striped" && devs.size() < 2)
+                    return err({StatusCode::RESOURCE_EXHAUSTED, "striping needs two or more devices for this accelerator"});
+                if (devs.empty()) return err({StatusCode::PERMISSION_DENIED, "no device is allowed for this accelerator"});
+            } else {
+                return err({StatusCode::INVALID_ARGUMENT, "selection must be allowed, explicit or striped"});
+            }
+        }
+        std::uint64_t session = std::strtoull(req.get("session", "0").c_str(), nullptr, 10);
+        bool opened = false;
+        if (session == 0) {
+            auto sr = ledger.open_session(req.get("client", "pid" + std::to_string(pid)), pid, process_start_time(pid),
+                                          accel, /*implicit=*/true);
+            if (!sr.ok()) return err(sr.status());
+            session = sr.value();
+            opened = true;
+        }
+        const auto queues = static_cast<std::uint32_t>(
+            std::strtoul(req.get("queues", req.get("num_queues", req.get("queues_per_controller", "0"))).c_str(), nullptr, 10));
+        auto l = ledger.acquire(session, devs, queues);
+        if (!l.ok()) {
+            if (opened) (void)ledger.close_session(session);
+            return err(l.status());
+        }
+        put_slices(rsp, l.value(), ledger, accel);
+        if (req.verb == "CONNECT" && !l.value().grants.empty()) {
+            // the single-device answer carries the slice's fields unprefixed
+            const Grant& gr = l.value().grants[0];
+            if (const DeviceInfo* d = ledger.device(gr.device)) {
+                put_device(rsp, "", *d, ledger);
+                rsp.kv["mount_path"] = rsp.kv["s0.view_path"].empty() ? d->mount : rsp.kv["s0.view_path"];
+            }
+            rsp.kv["granted_queues"] = std::to_string(gr.queues);
+            rsp.kv["first_queue"] = std::to_string(gr.first_queue);
+        }
     } else if (req.verb == "STATUS") {
         rsp.kv["leases"] = std::to_string(ledger.lease_count());
         rsp.kv["devices"] = std::to_string(ledger.devices().size());

@@ -33,6 +33,20 @@ struct DeviceInfo {
     std::uint32_t namespace_id = 1;
     std::uint32_t lba_bytes = 512;
     std::vector<std::int64_t> accelerators;  // who may lease its queues; empty: any accelerator
+    // Filled by the controller's bring-up when the daemon owns it (snvme).
+    std::string chrdev;        // the controller's snvme node
+    std::string block_device;  // the namespace's block device
+    std::uint32_t queue_depth = 0;
+    std::uint64_t max_data_size = 0;
+    std::uint32_t max_queues_per_group = 32;
+    bool available = true;     // false: bring-up or mount failed (see diagnostic); not leased
+    std::string diagnostic;
+};
+
+// An accelerator and the directory its processes reach the drives through.
+struct AcceleratorView {
+    std::int64_t id = -1;
+    std::string view_root;
 };
 
 struct Grant {
@@ -54,6 +68,7 @@ struct Session {
     std::int64_t pid = 0;
     std::uint64_t start_time = 0;  // /proc/<pid>/stat field 22 at HELLO
     std::int64_t accel = -1;       // the client's accelerator (HELLO accel=...), -1 if not given
+    bool implicit = false;         // opened by CONNECT / ACQUIRE_SLICES: closed with its lease
 };
 
 // Reads /proc/<pid>/stat start time (clock ticks since boot); 0 if the process is gone.
@@ -64,7 +79,9 @@ public:
     explicit LeaseLedger(std::vector<DeviceInfo> devices);
 
     Result<std::uint64_t> open_session(const std::string& client, std::int64_t pid, std::uint64_t start_time,
-                                       std::int64_t accel = -1);
+                                       std::int64_t accel = -1, bool implicit = false);
+    // Releases a lease; a session opened only for it is closed too.
+    Status release_allocation(std::uint64_t lease);
     Status close_session(std::uint64_t session);  // releases its leases
 
     // All-or-nothing: either every device gets `queues` queues or nothing changes.
@@ -88,6 +105,24 @@ public:
 
     std::vector<DeviceInfo> devices() const;
     std::uint32_t free_queues(std::int64_t device) const;
+    void set_accelerators(std::vector<AcceleratorView> a) {
+        std::lock_guard<std::mutex> g(mu_);
+        accels_ = std::move(a);
+    }
+    std::vector<AcceleratorView> accelerators() const {
+        std::lock_guard<std::mutex> g(mu_);
+        return accels_;
+    }
+    std::string view_root(std::int64_t accel) const;
+    void set_lease_timing(std::uint32_t heartbeat_interval_s, std::uint32_t timeout_s) {
+        std::lock_guard<std::mutex> g(mu_);
+        hb_interval_s_ = heartbeat_interval_s;
+        lease_timeout_s_ = timeout_s;
+    }
+    std::uint32_t heartbeat_interval_s() const { return hb_interval_s_; }
+    std::uint32_t lease_timeout_s() const { return lease_timeout_s_; }
+    // Available devices `accel` may lease (every device without a list, and those listing it).
+    std::vector<std::int64_t> allowed_devices(std::int64_t accel) const;
     std::size_t lease_count() const;
     const DeviceInfo* device(std::int64_t id) const;
 
@@ -100,9 +135,17 @@ private:
     std::map<std::uint64_t, Lease> leases_;
     std::uint64_t next_ = 1;
     std::uint32_t pool_default_ = 0, pool_max_ = 0;
+    std::vector<AcceleratorView> accels_;
+    std::uint32_t hb_interval_s_ = 10, lease_timeout_s_ = 30;
 };
 
 // Line protocol: "VERB key=value key=value\n" -> "OK key=value ...\n" | "ERR message\n".
+// Values carry '%', spaces, tabs and line breaks as %XX.
+// Verbs: HELLO, BYE, LIST, ACQUIRE, HEARTBEAT, RELEASE, STATUS (sessions and
+// leases), and the service surface of the reference's NvmeService:
+// LIST_DEVICES, CONNECT, DISCONNECT, LIST_ACCELERATORS, LIST_RESOURCES,
+// ACQUIRE_SLICES (HEARTBEAT and RELEASE also take allocation=). Lists come
+// back as indexed keys: devices=2 d0.device_id=... d1.device_id=...
 struct Message {
     std::string verb;
     std::map<std::string, std::string> kv;

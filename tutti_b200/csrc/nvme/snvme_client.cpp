@@ -2,7 +2,10 @@
 
 #include <algorithm>
 #include <cerrno>
+#include <chrono>
+#include <cstdio>
 #include <cstring>
+#include <thread>
 
 #include <fcntl.h>
 #include <sys/mman.h>
@@ -262,6 +265,97 @@ std::uint32_t* SnvmeClient::doorbell_host(std::uint32_t offset) const {
 
 std::uint32_t* SnvmeClient::doorbell_device(std::uint32_t offset) const {
     return bar_device_ ? reinterpret_cast<std::uint32_t*>(static_cast<char*>(bar_device_) + offset) : nullptr;
+}
+
+// ---- SnvmeOwner ----------------------------------------------------------------
+
+Result<uapi::PciAddress> parse_pci_address(const std::string& text) {
+    using R = Result<uapi::PciAddress>;
+    unsigned dom = 0, bus = 0, slot = 0, fn = 0;
+    char tail = 0;
+    if (std::sscanf(text.c_str(), "%x:%x:%x.%x%c", &dom, &bus, &slot, &fn, &tail) != 4 || bus > 0xFF || slot > 0x1F ||
+        fn > 7 || dom > 0xFFFF)
+        return R::Failure({StatusCode::INVALID_ARGUMENT, "bad PCI address '" + text + "' (want dddd:bb:ss.f)"});
+    uapi::PciAddress a{};
+    a.domain = static_cast<std::int32_t>(dom);
+    a.bus = static_cast<std::int32_t>(bus);
+    a.slot = static_cast<std::int32_t>(slot);
+    a.function = static_cast<std::int32_t>(fn);
+    return R(a);
+}
+
+Result<std::unique_ptr<SnvmeOwner>> SnvmeOwner::bring_up(const std::string& control_node, const std::string& pci,
+                                                         std::uint32_t kernel_ioq_cap, SnvmeSys& sys,
+                                                         std::uint32_t probe_wait_ms) {
+    using R = Result<std::unique_ptr<SnvmeOwner>>;
+    auto addr = parse_pci_address(pci);
+    if (!addr.ok()) return R::Failure(addr.status());
+    std::unique_ptr<SnvmeOwner> o(new SnvmeOwner());
+    o->sys_ = &sys;
+    o->pci_ = addr.value();
+    const int cfd = sys.open_node(control_node);
+    if (cfd < 0) return R::Failure(errno_status(cfd, "cannot open the snvme control node " + control_node));
+    o->control_fd_ = cfd;
+    uapi::PciAddress a = o->pci_;
+    if (int rc = sys.ioctl_node(cfd, uapi::kChrdevCreate, &a); rc != 0)
+        return R::Failure(errno_status(rc, pci + ": CHRDEV_CREATE"));
+    o->created_ = true;
+    o->minor_ = a.domain;  // the driver returns the node's minor in the domain field
+    o->node_ = "/dev/ssnvme" + std::to_string(o->minor_);
+    const int dfd = sys.open_node(o->node_);
+    if (dfd < 0) return R::Failure(errno_status(dfd, "cannot open " + o->node_));
+    o->dev_fd_ = dfd;
+    if (kernel_ioq_cap != 0) {
+        std::uint32_t cap = kernel_ioq_cap;
+        if (int rc = sys.ioctl_node(dfd, uapi::kSetKernelIoqCap, &cap); rc != 0)
+            return R::Failure(errno_status(rc, o->node_ + ": SET_KERNEL_IOQ_CAP"));
+    }
+    a = o->pci_;
+    if (int rc = sys.ioctl_node(cfd, uapi::kDeviceBind, &a); rc != 0)
+        return R::Failure(errno_status(rc, pci + ": DEVICE_BIND"));
+    o->bound_ = true;
+    // The bind returns before the namespace scan: poll until the disk is named.
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(probe_wait_ms);
+    for (;;) {
+        uapi::DevInfo di{};
+        const int rc = sys.ioctl_node(dfd, uapi::kGetDevInfo, &di);
+        if (rc == 0 && di.disk_name[0] != 0) {
+            if (di.abi_version != uapi::kAbiVersion)
+                return R::Failure({StatusCode::UNSUPPORTED, o->node_ + ": snvme driver ABI " + std::to_string(di.abi_version) +
+                                                                ", this build speaks " + std::to_string(uapi::kAbiVersion)});
+            SnvmeDeviceInfo& in = o->info_;
+            in.disk_name.assign(di.disk_name, strnlen(di.disk_name, sizeof(di.disk_name)));
+            in.abi_version = di.abi_version;
+            in.capabilities = di.capabilities;
+            in.lba_bytes = static_cast<std::uint32_t>(di.lba_bytes);
+            in.max_transfer_bytes = di.max_transfer_bytes;
+            in.queue_depth = di.queue_depth;
+            in.doorbell_stride = 4u << di.doorbell_stride_log;
+            in.first_user_qid = di.first_user_qid;
+            in.last_user_qid = di.last_user_qid;
+            in.max_queues_per_group = std::min(di.max_queues_per_group, uapi::kMaxQueuesPerGroup);
+            in.bar0_bytes = di.bar0_bytes;
+            in.sgl = di.sgl_support != 0;
+            break;
+        }
+        if (rc != 0 && rc != -EAGAIN && rc != -ENODEV) return R::Failure(errno_status(rc, o->node_ + ": GET_DEV_INFO"));
+        if (std::chrono::steady_clock::now() >= deadline)
+            return R::Failure({StatusCode::TIMEOUT, o->node_ + ": the namespace scan did not finish in " +
+                                                        std::to_string(probe_wait_ms) + " ms"});
+        std::this_thread::sleep_for(std::chrono::milliseconds(10));
+    }
+    return R(std::move(o));
+}
+
+SnvmeOwner::~SnvmeOwner() {
+    if (dev_fd_ >= 0) sys_->close_node(dev_fd_);
+    if (control_fd_ >= 0) {
+        uapi::PciAddress a = pci_;
+        if (bound_) (void)sys_->ioctl_node(control_fd_, uapi::kDeviceUnbind, &a);
+        a = pci_;
+        if (created_) (void)sys_->ioctl_node(control_fd_, uapi::kChrdevRemove, &a);
+        sys_->close_node(control_fd_);
+    }
 }
 
 // ---- SnvmeController -----------------------------------------------------------

@@ -128,6 +128,42 @@ private:
     std::vector<Mapped> maps_;
 };
 
+// "dddd:bb:ss.f" (hexadecimal fields) as the driver's PCI address.
+Result<snvme::uapi::PciAddress> parse_pci_address(const std::string& text);
+
+// Owner side: binds a controller to the snvme driver and creates its node,
+// which clients then attach to. Bring-up: open the control node,
+// CHRDEV_CREATE (the driver returns the node's minor), open the node, an
+// optional kernel I/O-queue cap (before the bind), DEVICE_BIND, then
+// GET_DEV_INFO until the namespace scan has named the disk (bounded). Any
+// failure undoes what was done. Destruction unbinds and removes the node.
+// Parity: the reference's nvm_controller_init_common
+// (csrc/device_manager/nvme/libnvm/src/linux/device.cpp:512-700).
+class SnvmeOwner {
+public:
+    static Result<std::unique_ptr<SnvmeOwner>> bring_up(const std::string& control_node, const std::string& pci,
+                                                        std::uint32_t kernel_ioq_cap, SnvmeSys& sys,
+                                                        std::uint32_t probe_wait_ms = 10000);
+    ~SnvmeOwner();
+    SnvmeOwner(const SnvmeOwner&) = delete;
+    SnvmeOwner& operator=(const SnvmeOwner&) = delete;
+
+    const std::string& node() const { return node_; }
+    int minor() const { return minor_; }
+    const SnvmeDeviceInfo& info() const { return info_; }
+    std::string block_device() const { return info_.disk_name.empty() ? "" : "/dev/" + info_.disk_name; }
+
+private:
+    SnvmeOwner() = default;
+    SnvmeSys* sys_ = nullptr;
+    int control_fd_ = -1, dev_fd_ = -1;
+    snvme::uapi::PciAddress pci_{};
+    bool created_ = false, bound_ = false;
+    int minor_ = -1;
+    std::string node_;
+    SnvmeDeviceInfo info_;
+};
+
 struct SnvmeControllerConfig {
     std::string node;                   // the controller's snvme node
     std::uint32_t num_io_queues = 64;

@@ -719,23 +719,37 @@ PYBIND11_MODULE(_core, m) {
         },
         py::arg("config"), py::arg("is_path") = false);
 
-    m.def("daemon_handle_request_selftest", [](const std::vector<std::string>& lines, py::list devices) {
-        // Runs lines through an in-process ledger (protocol tests without a socket).
-        std::vector<tutti::daemon::DeviceInfo> devs;
-        for (auto item : devices) {
-            auto d = item.cast<py::dict>();
-            tutti::daemon::DeviceInfo info;
-            info.id = d["id"].cast<std::int64_t>();
-            info.mount = d["mount"].cast<std::string>();
-            info.queues = d["queues"].cast<std::uint32_t>();
-            if (d.contains("accelerators")) info.accelerators = d["accelerators"].cast<std::vector<std::int64_t>>();
-            devs.push_back(info);
-        }
-        tutti::daemon::LeaseLedger ledger(devs);
-        std::vector<std::string> out;
-        for (auto& l : lines) out.push_back(tutti::daemon::handle_request(ledger, l));
-        return out;
-    });
+    m.def(
+        "daemon_handle_request_selftest",
+        [](const std::vector<std::string>& lines, py::list devices, py::list accelerators) {
+            // Runs lines through an in-process ledger (protocol tests without a socket).
+            std::vector<tutti::daemon::DeviceInfo> devs;
+            for (auto item : devices) {
+                auto d = item.cast<py::dict>();
+                tutti::daemon::DeviceInfo info;
+                info.id = d["id"].cast<std::int64_t>();
+                info.mount = d["mount"].cast<std::string>();
+                info.queues = d["queues"].cast<std::uint32_t>();
+                if (d.contains("accelerators")) info.accelerators = d["accelerators"].cast<std::vector<std::int64_t>>();
+                if (d.contains("pci")) info.pci = d["pci"].cast<std::string>();
+                if (d.contains("chrdev")) info.chrdev = d["chrdev"].cast<std::string>();
+                if (d.contains("available")) info.available = d["available"].cast<bool>();
+                if (d.contains("diagnostic")) info.diagnostic = d["diagnostic"].cast<std::string>();
+                if (d.contains("lba_bytes")) info.lba_bytes = d["lba_bytes"].cast<std::uint32_t>();
+                devs.push_back(info);
+            }
+            tutti::daemon::LeaseLedger ledger(devs);
+            std::vector<tutti::daemon::AcceleratorView> views;
+            for (auto item : accelerators) {
+                auto a = item.cast<py::dict>();
+                views.push_back({a["accel_id"].cast<std::int64_t>(), a["view_root"].cast<std::string>()});
+            }
+            ledger.set_accelerators(views);
+            std::vector<std::string> out;
+            for (auto& l : lines) out.push_back(tutti::daemon::handle_request(ledger, l));
+            return out;
+        },
+        py::arg("lines"), py::arg("devices"), py::arg("accelerators") = py::list());
 
     m.def("make_stub_runtime", [](int accel_id) {
         RuntimeConfig c;

@@ -2,6 +2,7 @@
 
 #include <algorithm>
 #include <cerrno>
+#include <cstdio>
 #include <cstring>
 
 namespace tutti {
@@ -19,6 +20,7 @@ Result<std::unique_ptr<FakeSnvmeDriver>> FakeSnvmeDriver::create(const FakeSnvme
     if (!drive.ok()) return R::Failure(drive.status());
     d->drive_ = std::move(drive).value();
     d->qid_used_.assign(hw.num_io_queues + 1, false);
+    if (cfg.owner_mode) d->node_created_ = d->bound_ = false;
     return R(std::move(d));
 }
 
@@ -30,11 +32,47 @@ FakeSnvmeDriver::~FakeSnvmeDriver() {
 }
 
 int FakeSnvmeDriver::open_node(const std::string& path) {
-    if (path != cfg_.node) return -ENOENT;
     std::lock_guard<std::mutex> g(mu_);
+    const bool control = path == cfg_.control_node;
+    if (!control && (path != cfg_.node || !node_created_)) return -ENOENT;
     const int fd = next_fd_++;
-    files_.emplace(fd, File{});
+    File f;
+    f.control = control;
+    files_.emplace(fd, std::move(f));
     return fd;
+}
+
+int FakeSnvmeDriver::control_ioctl(unsigned long request, void* arg) {
+    snvme::uapi::PciAddress a;
+    std::memcpy(&a, arg, sizeof(a));
+    char text[32];
+    std::snprintf(text, sizeof(text), "%04x:%02x:%02x.%x", a.domain, a.bus, a.slot, a.function);
+    if (cfg_.pci != text) return -ENODEV;
+    switch (request) {
+        case uapi::kChrdevCreate:
+            if (node_created_) return -EEXIST;
+            node_created_ = true;
+            a.domain = cfg_.minor;  // the node's minor comes back in the domain field
+            std::memcpy(arg, &a, sizeof(a));
+            return 0;
+        case uapi::kChrdevRemove:
+            if (!node_created_) return -ENOENT;
+            if (bound_) return -EBUSY;
+            node_created_ = false;
+            return 0;
+        case uapi::kDeviceBind:
+            if (!node_created_) return -ENODEV;
+            if (bound_) return -EBUSY;
+            bound_ = true;
+            probe_polls_left_ = cfg_.probe_polls;
+            return 0;
+        case uapi::kDeviceUnbind:
+            if (!bound_) return -EINVAL;
+            bound_ = false;
+            return 0;
+        default:
+            return -ENOTTY;
+    }
 }
 
 int FakeSnvmeDriver::close_node(int fd) {
@@ -62,7 +100,12 @@ int FakeSnvmeDriver::ioctl_node(int fd, unsigned long request, void* arg) {
     }
     if (!arg) return -EFAULT;
     File& file = it->second;
+    if (file.control) return control_ioctl(request, arg);
     switch (request) {
+        case uapi::kSetKernelIoqCap:
+            if (bound_) return -EBUSY;  // a pre-bind hint
+            kernel_ioq_cap_ = *static_cast<std::uint32_t*>(arg);
+            return 0;
         case uapi::kGetDevInfo: return get_info(arg);
         case uapi::kCreateQueueGroup: return create_group(file, arg);
         case uapi::kDestroyQueueGroup: return destroy_group(file, *static_cast<std::uint32_t*>(arg));
@@ -83,7 +126,11 @@ int FakeSnvmeDriver::get_info(void* arg) {
     di.doorbell_stride_log = 0;
     di.max_transfer_bytes = hw.mdts_bytes;
     di.lba_bytes = hw.lba_bytes;
-    std::snprintf(di.disk_name, sizeof(di.disk_name), "%sn1", hw.name.c_str());
+    // the disk is named once the driver is bound and its namespace scan ran
+    if (bound_ && probe_polls_left_ == 0)
+        std::snprintf(di.disk_name, sizeof(di.disk_name), "%sn1", hw.name.c_str());
+    else if (bound_)
+        --probe_polls_left_;
     di.queue_depth = static_cast<std::uint16_t>(hw.queue_depth);
     di.bar0_bytes = static_cast<std::uint32_t>(drive_->bar0_bytes());
     di.max_queues_per_group = cfg_.max_queues_per_group;
@@ -259,6 +306,9 @@ FakeSnvmeDriver::Counts FakeSnvmeDriver::counts() const {
     }
     c.bar_maps = bar_maps_;
     c.registered = registered_;
+    c.node_created = node_created_;
+    c.bound = bound_;
+    c.kernel_ioq_cap = kernel_ioq_cap_;
     return c;
 }
 

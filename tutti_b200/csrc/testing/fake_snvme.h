@@ -41,6 +41,15 @@ struct FakeSnvmeConfig {
     std::uint32_t capabilities = snvme::uapi::kClientCaps | snvme::uapi::kCapRawAdmin | snvme::uapi::kCapKernelIoqCap;
     std::uint32_t first_user_qid = 1;
     std::uint32_t max_queues_per_group = snvme::uapi::kMaxQueuesPerGroup;
+    // Owner side: the control node binds `pci` and creates `node` (minor
+    // `minor`). With owner_mode the node exists only after CHRDEV_CREATE and
+    // the disk is named only after DEVICE_BIND plus `probe_polls` device-info
+    // queries (the namespace scan); without it the controller is already up.
+    std::string control_node = "/dev/snvm_control";
+    std::string pci = "0000:1b:00.0";
+    int minor = 0;
+    bool owner_mode = false;
+    std::uint32_t probe_polls = 2;
 };
 
 class FakeSnvmeDriver final : public nvme::SnvmeSys {
@@ -63,6 +72,8 @@ public:
 
     struct Counts {
         std::uint32_t files = 0, groups = 0, queues = 0, ring_maps = 0, data_maps = 0, bar_maps = 0, registered = 0;
+        bool node_created = false, bound = false;
+        std::uint32_t kernel_ioq_cap = 0;
     };
     Counts counts() const;
     std::vector<std::uint32_t> live_qids() const;
@@ -80,9 +91,13 @@ private:
         std::vector<std::uint32_t> qids;
     };
     struct File {
+        bool control = false;
         std::vector<Group> groups;
         std::vector<Mapping> data;
     };
+    int control_ioctl(unsigned long request, void* arg);
+    bool node_created_ = true, bound_ = true;
+    std::uint32_t probe_polls_left_ = 0, kernel_ioq_cap_ = 0;
     int get_info(void* arg);
     int create_group(File& f, void* arg);
     int destroy_group(File& f, std::uint32_t id);

@@ -448,3 +448,65 @@ TEST(snvme_provider_is_reported_missing_on_a_machine_without_the_driver) {
 
 }  // namespace native_tests
 }  // namespace tutti
+
+namespace tutti {
+namespace native_tests {
+
+TEST(snvme_owner_binds_creates_the_node_and_waits_for_the_scan) {
+    auto cfg = small_fake();
+    cfg.owner_mode = true;
+    cfg.probe_polls = 3;
+    auto fake = make_fake(cfg);
+    CHECK(fake != nullptr);
+    // before the owner: no node to attach to
+    CHECK(!SnvmeClient::attach("/dev/ssnvme0", *fake, false).ok());
+    {
+        auto o = nvme::SnvmeOwner::bring_up("/dev/snvm_control", "0000:1b:00.0", 16, *fake);
+        CHECK(o.ok());
+        CHECK(o.value()->node() == "/dev/ssnvme0" && o.value()->minor() == 0);
+        CHECK(o.value()->info().disk_name == "fake0n1" && o.value()->block_device() == "/dev/fake0n1");
+        const auto c = fake->counts();
+        CHECK(c.node_created && c.bound && c.kernel_ioq_cap == 16);
+        // a client attaches to the node the owner made
+        auto cl = SnvmeClient::attach(o.value()->node(), *fake, false);
+        CHECK(cl.ok());
+    }
+    const auto c = fake->counts();
+    CHECK(!c.node_created && !c.bound && c.files == 0);  // unbound and removed
+}
+
+TEST(snvme_owner_rejects_bad_addresses_and_undoes_a_failed_bind) {
+    auto cfg = small_fake();
+    cfg.owner_mode = true;
+    auto fake = make_fake(cfg);
+    CHECK(fake != nullptr);
+    CHECK(!nvme::parse_pci_address("1b:00.0").ok());
+    CHECK(!nvme::parse_pci_address("0000:1b:00.9").ok());
+    auto a = nvme::parse_pci_address("0000:1b:00.1");
+    CHECK(a.ok() && a.value().bus == 0x1b && a.value().function == 1);
+    // another function than the driver knows
+    auto wrong = nvme::SnvmeOwner::bring_up("/dev/snvm_control", "0000:1b:00.1", 0, *fake);
+    CHECK(!wrong.ok() && wrong.status().code() == StatusCode::NOT_FOUND);
+    // the bind fails: the node created before it is removed again
+    fake->fail_next(uapi::kDeviceBind, EIO);
+    auto failed = nvme::SnvmeOwner::bring_up("/dev/snvm_control", "0000:1b:00.0", 0, *fake);
+    CHECK(!failed.ok());
+    CHECK(!fake->counts().node_created && fake->counts().files == 0);
+    // no control node at all
+    auto none = nvme::SnvmeOwner::bring_up("/dev/snvm_absent", "0000:1b:00.0", 0, *fake);
+    CHECK(!none.ok() && none.status().code() == StatusCode::NOT_FOUND);
+}
+
+TEST(snvme_owner_times_out_when_the_scan_never_names_the_disk) {
+    auto cfg = small_fake();
+    cfg.owner_mode = true;
+    cfg.probe_polls = 1000000;
+    auto fake = make_fake(cfg);
+    CHECK(fake != nullptr);
+    auto o = nvme::SnvmeOwner::bring_up("/dev/snvm_control", "0000:1b:00.0", 0, *fake, /*probe_wait_ms=*/50);
+    CHECK(!o.ok() && o.status().code() == StatusCode::TIMEOUT);
+    CHECK(!fake->counts().bound && !fake->counts().node_created);
+}
+
+}  // namespace native_tests
+}  // namespace tutti
