@@ -74,7 +74,11 @@ def parse():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons every 100 ms during the timed region."""
+    """Samples nvidia-smi clocks/throttle reasons every 100 ms during the timed region.
+
+    (The same sampler as tutti_b200.common.clocks, kept here so that the reference arm
+    imports nothing of this package.)
+    """
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"

@@ -215,3 +215,28 @@ def test_two_gpu_fanout_restore_matches_local(tmp_path, mode, store):
 
     res = json.loads(line)
     assert res["ok"] and res["results"]["fanout"]["verified"] and res["results"]["local"]["verified"]
+
+
+@pytest.mark.gpu
+def test_ready_wait_returns_when_the_flag_is_set_and_reports_a_flag_that_never_is():
+    """One GPU: a wait on words already at the value passes at once; a wait on a word that
+    nothing sets gives up at its deadline, reports it, and the stream goes on."""
+    from tutti_b200 import ops
+
+    board = torch.zeros(4, dtype=torch.int64, device="cuda")
+    status = torch.full((2,), -1, dtype=torch.int32).pin_memory()
+    board[:2] = 7
+    ops.ready_wait(board.data_ptr(), 2, 7, 2_000_000_000, status[0:1])
+    torch.cuda.synchronize()
+    assert int(status[0]) == 0
+    # word 3 stays 0: the wait expires after 50 ms with word 1 of [2, 3] missing
+    after = torch.zeros(1, device="cuda")
+    ops.ready_wait(board.data_ptr() + 16, 2, 1, 50_000_000, status[1:2])
+    after.fill_(1.0)  # work behind the expired wait still runs
+    torch.cuda.synchronize()
+    assert int(status[1]) == 0b11 and float(after) == 1.0
+    # a signal stores the value into each target word
+    targets = torch.tensor([board.data_ptr() + 16, board.data_ptr() + 24], dtype=torch.int64, device="cuda")
+    ops.ready_signal(targets, 9)
+    torch.cuda.synchronize()
+    assert board.tolist() == [7, 7, 9, 9]

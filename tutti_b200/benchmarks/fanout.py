@@ -38,7 +38,7 @@ import torch.distributed as dist
 
 from ..index.chunk_index import chunk_keys_for_tokens
 from ..models.kv_geometry import DEEPSEEK_V3_MLA, LLAMA3_70B
-from ..parallel.fanout import FanoutRestorer, PeerPools, RestoreItem, owner_of
+from ..parallel.fanout import FanoutRestorer, PeerPools, ReadyBoard, RestoreItem, owner_of
 from ..storage.tutti_store import TuttiKVStore
 
 
@@ -55,6 +55,8 @@ def parse(argv=None):
     p.add_argument("--controller-threads", type=int, default=0)
     p.add_argument("--leases", type=int, default=128)
     p.add_argument("--ctas", type=int, default=64)
+    p.add_argument("--ordering", choices=["flags", "barrier"], default="flags",
+                   help="order each rank after every rank's share: device ready flags or a host barrier")
     p.add_argument("--store", choices=["local", "fanout"], default="local",
                    help="persist the prefix with each rank's own writes or through the drive-affine GPUs")
     p.add_argument("--stored-format", choices=["native", "fp8_block128"], default="native",
@@ -136,6 +138,9 @@ def main(argv=None) -> int:
     stream = torch.cuda.current_stream(dev)
 
     host_ms = {"local": [], "fanout": []}
+    board = ReadyBoard(local, group=ctl) if args.ordering == "flags" else None
+    epoch = [0]
+    pending, tickets = [], []
 
     def step(mode: str) -> None:
         t0 = time.perf_counter()
@@ -144,20 +149,39 @@ def main(argv=None) -> int:
         else:
             c = fan.restore(items, drives, affine, stream=stream, placements=placements)
         host_ms[mode].append((time.perf_counter() - t0) * 1e3)
+        if board is None:
+            if c is not None:
+                c.wait()
+            fan.barrier()  # a pool is whole only once every rank's share has landed
+            return
+        # device-side: raise this rank's flag behind its share, wait for every rank's
+        epoch[0] += 1
+        board.signal(0, epoch[0], stream)
+        tickets.append(board.wait(0, epoch[0], stream))
         if c is not None:
+            pending.append(c)
+
+    def settle() -> None:
+        torch.cuda.synchronize()
+        for c in pending:
             c.wait()
+        pending.clear()
+        missing = [board.failed(t) for t in tickets] if board is not None else []
+        tickets.clear()
+        if any(missing):
+            raise RuntimeError(f"ready flags timed out waiting for ranks {missing}")
 
     def timed(mode: str) -> float:
         for _ in range(args.warmup):
             step(mode)
-        fan.barrier()
+        settle()
+        dist.barrier(group=ctl)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
             step(mode)
-            fan.barrier()  # a pool is whole only once every rank's share has landed
         e1.record(stream)
-        torch.cuda.synchronize()
+        settle()
         t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
@@ -195,12 +219,14 @@ def main(argv=None) -> int:
     # teardown: nobody reads a peer pool after this barrier
     store.close()
     peers.close()
+    if board is not None:
+        board.close()
     dist.barrier(group=ctl)
     ok = all(r["verified"] for r in results.values())
     if rank == 0:
         print(json.dumps({"bench": "fanout", "mode": args.mode, "n_gpus": world, "model": g.fingerprint(),
                           "prefix_tokens": args.prefix_tokens, "drives": drives, "affine_gpus": affine,
-                          "steps": args.steps, "warmup": args.warmup, "results": results,
+                          "steps": args.steps, "warmup": args.warmup, "ordering": args.ordering, "results": results,
                           "store": {"mode": args.store, "wall_ms": round(store_ms, 1)},
                           "controllers": len(peers_stats), "ok": ok, "io_timing": timing}))
     del pool

@@ -5,7 +5,8 @@
     python -m tutti_b200.benchmarks.kernels hash     # chained BLAKE2b-128 prefix keys
     python -m tutti_b200.benchmarks.kernels checksum # KV block checksums
     python -m tutti_b200.benchmarks.kernels io       # fused NVMe io kernel restore (emulated controllers);
-                                                     #   --direction write: store; --async-completion: split launches
+                                                     #   --direction write: store; --async-completion: split launches;
+                                                     #   --media memory [--direct-reads]: drive DMA into HBM
 
 Each prints one JSON line: kernel time (CUDA events, after warm-up, inputs
 larger than L2 where the kernel is bandwidth-bound) and achieved rates.
@@ -13,14 +14,20 @@ larger than L2 where the kernel is bandwidth-bound) and achieved rates.
 """
 from __future__ import annotations
 
-import argparse
-import json
 import os
-import shutil
-import tempfile
 
-import numpy as np
-import torch
+# Before CUDA starts: emulated drives that DMA into HBM need eager kernel
+# loading and enough hardware queues (see the GPU NVMe data path).
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
+
+import argparse  # noqa: E402
+import json  # noqa: E402
+import shutil  # noqa: E402
+import tempfile  # noqa: E402
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
 
 
 def _time(fn, iters: int, warmup: int) -> float:
@@ -121,7 +128,8 @@ def bench_io(args) -> dict:
         st = TuttiKVStore(root, g, capacity_chunks=max(16, 2 * nch), mounts=[os.path.join(root, f"nvme{d}") for d in range(4)],
                           device=0, segment_file_slots=max(4, nch // 2 + 1), stored_format=args.stored_format,
                           runtime_options={"controller_threads": 3, "leases": 64, "max_ctas_per_op": 64,
-                                           "slots_per_lease": 8, "async_completion": bool(args.async_completion)})
+                                           "slots_per_lease": 8, "async_completion": bool(args.async_completion),
+                                           "emulator_media": args.media, "direct_reads": bool(args.direct_reads)})
         st.open()
         nb = 2 * nblk + 64
         pool = torch.randn(g.pool_shape(nb), dtype=g.dtype, device="cuda")
@@ -154,6 +162,7 @@ def bench_io(args) -> dict:
         nbytes = nblk * g.num_layers * g.block_layer_bytes
         st.close()
         return {"kernel": "nvme_io_kernel", "direction": "read", "async_completion": bool(args.async_completion),
+                "media": args.media, "direct_reads": bool(args.direct_reads),
                 "stored_format": args.stored_format, "bytes": nbytes, "ms": ms,
                 "GBps": nbytes / ms / 1e6, "ok": ok}
     finally:
@@ -173,6 +182,10 @@ def main(argv=None):
     p.add_argument("--stored-format", choices=["native", "fp8_block128"], default="native")
     p.add_argument("--direction", choices=["read", "write"], default="read", help="io: restore or store")
     p.add_argument("--async-completion", action="store_true", help="io: split submit / drain launches")
+    p.add_argument("--media", choices=["files", "memory"], default="files",
+                   help="io: emulated drives' media (memory: copy-engine DMA into HBM)")
+    p.add_argument("--direct-reads", action="store_true",
+                   help="io: drives DMA reads straight into the pool pages (memory media)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     fn = {"copy": bench_copy, "fp8": bench_fp8, "hash": bench_hash, "checksum": bench_checksum, "io": bench_io}

@@ -193,6 +193,11 @@ Status GpuNvmeDataPath::init_device_side() {
     if (staging_on_device_) {
         // The drives' copies are CUDA work in this process, so two process-wide
         // settings decide whether they can stall behind a running io kernel.
+        // Eager loading covers the kernels of modules loaded at startup; a
+        // library that loads kernels on first use (cuBLAS on a new GEMM shape)
+        // takes the same lock, so an application runs its shapes once before
+        // restores start (measured: the first 4096 x 4096 GEMM of a prefill
+        // held the host for 10 s while the drives' copies waited).
         const char* loading = std::getenv("CUDA_MODULE_LOADING");
         const char* conns = std::getenv("CUDA_DEVICE_MAX_CONNECTIONS");
         if (!loading || std::strcmp(loading, "EAGER") != 0)

@@ -56,5 +56,15 @@ cudaError_t launch_checksum_uniform(const CopyItem* items, std::uint32_t n, std:
 // floats) is written only if the chains hit an impossible value.
 cudaError_t launch_persistent_fma(float* out, std::uint64_t iters, std::uint32_t blocks, cudaStream_t stream);
 
+// Cross-GPU ready flags (ready_flags.cu): store `value` (system-scope release,
+// after a system fence) into each of `targets` (device array of n pointers,
+// peers' board words mapped through IPC); wait until all n words of `words`
+// reach `value` or `timeout_ns` passes (status: 0, or a mask of the words
+// still below; `status` may be host-mapped memory).
+cudaError_t launch_ready_signal(std::uint64_t* const* targets, std::uint32_t n, std::uint64_t value,
+                                cudaStream_t stream);
+cudaError_t launch_ready_wait(const std::uint64_t* words, std::uint32_t n, std::uint64_t value,
+                              std::uint64_t timeout_ns, std::uint32_t* status, cudaStream_t stream);
+
 }  // namespace ops
 }  // namespace tutti

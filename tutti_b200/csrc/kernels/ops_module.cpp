@@ -202,10 +202,41 @@ void persistent_fma(const at::Tensor& out, int64_t iters, int64_t blocks_per_sm)
                "persistent_fma launch");
 }
 
+// Ready flags: `targets` is a uint64 CUDA tensor of word addresses; runs on the current stream.
+void ready_signal(const at::Tensor& targets, int64_t value) {
+    TORCH_CHECK(targets.is_cuda() && targets.scalar_type() == at::kLong && targets.is_contiguous(),
+                "targets: int64 CUDA tensor of addresses");
+    const c10::cuda::CUDAGuard guard(targets.device());
+    check_cuda(launch_ready_signal(reinterpret_cast<std::uint64_t* const*>(targets.data_ptr<int64_t>()),
+                                   static_cast<std::uint32_t>(targets.numel()), static_cast<std::uint64_t>(value),
+                                   at::cuda::getCurrentCUDAStream()),
+               "ready_signal launch");
+}
+
+// Waits on the current stream until words[0..n) >= value (bounded); status: int32 tensor
+// (CUDA, or pinned host memory for a host read without a copy).
+void ready_wait(int64_t words, int64_t n, int64_t value, int64_t timeout_ns, const at::Tensor& status) {
+    TORCH_CHECK(status.scalar_type() == at::kInt && status.numel() >= 1, "status: int32 tensor");
+    TORCH_CHECK(n > 0 && n <= 1024 && timeout_ns > 0, "1..1024 words and a positive timeout");
+    void* st = status.data_ptr();
+    if (!status.is_cuda()) {
+        void* dev = nullptr;
+        TORCH_CHECK(cudaHostGetDevicePointer(&dev, st, 0) == cudaSuccess, "status: pinned, mapped host memory");
+        st = dev;
+    }
+    check_cuda(launch_ready_wait(reinterpret_cast<const std::uint64_t*>(words), static_cast<std::uint32_t>(n),
+                                 static_cast<std::uint64_t>(value), static_cast<std::uint64_t>(timeout_ns),
+                                 static_cast<std::uint32_t*>(st), at::cuda::getCurrentCUDAStream()),
+               "ready_wait launch");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "tutti_b200 sm_100a kernels: page copy, fp8 block scaling, prefix hashing, checksums, IPC";
     m.def("copy_items", &copy_items, py::arg("items"), py::arg("tma") = true);
     m.def("persistent_fma", &persistent_fma, py::arg("out"), py::arg("iters"), py::arg("blocks_per_sm") = 1);
+    m.def("ready_signal", &ready_signal, py::arg("targets"), py::arg("value"));
+    m.def("ready_wait", &ready_wait, py::arg("words"), py::arg("n"), py::arg("value"), py::arg("timeout_ns"),
+          py::arg("status"));
     m.def("fp8_quant", &fp8_quant, py::arg("x"), py::arg("group") = 128);
     m.def("fp8_dequant", &fp8_dequant, py::arg("q"), py::arg("scale"), py::arg("dtype") = at::kBFloat16);
     m.def("fp8_gather_quant", &fp8_gather_quant);

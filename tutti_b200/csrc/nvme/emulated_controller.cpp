@@ -47,16 +47,13 @@ std::uint64_t now_ns() {
             .count());
 }
 
-// The drives' CUDA streams live in a context of their own: a green context
-// over the whole device, which shares the application's address space (copies
-// reach its HBM) but not its hardware queues. On a queue shared with the
-// application, a drive stream sits behind any stream-ordered wait the
-// application queued there (a kernel queued behind a running io kernel, an
-// event wait on a restore) until the io deadline frees it, since that wait
-// depends on the drive's own copies: measured in a layerwise restore, where
-// every command of a layer timed out. Driver entry points are looked up
-// through the runtime (no libcuda link). TUTTI_EMULATOR_STREAMS=plain keeps
-// them in the application's context.
+// With TUTTI_EMULATOR_STREAMS=green the drives' CUDA streams live in a
+// context of their own: a green context over the whole device, which shares
+// the application's address space (copies reach its HBM) but not its
+// hardware queues, so no stream-ordered wait of the application can sit in
+// front of a drive's copies. Off by default: the stalls that first suggested
+// it were kernel loads (see the data path's notes), not queue sharing.
+// Driver entry points are looked up through the runtime (no libcuda link).
 struct GreenDriveStreams {
     using DeviceGet = CUresult (*)(CUdevice*, int);
     using GetResource = CUresult (*)(CUdevice, CUdevResource*, CUdevResourceType);
@@ -116,7 +113,7 @@ cudaStream_t create_drive_stream(int device, bool* green) {
     static GreenDriveStreams greens;
     *green = false;
     const char* how = std::getenv("TUTTI_EMULATOR_STREAMS");
-    if (!how || std::strcmp(how, "plain") != 0) {
+    if (how && std::strcmp(how, "green") == 0) {
         if (cudaStream_t s = greens.create(device)) {
             *green = true;
             return s;

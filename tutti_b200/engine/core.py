@@ -343,30 +343,13 @@ class KVEngine:
 
     @property
     def host_gated_layer_waits(self) -> bool:
-        """Layer waits block the host instead of the consumer stream.
+        """Layer waits block the host instead of the consumer stream (``TUTTI_LAYER_WAIT=host``).
 
-        Needed when the drives' DMA runs in this process (emulated drives that
-        copy into HBM staging on their own CUDA streams): a consumer stream
-        waiting on a restore's event sits at the head of a hardware queue, and a
-        drive stream that shares that queue could not issue the very copies the
-        wait is for until the restore's deadline expired. Real drives DMA on
-        their own, and then the wait stays on the device.
-        ``TUTTI_LAYER_WAIT=host|device`` overrides.
+        The default is a device-side wait: the consumer stream waits on the
+        restore's event and the host runs ahead. The host-gated form launches
+        layer l's consumer work only after the host saw layer l restored.
         """
-        forced = (text("TUTTI_LAYER_WAIT") or "").strip().lower()
-        if forced in ("host", "device"):
-            return forced == "host"
-        cached = getattr(self, "_host_gated", None)
-        if cached is None:
-            rt = getattr(self.store, "runtime", None)
-            cached = False
-            try:
-                if rt is not None and rt.staging_on_device():
-                    cached = any(c.get("emulated") for c in rt.controller_stats())
-            except (AttributeError, RuntimeError):
-                cached = False
-            self._host_gated = cached
-        return cached
+        return (text("TUTTI_LAYER_WAIT") or "").strip().lower() == "host"
 
     @property
     def split_completion(self) -> bool:

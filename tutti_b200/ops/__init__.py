@@ -183,3 +183,16 @@ def ipc_close(ptr: int, device: int) -> None:
 
 def enable_peer_access(device: int, peer: int) -> bool:
     return _ops().enable_peer_access(device, peer)
+
+
+def ready_signal(targets: torch.Tensor, value: int) -> None:
+    """Store ``value`` into every word whose address is in ``targets`` (int64 CUDA tensor), on the
+    current stream, after the stream's earlier work (system-scope fence, release stores)."""
+    _ops().ready_signal(targets, int(value))
+
+
+def ready_wait(words: int, n: int, value: int, timeout_ns: int, status: torch.Tensor) -> None:
+    """Make the current stream wait until the ``n`` 64-bit words at device address ``words`` all hold
+    at least ``value``, for at most ``timeout_ns``; ``status[0]`` becomes 0, or a mask of the words
+    still below ``value`` when the deadline passed (the stream then continues)."""
+    _ops().ready_wait(int(words), int(n), int(value), int(timeout_ns), status)

@@ -7,8 +7,10 @@ slice straight into that rank's paged pool (CUDA-IPC-mapped peer pointers,
 P2P stores over NVLink 5/NVSwitch): no staging copy on the peer, no separate
 scatter kernel, no NCCL all-gather. Replicated caches (an MLA latent cache is
 identical on every TP rank) are read once and stored to every rank's pool by
-the same kernel (replica groups). A collective after the restore orders the
-peers' subsequent work after the stores.
+the same kernel (replica groups). Each rank then orders its own later work
+after every rank's share on the device: a ReadyBoard flag that each rank
+raises behind its io kernel and that the consumer's stream waits on (bounded),
+with no host round trip; ``FanoutRestorer.barrier`` is the host-side form.
 
 Control plane: pool IPC handles and per-rank placements are exchanged with
 ``torch.distributed`` object collectives (no data crosses it).
@@ -32,6 +34,73 @@ from .. import ops
 def owner_of(key: bytes, group_size: int) -> int:
     """Replica owner of a chunk: its first 8 key bytes, little-endian, modulo the group."""
     return int.from_bytes(bytes(key[:8]), "little") % group_size
+
+
+class ReadyBoard:
+    """Device-side ordering between the ranks of a group.
+
+    Every rank holds a ``[slots, world]`` board of 64-bit words in its own HBM,
+    mapped into every peer through CUDA IPC. ``signal(slot, value)`` stores
+    ``value`` into this rank's column of ``slot`` on every board, on a stream,
+    behind that stream's earlier work (a system-scope fence first, so the io
+    kernel's NVLink stores to the peers are visible before the flag).
+    ``wait(slot, value)`` makes a stream wait until every rank's word of
+    ``slot`` on this rank's board reached ``value``: one thread of one CTA
+    polls, bounded by a deadline; past it the stream continues and
+    ``failed(ticket)`` reports which ranks were missing. Values grow
+    monotonically (an epoch per restore), so a slot is reused without a reset.
+    """
+
+    def __init__(self, device: int, group=None, slots: int = 64, status_words: int = 1024):
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.slots = slots
+        self.device = device
+        self.board = torch.zeros(slots, self.world, dtype=torch.int64, device=device)
+        handle, offset, _ = ops.ipc_export(self.board)
+        everyone: list = [None] * self.world
+        dist.all_gather_object(everyone, (handle, offset, device), group=group)
+        self._opened: list[int] = []
+        bases = []
+        for r, (h, off, devi) in enumerate(everyone):
+            if r == self.rank:
+                bases.append(self.board.data_ptr())
+            else:
+                ops.enable_peer_access(device, devi)
+                base = ops.ipc_open(h, device)
+                self._opened.append(base)
+                bases.append(base + off)
+        # targets[s, r]: this rank's word of slot s on rank r's board
+        t = [[bases[r] + 8 * (s * self.world + self.rank) for r in range(self.world)] for s in range(slots)]
+        self._targets = torch.tensor(t, dtype=torch.int64, device=device)
+        self._status = torch.zeros(status_words, dtype=torch.int32).pin_memory()
+        self._next_status = 0
+
+    def signal(self, slot: int, value: int, stream: torch.cuda.Stream | None = None) -> None:
+        with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
+            ops.ready_signal(self._targets[slot], value)
+
+    def wait(self, slot: int, value: int, stream: torch.cuda.Stream | None = None, timeout_s: float = 10.0) -> int:
+        """Enqueue the wait; returns a ticket for ``failed`` (read once the stream passed the wait)."""
+        ticket = self._next_status
+        self._next_status = (self._next_status + 1) % self._status.numel()
+        self._status[ticket] = -1
+        words = self.board.data_ptr() + 8 * slot * self.world
+        with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
+            ops.ready_wait(words, self.world, value, int(timeout_s * 1e9), self._status[ticket:ticket + 1])
+        return ticket
+
+    def failed(self, ticket: int) -> list[int]:
+        """Ranks the wait gave up on (empty: all arrived); valid after the stream passed the wait."""
+        v = int(self._status[ticket]) & 0xFFFFFFFF
+        if v == 0xFFFFFFFF:
+            raise RuntimeError("the wait has not run yet")
+        return [r for r in range(min(self.world, 31)) if v & (1 << r)] + ([31] if v & (1 << 31) else [])
+
+    def close(self) -> None:
+        for p in self._opened:
+            ops.ipc_close(p, self.device)
+        self._opened.clear()
 
 
 class PeerPools:
