@@ -33,6 +33,8 @@
 #include <thread>
 #include <vector>
 
+#include <cuda_runtime_api.h>
+
 #include <tutti/status.h>
 
 #include "host_memory.h"
@@ -141,6 +143,10 @@ public:
     // The emulated drive that answers this controller's queues, if any (its
     // namespace is backed by files and it takes host-side fault injection).
     virtual class EmulatedNvmeController* emulated_drive() { return nullptr; }
+    // Makes every completed WRITE durable in the files a host process reads
+    // (a drive with a volatile write cache writes it back). A real drive's
+    // cache is flushed by the file system's own sync of those files.
+    virtual Status flush() { return Status::Ok(); }
 };
 
 struct EmulatedControllerConfig {
@@ -173,6 +179,12 @@ struct EmulatedControllerConfig {
     Media media = Media::FILES;
     std::uint64_t image_chunk_bytes = 64ull << 20;
     std::uint64_t image_budget_bytes = 0;
+    // Memory media only: a volatile write cache. A WRITE completes once its
+    // bytes are in the image (for GPU memory: its copy queued on the worker's
+    // stream, the CQE written after it); the dirty ranges reach the files on
+    // FLUSH, on flush(), when a file is detached and when the drive stops.
+    // Off: every WRITE is written through to its file before its CQE.
+    bool write_back = false;
     // Queue pairs are created by a driver over rings it was given
     // (create_io_queue_pair) instead of existing from the start on the
     // controller's own rings.
@@ -223,8 +235,10 @@ public:
     // `status`: for MEDIA_ERROR, the CQE status field (type and code) to post; 0: unrecovered read error.
     void inject(InjectKind kind, std::uint32_t count, std::uint32_t delay_us = 0, std::uint32_t status = 0);
 
-    // Stop workers (idempotent). Outstanding SQEs are left unexecuted.
+    // Stop workers (idempotent). Outstanding SQEs are left unexecuted; a write
+    // cache is written back.
     void stop();
+    Status flush() override;
 
 private:
     explicit EmulatedNvmeController(const EmulatedControllerConfig& cfg);
@@ -275,7 +289,14 @@ private:
         std::unique_ptr<std::atomic<char*>[]> chunks;
         std::size_t n_chunks = 0;
         std::mutex load_mu;
+        // write cache: per image chunk the dirty byte range [first, second) within it
+        std::unique_ptr<std::pair<std::uint64_t, std::uint64_t>[]> dirty;
+        std::mutex dirty_mu;
     };
+    void mark_dirty(Backing* b, std::uint64_t foff, std::uint64_t n);
+    Status write_back(Backing* b);
+    std::mutex streams_mu_;
+    std::vector<cudaStream_t> worker_streams_;  // registered while their workers run
     struct Window {
         std::uint64_t base;
         std::uint64_t bytes;

@@ -277,6 +277,83 @@ void EmulatedNvmeController::stop() {
     for (auto& t : workers_)
         if (t.joinable()) t.join();
     workers_.clear();
+    if (cfg_.write_back) (void)flush();  // the workers drained their streams on exit
+}
+
+void EmulatedNvmeController::mark_dirty(Backing* b, std::uint64_t foff, std::uint64_t n) {
+    const std::uint64_t cb = cfg_.image_chunk_bytes;
+    const std::size_t ci = static_cast<std::size_t>(foff / cb);
+    const std::uint64_t lo = foff % cb, hi = lo + n;  // n never crosses the chunk
+    std::lock_guard<std::mutex> g(b->dirty_mu);
+    auto& d = b->dirty[ci];
+    if (d.second <= d.first) {
+        d = {lo, hi};
+    } else {
+        d.first = std::min(d.first, lo);
+        d.second = std::max(d.second, hi);
+    }
+}
+
+Status EmulatedNvmeController::write_back(Backing* b) {
+    if (!b->dirty || b->fd < 0) return Status::Ok();
+    const std::uint64_t cb = cfg_.image_chunk_bytes;
+    std::vector<std::pair<std::size_t, std::pair<std::uint64_t, std::uint64_t>>> todo;
+    {
+        std::lock_guard<std::mutex> g(b->dirty_mu);
+        for (std::size_t ci = 0; ci < b->n_chunks; ++ci) {
+            auto& d = b->dirty[ci];
+            if (d.second > d.first) todo.push_back({ci, d});
+            d = {0, 0};
+        }
+    }
+    Status first;
+    for (const auto& t : todo) {
+        const char* base = b->chunks[t.first].load(std::memory_order_acquire);
+        const std::uint64_t lo = t.second.first, len = t.second.second - t.second.first;
+        std::uint64_t done = 0;
+        const std::uint64_t t0 = now_ns();
+        while (base && done < len) {
+            const ssize_t w = ::pwrite(b->fd, base + lo + done, len - done, static_cast<off_t>(t.first * cb + lo + done));
+            if (w < 0 && errno == EINTR) continue;
+            if (w <= 0) break;
+            done += static_cast<std::uint64_t>(w);
+        }
+        st_file_ns_.fetch_add(now_ns() - t0, std::memory_order_relaxed);
+        if (done < len) {
+            mark_dirty(b, t.first * cb + lo, len);  // keep it for the next flush
+            if (first.ok()) first = {StatusCode::DEVICE_ERROR, "write-back of " + b->path + " failed"};
+        }
+    }
+    if (!todo.empty() && ::fdatasync(b->fd) != 0 && first.ok())
+        first = {StatusCode::DEVICE_ERROR, "fdatasync of " + b->path + " failed"};
+    return first;
+}
+
+Status EmulatedNvmeController::flush() {
+    if (!cfg_.write_back) {
+        std::lock_guard<std::mutex> g(map_mu_);
+        for (auto& b : backings_)
+            if (b->fd >= 0) ::fdatasync(b->fd);
+        return Status::Ok();
+    }
+    // Every copy queued so far has landed in the image (the WRITEs that completed
+    // posted their CQEs after their copies; this also waits for those in flight).
+    {
+        std::lock_guard<std::mutex> g(streams_mu_);
+        for (cudaStream_t st : worker_streams_)
+            if (cudaStreamSynchronize(st) != cudaSuccess) cudaGetLastError();
+    }
+    std::vector<Backing*> bs;
+    {
+        std::lock_guard<std::mutex> g(map_mu_);
+        for (auto& b : backings_) bs.push_back(b.get());
+    }
+    Status first;
+    for (Backing* b : bs) {
+        Status s = write_back(b);
+        if (first.ok() && !s.ok()) first = s;
+    }
+    return first;
 }
 
 static QueuePairView make_view(char* sq, char* cq, char* bar, std::uint32_t i, std::uint32_t depth,
@@ -478,6 +555,7 @@ Status EmulatedNvmeController::attach_file(const std::string& path, const std::v
             nb->n_chunks = static_cast<std::size_t>((nb->file_bytes + cfg_.image_chunk_bytes - 1) / cfg_.image_chunk_bytes);
             nb->chunks.reset(new std::atomic<char*>[nb->n_chunks]);
             for (std::size_t i = 0; i < nb->n_chunks; ++i) nb->chunks[i].store(nullptr);
+            nb->dirty.reset(new std::pair<std::uint64_t, std::uint64_t>[nb->n_chunks]());
         }
         target = nb.get();
         backings_.push_back(std::move(nb));
@@ -507,6 +585,14 @@ Status EmulatedNvmeController::detach_file(const std::string& path) {
         return b->path == path;
     });
     if (it == backings_.end()) return {StatusCode::NOT_FOUND, "not attached: " + path};
+    if (cfg_.write_back) {
+        {
+            std::lock_guard<std::mutex> sg(streams_mu_);
+            for (cudaStream_t st : worker_streams_)
+                if (cudaStreamSynchronize(st) != cudaSuccess) cudaGetLastError();
+        }
+        TUTTI_RETURN_IF_ERROR(write_back(it->get()));  // the file holds every completed WRITE
+    }
     // Keep the fd and the image open (a worker may hold a span snapshot); clear its ranges.
     (*it)->ranges.clear();
     auto spans = std::make_shared<std::vector<Span>>();
@@ -707,11 +793,15 @@ std::uint32_t EmulatedNvmeController::move_span(bool read, Backing* b, int fd, c
                     }
                     st_dma_copies_.fetch_add(1, std::memory_order_relaxed);
                     w.stream_dirty = true;
-                    if (!sync_stream()) return xfer_error;
+                    // write cache: the CQE follows the copy on the stream; else the file first
+                    if (!cfg_.write_back && !sync_stream()) return xfer_error;
                 } else {
                     std::memcpy(img, buf, k);
                 }
-                if (!file_io(img, k, foff)) return media_error;  // write-through: the file stays durable
+                if (cfg_.write_back)
+                    mark_dirty(b, foff, k);
+                else if (!file_io(img, k, foff))
+                    return media_error;  // write-through: the file stays durable
             }
             buf += k;
             foff += k;
@@ -784,10 +874,10 @@ std::uint32_t EmulatedNvmeController::execute(const Sqe& sqe, WorkerCtx& w, bool
     }
 
     if (op == kOpFlush) {
-        std::lock_guard<std::mutex> g(map_mu_);
-        for (auto& b : backings_)
-            if (b->fd >= 0) ::fdatasync(b->fd);
-        return 0;
+        // this worker's own copies first (flush() waits for every worker's stream)
+        if (w.stream_dirty && cudaStreamSynchronize(w.stream) != cudaSuccess) cudaGetLastError();
+        w.stream_dirty = false;
+        return flush().ok() ? 0u : make_status(0, kScDataTransferError);
     }
     if (op != kOpRead && op != kOpWrite) {
         st_errors_.fetch_add(1);
@@ -854,7 +944,8 @@ std::uint32_t EmulatedNvmeController::execute(const Sqe& sqe, WorkerCtx& w, bool
                 st_errors_.fetch_add(1);
                 return st;
             }
-            if (read && s.device) *on_stream = true;
+            // the CQE follows the copy on the stream (a cached WRITE's slot is reused only after it)
+            if (s.device && (read || cfg_.write_back)) *on_stream = true;
             chunk -= n;
             pos += n;
             foff += n;
@@ -961,6 +1052,10 @@ void EmulatedNvmeController::worker_main(std::uint32_t worker) {
         w.stream = create_drive_stream(cuda_device_, &green);
         w.cuda = w.stream != nullptr;
         if (green) st_green_streams_.fetch_add(1, std::memory_order_relaxed);
+        if (w.stream) {
+            std::lock_guard<std::mutex> g(streams_mu_);
+            worker_streams_.push_back(w.stream);
+        }
     } else {
         cudaGetLastError();
     }
@@ -980,6 +1075,11 @@ void EmulatedNvmeController::worker_main(std::uint32_t worker) {
     }
     if (w.stream) {
         cudaStreamSynchronize(w.stream);
+        {
+            std::lock_guard<std::mutex> g(streams_mu_);
+            worker_streams_.erase(std::remove(worker_streams_.begin(), worker_streams_.end(), w.stream),
+                                  worker_streams_.end());
+        }
         cudaStreamDestroy(w.stream);
     }
     cudaGetLastError();

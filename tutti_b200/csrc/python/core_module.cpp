@@ -445,6 +445,15 @@ PYBIND11_MODULE(_core, m) {
                  auto s = r.rt->state();
                  return std::string(s == RuntimeState::RUNNING ? "running" : s == RuntimeState::DRAINING ? "draining" : "stopped");
              })
+        .def("flush_devices",
+             [](PyRuntime& r) {
+                 // every completed WRITE durable in its file (drives with a write cache write back)
+                 py::gil_scoped_release nogil;
+                 for (auto& c : r.extras.controllers) {
+                     Status s = c->flush();
+                     if (!s.ok()) throw std::runtime_error(s.to_string());
+                 }
+             })
         .def("controller_stats",
              [](PyRuntime& r) {
                  py::list out;
@@ -577,6 +586,7 @@ PYBIND11_MODULE(_core, m) {
             if (opts.contains("snvme_rings_in_gpu_memory"))
                 o.snvme_rings_in_gpu_memory = opts["snvme_rings_in_gpu_memory"].cast<bool>();
             if (opts.contains("image_budget_bytes")) o.image_budget_bytes = opts["image_budget_bytes"].cast<std::uint64_t>();
+            if (opts.contains("emulator_write_back")) o.write_back = opts["emulator_write_back"].cast<bool>();
             if (opts.contains("drive_gbps")) o.drive_gbps = opts["drive_gbps"].cast<double>();
             if (opts.contains("staging")) {
                 const std::string where = opts["staging"].cast<std::string>();

@@ -32,6 +32,7 @@ Result<PresetResult> make_emulated_nvme_runtime(const EmulatedPresetOptions& o) 
         c.media = o.media == "memory" ? nvme::EmulatedControllerConfig::Media::MEMORY
                                       : nvme::EmulatedControllerConfig::Media::FILES;
         c.image_budget_bytes = o.image_budget_bytes;
+        c.write_back = o.write_back && c.media == nvme::EmulatedControllerConfig::Media::MEMORY;
         c.max_gbps = o.drive_gbps;
         c.cuda_device = o.accel_id;
         c.name = "emu" + std::to_string(i);

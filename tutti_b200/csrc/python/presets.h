@@ -42,6 +42,7 @@ struct EmulatedPresetOptions {
     // image of the backing files, loaded on first touch, written through).
     std::string media = "files";
     std::uint64_t image_budget_bytes = 0;  // 0: no limit
+    bool write_back = false;  // memory media: a volatile write cache (durable on flush)
     double drive_gbps = 0.0;               // per-drive transfer cap (0: none)
     std::string mapping = "auto";      // fiemap | synthetic | auto
     std::string raid0_md;              // non-empty: mounts[0] is an md RAID0 array

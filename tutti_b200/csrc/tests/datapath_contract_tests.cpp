@@ -365,3 +365,70 @@ TEST(emulated_controller_rejects_bad_configurations) {
     c.max_gbps = -1;
     CHECK(!nvme::EmulatedNvmeController::create(c).ok());
 }
+
+namespace tutti {
+namespace native_tests {
+
+namespace {
+std::vector<unsigned char> file_bytes_at(const std::string& path, std::uint64_t off, std::size_t n) {
+    std::vector<unsigned char> out(n);
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd >= 0) {
+        (void)!::pread(fd, out.data(), n, static_cast<off_t>(off));
+        ::close(fd);
+    }
+    return out;
+}
+}  // namespace
+
+TEST(emulated_write_cache_reaches_the_file_on_flush_only) {
+    nvme::EmulatedControllerConfig cfg;
+    cfg.media = nvme::EmulatedControllerConfig::Media::MEMORY;
+    cfg.image_chunk_bytes = 1u << 20;
+    cfg.write_back = true;
+    Drive d(cfg);
+    HostSubmitter hs{d.ctl->host_queue(0)};
+    std::memset(d.buf, 0xA5, 8192);
+    nvme::Sqe w{};
+    nvme::build_rw_sqe(w, nvme::kOpWrite, 1, 1, (2u << 20) / 512, 16, d.iova, d.iova + 4096);
+    CHECK(hs.run(w) == 0);
+    // the drive answers reads from its cache, the file still holds the old bytes
+    std::memset(d.buf, 0, 8192);
+    CHECK(hs.run(d.read(2, 2u << 20, 8192, d.iova, d.iova + 4096)) == 0);
+    CHECK(static_cast<unsigned char*>(d.buf)[8191] == 0xA5);
+    CHECK(file_bytes_at(d.path, 2u << 20, 8192) == std::vector<unsigned char>(d.pattern.begin() + (2u << 20),
+                                                                              d.pattern.begin() + (2u << 20) + 8192));
+    CHECK(d.ctl->flush().ok());
+    CHECK(file_bytes_at(d.path, 2u << 20, 8192) == std::vector<unsigned char>(8192, 0xA5));
+}
+
+TEST(emulated_write_cache_is_written_back_by_flush_commands_detach_and_stop) {
+    nvme::EmulatedControllerConfig cfg;
+    cfg.media = nvme::EmulatedControllerConfig::Media::MEMORY;
+    cfg.image_chunk_bytes = 1u << 20;
+    cfg.write_back = true;
+    Drive d(cfg);
+    HostSubmitter hs{d.ctl->host_queue(0)};
+    auto write_at = [&](std::uint16_t cid, std::uint64_t off, unsigned char v) {
+        std::memset(d.buf, v, 4096);
+        nvme::Sqe w{};
+        nvme::build_rw_sqe(w, nvme::kOpWrite, cid, 1, off / 512, 8, d.iova, 0);
+        return hs.run(w);
+    };
+    CHECK(write_at(1, 0, 0x11) == 0);
+    nvme::Sqe f{};
+    f.cdw0 = nvme::kOpFlush | (2u << 16);
+    f.nsid = 1;
+    CHECK(hs.run(f) == 0);  // an NVMe FLUSH writes the cache back
+    CHECK(file_bytes_at(d.path, 0, 4096) == std::vector<unsigned char>(4096, 0x11));
+    CHECK(write_at(3, 5u << 20, 0x22) == 0);
+    CHECK(d.ctl->detach_file(d.path).ok());  // detaching writes the file's dirty ranges back
+    CHECK(file_bytes_at(d.path, 5u << 20, 4096) == std::vector<unsigned char>(4096, 0x22));
+    (void)d.ctl->attach_file(d.path, {{0, d.pattern.size(), 0}});
+    CHECK(write_at(4, 6u << 20, 0x33) == 0);
+    d.ctl->stop();  // stopping the drive writes back too
+    CHECK(file_bytes_at(d.path, 6u << 20, 4096) == std::vector<unsigned char>(4096, 0x33));
+}
+
+}  // namespace native_tests
+}  // namespace tutti

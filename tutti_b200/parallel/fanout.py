@@ -252,6 +252,10 @@ class FanoutRestorer:
                 if todo:
                     self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64),
                                                 np.asarray(mems, np.uint64), stream=stream).wait()
+                # this GPU's drives hold other ranks' chunks too: durable before anyone commits
+                flush = getattr(getattr(self.kv, "runtime", None), "flush_devices", None)
+                if flush is not None:
+                    flush()
             except Exception as e:  # noqa: BLE001  (reported through the collective below)
                 errors.append(f"rank {me}: {e}")
                 ok = False

@@ -175,7 +175,8 @@ class TuttiKVStore:
         self.device = device
         self.backend = backend
         self.mounts = [str(m) for m in (mounts or [self.root / "dev0"])]
-        self.runtime_options = {**runtime_option_defaults(), **dict(runtime_options or {})}
+        # emulated drives with in-memory media get a write cache: this store flushes before it commits
+        self.runtime_options = {"emulator_write_back": True, **runtime_option_defaults(), **dict(runtime_options or {})}
         self.prp_mode = prp_mode()
         self.stored = stored_geometry(geometry, stored_format)
         if stored_format != "native" and backend != "nvme-gpu":
@@ -493,10 +494,18 @@ class TuttiKVStore:
         except Exception:
             self.objects.abort(wkeys)
             raise
-        comp = NativeCompletion(self.runtime, ios, on_success=lambda: self.objects.commit(wkeys),
+        comp = NativeCompletion(self.runtime, ios, on_success=lambda: self._commit(wkeys),
                                 on_failure=lambda: self.objects.abort(wkeys), nbytes=nbytes, kind="store")
         self._track(comp)
         return comp
+
+    def _commit(self, keys) -> None:
+        """Payload durable on the drives first (a drive's write cache is written back), then the
+        object store's commit (payload fdatasync, headers, their fdatasync)."""
+        flush = getattr(self.runtime, "flush_devices", None)
+        if flush is not None:
+            flush()
+        self.objects.commit(keys)
 
     def _track(self, comp: NativeCompletion) -> None:
         self._inflight.append(comp)
