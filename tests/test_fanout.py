@@ -240,3 +240,74 @@ def test_ready_wait_returns_when_the_flag_is_set_and_reports_a_flag_that_never_i
     ops.ready_signal(targets, 9)
     torch.cuda.synchronize()
     assert board.tolist() == [7, 7, 9, 9]
+
+
+def _replica_io_worker_rank(rank, world, port, q, root):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        from tutti_b200.integration.vllm.factory import ConnectorConfig, make_engine
+        from tutti_b200.integration.vllm.metadata import LoadSpec, SaveSpec, TuttiConnectorMetadata
+        from tutti_b200.integration.vllm.worker import WorkerSide
+
+        bs, chunk, nl, nb = 16, 64, 4, 128
+        cfg = ConnectorConfig.from_extra({
+            "chunk_tokens": chunk, "replica_io": True,
+            "store": {"type": "tutti", "root": f"{root}/r{{RANK}}",
+                      "mounts": [f"{root}/nvme0", f"{root}/nvme1"], "capacity_chunks": 64,
+                      "segment_file_slots": 16,
+                      "runtime_options": {"leases": 16, "max_ctas_per_op": 8, "emulator_media": "memory",
+                                          "image_budget_bytes": 256 << 20}}})
+        g = torch.Generator(device="cuda").manual_seed(100 + rank)
+        # this rank's KV-head slice: different values on every rank
+        layers = [torch.randn(2, nb, bs, 2, 128, device="cuda", generator=g, dtype=torch.bfloat16) for _ in range(nl)]
+        w = WorkerSide(lambda t, entity="": make_engine(cfg, t, rank, rank, world, entity), block_size=bs,
+                       chunk_tokens=chunk, tp_rank=rank, tp_size=world, replica_io=True, group=dist.group.WORLD)
+        w.register_kv_caches({f"model.layers.{i}.self_attn.attn": t for i, t in enumerate(layers)})
+        assert w._fan is not None, "replica_io was not set up"
+        keys = [bytes([i + 1]) * 16 for i in range(6)]
+        src = list(range(0, 24))  # 6 chunks x 4 blocks
+        w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, src)]))
+        for _ in range(2000):
+            if w.saves_in_flight() == 0:
+                break
+            w.wait_for_save(TuttiConnectorMetadata(2, [], []))
+        ref = [t[:, 0:24].clone() for t in layers]
+        dst = list(range(64, 88))
+        for t in layers:
+            t[:, 64:88].zero_()
+        meta = TuttiConnectorMetadata(3, [LoadSpec("b", keys, dst, len(keys) * chunk)], [])
+        w.start_load_kv(meta)
+        for i in range(nl):
+            w.wait_for_layer_load(f"model.layers.{i}.self_attn.attn")
+        wm = w.wait_for_save(meta)
+        torch.cuda.synchronize()
+        ok = all(torch.equal(layers[i][:, 64:88], ref[i]) for i in range(nl))
+        stats = w.engine.store.runtime.controller_stats()
+        q.put((rank, (ok, dict(wm.failed_loads), sum(s["read_bytes"] for s in stats))))
+        dist.barrier()
+        w.shutdown()
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, "".join(traceback.format_exception(e))[-3000:]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_gpu_vllm_worker_with_replica_io_restores_every_rank(tmp_path):
+    """replica_io in the vLLM worker: each GPU reads the chunks on its affine drive for both
+    ranks, its io kernel stores each rank's slice into that rank's per-layer caches over NVLink,
+    and every layer's attention waits on device-side ready flags from both ranks."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _spawn(_replica_io_worker_rank, 2, str(tmp_path))
+    for r in range(2):
+        assert isinstance(out[r], tuple), out[r]
+        ok, failed, read_bytes = out[r]
+        assert ok and failed == {}
+    # drive-affine: each GPU read part of the chunks (for both ranks), none read them all
+    assert all(out[r][2] > 0 for r in range(2))

@@ -79,7 +79,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                       # vLLM's scheduler applies kv_load_failure_policy (recompute or fail the
                                       # requests) to the blocks the worker reports; the worker only reports
                                       failure_policy="recompute", lookahead=self.cfg.lookahead_k,
-                                      max_inflight_saves=self.cfg.max_inflight_saves)
+                                      max_inflight_saves=self.cfg.max_inflight_saves,
+                                      replica_io=self.cfg.replica_io, group=cpu_group)
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""

@@ -15,7 +15,8 @@
   physical_chunk_tokens    must equal chunk_tokens (one object per chunk)
   direct_transfer          true: refuse a store that moves chunks through staging buffers
   max_chunks_per_wave      accepted; a restore is one submission the io kernel pipelines
-  replica_io               accepted with a warning: the worker restores each rank's own slice
+  replica_io               each GPU reads the chunks on its affine drives for every TP rank and stores
+                           each rank's slice into that rank's caches over NVLink (TP > 1)
   kv_load_failure_policy   recompute | fail: vLLM's own kv_transfer_config field governs, applied by
                            vLLM's scheduler to the blocks the worker reports as failed
   store:
@@ -85,6 +86,7 @@ class ConnectorConfig:
     failure_timeout_s: float = 30.0
     lookahead_k: int = 4  # layers restored ahead of the layer attention is waiting for
     max_inflight_saves: int = 64  # saves in flight per worker before a step waits for the oldest
+    replica_io: bool = False  # drive-affine reads for every TP rank, stored over NVLink
     expect: dict = field(default_factory=dict)  # num_layers / chunk_kv_bytes / segment_bytes given in the config
     direct_transfer: bool = False  # require the direct (paged) path
     segment_header_bytes: int = 0  # 0: the store's default
@@ -116,9 +118,7 @@ class ConnectorConfig:
         c.direct_transfer = bool(extra.get("direct_transfer", False))
         if "max_chunks_per_wave" in extra and int(extra["max_chunks_per_wave"]) <= 0:
             raise ValueError("max_chunks_per_wave must be positive")
-        if extra.get("replica_io"):
-            LOG.warning("[tutti] replica_io is not wired into the vLLM worker here: each TP rank restores its "
-                        "own slice (the NVLink fan-out is available as parallel.fanout.FanoutRestorer)")
+        c.replica_io = bool(extra.get("replica_io", False))
         c.lookahead_k = extra.get("lookahead_k", c.lookahead_k)
         if not isinstance(c.lookahead_k, int) or isinstance(c.lookahead_k, bool) or c.lookahead_k <= 0:
             raise ValueError(f"lookahead_k must be a positive integer, got {c.lookahead_k!r}")

@@ -122,7 +122,7 @@ class WorkerSide:
     def __init__(self, make_engine: Callable[..., KVEngine], *, block_size: int,
                  chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
                  consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute",
-                 lookahead: int = 4, max_inflight_saves: int = 64):
+                 lookahead: int = 4, max_inflight_saves: int = 64, replica_io: bool = False, group=None):
         if failure_policy not in ("recompute", "fail"):
             raise ValueError("kv_load_failure_policy must be recompute or fail")
         self.make_engine = make_engine
@@ -147,6 +147,13 @@ class WorkerSide:
         self._step_timing: list[tuple[object, object, int]] = []  # (start, end, tokens) of steps w/o sync reads
         self._step: tuple[object, int, bool] | None = None  # this step's start event, tokens, had sync loads
         self.max_inflight_saves = max(1, int(max_inflight_saves))
+        # replica_io: each GPU reads the chunks on the drives affine to it for every TP rank
+        # and its io kernel stores each rank's slice into that rank's caches over NVLink
+        self.replica_io = bool(replica_io) and tp_size > 1
+        self.group = group
+        self._fan = None
+        self._board = None
+        self._epoch = 0
         self._saves: deque = deque()  # (SaveSpec, completion) in submission order
         self._saves_of: dict[str, int] = {}  # request id -> saves in flight on this rank
         self._had_saves: set[str] = set()  # requests with a save on this rank (their blocks wait for it)
@@ -164,6 +171,8 @@ class WorkerSide:
             groups.setdefault((t.shape[0],) + tuple(t.shape[2:]) + (t.dtype,), []).append(n)
         if len(groups) == 1:
             self.engine = self.make_engine([views[n] for n in names])
+            if self.replica_io:
+                self._setup_fanout([views[n] for n in names])
             return
         ordered = sorted(groups.values(), key=len, reverse=True)  # the main KV has the most layers
         engines, where = [], {}
@@ -173,6 +182,21 @@ class WorkerSide:
             for li, n in enumerate(members):
                 where[n] = (e, li)
         self.engine = EntityEngines(engines, [where[n] for n in names], [entity_tag(g[0]) for g in ordered])
+
+    def _setup_fanout(self, layers) -> None:
+        """Peer mappings of every rank's per-layer caches and a ready-flag board (collective)."""
+        from ...parallel.fanout import FanoutRestorer, PeerLayers, ReadyBoard
+
+        store = self.engine.store
+        if not hasattr(store, "restore_placements") or self.engine.staged:
+            LOG.warning("[tutti] replica_io needs the direct (paged) NVMe store; each rank restores its own slice")
+            self.replica_io = False
+            return
+        self._peers = PeerLayers(layers, self.group)
+        self._fan = FanoutRestorer(store, self._peers, self.group)
+        self._board = ReadyBoard(layers[0].device.index, self.group, slots=len(layers))
+        self._n_drives = max(1, len(getattr(store, "mounts", [None])))
+        self._affine = list(range(self.tp_size))
 
     # -- loads ----------------------------------------------------------------
     def start_load_kv(self, meta: TuttiConnectorMetadata) -> None:
@@ -196,12 +220,25 @@ class WorkerSide:
             keys = [k for s in sync for k in s.keys]
             blocks = np.asarray([b for s in sync for b in s.block_ids], dtype=np.int64)
             try:
-                if self.engine.staged:
+                if self._fan is not None:
+                    self._plan = self._start_fanout_plan(keys, blocks)
+                elif self.engine.staged:
                     self._plan = self.engine.load(keys, blocks)
                 else:
                     self._plan = self.engine.start_read_plan(keys, blocks, window=self.lookahead)
             except Exception as e:  # noqa: BLE001 - settled (with TP consensus) in wait_for_save
                 self._plan = _FailedLoad(e)
+
+    def _start_fanout_plan(self, keys, blocks):
+        from ...parallel.fanout import FanoutLayerPlan, RestoreItem
+
+        bpc = self.blocks_per_chunk
+        items = [RestoreItem(rank=r, key=k, block_ids=blocks[i * bpc:(i + 1) * bpc].tolist())
+                 for r in range(self.tp_size) for i, k in enumerate(keys)]
+        self._epoch += 1
+        return FanoutLayerPlan(self._fan, self._board, items, self._n_drives, self._affine,
+                               list(range(self.engine.geometry.num_layers)), self.engine.io_stream, self._epoch,
+                               window=self.lookahead)
 
     def wait_for_layer_load(self, layer_name: str) -> None:
         if self._plan is not None and hasattr(self._plan, "wait_layer"):
@@ -353,6 +390,9 @@ class WorkerSide:
     def shutdown(self) -> None:
         while self._saves:
             self._settle_save(*self._saves.popleft())
+        if self._board is not None:
+            self._board.close()
+            self._peers.close()
         for comp, _, _ in self._async.values():
             try:
                 comp.wait()

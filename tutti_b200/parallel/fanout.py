@@ -136,6 +136,65 @@ class PeerPools:
         self._opened.clear()
 
 
+class PeerLayers:
+    """Every rank's per-layer KV tensors (one allocation per layer, as vLLM keeps
+    them), mapped into this process through CUDA IPC: ``ptrs[r][l]``."""
+
+    def __init__(self, layers: Sequence[torch.Tensor], group=None):
+        self.layers = list(layers)
+        self.device = self.layers[0].device.index
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        mine = []
+        for t in self.layers:
+            h, off, _size = ops.ipc_export(t)
+            mine.append((h, off, t.numel() * t.element_size()))
+        everyone: list = [None] * self.world
+        dist.all_gather_object(everyone, (self.device, mine), group=group)
+        self.ptrs: list[list[int]] = []
+        self.nbytes: list[list[int]] = []
+        self.devices: list[int] = []
+        self._opened: list[int] = []
+        for r, (devi, entries) in enumerate(everyone):
+            self.devices.append(devi)
+            self.nbytes.append([nb for _h, _o, nb in entries])
+            if r == self.rank:
+                self.ptrs.append([t.data_ptr() for t in self.layers])
+                continue
+            ops.enable_peer_access(self.device, devi)
+            row = []
+            for h, off, _nb in entries:
+                base = ops.ipc_open(h, self.device)
+                self._opened.append(base)
+                row.append(base + off)
+            self.ptrs.append(row)
+
+    def close(self) -> None:
+        for p in self._opened:
+            ops.ipc_close(p, self.device)
+        self._opened.clear()
+
+
+class Completions:
+    """Several submissions waited on as one."""
+
+    def __init__(self, comps):
+        self.comps = [c for c in comps if c is not None]
+
+    def query(self) -> bool:
+        return all(c.query() for c in self.comps)
+
+    def wait(self) -> None:
+        first = None
+        for c in self.comps:
+            try:
+                c.wait()
+            except Exception as e:  # noqa: BLE001 - every submission settles before the first error is raised
+                first = first or e
+        if first is not None:
+            raise first
+
+
 @dataclass
 class RestoreItem:
     """Restore chunk ``key`` into rank ``rank``'s pool blocks ``block_ids``.
@@ -158,12 +217,26 @@ class RestoreItem:
 class FanoutRestorer:
     """Restores (and stores) chunks for all ranks through the drives this GPU owns (drive-affine)."""
 
-    def __init__(self, store, peers: PeerPools, group=None):
+    def __init__(self, store, peers, group=None):
         self.kv = store
         self.peers = peers
         self.group = group
-        self.mems = [store._pool[1] if r == peers.rank else store.register_peer_pool(p, peers.nbytes[r], peers.devices[r])
-                     for r, p in enumerate(peers.ptrs)]
+        if isinstance(peers, PeerLayers):
+            # per-layer caches: layer l of rank r lands in layer_mems[r][l]
+            self.mems = None
+            self.layer_mems = []
+            for r in range(peers.world):
+                if r == peers.rank:
+                    self.layer_mems.append(np.asarray(store._layer_mems, dtype=np.uint64))
+                else:
+                    self.layer_mems.append(np.asarray([store.register_peer_pool(p, nb, peers.devices[r])
+                                                       for p, nb in zip(peers.ptrs[r], peers.nbytes[r])],
+                                                      dtype=np.uint64))
+        else:
+            self.layer_mems = None
+            self.mems = [store._pool[1] if r == peers.rank else store.register_peer_pool(p, peers.nbytes[r],
+                                                                                        peers.devices[r])
+                         for r, p in enumerate(peers.ptrs)]
 
     def placements(self, keys_by_rank: dict[int, Sequence[bytes]]) -> dict[tuple[int, bytes], tuple[str, int, int]]:
         """Every rank looks up its own chunks; the (path, offset, slot) map is shared by all."""
@@ -190,7 +263,7 @@ class FanoutRestorer:
         """
         pl = placements if placements is not None else self.placements(
             {r: sorted({bytes(it.key) for it in items if it.src == r}) for r in range(self.peers.world)})
-        todo, mems, blocks = [], [], []
+        todo, ranks, blocks = [], [], []
         for it in items:
             p = pl.get((it.src, bytes(it.key)))
             if p is None:
@@ -199,10 +272,20 @@ class FanoutRestorer:
             if affine_gpus[(slot % n_drives) % len(affine_gpus)] != self.peers.rank:
                 continue
             todo.append((path, off))
-            mems.append(self.mems[it.rank])
+            ranks.append(it.rank)
             blocks.append(list(it.block_ids))
         if not todo:
             return None
+        if self.layer_mems is not None:
+            # one submission per destination rank: its per-layer caches
+            comps = []
+            for r in sorted(set(ranks)):
+                sel = [i for i, x in enumerate(ranks) if x == r]
+                comps.append(self.kv.restore_placements([todo[i] for i in sel],
+                                                        np.asarray([blocks[i] for i in sel], dtype=np.int64),
+                                                        layers=layers, stream=stream, layer_mems=self.layer_mems[r]))
+            return Completions(comps)
+        mems = [self.mems[r] for r in ranks]
         return self.kv.restore_placements(todo, np.asarray(blocks, dtype=np.int64), np.asarray(mems, np.uint64),
                                              layers=layers, stream=stream)
 
@@ -237,7 +320,7 @@ class FanoutRestorer:
             placements.update(m)
         ok = not errors
         if ok:
-            todo, mems, blocks = [], [], []
+            todo, ranks, blocks = [], [], []
             for it in items:
                 p = placements.get((it.rank, bytes(it.key)))
                 if p is None:
@@ -246,12 +329,18 @@ class FanoutRestorer:
                 if affine_gpus[(slot % n_drives) % len(affine_gpus)] != me:
                     continue
                 todo.append((path, off))
-                mems.append(self.mems[it.rank])
+                ranks.append(it.rank)
                 blocks.append(list(it.block_ids))
             try:
-                if todo:
+                if todo and self.layer_mems is not None:
+                    for r in sorted(set(ranks)):
+                        sel = [i for i, x in enumerate(ranks) if x == r]
+                        self.kv.write_placements([todo[i] for i in sel],
+                                                 np.asarray([blocks[i] for i in sel], dtype=np.int64),
+                                                 stream=stream, layer_mems=self.layer_mems[r]).wait()
+                elif todo:
                     self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64),
-                                                np.asarray(mems, np.uint64), stream=stream).wait()
+                                             np.asarray([self.mems[r] for r in ranks], np.uint64), stream=stream).wait()
                 # this GPU's drives hold other ranks' chunks too: durable before anyone commits
                 flush = getattr(getattr(self.kv, "runtime", None), "flush_devices", None)
                 if flush is not None:
@@ -276,3 +365,91 @@ class FanoutRestorer:
         if torch.cuda.is_available():
             torch.cuda.current_stream().synchronize()
         dist.barrier(group=self.group)
+
+
+class FanoutLayerPlan:
+    """Layer-by-layer drive-affine restore of one batch for every rank, ordered on the device.
+
+    The placements are gathered here, on the calling thread (a collective of the
+    group: every rank builds its plans in the same order). A feeder thread then
+    submits, layer by layer, this GPU's share of every rank's chunks (at most
+    ``window`` layers in flight) and raises the layer's flag on the ReadyBoard
+    behind it on the IO stream, also when this GPU has nothing to read for the
+    layer. ``wait_layer(l)`` makes the current stream wait until every rank raised
+    layer l's flag for this plan's epoch; ``finish`` settles the submissions and
+    reports ranks that never raised a flag.
+    """
+
+    def __init__(self, fan: FanoutRestorer, board: ReadyBoard, items: Sequence[RestoreItem], n_drives: int,
+                 affine_gpus: Sequence[int], layers: Sequence[int], io_stream: torch.cuda.Stream, epoch: int,
+                 window: int = 4, timeout_s: float = 30.0):
+        import threading
+
+        world = fan.peers.world
+        self.fan, self.board, self.items = fan, board, list(items)
+        self.n_drives, self.affine = n_drives, list(affine_gpus)
+        self.layers, self.io_stream, self.epoch = list(layers), io_stream, epoch
+        self.window, self.timeout_s = max(1, window), timeout_s
+        self.placements = fan.placements({r: sorted({bytes(it.key) for it in items if it.src == r})
+                                          for r in range(world)})
+        self._comps: list = []
+        self._submitted = 0
+        self._tickets: list[int] = []
+        self._error: BaseException | None = None
+        self._cv = threading.Condition()
+        self._thread = threading.Thread(target=self._feed, name="tutti-fanout-feeder", daemon=True)
+        self._thread.start()
+
+    def _feed(self) -> None:
+        try:
+            torch.cuda.set_device(self.board.device)
+            for li, layer in enumerate(self.layers):
+                if li >= self.window and self._comps[li - self.window] is not None:
+                    self._comps[li - self.window].wait()
+                comp = self.fan.restore(self.items, self.n_drives, self.affine, layers=[layer],
+                                        stream=self.io_stream, placements=self.placements)
+                self.board.signal(layer % self.board.slots, self.epoch, self.io_stream)
+                with self._cv:
+                    self._comps.append(comp)
+                    self._submitted = li + 1
+                    self._cv.notify_all()
+        except BaseException as e:  # noqa: BLE001 - surfaced by wait_layer / finish
+            with self._cv:
+                self._error = e
+                self._cv.notify_all()
+
+    def wait_layer(self, layer: int) -> None:
+        li = self.layers.index(layer)
+        with self._cv:
+            while self._submitted <= li and self._error is None:
+                self._cv.wait(timeout=self.timeout_s)
+        # every rank's share of this layer, including the ones this GPU did not read
+        self._tickets.append(self.board.wait(layer % self.board.slots, self.epoch, torch.cuda.current_stream(),
+                                             self.timeout_s))
+
+    def finish(self) -> None:
+        from ..engine.completion import LoadGateError
+
+        self._thread.join(timeout=self.timeout_s * len(self.layers))
+        err = self._error
+        for c in self._comps:
+            if c is None:
+                continue
+            try:
+                c.wait()
+            except Exception as e:  # noqa: BLE001
+                err = err or e
+        torch.cuda.current_stream().synchronize()
+        missing = sorted({r for t in self._tickets for r in self.board.failed(t)})
+        if err is not None or missing:
+            why = str(err) if err is not None else f"ranks {missing} never signalled"
+            raise LoadGateError(f"fan-out restore failed: {why}")  # no chunk list: every chunk counts as failed
+
+    def abort(self) -> None:
+        try:
+            self.finish()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def read_ms(self):
+        return None

@@ -368,22 +368,25 @@ class TuttiKVStore:
         """Register another GPU's whole KV pool (CUDA-IPC mapped) as a restore destination."""
         return self.runtime.register_memory(int(ptr), int(nbytes), "device", int(device))
 
-    def restore_placements(self, placements, block_ids, chunk_mems=None, layers=None, stream=None):
+    def restore_placements(self, placements, block_ids, chunk_mems=None, layers=None, stream=None, layer_mems=None):
         """Restore chunks given by explicit (segment file path, payload offset) placements.
 
         ``chunk_mems[i]`` names the pool (this rank's or a peer's) chunk i lands in;
-        placements may belong to other ranks' namespaces (the files are opened here).
+        ``layer_mems[l]`` instead names the per-layer tensor layer l lands in (a peer's
+        per-layer caches, mapped through IPC); placements may belong to other ranks'
+        namespaces (the files are opened here).
         """
         g = self.geometry
         block_ids = np.asarray(block_ids, dtype=np.int64).reshape(len(placements), g.blocks_per_chunk)
         layers = np.arange(g.num_layers) if layers is None else np.asarray(layers, dtype=np.int64).reshape(-1)
         cm = None if chunk_mems is None else np.asarray(chunk_mems, dtype=np.uint64)
-        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream, chunk_mems=cm)
+        lm = None if layer_mems is None else np.asarray(layer_mems, dtype=np.uint64)
+        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream, chunk_mems=cm, layer_mems=lm)
         comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
         self._track(comp)
         return comp
 
-    def write_placements(self, placements, block_ids, chunk_mems=None, stream=None) -> NativeCompletion:
+    def write_placements(self, placements, block_ids, chunk_mems=None, stream=None, layer_mems=None) -> NativeCompletion:
         """Write all layers of chunks to explicit (segment file path, payload offset) placements.
 
         The slots must already be reserved (by this rank or by the rank that owns them);
@@ -395,13 +398,15 @@ class TuttiKVStore:
         cm = None if chunk_mems is None else np.asarray(chunk_mems, dtype=np.uint64)
         if stream is None and self.backend == "nvme-gpu":
             stream = torch.cuda.current_stream(self.device)
-        ios, nbytes = self._submit_paged("write", placements, block_ids, np.arange(g.num_layers), stream, chunk_mems=cm)
+        lm = None if layer_mems is None else np.asarray(layer_mems, dtype=np.uint64)
+        ios, nbytes = self._submit_paged("write", placements, block_ids, np.arange(g.num_layers), stream, chunk_mems=cm,
+                                         layer_mems=lm)
         comp = NativeCompletion(self.runtime, ios, nbytes=nbytes, kind="store")
         self._track(comp)
         return comp
 
     def _submit_paged(self, direction: str, placements, block_ids: np.ndarray, layers: np.ndarray, stream,
-                      chunk_mems: np.ndarray | None = None):
+                      chunk_mems: np.ndarray | None = None, layer_mems: np.ndarray | None = None):
         """Paged requests generated natively (no per-request Python work); retried while leases are busy."""
         g = self.geometry
         handles = np.asarray(self.targets_for([p for p, _ in placements]), dtype=np.uint64)
@@ -417,7 +422,7 @@ class TuttiKVStore:
         host = self.backend != "nvme-gpu"
         for _ in range(self.max_retries):
             r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host,
-                                          self._layer_mems,
+                                          self._layer_mems if layer_mems is None else layer_mems,
                                           chunk_mems if chunk_mems is not None else np.zeros(0, dtype=np.uint64))
             if not r["rejected"]:
                 return [r["io"]], int(r["count"]) * g.plane_block_bytes
