@@ -334,6 +334,7 @@ class _SaveEngine:
     def __init__(self):
         self.gates = []
         self.index = SimpleNamespace(is_resident=lambda k: False)
+        self.store = SimpleNamespace()
 
     def store_chunks(self, keys, block_table, after=None):
         g = _SaveGate()
@@ -353,13 +354,12 @@ def test_worker_step_does_not_wait_for_its_own_saves():
     wm = w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, [0, 1, 2, 3])]))
     gate = w.engine.gates[0]
     assert not gate.waited_before_done and wm.committed == {} and w.saves_in_flight() == 1
-    # the request finished, but its blocks are held until the save settles
-    assert w.get_finished({"a"}) == (None, None)
+    # the request finished; the next step names it (its blocks may be reused) and goes on
+    w.start_load_kv(TuttiConnectorMetadata(2, [], [], finished_saving=["a"]))
+    assert w.get_finished({"a"}) == (None, None) and not gate.waited_before_done
     gate.done = True  # the write finished on the device
     wm = w.wait_for_save(TuttiConnectorMetadata(2, [], []))
     assert wm.committed == {keys[0]: 1, keys[1]: 1} and w.saves_in_flight() == 0
-    assert w.get_finished(set()) == ({"a"}, None)
-    assert w.get_finished(set()) == (None, None)  # reported once
 
 
 def test_worker_saves_settle_from_get_finished_and_in_any_order():
@@ -368,9 +368,11 @@ def test_worker_saves_settle_from_get_finished_and_in_any_order():
                                                    SaveSpec("b", [b"b" * 16], [2, 3])]))
     ga, gb = w.engine.gates
     gb.done = True
-    assert w.get_finished({"a", "b"}) == ({"b"}, None)  # b settled, a still in flight
+    w.get_finished({"a", "b"})  # b settles here, a stays in flight
+    assert w.saves_in_flight() == 1
     ga.done = True
-    assert w.get_finished(set()) == ({"a"}, None)
+    wm = w.wait_for_save(TuttiConnectorMetadata(2, [], []))
+    assert w.saves_in_flight() == 0 and set(wm.committed) == {b"a" * 16, b"b" * 16}
     assert not ga.waited_before_done and not gb.waited_before_done
 
 
@@ -387,7 +389,7 @@ def test_worker_back_pressure_waits_for_the_oldest_save_only():
     assert w.saves_in_flight() == 0 and g2.done
 
 
-def test_scheduler_holds_blocks_of_finished_requests_with_saves():
+def test_scheduler_names_finished_requests_whose_saves_may_be_in_flight():
     s = SchedulerSide(BS, CHUNK, capacity_chunks=64)
     for rid in ("a", "b"):
         r = req(rid, 17 if rid == "a" else 5, base=100 if rid == "b" else 0)
@@ -395,6 +397,7 @@ def test_scheduler_holds_blocks_of_finished_requests_with_saves():
         s.update_state_after_alloc(r, list(range(10, 15)), 0)
     meta = s.build_meta([("a", list(range(10, 15)), 0, 17), ("b", list(range(20, 22)), 0, 5)])
     assert [sp.request_id for sp in meta.saves] == ["a"]  # b has no full chunk
-    assert s.request_finished("a") is True  # its blocks wait for the workers' finished_sending
-    assert s.request_finished("b") is False
-    assert s.request_finished("a") is False  # already released
+    assert s.request_finished("a") is False and s.request_finished("b") is False  # blocks freed at once
+    nxt = s.build_meta([])
+    assert nxt.finished_saving == ["a"]  # the workers order this step's forward after a's saves
+    assert s.build_meta([]).finished_saving == []

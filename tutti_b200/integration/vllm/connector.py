@@ -143,8 +143,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
         self._sched.update_from_workers(wm if isinstance(wm, TuttiWorkerMetadata) else None, received)
 
     def request_finished(self, request, block_ids: list[int]) -> tuple[bool, dict[str, Any] | None]:
-        # a request whose chunks are being saved keeps its blocks until every
-        # worker reports it in finished_sending (saves run behind the step)
+        # blocks are freed now; the next step's forward is ordered after the
+        # request's saves on the device (see TuttiConnectorMetadata.finished_saving)
         return self._sched.request_finished(request.request_id), None
 
     # ---------------- worker role ----------------

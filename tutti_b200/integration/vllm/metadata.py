@@ -42,6 +42,9 @@ class TuttiConnectorMetadata(_MetaBase):
     loads: list[LoadSpec] = field(default_factory=list)
     saves: list[SaveSpec] = field(default_factory=list)
     step_tokens: int = 0  # tokens this step computes (the workers' step-time samples are per token)
+    # requests finished since the last step whose blocks saves may still read: vLLM frees
+    # their blocks now, so this step's forward must follow those saves on the device
+    finished_saving: list[str] = field(default_factory=list)
 
 
 @dataclass

@@ -73,7 +73,8 @@ class SchedulerSide:
         self.requests: dict[str, _RequestState] = {}
         self.generation = 0
         self._planned: dict[bytes, str] = {}  # pending saves: key -> request
-        self._saving_requests: set[str] = set()  # requests that had a save (their blocks wait for it)
+        self._saving_requests: set[str] = set()  # requests that had a save
+        self._finished_saving: set[str] = set()  # ... and finished since the last step
         self.total_blocks = total_blocks  # vLLM's KV pool size, when known
         self.min_retrieve_tokens = min_retrieve_tokens  # shorter hits are computed instead
         self.max_tokens_per_load = max_tokens_per_load  # 0: no cap
@@ -172,7 +173,9 @@ class SchedulerSide:
         self.index.advance_epoch()
         self.reclaim()
         meta = TuttiConnectorMetadata(generation=self.generation,
-                                      step_tokens=sum(s[3] for s in scheduled) if step_tokens is None else step_tokens)
+                                      step_tokens=sum(s[3] for s in scheduled) if step_tokens is None else step_tokens,
+                                      finished_saving=sorted(self._finished_saving))
+        self._finished_saving.clear()
         for st_id, st in self.requests.items():
             if st.pending_load is not None:
                 ld = st.pending_load
@@ -252,13 +255,15 @@ class SchedulerSide:
             self.index.forget(keys[max(0, first_failed_token) // self.chunk_tokens:])
 
     def request_finished(self, request_id: str) -> bool:
-        """Forget the request; True when its blocks must wait for the workers' saves of it
-        (every worker reports it in ``finished_sending`` once they settled)."""
+        """Forget the request. Its blocks are freed at once; if it had saves, the next step's
+        metadata names it, and the workers order that step's forward after those saves on
+        the device (a freed block may be written again only once the saves read it).
+        Returns False: no delayed free."""
         self.requests.pop(request_id, None)
         self._live.pop(request_id, None)
         if request_id in self._saving_requests:
             self._saving_requests.discard(request_id)
-            return True
+            self._finished_saving.add(request_id)
         return False
 
     def maybe_log(self, force: bool = False) -> bool:

@@ -14,9 +14,12 @@
   header) and reported committed in that step's metadata. At most
   ``max_inflight_saves`` saves stay in flight; beyond that the oldest is
   waited for (back-pressure).
-* ``get_finished``: finished asynchronous loads (``finished_recving``), and
-  finished requests whose saves have all settled (``finished_sending``): the
-  scheduler keeps the blocks of a request that had saves until then.
+* Block reuse after a request finishes: vLLM frees its blocks at once. A
+  save of them may still be queued on the device, so the next step names the
+  request (``finished_saving``) and ``start_load_kv`` makes the compute stream
+  wait for the save kernels' device events before the forward that may write
+  those blocks again: ordering on the device, no host wait.
+* ``get_finished``: finished asynchronous loads (``finished_recving``).
 * Measurements for the scheduler's load policy, harvested without blocking
   (a sample whose events have not completed waits for a later step):
   ``read_samples`` (chunks, device ms) of finished restores and
@@ -156,8 +159,7 @@ class WorkerSide:
         self._epoch = 0
         self._saves: deque = deque()  # (SaveSpec, completion) in submission order
         self._saves_of: dict[str, int] = {}  # request id -> saves in flight on this rank
-        self._had_saves: set[str] = set()  # requests with a save on this rank (their blocks wait for it)
-        self._finishing: set[str] = set()  # finished requests whose saves are still in flight
+        self._save_events: dict[str, list] = {}  # request id -> device events after its save kernels
 
     # -- binding --------------------------------------------------------------
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
@@ -201,6 +203,11 @@ class WorkerSide:
     # -- loads ----------------------------------------------------------------
     def start_load_kv(self, meta: TuttiConnectorMetadata) -> None:
         self._meta = TuttiWorkerMetadata()
+        # blocks of requests that finished may be written by this step's forward:
+        # it follows their save kernels on the device
+        for rid in getattr(meta, "finished_saving", ()) or ():
+            for ev in self._save_events.pop(rid, ()):
+                torch.cuda.current_stream().wait_event(ev)
         if self.engine is not None:
             if self.health is None:
                 self.health = HealthReporter(self.engine.store)
@@ -310,11 +317,15 @@ class WorkerSide:
             if ev is not None:
                 ev.record()
             for spec in meta.saves:
-                self._had_saves.add(spec.request_id)
                 comp = self.engine.store_chunks(spec.keys, np.asarray(spec.block_ids, dtype=np.int64), after=ev)
                 if comp is None:  # nothing new to write: resident chunks count as committed
                     self._count_resident(spec.keys)
                     continue
+                ws = getattr(self.engine, "write_stream", None) if ev is not None else None
+                if ws is not None:
+                    done = torch.cuda.Event()
+                    done.record(ws)  # behind the save kernel on the engine's write stream
+                    self._save_events.setdefault(spec.request_id, []).append(done)
                 self._saves.append((spec, comp))
                 self._saves_of[spec.request_id] = self._saves_of.get(spec.request_id, 0) + 1
             while len(self._saves) > self.max_inflight_saves:
@@ -361,14 +372,7 @@ class WorkerSide:
 
     # -- completion reporting -------------------------------------------------
     def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
-        # finished requests hold their blocks until this rank's saves of them settled
-        for rid in finished_req_ids or ():
-            if rid in self._had_saves:
-                self._finishing.add(rid)
         self._harvest_saves()
-        sending = {rid for rid in self._finishing if rid not in self._saves_of}
-        self._finishing -= sending
-        self._had_saves -= sending
         done = set()
         for rid, (comp, spec, t0) in list(self._async.items()):
             if comp.query():
@@ -381,7 +385,7 @@ class WorkerSide:
                     self._meta.failed_loads[rid] = 0
                 done.add(rid)
                 del self._async[rid]
-        return (sending or None), (done or None)
+        return None, (done or None)
 
     def get_block_ids_with_load_errors(self) -> set[int]:
         out, self._load_error_blocks = self._load_error_blocks, set()
