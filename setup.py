@@ -54,6 +54,7 @@ OPS_SOURCES = [
     src("kernels", "fp8_block.cu"),
     src("kernels", "blake2b.cu"),
     src("kernels", "probe_kernels.cu"),
+    src("kernels", "ready_flags.cu"),
 ]
 
 ext_modules = [
