@@ -389,6 +389,18 @@ def test_worker_back_pressure_waits_for_the_oldest_save_only():
     assert w.saves_in_flight() == 0 and g2.done
 
 
+def test_worker_settle_saves_commits_every_save_in_flight():
+    w = _saving_worker()
+    w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", [b"a" * 16], [0, 1]),
+                                                   SaveSpec("b", [b"b" * 16], [2, 3])]))
+    assert w.saves_in_flight() == 2
+    assert w.settle_saves() == 2 and w.saves_in_flight() == 0
+    assert all(g.done for g in w.engine.gates)
+    # reported committed in the next step's metadata
+    wm = w.wait_for_save(TuttiConnectorMetadata(2, [], []))
+    assert set(wm.committed) == {b"a" * 16, b"b" * 16}
+
+
 def test_scheduler_names_finished_requests_whose_saves_may_be_in_flight():
     s = SchedulerSide(BS, CHUNK, capacity_chunks=64)
     for rid in ("a", "b"):

@@ -370,6 +370,17 @@ class WorkerSide:
     def saves_in_flight(self) -> int:
         return len(self._saves)
 
+    def settle_saves(self) -> int:
+        """Wait for every save in flight and commit it (reported in the next step's metadata).
+
+        Not needed by vLLM's step loop (commits are harvested without blocking);
+        for shutdown and for callers that must see their chunks committed now.
+        """
+        n = len(self._saves)
+        while self._saves:
+            self._settle_save(*self._saves.popleft())
+        return n
+
     # -- completion reporting -------------------------------------------------
     def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
         self._harvest_saves()
@@ -392,8 +403,7 @@ class WorkerSide:
         return out
 
     def shutdown(self) -> None:
-        while self._saves:
-            self._settle_save(*self._saves.popleft())
+        self.settle_saves()
         if self._board is not None:
             self._board.close()
             self._peers.close()

@@ -414,6 +414,14 @@ class FanoutLayerPlan:
                     self._submitted = li + 1
                     self._cv.notify_all()
         except BaseException as e:  # noqa: BLE001 - surfaced by wait_layer / finish
+            # the peers' layer waits must not run into their deadlines: raise the
+            # flags of the layers not submitted; the failure reaches every rank
+            # through finish() and the TP failure consensus, not through the flags
+            try:
+                for layer in self.layers[len(self._comps):]:
+                    self.board.signal(layer % self.board.slots, self.epoch, self.io_stream)
+            except Exception:  # noqa: BLE001 - the original error is the one to report
+                pass
             with self._cv:
                 self._error = e
                 self._cv.notify_all()
