@@ -82,3 +82,28 @@ def test_cpp_api_example_round_trip(tmp_path):
     out = subprocess.run([exe, str(tmp_path)], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip() == "OK 1048576"
+
+
+def test_device_admin_commands_on_a_plain_sysfs_tree(tmp_path, capsys):
+    from tutti_b200.cli import main
+
+    # a plain tree (no kernel behind it): writes land in files, so a bind cannot be verified
+    drv = tmp_path / "bus" / "pci" / "drivers"
+    dev = tmp_path / "bus" / "pci" / "devices" / "0000:1b:00.0"
+    for d in (drv / "nvme", drv / "snvme", dev):
+        d.mkdir(parents=True)
+    for f in ("bind", "unbind"):
+        (drv / "snvme" / f).write_text("")
+        (drv / "nvme" / f).write_text("")
+    for name, value in (("class", "0x010802"), ("vendor", "0x144d"), ("device", "0xa80a"), ("driver_override", "")):
+        (dev / name).write_text(value + "\n")
+    (drv / "snvme" / "0000:1b:00.0").symlink_to(dev)
+    (dev / "driver").symlink_to(drv / "snvme")
+    assert main(["nvme-unbind", "--sysfs", str(tmp_path)]) == 0
+    assert "0000:1b:00.0: unbound from snvme" in capsys.readouterr().out
+    assert (drv / "snvme" / "unbind").read_text() == "0000:1b:00.0"
+    assert main(["nvme-bind", "0000:1b:00.0", "--driver", "nvme", "--sysfs", str(tmp_path)]) == 1
+    assert "instead of nvme" in capsys.readouterr().err
+    assert main(["raid0-create", "/dev/nonexistent0", "/dev/nonexistent1"]) == 1
+    err = capsys.readouterr().err  # mdadm is checked first; either way nothing is created
+    assert "mdadm is not installed" in err or "not a block device" in err

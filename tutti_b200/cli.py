@@ -7,6 +7,10 @@
     python -m tutti_b200 fiemap FILE           # extents the FIEMAP resolver sees
     python -m tutti_b200 probe-raid0 md0 [--sysfs /sys]
     python -m tutti_b200 topology [--sysfs /sys]   # NVMe drive -> affine GPU over the PCIe tree
+    python -m tutti_b200 nvme-bind BDF [--driver nvme|snvme]    # move one controller to a driver
+    python -m tutti_b200 nvme-unbind [BDF ...] [--driver snvme] # release controllers (all by default)
+    python -m tutti_b200 raid0-create DEV DEV ... [--chunk-kib 64] --yes   # destroys the drives' data
+    python -m tutti_b200 raid0-delete mdN --yes                 # stops the array
     python -m tutti_b200 bench {kernels,ttft,fanout,mla,trace,sweep,plumbing,vllm} [args...]
     python -m tutti_b200 test [--gpu] [--dry-run] [pytest args...]   # pytest suites + C++ contract suite
     python -m tutti_b200 vllm-config --root R [--mounts M ...] [--preset JSON] ...   # --kv-transfer-config JSON
@@ -14,8 +18,10 @@
 
 Parity: reference scripts/tutti-env.sh (build, build-ext, test, daemon, status
 subcommands), scripts/tutti-md (md RAID0 inspection),
-scripts/pci_topology_check.sh (drive / GPU switch affinity) and
-scripts/vllm/run/serve-8gpu-striped.sh (vLLM serve with the connector).
+scripts/pci_topology_check.sh (drive / GPU switch affinity),
+scripts/{bind_nvme_device,unbind,raid0_create,raid0_delete}.sh (through
+``device_admin``) and scripts/vllm/run/serve-8gpu-striped.sh (vLLM serve with
+the connector).
 """
 from __future__ import annotations
 
@@ -123,6 +129,43 @@ def cmd_topology(args) -> int:
     return 0
 
 
+def _admin(fn) -> int:
+    from .device_admin import AdminError
+
+    try:
+        rep = fn()
+    except AdminError as e:
+        print(f"error: {e}", file=sys.stderr)
+        return 1
+    for line in getattr(rep, "steps", []):
+        print(line)
+    return 0
+
+
+def cmd_nvme_bind(args) -> int:
+    from . import device_admin as da
+
+    return _admin(lambda: da.bind_driver(args.bdf, args.driver, da.Host(sysfs=args.sysfs)))
+
+
+def cmd_nvme_unbind(args) -> int:
+    from . import device_admin as da
+
+    return _admin(lambda: da.unbind_driver(args.driver, list(args.bdfs) or None, da.Host(sysfs=args.sysfs)))
+
+
+def cmd_raid0_create(args) -> int:
+    from . import device_admin as da
+
+    return _admin(lambda: da.raid0_create(list(args.devices), args.chunk_kib, args.yes)[1])
+
+
+def cmd_raid0_delete(args) -> int:
+    from . import device_admin as da
+
+    return _admin(lambda: da.raid0_delete(args.md, args.yes))
+
+
 def cmd_bench(args) -> int:
     mod = importlib.import_module(f"tutti_b200.benchmarks.{BENCHES[args.which]}")
     rc = mod.main(list(args.rest))
@@ -212,6 +255,25 @@ def main(argv=None) -> int:
     t = sub.add_parser("topology")
     t.add_argument("--sysfs", default="/sys")
     t.set_defaults(fn=cmd_topology)
+    nb = sub.add_parser("nvme-bind")
+    nb.add_argument("bdf")
+    nb.add_argument("--driver", choices=["nvme", "snvme"], default="nvme")
+    nb.add_argument("--sysfs", default="/sys")
+    nb.set_defaults(fn=cmd_nvme_bind)
+    nu = sub.add_parser("nvme-unbind")
+    nu.add_argument("bdfs", nargs="*")
+    nu.add_argument("--driver", choices=["nvme", "snvme"], default="snvme")
+    nu.add_argument("--sysfs", default="/sys")
+    nu.set_defaults(fn=cmd_nvme_unbind)
+    rc = sub.add_parser("raid0-create")
+    rc.add_argument("devices", nargs="+")
+    rc.add_argument("--chunk-kib", type=int, default=64)
+    rc.add_argument("--yes", action="store_true", help="confirm: every byte on the drives is lost")
+    rc.set_defaults(fn=cmd_raid0_create)
+    rd = sub.add_parser("raid0-delete")
+    rd.add_argument("md")
+    rd.add_argument("--yes", action="store_true", help="confirm: the array is stopped")
+    rd.set_defaults(fn=cmd_raid0_delete)
     b = sub.add_parser("bench")
     b.add_argument("which", choices=sorted(BENCHES))
     b.add_argument("rest", nargs=argparse.REMAINDER)
