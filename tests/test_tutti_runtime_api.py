@@ -37,6 +37,51 @@ def test_mixed_submit_wait_and_retained_results():
     rt.shutdown(1000)
 
 
+def test_stub_runtime_ios_stay_in_flight_until_forced():
+    import numpy as np
+
+    rt = tutti_runtime.make_stub_runtime()
+    buf = np.zeros(8192, dtype=np.uint8)
+    mem = rt.register_memory(buf.ctypes.data, buf.nbytes, "host")
+    (t,) = rt.open_batch(["file:///no/such/file"])  # any URI: a stub target
+    r = rt.submit([(t, 0, mem, 0, 4096, "read"), (t, 4096, mem, 4096, 8192, "write")], -1, None, "host")
+    assert r.initial_states == [True, False] and r.io_handle is not None  # the second overruns the memory
+    assert rt.query_io(r.io_handle) == "IN_FLIGHT" and rt.wait(r.io_handle, 5) == ("TIMEOUT", "IN_FLIGHT")
+    rt.testing_force_complete(r.io_handle, "FAILED")
+    res = rt.wait_result(r.io_handle, 0)
+    assert res.state == "FAILED" and res.failed_request_indices == [0]
+    rt.release_io(r.io_handle)
+    assert rt.query_io(r.io_handle) == "FAILED"  # retained after release
+    r2 = rt.submit([(t, 0, mem, 0, 4096, "write")], -1, None, "host")
+    with pytest.raises(ValueError):
+        rt.testing_force_complete(r2.io_handle, "DONE")
+    rt.testing_force_complete(r2.io_handle, "COMPLETED")
+    assert rt.wait(r2.io_handle, 0) == ("OK", "COMPLETED")
+    rt.release_io(r2.io_handle)
+    assert rt.open_io_count() == 0
+    rt.shutdown(100)
+
+
+def test_force_complete_is_refused_on_a_component_backed_runtime(tmp_path):
+    import numpy as np
+
+    from tutti_b200._native import core
+
+    native = core().make_posix_runtime(-1, [str(tmp_path)])
+    rt = tutti_runtime.Runtime(native)
+    p = tmp_path / "f.bin"
+    p.write_bytes(b"x" * 8192)
+    (t,) = rt.open_batch([f"file://{p}"])
+    buf = np.zeros(4096, dtype=np.uint8)
+    mem = rt.register_memory(buf.ctypes.data, buf.nbytes, "host")
+    r = rt.submit([(t, 0, mem, 0, 4096, "read")], -1, None, "host")
+    rt.wait(r.io_handle, 5000)
+    with pytest.raises(Exception, match="stub"):
+        rt.testing_force_complete(r.io_handle, "COMPLETED")
+    rt.release_io(r.io_handle)
+    rt.shutdown(1000)
+
+
 def test_factories_take_tutti_presets(tmp_path):
     stub = tutti_runtime.make_stub_runtime()
     assert isinstance(stub, tutti_runtime.Runtime)

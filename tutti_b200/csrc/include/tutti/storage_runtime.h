@@ -135,8 +135,10 @@ public:
                                                           const RuntimeComponents& components);
     static Result<std::unique_ptr<StorageRuntime>> create_owning(const RuntimeConfig& config,
                                                                  OwnedComponents components);
-    // A runtime with no components: memory verbs work; open/submit report
-    // NOT_FOUND/UNSUPPORTED. Used for API tests.
+    // A runtime with no components, for hardware-free API tests: memory verbs
+    // work; open gives any URI a 1 GiB stub target; submit validates requests
+    // as usual and accepts them into an IO that stays IN_FLIGHT (no DataPath
+    // moves data) until testing_force_complete makes it terminal.
     static std::unique_ptr<StorageRuntime> create_stub(const RuntimeConfig& config);
 
     ~StorageRuntime();
@@ -175,6 +177,13 @@ public:
 
     // Test seam: number of terminal results not yet released.
     std::size_t unreleased_terminal_results() const;
+
+    // Test seam, stub runtimes only: make an IO of a stub runtime terminal.
+    // `terminal` is COMPLETED or FAILED; a FAILED IO reports `io_status` (an
+    // error; INTERNAL when Ok is given) and every accepted request as failed.
+    // UNSUPPORTED on a component-backed runtime (its DataPaths complete IO),
+    // NOT_FOUND for an unknown handle, INVALID_ARGUMENT for a terminal IO.
+    Status testing_force_complete(const IoHandle& handle, IoState terminal, Status io_status = Status::Ok());
 
     // The DataPath-level identity an open target maps to (for callers that
     // drive a DataPath directly, e.g. the allocation-free C entry point).

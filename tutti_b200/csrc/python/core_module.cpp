@@ -430,6 +430,20 @@ PYBIND11_MODULE(_core, m) {
              })
         .def("unreleased_terminal_results", [](PyRuntime& r) { return r.rt->unreleased_terminal_results(); })
         .def(
+            "testing_force_complete",
+            [](PyRuntime& r, std::uint64_t io, const std::string& state) {
+                // stub runtimes only: their IOs have no DataPath to complete them
+                IoState terminal;
+                if (state == "COMPLETED")
+                    terminal = IoState::COMPLETED;
+                else if (state == "FAILED")
+                    terminal = IoState::FAILED;
+                else
+                    throw py::value_error("state must be 'COMPLETED' or 'FAILED', got '" + state + "'");
+                check(r.rt->testing_force_complete(unpack<IoHandle>(r.rid_, io), terminal));
+            },
+            py::arg("io"), py::arg("state"))
+        .def(
             "shutdown",
             [](PyRuntime& r, std::uint64_t timeout_ms) {
                 Status st;

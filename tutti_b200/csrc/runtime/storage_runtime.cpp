@@ -87,12 +87,17 @@ struct StorageRuntime::Impl {
         std::vector<std::pair<std::uint32_t, std::uint32_t>> mem_refs, tgt_refs;
         IoResult result;
         bool refs_released = false;
+        // stub runtimes: accepted request indices of an IO with no DataPath part,
+        // in flight until testing_force_complete
+        bool stub = false;
+        std::vector<std::uint32_t> stub_requests;
     };
 
     RuntimeConfig cfg;
     std::uint32_t id = 0;
     mutable std::mutex mu;
     RuntimeState state = RuntimeState::RUNNING;
+    bool stub = false;  // create_stub: targets and IOs without components
     std::map<std::string, StorageTargetResolver*> resolvers;
     std::vector<DpEntry> dps;
     OwnedComponents owned;
@@ -156,7 +161,7 @@ struct StorageRuntime::Impl {
 
     // Refresh an IO entry from its DataPath parts.
     void refresh(IoEntry& e) {
-        if (e.state != IoState::IN_FLIGHT) return;
+        if (e.state != IoState::IN_FLIGHT || e.stub) return;
         bool all_terminal = true;
         for (auto& p : e.parts) {
             if (p.terminal) continue;
@@ -303,7 +308,37 @@ std::unique_ptr<StorageRuntime> StorageRuntime::create_stub(const RuntimeConfig&
     auto im = std::make_unique<Impl>();
     im->cfg = config;
     im->id = g_runtime_ids.fetch_add(1);
+    im->stub = true;
     return std::unique_ptr<StorageRuntime>(new StorageRuntime(std::move(im)));
+}
+
+namespace {
+constexpr std::uint64_t kStubTargetBytes = 1ull << 30;
+}
+
+Status StorageRuntime::testing_force_complete(const IoHandle& h, IoState terminal, Status io_status) {
+    auto& im = *impl_;
+    std::lock_guard<std::mutex> g(im.mu);
+    if (!im.stub) return {StatusCode::UNSUPPORTED, "only a stub runtime's IO can be forced terminal"};
+    auto* e = im.io(h);
+    if (!e) return {StatusCode::NOT_FOUND, "unknown IO handle"};
+    if (terminal != IoState::COMPLETED && terminal != IoState::FAILED)
+        return {StatusCode::INVALID_ARGUMENT, "terminal state must be COMPLETED or FAILED"};
+    if (e->state != IoState::IN_FLIGHT) return {StatusCode::INVALID_ARGUMENT, "IO is already terminal"};
+    IoResult res;
+    res.state = terminal;
+    if (terminal == IoState::FAILED) {
+        res.status = io_status.ok() ? Status(StatusCode::INTERNAL, "forced failure") : io_status;
+        res.detail.failure_kind = IoFailureKind::UNKNOWN;
+        res.detail.failure_scope = IoFailureScope::WHOLE_OPERATION;
+        res.detail.failed_request_indices = e->stub_requests;
+        if (!e->stub_requests.empty()) res.detail.first_failed_entry = e->stub_requests.front();
+    }
+    e->result = std::move(res);
+    e->state = terminal;
+    ++im.terminal_unreleased;
+    im.release_refs(*e);
+    return Status::Ok();
 }
 
 RuntimeState StorageRuntime::state() const noexcept {
@@ -564,6 +599,19 @@ std::vector<Result<TargetHandle>> StorageRuntime::open_batch(const std::vector<s
                 out.push_back(R::Failure({StatusCode::NOT_READY, "runtime is not running"}));
             return out;
         }
+        if (im.stub) {
+            for (const auto& u : uris) {
+                const std::uint32_t slot = Impl::alloc_slot(im.tgts);
+                auto& t = im.tgts[slot];
+                t = Impl::TargetEntry{};
+                t.generation = im.next_gen++;
+                t.live = true;
+                t.uri = u;
+                t.size = kStubTargetBytes;
+                out.push_back(TargetHandle::from_raw(im.id, slot, t.generation));
+            }
+            return out;
+        }
         for (std::size_t i = 0; i < uris.size(); ++i) {
             auto it = im.resolvers.find(scheme_of(uris[i], o));
             if (it != im.resolvers.end()) rs[i] = it->second;
@@ -725,6 +773,7 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
     const bool xform = ctx.transform != IoTransform::NONE;
     if (xform && ctx.transform != IoTransform::FP8_E4M3_BLOCK128)
         return reject_all({StatusCode::INVALID_ARGUMENT, "unknown IoTransform"});
+    std::vector<std::uint32_t> stub_accepted;
     for (std::size_t i = 0; i < count; ++i) {
         const IoRequest& r = reqs[i];
         if (!last_m || r.memory != last_mh) {
@@ -750,6 +799,18 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
             bad = {StatusCode::OUT_OF_RANGE, "target range exceeds logical size"};
         else if (xform && (r.length % 1024 || r.target_offset % 16))
             bad = {StatusCode::INVALID_ARGUMENT, "fp8 block transform needs 1024-byte lengths, 16-byte target offsets"};
+        if (im.stub) {  // no DataPath: accepted into an IO that waits for testing_force_complete
+            if (!bad.ok()) {
+                out.initial_states[i] = {IoRequestState::REJECTED, bad};
+                if (first_reject.ok()) first_reject = bad;
+            } else {
+                out.initial_states[i] = {IoRequestState::ACCEPTED, Status::Ok()};
+                stub_accepted.push_back(static_cast<std::uint32_t>(i));
+                ++mem_count[r.memory.slot()];
+                ++tgt_count[r.target.slot()];
+            }
+            continue;
+        }
         Impl::DpEntry* d = nullptr;
         if (bad.ok()) {
             d = t->dpe;
@@ -847,7 +908,12 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
         }
     }
     out.status = first_reject;
-    if (entry.parts.empty()) return out;
+    if (im.stub && !stub_accepted.empty()) {
+        entry.stub = true;
+        entry.stub_requests = std::move(stub_accepted);
+    } else if (entry.parts.empty()) {
+        return out;
+    }
     for (std::uint32_t s = 0; s < mem_count.size(); ++s)
         if (mem_count[s]) {
             im.mems[s].inflight += static_cast<int>(mem_count[s]);

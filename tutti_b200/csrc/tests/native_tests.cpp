@@ -259,7 +259,7 @@ TEST(upload_runs_merge_within_an_allocation_only) {
     CHECK(runs.size() == 1 && runs[0].bytes.size() == 160 && runs[0].bytes[159] == 4);
 }
 
-TEST(stub_runtime_memory_only) {
+TEST(stub_runtime_ios_wait_for_a_forced_completion) {
     RuntimeConfig c;
     auto rt = StorageRuntime::create_stub(c);
     std::vector<char> b(64);
@@ -270,7 +270,42 @@ TEST(stub_runtime_memory_only) {
     auto h = rt->register_memory(v);
     CHECK(h.ok());
     CHECK(rt->query_memory(h.value()).value().size == 64);
-    CHECK(rt->open("file:///x").status().code() == StatusCode::NOT_FOUND);
+    auto t = rt->open("file:///anything");  // any URI: a 1 GiB stub target
+    CHECK(t.ok());
+    IoRequest reqs[3];
+    for (auto& r : reqs) {
+        r.direction = IoDirection::READ;
+        r.memory = h.value();
+        r.memory_offset = 0;
+        r.target = t.value();
+        r.target_offset = 4096;
+        r.length = 64;
+    }
+    reqs[1].length = 65;  // past the registration: rejected, the others accepted
+    HostSubmitContext ctx;
+    auto o = rt->submit(reqs, 3, ctx);
+    CHECK(o.io.has_value());
+    CHECK(o.initial_states[0].state == IoRequestState::ACCEPTED);
+    CHECK(o.initial_states[1].state == IoRequestState::REJECTED);
+    CHECK(o.initial_states[1].status.code() == StatusCode::OUT_OF_RANGE);
+    CHECK(rt->query(*o.io).value().state == IoState::IN_FLIGHT);
+    CHECK(rt->wait(*o.io, 5).observation_status.code() == StatusCode::TIMEOUT);
+    CHECK(rt->release_io(*o.io).code() == StatusCode::BUSY);
+    CHECK(rt->unregister_memory(h.value()).code() != StatusCode::OK);  // in use
+    CHECK(rt->testing_force_complete(*o.io, IoState::IN_FLIGHT).code() == StatusCode::INVALID_ARGUMENT);
+    CHECK(rt->testing_force_complete(*o.io, IoState::FAILED, Status(StatusCode::DEVICE_ERROR, "media")).ok());
+    CHECK(rt->testing_force_complete(*o.io, IoState::COMPLETED).code() == StatusCode::INVALID_ARGUMENT);
+    auto w = rt->wait(*o.io, 0);
+    CHECK(w.observation_status.ok() && w.result->state == IoState::FAILED);
+    CHECK(w.result->status.code() == StatusCode::DEVICE_ERROR);
+    CHECK((w.result->detail.failed_request_indices == std::vector<std::uint32_t>{0, 2}));
+    CHECK(rt->unreleased_terminal_results() == 1);
+    CHECK(rt->release_io(*o.io).ok());
+    CHECK(rt->testing_force_complete(*o.io, IoState::COMPLETED).code() == StatusCode::NOT_FOUND);
+    auto o2 = rt->submit(reqs, 1, ctx);
+    CHECK(rt->testing_force_complete(*o2.io, IoState::COMPLETED).ok());
+    CHECK(rt->wait(*o2.io, 0).result->state == IoState::COMPLETED);
+    CHECK(rt->release_io(*o2.io).ok());
     CHECK(rt->unregister_memory(h.value()).ok());
 }
 

@@ -5,7 +5,8 @@
     make_raid0_nvme_runtime(preset) -> Runtime
     Runtime: caps / open_batch / close_target / close_batch / register_memory /
              unregister_memory / submit / enqueue_wait / release_io / query_io /
-             open_io_count / wait / wait_result / wait_detail / shutdown
+             open_io_count / wait / wait_result / wait_detail / shutdown /
+             testing_force_complete (stub runtimes: their IOs wait for it)
     SubmitResult, WaitResult
     ObjectStore: open(scheme, config) / contains_prefix_all_ranks / lookup / usage / ...
 
@@ -186,6 +187,17 @@ class Runtime:
 
     def open_io_count(self) -> int:
         return len(self._open)
+
+    def testing_force_complete(self, io_handle: int, state: str) -> None:
+        """Stub runtimes only: make an in-flight IO terminal (``"COMPLETED"`` or ``"FAILED"``).
+
+        A stub runtime's IO has no DataPath behind it and stays in flight until this
+        call; a FAILED IO reports every accepted request as failed. Component-backed
+        runtimes refuse (their DataPaths complete IO).
+        """
+        if state not in ("COMPLETED", "FAILED"):
+            raise ValueError(f"state must be 'COMPLETED' or 'FAILED', got {state!r}")
+        self.native.testing_force_complete(int(io_handle), state)
 
     def testing_inject_next_read_nvme_error(self, raw_cq_status: int) -> None:
         """The next command the first drive serves completes with ``raw_cq_status`` (type and code bits)."""
