@@ -107,3 +107,22 @@ def test_device_admin_commands_on_a_plain_sysfs_tree(tmp_path, capsys):
     assert main(["raid0-create", "/dev/nonexistent0", "/dev/nonexistent1"]) == 1
     err = capsys.readouterr().err  # mdadm is checked first; either way nothing is created
     assert "mdadm is not installed" in err or "not a block device" in err
+
+
+def test_snvme_smoke_rounds_against_the_fake_driver():
+    import os
+
+    exe = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "tutti_b200", "bin",
+                       "tutti_snvme_smoke")
+    if not os.path.exists(exe):
+        pytest.skip("native executables not built")
+    for args in (["--fake"], ["--fake", "--write", "--queues", "3", "--rounds", "6", "--bytes", "1048576"],
+                 ["--fake", "--write", "--bytes", "8192"]):
+        r = subprocess.run([exe] + args, capture_output=True, text=True, timeout=120)
+        assert r.returncode == 0, r.stdout + r.stderr
+        res = json.loads(r.stdout.strip().splitlines()[-1])
+        assert res["ok"] and res["fake"] and len(res["read_us"]) >= 4
+    r = subprocess.run([exe, "--node", "/dev/no_such_snvme_node"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1 and "cannot open snvme node" in r.stdout
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2 and "exactly one of" in r.stderr

@@ -3,7 +3,9 @@
 * ``tutti_b200/bin/tutti_daemon``        - the device-manager daemon (queue leases);
 * ``tutti_b200/bin/tutti_posix_roundtrip`` - the public C++ API end to end on the POSIX data path
 * ``tutti_b200/bin/tutti_native_tests``  - C++ contract tests of the runtime
-  (StorageRuntime against the mock DataPath kit, object store, config spec).
+  (StorageRuntime against the mock DataPath kit, object store, config spec);
+* ``tutti_b200/bin/tutti_snvme_smoke``   - bring-up check of one controller behind
+  the snvme driver (``--node /dev/snvmN``) or the fake driver (``--fake``).
 
     python -m tutti_b200.build_native
 """
@@ -33,6 +35,10 @@ TARGETS = {
         "runtime/storage_runtime.cpp", "datapaths/posix_data_path.cpp", "objects/object_store.cpp",
         "config/yaml_lite.cpp", "config/runtime_spec.cpp", "daemon/lease_ledger.cpp",
         "resolvers/file_resolvers.cpp", "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",
+    ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
+    "tutti_snvme_smoke": ([
+        "examples/snvme_smoke.cpp", "nvme/snvme_client.cpp", "testing/fake_snvme.cpp",
+        "nvme/emulated_controller.cpp", "nvme/host_memory.cpp",
     ], ["-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.join(CUDA, "lib64")]),
     # the public C++ API without a GPU: runtime assembly, open, register, submit, wait
     "tutti_posix_roundtrip": ([

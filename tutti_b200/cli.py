@@ -11,6 +11,7 @@
     python -m tutti_b200 nvme-unbind [BDF ...] [--driver snvme] # release controllers (all by default)
     python -m tutti_b200 raid0-create DEV DEV ... [--chunk-kib 64] --yes   # destroys the drives' data
     python -m tutti_b200 raid0-delete mdN --yes                 # stops the array
+    python -m tutti_b200 snvme-smoke (--node /dev/snvmN | --fake) [--write] ...   # controller bring-up check
     python -m tutti_b200 bench {kernels,ttft,fanout,mla,trace,sweep,plumbing,vllm} [args...]
     python -m tutti_b200 test [--gpu] [--dry-run] [pytest args...]   # pytest suites + C++ contract suite
     python -m tutti_b200 vllm-config --root R [--mounts M ...] [--preset JSON] ...   # --kv-transfer-config JSON
@@ -166,6 +167,14 @@ def cmd_raid0_delete(args) -> int:
     return _admin(lambda: da.raid0_delete(args.md, args.yes))
 
 
+def cmd_snvme_smoke(args) -> int:
+    exe = _bin("tutti_snvme_smoke")
+    if not os.path.exists(exe):
+        print("tutti_snvme_smoke is not built (python -m tutti_b200 build)", file=sys.stderr)
+        return 1
+    return subprocess.run([exe] + list(args.rest)).returncode
+
+
 def cmd_bench(args) -> int:
     mod = importlib.import_module(f"tutti_b200.benchmarks.{BENCHES[args.which]}")
     rc = mod.main(list(args.rest))
@@ -274,6 +283,8 @@ def main(argv=None) -> int:
     rd.add_argument("md")
     rd.add_argument("--yes", action="store_true", help="confirm: the array is stopped")
     rd.set_defaults(fn=cmd_raid0_delete)
+    sm = sub.add_parser("snvme-smoke")
+    sm.set_defaults(fn=cmd_snvme_smoke, passthrough=True)  # arguments go to tutti_snvme_smoke
     b = sub.add_parser("bench")
     b.add_argument("which", choices=sorted(BENCHES))
     b.add_argument("rest", nargs=argparse.REMAINDER)
