@@ -384,6 +384,41 @@ TEST(contract_shutdown_waits_for_inflight_then_releases_them) {
     CHECK(f.rt->state() == RuntimeState::STOPPED);
 }
 
+TEST(contract_shutdown_past_its_deadline_keeps_pending_ops_and_can_be_retried) {
+    Fixture f;
+    f.dp.set_manual_mode(true);
+    IoRequest r[1] = {f.req(0, 512)};
+    auto o = f.rt->submit(r, 1, f.ctx());
+    CHECK(o.io.has_value());
+    auto st = f.rt->shutdown(20);
+    CHECK(st.code() == StatusCode::TIMEOUT);
+    CHECK(f.rt->state() == RuntimeState::DRAINING && !f.dp.shut_down);
+    // draining: no new work, the pending op stays observable and completes normally
+    auto o2 = f.rt->submit(r, 1, f.ctx());
+    CHECK(!o2.io && o2.status.code() == StatusCode::NOT_READY);
+    CHECK(f.rt->query(*o.io).value().state == IoState::IN_FLIGHT);
+    f.dp.complete_all();
+    CHECK(completed(*f.rt, *o.io, 512));
+    CHECK(f.rt->shutdown(1000).ok());
+    CHECK(f.rt->state() == RuntimeState::STOPPED && f.dp.shut_down);
+}
+
+TEST(contract_close_and_unregister_wait_for_the_io_that_uses_them) {
+    Fixture f;
+    f.dp.set_manual_mode(true);
+    IoRequest r[1] = {f.req(0, 512)};
+    auto o = f.rt->submit(r, 1, f.ctx());
+    CHECK(f.rt->close(f.tgt).code() == StatusCode::BUSY);
+    CHECK(f.rt->unregister_memory(f.mem).code() == StatusCode::BUSY);
+    CHECK(f.rt->query_target(f.tgt).ok());  // the refused close changed nothing
+    f.dp.complete_all();
+    CHECK(completed(*f.rt, *o.io, 512));
+    // a terminal op no longer holds them, released or not
+    CHECK(f.rt->close(f.tgt).ok());
+    CHECK(f.rt->unregister_memory(f.mem).ok());
+    CHECK(f.rt->release_io(*o.io).ok());
+}
+
 TEST(contract_failed_progress_does_not_lose_the_op) {
     Fixture f;
     f.dp.set_manual_mode(true);
