@@ -76,8 +76,11 @@ class _Store:
     def register_peer_pool(self, ptr, nbytes, device):
         return 1000 + device
 
-    def restore_placements(self, todo, blocks, mems, layers=None, stream=None):
-        self.calls.append((list(todo), blocks.tolist(), [int(m) for m in mems]))
+    def restore_placements(self, todo, blocks, mems=None, layers=None, stream=None, chunk_layer_mems=None):
+        if chunk_layer_mems is not None:
+            self.calls.append((list(todo), blocks.tolist(), chunk_layer_mems.tolist(), layers))
+        else:
+            self.calls.append((list(todo), blocks.tolist(), [int(m) for m in mems]))
         return "completion"
 
 
@@ -109,6 +112,68 @@ def _fanout_rank_q(rank, world, port, q):
         q.put((rank, repr(e)))
     finally:
         dist.destroy_process_group()
+
+
+def _per_layer_rank_q(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        from tutti_b200.integration.vllm.worker import fanout_items
+
+        keys = [bytes([i]) * 16 for i in range(4)]
+        store = _Store(rank, keys)
+        fan = FanoutRestorer(store, _Peers(rank, world))
+        # vLLM's per-layer caches: layer l of rank r registered as handle 500 + 10 r + l
+        fan.mems, fan.layer_mems = None, [np.asarray([500 + 10 * r + l for l in range(3)], dtype=np.uint64)
+                                          for r in range(world)]
+        blocks = np.arange(8, dtype=np.int64)
+        sliced = fanout_items(keys, blocks, 2, [(r,) for r in range(world)])
+        fan.restore(sliced, n_drives=2, affine_gpus=[0, 1], layers=[1])
+        shared = fanout_items(keys, blocks, 2, [tuple(range(world))] * world)  # an MLA latent cache
+        fan.restore(shared, n_drives=2, affine_gpus=[0, 1], layers=[2])
+        q.put((rank, store.calls))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_per_layer_fanout_is_one_submission_and_replicas_share_a_placement():
+    out = _spawn(_per_layer_rank_q, 2)
+    keys = [bytes([i]) * 16 for i in range(4)]
+    for r in range(2):
+        assert not isinstance(out[r], str), out[r]
+        (todo, blocks, clm, layers), (rtodo, rblocks, rclm, rlayers) = out[r]
+        # sliced: GPU r reads slots {r, r+2} of both ranks' files in ONE submission; row i holds the
+        # per-layer caches of the rank item i lands in
+        assert todo == [(f"/r{o}/seg{i % 2}", 4096 * i) for o in range(2) for i in (r, r + 2)]
+        assert clm == [[500 + 10 * o + l for l in range(3)] for o in range(2) for _ in (r, r + 2)]
+        assert blocks == [[2 * i, 2 * i + 1] for _ in range(2) for i in (r, r + 2)] and layers == [1]
+        # replicated: each chunk's owner holds it; both ranks' items name the owner's placement, so
+        # the data path reads it once and stores it into both ranks' caches
+        owners = [int.from_bytes(k[:8], "little") % 2 for k in keys]
+        mine = [i for i, k in enumerate(keys) if i % 2 == r]  # slot i sits on drive i % 2 -> GPU i % 2
+        assert rtodo == [(f"/r{owners[i]}/seg{i % 2}", 4096 * i) for _ in range(2) for i in mine]
+        assert rclm == [[500 + 10 * o + l for l in range(3)] for o in range(2) for _ in mine] and rlayers == [2]
+
+
+def test_fanout_items_follow_replica_groups():
+    from tutti_b200.integration.vllm.worker import fanout_items
+    from tutti_b200.parallel.replica_layout import replica_group, replica_owner
+
+    keys = [bytes([i, 7]) * 8 for i in range(3)]
+    blocks = np.arange(6)
+    groups = [replica_group(r, 4, 2) for r in range(4)]  # 2 KV heads over TP4: pairs (0,1), (2,3)
+    items = fanout_items(keys, blocks, 2, groups)
+    assert len(items) == 12
+    for it in items:
+        g = groups[it.rank]
+        assert it.src == replica_owner(it.key, g) and it.src in g
+        i = keys.index(it.key)
+        assert list(it.block_ids) == [2 * i, 2 * i + 1]
+    sliced = fanout_items(keys, blocks, 2, [(r,) for r in range(4)])
+    assert all(it.src == it.rank and it.source is None for it in sliced)
 
 
 def _spawn(fn, world=2, *extra):

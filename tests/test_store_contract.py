@@ -103,3 +103,36 @@ def test_layerwise_plan_on_a_host_pool(env):
         plan.wait_layer(layer)
     plan.finish()
     assert torch.equal(pool[:, :, 20:24], ref) and plan.read_ms() is not None
+
+
+def test_one_placement_restore_lands_in_several_ranks_per_layer_caches(tmp_path):
+    """chunk_layer_mems: row i names the per-layer caches of the rank item i lands in; a placement
+    named for two ranks (a replicated cache) is read once and stored into both."""
+    store = open_store("segment-files", tmp_path)
+    try:
+        gen = torch.Generator().manual_seed(5)
+        own = [torch.randn(G.planes, 32, G.block_size, G.num_kv_heads, G.head_dim, generator=gen).to(torch.bfloat16)
+               for _ in range(G.num_layers)]
+        store.register_layers(own)
+        k = keys_for(7, 2)
+        store.put_paged(k, np.arange(4).reshape(2, 2)).wait()
+        peer = [torch.zeros_like(t) for t in own]  # another rank's per-layer caches
+        peer_h = [store.runtime.register_memory(t.data_ptr(), t.numel() * t.element_size(), "host", -1) for t in peer]
+        own_h = [int(h) for h in store._layer_mems]
+        places = []
+        for key in k:
+            uri, off, _slot, _gen = store.objects.lookup(bytes(key))
+            places.append((uri[len("file://"):], off))
+        # chunk 0 for both ranks (same placement twice), chunk 1 for the peer only
+        todo = [places[0], places[0], places[1]]
+        blocks = np.asarray([[10, 11], [20, 21], [22, 23]], dtype=np.int64)
+        clm = np.asarray([own_h, peer_h, peer_h], dtype=np.uint64)
+        store.restore_placements(todo, blocks, chunk_layer_mems=clm).wait()
+        for l in range(G.num_layers):
+            assert torch.equal(own[l][:, 10:12], own[l][:, 0:2])
+            assert torch.equal(peer[l][:, 20:22], own[l][:, 0:2])
+            assert torch.equal(peer[l][:, 22:24], own[l][:, 2:4])
+        with pytest.raises(ValueError, match="chunk_layer_mems"):
+            store.restore_placements(todo, blocks, chunk_layer_mems=clm[:2])
+    finally:
+        store.close()

@@ -304,17 +304,27 @@ PYBIND11_MODULE(_core, m) {
                py::array_t<std::int64_t, py::array::c_style> block_ids, py::array_t<std::int64_t, py::array::c_style> layers,
                py::dict geo, std::uintptr_t stream, bool host_exec,
                py::array_t<std::uint64_t, py::array::c_style> layer_mems,
-               py::array_t<std::uint64_t, py::array::c_style> chunk_mems) {
+               py::array_t<std::uint64_t, py::array::c_style> chunk_mems,
+               py::array_t<std::uint64_t, py::array::c_style> chunk_layer_mems) {
                 // layer_mems (optional): one memory handle per model layer, for engines that
                 // allocate each layer's KV separately; offsets then omit the layer term.
                 // chunk_mems (optional): one whole-pool memory handle per chunk (e.g. the
                 // pool of the TP rank that chunk is restored for, reached over NVLink).
-                const bool per_layer = layer_mems.size() > 0;
+                // chunk_layer_mems (optional, [chunks, model layers]): per-layer caches of
+                // the rank each chunk lands in; one submission can then serve several
+                // ranks, and chunks named for several ranks are read once (replica merge).
+                const bool per_chunk_layer = chunk_layer_mems.size() > 0;
+                const bool per_layer = layer_mems.size() > 0 || per_chunk_layer;
                 const bool per_chunk = chunk_mems.size() > 0;
                 if (per_chunk && chunk_mems.size() != chunk_targets.size())
                     throw py::value_error("chunk_mems needs one handle per chunk");
+                if (per_chunk_layer && (per_chunk || layer_mems.size() > 0 || chunk_layer_mems.ndim() != 2 ||
+                                        chunk_layer_mems.shape(0) != chunk_targets.size()))
+                    throw py::value_error("chunk_layer_mems is [chunks, layers] and excludes layer_mems and chunk_mems");
                 auto lm = layer_mems.unchecked<1>();
                 auto cm = chunk_mems.unchecked<1>();
+                const std::size_t clm_layers = per_chunk_layer ? static_cast<std::size_t>(chunk_layer_mems.shape(1)) : 0;
+                const std::uint64_t* clm = per_chunk_layer ? chunk_layer_mems.data() : nullptr;
                 // Requests of a paged restore/store in (chunk, layer, block, plane) order:
                 //   target_offset = chunk_offset + layer*segment + j*block_layer + plane*plane_bytes
                 //   memory_offset = ((layer*planes + plane)*num_blocks + block) * plane_bytes
@@ -350,11 +360,13 @@ PYBIND11_MODULE(_core, m) {
                     const TargetHandle th = unpack<TargetHandle>(r.rid_, ct(c));
                     for (std::size_t l = 0; l < nl; ++l) {
                         const std::uint64_t L = static_cast<std::uint64_t>(ly(l));
-                        if (per_layer && !per_chunk && L >= static_cast<std::uint64_t>(layer_mems.size()))
+                        if (per_chunk_layer ? L >= clm_layers
+                                            : (per_layer && !per_chunk && L >= static_cast<std::uint64_t>(layer_mems.size())))
                             throw py::value_error("layer beyond layer_mems");
-                        const MemoryHandle lmh = per_chunk   ? unpack<MemoryHandle>(r.rid_, cm(c))
-                                                 : per_layer ? unpack<MemoryHandle>(r.rid_, lm(L))
-                                                             : mh;
+                        const MemoryHandle lmh = per_chunk_layer ? unpack<MemoryHandle>(r.rid_, clm[c * clm_layers + L])
+                                                 : per_chunk     ? unpack<MemoryHandle>(r.rid_, cm(c))
+                                                 : per_layer     ? unpack<MemoryHandle>(r.rid_, lm(L))
+                                                                 : mh;
                         const std::uint64_t lterm = (per_layer && !per_chunk) ? 0 : L * planes;
                         for (std::size_t j = 0; j < bpc; ++j) {
                             const std::int64_t b = bt(c, j);
@@ -402,7 +414,8 @@ PYBIND11_MODULE(_core, m) {
             py::arg("direction"), py::arg("mem"), py::arg("chunk_targets"), py::arg("chunk_offsets"),
             py::arg("block_ids"), py::arg("layers"), py::arg("geometry"), py::arg("stream") = 0,
             py::arg("host_exec") = false, py::arg("layer_mems") = py::array_t<std::uint64_t>(),
-            py::arg("chunk_mems") = py::array_t<std::uint64_t>())
+            py::arg("chunk_mems") = py::array_t<std::uint64_t>(),
+            py::arg("chunk_layer_mems") = py::array_t<std::uint64_t>())
         .def("query_io",
              [](PyRuntime& r, std::uint64_t io) {
                  auto s = unwrap(r.rt->query(unpack<IoHandle>(r.rid_, io)));

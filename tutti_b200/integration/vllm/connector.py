@@ -40,6 +40,19 @@ def _tp_info():
         return 0, 1, None
 
 
+def _uses_mla(vllm_config) -> bool:
+    return bool(getattr(getattr(vllm_config, "model_config", None), "use_mla", False))
+
+
+def _total_kv_heads(vllm_config) -> int | None:
+    """The model's KV-head count (all TP ranks), or None when vLLM does not say."""
+    mc = getattr(vllm_config, "model_config", None)
+    try:
+        return int(mc.get_total_num_kv_heads())
+    except Exception:  # noqa: BLE001 - replica groups then default to one rank each
+        return None
+
+
 class TuttiConnectorV1(KVConnectorBase_V1):
     def __init__(self, vllm_config, role, kv_cache_config=None):
         super().__init__(vllm_config, role, kv_cache_config)
@@ -80,7 +93,9 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                       # requests) to the blocks the worker reports; the worker only reports
                                       failure_policy="recompute", lookahead=self.cfg.lookahead_k,
                                       max_inflight_saves=self.cfg.max_inflight_saves,
-                                      replica_io=self.cfg.replica_io, group=cpu_group)
+                                      replica_io=self.cfg.replica_io, group=cpu_group,
+                                      replica_kind="latent" if _uses_mla(vllm_config) else "main",
+                                      kv_heads=_total_kv_heads(vllm_config))
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""

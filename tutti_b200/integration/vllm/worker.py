@@ -121,11 +121,33 @@ def layer_index(name: str) -> int:
     return int(m[0])
 
 
+def fanout_items(keys, blocks, blocks_per_chunk: int, groups):
+    """Restore items of one step's loads for every TP rank (``groups[r]``: rank r's replica group).
+
+    Rank r's copy of chunk i lands in the same block ids on every rank (vLLM's
+    block table is shared by the TP group). A rank alone in its group reads its
+    own slice (source = itself); in a larger group every member's item names the
+    chunk's owner (``replica_owner``), so the group's copies share one read.
+    """
+    from ...parallel.fanout import RestoreItem
+    from ...parallel.replica_layout import replica_owner
+
+    bpc = int(blocks_per_chunk)
+    out = []
+    for r, g in enumerate(groups):
+        for i, k in enumerate(keys):
+            src = None if len(g) == 1 else replica_owner(k, g)
+            out.append(RestoreItem(rank=r, key=bytes(k), block_ids=[int(b) for b in blocks[i * bpc:(i + 1) * bpc]],
+                                   source=src))
+    return out
+
+
 class WorkerSide:
     def __init__(self, make_engine: Callable[..., KVEngine], *, block_size: int,
                  chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
                  consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute",
-                 lookahead: int = 4, max_inflight_saves: int = 64, replica_io: bool = False, group=None):
+                 lookahead: int = 4, max_inflight_saves: int = 64, replica_io: bool = False, group=None,
+                 replica_kind: str = "main", kv_heads: int | None = None):
         if failure_policy not in ("recompute", "fail"):
             raise ValueError("kv_load_failure_policy must be recompute or fail")
         self.make_engine = make_engine
@@ -154,6 +176,11 @@ class WorkerSide:
         # and its io kernel stores each rank's slice into that rank's caches over NVLink
         self.replica_io = bool(replica_io) and tp_size > 1
         self.group = group
+        # which ranks hold identical copies (duplicated KV heads, an MLA latent cache):
+        # a chunk of such a cache is read once, by its owner's affine GPU, for the group
+        self.replica_kind = replica_kind
+        self.kv_heads = kv_heads
+        self._replica_groups = [(r,) for r in range(tp_size)]
         self._fan = None
         self._board = None
         self._epoch = 0
@@ -194,6 +221,15 @@ class WorkerSide:
             LOG.warning("[tutti] replica_io needs the direct (paged) NVMe store; each rank restores its own slice")
             self.replica_io = False
             return
+        from ...parallel.replica_layout import replica_group, validate_replica_io
+
+        if self.kv_heads:
+            try:
+                validate_replica_io(self.tp_size, int(self.kv_heads))
+                self._replica_groups = [replica_group(r, self.tp_size, int(self.kv_heads), self.replica_kind)
+                                        for r in range(self.tp_size)]
+            except ValueError as e:
+                LOG.warning("[tutti] replica_io: %s; every rank's slice is read on its own", e)
         self._peers = PeerLayers(layers, self.group)
         self._fan = FanoutRestorer(store, self._peers, self.group)
         self._board = ReadyBoard(layers[0].device.index, self.group, slots=len(layers))
@@ -237,11 +273,9 @@ class WorkerSide:
                 self._plan = _FailedLoad(e)
 
     def _start_fanout_plan(self, keys, blocks):
-        from ...parallel.fanout import FanoutLayerPlan, RestoreItem
+        from ...parallel.fanout import FanoutLayerPlan
 
-        bpc = self.blocks_per_chunk
-        items = [RestoreItem(rank=r, key=k, block_ids=blocks[i * bpc:(i + 1) * bpc].tolist())
-                 for r in range(self.tp_size) for i, k in enumerate(keys)]
+        items = fanout_items(keys, blocks, self.blocks_per_chunk, self._replica_groups)
         self._epoch += 1
         return FanoutLayerPlan(self._fan, self._board, items, self._n_drives, self._affine,
                                list(range(self.engine.geometry.num_layers)), self.engine.io_stream, self._epoch,

@@ -175,26 +175,6 @@ class PeerLayers:
         self._opened.clear()
 
 
-class Completions:
-    """Several submissions waited on as one."""
-
-    def __init__(self, comps):
-        self.comps = [c for c in comps if c is not None]
-
-    def query(self) -> bool:
-        return all(c.query() for c in self.comps)
-
-    def wait(self) -> None:
-        first = None
-        for c in self.comps:
-            try:
-                c.wait()
-            except Exception as e:  # noqa: BLE001 - every submission settles before the first error is raised
-                first = first or e
-        if first is not None:
-            raise first
-
-
 @dataclass
 class RestoreItem:
     """Restore chunk ``key`` into rank ``rank``'s pool blocks ``block_ids``.
@@ -277,14 +257,12 @@ class FanoutRestorer:
         if not todo:
             return None
         if self.layer_mems is not None:
-            # one submission per destination rank: its per-layer caches
-            comps = []
-            for r in sorted(set(ranks)):
-                sel = [i for i, x in enumerate(ranks) if x == r]
-                comps.append(self.kv.restore_placements([todo[i] for i in sel],
-                                                        np.asarray([blocks[i] for i in sel], dtype=np.int64),
-                                                        layers=layers, stream=stream, layer_mems=self.layer_mems[r]))
-            return Completions(comps)
+            # one submission for every destination rank: row i names the per-layer caches of
+            # the rank item i lands in; a placement named for several ranks (a replicated
+            # cache) becomes one read stored into each of them
+            clm = np.stack([self.layer_mems[r] for r in ranks])
+            return self.kv.restore_placements(todo, np.asarray(blocks, dtype=np.int64), layers=layers, stream=stream,
+                                              chunk_layer_mems=clm)
         mems = [self.mems[r] for r in ranks]
         return self.kv.restore_placements(todo, np.asarray(blocks, dtype=np.int64), np.asarray(mems, np.uint64),
                                              layers=layers, stream=stream)

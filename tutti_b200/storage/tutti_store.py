@@ -368,20 +368,25 @@ class TuttiKVStore:
         """Register another GPU's whole KV pool (CUDA-IPC mapped) as a restore destination."""
         return self.runtime.register_memory(int(ptr), int(nbytes), "device", int(device))
 
-    def restore_placements(self, placements, block_ids, chunk_mems=None, layers=None, stream=None, layer_mems=None):
+    def restore_placements(self, placements, block_ids, chunk_mems=None, layers=None, stream=None, layer_mems=None,
+                           chunk_layer_mems=None):
         """Restore chunks given by explicit (segment file path, payload offset) placements.
 
         ``chunk_mems[i]`` names the pool (this rank's or a peer's) chunk i lands in;
         ``layer_mems[l]`` instead names the per-layer tensor layer l lands in (a peer's
-        per-layer caches, mapped through IPC); placements may belong to other ranks'
-        namespaces (the files are opened here).
+        per-layer caches, mapped through IPC); ``chunk_layer_mems[i, l]`` names layer
+        l's tensor of the rank chunk i lands in (one submission for several ranks'
+        per-layer caches: a placement named for several ranks is read once).
+        Placements may belong to other ranks' namespaces (the files are opened here).
         """
         g = self.geometry
         block_ids = np.asarray(block_ids, dtype=np.int64).reshape(len(placements), g.blocks_per_chunk)
         layers = np.arange(g.num_layers) if layers is None else np.asarray(layers, dtype=np.int64).reshape(-1)
         cm = None if chunk_mems is None else np.asarray(chunk_mems, dtype=np.uint64)
         lm = None if layer_mems is None else np.asarray(layer_mems, dtype=np.uint64)
-        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream, chunk_mems=cm, layer_mems=lm)
+        clm = None if chunk_layer_mems is None else np.ascontiguousarray(chunk_layer_mems, dtype=np.uint64)
+        ios, nbytes = self._submit_paged("read", placements, block_ids, layers, stream, chunk_mems=cm, layer_mems=lm,
+                                         chunk_layer_mems=clm)
         comp = NativeCompletion(self.runtime, ios, nbytes=nbytes)
         self._track(comp)
         return comp
@@ -406,7 +411,8 @@ class TuttiKVStore:
         return comp
 
     def _submit_paged(self, direction: str, placements, block_ids: np.ndarray, layers: np.ndarray, stream,
-                      chunk_mems: np.ndarray | None = None, layer_mems: np.ndarray | None = None):
+                      chunk_mems: np.ndarray | None = None, layer_mems: np.ndarray | None = None,
+                      chunk_layer_mems: np.ndarray | None = None):
         """Paged requests generated natively (no per-request Python work); retried while leases are busy."""
         g = self.geometry
         handles = np.asarray(self.targets_for([p for p, _ in placements]), dtype=np.uint64)
@@ -421,9 +427,14 @@ class TuttiKVStore:
         sptr = self._stream_ptr(stream)
         host = self.backend != "nvme-gpu"
         for _ in range(self.max_retries):
-            r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host,
-                                          self._layer_mems if layer_mems is None else layer_mems,
-                                          chunk_mems if chunk_mems is not None else np.zeros(0, dtype=np.uint64))
+            none = np.zeros(0, dtype=np.uint64)
+            if chunk_layer_mems is not None:
+                r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host,
+                                              none, none, chunk_layer_mems)
+            else:
+                r = self.runtime.submit_paged(direction, int(self._pool[1]), handles, offsets, bt, ly, geo, sptr, host,
+                                              self._layer_mems if layer_mems is None else layer_mems,
+                                              chunk_mems if chunk_mems is not None else none)
             if not r["rejected"]:
                 return [r["io"]], int(r["count"]) * g.plane_block_bytes
             reasons = " ".join(r["reasons"])
