@@ -20,12 +20,17 @@ and taken as the max over ranks; the uncached remainder is persisted after its
 (modelled) prefill. Nothing is kept in HBM between requests, so every reuse is
 an SSD restore.
 
-The prefill and decode compute of a 70B model is not run: prefill time is
-modelled as FLOPs / (sustained bf16 peak x ``--mfu``) (weights GEMMs plus
-causal attention over the context), decode as 256 steps of reading the rank's
-weights at the measured HBM bandwidth, and continuous batching is assumed so
-that only prefills queue. TTFT at each arrival rate (0.5, 1, 2, 4 req/s) is
-the FIFO wait plus the request's restore and modelled prefill.
+Prefill (``--prefill run``, the default) runs for real: a random-init
+Llama-3.1-70B sharded over the TP ranks (``models.llama.LlamaModel``: sharded
+heads and MLP, NCCL all-reduce after the row-parallel GEMMs) prefills each
+request's uncached tokens after its restored prefix, attending over the
+restored KV in the paged pool, and the new chunks it writes are what gets
+persisted; the recompute baseline prefills the whole prompt. Both are
+CUDA-event timed, max over ranks. ``--prefill model`` instead models prefill
+as FLOPs / (sustained bf16 peak x ``--mfu``). Decode is modelled as 256 steps
+of reading the rank's weights at the measured HBM bandwidth, and continuous
+batching is assumed so that only prefills queue. TTFT at each arrival rate
+(0.5, 1, 2, 4 req/s) is the FIFO wait plus the request's restore and prefill.
 Parity: reference scripts/vllm/vllm_profile_offline.py (--tokens, --reuse-pct)
 and doc/design/kv-storage-layout-and-io-submission.md (A/B request latency).
 """
@@ -46,6 +51,7 @@ import torch.distributed as dist
 from .. import ops
 from ..index.chunk_index import chunk_keys_for_tokens
 from ..models.kv_geometry import LLAMA3_70B
+from ..models.llama import LLAMA_3_1_70B, LlamaModel
 from ..parallel.fanout import FanoutRestorer, PeerPools, RestoreItem
 from ..storage.tutti_store import TuttiKVStore
 
@@ -70,7 +76,9 @@ def parse(argv=None):
     p.add_argument("--affine", default="", help="drive d belongs to GPU affine[d %% len]; default all ranks")
     p.add_argument("--warm", type=int, default=16,
                    help="persist the N most popular prefixes before the trace (a warm SSD cache)")
-    p.add_argument("--mfu", type=float, default=0.5)
+    p.add_argument("--mfu", type=float, default=0.5, help="--prefill model: fraction of the sustained bf16 peak")
+    p.add_argument("--prefill", choices=["run", "model"], default="run",
+                   help="run: a random-init 70B TP prefill on the GPUs; model: FLOPs at --mfu")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--root", default=os.environ.get("TUTTI_BENCH_ROOT", "/tmp/tutti_trace"))
     p.add_argument("--leases", type=int, default=128)
@@ -181,6 +189,24 @@ def main(argv=None) -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    model = None
+    if args.prefill == "run":
+        model = LlamaModel(LLAMA_3_1_70B, dev, seed=3, tp_rank=rank, tp_size=world)
+        # load the prefill's kernels before any restore is in flight (a lazily loaded
+        # kernel waits for the running io kernel)
+        model.prefill([torch.zeros(g.chunk_tokens, dtype=torch.long)], [0], [torch.arange(g.blocks_per_chunk)], pool)
+        torch.cuda.synchronize()
+
+    def run_prefill(tokens: list[int], cached: int, table: np.ndarray) -> float:
+        """Device ms (max over ranks) of prefilling ``tokens[cached:]`` after ``cached`` tokens."""
+        new = torch.tensor(tokens[cached:], dtype=torch.long)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        model.prefill([new], [cached], [torch.from_numpy(table.reshape(-1))], pool)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return mx(e0.elapsed_time(e1))
+
     records = []
     gen = torch.Generator(device=dev).manual_seed(rank)
     digests: dict[bytes, torch.Tensor] = {}  # this rank's slice of every persisted chunk
@@ -228,12 +254,18 @@ def main(argv=None) -> int:
             got = got.reshape(hit, g.blocks_per_chunk, *got.shape[1:])
             mismatches += sum(int(not torch.equal(got[c], digests[keys[c]])) for c in range(hit))
         write_ms = 0.0
+        prefill_ms = recompute_ms = None
+        toks = prefix_tokens(req["prefix"], n)
+        if model is not None:
+            # the uncached tokens (at least the last one, whose logits start decoding)
+            prefill_ms = run_prefill(toks, min(hit * g.chunk_tokens, n - 1), blocks)
         if hit < len(keys):
-            # the prefill (modelled) produced the remaining chunks: fill them, then persist them
+            # the prefill produced the remaining chunks (modelled: random KV); persist them
             nb = (len(keys) - hit) * g.blocks_per_chunk
             bidx = torch.from_numpy(blocks[hit:].reshape(-1)).to(dev)
-            pool[:, :, bidx] = torch.randn((g.num_layers, g.planes, nb) + tuple(pool.shape[3:]), dtype=g.dtype,
-                                           device=dev, generator=gen)
+            if model is None:
+                pool[:, :, bidx] = torch.randn((g.num_layers, g.planes, nb) + tuple(pool.shape[3:]), dtype=g.dtype,
+                                               device=dev, generator=gen)
             torch.cuda.synchronize()
             t0 = time.perf_counter()
             if args.restore == "fanout":
@@ -247,14 +279,19 @@ def main(argv=None) -> int:
             dg = ops.kv_checksum(pool, bidx).cpu().reshape(len(keys) - hit, g.blocks_per_chunk, g.num_layers, g.planes)
             for c in range(hit, len(keys)):
                 digests[keys[c]] = dg[c - hit]
+        if model is not None:
+            recompute_ms = run_prefill(toks, 0, blocks)  # the same prompt without the store
         hit_tokens = hit * g.chunk_tokens
         records.append({"tokens": n, "hit_tokens": hit_tokens, "restore_ms": restore_ms, "write_ms": write_ms,
                         "restore_bytes": world * hit * g.blocks_per_chunk * g.num_layers * g.block_layer_bytes,
-                        "prefill_s": prefill_seconds(n - hit_tokens, hit_tokens, world, pk, args.mfu),
-                        "prefill_full_s": prefill_seconds(n, 0, world, pk, args.mfu)})
+                        "prefill_s": prefill_ms / 1e3 if prefill_ms is not None
+                        else prefill_seconds(n - hit_tokens, hit_tokens, world, pk, args.mfu),
+                        "prefill_full_s": recompute_ms / 1e3 if recompute_ms is not None
+                        else prefill_seconds(n, 0, world, pk, args.mfu)})
 
     store.close()
     peers.close()
+    del model
     bad = torch.tensor([mismatches], dtype=torch.int64)
     dist.all_reduce(bad, group=ctl)
     ok = int(bad.item()) == 0
@@ -294,8 +331,11 @@ def main(argv=None) -> int:
                "write_GBps": round(sum(world * (r["tokens"] - r["hit_tokens"]) // g.block_size * g.num_layers
                                        * g.block_layer_bytes for r in records)
                                    / max(1e-9, sum(r["write_ms"] for r in records) / 1e3) / 1e9, 3),
-               "ttft": per_rate, "decode_model_s": round(decode_s, 3),
-               "compute_model": {"mfu": args.mfu, "peaks": pk}, "restored_chunks_mismatched": int(bad.item()),
+               "ttft": per_rate, "decode_model_s": round(decode_s, 3), "prefill": args.prefill,
+               "prefill_ms_p50": round(float(np.median([r["prefill_s"] for r in records])) * 1e3, 2),
+               "recompute_prefill_ms_p50": round(float(np.median([r["prefill_full_s"] for r in records])) * 1e3, 2),
+               "compute_model": {"mfu": args.mfu, "peaks": pk} if args.prefill == "model" else None,
+               "restored_chunks_mismatched": int(bad.item()),
                "ok": ok}
         print(json.dumps(out))
     del pool
