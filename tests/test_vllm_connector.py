@@ -383,9 +383,10 @@ def test_worker_back_pressure_waits_for_the_oldest_save_only():
     g0, g1, g2 = w.engine.gates
     assert g0.waited_before_done and not g1.waited_before_done and not g2.waited_before_done
     assert w.saves_in_flight() == 2
-    w.engine.wait_idle = lambda: None
+    w.engine.wait_idle = lambda timeout_s=None: None
     w.engine.store = SimpleNamespace()
-    w.shutdown()  # settles everything still in flight
+    g1.done = g2.done = True  # their writes finished on the device
+    w.shutdown()  # settles (commits) everything still in flight
     assert w.saves_in_flight() == 0 and g2.done
 
 
@@ -413,3 +414,20 @@ def test_scheduler_names_finished_requests_whose_saves_may_be_in_flight():
     nxt = s.build_meta([])
     assert nxt.finished_saving == ["a"]  # the workers order this step's forward after a's saves
     assert s.build_meta([]).finished_saving == []
+
+
+def test_worker_shutdown_does_not_wait_past_its_deadline_for_a_stuck_save():
+    class _Stuck(_SaveGate):
+        def wait(self):  # a save that never finishes would block here
+            raise AssertionError("waited on a running save")
+
+    w = _saving_worker()
+    w.engine.store_chunks = lambda keys, bt, after=None: _Stuck()
+    w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", [b"a" * 16], [0, 1])]))
+    idle = []
+    w.engine.wait_idle = lambda timeout_s=None: idle.append(timeout_s)
+    t0 = __import__("time").monotonic()
+    w.shutdown(timeout_s=0.2)
+    assert __import__("time").monotonic() - t0 < 5.0
+    assert w.saves_in_flight() == 1  # left uncommitted, not waited for
+    assert idle and idle[0] <= 0.2

@@ -17,6 +17,22 @@ class LoadGateError(RuntimeError):
         self.failed_chunks = sorted(set(failed_chunks))
 
 
+def settle_by(comp, deadline: float | None) -> bool:
+    """Wait for ``comp`` until ``deadline`` (``time.monotonic()``; None: no limit).
+
+    Returns False, without waiting further, when it is still running at the
+    deadline; otherwise settles it (``wait``, which may raise its failure) and
+    returns True. For shutdown paths that must not block on a stuck operation.
+    """
+    if deadline is not None:
+        while not comp.query():
+            if time.monotonic() >= deadline:
+                return False
+            time.sleep(0.001)
+    comp.wait()
+    return True
+
+
 class AggregateCompletion:
     """Waits on several completions; the first error is raised after all were waited."""
 

@@ -466,12 +466,21 @@ class KVEngine:
         self._maybe_checkpoint()
         return done
 
-    def wait_idle(self) -> None:
+    def wait_idle(self, timeout_s: float | None = None) -> None:
+        """Settle the queued writes; with ``timeout_s``, writes still running then are dropped (not committed)."""
+        from .completion import settle_by
+
+        deadline = None if timeout_s is None else time.monotonic() + float(timeout_s)
         while self._writes:
             try:
-                self._writes.popleft().wait()
+                if not settle_by(self._writes[0], deadline):
+                    LOG.warning("%d write(s) still running after %.0f s; left uncommitted", len(self._writes), timeout_s)
+                    self._writes.clear()
+                    break
             except Exception as e:  # noqa: BLE001
                 LOG.warning("write failed: %s", e)
+            if self._writes:
+                self._writes.popleft()
         self._maybe_checkpoint(force=False)
 
     def _maybe_checkpoint(self, force: bool = False) -> None:

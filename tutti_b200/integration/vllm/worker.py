@@ -404,15 +404,29 @@ class WorkerSide:
     def saves_in_flight(self) -> int:
         return len(self._saves)
 
-    def settle_saves(self) -> int:
-        """Wait for every save in flight and commit it (reported in the next step's metadata).
+    def settle_saves(self, timeout_s: float | None = None) -> int:
+        """Wait for the saves in flight and commit them (reported in the next step's metadata).
 
         Not needed by vLLM's step loop (commits are harvested without blocking);
         for shutdown and for callers that must see their chunks committed now.
+        With ``timeout_s``, saves still running at the deadline are left
+        uncommitted (their chunks are simply not persisted) instead of waited
+        for. Returns how many saves were settled.
         """
-        n = len(self._saves)
+        n = 0
+        deadline = None if timeout_s is None else time.monotonic() + float(timeout_s)
         while self._saves:
-            self._settle_save(*self._saves.popleft())
+            spec, comp = self._saves[0]
+            if deadline is not None:
+                while not comp.query() and time.monotonic() < deadline:
+                    time.sleep(0.001)
+                if not comp.query():
+                    LOG.warning("[tutti] %d save(s) still running after %.0f s; left uncommitted",
+                                len(self._saves), timeout_s)
+                    break
+            self._saves.popleft()
+            self._settle_save(spec, comp)
+            n += 1
         return n
 
     # -- completion reporting -------------------------------------------------
@@ -436,18 +450,26 @@ class WorkerSide:
         out, self._load_error_blocks = self._load_error_blocks, set()
         return out
 
-    def shutdown(self) -> None:
-        self.settle_saves()
+    def shutdown(self, timeout_s: float = 120.0) -> None:
+        """Settle saves and loads, then close the store; nothing waits past ``timeout_s`` in all."""
+        from ...engine.completion import settle_by
+
+        deadline = time.monotonic() + float(timeout_s)
+        left = lambda: max(0.0, deadline - time.monotonic())  # noqa: E731
+        self.settle_saves(left())
         if self._board is not None:
             self._board.close()
             self._peers.close()
         for comp, _, _ in self._async.values():
             try:
-                comp.wait()
+                settle_by(comp, deadline)
             except Exception:  # noqa: BLE001
                 pass
         self._async.clear()
         if self.engine is not None:
-            self.engine.wait_idle()
+            self.engine.wait_idle(left())
             if hasattr(self.engine.store, "close"):
-                self.engine.store.close()
+                try:
+                    self.engine.store.close(left())
+                except TypeError:  # a store whose close takes no deadline
+                    self.engine.store.close()

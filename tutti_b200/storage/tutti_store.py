@@ -220,15 +220,26 @@ class TuttiKVStore:
             raise ValueError(f"unknown backend {self.backend!r}")
         return self
 
-    def close(self) -> None:
+    def close(self, timeout_s: float | None = None) -> None:
+        """Settle what is in flight and shut the runtime down; with ``timeout_s`` nothing waits past it."""
+        from ..engine.completion import settle_by
+
+        deadline = None if timeout_s is None else time.monotonic() + float(timeout_s)
         for comp in list(self._inflight):
             try:
-                comp.wait()
+                if not settle_by(comp, deadline):
+                    break  # the runtime's shutdown below reports what is still running
             except StoreIOError:
                 pass
         self._inflight.clear()
         if self.runtime is not None:
-            self.runtime.shutdown(30_000)
+            left_ms = 30_000 if deadline is None else int(max(0.0, min(30.0, deadline - time.monotonic())) * 1e3)
+            try:
+                self.runtime.shutdown(left_ms)
+            except Exception as e:  # noqa: BLE001 - IO still running at the deadline
+                import logging
+
+                logging.getLogger("tutti_b200.store").warning("runtime shutdown: %s", e)
             self.runtime = None
         self._targets.clear()
         self._pool = None
