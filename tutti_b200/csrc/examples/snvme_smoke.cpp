@@ -106,7 +106,8 @@ struct HostQueue {
     std::uint16_t cid = 1;
 
     // status field of the CQE; -1 when none arrived within `timeout_ms`
-    int run(tutti::nvme::Sqe e, int timeout_ms) {
+    int run(const tutti::nvme::Sqe& cmd, int timeout_ms) {
+        tutti::nvme::Sqe e = cmd;
         e.cdw0 = (e.cdw0 & 0xFFFFu) | (static_cast<std::uint32_t>(cid++) << 16);
         volatile tutti::nvme::Sqe* slot = q.sq + tail;
         std::memcpy(const_cast<tutti::nvme::Sqe*>(slot), &e, sizeof e);
