@@ -3,6 +3,7 @@
     python -m tutti_b200 build                 # CUDA extensions (sm_100a) + native executables
     python -m tutti_b200 status [--json]       # GPUs, extensions, native binaries, a runtime's capabilities
     python -m tutti_b200 daemon --config F     # run tutti_daemon (queue leases) in the foreground
+    python -m tutti_b200 daemon-grpc --socket S [--listen 127.0.0.1:50051]   # Tutti's NvmeService over it
     python -m tutti_b200 selftest              # C++ contract suite (no GPU needed)
     python -m tutti_b200 fiemap FILE           # extents the FIEMAP resolver sees
     python -m tutti_b200 probe-raid0 md0 [--sysfs /sys]
@@ -93,6 +94,12 @@ def cmd_daemon(args) -> int:
         return 2
     os.execv(exe, [exe, "--config", args.config] + list(args.rest))
     return 0  # not reached
+
+
+def cmd_daemon_grpc(args) -> int:
+    from . import daemon_grpc
+
+    return daemon_grpc.main(list(args.rest))
 
 
 def cmd_selftest(_args) -> int:
@@ -253,6 +260,8 @@ def main(argv=None) -> int:
     d.add_argument("--config", required=True)
     d.add_argument("rest", nargs=argparse.REMAINDER)
     d.set_defaults(fn=cmd_daemon)
+    dg = sub.add_parser("daemon-grpc")
+    dg.set_defaults(fn=cmd_daemon_grpc, passthrough=True)  # --socket/--listen go to the gateway
     sub.add_parser("selftest").set_defaults(fn=cmd_selftest)
     f = sub.add_parser("fiemap")
     f.add_argument("file")

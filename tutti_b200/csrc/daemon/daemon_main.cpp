@@ -269,6 +269,11 @@ int main(int argc, char** argv) {
             d.max_data_size = o.value()->info().max_transfer_bytes;
             d.max_queues_per_group = o.value()->info().max_queues_per_group;
             d.lba_bytes = o.value()->info().lba_bytes;
+            d.max_user_qid = o.value()->info().last_user_qid;
+            d.chrdev_minor = o.value()->minor();
+            std::uint32_t stride_log = 0;
+            while ((4u << stride_log) < o.value()->info().doorbell_stride && stride_log < 15) ++stride_log;
+            d.doorbell_stride = stride_log;
             owners.push_back(std::move(o).value());
         }
     }

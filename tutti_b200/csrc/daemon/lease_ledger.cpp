@@ -328,6 +328,10 @@ void put_device(Message& rsp, const std::string& p, const DeviceInfo& d, const L
     rsp.kv[p + "queue_depth"] = std::to_string(d.queue_depth);
     rsp.kv[p + "max_data_size"] = std::to_string(d.max_data_size);
     rsp.kv[p + "max_queues_per_group"] = std::to_string(d.max_queues_per_group);
+    rsp.kv[p + "page_size"] = std::to_string(d.page_size);
+    rsp.kv[p + "dstrd"] = std::to_string(d.doorbell_stride);
+    rsp.kv[p + "max_user_qid"] = std::to_string(d.max_user_qid);
+    rsp.kv[p + "chrdev_minor"] = std::to_string(d.chrdev_minor);
     rsp.kv[p + "allowed_accel_ids"] = d.accelerators.empty() ? "*" : join_ids(d.accelerators);
     rsp.kv[p + "kind"] = d.kind;
     (void)ledger;

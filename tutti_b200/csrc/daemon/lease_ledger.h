@@ -39,6 +39,10 @@ struct DeviceInfo {
     std::uint32_t queue_depth = 0;
     std::uint64_t max_data_size = 0;
     std::uint32_t max_queues_per_group = 32;
+    std::uint32_t page_size = 4096;      // the controller's memory page size (CC.MPS)
+    std::uint32_t doorbell_stride = 0;   // CAP.DSTRD (doorbells 4 << DSTRD bytes apart)
+    std::uint32_t max_user_qid = 0;      // highest QID the driver hands to user queues (0: unknown)
+    std::int32_t chrdev_minor = -1;      // the snvme node's minor (-1: none)
     bool available = true;     // false: bring-up or mount failed (see diagnostic); not leased
     std::string diagnostic;
 };
