@@ -196,7 +196,8 @@ def _ensure_reference_kernels() -> str | None:
 
     if glob.glob(os.path.join(REF_DIR, "tutti_kv_transfer", "_native*.so")):
         return None
-    src = os.environ.get("TUTTI_REFERENCE_SRC", "/root/reference")
+    # the reference checkout next to this repository, unless named
+    src = os.environ.get("TUTTI_REFERENCE_SRC") or os.path.join(os.path.dirname(ROOT), "reference")
     if not os.path.isdir(os.path.join(src, "csrc", "kv_transfer")):
         return "reference kv_transfer extension not built and its sources are not on this machine"
     import tempfile
