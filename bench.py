@@ -39,6 +39,8 @@ ZERO_COPY_GBPS = 51.4  # GPU reads of pinned host memory, measured on this pool'
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--no-numa-bind", action="store_true",
+                   help="keep every CPU (default: each rank runs on its GPU's NUMA node)")
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="tutti", choices=["tutti", "reference", "posix"])
@@ -49,7 +51,7 @@ def parse():
     p.add_argument("--controller-threads", type=int, default=0, help="0: auto")
     p.add_argument("--direct-io", action="store_true", help="O_DIRECT backing reads (drive-bound)")
     p.add_argument("--no-verify", action="store_true")
-    p.add_argument("--timing", action="store_true", help="per-command %globaltimer breakdown (stderr)")
+    p.add_argument("--timing", action="store_true", help="per-command %%globaltimer breakdown (stderr)")
     p.add_argument("--leases", type=int, default=192, help="queue leases (CTAs) per GPU")
     p.add_argument("--ctas", type=int, default=0, help="CTAs one restore may use (0: by media)")
     p.add_argument("--slots", type=int, default=16)
@@ -130,6 +132,37 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+NUMA_BIND: dict = {"bound": False, "why": "not requested"}
+
+
+def numa_bind(local: int) -> dict:
+    """Run this rank's host work on its GPU's NUMA node (both arms; the harness, not either product).
+
+    The calling thread, and every thread it starts afterwards (drive threads,
+    staging copies), is restricted to the CPUs sysfs lists as local to the
+    GPU's PCIe function, so page-locked buffers allocated afterwards land on
+    that node. Nothing outside this process changes.
+    """
+    import torch
+
+    try:
+        p = torch.cuda.get_device_properties(local)
+        bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bdf}/local_cpulist") as f:
+            cpus = set()
+            for part in f.read().strip().split(","):
+                a, _, b = part.partition("-")
+                if a:
+                    cpus.update(range(int(a), int(b or a) + 1))
+    except (OSError, ValueError, RuntimeError, AttributeError) as e:
+        return {"bound": False, "why": f"{type(e).__name__}: {e}"[:120]}
+    allowed = cpus & os.sched_getaffinity(0)
+    if not allowed:
+        return {"bound": False, "gpu": bdf, "why": "no local CPU is allowed"}
+    os.sched_setaffinity(0, allowed)
+    return {"bound": True, "gpu": bdf, "cpus": len(allowed)}
+
+
 def dist_setup():
     import torch
     import torch.distributed as dist
@@ -137,6 +170,10 @@ def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    global NUMA_BIND
+    torch.cuda.set_device(local)  # before the first CUDA query: no context on another GPU
+    if os.environ.get("TUTTI_BENCH_NUMA_BIND", "1") != "0":
+        NUMA_BIND = numa_bind(local)
     if world > 1:
         import datetime
 
@@ -359,7 +396,7 @@ def reference_arm(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (randn KV of the named shape; prefix held by the reference's MemoryKVStore)",
-            "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world,
+            "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world, "numa_bind": NUMA_BIND,
                        "seq_len": args.prefix_tokens, "parallelism": f"dp{world} (one prefix per rank)",
                        "pool_blocks": args.pool_blocks, "path": REF_STAGED_NOTE,
                        "l2": "inputs (4.29 GB/step) larger than L2"},
@@ -444,6 +481,8 @@ def measure_dma_gbps(dev, piece: int = 1 << 20, total: int = 2 << 30) -> float:
 
 def main():
     args = parse()
+    if args.no_numa_bind:
+        os.environ["TUTTI_BENCH_NUMA_BIND"] = "0"
     # More hardware queues (before CUDA starts): the emulated drives' copy
     # streams then rarely share one with a stream that has work waiting on an
     # io kernel.
@@ -642,7 +681,7 @@ def main():
             "data": ("synthetic (randn KV of the named shape; emulated NVMe drives with in-memory media, "
                      "copy-engine DMA into HBM staging)" if memory else
                      "synthetic (randn KV of the named shape; emulated NVMe over page-cached segment files)"),
-            "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world,
+            "config": {"model": "llama-3.1-8b KV (32L x 8H x 128D, block 16)", "global_batch": world, "numa_bind": NUMA_BIND,
                        "seq_len": args.prefix_tokens, "parallelism": f"dp{world} (one prefix per rank)",
                        "pool_blocks": args.pool_blocks, "drives_per_rank": args.drives,
                        "backing": "O_DIRECT" if args.direct_io else "page cache", "media": args.media,

@@ -39,6 +39,7 @@ import torch.distributed as dist
 from ..index.chunk_index import chunk_keys_for_tokens
 from ..models.kv_geometry import DEEPSEEK_V3_MLA, LLAMA3_70B
 from ..parallel.fanout import FanoutRestorer, PeerPools, ReadyBoard, RestoreItem, owner_of
+from ..common import numa
 from ..storage.tutti_store import TuttiKVStore
 
 
@@ -72,6 +73,7 @@ def main(argv=None) -> int:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa_bind = numa.bind_to_gpu(local)  # host work on the GPU's node, before any thread or pinned buffer
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     ctl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
     g = (LLAMA3_70B.with_tp(world) if args.mode == "tp" else DEEPSEEK_V3_MLA)
@@ -224,7 +226,7 @@ def main(argv=None) -> int:
     dist.barrier(group=ctl)
     ok = all(r["verified"] for r in results.values())
     if rank == 0:
-        print(json.dumps({"bench": "fanout", "mode": args.mode, "n_gpus": world, "model": g.fingerprint(),
+        print(json.dumps({"bench": "fanout", "mode": args.mode, "n_gpus": world, "numa_bind": numa_bind, "model": g.fingerprint(),
                           "prefix_tokens": args.prefix_tokens, "drives": drives, "affine_gpus": affine,
                           "steps": args.steps, "warmup": args.warmup, "ordering": args.ordering, "results": results,
                           "store": {"mode": args.store, "wall_ms": round(store_ms, 1)},

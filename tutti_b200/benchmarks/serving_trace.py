@@ -53,6 +53,7 @@ from ..index.chunk_index import chunk_keys_for_tokens
 from ..models.kv_geometry import LLAMA3_70B
 from ..models.llama import LLAMA_3_1_70B, LlamaModel
 from ..parallel.fanout import FanoutRestorer, PeerPools, RestoreItem
+from ..common import numa
 from ..storage.tutti_store import TuttiKVStore
 
 PARAMS_70B = 70.6e9
@@ -147,6 +148,7 @@ def main(argv=None) -> int:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa_bind = numa.bind_to_gpu(local)  # host work on the GPU's node, before any thread or pinned buffer
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     ctl = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=600))
     g = LLAMA3_70B.with_tp(world)
@@ -321,7 +323,7 @@ def main(argv=None) -> int:
         rest_bytes = sum(r["restore_bytes"] for r in hits)
         rest_s = sum(r["restore_ms"] for r in hits) / 1e3
         decode_s = args.output_tokens * (2 * PARAMS_70B / world) / (pk["hbm_gbs"] * 1e9)
-        out = {"bench": "serving_trace", "n_gpus": world, "tp": world, "restore": args.restore,
+        out = {"bench": "serving_trace", "n_gpus": world, "tp": world, "restore": args.restore, "numa_bind": numa_bind,
                "model": g.fingerprint(), "requests": len(records),
                "prefix_tokens": [int(args.min_prefix * args.length_scale), int(args.max_prefix * args.length_scale)],
                "length_scale": args.length_scale, "reuse": args.reuse, "zipf": args.zipf,
