@@ -66,3 +66,26 @@ def test_bench_reference_arm_prints_one_json_line():
     assert len(lines) == 1
     rec = json.loads(lines[0])
     assert rec["impl"] == "reference" and ("unavailable" in rec or "value" in rec)
+
+
+def test_vllm_phase_runner_reaps_the_session_and_bounds_a_hang(tmp_path):
+    """A phase that leaves a child holding its output, and one that hangs: neither blocks the harness."""
+    import sys
+    import time
+
+    from tutti_b200.benchmarks.vllm_e2e import _run_phase_process
+
+    # exits at once but leaves a grandchild (holding stdout) sleeping for a minute
+    leaver = ("import subprocess, sys; subprocess.Popen([sys.executable, '-c', 'import time; time.sleep(60)']);"
+              " print('RESULT {}', flush=True)")
+    t0 = time.monotonic()
+    rc, out, err = _run_phase_process([sys.executable, "-c", leaver], None, 30, str(tmp_path), "leaver")
+    assert rc == 0 and "RESULT {}" in out and time.monotonic() - t0 < 20
+    # hangs: SIGUSR1 makes faulthandler dump the stacks, then the session is killed
+    hang = ("import faulthandler, signal, time; faulthandler.register(signal.SIGUSR1, all_threads=True);"
+            " print('started', flush=True); time.sleep(120)")
+    t0 = time.monotonic()
+    rc, out, err = _run_phase_process([sys.executable, "-c", hang], None, 2, str(tmp_path), "hang")
+    assert rc is None and "started" in out
+    assert "most recent call first" in err  # the dumped stack
+    assert time.monotonic() - t0 < 30
