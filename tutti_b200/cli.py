@@ -55,7 +55,8 @@ def cmd_build(_args) -> int:
 
 
 def status() -> dict:
-    out = {"package": PKG, "binaries": {n: os.path.exists(_bin(n)) for n in ("tutti_daemon", "tutti_native_tests")}}
+    out = {"package": PKG, "binaries": {n: os.path.exists(_bin(n)) for n in ("tutti_daemon", "tutti_native_tests",
+                                                                          "tutti_posix_roundtrip", "tutti_snvme_smoke")}}
     try:
         import torch
 
