@@ -375,3 +375,142 @@ def test_two_gpu_vllm_worker_with_replica_io_restores_every_rank(tmp_path):
         assert ok and failed == {}
     # drive-affine: each GPU read part of the chunks (for both ranks), none read them all
     assert all(out[r][2] > 0 for r in range(2))
+
+
+class _Comp:
+    def __init__(self, fail=False):
+        self.done, self.fail = False, fail
+
+    def query(self):
+        return self.done
+
+    def wait(self):
+        if self.fail:
+            raise OSError("injected write failure")
+
+
+class _Board:
+    """ReadyBoard stand-in: waits are tickets whose outcome the test decides."""
+
+    def __init__(self):
+        self.signals, self.waits = [], []
+        self.gave_up = set()
+
+    def signal(self, slot, value, stream=None):
+        self.signals.append((slot, value))
+
+    def wait(self, slot, value, stream=None, timeout_s=10.0):
+        self.waits.append((slot, value))
+        return len(self.waits) - 1
+
+    def passed(self, t):
+        return True
+
+    def failed(self, t):
+        return [1] if t in self.gave_up else []
+
+    def close(self):
+        pass
+
+
+def _fanin_rank(rank, world, port, q, fail_rank):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from types import SimpleNamespace
+
+        from tutti_b200.integration.vllm.metadata import SaveSpec, TuttiConnectorMetadata
+        from tutti_b200.integration.vllm.worker import WorkerSide
+
+        keys = [bytes([i]) * 16 for i in range(4)]
+        more = [bytes([i]) * 16 for i in range(4, 6)]
+        store = _Store(rank, [])
+        store.objects.reserved = []
+        comps = []
+
+        def write_placements(todo, blocks, mems=None, stream=None, chunk_layer_mems=None):
+            if rank == fail_rank and len(comps) == 1:
+                raise OSError("injected write failure")
+            store.writes.append((list(todo), blocks.tolist(), chunk_layer_mems.tolist()))
+            comps.append(_Comp())
+            return comps[-1]
+
+        store.write_placements = write_placements
+        fan = FanoutRestorer(store, _Peers(rank, world))
+        fan.mems, fan.layer_mems = None, [np.asarray([500 + 10 * r + l for l in range(2)], dtype=np.uint64)
+                                          for r in range(world)]
+        confirmed = []
+        index = SimpleNamespace(confirm_store=lambda ks, ok: confirmed.append((list(ks), ok)),
+                                is_resident=lambda k: False)
+        engine = SimpleNamespace(plan_store=lambda ks: SimpleNamespace(new_keys=list(ks)), index=index,
+                                 write_stream=None, staged=False, store=store)
+        w = WorkerSide(lambda t: None, block_size=16, chunk_tokens=32, tp_rank=rank, tp_size=world,
+                       replica_io=True, replica_io_saves="fanin")
+        board = _Board()
+        w.engine, w._fan, w._save_board, w._fanin_on = engine, fan, board, True
+        w._n_drives, w._affine = 2, [0, 1]
+        out = {}
+        # step 1: four chunks saved; this GPU writes the chunks on its drive for both ranks
+        m1 = w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, list(range(8)))]))
+        out["step1_committed"] = dict(m1.committed)
+        out["writes"] = store.writes[0]
+        out["signals"] = list(board.signals)
+        # step 2: request a finished: its next forward waits for every GPU's writes of batch 1
+        w.start_load_kv(TuttiConnectorMetadata(2, [], [], finished_saving=["a"]))
+        out["reuse_waits"] = [x for x in board.waits if x[0] == 1]
+        m2 = w.wait_for_save(TuttiConnectorMetadata(2, [], []))  # writes still running: undecided
+        out["step2_committed"] = dict(m2.committed)
+        comps[0].done = True
+        w.start_load_kv(TuttiConnectorMetadata(3, [], []))
+        m3 = w.wait_for_save(TuttiConnectorMetadata(3, [], [SaveSpec("b", more, list(range(8, 12)))]))
+        out["step3_committed"] = sorted(m3.committed)
+        for c in comps:
+            c.done = True
+        w.start_load_kv(TuttiConnectorMetadata(4, [], []))
+        m4 = w.wait_for_save(TuttiConnectorMetadata(4, [], []))
+        out["step4_committed"] = sorted(m4.committed)
+        out["objects"] = (list(store.objects.committed), list(store.objects.aborted))
+        out["confirmed"] = confirmed
+        out["pending"] = len(w._fanin)
+        q.put((rank, out))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, "".join(traceback.format_exception(e))[-3000:]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fanin_saves_commit_together_after_every_gpu_wrote():
+    out = _spawn(_fanin_rank, 2, -1)
+    keys = [bytes([i]) * 16 for i in range(4)]
+    more = [bytes([i]) * 16 for i in range(4, 6)]
+    for r in range(2):
+        o = out[r]
+        assert not isinstance(o, str), o
+        todo, blocks, clm = o["writes"]
+        # GPU r writes slots {r, r+2} of both ranks' namespaces, gathering from each owner's caches
+        assert todo == [(f"/w{owner}/seg{i % 2}", 8192 * i) for owner in range(2) for i in (r, r + 2)]
+        assert clm == [[500 + 10 * owner + l for l in range(2)] for owner in range(2) for _ in (r, r + 2)]
+        assert blocks == [[2 * i, 2 * i + 1] for _ in range(2) for i in (r, r + 2)]
+        assert (0, 1) in o["signals"] and (1, 1) in o["signals"]  # forward done, writes done
+        assert o["reuse_waits"] == [(1, 1)]
+        assert o["step1_committed"] == {} and o["step2_committed"] == {}
+        assert o["step3_committed"] == sorted(keys)  # batch 1 decided once both GPUs' writes ended
+        assert o["step4_committed"] == sorted(more)
+        committed, aborted = o["objects"]
+        assert committed == keys + more and aborted == [] and o["pending"] == 0
+        assert (keys, True) in o["confirmed"] and (more, True) in o["confirmed"]
+
+
+def test_fanin_save_failure_on_one_gpu_aborts_the_batch_on_every_rank():
+    out = _spawn(_fanin_rank, 2, 1)  # GPU 1's second batch fails to submit
+    keys = [bytes([i]) * 16 for i in range(4)]
+    more = [bytes([i]) * 16 for i in range(4, 6)]
+    for r in range(2):
+        o = out[r]
+        assert not isinstance(o, str), o
+        committed, aborted = o["objects"]
+        assert committed == keys and aborted == more
+        assert o["step4_committed"] == [] and (more, False) in o["confirmed"] and o["pending"] == 0

@@ -95,7 +95,8 @@ class TuttiConnectorV1(KVConnectorBase_V1):
                                       max_inflight_saves=self.cfg.max_inflight_saves,
                                       replica_io=self.cfg.replica_io, group=cpu_group,
                                       replica_kind="latent" if _uses_mla(vllm_config) else "main",
-                                      kv_heads=_total_kv_heads(vllm_config))
+                                      kv_heads=_total_kv_heads(vllm_config),
+                                      replica_io_saves=self.cfg.replica_io_saves)
 
     def _cold_start(self) -> None:
         """Publish the chunks a previous run left in the store (a read-only view; no model geometry needed)."""

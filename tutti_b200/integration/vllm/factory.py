@@ -17,6 +17,8 @@
   max_chunks_per_wave      accepted; a restore is one submission the io kernel pipelines
   replica_io               each GPU reads the chunks on its affine drives for every TP rank and stores
                            each rank's slice into that rank's caches over NVLink (TP > 1)
+  replica_io_saves         local (default): each rank writes its own chunks; fanin: the drive-affine
+                           GPUs gather every rank's blocks over NVLink and write them (with replica_io)
   kv_load_failure_policy   recompute | fail: vLLM's own kv_transfer_config field governs, applied by
                            vLLM's scheduler to the blocks the worker reports as failed
   store:
@@ -87,6 +89,7 @@ class ConnectorConfig:
     lookahead_k: int = 4  # layers restored ahead of the layer attention is waiting for
     max_inflight_saves: int = 64  # saves in flight per worker before a step waits for the oldest
     replica_io: bool = False  # drive-affine reads for every TP rank, stored over NVLink
+    replica_io_saves: str = "local"  # local | fanin (drive-affine GPUs write every rank's chunks)
     expect: dict = field(default_factory=dict)  # num_layers / chunk_kv_bytes / segment_bytes given in the config
     direct_transfer: bool = False  # require the direct (paged) path
     segment_header_bytes: int = 0  # 0: the store's default
@@ -96,7 +99,7 @@ class ConnectorConfig:
         extra = dict(extra or {})
         known = {"chunk_tokens", "namespace", "load_mode", "kv_load_failure_policy", "store", "async_load_free_ratio",
                  "min_retrieve_tokens", "max_tokens_per_load", "failure_collective_timeout_s", "lookahead_k",
-                 "max_inflight_saves",
+                 "max_inflight_saves", "replica_io_saves",
                  # Tutti's keys for facts derived here from vLLM's tensors (checked, not required)
                  "num_layers", "chunk_kv_bytes", "segment_bytes", "physical_chunk_tokens",
                  "direct_transfer", "max_chunks_per_wave", "replica_io"}
@@ -119,6 +122,9 @@ class ConnectorConfig:
         if "max_chunks_per_wave" in extra and int(extra["max_chunks_per_wave"]) <= 0:
             raise ValueError("max_chunks_per_wave must be positive")
         c.replica_io = bool(extra.get("replica_io", False))
+        c.replica_io_saves = str(extra.get("replica_io_saves", "local"))
+        if c.replica_io_saves not in ("local", "fanin"):
+            raise ValueError(f"replica_io_saves must be local or fanin, got {c.replica_io_saves!r}")
         c.lookahead_k = extra.get("lookahead_k", c.lookahead_k)
         if not isinstance(c.lookahead_k, int) or isinstance(c.lookahead_k, bool) or c.lookahead_k <= 0:
             raise ValueError(f"lookahead_k must be a positive integer, got {c.lookahead_k!r}")

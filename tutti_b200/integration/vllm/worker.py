@@ -147,7 +147,7 @@ class WorkerSide:
                  chunk_tokens: int, tp_rank: int = 0, tp_size: int = 1,
                  consensus: TpFailureConsensus | None = None, failure_policy: str = "recompute",
                  lookahead: int = 4, max_inflight_saves: int = 64, replica_io: bool = False, group=None,
-                 replica_kind: str = "main", kv_heads: int | None = None):
+                 replica_kind: str = "main", kv_heads: int | None = None, replica_io_saves: str = "local"):
         if failure_policy not in ("recompute", "fail"):
             raise ValueError("kv_load_failure_policy must be recompute or fail")
         self.make_engine = make_engine
@@ -181,6 +181,16 @@ class WorkerSide:
         self.replica_kind = replica_kind
         self.kv_heads = kv_heads
         self._replica_groups = [(r,) for r in range(tp_size)]
+        # replica_io_saves="fanin": a step's saves are written by the drive-affine GPUs, which
+        # gather every rank's blocks over NVLink; commits are decided together (store_harvest)
+        if replica_io_saves not in ("local", "fanin"):
+            raise ValueError("replica_io_saves must be local or fanin")
+        self.replica_io_saves = replica_io_saves
+        self._fanin_on = False
+        self._save_board = None
+        self._fanin: dict = {}  # batch id -> FaninBatch not yet decided (the same ids on every rank)
+        self._fanin_of: dict[str, set[int]] = {}  # request id -> undecided batches holding its saves
+        self._fanin_next = 0
         self._fan = None
         self._board = None
         self._epoch = 0
@@ -235,6 +245,10 @@ class WorkerSide:
         self._board = ReadyBoard(layers[0].device.index, self.group, slots=len(layers))
         self._n_drives = max(1, len(getattr(store, "mounts", [None])))
         self._affine = list(range(self.tp_size))
+        if self.replica_io_saves == "fanin":
+            # slot 0: every rank's forward of batch E wrote its blocks; slot 1: every GPU's writes of E ended
+            self._save_board = ReadyBoard(layers[0].device.index, self.group, slots=2)
+            self._fanin_on = True
 
     # -- loads ----------------------------------------------------------------
     def start_load_kv(self, meta: TuttiConnectorMetadata) -> None:
@@ -244,6 +258,13 @@ class WorkerSide:
         for rid in getattr(meta, "finished_saving", ()) or ():
             for ev in self._save_events.pop(rid, ()):
                 torch.cuda.current_stream().wait_event(ev)
+            # fan-in saves: until every GPU's writes of the request's batches ended (device wait,
+            # bounded; a wait that gives up fails the batch, so nothing torn is committed)
+            for bid in sorted(self._fanin_of.pop(rid, ())):
+                b = self._fanin.get(bid)
+                if b is not None:
+                    cs = torch.cuda.current_stream() if torch.cuda.is_available() else None
+                    b.reuse_tickets.append(self._save_board.wait(1, bid, cs))
         if self.engine is not None:
             if self.health is None:
                 self.health = HealthReporter(self.engine.store)
@@ -346,6 +367,13 @@ class WorkerSide:
                 end.record()
                 self._step_timing.append((start, end, tokens))
         self._settle_sync_loads(meta.generation)
+        if self._fanin_on:
+            if meta.saves:
+                self._fanin_begin(meta.saves)
+            if self._fanin:
+                self._fanin_harvest()
+            self._harvest_samples()
+            return self._meta
         if meta.saves:
             ev = torch.cuda.Event() if torch.cuda.is_available() and not self.engine.staged else None
             if ev is not None:
@@ -367,6 +395,40 @@ class WorkerSide:
         self._harvest_saves()
         self._harvest_samples()
         return self._meta
+
+    # -- fan-in saves (replica_io_saves="fanin") ---------------------------------------------
+    def _fanin_begin(self, saves) -> None:
+        """Start one batch for this step's saves (collective: every rank, same step, same specs)."""
+        self._fanin_next += 1
+        bid = self._fanin_next
+        stream = torch.cuda.current_stream() if torch.cuda.is_available() else None
+        self._save_board.signal(0, bid, stream)  # this rank's forward wrote the blocks
+        keys, blocks = [], []
+        for spec in saves:
+            keys += [bytes(k) for k in spec.keys]
+            blocks += list(spec.block_ids)
+        plan = self.engine.plan_store(keys)  # this rank's index: capacity closure, pending keys
+        mine = list(plan.new_keys) if plan is not None else []
+        items = fanout_items(keys, np.asarray(blocks, dtype=np.int64), self.blocks_per_chunk,
+                             [(r,) for r in range(self.tp_size)])
+        b = self._fan.store_begin(bid, items, mine, self._n_drives, self._affine, self._save_board,
+                                  getattr(self.engine, "write_stream", None))
+        b.all_keys, b.index_keys = keys, mine
+        self._fanin[bid] = b
+        for spec in saves:
+            self._fanin_of.setdefault(spec.request_id, set()).add(bid)
+
+    def _fanin_harvest(self, blocking: bool = False) -> None:
+        """Commit or abort the batches every rank finished (collective, lockstep on all ranks)."""
+        for b in self._fan.store_harvest(list(self._fanin.values()), self._save_board, blocking):
+            del self._fanin[b.batch_id]
+            self.engine.index.confirm_store(getattr(b, "index_keys", b.keys), bool(b.committed))
+            if b.committed:
+                for k in b.keys:
+                    self._meta.committed[k] = self._meta.committed.get(k, 0) + 1
+            else:
+                LOG.warning("fan-in save batch %d aborted: %s", b.batch_id, b.error or "a peer failed")
+            self._count_resident(getattr(b, "all_keys", ()))
 
     def _count_resident(self, keys) -> None:
         for k in keys:
@@ -457,6 +519,20 @@ class WorkerSide:
         deadline = time.monotonic() + float(timeout_s)
         left = lambda: max(0.0, deadline - time.monotonic())  # noqa: E731
         self.settle_saves(left())
+        # undecided fan-in batches: no collective at shutdown (peers may be gone); their
+        # writes are waited for (no DMA outlives the caches) and this rank's keys aborted
+        for b in list(self._fanin.values()):
+            try:
+                if b.comp is not None:
+                    settle_by(b.comp, deadline)
+            except Exception:  # noqa: BLE001
+                pass
+            if b.keys:
+                self.engine.store.objects.abort(b.keys)
+            self.engine.index.confirm_store(getattr(b, "index_keys", b.keys), False)
+        self._fanin.clear()
+        if self._save_board is not None:
+            self._save_board.close()
         if self._board is not None:
             self._board.close()
             self._peers.close()

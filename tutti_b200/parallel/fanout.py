@@ -21,7 +21,7 @@ owner pushes inside the io kernel instead of consumers pulling afterwards.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Sequence
 
 import numpy as np
@@ -89,6 +89,10 @@ class ReadyBoard:
         with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
             ops.ready_wait(words, self.world, value, int(timeout_s * 1e9), self._status[ticket:ticket + 1])
         return ticket
+
+    def passed(self, ticket: int) -> bool:
+        """True once the stream ran the wait (its outcome is then readable with ``failed``)."""
+        return (int(self._status[ticket]) & 0xFFFFFFFF) != 0xFFFFFFFF
 
     def failed(self, ticket: int) -> list[int]:
         """Ranks the wait gave up on (empty: all arrived); valid after the stream passed the wait."""
@@ -173,6 +177,41 @@ class PeerLayers:
         for p in self._opened:
             ops.ipc_close(p, self.device)
         self._opened.clear()
+
+
+@dataclass
+class FaninBatch:
+    """One step's saves in flight through the drive-affine GPUs (``FanoutRestorer.store_begin``)."""
+
+    batch_id: int
+    keys: list = field(default_factory=list)  # this rank's reserved keys (committed or aborted together)
+    comp: object = None  # this GPU's writes (None: it had nothing to write)
+    ticket: int | None = None  # the device wait for every rank's forward, on the io stream
+    reuse_tickets: list = field(default_factory=list)  # device waits of forwards that reuse the blocks
+    error: str = ""
+    committed: bool | None = None
+
+    def local_state(self, board, blocking: bool = False) -> str:
+        """"pending", "ok" or "fail" on this rank."""
+        if self.error:
+            return "fail"
+        if self.comp is not None:
+            if not blocking and not self.comp.query():
+                return "pending"
+            try:
+                self.comp.wait()
+            except Exception as e:  # noqa: BLE001
+                self.error = str(e)
+                return "fail"
+        for t in ([self.ticket] if self.ticket is not None else []) + list(self.reuse_tickets):
+            if not board.passed(t):
+                if not blocking:
+                    return "pending"
+                torch.cuda.synchronize()
+            if board.failed(t):
+                self.error = "a device wait gave up"
+                return "fail"
+        return "ok"
 
 
 @dataclass
@@ -337,6 +376,101 @@ class FanoutRestorer:
         if errors:
             raise RuntimeError("; ".join(errors))
         raise RuntimeError("a peer's drive-affine write failed; this rank's chunks were aborted")
+
+    # -- asynchronous fan-in stores (the vLLM worker's saves under replica_io) -------------
+    def store_begin(self, batch_id: int, items: Sequence[RestoreItem], mine: Sequence[bytes], n_drives: int,
+                    affine_gpus: Sequence[int], board, stream=None) -> "FaninBatch":
+        """Start persisting ``items`` through the drive-affine GPUs without waiting for the writes.
+
+        Collective over the group, called by every rank for the same batch in the same
+        order. This rank reserves ``mine`` (its own new keys) in its namespace and the
+        reservations are exchanged; on ``stream`` this GPU then waits on the device until
+        every rank raised ``board`` slot 0 to ``batch_id`` (its forward wrote the blocks),
+        gathers the blocks of the chunks on its affine drives from their owners' caches
+        (P2P loads in the io kernel) and writes them, and raises slot 1 to ``batch_id``
+        behind the writes. Commits are decided later by ``store_harvest``.
+        """
+        me = self.peers.rank
+        objects = self.kv.objects
+        reserved, err = {}, ""
+        mine = [bytes(k) for k in mine if not objects.contains(bytes(k))]  # stored by an earlier batch
+        if mine:
+            reserve = getattr(self.kv, "reserve", objects.reserve)
+            accepted, rejected = reserve(mine)
+            for k, uri, off, slot, _gen in accepted:
+                reserved[(me, bytes(k))] = (uri[len("file://"):], off, slot)
+            if rejected:
+                err = f"rank {me}: {rejected} chunk(s) did not fit"
+        allmaps: list = [None] * self.peers.world
+        dist.all_gather_object(allmaps, (reserved, err), group=self.group)
+        placements, errors = {}, [e for _, e in allmaps if e]
+        for m, _ in allmaps:
+            placements.update(m)
+        batch = FaninBatch(batch_id, keys=[k for (_r, k) in reserved], error="; ".join(errors))
+        if errors:
+            board.signal(1, batch_id, stream)  # nothing will be written: no rank waits on this GPU
+            return batch
+        todo, ranks, blocks = [], [], []
+        for it in items:
+            p = placements.get((it.rank, bytes(it.key)))
+            if p is None:
+                continue  # already stored by its rank
+            path, off, slot = p
+            if affine_gpus[(slot % n_drives) % len(affine_gpus)] != me:
+                continue
+            todo.append((path, off))
+            ranks.append(it.rank)
+            blocks.append(list(it.block_ids))
+        batch.ticket = board.wait(0, batch_id, stream)  # every rank's forward of this batch is done
+        try:
+            if todo and self.layer_mems is not None:
+                batch.comp = self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64), stream=stream,
+                                                      chunk_layer_mems=np.stack([self.layer_mems[r] for r in ranks]))
+            elif todo:
+                batch.comp = self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64),
+                                                      np.asarray([self.mems[r] for r in ranks], np.uint64),
+                                                      stream=stream)
+        except Exception as e:  # noqa: BLE001 - reported through store_harvest
+            batch.error = f"rank {me}: {e}"
+        board.signal(1, batch_id, stream)
+        return batch
+
+    def store_harvest(self, batches: Sequence["FaninBatch"], board, blocking: bool = False) -> list["FaninBatch"]:
+        """Decide the batches every rank has finished: commit each rank's own keys, or abort them.
+
+        Collective over the group (every rank calls it at the same point with the same
+        batch ids). A batch is finished on this rank when its writes completed and every
+        device wait registered on it (before the writes, and ``reuse_tickets`` of forwards
+        that reuse its blocks) has run; it fails if a write failed or a wait gave up (a
+        block may have changed while it was gathered). Returns the batches decided now,
+        with ``committed`` set on each.
+        """
+        flushed = False
+        local: dict[int, str] = {}
+        for b in batches:
+            state = b.local_state(board, blocking)
+            if state == "ok" and b.comp is not None and not flushed:
+                flush = getattr(getattr(self.kv, "runtime", None), "flush_devices", None)
+                try:
+                    if flush is not None:
+                        flush()  # this GPU's drives hold other ranks' chunks too: durable first
+                except Exception as e:  # noqa: BLE001
+                    b.error = b.error or f"rank {self.peers.rank}: flush: {e}"
+                    state = "fail"
+                flushed = True
+            local[b.batch_id] = state
+        states: list = [None] * self.peers.world
+        dist.all_gather_object(states, local, group=self.group)
+        decided = []
+        for b in batches:
+            seen = [st.get(b.batch_id, "pending") for st in states]
+            if "pending" in seen:
+                continue
+            b.committed = all(x == "ok" for x in seen)
+            if b.keys:
+                (self.kv.objects.commit if b.committed else self.kv.objects.abort)(b.keys)
+            decided.append(b)
+        return decided
 
     def barrier(self) -> None:
         """Orders every rank after all ranks' restores (their kernels completed before this)."""

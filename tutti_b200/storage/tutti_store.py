@@ -402,12 +402,15 @@ class TuttiKVStore:
         self._track(comp)
         return comp
 
-    def write_placements(self, placements, block_ids, chunk_mems=None, stream=None, layer_mems=None) -> NativeCompletion:
+    def write_placements(self, placements, block_ids, chunk_mems=None, stream=None, layer_mems=None,
+                         chunk_layer_mems=None) -> NativeCompletion:
         """Write all layers of chunks to explicit (segment file path, payload offset) placements.
 
         The slots must already be reserved (by this rank or by the rank that owns them);
         committing them is the caller's job. ``chunk_mems[i]`` names the pool the chunk is
-        gathered from (a peer's pool is read over NVLink by the io kernel).
+        gathered from (a peer's pool is read over NVLink by the io kernel);
+        ``chunk_layer_mems[i, l]`` instead names layer l's tensor of the rank chunk i is
+        gathered from (per-layer caches, several ranks in one submission).
         """
         g = self.geometry
         block_ids = np.asarray(block_ids, dtype=np.int64).reshape(len(placements), g.blocks_per_chunk)
@@ -415,8 +418,9 @@ class TuttiKVStore:
         if stream is None and self.backend == "nvme-gpu":
             stream = torch.cuda.current_stream(self.device)
         lm = None if layer_mems is None else np.asarray(layer_mems, dtype=np.uint64)
+        clm = None if chunk_layer_mems is None else np.ascontiguousarray(chunk_layer_mems, dtype=np.uint64)
         ios, nbytes = self._submit_paged("write", placements, block_ids, np.arange(g.num_layers), stream, chunk_mems=cm,
-                                         layer_mems=lm)
+                                         layer_mems=lm, chunk_layer_mems=clm)
         comp = NativeCompletion(self.runtime, ios, nbytes=nbytes, kind="store")
         self._track(comp)
         return comp
