@@ -307,7 +307,7 @@ def test_ready_wait_returns_when_the_flag_is_set_and_reports_a_flag_that_never_i
     assert board.tolist() == [7, 7, 9, 9]
 
 
-def _replica_io_worker_rank(rank, world, port, q, root):
+def _replica_io_worker_rank(rank, world, port, q, root, saves="local"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -329,14 +329,22 @@ def _replica_io_worker_rank(rank, world, port, q, root):
         # this rank's KV-head slice: different values on every rank
         layers = [torch.randn(2, nb, bs, 2, 128, device="cuda", generator=g, dtype=torch.bfloat16) for _ in range(nl)]
         w = WorkerSide(lambda t, entity="": make_engine(cfg, t, rank, rank, world, entity), block_size=bs,
-                       chunk_tokens=chunk, tp_rank=rank, tp_size=world, replica_io=True, group=dist.group.WORLD)
+                       chunk_tokens=chunk, tp_rank=rank, tp_size=world, replica_io=True, group=dist.group.WORLD,
+                       replica_io_saves=saves)
         w.register_kv_caches({f"model.layers.{i}.self_attn.attn": t for i, t in enumerate(layers)})
         assert w._fan is not None, "replica_io was not set up"
         keys = [bytes([i + 1]) * 16 for i in range(6)]
         src = list(range(0, 24))  # 6 chunks x 4 blocks
-        w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, src)]))
+        committed = dict(w.wait_for_save(TuttiConnectorMetadata(1, [], [SaveSpec("a", keys, src)])).committed)
         # vLLM's scheduler loads a chunk only once every TP rank reported it committed
-        assert w.settle_saves() == 1
+        if saves == "fanin":
+            for step in range(2, 2000):  # every rank decides a batch at the same call
+                if len(committed) == len(keys):
+                    break
+                committed.update(w.wait_for_save(TuttiConnectorMetadata(step, [], [])).committed)
+            assert len(committed) == len(keys), committed
+        else:
+            assert w.settle_saves() == 1
         dist.barrier()
         ref = [t[:, 0:24].clone() for t in layers]
         dst = list(range(64, 88))
@@ -362,13 +370,14 @@ def _replica_io_worker_rank(rank, world, port, q, root):
 
 
 @pytest.mark.gpu
-def test_two_gpu_vllm_worker_with_replica_io_restores_every_rank(tmp_path):
+@pytest.mark.parametrize("saves", ["local", "fanin"])
+def test_two_gpu_vllm_worker_with_replica_io_restores_every_rank(tmp_path, saves):
     """replica_io in the vLLM worker: each GPU reads the chunks on its affine drive for both
     ranks, its io kernel stores each rank's slice into that rank's per-layer caches over NVLink,
     and every layer's attention waits on device-side ready flags from both ranks."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    out = _spawn(_replica_io_worker_rank, 2, str(tmp_path))
+    out = _spawn(_replica_io_worker_rank, 2, str(tmp_path), saves)
     for r in range(2):
         assert isinstance(out[r], tuple), out[r]
         ok, failed, read_bytes = out[r]
