@@ -350,11 +350,8 @@ class FanoutRestorer:
                 blocks.append(list(it.block_ids))
             try:
                 if todo and self.layer_mems is not None:
-                    for r in sorted(set(ranks)):
-                        sel = [i for i, x in enumerate(ranks) if x == r]
-                        self.kv.write_placements([todo[i] for i in sel],
-                                                 np.asarray([blocks[i] for i in sel], dtype=np.int64),
-                                                 stream=stream, layer_mems=self.layer_mems[r]).wait()
+                    self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64), stream=stream,
+                                             chunk_layer_mems=np.stack([self.layer_mems[r] for r in ranks])).wait()
                 elif todo:
                     self.kv.write_placements(todo, np.asarray(blocks, dtype=np.int64),
                                              np.asarray([self.mems[r] for r in ranks], np.uint64), stream=stream).wait()
