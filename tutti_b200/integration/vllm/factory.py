@@ -38,6 +38,7 @@ config/integration/vllm/kv_transfer.json.
 from __future__ import annotations
 
 import logging
+import os
 import re
 from dataclasses import dataclass, field
 
@@ -250,6 +251,12 @@ def make_engine(cfg: ConnectorConfig, tensors: list[torch.Tensor], rank: int, lo
     ctx = StoreContext(geometry=g, capacity_chunks=cap, namespace=ns, device=device, rank=rank,
                        local_rank=local_rank, world=world, entity=entity, options=options)
     store = create_store(kind, ctx)
+    media = (getattr(store, "runtime_options", None) or {}).get("emulator_media")
+    if media == "memory" and os.environ.get("CUDA_MODULE_LOADING", "").upper() != "EAGER":
+        # drives that DMA from this process: a kernel loaded lazily while an io kernel waits
+        # on them takes a context-wide lock that also holds their copies until the io deadline
+        LOG.warning("[tutti] emulated drives with memory media: start vLLM with CUDA_MODULE_LOADING=EAGER "
+                    "(or warm every kernel shape up first); a lazy kernel load during a restore stalls it")
     staged = kind == "memory" or not hasattr(store, "get_paged")
     if staged and cfg.direct_transfer:
         raise ValueError(f"direct_transfer: the {kind} store on {device} moves chunks through staging buffers")
