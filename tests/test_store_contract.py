@@ -136,3 +136,32 @@ def test_one_placement_restore_lands_in_several_ranks_per_layer_caches(tmp_path)
             store.restore_placements(todo, blocks, chunk_layer_mems=clm[:2])
     finally:
         store.close()
+
+
+def test_one_write_submission_gathers_from_several_ranks_per_layer_caches(tmp_path):
+    """write_placements with chunk_layer_mems: chunk i is gathered from the per-layer caches row i names
+    (the fan-in store's single submission for every owner), then read back and compared."""
+    store = open_store("segment-files", tmp_path)
+    try:
+        gen = torch.Generator().manual_seed(9)
+        shape = (G.planes, 16, G.block_size, G.num_kv_heads, G.head_dim)
+        own = [torch.randn(*shape, generator=gen).to(torch.bfloat16) for _ in range(G.num_layers)]
+        peer = [torch.randn(*shape, generator=gen).to(torch.bfloat16) for _ in range(G.num_layers)]
+        store.register_layers(own)
+        peer_h = [store.runtime.register_memory(t.data_ptr(), t.numel() * t.element_size(), "host", -1) for t in peer]
+        own_h = [int(h) for h in store._layer_mems]
+        keys = keys_for(11, 2)
+        accepted, rejected = store.reserve(keys)
+        assert rejected == 0
+        where = {bytes(k): (uri[len("file://"):], off) for k, uri, off, _slot, _gen in accepted}
+        todo = [where[bytes(keys[0])], where[bytes(keys[1])]]
+        # chunk 0 from this rank's blocks 0-1, chunk 1 from the peer's blocks 4-5
+        store.write_placements(todo, np.asarray([[0, 1], [4, 5]]),
+                               chunk_layer_mems=np.asarray([own_h, peer_h], dtype=np.uint64)).wait()
+        store.objects.commit([bytes(k) for k in keys])
+        store.get_paged(keys, np.asarray([[8, 9], [10, 11]])).wait()
+        for l in range(G.num_layers):
+            assert torch.equal(own[l][:, 8:10], own[l][:, 0:2])
+            assert torch.equal(own[l][:, 10:12], peer[l][:, 4:6])
+    finally:
+        store.close()
