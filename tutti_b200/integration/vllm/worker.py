@@ -371,7 +371,9 @@ class WorkerSide:
             if meta.saves:
                 self._fanin_begin(meta.saves)
             if self._fanin:
-                self._fanin_harvest()
+                # back-pressure: past max_inflight_saves undecided batches every rank waits for its
+                # own writes (the condition is the same on every rank: they hold the same batches)
+                self._fanin_harvest(blocking=len(self._fanin) > self.max_inflight_saves)
             self._harvest_samples()
             return self._meta
         if meta.saves:
