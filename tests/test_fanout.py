@@ -523,3 +523,53 @@ def test_fanin_save_failure_on_one_gpu_aborts_the_batch_on_every_rank():
         committed, aborted = o["objects"]
         assert committed == keys and aborted == more
         assert o["step4_committed"] == [] and (more, False) in o["confirmed"] and o["pending"] == 0
+
+
+def _fanin_pressure_rank(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from types import SimpleNamespace
+
+        from tutti_b200.integration.vllm.metadata import SaveSpec, TuttiConnectorMetadata
+        from tutti_b200.integration.vllm.worker import WorkerSide
+
+        store = _Store(rank, [])
+        comps = []
+
+        def write_placements(todo, blocks, mems=None, stream=None, chunk_layer_mems=None):
+            comps.append(_Comp())  # never reports done on its own: only a blocking wait settles it
+            return comps[-1]
+
+        store.write_placements = write_placements
+        fan = FanoutRestorer(store, _Peers(rank, world))
+        fan.mems, fan.layer_mems = None, [np.zeros(2, dtype=np.uint64) for _ in range(world)]
+        index = SimpleNamespace(confirm_store=lambda ks, ok: None, is_resident=lambda k: False)
+        engine = SimpleNamespace(plan_store=lambda ks: SimpleNamespace(new_keys=list(ks)), index=index,
+                                 write_stream=None, staged=False, store=store)
+        w = WorkerSide(lambda t: None, block_size=16, chunk_tokens=32, tp_rank=rank, tp_size=world,
+                       replica_io=True, replica_io_saves="fanin", max_inflight_saves=1)
+        w.engine, w._fan, w._save_board, w._fanin_on = engine, fan, _Board(), True
+        w._n_drives, w._affine = 2, [0, 1]
+        sizes = []
+        for step in range(3):
+            keys = [bytes([10 * step + i]) * 16 for i in range(2)]
+            w.wait_for_save(TuttiConnectorMetadata(step + 1, [], [SaveSpec(f"r{step}", keys, [0, 1, 2, 3])]))
+            sizes.append(len(w._fanin))
+        q.put((rank, (sizes, len(store.objects.committed))))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        q.put((rank, "".join(traceback.format_exception(e))[-3000:]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fanin_saves_back_pressure_decides_every_batch_when_too_many_wait():
+    out = _spawn(_fanin_pressure_rank, 2)
+    for r in range(2):
+        assert not isinstance(out[r], str), out[r]
+        sizes, committed = out[r]
+        # one batch may stay undecided; the second forces a blocking harvest that decides both
+        assert sizes == [1, 0, 1] and committed == 4
