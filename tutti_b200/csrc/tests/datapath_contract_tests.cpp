@@ -264,6 +264,27 @@ TEST(emulated_delay_injection_delays_one_command) {
     CHECK(ms2 < 29.0);
 }
 
+TEST(emulated_late_completion_after_a_reset_is_not_taken_for_the_next_command) {
+    // the host gives up on a command the drive still holds, resets the queue and
+    // reuses slot 0: the old command's completion, arriving later, must not land
+    // in the fresh queue (it would complete the next command before its data)
+    Drive d({});
+    HostSubmitter hs{d.ctl->host_queue(0)};
+    d.ctl->inject(nvme::InjectKind::DELAY, 1, 200000);  // 200 ms
+    CHECK(hs.run(d.read(1, 0, 4096, d.iova, 0), 2000) == -1);  // gave up after about 20 ms
+    CHECK(d.ctl->reset_queue(0).ok());
+    hs.reset();
+    std::memset(d.buf, 0, 2 * 4096);
+    const auto* cq = d.ctl->host_queue(0).cq;
+    CHECK(hs.run(d.read(2, 8192, 4096, d.iova + 4096, 0)) == 0);
+    CHECK(nvme::cqe_cid(cq[0].dw3) == 2);  // slot 0 holds the new command's completion
+    CHECK(std::memcmp(static_cast<char*>(d.buf) + 4096, d.pattern.data() + 8192, 4096) == 0);
+    std::this_thread::sleep_for(std::chrono::milliseconds(250));  // past the old command's delay
+    CHECK(hs.run(d.read(3, 16384, 4096, d.iova + 4096, 0)) == 0);
+    CHECK(nvme::cqe_cid(cq[1].dw3) == 3);  // and the next slot the one after it
+    CHECK(std::memcmp(static_cast<char*>(d.buf) + 4096, d.pattern.data() + 16384, 4096) == 0);
+}
+
 TEST(emulated_bandwidth_cap_paces_the_drive) {
     nvme::EmulatedControllerConfig cfg;
     cfg.max_gbps = 0.1;  // 100 MB/s: 10 x 1 MiB take at least ~94 ms
