@@ -888,12 +888,16 @@ IoSubmitOutcome StorageRuntime::submit(const IoRequest* reqs, std::size_t count,
         Impl::OpPart part;
         part.dp_key = gp.d->key;
         for (std::size_t k = 0; k < gp.reqs.size(); ++k) {
-            const auto& st = k < so.initial_states.size() ? so.initial_states[k]
-                                                          : IoRequestInitialState{IoRequestState::REJECTED,
-                                                                                  {StatusCode::INTERNAL, "missing state"}};
-            out.initial_states[gp.idx[k]] = st;
-            if (st.state == IoRequestState::REJECTED) {
-                if (first_reject.ok()) first_reject = st.status;
+            auto& dst = out.initial_states[gp.idx[k]];
+            if (k >= so.initial_states.size()) {
+                dst = {IoRequestState::REJECTED, {StatusCode::INTERNAL, "missing state"}};
+            } else if (so.initial_states[k].state == IoRequestState::ACCEPTED && so.initial_states[k].status.ok()) {
+                dst.state = IoRequestState::ACCEPTED;  // the common case: no status to copy
+            } else {
+                dst = std::move(so.initial_states[k]);
+            }
+            if (dst.state == IoRequestState::REJECTED) {
+                if (first_reject.ok()) first_reject = dst.status;
                 continue;
             }
             const IoRequest& r = reqs[gp.idx[k]];
