@@ -758,7 +758,7 @@ SubmitOutcome GpuNvmeDataPath::submit(const DataPathRequest* reqs, std::size_t c
             if (first_reject.ok()) first_reject = bad;
             continue;
         }
-        out.initial_states[i] = {IoRequestState::ACCEPTED, Status::Ok()};
+        out.initial_states[i].state = IoRequestState::ACCEPTED;  // its status is already Ok
         const std::uint32_t req_idx = static_cast<std::uint32_t>(accepted++);
         op->req_input_index.push_back(static_cast<std::uint32_t>(i));
         op->req_bytes.push_back(in.length);
