@@ -89,3 +89,22 @@ def test_vllm_phase_runner_reaps_the_session_and_bounds_a_hang(tmp_path):
     assert rc is None and "started" in out
     assert "most recent call first" in err  # the dumped stack
     assert time.monotonic() - t0 < 30
+
+
+def test_bench_numa_bind_reports_and_changes_nothing_without_a_gpu():
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    try:
+        import bench
+    finally:
+        sys.path.remove(root)
+    import torch
+
+    if torch.cuda.is_available():
+        return
+    before = os.sched_getaffinity(0)
+    r = bench.numa_bind(0)
+    assert r["bound"] is False and r["why"] and os.sched_getaffinity(0) == before
