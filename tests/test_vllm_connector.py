@@ -431,3 +431,22 @@ def test_worker_shutdown_does_not_wait_past_its_deadline_for_a_stuck_save():
     assert __import__("time").monotonic() - t0 < 5.0
     assert w.saves_in_flight() == 1  # left uncommitted, not waited for
     assert idle and idle[0] <= 0.2
+
+
+def test_worker_connector_passes_replica_options_from_the_model():
+    """The worker role hands replica_io, its save mode and the model's KV-head count / MLA to the worker."""
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+
+    from tutti_b200.integration.vllm.connector import TuttiConnectorV1
+
+    extra = {"chunk_tokens": CHUNK, "replica_io": True, "replica_io_saves": "fanin"}
+    mc = SimpleNamespace(use_mla=True, get_total_num_kv_heads=lambda: 1)
+    cfg = SimpleNamespace(kv_transfer_config=SimpleNamespace(kv_connector_extra_config=extra),
+                          cache_config=SimpleNamespace(block_size=BS), model_config=mc,
+                          parallel_config=SimpleNamespace(tensor_parallel_size=1))
+    w = TuttiConnectorV1(cfg, KVConnectorRole.WORKER, None)._worker
+    assert w.replica_io_saves == "fanin" and w.replica_kind == "latent" and w.kv_heads == 1
+    assert w.replica_io is False  # TP 1: nothing to fan out
+    cfg.kv_transfer_config.kv_connector_extra_config = dict(extra, replica_io_saves="nope")
+    with pytest.raises(ValueError, match="replica_io_saves"):
+        TuttiConnectorV1(cfg, KVConnectorRole.WORKER, None)
